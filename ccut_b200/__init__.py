@@ -1,0 +1,18 @@
+"""ccut_b200 -- B200 (sm_100a) quantized MoE expert forward for CostCut-Infer.
+
+The compute path is ``libccut_moe.so`` (hand-written CUDA, C ABI in ``include/ccut_moe.h``)
+driven through ctypes; PyTorch supplies device memory, streams and ``torch.distributed``.
+There is no CPU fallback: a missing library raises.
+
+Public entry points
+-------------------
+``MoeLayer``                 HBM-resident MoE layer: ``forward``, ``route``, ``topk``,
+                             ``permute``, ``expert_ffn``, ``combine``, ``dequant``
+``blocks.moe``               drop-ins for ``ccut.blocks.moe`` / ``ccut.models.generic.moe_forward``
+``quant``                    ``QuantizeMethodBase``-compatible AWQ-int4-g128 / FP8-block-128 methods
+"""
+
+from ccut_b200.layer import MoeLayer, Permutation, Routing  # noqa: F401
+
+__all__ = ["MoeLayer", "Permutation", "Routing"]
+__version__ = "0.1.0"

@@ -1,0 +1,401 @@
+// capi.cu -- extern "C" entry points of libccut_moe.so (declared in include/ccut_moe.h).
+//
+// Argument checks happen here, on the host, before anything is enqueued; kernels never
+// see a shape they were not written for.  Workspaces are carved into 256-byte aligned
+// regions; the first region is the device status word of ccut_workspace_status().
+#include "kernels.cuh"
+
+namespace ccut {
+namespace {
+
+constexpr int kMaxTopK = 16;
+constexpr int kMaxRoutedExperts = 256;
+
+int num_sms() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!cache[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+struct Carver {
+  uint8_t* base;
+  size_t off = 0;
+  explicit Carver(void* b) : base(static_cast<uint8_t*>(b)) {}
+  template <class T>
+  T* take(size_t n) {
+    off = (off + 255) / 256 * 256;
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += n * sizeof(T);
+    return p;
+  }
+};
+
+bool valid_fmt(int f) { return f == CCUT_FMT_AWQ_INT4_G128 || f == CCUT_FMT_FP8_E4M3_B128; }
+
+int check_layer(const ccut_moe_layer* L) {
+  if (!L) return CCUT_ERR_INVALID;
+  if (!valid_fmt(L->format)) return CCUT_ERR_UNSUPPORTED;
+  if (L->hidden <= 0 || L->inter <= 0 || L->hidden % 128 || L->inter % 128) return CCUT_ERR_INVALID;
+  if (L->num_experts < 1 || L->num_experts > kMaxRoutedExperts) return CCUT_ERR_UNSUPPORTED;
+  if (L->num_shared_slices < 0 || L->num_experts + L->num_shared_slices > kMaxExperts) return CCUT_ERR_UNSUPPORTED;
+  if (!L->w13 || !L->w2) return CCUT_ERR_INVALID;
+  return CCUT_OK;
+}
+
+int check_route(const ccut_route_params* rp, int E) {
+  if (!rp) return CCUT_ERR_INVALID;
+  if (rp->top_k < 1 || rp->top_k > kMaxTopK || rp->top_k > E) return CCUT_ERR_INVALID;
+  if (E > kMaxRoutedExperts) return CCUT_ERR_UNSUPPORTED;
+  if (rp->mode == CCUT_ROUTE_SIGMOID_GROUP) {
+    if (rp->n_group < 1 || rp->n_group > 32 || E % rp->n_group) return CCUT_ERR_INVALID;
+    if (rp->topk_group < 1 || rp->topk_group > rp->n_group) return CCUT_ERR_INVALID;
+    if (rp->topk_group * (E / rp->n_group) < rp->top_k) return CCUT_ERR_INVALID;
+  } else if (rp->mode != CCUT_ROUTE_SOFTMAX_TOPK && rp->mode != CCUT_ROUTE_TOPK_SOFTMAX) {
+    return CCUT_ERR_UNSUPPORTED;
+  }
+  return CCUT_OK;
+}
+
+int cuda_ok() { return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA; }
+
+int pick_mt(int T, int k, int E) {
+  const long rows_per_expert = (long)T * k / (E > 0 ? E : 1);
+  return rows_per_expert <= 24 ? 32 : 64;
+}
+
+// Expert-FFN scratch: f16 copy of x (FP8), intermediate rows.
+struct FfnScratch {
+  uint16_t* x16;
+  uint16_t* hbuf;
+};
+
+FfnScratch carve_ffn(Carver& c, const ccut_moe_layer* L, int T, int k, bool need_x16) {
+  const size_t R = (size_t)T * k + (size_t)L->num_shared_slices * T;
+  FfnScratch s;
+  s.x16 = need_x16 ? c.take<uint16_t>((size_t)T * L->hidden) : nullptr;
+  s.hbuf = c.take<uint16_t>(R * L->inter);
+  return s;
+}
+
+struct FwdScratch {
+  int* status;
+  float* part;
+  int* counts;
+  int32_t* offsets;
+  int32_t* ids;
+  float* wts;
+  int32_t* row_token;
+  float* row_weight;
+  int32_t* pair_row;
+  FfnScratch ffn;
+  float* ybuf;
+};
+
+FwdScratch carve_fwd(Carver& c, const ccut_moe_layer* L, int T, int k) {
+  const int E = L->num_experts, H = L->hidden, S = L->num_shared_slices;
+  const size_t R = (size_t)T * k + (size_t)S * T;
+  FwdScratch s;
+  s.status = c.take<int>(64);
+  s.part = c.take<float>((size_t)route_hsplit(T, E, H) * T * E);
+  s.counts = c.take<int>(E);
+  s.offsets = c.take<int32_t>(E + S + 1);
+  s.ids = c.take<int32_t>((size_t)T * k);
+  s.wts = c.take<float>((size_t)T * k);
+  s.row_token = c.take<int32_t>(R);
+  s.row_weight = c.take<float>(R);
+  s.pair_row = c.take<int32_t>((size_t)T * k);
+  s.ffn = carve_ffn(c, L, T, k, L->format == CCUT_FMT_FP8_E4M3_B128);
+  s.ybuf = c.take<float>(R * H);
+  return s;
+}
+
+int run_ffn(const ccut_moe_layer* L, const uint16_t* x, const uint16_t* x16, int T, int k, const int32_t* offsets,
+            const int32_t* row_token, const float* row_weight, float* y_rows, uint16_t* hbuf, int* status,
+            cudaStream_t st) {
+  const int fmt = L->format;
+  const int ne = L->num_experts + L->num_shared_slices;
+  const int mt = pick_mt(T, k, L->num_experts);
+  GemmArgs a1{static_cast<const uint8_t*>(L->w13),
+              ccut_w13_bytes(fmt, L->hidden, L->inter),
+              L->hidden,
+              L->inter,
+              fmt == CCUT_FMT_FP8_E4M3_B128 ? x16 : x,
+              L->hidden,
+              row_token,
+              offsets,
+              ne,
+              hbuf,
+              L->inter,
+              nullptr,
+              status};
+  int rc = launch_gemm(fmt, 0, mt, a1, num_sms(), st);
+  if (rc) return rc;
+  GemmArgs a2{static_cast<const uint8_t*>(L->w2),
+              ccut_w2_bytes(fmt, L->hidden, L->inter),
+              L->inter,
+              L->hidden,
+              hbuf,
+              L->inter,
+              nullptr,
+              offsets,
+              ne,
+              y_rows,
+              L->hidden,
+              row_weight,
+              status};
+  return launch_gemm(fmt, 1, mt, a2, num_sms(), st);
+}
+
+}  // namespace
+}  // namespace ccut
+
+using namespace ccut;
+
+extern "C" {
+
+const char* ccut_strerror(int code) {
+  switch (code) {
+    case CCUT_OK: return "ok";
+    case CCUT_ERR_INVALID: return "invalid argument or shape";
+    case CCUT_ERR_UNSUPPORTED: return "unsupported format, mode or size";
+    case CCUT_ERR_CUDA: return "CUDA launch or runtime failure";
+    case CCUT_ERR_WORKSPACE: return "workspace too small";
+    case CCUT_ERR_TIMEOUT: return "bounded device wait expired";
+    case CCUT_ERR_NCCL: return "NCCL failure";
+    default: return "unknown error";
+  }
+}
+
+int ccut_abi_version(void) { return 1; }
+
+size_t ccut_packed_matrix_bytes(int format, int K, int N) {
+  if (!valid_fmt(format) || K <= 0 || N <= 0 || K % 128 || N % 128) return 0;
+  return (size_t)(N / kTileN) * (K / kTileK) * block_bytes(format);
+}
+
+size_t ccut_w13_bytes(int format, int hidden, int inter) { return 2 * ccut_packed_matrix_bytes(format, hidden, inter); }
+
+size_t ccut_w2_bytes(int format, int hidden, int inter) { return ccut_packed_matrix_bytes(format, inter, hidden); }
+
+int ccut_pack_matrix(int format, const void* q, const void* z, const void* s, int K, int N, int nibble_order,
+                     void* dst, int nmat, int slot, ccut_stream_t stream) {
+  if (!valid_fmt(format)) return CCUT_ERR_UNSUPPORTED;
+  if (!q || !s || !dst || K <= 0 || N <= 0 || K % 128 || N % 128) return CCUT_ERR_INVALID;
+  if (nmat < 1 || nmat > 2 || slot < 0 || slot >= nmat) return CCUT_ERR_INVALID;
+  if (format == CCUT_FMT_AWQ_INT4_G128) {
+    if (!z) return CCUT_ERR_INVALID;
+    if (nibble_order != CCUT_NIBBLES_AWQ && nibble_order != CCUT_NIBBLES_SEQUENTIAL) return CCUT_ERR_INVALID;
+  }
+  return launch_pack(format, q, z, s, K, N, nibble_order, dst, nmat, slot, stream);
+}
+
+int ccut_dequant_matrix(int format, const void* packed, int K, int N, int nmat, int slot, float* out,
+                        ccut_stream_t stream) {
+  if (!valid_fmt(format)) return CCUT_ERR_UNSUPPORTED;
+  if (!packed || !out || K <= 0 || N <= 0 || K % 128 || N % 128) return CCUT_ERR_INVALID;
+  if (nmat < 1 || nmat > 2 || slot < 0 || slot >= nmat) return CCUT_ERR_INVALID;
+  return launch_dequant(format, packed, K, N, nmat, slot, out, stream);
+}
+
+size_t ccut_route_workspace_bytes(int T, int E, int H) {
+  if (T <= 0 || E <= 0 || H <= 0 || H % 64) return 256;
+  Carver c(nullptr);
+  c.take<int>(64);
+  c.take<float>((size_t)route_hsplit(T, E, H) * T * E);
+  return c.off;
+}
+
+int ccut_moe_route(const uint16_t* x, const float* router, int T, int H, int E, const ccut_route_params* rp,
+                   int32_t* ids, float* weights, float* logits, void* workspace, size_t ws_bytes,
+                   ccut_stream_t stream) {
+  int rc = check_route(rp, E);
+  if (rc) return rc;
+  if (T < 0 || H <= 0 || H % 128) return CCUT_ERR_INVALID;
+  if (T == 0) return CCUT_OK;
+  if (!x || !router || !ids || !weights || !workspace) return CCUT_ERR_INVALID;
+  if (ws_bytes < ccut_route_workspace_bytes(T, E, H)) return CCUT_ERR_WORKSPACE;
+  Carver c(workspace);
+  c.take<int>(64);
+  float* part = c.take<float>((size_t)route_hsplit(T, E, H) * T * E);
+  return launch_route(x, router, T, H, E, *rp, ids, weights, logits, part, nullptr, nullptr, stream);
+}
+
+int ccut_moe_topk(const float* logits, int T, int E, const ccut_route_params* rp, int32_t* ids, float* weights,
+                  ccut_stream_t stream) {
+  int rc = check_route(rp, E);
+  if (rc) return rc;
+  if (T < 0) return CCUT_ERR_INVALID;
+  if (T == 0) return CCUT_OK;
+  if (!logits || !ids || !weights) return CCUT_ERR_INVALID;
+  return launch_topk(logits, T, E, *rp, ids, weights, stream);
+}
+
+size_t ccut_permute_workspace_bytes(int E) {
+  Carver c(nullptr);
+  c.take<int>(64);
+  c.take<int>(E > 0 ? E : 1);
+  return c.off;
+}
+
+int ccut_moe_permute(const int32_t* ids, const float* weights, int T, int k, int E, int num_shared_slices,
+                     float shared_gate, int32_t* offsets, int32_t* row_token, float* row_weight, int32_t* pair_row,
+                     void* workspace, size_t ws_bytes, ccut_stream_t stream) {
+  if (T < 0 || k < 1 || k > kMaxTopK || E < 1 || E > kMaxRoutedExperts || num_shared_slices < 0 ||
+      E + num_shared_slices > kMaxExperts)
+    return CCUT_ERR_INVALID;
+  if (!offsets || !row_token || !row_weight || !pair_row || !workspace || (T > 0 && (!ids || !weights)))
+    return CCUT_ERR_INVALID;
+  if (ws_bytes < ccut_permute_workspace_bytes(E)) return CCUT_ERR_WORKSPACE;
+  Carver c(workspace);
+  c.take<int>(64);
+  int* counts = c.take<int>(E);
+  if (T > 0 && cudaMemsetAsync(pair_row, 0xFF, sizeof(int32_t) * (size_t)T * k, stream) != cudaSuccess)
+    return CCUT_ERR_CUDA;
+  int rc = launch_count(ids, T * k, E, counts, stream);
+  if (rc) return rc;
+  return launch_permute(ids, weights, T, k, E, num_shared_slices, shared_gate, counts, offsets, row_token,
+                        row_weight, pair_row, stream);
+}
+
+size_t ccut_expert_ffn_workspace_bytes(const ccut_moe_layer* L, int T, int k) {
+  if (check_layer(L) || T < 0 || k < 1) return 0;
+  Carver c(nullptr);
+  c.take<int>(64);
+  carve_ffn(c, L, T, k, L->format == CCUT_FMT_FP8_E4M3_B128);
+  return c.off;
+}
+
+int ccut_moe_expert_ffn(const ccut_moe_layer* L, const uint16_t* x, int T, int k, const int32_t* offsets,
+                        const int32_t* row_token, const float* row_weight, float* y_rows, void* workspace,
+                        size_t ws_bytes, ccut_stream_t stream) {
+  int rc = check_layer(L);
+  if (rc) return rc;
+  if (T < 0 || k < 1 || k > kMaxTopK || k > L->num_experts) return CCUT_ERR_INVALID;
+  if (T == 0) return CCUT_OK;
+  if (!x || !offsets || !row_token || !row_weight || !y_rows || !workspace) return CCUT_ERR_INVALID;
+  if (ws_bytes < ccut_expert_ffn_workspace_bytes(L, T, k)) return CCUT_ERR_WORKSPACE;
+  Carver c(workspace);
+  int* status = c.take<int>(64);
+  const bool fp8 = L->format == CCUT_FMT_FP8_E4M3_B128;
+  FfnScratch s = carve_ffn(c, L, T, k, fp8);
+  if (fp8) {
+    rc = launch_bf16_to_f16(x, s.x16, (size_t)T * L->hidden, stream);
+    if (rc) return rc;
+  }
+  return run_ffn(L, x, s.x16, T, k, offsets, row_token, row_weight, y_rows, s.hbuf, status, stream);
+}
+
+int ccut_moe_expert_ffn_w4a16(const ccut_moe_layer* L, const uint16_t* x, int T, int k, const int32_t* offsets,
+                              const int32_t* row_token, const float* row_weight, float* y_rows, void* workspace,
+                              size_t ws_bytes, ccut_stream_t stream) {
+  if (!L || L->format != CCUT_FMT_AWQ_INT4_G128) return CCUT_ERR_UNSUPPORTED;
+  return ccut_moe_expert_ffn(L, x, T, k, offsets, row_token, row_weight, y_rows, workspace, ws_bytes, stream);
+}
+
+int ccut_moe_expert_ffn_fp8b128(const ccut_moe_layer* L, const uint16_t* x, int T, int k, const int32_t* offsets,
+                                const int32_t* row_token, const float* row_weight, float* y_rows, void* workspace,
+                                size_t ws_bytes, ccut_stream_t stream) {
+  if (!L || L->format != CCUT_FMT_FP8_E4M3_B128) return CCUT_ERR_UNSUPPORTED;
+  return ccut_moe_expert_ffn(L, x, T, k, offsets, row_token, row_weight, y_rows, workspace, ws_bytes, stream);
+}
+
+int ccut_moe_combine(const float* y_rows, const int32_t* pair_row, int T, int k, int H, int num_shared_slices,
+                     void* out, int out_dtype, ccut_stream_t stream) {
+  if (T < 0 || k < 1 || k > kMaxTopK || H <= 0 || H % 4 || num_shared_slices < 0) return CCUT_ERR_INVALID;
+  if (out_dtype != CCUT_OUT_BF16 && out_dtype != CCUT_OUT_F32) return CCUT_ERR_INVALID;
+  if (T == 0) return CCUT_OK;
+  if (!y_rows || !pair_row || !out) return CCUT_ERR_INVALID;
+  return launch_combine(y_rows, pair_row, T, k, H, num_shared_slices, out, out_dtype, stream);
+}
+
+size_t ccut_moe_forward_workspace_bytes(const ccut_moe_layer* L, int T, int top_k) {
+  if (check_layer(L) || T < 0 || top_k < 1) return 0;
+  if (T == 0) return 256;
+  Carver c(nullptr);
+  carve_fwd(c, L, T, top_k);
+  return c.off;
+}
+
+int ccut_moe_forward(const ccut_moe_layer* L, const ccut_route_params* rp, const uint16_t* x, int T, void* out,
+                     int out_dtype, int32_t* ids, float* weights, void* workspace, size_t ws_bytes,
+                     ccut_stream_t stream) {
+  int rc = check_layer(L);
+  if (rc) return rc;
+  if (!L->router) return CCUT_ERR_INVALID;
+  rc = check_route(rp, L->num_experts);
+  if (rc) return rc;
+  if (out_dtype != CCUT_OUT_BF16 && out_dtype != CCUT_OUT_F32) return CCUT_ERR_INVALID;
+  if (T < 0) return CCUT_ERR_INVALID;
+  if (T == 0) return CCUT_OK;
+  if (!x || !out || !workspace) return CCUT_ERR_INVALID;
+  const int k = rp->top_k, E = L->num_experts, H = L->hidden;
+  if (ws_bytes < ccut_moe_forward_workspace_bytes(L, T, k)) return CCUT_ERR_WORKSPACE;
+  Carver c(workspace);
+  FwdScratch s = carve_fwd(c, L, T, k);
+  cudaStream_t st = stream;
+  rc = launch_route(x, L->router, T, H, E, *rp, s.ids, s.wts, nullptr, s.part, s.counts, s.ffn.x16, st);
+  if (rc) return rc;
+  if (cudaMemsetAsync(s.pair_row, 0xFF, sizeof(int32_t) * (size_t)T * k, st) != cudaSuccess) return CCUT_ERR_CUDA;
+  rc = launch_permute(s.ids, s.wts, T, k, E, L->num_shared_slices, L->shared_gate, s.counts, s.offsets, s.row_token,
+                      s.row_weight, s.pair_row, st);
+  if (rc) return rc;
+  rc = run_ffn(L, x, s.ffn.x16, T, k, s.offsets, s.row_token, s.row_weight, s.ybuf, s.ffn.hbuf, s.status, st);
+  if (rc) return rc;
+  rc = launch_combine(s.ybuf, s.pair_row, T, k, H, L->num_shared_slices, out, out_dtype, st);
+  if (rc) return rc;
+  if (ids && cudaMemcpyAsync(ids, s.ids, sizeof(int32_t) * (size_t)T * k, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+    return CCUT_ERR_CUDA;
+  if (weights &&
+      cudaMemcpyAsync(weights, s.wts, sizeof(float) * (size_t)T * k, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+    return CCUT_ERR_CUDA;
+  return CCUT_OK;
+}
+
+size_t ccut_quant_linear_workspace_bytes(int format, int M, int K) {
+  if (!valid_fmt(format) || M < 0 || K <= 0) return 0;
+  Carver c(nullptr);
+  c.take<int>(64);
+  c.take<int32_t>(2);
+  if (format == CCUT_FMT_FP8_E4M3_B128) c.take<uint16_t>((size_t)M * K);
+  return c.off;
+}
+
+int ccut_quant_linear(int format, const void* packed, int K, int N, const uint16_t* x, int M, float* y,
+                      void* workspace, size_t ws_bytes, ccut_stream_t stream) {
+  if (!valid_fmt(format)) return CCUT_ERR_UNSUPPORTED;
+  if (K <= 0 || N <= 0 || K % 128 || N % 128 || M < 0) return CCUT_ERR_INVALID;
+  if (M == 0) return CCUT_OK;
+  if (!packed || !x || !y || !workspace) return CCUT_ERR_INVALID;
+  if (ws_bytes < ccut_quant_linear_workspace_bytes(format, M, K)) return CCUT_ERR_WORKSPACE;
+  Carver c(workspace);
+  int* status = c.take<int>(64);
+  int32_t* off = c.take<int32_t>(2);
+  const uint16_t* xa = x;
+  int rc = launch_fill_offsets(off, M, stream);
+  if (rc) return rc;
+  if (format == CCUT_FMT_FP8_E4M3_B128) {
+    uint16_t* x16 = c.take<uint16_t>((size_t)M * K);
+    rc = launch_bf16_to_f16(x, x16, (size_t)M * K, stream);
+    if (rc) return rc;
+    xa = x16;
+  }
+  GemmArgs a{static_cast<const uint8_t*>(packed), 0, K, N, xa, K, nullptr, off, 1, y, N, nullptr, status};
+  return launch_gemm(format, 1, M <= 32 ? 32 : 64, a, num_sms(), stream);
+}
+
+int ccut_workspace_status(void* workspace, ccut_stream_t stream) {
+  if (!workspace) return CCUT_ERR_INVALID;
+  int v = 0;
+  if (cudaMemcpyAsync(&v, workspace, sizeof(int), cudaMemcpyDeviceToHost, stream) != cudaSuccess) return CCUT_ERR_CUDA;
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return CCUT_ERR_CUDA;
+  if (v != 0 && cudaMemsetAsync(workspace, 0, sizeof(int), stream) != cudaSuccess) return CCUT_ERR_CUDA;
+  return v;
+}
+
+}  // extern "C"

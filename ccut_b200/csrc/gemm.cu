@@ -1,0 +1,309 @@
+// gemm.cu -- dequant-fused grouped expert GEMM (gate/up + SiLU, and down).
+//
+// Work item = (expert, m tile of MT rows, n tile of 128 channels).  A persistent grid of
+// one CTA per SM walks the items; inside a CTA
+//   * warp 8 (producer) streams, per 128-k stage, the item's packed weight block(s) with
+//     one bulk async copy and the MT activation row chunks (gathered through row_src) with
+//     one bulk copy each, into a ring of shared-memory stages guarded by mbarriers;
+//   * warps 0..7 (consumers) each own 16 output channels: they load their A fragments
+//     with 128-bit shared loads, dequantize in registers (AWQ: nibble -> bf16 (q - z),
+//     exact; FP8: e4m3 -> f16, exact), read the activations with ldmatrix and issue
+//     m16n8k16 tensor-core MMAs into a per-stage fp32 partial, which is then scaled by the
+//     stage's group/block scale and added to the fp32 accumulator.  The weight operand is
+//     therefore never rounded: (q - z) and e4m3 values are exact in bf16/f16, and the
+//     scale is applied in fp32 once per 128-k group (AWQ per channel, FP8 per block).
+// Epilogues: FFN1 writes silu(gate) * up as bf16 (AWQ) / f16 (FP8) rows; FFN2 writes
+// row_weight[row] * acc as fp32 rows.
+//
+// Follows ccut/blocks/moe.py:122-141 (expert_ffn), ccut/quant/kernels.py:219-231 (SiLU),
+// the dequant of ccut/quant/kernels.py:150-171 / :276-295 (restated for the g128 / block
+// formats), and ccut/models/generic.py:377-378 (routing-weight scaling).
+#include "kernels.cuh"
+
+namespace ccut {
+
+template <int FMT, int MODE, int MT>
+struct GemmCfg {
+  using B = Blk<FMT>;
+  static constexpr int kNWarps = 8;
+  static constexpr int kThreads = (kNWarps + 1) * 32;
+  static constexpr int kNMat = MODE == kFfn1 ? 2 : 1;
+  static constexpr int kWBytes = kNMat * B::kBytes;
+  static constexpr int kXRow = kTileK * 2 + 16;  // padded row: conflict-free ldmatrix
+  static constexpr int kXBytes = MT * kXRow;
+  static constexpr int kStageBytes = kWBytes + kXBytes;
+  static constexpr int kBudget = 200 * 1024;
+  static constexpr int kStages0 = kBudget / kStageBytes;
+  static constexpr int kStages = kStages0 > 8 ? 8 : kStages0;
+  static constexpr int kHeader = 2 * 8 * kStages + 4 * (kMaxExperts + 1);
+  static constexpr int kHeaderAligned = (kHeader + 127) / 128 * 128;
+  static constexpr int kSmem = kHeaderAligned + kStages * kStageBytes;
+  static_assert(kStages >= 2, "stage does not fit");
+  static_assert(MT % 16 == 0 && MT <= 64, "MT must be 16, 32, 48 or 64");
+  static_assert(kWBytes % 16 == 0 && kXRow % 16 == 0, "bulk copies need 16-byte granules");
+};
+
+template <int MT>
+__device__ __forceinline__ void decode_item(int item, const int* tprefix, int num_e, const int* offsets, int ntiles,
+                                            int& e, int& nt, int& m0, int& rows) {
+  int lo = 0, hi = num_e - 1;  // last e with tprefix[e] <= item
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (tprefix[mid] <= item) lo = mid;
+    else hi = mid - 1;
+  }
+  e = lo;
+  const int me = offsets[e + 1] - offsets[e];
+  const int mtiles = (me + MT - 1) / MT;
+  const int local = item - tprefix[e];
+  nt = local / mtiles;
+  const int mt = local % mtiles;
+  m0 = mt * MT;
+  rows = min(MT, me - m0);
+}
+
+template <int FMT, int MODE, int MT>
+__global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, 1) moe_gemm_kernel(GemmArgs a) {
+  using C = GemmCfg<FMT, MODE, MT>;
+  using B = typename C::B;
+  constexpr int S = C::kStages;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + S;
+  int* tprefix = reinterpret_cast<int*>(smem + 16 * S);
+  uint8_t* stages = smem + C::kHeaderAligned;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ntiles = a.N / kTileN, ktiles = a.K / kTileK;
+
+  if (warp == 0) {  // item prefix over experts: tiles(e) = ceil(M_e / MT) * ntiles
+    int carry = 0;
+    for (int b = 0; b < a.num_e; b += 32) {
+      const int e = b + lane;
+      const int me = e < a.num_e ? a.offsets[e + 1] - a.offsets[e] : 0;
+      const int c = ((me + MT - 1) / MT) * ntiles;
+      int inc = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += u;
+      }
+      if (e < a.num_e) tprefix[e] = carry + inc - c;
+      carry += __shfl_sync(0xffffffffu, inc, 31);
+    }
+    if (lane == 0) tprefix[a.num_e] = carry;
+  }
+  if (threadIdx.x == 32) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], C::kNWarps);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const int total = tprefix[a.num_e];
+
+  if (warp == C::kNWarps) {
+    // ---------------- producer ----------------
+    int use = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
+      int e, nt, m0, rows;
+      decode_item<MT>(item, tprefix, a.num_e, a.offsets, ntiles, e, nt, m0, rows);
+      const int row0 = a.offsets[e] + m0;
+      int src[MT / 32 + 1];
+#pragma unroll
+      for (int i = 0; i * 32 < MT; ++i) {
+        const int r = lane + 32 * i;
+        src[i] = r < rows ? (a.row_src ? a.row_src[row0 + r] : row0 + r) : 0;
+      }
+      const uint8_t* wb = a.w + (size_t)e * a.expert_stride + (size_t)nt * ktiles * C::kWBytes;
+      for (int kt = 0; kt < ktiles; ++kt, ++use) {
+        const int s = use % S;
+        const uint32_t ph = (use / S) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, a.status)) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = stages + s * C::kStageBytes;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[s], C::kWBytes + rows * (kTileK * 2));
+          bulk_g2s(st, wb + (size_t)kt * C::kWBytes, C::kWBytes, &full[s]);
+        }
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i * 32 < MT; ++i) {
+          const int r = lane + 32 * i;
+          if (r < rows)
+            bulk_g2s(st + C::kWBytes + r * C::kXRow, a.x + (size_t)src[i] * a.x_ld + kt * kTileK, kTileK * 2,
+                     &full[s]);
+        }
+      }
+    }
+    if (!ok && lane == 0) {  // let the copies already issued land before the CTA exits
+      for (int u = use > S ? use - S : 0; u < use; ++u) mbar_wait(&full[u % S], (u / S) & 1, nullptr);
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  const int g = lane >> 2, t = lane & 3;
+  const int ch_lo = warp * 16 + g, ch_hi = ch_lo + 8;  // channels within the 128-tile
+  int use = 0;
+  for (int item = blockIdx.x; item < total; item += gridDim.x) {
+    int e, nt, m0, rows;
+    decode_item<MT>(item, tprefix, a.num_e, a.offsets, ntiles, e, nt, m0, rows);
+    const int nblk = (rows + 7) >> 3;  // 8-token MMA column blocks in use
+    float acc[C::kNMat][MT / 8][4];
+#pragma unroll
+    for (int m = 0; m < C::kNMat; ++m)
+#pragma unroll
+      for (int b = 0; b < MT / 8; ++b)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[m][b][i] = 0.f;
+
+    for (int kt = 0; kt < ktiles; ++kt, ++use) {
+      const int s = use % S;
+      if (!mbar_wait(&full[s], (use / S) & 1, a.status)) return;
+      const uint8_t* st = stages + s * C::kStageBytes;
+      const uint8_t* xs = st + C::kWBytes;
+      float part[C::kNMat][MT / 8][4];
+#pragma unroll
+      for (int m = 0; m < C::kNMat; ++m)
+#pragma unroll
+        for (int b = 0; b < MT / 8; ++b)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) part[m][b][i] = 0.f;
+
+      // per-stage scale (and AWQ zero-point) of this lane's two channels
+      float sc_lo[C::kNMat], sc_hi[C::kNMat];
+      uint32_t zp_lo[C::kNMat], zp_hi[C::kNMat];
+#pragma unroll
+      for (int m = 0; m < C::kNMat; ++m) {
+        const uint8_t* blk = st + m * B::kBytes;
+        if constexpr (FMT == CCUT_FMT_AWQ_INT4_G128) {
+          const uint16_t* sc = reinterpret_cast<const uint16_t*>(blk + B::kScaleOff);
+          sc_lo[m] = __half2float(__ushort_as_half(sc[ch_lo]));
+          sc_hi[m] = __half2float(__ushort_as_half(sc[ch_hi]));
+          zp_lo[m] = zero_pair_bf16(blk[B::kZeroOff + (ch_lo >> 1)] >> (4 * (ch_lo & 1)));
+          zp_hi[m] = zero_pair_bf16(blk[B::kZeroOff + (ch_hi >> 1)] >> (4 * (ch_hi & 1)));
+        } else {
+          sc_lo[m] = sc_hi[m] = reinterpret_cast<const float*>(blk + B::kScaleOff)[0];
+          zp_lo[m] = zp_hi[m] = 0;
+        }
+      }
+
+#pragma unroll
+      for (int kc = 0; kc < B::kChunks; ++kc) {
+        uint4 raw[C::kNMat];
+#pragma unroll
+        for (int m = 0; m < C::kNMat; ++m)
+          raw[m] = *reinterpret_cast<const uint4*>(st + m * B::kBytes + ((warp * B::kChunks + kc) * 32 + lane) * 16);
+#pragma unroll
+        for (int j = 0; j < B::kStepsPerChunk; ++j) {
+          uint32_t af[C::kNMat][4];
+#pragma unroll
+          for (int m = 0; m < C::kNMat; ++m) {
+            if constexpr (FMT == CCUT_FMT_AWQ_INT4_G128) {
+              const uint32_t wd = j == 0 ? raw[m].x : j == 1 ? raw[m].y : j == 2 ? raw[m].z : raw[m].w;
+              af[m][0] = nib2_to_bf16x2_minus(wd, zp_lo[m]);
+              af[m][1] = nib2_to_bf16x2_minus(wd >> 4, zp_hi[m]);
+              af[m][2] = nib2_to_bf16x2_minus(wd >> 8, zp_lo[m]);
+              af[m][3] = nib2_to_bf16x2_minus(wd >> 12, zp_hi[m]);
+            } else {
+              const uint32_t w0 = j == 0 ? raw[m].x : raw[m].z;
+              const uint32_t w1 = j == 0 ? raw[m].y : raw[m].w;
+              af[m][0] = e4m3x2_to_f16x2(static_cast<uint16_t>(w0));
+              af[m][1] = e4m3x2_to_f16x2(static_cast<uint16_t>(w0 >> 16));
+              af[m][2] = e4m3x2_to_f16x2(static_cast<uint16_t>(w1));
+              af[m][3] = e4m3x2_to_f16x2(static_cast<uint16_t>(w1 >> 16));
+            }
+          }
+          const int koff = kc * B::kChunkK + j * 16;
+#pragma unroll
+          for (int b = 0; b < MT / 8; b += 2) {
+            if (b < nblk) {
+              const int tok = 8 * (b + (lane >> 4)) + (lane & 7);
+              const int kk = koff + ((lane >> 3) & 1) * 8;
+              uint32_t r0, r1, r2, r3;
+              ldmatrix_x4(r0, r1, r2, r3, xs + tok * C::kXRow + kk * 2);
+#pragma unroll
+              for (int m = 0; m < C::kNMat; ++m) {
+                mma_16816<B::kBf16>(part[m][b], af[m], r0, r1);
+                if (b + 1 < nblk) mma_16816<B::kBf16>(part[m][b + 1], af[m], r2, r3);
+              }
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      // promote: acc += scale * partial (fp32)
+#pragma unroll
+      for (int m = 0; m < C::kNMat; ++m)
+#pragma unroll
+        for (int b = 0; b < MT / 8; ++b) {
+          acc[m][b][0] = fmaf(sc_lo[m], part[m][b][0], acc[m][b][0]);
+          acc[m][b][1] = fmaf(sc_lo[m], part[m][b][1], acc[m][b][1]);
+          acc[m][b][2] = fmaf(sc_hi[m], part[m][b][2], acc[m][b][2]);
+          acc[m][b][3] = fmaf(sc_hi[m], part[m][b][3], acc[m][b][3]);
+        }
+    }
+
+    // ---------------- epilogue ----------------
+    const int row0 = a.offsets[e] + m0;
+    const int n_lo = nt * kTileN + ch_lo, n_hi = n_lo + 8;
+#pragma unroll
+    for (int b = 0; b < MT / 8; ++b) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int tok = 8 * b + 2 * t + (i & 1);
+        if (tok < rows) {
+          const int n = i < 2 ? n_lo : n_hi;
+          const size_t o = (size_t)(row0 + tok) * a.out_ld + n;
+          if constexpr (MODE == kFfn1) {
+            const float h = silu(acc[0][b][i]) * acc[1][b][i];
+            uint16_t hv;
+            if constexpr (B::kBf16) hv = __bfloat16_as_ushort(__float2bfloat16_rn(h));
+            else hv = __half_as_ushort(__float2half_rn(h));
+            static_cast<uint16_t*>(a.out)[o] = hv;
+          } else {
+            const float wr = a.row_weight ? a.row_weight[row0 + tok] : 1.f;
+            static_cast<float*>(a.out)[o] = acc[0][b][i] * wr;
+          }
+        }
+      }
+    }
+  }
+}
+
+template <int FMT, int MODE, int MT>
+static int launch_gemm_t(const GemmArgs& a, int num_sms, cudaStream_t st) {
+  using C = GemmCfg<FMT, MODE, MT>;
+  auto kern = moe_gemm_kernel<FMT, MODE, MT>;
+  static bool attr_done = false;  // per instantiation; benign race (idempotent)
+  if (!attr_done) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) != cudaSuccess)
+      return CCUT_ERR_CUDA;
+    attr_done = true;
+  }
+  kern<<<num_sms, C::kThreads, C::kSmem, st>>>(a);
+  return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
+}
+
+// Token-tile height: 32 covers decode batches in one tile; 64 halves weight re-reads for
+// larger batches.
+int launch_gemm(int fmt, int mode, int mt, const GemmArgs& a, int num_sms, cudaStream_t st) {
+  if (fmt == CCUT_FMT_AWQ_INT4_G128) {
+    if (mode == kFfn1) return mt <= 32 ? launch_gemm_t<CCUT_FMT_AWQ_INT4_G128, kFfn1, 32>(a, num_sms, st)
+                                       : launch_gemm_t<CCUT_FMT_AWQ_INT4_G128, kFfn1, 64>(a, num_sms, st);
+    return mt <= 32 ? launch_gemm_t<CCUT_FMT_AWQ_INT4_G128, kFfn2, 32>(a, num_sms, st)
+                    : launch_gemm_t<CCUT_FMT_AWQ_INT4_G128, kFfn2, 64>(a, num_sms, st);
+  }
+  if (mode == kFfn1) return mt <= 32 ? launch_gemm_t<CCUT_FMT_FP8_E4M3_B128, kFfn1, 32>(a, num_sms, st)
+                                     : launch_gemm_t<CCUT_FMT_FP8_E4M3_B128, kFfn1, 64>(a, num_sms, st);
+  return mt <= 32 ? launch_gemm_t<CCUT_FMT_FP8_E4M3_B128, kFfn2, 32>(a, num_sms, st)
+                  : launch_gemm_t<CCUT_FMT_FP8_E4M3_B128, kFfn2, 64>(a, num_sms, st);
+}
+
+}  // namespace ccut

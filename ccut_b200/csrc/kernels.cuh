@@ -1,0 +1,48 @@
+// kernels.cuh -- host-side launchers implemented in the .cu files, used by capi.cu.
+#pragma once
+
+#include "layout.cuh"
+
+namespace ccut {
+
+enum { kFfn1 = 0, kFfn2 = 1 };
+
+struct GemmArgs {
+  const uint8_t* w;      // packed weights of expert 0
+  size_t expert_stride;  // bytes between experts
+  int K, N;              // inputs, outputs of one matrix
+  const uint16_t* x;     // activation rows (bf16 for AWQ, f16 for FP8)
+  int x_ld;              // elements per activation row
+  const int* row_src;    // activation row of each GEMM row, or null (identity)
+  const int* offsets;    // [num_e + 1] first GEMM row of each expert
+  int num_e;
+  void* out;
+  int out_ld;
+  const float* row_weight;  // FFN2: per-row multiplier (null -> 1)
+  int* status;
+};
+
+// pack.cu
+int launch_pack(int fmt, const void* q, const void* z, const void* s, int K, int N, int nibble_order, void* dst,
+                int nmat, int slot, cudaStream_t st);
+int launch_dequant(int fmt, const void* packed, int K, int N, int nmat, int slot, float* out, cudaStream_t st);
+// route.cu
+int route_hsplit(int T, int E, int H);
+int launch_route(const uint16_t* x, const float* router, int T, int H, int E, const ccut_route_params& rp,
+                 int32_t* ids, float* weights, float* logits, float* part, int* counts, uint16_t* x16,
+                 cudaStream_t st);
+int launch_topk(const float* logits, int T, int E, const ccut_route_params& rp, int32_t* ids, float* weights,
+                cudaStream_t st);
+int launch_permute(const int32_t* ids, const float* weights, int T, int k, int E, int slices, float shared_gate,
+                   const int* counts, int32_t* offsets, int32_t* row_token, float* row_weight, int32_t* pair_row,
+                   cudaStream_t st);
+int launch_count(const int32_t* ids, int n, int E, int* counts, cudaStream_t st);
+// gemm.cu
+int launch_gemm(int fmt, int mode, int mt, const GemmArgs& a, int num_sms, cudaStream_t st);
+// combine.cu
+int launch_combine(const float* y, const int32_t* pair_row, int T, int k, int H, int slices, void* out,
+                   int out_dtype, cudaStream_t st);
+int launch_bf16_to_f16(const uint16_t* in, uint16_t* out, size_t n, cudaStream_t st);
+int launch_fill_offsets(int32_t* off, int m, cudaStream_t st);
+
+}  // namespace ccut

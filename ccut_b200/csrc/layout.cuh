@@ -1,0 +1,85 @@
+// layout.cuh -- HBM tile layout of packed expert matrices.
+//
+// A matrix with K inputs and N outputs (both multiples of 128) is stored as blocks of
+// 128 output channels x 128 inputs, ordered [n_tile][k_tile][slot], where `slot`
+// interleaves gate (0) and up (1) for the fused gate/up matrix and is always 0 for a lone
+// matrix.  One block is exactly what one pipeline stage of the grouped GEMM consumes, so
+// a stage is a single contiguous bulk copy.
+//
+// Inside a block the weights are pre-arranged in tensor-core A-fragment order
+// (mma m16n8k16, rows = output channels, cols = k): channel block cb (16 channels) x
+// k chunk kc, 32 lanes x 16 bytes per (cb, kc).  A lane's 128-bit load therefore holds
+// the fragments it feeds to the MMA with no shuffling.
+//
+//   AWQ int4 block (8512 B):  [0, 8192)     8 cb x 2 kc(64 k) x 32 lanes x 4 words
+//                             [8192, 8448)  fp16 scale of each of the 128 channels
+//                             [8448, 8512)  zero-point nibbles, channel c in byte c/2,
+//                                           low nibble for even c
+//     word j of a lane covers k-step j (16 k) of the chunk; nibble p of the word is
+//     A-tile element (row g + 8*(p&1), col 2t + (p>>2) + 8*((p>>1)&1)), g = lane/4,
+//     t = lane%4.  (w >> 4r) & 0x000F000F is then A register r as two 16-bit halves.
+//   FP8 e4m3 block (16400 B): [0, 16384)    8 cb x 4 kc(32 k) x 32 lanes x 16 bytes
+//                             [16384, 16388) fp32 block scale, 12 bytes padding
+//     bytes [8j, 8j+8) of a lane cover k-step j; byte b is A-tile element
+//     (row g + 8*((b>>1)&1), col 2t + 8*(b>>2) + (b&1)), i.e. byte pair r is A register r.
+#pragma once
+
+#include "common.cuh"
+
+namespace ccut {
+
+constexpr int kTileN = 128;  // output channels per block
+constexpr int kTileK = 128;  // inputs per block (= AWQ group = FP8 block)
+constexpr int kMaxExperts = 512;
+
+template <int FMT>
+struct Blk;
+
+template <>
+struct Blk<CCUT_FMT_AWQ_INT4_G128> {
+  static constexpr int kChunks = 2;         // k chunks of 64 per channel block
+  static constexpr int kChunkK = 64;
+  static constexpr int kStepsPerChunk = 4;  // 16-k MMA steps per chunk
+  static constexpr int kAtomBytes = 8192;
+  static constexpr int kScaleOff = 8192;
+  static constexpr int kZeroOff = 8448;
+  static constexpr int kBytes = 8512;
+  static constexpr bool kBf16 = true;  // MMA operand type
+};
+
+template <>
+struct Blk<CCUT_FMT_FP8_E4M3_B128> {
+  static constexpr int kChunks = 4;  // k chunks of 32
+  static constexpr int kChunkK = 32;
+  static constexpr int kStepsPerChunk = 2;
+  static constexpr int kAtomBytes = 16384;
+  static constexpr int kScaleOff = 16384;
+  static constexpr int kZeroOff = 0;
+  static constexpr int kBytes = 16400;
+  static constexpr bool kBf16 = false;  // f16 operands (e4m3 -> f16 is exact)
+};
+
+inline __host__ __device__ size_t block_bytes(int fmt) {
+  return fmt == CCUT_FMT_AWQ_INT4_G128 ? Blk<CCUT_FMT_AWQ_INT4_G128>::kBytes
+                                       : Blk<CCUT_FMT_FP8_E4M3_B128>::kBytes;
+}
+
+// Byte offset of block (nt, kt, slot) in a packed buffer with `ktiles` k tiles and `nmat`
+// interleaved matrices.
+inline __host__ __device__ size_t block_offset(int fmt, int nt, int kt, int slot, int ktiles, int nmat) {
+  return ((size_t)(nt * ktiles + kt) * nmat + slot) * block_bytes(fmt);
+}
+
+// A-tile element of nibble p (AWQ word) -> (row, col) inside the 16x16 tile.
+inline __host__ __device__ void awq_nibble_pos(int p, int g, int t, int& row, int& col) {
+  row = g + 8 * (p & 1);
+  col = 2 * t + (p >> 2) + 8 * ((p >> 1) & 1);
+}
+
+// A-tile element of byte b (FP8 k-step) -> (row, col).
+inline __host__ __device__ void fp8_byte_pos(int b, int g, int t, int& row, int& col) {
+  row = g + 8 * ((b >> 1) & 1);
+  col = 2 * t + 8 * (b >> 2) + (b & 1);
+}
+
+}  // namespace ccut

@@ -1,0 +1,226 @@
+// pack.cu -- checkpoint layout -> HBM tile layout, and the fp32 dequant export.
+//
+// Packing runs once per matrix at load time (the weights then stay resident in HBM); the
+// export decodes the packed tiles with the same fragment mapping the GEMM uses, so the
+// bit-exact comparison of the export with the CPU dequant also checks the packed layout.
+#include "layout.cuh"
+
+namespace ccut {
+
+// AWQ nibble of logical column n in row r of a packed [R, N/8] int32 array.
+__device__ __forceinline__ uint32_t awq_get(const int32_t* a, int ncols8, int r, int n, const int* slot_of_col) {
+  uint32_t w = static_cast<uint32_t>(a[(size_t)r * ncols8 + (n >> 3)]);
+  return (w >> (4 * slot_of_col[n & 7])) & 0xFu;
+}
+
+struct NibbleOrder {
+  int slot_of_col[8];
+};
+
+__global__ void pack_awq_atoms_kernel(const int32_t* __restrict__ qweight, int K, int N, NibbleOrder ord,
+                                      uint8_t* __restrict__ dst, int nmat, int slot) {
+  constexpr int kWordsPerBlock = Blk<CCUT_FMT_AWQ_INT4_G128>::kAtomBytes / 4;
+  const int ktiles = K / kTileK;
+  const size_t total = (size_t)(N / kTileN) * ktiles * kWordsPerBlock;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int widx = static_cast<int>(i % kWordsPerBlock);
+    const size_t blk = i / kWordsPerBlock;
+    const int kt = static_cast<int>(blk % ktiles);
+    const int nt = static_cast<int>(blk / ktiles);
+    const int j = widx & 3;
+    const int lane = (widx >> 2) & 31;
+    const int kc = (widx >> 7) & 1;
+    const int cb = widx >> 8;
+    const int g = lane >> 2, t = lane & 3;
+    uint32_t word = 0;
+#pragma unroll
+    for (int p = 0; p < 8; ++p) {
+      int row, col;
+      awq_nibble_pos(p, g, t, row, col);
+      const int n = nt * kTileN + cb * 16 + row;
+      const int k = kt * kTileK + kc * 64 + j * 16 + col;
+      word |= awq_get(qweight, N / 8, k, n, ord.slot_of_col) << (4 * p);
+    }
+    uint8_t* b = dst + block_offset(CCUT_FMT_AWQ_INT4_G128, nt, kt, slot, ktiles, nmat);
+    reinterpret_cast<uint32_t*>(b)[widx] = word;
+  }
+}
+
+__global__ void pack_awq_meta_kernel(const int32_t* __restrict__ qzeros, const uint16_t* __restrict__ scales, int K,
+                                     int N, NibbleOrder ord, uint8_t* __restrict__ dst, int nmat, int slot) {
+  using B = Blk<CCUT_FMT_AWQ_INT4_G128>;
+  const int ktiles = K / kTileK;
+  const size_t total = (size_t)(N / kTileN) * ktiles * (kTileN / 2);  // one thread per channel pair
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int cp = static_cast<int>(i % (kTileN / 2));
+    const size_t blk = i / (kTileN / 2);
+    const int kt = static_cast<int>(blk % ktiles);
+    const int nt = static_cast<int>(blk / ktiles);
+    uint8_t* b = dst + block_offset(CCUT_FMT_AWQ_INT4_G128, nt, kt, slot, ktiles, nmat);
+    const int n0 = nt * kTileN + 2 * cp;
+    uint16_t* sc = reinterpret_cast<uint16_t*>(b + B::kScaleOff);
+    sc[2 * cp] = scales[(size_t)kt * N + n0];
+    sc[2 * cp + 1] = scales[(size_t)kt * N + n0 + 1];
+    const uint32_t z0 = awq_get(qzeros, N / 8, kt, n0, ord.slot_of_col);
+    const uint32_t z1 = awq_get(qzeros, N / 8, kt, n0 + 1, ord.slot_of_col);
+    b[B::kZeroOff + cp] = static_cast<uint8_t>(z0 | (z1 << 4));
+  }
+}
+
+__global__ void pack_fp8_kernel(const uint8_t* __restrict__ w, const float* __restrict__ scale, int K, int N,
+                                uint8_t* __restrict__ dst, int nmat, int slot) {
+  using B = Blk<CCUT_FMT_FP8_E4M3_B128>;
+  const int ktiles = K / kTileK;
+  constexpr int kFragsPerBlock = B::kAtomBytes / 8;  // 8-byte k-step fragments
+  const size_t total = (size_t)(N / kTileN) * ktiles * kFragsPerBlock;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int fidx = static_cast<int>(i % kFragsPerBlock);
+    const size_t blk = i / kFragsPerBlock;
+    const int kt = static_cast<int>(blk % ktiles);
+    const int nt = static_cast<int>(blk / ktiles);
+    const int j = fidx & 1;
+    const int lane = (fidx >> 1) & 31;
+    const int kc = (fidx >> 6) & 3;
+    const int cb = fidx >> 8;
+    const int g = lane >> 2, t = lane & 3;
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int bb = 0; bb < 8; ++bb) {
+      int row, col;
+      fp8_byte_pos(bb, g, t, row, col);
+      const int n = nt * kTileN + cb * 16 + row;
+      const int k = kt * kTileK + kc * 32 + j * 16 + col;
+      const uint32_t v = w[(size_t)n * K + k];
+      if (bb < 4) lo |= v << (8 * bb);
+      else hi |= v << (8 * (bb - 4));
+    }
+    uint8_t* b = dst + block_offset(CCUT_FMT_FP8_E4M3_B128, nt, kt, slot, ktiles, nmat);
+    reinterpret_cast<uint2*>(b)[fidx] = make_uint2(lo, hi);
+    if (fidx == 0) {
+      float* s = reinterpret_cast<float*>(b + B::kScaleOff);
+      s[0] = scale[(size_t)nt * ktiles + kt];
+      s[1] = 0.f;
+      s[2] = 0.f;
+      s[3] = 0.f;
+    }
+  }
+}
+
+// ---- export -------------------------------------------------------------------------
+__global__ void dequant_awq_kernel(const uint8_t* __restrict__ src, int K, int N, int nmat, int slot,
+                                   float* __restrict__ out) {
+  using B = Blk<CCUT_FMT_AWQ_INT4_G128>;
+  constexpr int kWordsPerBlock = B::kAtomBytes / 4;
+  const int ktiles = K / kTileK;
+  const size_t total = (size_t)(N / kTileN) * ktiles * kWordsPerBlock;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int widx = static_cast<int>(i % kWordsPerBlock);
+    const size_t blk = i / kWordsPerBlock;
+    const int kt = static_cast<int>(blk % ktiles);
+    const int nt = static_cast<int>(blk / ktiles);
+    const int j = widx & 3, lane = (widx >> 2) & 31, kc = (widx >> 7) & 1, cb = widx >> 8;
+    const int g = lane >> 2, t = lane & 3;
+    const uint8_t* b = src + block_offset(CCUT_FMT_AWQ_INT4_G128, nt, kt, slot, ktiles, nmat);
+    const uint32_t word = reinterpret_cast<const uint32_t*>(b)[widx];
+    const uint16_t* sc = reinterpret_cast<const uint16_t*>(b + B::kScaleOff);
+#pragma unroll
+    for (int p = 0; p < 8; ++p) {
+      int row, col;
+      awq_nibble_pos(p, g, t, row, col);
+      const int c = cb * 16 + row;
+      const uint32_t q = (word >> (4 * p)) & 0xF;
+      const uint32_t z = (b[B::kZeroOff + (c >> 1)] >> (4 * (c & 1))) & 0xF;
+      const float s = __half2float(__ushort_as_half(sc[c]));
+      const int n = nt * kTileN + c;
+      const int k = kt * kTileK + kc * 64 + j * 16 + col;
+      out[(size_t)k * N + n] = __fmul_rn(__fsub_rn((float)q, (float)z), s);
+    }
+  }
+}
+
+__global__ void dequant_fp8_kernel(const uint8_t* __restrict__ src, int K, int N, int nmat, int slot,
+                                   float* __restrict__ out) {
+  using B = Blk<CCUT_FMT_FP8_E4M3_B128>;
+  constexpr int kFragsPerBlock = B::kAtomBytes / 8;
+  const int ktiles = K / kTileK;
+  const size_t total = (size_t)(N / kTileN) * ktiles * kFragsPerBlock;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int fidx = static_cast<int>(i % kFragsPerBlock);
+    const size_t blk = i / kFragsPerBlock;
+    const int kt = static_cast<int>(blk % ktiles);
+    const int nt = static_cast<int>(blk / ktiles);
+    const int j = fidx & 1, lane = (fidx >> 1) & 31, kc = (fidx >> 6) & 3, cb = fidx >> 8;
+    const int g = lane >> 2, t = lane & 3;
+    const uint8_t* b = src + block_offset(CCUT_FMT_FP8_E4M3_B128, nt, kt, slot, ktiles, nmat);
+    const uint2 frag = reinterpret_cast<const uint2*>(b)[fidx];
+    const float s = reinterpret_cast<const float*>(b + B::kScaleOff)[0];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const uint32_t word = r < 2 ? frag.x : frag.y;
+      const uint16_t pair = static_cast<uint16_t>(word >> (16 * (r & 1)));
+      const uint32_t h2 = e4m3x2_to_f16x2(pair);
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int bb = 2 * r + e;
+        int row, col;
+        fp8_byte_pos(bb, g, t, row, col);
+        const float v = __half2float(__ushort_as_half(static_cast<uint16_t>(h2 >> (16 * e))));
+        const int n = nt * kTileN + cb * 16 + row;
+        const int k = kt * kTileK + kc * 32 + j * 16 + col;
+        out[(size_t)k * N + n] = __fmul_rn(v, s);
+      }
+    }
+  }
+}
+
+static int grid_for(size_t total, int threads) {
+  size_t g = (total + threads - 1) / threads;
+  if (g > 148 * 32) g = 148 * 32;
+  return static_cast<int>(g < 1 ? 1 : g);
+}
+
+static NibbleOrder make_order(int nibble_order) {
+  NibbleOrder o;
+  static const int awq_slot_of_col[8] = {0, 4, 1, 5, 2, 6, 3, 7};  // column c lives in slot [c]
+  for (int c = 0; c < 8; ++c) o.slot_of_col[c] = nibble_order == CCUT_NIBBLES_AWQ ? awq_slot_of_col[c] : c;
+  return o;
+}
+
+int launch_pack(int fmt, const void* q, const void* z, const void* s, int K, int N, int nibble_order, void* dst,
+                int nmat, int slot, cudaStream_t st) {
+  const int threads = 256;
+  const int ktiles = K / kTileK, ntiles = N / kTileN;
+  if (fmt == CCUT_FMT_AWQ_INT4_G128) {
+    NibbleOrder o = make_order(nibble_order);
+    size_t t1 = (size_t)ntiles * ktiles * (Blk<CCUT_FMT_AWQ_INT4_G128>::kAtomBytes / 4);
+    pack_awq_atoms_kernel<<<grid_for(t1, threads), threads, 0, st>>>(static_cast<const int32_t*>(q), K, N, o,
+                                                                     static_cast<uint8_t*>(dst), nmat, slot);
+    size_t t2 = (size_t)ntiles * ktiles * (kTileN / 2);
+    pack_awq_meta_kernel<<<grid_for(t2, threads), threads, 0, st>>>(
+        static_cast<const int32_t*>(z), static_cast<const uint16_t*>(s), K, N, o, static_cast<uint8_t*>(dst), nmat,
+        slot);
+  } else {
+    size_t t1 = (size_t)ntiles * ktiles * (Blk<CCUT_FMT_FP8_E4M3_B128>::kAtomBytes / 8);
+    pack_fp8_kernel<<<grid_for(t1, threads), threads, 0, st>>>(static_cast<const uint8_t*>(q),
+                                                               static_cast<const float*>(s), K, N,
+                                                               static_cast<uint8_t*>(dst), nmat, slot);
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
+}
+
+int launch_dequant(int fmt, const void* packed, int K, int N, int nmat, int slot, float* out, cudaStream_t st) {
+  const int threads = 256;
+  const int ktiles = K / kTileK, ntiles = N / kTileN;
+  if (fmt == CCUT_FMT_AWQ_INT4_G128) {
+    size_t t = (size_t)ntiles * ktiles * (Blk<CCUT_FMT_AWQ_INT4_G128>::kAtomBytes / 4);
+    dequant_awq_kernel<<<grid_for(t, threads), threads, 0, st>>>(static_cast<const uint8_t*>(packed), K, N, nmat,
+                                                                 slot, out);
+  } else {
+    size_t t = (size_t)ntiles * ktiles * (Blk<CCUT_FMT_FP8_E4M3_B128>::kAtomBytes / 8);
+    dequant_fp8_kernel<<<grid_for(t, threads), threads, 0, st>>>(static_cast<const uint8_t*>(packed), K, N, nmat,
+                                                                 slot, out);
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
+}
+
+}  // namespace ccut

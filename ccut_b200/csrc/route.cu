@@ -1,0 +1,355 @@
+// route.cu -- router logits, top-k and token permutation.
+//
+//   logits[t, e] = sum_h x[t, h] * router[e, h]   fp32 (ccut/models/generic.py:361)
+//   top-k per token, three modes                  (ccut/blocks/moe.py:46-89 + grouped sigmoid)
+//   stable counting sort of (token, slot) pairs by expert (ccut/models/generic.py:367-371)
+//
+// The logits GEMV splits H across CTAs so that a decode batch still spreads over the SMs;
+// the partial sums are added in a fixed order by the top-k kernel, so the routing is
+// deterministic run to run.
+#include <math.h>
+
+#include "layout.cuh"
+
+namespace ccut {
+
+constexpr int kRtTok = 16;  // tokens per logits CTA
+constexpr int kRtExp = 64;  // experts per logits CTA
+constexpr int kRtH = 64;    // h per smem chunk
+
+// Number of H splits: enough CTAs to cover the SMs at small T, one split at large T.
+int route_hsplit(int T, int E, int H) {
+  const int chunks = H / kRtH;
+  const int ctas = ((T + kRtTok - 1) / kRtTok) * ((E + kRtExp - 1) / kRtExp);
+  int hs = (296 + ctas - 1) / ctas;
+  if (hs > chunks) hs = chunks;
+  if (hs < 1) hs = 1;
+  while (chunks % hs) --hs;
+  return hs;
+}
+
+// part[hs][t][e]; also zeroes counts[E] and writes x16 (f16 copy of x) when requested.
+__global__ void __launch_bounds__(256) route_logits_kernel(const uint16_t* __restrict__ x,
+                                                           const float* __restrict__ router, int T, int H, int E,
+                                                           int hsplit, float* __restrict__ part,
+                                                           int* __restrict__ counts, uint16_t* __restrict__ x16) {
+  __shared__ float xs[kRtTok][kRtH];
+  __shared__ float ws[kRtExp][kRtH + 1];
+  const int t0 = blockIdx.x * kRtTok, e0 = blockIdx.y * kRtExp, hs = blockIdx.z;
+  const int hlen = H / hsplit, hbeg = hs * hlen;
+  const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+  if (counts && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+    for (int e = tid; e < E; e += blockDim.x) counts[e] = 0;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int h0 = hbeg; h0 < hbeg + hlen; h0 += kRtH) {
+    for (int i = tid; i < kRtTok * kRtH; i += 256) {
+      const int r = i / kRtH, c = i % kRtH, t = t0 + r;
+      float v = 0.f;
+      if (t < T) {
+        const uint16_t b = x[(size_t)t * H + h0 + c];
+        v = __uint_as_float(static_cast<uint32_t>(b) << 16);
+        if (x16 && blockIdx.y == 0) x16[(size_t)t * H + h0 + c] = __half_as_ushort(__float2half_rn(v));
+      }
+      xs[r][c] = v;
+    }
+    for (int i = tid; i < kRtExp * kRtH; i += 256) {
+      const int r = i / kRtH, c = i % kRtH, e = e0 + r;
+      ws[r][c] = e < E ? router[(size_t)e * H + h0 + c] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int c = 0; c < kRtH; ++c) {
+      const float xv = xs[ty][c];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[j] = fmaf(xv, ws[tx + 16 * j][c], acc[j]);
+    }
+    __syncthreads();
+  }
+  const int t = t0 + ty;
+  if (t < T) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int e = e0 + tx + 16 * j;
+      if (e < E) part[((size_t)hs * T + t) * E + e] = acc[j];
+    }
+  }
+}
+
+struct VI {
+  float v;
+  int i;
+};
+
+// Larger value wins; equal values -> lower index (the reference's strict '>' scan).
+__device__ __forceinline__ bool better(float a, int ia, float b, int ib) { return a > b || (a == b && ia < ib); }
+
+__device__ __forceinline__ VI warp_best(VI x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, x.v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, x.i, o);
+    if (better(ov, oi, x.v, x.i)) {
+      x.v = ov;
+      x.i = oi;
+    }
+  }
+  return x;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+constexpr int kMaxPerLane = 8;  // E <= 256
+constexpr int kMaxTopK = 16;
+
+// One warp per token.  Logits come either from `part` (hsplit partial sums) or `logits_in`.
+__global__ void __launch_bounds__(256) route_topk_kernel(const float* __restrict__ part, int hsplit,
+                                                         const float* __restrict__ logits_in, int T, int E,
+                                                         ccut_route_params rp, int32_t* __restrict__ ids,
+                                                         float* __restrict__ weights, float* __restrict__ logits_out,
+                                                         int* __restrict__ counts) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + warp;
+  if (t >= T) return;
+  const int k = rp.top_k;
+  float v[kMaxPerLane];
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) {
+    const int e = lane + 32 * i;
+    float val = -INFINITY;
+    if (e < E) {
+      if (logits_in) {
+        val = logits_in[(size_t)t * E + e];
+      } else {
+        val = 0.f;
+        for (int s = 0; s < hsplit; ++s) val += part[((size_t)s * T + t) * E + e];
+      }
+      if (logits_out) logits_out[(size_t)t * E + e] = val;
+    }
+    v[i] = val;
+  }
+  // selection score
+  float sel[kMaxPerLane], sg[kMaxPerLane];
+  if (rp.mode == CCUT_ROUTE_SIGMOID_GROUP) {
+    const int gsize = E / rp.n_group;
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) {
+      const int e = lane + 32 * i;
+      sg[i] = e < E ? 1.f / (1.f + expf(-v[i])) : 0.f;
+      sel[i] = e < E ? sg[i] + (rp.bias ? rp.bias[e] : 0.f) : -INFINITY;
+    }
+    // group score = sum of the two best selection scores in the group
+    uint32_t keep = 0;
+    float gscore_lane = -INFINITY;  // lane g holds the score of group g
+    for (int g = 0; g < rp.n_group; ++g) {
+      VI b1{-INFINITY, 0x7fffffff}, b2{-INFINITY, 0x7fffffff};
+#pragma unroll
+      for (int i = 0; i < kMaxPerLane; ++i) {
+        const int e = lane + 32 * i;
+        if (e < E && e / gsize == g) {
+          if (better(sel[i], e, b1.v, b1.i)) {
+            b2 = b1;
+            b1 = VI{sel[i], e};
+          } else if (better(sel[i], e, b2.v, b2.i)) {
+            b2 = VI{sel[i], e};
+          }
+        }
+      }
+      // merge top-2 across the warp
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        VI c1{__shfl_xor_sync(0xffffffffu, b1.v, o), __shfl_xor_sync(0xffffffffu, b1.i, o)};
+        VI c2{__shfl_xor_sync(0xffffffffu, b2.v, o), __shfl_xor_sync(0xffffffffu, b2.i, o)};
+        VI n1, n2;
+        if (better(c1.v, c1.i, b1.v, b1.i)) {
+          n1 = c1;
+          n2 = better(b1.v, b1.i, c2.v, c2.i) ? b1 : c2;
+        } else {
+          n1 = b1;
+          n2 = better(c1.v, c1.i, b2.v, b2.i) ? c1 : b2;
+        }
+        b1 = n1;
+        b2 = n2;
+      }
+      if (lane == g) gscore_lane = b1.v + b2.v;
+    }
+    for (int r = 0; r < rp.topk_group; ++r) {
+      VI b = warp_best(VI{lane < rp.n_group && !((keep >> lane) & 1) ? gscore_lane : -INFINITY,
+                          lane < rp.n_group ? lane : 0x7fffffff});
+      keep |= 1u << b.i;
+    }
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) {
+      const int e = lane + 32 * i;
+      if (e < E && !((keep >> (e / gsize)) & 1)) sel[i] = -INFINITY;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) {
+      sel[i] = v[i];
+      sg[i] = 0.f;
+    }
+  }
+  // top-k by repeated warp arg-max
+  uint32_t used = 0;
+  int my_id = -1;
+  float my_logit = 0.f, my_sig = 0.f;  // lane j < k keeps pick j
+  for (int j = 0; j < k; ++j) {
+    VI b{-INFINITY, 0x7fffffff};
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) {
+      const int e = lane + 32 * i;
+      if (e < E && !((used >> i) & 1) && better(sel[i], e, b.v, b.i)) b = VI{sel[i], e};
+    }
+    b = warp_best(b);
+    float lg = 0.f, sgv = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i) {
+      if (lane + 32 * i == b.i) {
+        used |= 1u << i;
+        lg = v[i];
+        sgv = sg[i];
+      }
+    }
+    const int owner = b.i & 31;
+    lg = __shfl_sync(0xffffffffu, lg, owner);
+    sgv = __shfl_sync(0xffffffffu, sgv, owner);
+    if (lane == j) {
+      my_id = b.i;
+      my_logit = lg;
+      my_sig = sgv;
+    }
+  }
+  float w = 0.f;
+  if (rp.mode == CCUT_ROUTE_SOFTMAX_TOPK) {
+    // softmax over all E, keep the k picks (no renormalisation)
+    const float m = __shfl_sync(0xffffffffu, my_logit, 0);  // pick 0 is the max logit
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxPerLane; ++i)
+      if (lane + 32 * i < E) s += expf(v[i] - m);
+    s = warp_sum(s);
+    w = expf(my_logit - m) / fmaxf(s, 1e-30f);
+  } else if (rp.mode == CCUT_ROUTE_TOPK_SOFTMAX) {
+    const float m = __shfl_sync(0xffffffffu, my_logit, 0);
+    const float ex = lane < k ? expf(my_logit - m) : 0.f;
+    const float s = warp_sum(ex);
+    w = ex / fmaxf(s, 1e-30f);
+  } else {
+    const float s = warp_sum(lane < k ? my_sig : 0.f);
+    w = my_sig / (s + 1e-20f) * rp.routed_scaling;
+  }
+  if (my_id < 0 || my_id >= E) {  // no finite score left (NaN logits): route nowhere
+    my_id = 0;
+    w = 0.f;
+  }
+  if (lane < k) {
+    ids[(size_t)t * k + lane] = my_id;
+    weights[(size_t)t * k + lane] = w;
+    if (counts) atomicAdd(&counts[my_id], 1);
+  }
+}
+
+// One warp per expert: stable compaction of the pairs routed to it.
+__global__ void __launch_bounds__(256) permute_kernel(const int32_t* __restrict__ ids,
+                                                      const float* __restrict__ weights, int T, int k, int E,
+                                                      int slices, float shared_gate, const int* __restrict__ counts,
+                                                      int32_t* __restrict__ offsets, int32_t* __restrict__ row_token,
+                                                      float* __restrict__ row_weight, int32_t* __restrict__ pair_row) {
+  __shared__ int cnt[kMaxExperts];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = counts[e];
+  __syncthreads();
+  const int tk = T * k;
+  const int e = blockIdx.x * 8 + warp;
+  if (blockIdx.x == 0 && warp == 0) {
+    int carry = 0;
+    for (int b = 0; b < E; b += 32) {
+      const int ee = b + lane;
+      int c = ee < E ? cnt[ee] : 0;
+      int inc = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += u;
+      }
+      if (ee < E) offsets[ee] = carry + inc - c;
+      carry += __shfl_sync(0xffffffffu, inc, 31);
+    }
+    if (lane == 0)
+      for (int s = 0; s <= slices; ++s) offsets[E + s] = tk + s * T;
+  }
+  if (e < E) {
+    int base = 0;
+    for (int i = lane; i < e; i += 32) base += cnt[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) base += __shfl_xor_sync(0xffffffffu, base, o);
+    int pos = 0;
+    const unsigned lt = (1u << lane) - 1u;
+    for (int i0 = 0; i0 < tk; i0 += 32) {
+      const int i = i0 + lane;
+      const bool m = i < tk && ids[i] == e;
+      const unsigned bal = __ballot_sync(0xffffffffu, m);
+      if (m) {
+        const int p = base + pos + __popc(bal & lt);
+        row_token[p] = i / k;
+        row_weight[p] = weights[i];
+        pair_row[i] = p;
+      }
+      pos += __popc(bal);
+    }
+  }
+  // shared-expert rows: every token once per slice
+  const int nsh = slices * T;
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < nsh; r += gridDim.x * blockDim.x) {
+    row_token[tk + r] = r % T;
+    row_weight[tk + r] = shared_gate;
+  }
+}
+
+int launch_route(const uint16_t* x, const float* router, int T, int H, int E, const ccut_route_params& rp,
+                 int32_t* ids, float* weights, float* logits, float* part, int* counts, uint16_t* x16,
+                 cudaStream_t st) {
+  const int hs = route_hsplit(T, E, H);
+  dim3 g1((T + kRtTok - 1) / kRtTok, (E + kRtExp - 1) / kRtExp, hs);
+  route_logits_kernel<<<g1, 256, 0, st>>>(x, router, T, H, E, hs, part, counts, x16);
+  route_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(part, hs, nullptr, T, E, rp, ids, weights, logits, counts);
+  return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
+}
+
+int launch_topk(const float* logits, int T, int E, const ccut_route_params& rp, int32_t* ids, float* weights,
+                cudaStream_t st) {
+  route_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(nullptr, 0, logits, T, E, rp, ids, weights, nullptr, nullptr);
+  return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
+}
+
+int launch_permute(const int32_t* ids, const float* weights, int T, int k, int E, int slices, float shared_gate,
+                   const int* counts, int32_t* offsets, int32_t* row_token, float* row_weight, int32_t* pair_row,
+                   cudaStream_t st) {
+  const int blocks = (E + 7) / 8;
+  permute_kernel<<<blocks, 256, 0, st>>>(ids, weights, T, k, E, slices, shared_gate, counts, offsets, row_token,
+                                         row_weight, pair_row);
+  return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
+}
+
+// counts[e] from ids (used when the caller supplies its own routing).
+__global__ void count_kernel(const int32_t* __restrict__ ids, int n, int E, int* __restrict__ counts) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int e = ids[i];
+    if (e >= 0 && e < E) atomicAdd(&counts[e], 1);
+  }
+}
+
+int launch_count(const int32_t* ids, int n, int E, int* counts, cudaStream_t st) {
+  if (cudaMemsetAsync(counts, 0, sizeof(int) * E, st) != cudaSuccess) return CCUT_ERR_CUDA;
+  int blocks = (n + 255) / 256;
+  if (blocks > 1024) blocks = 1024;
+  if (blocks < 1) blocks = 1;
+  count_kernel<<<blocks, 256, 0, st>>>(ids, n, E, counts);
+  return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
+}
+
+}  // namespace ccut

@@ -1,0 +1,292 @@
+"""HBM-resident quantized MoE layer driving the sm_100a kernels through the C ABI.
+
+Replaces the reference's streamed expert tier (``ccut/experts/reader.py:86-334`` ring
+buffer + ``ccut/models/generic.py:389-400`` per-call segment dequant): every expert's
+checkpoint tensors are uploaded once, packed on the device into the kernel tile layout
+and stay resident.  ``forward`` is the whole MoE layer of ``ccut/models/generic.py:348-386``.
+
+Checkpoint tensors are accepted per matrix as a mapping (or object with attributes):
+AWQ ``{"qweight": int32 [K, N/8], "qzeros": int32 [K/128, N/8], "scales": fp16 [K/128, N]}``
+(``[in, out]``); FP8 ``{"weight": e4m3/uint8 [N, K], "scale": fp32 [N/128, K/128]}``
+(``[out, in]``, the ``weight_scale_inv`` tensor of DeepSeek checkpoints).
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from ccut_b200 import _lib
+
+__all__ = ["MoeLayer", "Routing", "Permutation"]
+
+
+def _get(m, *names):
+    for n in names:
+        if isinstance(m, dict) and n in m:
+            return m[n]
+        if hasattr(m, n):
+            return getattr(m, n)
+    raise KeyError(f"checkpoint matrix lacks any of {names}")
+
+
+def _dev(a, device, dtype=None) -> torch.Tensor:
+    if isinstance(a, torch.Tensor):
+        t = a
+    else:
+        t = torch.from_numpy(np.ascontiguousarray(a))
+    if dtype is not None and t.dtype != dtype:
+        t = t.view(dtype) if t.element_size() == torch.empty((), dtype=dtype).element_size() else t.to(dtype)
+    return t.to(device, non_blocking=False).contiguous()
+
+
+def _stream() -> C.c_void_p:
+    return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _ptr(t: torch.Tensor | None) -> C.c_void_p:
+    return C.c_void_p(t.data_ptr() if t is not None else 0)
+
+
+@dataclass
+class Routing:
+    ids: torch.Tensor  # int32 [T, k]
+    weights: torch.Tensor  # fp32 [T, k]
+    logits: torch.Tensor | None = None  # fp32 [T, E]
+
+
+@dataclass
+class Permutation:
+    offsets: torch.Tensor  # int32 [E + slices + 1]
+    row_token: torch.Tensor  # int32 [R]
+    row_weight: torch.Tensor  # fp32 [R]
+    pair_row: torch.Tensor  # int32 [T * k]
+
+
+class MoeLayer:
+    """One MoE layer with experts resident in HBM.
+
+    ``fmt``: ``"awq_int4_g128"`` or ``"fp8_b128"``; ``routing``: ``"softmax_topk"``
+    (``norm_topk_prob=False``), ``"topk_softmax"`` (``norm_topk_prob=True``) or
+    ``"sigmoid_group"``."""
+
+    def __init__(
+        self,
+        fmt: str,
+        hidden: int,
+        inter: int,
+        num_experts: int,
+        top_k: int,
+        routing: str,
+        router: np.ndarray | torch.Tensor,
+        experts: list,
+        shared: list | None = None,
+        shared_inter: int | None = None,
+        shared_gate: float = 1.0,
+        n_group: int = 1,
+        topk_group: int = 1,
+        routed_scaling: float = 1.0,
+        bias: np.ndarray | torch.Tensor | None = None,
+        nibble_order: str = "awq",
+        device: str | torch.device = "cuda",
+    ):
+        if fmt not in _lib.FORMATS:
+            raise NotImplementedError(f"weight format {fmt!r} is not supported (have {sorted(_lib.FORMATS)})")
+        if routing not in _lib.ROUTING:
+            raise NotImplementedError(f"routing mode {routing!r} is not supported")
+        if hidden % 128 or inter % 128:
+            raise ValueError("hidden and inter must be multiples of 128")
+        if len(experts) != num_experts:
+            raise ValueError(f"expected {num_experts} experts, got {len(experts)}")
+        self.lib = _lib.load()
+        self.fmt, self.fmt_code = fmt, _lib.FORMATS[fmt]
+        self.hidden, self.inter, self.num_experts, self.top_k = hidden, inter, num_experts, top_k
+        self.routing = routing
+        self.device = torch.device(device)
+        shared = list(shared or [])
+        s_inter = shared_inter if shared_inter is not None else inter
+        if shared and s_inter % inter:
+            raise NotImplementedError("shared-expert intermediate must be a multiple of the routed one")
+        self.slices_per_shared = s_inter // inter if shared else 0
+        self.num_slices = len(shared) * self.slices_per_shared
+        self.shared_gate = float(shared_gate)
+        self.router = _dev(router, self.device, torch.float32)
+        if tuple(self.router.shape) != (num_experts, hidden):
+            raise ValueError(f"router must be [E, H] = {(num_experts, hidden)}, got {tuple(self.router.shape)}")
+        self.bias = _dev(bias, self.device, torch.float32) if bias is not None else None
+        self.route_params = _lib.RouteParams(
+            _lib.ROUTING[routing], top_k, n_group, topk_group, float(routed_scaling), _ptr(self.bias).value or None
+        )
+        self.nibbles = _lib.NIBBLES_AWQ if nibble_order == "awq" else _lib.NIBBLES_SEQUENTIAL
+        L = self.lib
+        self.w13_bytes = L.ccut_w13_bytes(self.fmt_code, hidden, inter)
+        self.w2_bytes = L.ccut_w2_bytes(self.fmt_code, hidden, inter)
+        ne = num_experts + self.num_slices
+        self.w13 = torch.empty(ne * self.w13_bytes, dtype=torch.uint8, device=self.device)
+        self.w2 = torch.empty(ne * self.w2_bytes, dtype=torch.uint8, device=self.device)
+        with torch.cuda.device(self.device):
+            for e, ew in enumerate(experts):
+                self._pack_expert(e, ew, 0, inter)
+            for j, sw in enumerate(shared):
+                for s in range(self.slices_per_shared):
+                    self._pack_expert(num_experts + j * self.slices_per_shared + s, sw, s * inter, inter)
+            torch.cuda.current_stream().synchronize()
+        self.desc = _lib.MoeLayerDesc(
+            self.fmt_code, hidden, inter, num_experts, self.num_slices, self.shared_gate,
+            _ptr(self.w13), _ptr(self.w2), _ptr(self.router),
+        )
+        self._ws: dict[str, torch.Tensor] = {}
+
+    # ---- packing ------------------------------------------------------------------
+    def _slice(self, mat, role: str, lo: int, width: int):
+        """Checkpoint tensors of intermediate channels [lo, lo+width) of one matrix."""
+        if self.fmt == "awq_int4_g128":
+            q, z, s = _get(mat, "qweight"), _get(mat, "qzeros"), _get(mat, "scales")
+            if role in ("gate", "up"):  # [K=H, N=I]: slice N
+                return q[:, lo // 8:(lo + width) // 8], z[:, lo // 8:(lo + width) // 8], s[:, lo:lo + width]
+            return q[lo:lo + width], z[lo // 128:(lo + width) // 128], s[lo // 128:(lo + width) // 128]
+        w, sc = _get(mat, "weight"), _get(mat, "scale", "weight_scale_inv")
+        if role in ("gate", "up"):  # [N=I, K=H]: slice N
+            return w[lo:lo + width], None, sc[lo // 128:(lo + width) // 128]
+        return w[:, lo:lo + width], None, sc[:, lo // 128:(lo + width) // 128]
+
+    def _pack_one(self, mat, role, lo, width, K, N, dst: torch.Tensor, nmat: int, slot: int):
+        q, z, s = self._slice(mat, role, lo, width)
+        if self.fmt == "awq_int4_g128":
+            qd, zd, sd = _dev(q, self.device, torch.int32), _dev(z, self.device, torch.int32), _dev(s, self.device,
+                                                                                                   torch.float16)
+            if tuple(qd.shape) != (K, N // 8) or tuple(sd.shape) != (K // 128, N):
+                raise ValueError(f"{role}: AWQ tensors have shapes q{tuple(qd.shape)} s{tuple(sd.shape)} for K={K} N={N}")
+        else:
+            qd, zd, sd = _dev(q, self.device, torch.uint8), None, _dev(s, self.device, torch.float32)
+            if tuple(qd.shape) != (N, K) or tuple(sd.shape) != (N // 128, K // 128):
+                raise ValueError(f"{role}: FP8 tensors have shapes w{tuple(qd.shape)} s{tuple(sd.shape)} for K={K} N={N}")
+        _lib.call("ccut_pack_matrix", self.fmt_code, _ptr(qd), _ptr(zd), _ptr(sd), K, N, self.nibbles,
+                  _ptr(dst), nmat, slot, _stream())
+
+    def _pack_expert(self, e: int, ew, lo: int, width: int):
+        H, I = self.hidden, self.inter
+        w13 = self.w13[e * self.w13_bytes:(e + 1) * self.w13_bytes]
+        w2 = self.w2[e * self.w2_bytes:(e + 1) * self.w2_bytes]
+        self._pack_one(_get(ew, "gate"), "gate", lo, width, H, I, w13, 2, 0)
+        self._pack_one(_get(ew, "up"), "up", lo, width, H, I, w13, 2, 1)
+        self._pack_one(_get(ew, "down"), "down", lo, width, I, H, w2, 1, 0)
+
+    # ---- workspace ------------------------------------------------------------------
+    def _workspace(self, key: str, nbytes: int) -> torch.Tensor:
+        ws = self._ws.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=self.device)
+            self._ws[key] = ws
+        return ws
+
+    def _check_x(self, x: torch.Tensor) -> torch.Tensor:
+        if x.device != self.device and not (x.is_cuda and self.device.type == "cuda" and self.device.index is None):
+            raise ValueError("activations must be on the layer's device")
+        if x.dtype != torch.bfloat16:
+            raise ValueError("activations must be bf16")
+        if x.dim() != 2 or x.shape[1] != self.hidden:
+            raise ValueError(f"activations must be [T, {self.hidden}]")
+        return x.contiguous()
+
+    # ---- whole layer ----------------------------------------------------------------
+    def forward(self, x: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16,
+                return_routing: bool = False):
+        x = self._check_x(x)
+        T = x.shape[0]
+        out = torch.empty((T, self.hidden), dtype=out_dtype, device=self.device)
+        ids = torch.empty((T, self.top_k), dtype=torch.int32, device=self.device) if return_routing else None
+        wts = torch.empty((T, self.top_k), dtype=torch.float32, device=self.device) if return_routing else None
+        nbytes = self.lib.ccut_moe_forward_workspace_bytes(C.byref(self.desc), T, self.top_k)
+        ws = self._workspace("fwd", nbytes)
+        od = _lib.OUT_BF16 if out_dtype == torch.bfloat16 else _lib.OUT_F32
+        if out_dtype not in (torch.bfloat16, torch.float32):
+            raise ValueError("out_dtype must be bf16 or fp32")
+        _lib.call("ccut_moe_forward", C.byref(self.desc), C.byref(self.route_params), _ptr(x), T, _ptr(out), od,
+                  _ptr(ids), _ptr(wts), _ptr(ws), ws.numel(), _stream())
+        if return_routing:
+            return out, Routing(ids, wts)
+        return out
+
+    __call__ = forward
+
+    def workspace_status(self) -> int:
+        """Device status word of the forward workspace (0 = ok); clears it."""
+        ws = self._ws.get("fwd")
+        if ws is None:
+            return 0
+        return self.lib.ccut_workspace_status(_ptr(ws), _stream())
+
+    # ---- stages ---------------------------------------------------------------------
+    def route(self, x: torch.Tensor, want_logits: bool = False) -> Routing:
+        x = self._check_x(x)
+        T, E, k = x.shape[0], self.num_experts, self.top_k
+        ids = torch.empty((T, k), dtype=torch.int32, device=self.device)
+        wts = torch.empty((T, k), dtype=torch.float32, device=self.device)
+        lg = torch.empty((T, E), dtype=torch.float32, device=self.device) if want_logits else None
+        ws = self._workspace("route", self.lib.ccut_route_workspace_bytes(T, E, self.hidden))
+        _lib.call("ccut_moe_route", _ptr(x), _ptr(self.router), T, self.hidden, E, C.byref(self.route_params),
+                  _ptr(ids), _ptr(wts), _ptr(lg), _ptr(ws), ws.numel(), _stream())
+        return Routing(ids, wts, lg)
+
+    def topk(self, logits: torch.Tensor) -> Routing:
+        logits = logits.to(self.device, torch.float32).contiguous()
+        T, E = logits.shape
+        ids = torch.empty((T, self.top_k), dtype=torch.int32, device=self.device)
+        wts = torch.empty((T, self.top_k), dtype=torch.float32, device=self.device)
+        _lib.call("ccut_moe_topk", _ptr(logits), T, E, C.byref(self.route_params), _ptr(ids), _ptr(wts), _stream())
+        return Routing(ids, wts, logits)
+
+    def permute(self, routing: Routing) -> Permutation:
+        ids = routing.ids.to(self.device, torch.int32).contiguous()
+        wts = routing.weights.to(self.device, torch.float32).contiguous()
+        T, k = ids.shape
+        R = T * k + self.num_slices * T
+        ne = self.num_experts + self.num_slices
+        perm = Permutation(
+            torch.empty(ne + 1, dtype=torch.int32, device=self.device),
+            torch.empty(max(R, 1), dtype=torch.int32, device=self.device),
+            torch.empty(max(R, 1), dtype=torch.float32, device=self.device),
+            torch.empty(max(T * k, 1), dtype=torch.int32, device=self.device),
+        )
+        ws = self._workspace("perm", self.lib.ccut_permute_workspace_bytes(self.num_experts))
+        _lib.call("ccut_moe_permute", _ptr(ids), _ptr(wts), T, k, self.num_experts, self.num_slices,
+                  C.c_float(self.shared_gate), _ptr(perm.offsets), _ptr(perm.row_token), _ptr(perm.row_weight),
+                  _ptr(perm.pair_row), _ptr(ws), ws.numel(), _stream())
+        return perm
+
+    def expert_ffn(self, x: torch.Tensor, perm: Permutation, k: int | None = None) -> torch.Tensor:
+        x = self._check_x(x)
+        T = x.shape[0]
+        k = k or self.top_k
+        R = T * k + self.num_slices * T
+        y = torch.empty((max(R, 1), self.hidden), dtype=torch.float32, device=self.device)
+        ws = self._workspace("ffn", self.lib.ccut_expert_ffn_workspace_bytes(C.byref(self.desc), T, k))
+        _lib.call("ccut_moe_expert_ffn", C.byref(self.desc), _ptr(x), T, k, _ptr(perm.offsets), _ptr(perm.row_token),
+                  _ptr(perm.row_weight), _ptr(y), _ptr(ws), ws.numel(), _stream())
+        return y[:R]
+
+    def combine(self, y_rows: torch.Tensor, perm: Permutation, T: int, k: int | None = None,
+                out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+        k = k or self.top_k
+        out = torch.empty((T, self.hidden), dtype=out_dtype, device=self.device)
+        od = _lib.OUT_BF16 if out_dtype == torch.bfloat16 else _lib.OUT_F32
+        _lib.call("ccut_moe_combine", _ptr(y_rows), _ptr(perm.pair_row), T, k, self.hidden, self.num_slices,
+                  _ptr(out), od, _stream())
+        return out
+
+    def dequant(self, expert: int, which: str) -> torch.Tensor:
+        """fp32 [K, N] ([in, out]) export of one packed matrix ("gate" | "up" | "down")."""
+        H, I = self.hidden, self.inter
+        if which in ("gate", "up"):
+            src = self.w13[expert * self.w13_bytes:(expert + 1) * self.w13_bytes]
+            K, N, nmat, slot = H, I, 2, 0 if which == "gate" else 1
+        else:
+            src = self.w2[expert * self.w2_bytes:(expert + 1) * self.w2_bytes]
+            K, N, nmat, slot = I, H, 1, 0
+        out = torch.empty((K, N), dtype=torch.float32, device=self.device)
+        _lib.call("ccut_dequant_matrix", self.fmt_code, _ptr(src), K, N, nmat, slot, _ptr(out), _stream())
+        return out

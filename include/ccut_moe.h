@@ -1,0 +1,197 @@
+/*
+ * ccut_moe.h -- C ABI of the B200 (sm_100a) quantized MoE expert forward.
+ *
+ * Drop-in boundary for CostCut-Infer's MoE expert path.  The reference is pure Python
+ * (numpy + numba) and has no native FFI; each entry point below replaces one Python
+ * function on the path and is bound from Python with ctypes (ccut_b200/_lib.py).
+ * Reference paths are relative to the reference's python/ directory.
+ *
+ * Conventions
+ *   - Every pointer argument is a DEVICE pointer unless stated otherwise.
+ *   - Every entry point returns CCUT_OK (0) or a CCUT_ERR_* code; none aborts or traps.
+ *   - Work is enqueued on `stream` (a cudaStream_t); nothing synchronises the host unless
+ *     stated.  Calls on the same stream are ordered; calls that share a workspace must not
+ *     overlap on different streams.
+ *   - Activations are bf16 bit patterns (uint16_t); routing ids are int32.
+ *   - Hidden, intermediate and every matrix dimension must be multiples of 128.
+ */
+#ifndef CCUT_MOE_H
+#define CCUT_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define CCUT_API __attribute__((visibility("default")))
+#else
+#define CCUT_API
+#endif
+
+typedef struct CUstream_st* ccut_stream_t; /* == cudaStream_t */
+
+/* Status codes.  The Python shim maps them onto the exception classes the reference
+ * raises: INVALID/WORKSPACE -> ValueError (ccut/quant/weight_only.py:46,53,
+ * ccut/quant/method.py:42), UNSUPPORTED -> NotImplementedError (ccut/quant/method.py:115,
+ * ccut/models/generic.py:198, ccut/quant/fp8.py:48), TIMEOUT -> TimeoutError
+ * (ccut/experts/reader.py:327), CUDA/NCCL -> RuntimeError. */
+enum {
+  CCUT_OK = 0,
+  CCUT_ERR_INVALID = 1,
+  CCUT_ERR_UNSUPPORTED = 2,
+  CCUT_ERR_CUDA = 3,
+  CCUT_ERR_WORKSPACE = 4,
+  CCUT_ERR_TIMEOUT = 5,
+  CCUT_ERR_NCCL = 6
+};
+
+/* Weight formats (the reference registers formats as QuantKey names,
+ * ccut/quant/spec.py:72-149; these two are new keys). */
+enum {
+  CCUT_FMT_AWQ_INT4_G128 = 1, /* AWQ: qweight int32 [K,N/8], qzeros int32 [K/128,N/8], scales fp16 [K/128,N] */
+  CCUT_FMT_FP8_E4M3_B128 = 2  /* DeepSeek fp8: weight e4m3 [N,K], scale fp32 [N/128,K/128] */
+};
+
+/* AWQ nibble order inside a 32-bit word. */
+enum { CCUT_NIBBLES_AWQ = 0, CCUT_NIBBLES_SEQUENTIAL = 1 };
+
+/* Routing modes (ccut/blocks/moe.py:71-89 for 0 and 1; 2 has no reference counterpart). */
+enum {
+  CCUT_ROUTE_SOFTMAX_TOPK = 0,  /* norm_topk_prob=False: softmax over E, then top-k */
+  CCUT_ROUTE_TOPK_SOFTMAX = 1,  /* norm_topk_prob=True: top-k of logits, softmax over k */
+  CCUT_ROUTE_SIGMOID_GROUP = 2  /* DeepSeek-V3 grouped sigmoid top-k */
+};
+
+enum { CCUT_OUT_BF16 = 0, CCUT_OUT_F32 = 1 };
+
+typedef struct {
+  int mode;             /* CCUT_ROUTE_* */
+  int top_k;            /* 1..16 */
+  int n_group;          /* sigmoid_group: number of expert groups (E % n_group == 0) */
+  int topk_group;       /* sigmoid_group: groups kept */
+  float routed_scaling; /* sigmoid_group: weight multiplier */
+  const float* bias;    /* sigmoid_group: [E] selection bias, or NULL */
+} ccut_route_params;
+
+/* One MoE layer resident in HBM (replaces the reference's streamed expert reader,
+ * ccut/experts/reader.py:86-334, and the per-call segment reads of
+ * ccut/models/generic.py:389-400).  Shared experts (ccut/models/generic.py:380-385) are
+ * stored after the routed ones as `num_shared_slices` slices of width `inter` each. */
+typedef struct {
+  int format;            /* CCUT_FMT_* */
+  int hidden;            /* H */
+  int inter;             /* I, routed expert intermediate size */
+  int num_experts;       /* E */
+  int num_shared_slices; /* shared-expert intermediate / I (0 = no shared expert) */
+  float shared_gate;     /* multiplier of the shared-expert output (ccut/blocks/moe.py:177-179) */
+  const void* w13;       /* packed gate/up of E + slices experts, ccut_w13_bytes() each */
+  const void* w2;        /* packed down of E + slices experts, ccut_w2_bytes() each */
+  const float* router;   /* fp32 [E, H] router weight (gate_w in ccut/models/generic.py:361) */
+} ccut_moe_layer;
+
+/* ---- misc ---------------------------------------------------------------------- */
+CCUT_API const char* ccut_strerror(int code);
+CCUT_API int ccut_abi_version(void);
+
+/* ---- packing: checkpoint layout (device) -> kernel tile layout (device) ---------- */
+/* Bytes of one packed matrix of K inputs x N outputs. */
+CCUT_API size_t ccut_packed_matrix_bytes(int format, int K, int N);
+/* Bytes of one expert's packed gate+up (K = H, N = I) and down (K = I, N = H). */
+CCUT_API size_t ccut_w13_bytes(int format, int hidden, int inter);
+CCUT_API size_t ccut_w2_bytes(int format, int hidden, int inter);
+
+/* Pack one matrix.  `nmat` = 2 interleaves two matrices (gate = slot 0, up = slot 1)
+ * in one buffer of 2 * ccut_packed_matrix_bytes(); `nmat` = 1 packs a lone matrix.
+ * AWQ: q = qweight [K, N/8], z = qzeros [K/128, N/8], s = scales fp16 [K/128, N].
+ * FP8: q = weight e4m3 [N, K], z unused (NULL), s = scale fp32 [N/128, K/128].
+ * Replaces the load-time layout handling of ccut/quant/method.py:35-43 (create_weights). */
+CCUT_API int ccut_pack_matrix(int format, const void* q, const void* z, const void* s, int K, int N,
+                     int nibble_order, void* dst, int nmat, int slot, ccut_stream_t stream);
+
+/* Debug export: packed matrix -> fp32 [K, N] (in, out), bit-identical to the checkpoint
+ * dequant ((q - z) * s for AWQ; e4m3 * scale for FP8, NaN codes -> NaN).
+ * Replaces ccut/quant/kernels.py:150-171 (fp8_dequant_mat) / :276-295 (int4_dequant_row). */
+CCUT_API int ccut_dequant_matrix(int format, const void* packed, int K, int N, int nmat, int slot,
+                        float* out, ccut_stream_t stream);
+
+/* ---- routing (ccut/models/generic.py:361-362, ccut/blocks/moe.py:46-89) ----------- */
+/* Workspace bytes for ccut_moe_route / ccut_moe_topk with T tokens and E experts. */
+CCUT_API size_t ccut_route_workspace_bytes(int T, int E, int H);
+/* logits = x @ router^T in fp32, then top-k per `rp`.  ids int32 [T, k], weights fp32
+ * [T, k], logits fp32 [T, E] (may be NULL).  Ids are ordered by descending score; ties go
+ * to the lowest expert index. */
+CCUT_API int ccut_moe_route(const uint16_t* x, const float* router, int T, int H, int E,
+                   const ccut_route_params* rp, int32_t* ids, float* weights, float* logits,
+                   void* workspace, size_t ws_bytes, ccut_stream_t stream);
+/* Top-k on precomputed fp32 logits [T, E] (the topk_softmax call of
+ * ccut/blocks/moe.py:71-89). */
+CCUT_API int ccut_moe_topk(const float* logits, int T, int E, const ccut_route_params* rp,
+                  int32_t* ids, float* weights, ccut_stream_t stream);
+
+/* ---- token permutation (ccut/models/generic.py:367-371, ccut/blocks/moe.py:164-170) - */
+/* Sort the T*k (token, slot) pairs by expert, stable in (token, slot) order, and append
+ * `num_shared_slices` blocks of all T tokens.  Outputs (R = T*k + slices*T rows):
+ *   offsets   int32 [E + slices + 1]  first row of each expert
+ *   row_token int32 [R]               token of each row
+ *   row_weight fp32 [R]               routing weight of each row (shared_gate for shared)
+ *   pair_row  int32 [T*k]             row of pair (t, j)
+ * Ids must lie in [0, E).  `workspace` holds ccut_permute_workspace_bytes(E) bytes. */
+CCUT_API size_t ccut_permute_workspace_bytes(int E);
+CCUT_API int ccut_moe_permute(const int32_t* ids, const float* weights, int T, int k, int E,
+                     int num_shared_slices, float shared_gate, int32_t* offsets,
+                     int32_t* row_token, float* row_weight, int32_t* pair_row,
+                     void* workspace, size_t ws_bytes, ccut_stream_t stream);
+
+/* ---- expert FFN (ccut/blocks/moe.py:122-141, ccut/quant/kernels.py:219-231) ------- */
+/* Workspace bytes of ccut_moe_expert_ffn (intermediate activations) for R rows. */
+CCUT_API size_t ccut_expert_ffn_workspace_bytes(const ccut_moe_layer* L, int T, int k);
+/* y_rows fp32 [R, H] = row_weight[r] * down(silu(x_r @ Wg) * (x_r @ Wu)) for every row
+ * produced by ccut_moe_permute, using each row's expert.  `x` is bf16 [T, H]. */
+CCUT_API int ccut_moe_expert_ffn(const ccut_moe_layer* L, const uint16_t* x, int T, int k,
+                        const int32_t* offsets, const int32_t* row_token,
+                        const float* row_weight, float* y_rows, void* workspace,
+                        size_t ws_bytes, ccut_stream_t stream);
+/* Same call restricted to one format (fails with CCUT_ERR_UNSUPPORTED otherwise). */
+CCUT_API int ccut_moe_expert_ffn_w4a16(const ccut_moe_layer* L, const uint16_t* x, int T, int k,
+                              const int32_t* offsets, const int32_t* row_token,
+                              const float* row_weight, float* y_rows, void* workspace,
+                              size_t ws_bytes, ccut_stream_t stream);
+CCUT_API int ccut_moe_expert_ffn_fp8b128(const ccut_moe_layer* L, const uint16_t* x, int T, int k,
+                                const int32_t* offsets, const int32_t* row_token,
+                                const float* row_weight, float* y_rows, void* workspace,
+                                size_t ws_bytes, ccut_stream_t stream);
+
+/* ---- combine (ccut/blocks/moe.py:172-173, ccut/models/generic.py:377-385) --------- */
+/* out[t] = sum_j y_rows[pair_row[t, j]] + sum_s y_rows[T*k + s*T + t], summed in that
+ * order in fp32; written as bf16 or fp32 per `out_dtype`. */
+CCUT_API int ccut_moe_combine(const float* y_rows, const int32_t* pair_row, int T, int k, int H,
+                     int num_shared_slices, void* out, int out_dtype, ccut_stream_t stream);
+
+/* ---- whole layer (ccut/models/generic.py:348-386, moe_forward) --------------------- */
+CCUT_API size_t ccut_moe_forward_workspace_bytes(const ccut_moe_layer* L, int T, int top_k);
+/* route -> permute -> expert FFN -> combine.  ids / weights (may be NULL) receive the
+ * routing decision. */
+CCUT_API int ccut_moe_forward(const ccut_moe_layer* L, const ccut_route_params* rp, const uint16_t* x,
+                     int T, void* out, int out_dtype, int32_t* ids, float* weights,
+                     void* workspace, size_t ws_bytes, ccut_stream_t stream);
+
+/* ---- quant linear (ccut/quant/method.py:45-58, QuantizeMethodBase.apply) ----------- */
+/* y fp32 [M, N] = x [M, K] @ W, W a packed (nmat = 1) matrix; x bf16 [M, K]. */
+CCUT_API size_t ccut_quant_linear_workspace_bytes(int format, int M, int K);
+CCUT_API int ccut_quant_linear(int format, const void* packed, int K, int N, const uint16_t* x, int M,
+                      float* y, void* workspace, size_t ws_bytes, ccut_stream_t stream);
+
+/* ---- diagnostics ------------------------------------------------------------------- */
+/* Device-side status word kept at the start of every workspace: a kernel whose bounded
+ * wait expired stores CCUT_ERR_TIMEOUT there instead of hanging.  Reads it (synchronises
+ * `stream`) and clears it. */
+CCUT_API int ccut_workspace_status(void* workspace, ccut_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CCUT_MOE_H */
