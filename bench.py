@@ -1,0 +1,386 @@
+"""Benchmark of the B200 quantized MoE layer (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+A step is one pass of the MoE layer (route -> permute -> gate/up GEMM -> down GEMM ->
+combine) over one batch of `tokens` seeded synthetic bf16 activations per GPU, with the
+seeded random-init layer resident in HBM.  Under torchrun each rank runs its own batch
+(weak scaling); timing is CUDA events on the launching stream between barrier +
+synchronize fences, max over ranks.
+
+`--impl reference` times the reference algorithm on the host cores instead (the numpy
+oracle port of CostCut-Infer's MoE path: per-call dequant of every touched expert, fp32
+BLAS matmuls, the reference's combine loop) on a bounded token sample; rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+# name -> (config, tokens per GPU, roofline bound of the dominant kernel)
+WORKLOADS = {
+    "cfg1_prefill": ("cfg1", 2048, "tensor"),
+    "cfg1_decode": ("cfg1", 64, "hbm"),
+    "cfg1_decode256": ("cfg1", 256, "hbm"),
+    "cfg0_decode": ("cfg0", 64, "hbm"),
+    "cfg0_decode1": ("cfg0", 1, "hbm"),
+    "cfg0_prefill": ("cfg0", 4096, "tensor"),
+    "cfg3_decode": ("cfg3", 64, "hbm"),
+    "cfg3_prefill": ("cfg3", 4096, "tensor"),
+}
+DEFAULT_WORKLOAD = "cfg1_prefill"
+METRIC = "MoE-layer tokens/s"
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def peaks() -> tuple[dict, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()), "measured"
+        except Exception:
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling while the GPU is under load."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(gpu_index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out = ""
+        sm, smax, reasons = [], None, set()
+        for line in out.strip().splitlines():
+            f = [c.strip() for c in line.split(",")]
+            if len(f) < 7:
+                continue
+            try:
+                sm.append(float(f[0]))
+                smax = float(f[1])
+            except ValueError:
+                continue
+            for name, v in zip(self.NAMES, f[3:7]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ algorithmic counts
+def gate_up_counts(cfg, offsets: np.ndarray) -> tuple[float, float]:
+    """(bytes, flops) of one gate/up launch: weights of experts with rows, rows read once,
+    intermediate rows written once."""
+    from ccut_b200.synthetic import _matrix_bytes
+
+    ne = cfg.num_experts + (cfg.num_shared * cfg.shared_inter // cfg.inter if cfg.num_shared else 0)
+    m = np.diff(offsets[:ne + 1]).astype(np.int64)
+    active = int((m > 0).sum())
+    rows = int(m.sum())
+    wbytes = active * 2 * _matrix_bytes(cfg.fmt, cfg.hidden, cfg.inter)
+    byts = wbytes + rows * cfg.hidden * 2 + rows * cfg.inter * 2
+    flops = 4.0 * rows * cfg.hidden * cfg.inter
+    return float(byts), flops
+
+
+def layer_flops(cfg, T: int) -> float:
+    per_tok = 2 * 3 * cfg.hidden * cfg.inter * cfg.top_k
+    shared = 2 * 3 * cfg.hidden * cfg.shared_inter * cfg.num_shared
+    return float(T * (per_tok + shared) + 2 * T * cfg.num_experts * cfg.hidden)
+
+
+# ------------------------------------------------------------------ CPU (oracle) leg
+def cpu_sample_run(cfg_name: str, T: int, sample: int, steps: int, budget_s: float) -> dict:
+    """Time the oracle port of the reference path on `sample` tokens of the workload."""
+    from oracle import formats, inputs, moe  # the checker; only this leg runs it
+
+    cores = os.cpu_count() or 1
+    try:
+        import torch
+
+        torch.set_num_threads(cores)
+    except Exception:
+        pass
+    cfg = inputs.CONFIGS[cfg_name]
+    lw = inputs.make_layer(cfg, seed=0)
+    xb = lw.make_x(T)[:sample]
+    xf = formats.bf16_bits_to_f32(xb)
+    times = []
+    t_start = time.perf_counter()
+    for _ in range(steps):
+        lw._cache.clear()  # the reference dequantizes every touched expert on every call
+        t0 = time.perf_counter()
+        moe.moe_forward(xf, lw.router, cfg.top_k, cfg.routing, lw.w_lookup, shared=lw.shared_cat(),
+                        route_kw=cfg.route_kw)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s:
+            break
+    med = statistics.median(times)
+    return {
+        "value": sample / med, "unit": "tokens/s", "cores": cores, "kind": "port", "steps_run": len(times),
+        "sample": (f"{sample} of the {T} tokens of {cfg_name}; numpy oracle port of the reference path "
+                   f"(per-call dequant of every touched expert as the reference does, fp32 BLAS on {cores} "
+                   f"threads); median of {len(times)} call(s)"),
+    }
+
+
+def run_reference(args, wl) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cfg_name, T, _ = WORKLOADS[wl]
+    sample = min(T, args.cpu_sample)
+    for _ in range(max(0, min(args.warmup, 1))):
+        cpu_sample_run(cfg_name, T, min(sample, 8), 1, 60)
+    r = cpu_sample_run(cfg_name, T, sample, args.steps, args.cpu_budget)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": r["value"], "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": r["steps_run"], "warmup": args.warmup, "ms_per_step": sample / r["value"] * 1000.0,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(wl, args.gpus, parallelism="host cores"),
+        "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": r["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(wl: str, n: int, parallelism: str) -> dict:
+    from ccut_b200.synthetic import CONFIGS
+
+    cfg_name, T, _ = WORKLOADS[wl]
+    c = CONFIGS[cfg_name]
+    return {
+        "workload": wl, "baseline_config": cfg_name, "tokens_per_gpu": T, "global_tokens": T * n,
+        "format": c.fmt, "hidden": c.hidden, "inter": c.inter, "experts": c.num_experts, "top_k": c.top_k,
+        "shared_experts": c.num_shared, "routing": c.routing, "parallelism": parallelism,
+        "l2": "inputs larger than L2: expert weights "
+              f"{(c.expert_bytes() * c.num_experts + c.shared_bytes()) / 1e6:.0f} MB > 126 MB L2, no flush",
+    }
+
+
+# ------------------------------------------------------------------ GPU leg
+def run_ours(args, wl) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from ccut_b200 import MoeLayer, build
+    from ccut_b200.synthetic import make_layer
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    build.build()
+    cfg_name, T, bound = WORKLOADS[wl]
+    lw = make_layer(cfg_name, seed=0)
+    c = lw.cfg
+    L = MoeLayer(c.fmt, c.hidden, c.inter, c.num_experts, c.top_k, c.routing, lw.router, lw.experts,
+                 shared=lw.shared, shared_inter=c.shared_inter, n_group=c.n_group, topk_group=c.topk_group,
+                 routed_scaling=c.routed_scaling, device=dev)
+    xb_all = lw.make_x(T * world)
+    xb = xb_all[rank * T:(rank + 1) * T]
+    x = torch.from_numpy(xb.view(np.int16)).to(dev).view(torch.bfloat16)
+    del lw
+    use_graph = args.graph == "on" or (args.graph == "auto" and T <= 256)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def step(ev0=None, ev1=None):
+        r = L.route(x)
+        p = L.permute(r)
+        if ev0 is not None:
+            ev0.record()
+        h = L.gate_up(x, p)
+        if ev1 is not None:
+            ev1.record()
+        y = L.down(h, p, T)
+        return L.combine(y, p, T), p
+
+    # warm-up (also sizes every workspace before any capture)
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    _, perm = step()
+    offsets = perm.offsets.cpu().numpy()
+    K = args.steps
+    mk = lambda: torch.cuda.Event(enable_timing=True, external=use_graph)  # noqa: E731
+    ev0 = [mk() for _ in range(K)]
+    ev1 = [mk() for _ in range(K)]
+    graph = None
+    if use_graph:
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            step()  # warm the side stream
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g, stream=s):
+                for i in range(K):
+                    step(ev0[i], ev1[i])
+        torch.cuda.current_stream().wait_stream(s)
+        graph = g
+        graph.replay()
+        torch.cuda.synchronize()
+
+    clocks = ClockSampler(local)
+    t_soak = time.perf_counter()
+    while time.perf_counter() - t_soak < args.soak:  # steady clocks before the timed region
+        if graph is not None:
+            graph.replay()
+        else:
+            step()
+        torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    start.record()
+    if graph is not None:
+        graph.replay()
+    else:
+        for i in range(K):
+            step(ev0[i], ev1[i])
+    end.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms = start.elapsed_time(end)
+    kern_ms = [a.elapsed_time(b) for a, b in zip(ev0, ev1)]
+
+    # end to end: host bf16 in (pinned) -> public forward -> host bf16 out, every step
+    x_pin = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).pin_memory()
+    out_pin = torch.empty((T, c.hidden), dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty_like(x)
+    for _ in range(2):
+        xd.copy_(x_pin, non_blocking=True)
+        out_pin.copy_(L.forward(xd), non_blocking=True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(K):
+        xd.copy_(x_pin, non_blocking=True)
+        out_pin.copy_(L.forward(xd), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    if L.workspace_status() != 0:
+        raise SystemExit("device status word reports an expired wait")
+
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = float(t[0]), float(t[1])
+        kt = torch.tensor([statistics.mean(kern_ms)], device=dev)
+        dist.all_reduce(kt, op=dist.ReduceOp.MAX)
+        kmean = float(kt[0])
+    else:
+        kmean = statistics.mean(kern_ms)
+
+    if rank == 0:
+        pk, src = peaks()
+        byts, flops = gate_up_counts(c, offsets)
+        if bound == "hbm":
+            achieved = byts / (kmean * 1e-3) / 1e9
+            peak = pk.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+            roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                    "traffic": None, "kernel": "moe_gemm_kernel<gate/up>", "algorithmic_bytes_per_launch": byts}
+        else:
+            achieved = flops / (kmean * 1e-3) / 1e12
+            peak = pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+            roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                    "frac": achieved / peak, "traffic": None, "kernel": "moe_gemm_kernel<gate/up>",
+                    "algorithmic_flops_per_launch": flops}
+        roof["peak_source"] = f"{src} (MEASURED_PEAKS.json)" if src == "measured" else "fallback"
+        roof["kernel_ms"] = kmean
+        launches_per_step = 7 + (1 if c.fmt == "fp8_b128" else 0)
+        line = {
+            "metric": METRIC, "value": world * T * K / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16" if c.fmt == "awq_int4_g128" else "f16", "data": "synthetic",
+            "config": workload_config(wl, world, "replicas" if world > 1 else "single"),
+            "roofline": roof,
+            "e2e": {"value": world * T * K / (e2e_ms * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": T * c.hidden * 2, "d2h_bytes_per_step": T * c.hidden * 2},
+            "gpu_launches": launches_per_step * K,
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]},
+            "layer_tflops": layer_flops(c, T) * world * K / (ms * 1e-3) / 1e12,
+            "cuda_graph": use_graph,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            r = cpu_sample_run(cfg_name, T, min(T, args.cpu_sample), 1, args.cpu_budget)
+            line["cpu_baseline"] = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        print(json.dumps(line), flush=True)
+    if graph is not None:
+        del graph
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
+    ap.add_argument("--graph", choices=("auto", "on", "off"), default="auto")
+    ap.add_argument("--soak", type=float, default=1.0, help="untimed seconds of load before timing")
+    ap.add_argument("--cpu-sample", type=int, default=128, help="tokens in the CPU baseline sample")
+    ap.add_argument("--cpu-budget", type=float, default=60.0, help="seconds cap of the CPU timing")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args, args.workload)
+    else:
+        run_ours(args, args.workload)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -62,8 +62,6 @@ int check_route(const ccut_route_params* rp, int E) {
   return CCUT_OK;
 }
 
-int cuda_ok() { return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA; }
-
 int pick_mt(int T, int k, int E) {
   const long rows_per_expert = (long)T * k / (E > 0 ? E : 1);
   return rows_per_expert <= 24 ? 32 : 64;
@@ -115,41 +113,51 @@ FwdScratch carve_fwd(Carver& c, const ccut_moe_layer* L, int T, int k) {
   return s;
 }
 
+int run_gate_up(const ccut_moe_layer* L, const uint16_t* xa, int T, int k, const int32_t* offsets,
+                const int32_t* row_token, uint16_t* hbuf, int* status, cudaStream_t st) {
+  const int fmt = L->format;
+  GemmArgs a{static_cast<const uint8_t*>(L->w13),
+             ccut_w13_bytes(fmt, L->hidden, L->inter),
+             L->hidden,
+             L->inter,
+             xa,
+             L->hidden,
+             row_token,
+             offsets,
+             L->num_experts + L->num_shared_slices,
+             hbuf,
+             L->inter,
+             nullptr,
+             status};
+  return launch_gemm(fmt, kFfn1, pick_mt(T, k, L->num_experts), a, num_sms(), st);
+}
+
+int run_down(const ccut_moe_layer* L, const uint16_t* hbuf, int T, int k, const int32_t* offsets,
+             const float* row_weight, float* y_rows, int* status, cudaStream_t st) {
+  const int fmt = L->format;
+  GemmArgs a{static_cast<const uint8_t*>(L->w2),
+             ccut_w2_bytes(fmt, L->hidden, L->inter),
+             L->inter,
+             L->hidden,
+             hbuf,
+             L->inter,
+             nullptr,
+             offsets,
+             L->num_experts + L->num_shared_slices,
+             y_rows,
+             L->hidden,
+             row_weight,
+             status};
+  return launch_gemm(fmt, kFfn2, pick_mt(T, k, L->num_experts), a, num_sms(), st);
+}
+
 int run_ffn(const ccut_moe_layer* L, const uint16_t* x, const uint16_t* x16, int T, int k, const int32_t* offsets,
             const int32_t* row_token, const float* row_weight, float* y_rows, uint16_t* hbuf, int* status,
             cudaStream_t st) {
-  const int fmt = L->format;
-  const int ne = L->num_experts + L->num_shared_slices;
-  const int mt = pick_mt(T, k, L->num_experts);
-  GemmArgs a1{static_cast<const uint8_t*>(L->w13),
-              ccut_w13_bytes(fmt, L->hidden, L->inter),
-              L->hidden,
-              L->inter,
-              fmt == CCUT_FMT_FP8_E4M3_B128 ? x16 : x,
-              L->hidden,
-              row_token,
-              offsets,
-              ne,
-              hbuf,
-              L->inter,
-              nullptr,
-              status};
-  int rc = launch_gemm(fmt, 0, mt, a1, num_sms(), st);
+  const uint16_t* xa = L->format == CCUT_FMT_FP8_E4M3_B128 ? x16 : x;
+  int rc = run_gate_up(L, xa, T, k, offsets, row_token, hbuf, status, st);
   if (rc) return rc;
-  GemmArgs a2{static_cast<const uint8_t*>(L->w2),
-              ccut_w2_bytes(fmt, L->hidden, L->inter),
-              L->inter,
-              L->hidden,
-              hbuf,
-              L->inter,
-              nullptr,
-              offsets,
-              ne,
-              y_rows,
-              L->hidden,
-              row_weight,
-              status};
-  return launch_gemm(fmt, 1, mt, a2, num_sms(), st);
+  return run_down(L, hbuf, T, k, offsets, row_weight, y_rows, status, st);
 }
 
 }  // namespace
@@ -303,6 +311,46 @@ int ccut_moe_expert_ffn_fp8b128(const ccut_moe_layer* L, const uint16_t* x, int 
                                 size_t ws_bytes, ccut_stream_t stream) {
   if (!L || L->format != CCUT_FMT_FP8_E4M3_B128) return CCUT_ERR_UNSUPPORTED;
   return ccut_moe_expert_ffn(L, x, T, k, offsets, row_token, row_weight, y_rows, workspace, ws_bytes, stream);
+}
+
+size_t ccut_gate_up_workspace_bytes(const ccut_moe_layer* L, int T) {
+  if (check_layer(L) || T < 0) return 0;
+  Carver c(nullptr);
+  c.take<int>(64);
+  if (L->format == CCUT_FMT_FP8_E4M3_B128) c.take<uint16_t>((size_t)T * L->hidden);
+  return c.off;
+}
+
+int ccut_moe_gate_up(const ccut_moe_layer* L, const uint16_t* x, int T, int k, const int32_t* offsets,
+                     const int32_t* row_token, uint16_t* h_rows, void* workspace, size_t ws_bytes,
+                     ccut_stream_t stream) {
+  int rc = check_layer(L);
+  if (rc) return rc;
+  if (T < 0 || k < 1 || k > kMaxTopK || k > L->num_experts) return CCUT_ERR_INVALID;
+  if (T == 0) return CCUT_OK;
+  if (!x || !offsets || !row_token || !h_rows || !workspace) return CCUT_ERR_INVALID;
+  if (ws_bytes < ccut_gate_up_workspace_bytes(L, T)) return CCUT_ERR_WORKSPACE;
+  Carver c(workspace);
+  int* status = c.take<int>(64);
+  const uint16_t* xa = x;
+  if (L->format == CCUT_FMT_FP8_E4M3_B128) {
+    uint16_t* x16 = c.take<uint16_t>((size_t)T * L->hidden);
+    rc = launch_bf16_to_f16(x, x16, (size_t)T * L->hidden, stream);
+    if (rc) return rc;
+    xa = x16;
+  }
+  return run_gate_up(L, xa, T, k, offsets, row_token, h_rows, status, stream);
+}
+
+int ccut_moe_down(const ccut_moe_layer* L, const uint16_t* h_rows, int T, int k, const int32_t* offsets,
+                  const float* row_weight, float* y_rows, void* workspace, size_t ws_bytes, ccut_stream_t stream) {
+  int rc = check_layer(L);
+  if (rc) return rc;
+  if (T < 0 || k < 1 || k > kMaxTopK || k > L->num_experts) return CCUT_ERR_INVALID;
+  if (T == 0) return CCUT_OK;
+  if (!h_rows || !offsets || !row_weight || !y_rows || !workspace) return CCUT_ERR_INVALID;
+  if (ws_bytes < 256) return CCUT_ERR_WORKSPACE;
+  return run_down(L, h_rows, T, k, offsets, row_weight, y_rows, static_cast<int*>(workspace), stream);
 }
 
 int ccut_moe_combine(const float* y_rows, const int32_t* pair_row, int T, int k, int H, int num_shared_slices,

@@ -269,6 +269,27 @@ class MoeLayer:
                   _ptr(perm.row_weight), _ptr(y), _ptr(ws), ws.numel(), _stream())
         return y[:R]
 
+    def gate_up(self, x: torch.Tensor, perm: Permutation, k: int | None = None) -> torch.Tensor:
+        """Intermediate rows h [R, I] (16-bit bit patterns: bf16 for AWQ, f16 for FP8)."""
+        x = self._check_x(x)
+        T = x.shape[0]
+        k = k or self.top_k
+        R = T * k + self.num_slices * T
+        h = torch.empty((max(R, 1), self.inter), dtype=torch.int16, device=self.device)
+        ws = self._workspace("gate_up", self.lib.ccut_gate_up_workspace_bytes(C.byref(self.desc), T))
+        _lib.call("ccut_moe_gate_up", C.byref(self.desc), _ptr(x), T, k, _ptr(perm.offsets), _ptr(perm.row_token),
+                  _ptr(h), _ptr(ws), ws.numel(), _stream())
+        return h[:R]
+
+    def down(self, h: torch.Tensor, perm: Permutation, T: int, k: int | None = None) -> torch.Tensor:
+        k = k or self.top_k
+        R = T * k + self.num_slices * T
+        y = torch.empty((max(R, 1), self.hidden), dtype=torch.float32, device=self.device)
+        ws = self._workspace("down", 256)
+        _lib.call("ccut_moe_down", C.byref(self.desc), _ptr(h), T, k, _ptr(perm.offsets), _ptr(perm.row_weight),
+                  _ptr(y), _ptr(ws), ws.numel(), _stream())
+        return y[:R]
+
     def combine(self, y_rows: torch.Tensor, perm: Permutation, T: int, k: int | None = None,
                 out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
         k = k or self.top_k

@@ -164,6 +164,18 @@ CCUT_API int ccut_moe_expert_ffn_fp8b128(const ccut_moe_layer* L, const uint16_t
                                 const float* row_weight, float* y_rows, void* workspace,
                                 size_t ws_bytes, ccut_stream_t stream);
 
+/* The two halves of ccut_moe_expert_ffn, for callers that schedule them separately.
+ * gate/up: h_rows [R, I] = silu(x_r @ Wg) * (x_r @ Wu), 16-bit (bf16 for AWQ, f16 for FP8)
+ * (ccut/blocks/moe.py:128-136); down: y_rows fp32 [R, H] = row_weight[r] * h_r @ Wd
+ * (ccut/blocks/moe.py:137, ccut/models/generic.py:377-378). */
+CCUT_API size_t ccut_gate_up_workspace_bytes(const ccut_moe_layer* L, int T);
+CCUT_API int ccut_moe_gate_up(const ccut_moe_layer* L, const uint16_t* x, int T, int k,
+                              const int32_t* offsets, const int32_t* row_token, uint16_t* h_rows,
+                              void* workspace, size_t ws_bytes, ccut_stream_t stream);
+CCUT_API int ccut_moe_down(const ccut_moe_layer* L, const uint16_t* h_rows, int T, int k,
+                           const int32_t* offsets, const float* row_weight, float* y_rows,
+                           void* workspace, size_t ws_bytes, ccut_stream_t stream);
+
 /* ---- combine (ccut/blocks/moe.py:172-173, ccut/models/generic.py:377-385) --------- */
 /* out[t] = sum_j y_rows[pair_row[t, j]] + sum_s y_rows[T*k + s*T + t], summed in that
  * order in fp32; written as bf16 or fp32 per `out_dtype`. */

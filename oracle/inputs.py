@@ -1,155 +1,62 @@
-"""Seeded synthetic MoE layers for the benchmark configurations (test infrastructure only).
+"""Seeded synthetic layers viewed through the oracle (test infrastructure only).
 
-No public dataset or checkpoint is involved; these tensors are the whole workload.
-Everything comes from ``numpy.random.default_rng(seed)`` drawn in a fixed order:
-router, routed experts ``0..E-1`` (gate, up, down), shared experts (gate, up, down),
-then activations.  Within one matrix: AWQ ``qweight``, ``qzeros``, ``scales``; FP8
-``weight``, ``scale``.  Distributions:
-
-* router fp32 ``N(0, 0.02)``; activations bf16 ``N(0, 1)`` (fp32 draw rounded to bf16);
-* AWQ nibbles and zero-points uniform in ``[0, 15]`` (uniform 32-bit words), scales
-  fp16 ``|N(0, 0.02)| + 1e-3``;
-* FP8 values ``N(0, 1)`` clipped to +-448 and rounded to e4m3 (nearest-even), block
-  scales fp32 log-uniform in ``[1e-3, 1e-1]``.
+The tensors themselves come from ``ccut_b200.synthetic`` (the seeded random-init
+generator that the benchmark also uses, so the checker and the measured path see the
+same inputs).  This module adds the oracle's fp32 dequant of each matrix
+(``oracle.formats``) and the expert lookup that ``oracle.moe.moe_forward`` consumes.
 """
 
 from __future__ import annotations
 
-import math
-from dataclasses import dataclass, field, replace
-
 import numpy as np
 
+from ccut_b200.synthetic import (  # noqa: F401  (re-exported)
+    CONFIGS,
+    AwqMatrix,
+    ExpertWeights,
+    Fp8Matrix,
+    LayerWeights,
+    MoeLayerConfig,
+    scaled_config,
+)
+from ccut_b200 import synthetic
 from oracle import formats
 
-__all__ = [
-    "MoeLayerConfig",
-    "CONFIGS",
-    "AwqMatrix",
-    "Fp8Matrix",
-    "ExpertWeights",
-    "LayerWeights",
-    "make_layer",
-    "scaled_config",
-]
+__all__ = ["CONFIGS", "MoeLayerConfig", "AwqMatrix", "Fp8Matrix", "ExpertWeights", "OracleLayer", "make_layer",
+           "scaled_config", "dequant"]
 
 
-@dataclass(frozen=True)
-class MoeLayerConfig:
-    name: str
-    hidden: int
-    inter: int
-    num_experts: int
-    top_k: int
-    num_shared: int
-    shared_inter: int
-    fmt: str  # "awq_int4_g128" | "fp8_b128"
-    routing: str  # "softmax_topk" | "topk_softmax" | "sigmoid_group"
-    n_group: int = 1
-    topk_group: int = 1
-    routed_scaling: float = 1.0
-    tokens: tuple = ()
-
-    @property
-    def route_kw(self) -> dict:
-        if self.routing == "sigmoid_group":
-            return {"n_group": self.n_group, "topk_group": self.topk_group, "routed_scaling": self.routed_scaling}
-        return {}
-
-    def expert_bytes(self) -> int:
-        """Algorithmic HBM bytes of one routed expert (weights + scales + zero-points)."""
-        return _matrix_bytes(self.fmt, self.hidden, self.inter) * 2 + _matrix_bytes(self.fmt, self.inter, self.hidden)
-
-    def shared_bytes(self) -> int:
-        return self.num_shared * (
-            _matrix_bytes(self.fmt, self.hidden, self.shared_inter) * 2
-            + _matrix_bytes(self.fmt, self.shared_inter, self.hidden)
-        )
+def dequant(mat) -> np.ndarray:
+    """fp32 [K, N] ([in, out], the layout ``expert_ffn`` consumes) of one checkpoint matrix."""
+    if isinstance(mat, AwqMatrix):
+        return formats.awq_dequant(mat.qweight, mat.qzeros, mat.scales)
+    if isinstance(mat, Fp8Matrix):
+        return np.ascontiguousarray(formats.fp8_block_dequant(mat.weight, mat.scale).T)
+    raise TypeError(f"unknown matrix type {type(mat).__name__}")
 
 
-def _matrix_bytes(fmt: str, k: int, n: int) -> int:
-    if fmt == "awq_int4_g128":
-        groups = k // formats.GROUP
-        return k * n // 2 + groups * n * 2 + groups * n // 2
-    nb, kb = math.ceil(n / formats.BLOCK), math.ceil(k / formats.BLOCK)
-    return k * n + nb * kb * 4
+class OracleLayer:
+    """A ``synthetic.LayerWeights`` plus cached oracle dequant lookups."""
 
+    def __init__(self, lw: LayerWeights):
+        self.lw = lw
+        self._cache: dict = {}
 
-CONFIGS: dict[str, MoeLayerConfig] = {
-    # DeepSeek-V2-Lite MoE layer, AWQ int4 g128
-    "cfg0": MoeLayerConfig("cfg0", 2048, 1408, 64, 6, 2, 1408, "awq_int4_g128", "softmax_topk", tokens=(1, 8, 64)),
-    # same layer, FP8 e4m3 128x128 blocks
-    "cfg1": MoeLayerConfig("cfg1", 2048, 1408, 64, 6, 2, 1408, "fp8_b128", "softmax_topk", tokens=(1, 16, 64, 256, 2048)),
-    # Qwen3-30B-A3B MoE layer (no shared expert), AWQ int4
-    "cfg3": MoeLayerConfig("cfg3", 2048, 768, 128, 8, 0, 0, "awq_int4_g128", "topk_softmax", tokens=(64, 4096)),
-    # DeepSeek-V3 MoE layer, FP8 blocks, grouped sigmoid routing
-    "cfg4": MoeLayerConfig(
-        "cfg4", 7168, 2048, 256, 8, 1, 2048, "fp8_b128", "sigmoid_group",
-        n_group=8, topk_group=4, routed_scaling=2.5, tokens=(256, 4096, 16384),
-    ),
-}
-
-
-def scaled_config(base: str | MoeLayerConfig, **over) -> MoeLayerConfig:
-    """A smaller layer with the same format and routing (for oracle-sized parity tests)."""
-    cfg = CONFIGS[base] if isinstance(base, str) else base
-    return replace(cfg, **over)
-
-
-@dataclass
-class AwqMatrix:
-    """AWQ int4 g128 matrix, [in, out] = [K, N]."""
-
-    qweight: np.ndarray  # int32 [K, N/8]
-    qzeros: np.ndarray  # int32 [K/128, N/8]
-    scales: np.ndarray  # fp16 [K/128, N]
-
-    def dequant(self) -> np.ndarray:  # fp32 [K, N]
-        return formats.awq_dequant(self.qweight, self.qzeros, self.scales)
-
-
-@dataclass
-class Fp8Matrix:
-    """FP8 e4m3 128x128-block matrix, [out, in] = [N, K]."""
-
-    weight: np.ndarray  # uint8 [N, K]
-    scale: np.ndarray  # fp32 [N/128, K/128]
-
-    def dequant(self) -> np.ndarray:  # fp32 [K, N] ([in, out])
-        return np.ascontiguousarray(formats.fp8_block_dequant(self.weight, self.scale).T)
-
-
-@dataclass
-class ExpertWeights:
-    gate: object
-    up: object
-    down: object
-
-    def dequant(self) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
-        """fp32 (wg [H, I], wu [H, I], wd [I, H]) in the [in, out] layout."""
-        return self.gate.dequant(), self.up.dequant(), self.down.dequant()
-
-
-@dataclass
-class LayerWeights:
-    cfg: MoeLayerConfig
-    router: np.ndarray  # fp32 [E, H]
-    experts: list
-    shared: list
-    rng_state: dict = field(repr=False, default_factory=dict)
-    _cache: dict = field(repr=False, default_factory=dict)
+    def __getattr__(self, name):
+        return getattr(self.lw, name)
 
     def w_lookup(self, e: int):
         if e not in self._cache:
-            self._cache[e] = self.experts[e].dequant()
+            ew = self.lw.experts[e]
+            self._cache[e] = (dequant(ew.gate), dequant(ew.up), dequant(ew.down))
         return self._cache[e]
 
     def shared_cat(self):
         """Shared experts as one concatenated SwiGLU MLP (inter = S * shared_inter)."""
-        if not self.shared:
+        if not self.lw.shared:
             return None
         if "shared" not in self._cache:
-            parts = [s.dequant() for s in self.shared]
+            parts = [(dequant(s.gate), dequant(s.up), dequant(s.down)) for s in self.lw.shared]
             self._cache["shared"] = (
                 np.concatenate([p[0] for p in parts], axis=1),
                 np.concatenate([p[1] for p in parts], axis=1),
@@ -157,52 +64,6 @@ class LayerWeights:
             )
         return self._cache["shared"]
 
-    def make_x(self, tokens: int) -> np.ndarray:
-        """bf16 activations (uint16 bit patterns) [tokens, H], drawn after the weights."""
-        rng = np.random.default_rng()
-        rng.bit_generator.state = self.rng_state
-        x = rng.standard_normal((tokens, self.cfg.hidden), dtype=np.float32)
-        return formats.bf16_bits_from_f32(x)
 
-
-def _encode_e4m3(x: np.ndarray) -> np.ndarray:
-    try:  # torch's cast is the same round-to-nearest-even encode, much faster
-        import torch
-
-        return torch.from_numpy(np.ascontiguousarray(x)).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
-    except Exception:  # pragma: no cover - torch is present wherever the tests run
-        return formats.fp8_e4m3_encode(x)
-
-
-def _gen_matrix(rng: np.random.Generator, fmt: str, k: int, n: int):
-    if fmt == "awq_int4_g128":
-        g = k // formats.GROUP
-        qweight = rng.integers(0, 2**32, size=(k, n // 8), dtype=np.uint32).view(np.int32)
-        qzeros = rng.integers(0, 2**32, size=(g, n // 8), dtype=np.uint32).view(np.int32)
-        scales = (np.abs(rng.normal(0.0, 0.02, size=(g, n))) + 1e-3).astype(np.float16)
-        return AwqMatrix(qweight, qzeros, scales)
-    if fmt == "fp8_b128":
-        w = np.clip(rng.standard_normal((n, k), dtype=np.float32), -448.0, 448.0)
-        nb, kb = math.ceil(n / formats.BLOCK), math.ceil(k / formats.BLOCK)
-        scale = np.exp(rng.uniform(math.log(1e-3), math.log(1e-1), size=(nb, kb))).astype(np.float32)
-        return Fp8Matrix(_encode_e4m3(w), scale)
-    raise ValueError(f"unknown format {fmt!r}")
-
-
-def _gen_expert(rng, fmt: str, hidden: int, inter: int) -> ExpertWeights:
-    gate = _gen_matrix(rng, fmt, hidden, inter)
-    up = _gen_matrix(rng, fmt, hidden, inter)
-    down = _gen_matrix(rng, fmt, inter, hidden)
-    return ExpertWeights(gate, up, down)
-
-
-def make_layer(cfg: str | MoeLayerConfig, seed: int = 0) -> LayerWeights:
-    """Generate one MoE layer's weights (host, checkpoint layouts) from ``seed``."""
-    cfg = CONFIGS[cfg] if isinstance(cfg, str) else cfg
-    if cfg.hidden % formats.GROUP or cfg.inter % formats.GROUP:
-        raise ValueError("hidden and inter must be multiples of 128")
-    rng = np.random.default_rng(seed)
-    router = rng.normal(0.0, 0.02, size=(cfg.num_experts, cfg.hidden)).astype(np.float32)
-    experts = [_gen_expert(rng, cfg.fmt, cfg.hidden, cfg.inter) for _ in range(cfg.num_experts)]
-    shared = [_gen_expert(rng, cfg.fmt, cfg.hidden, cfg.shared_inter) for _ in range(cfg.num_shared)]
-    return LayerWeights(cfg, router, experts, shared, rng_state=rng.bit_generator.state)
+def make_layer(cfg, seed: int = 0) -> OracleLayer:
+    return OracleLayer(synthetic.make_layer(cfg, seed))

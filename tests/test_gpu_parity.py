@@ -45,7 +45,7 @@ def test_dequant_export_bit_exact(fmt, order):
         deq = lambda m: formats.awq_dequant(m.qweight, m.qzeros, m.scales, order="sequential")  # noqa: E731
     else:
         L = gpu_layer(lw)
-        deq = lambda m: m.dequant()  # noqa: E731
+        deq = inputs.dequant
     for e, ew in enumerate(lw.experts + lw.shared):
         for which in ("gate", "up", "down"):
             ref = deq(getattr(ew, which)).astype(np.float32)
