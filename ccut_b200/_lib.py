@@ -19,10 +19,12 @@ LIB_PATH = Path(os.environ.get("CCUT_B200_LIB", _PKG / "_build" / "libccut_moe.s
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE, ERR_TIMEOUT, ERR_NCCL = range(7)
 FMT_AWQ_INT4_G128, FMT_FP8_E4M3_B128 = 1, 2
 NIBBLES_AWQ, NIBBLES_SEQUENTIAL = 0, 1
+LAYOUT_ROWS, LAYOUT_FRAGS = 0, 1
 ROUTE_SOFTMAX_TOPK, ROUTE_TOPK_SOFTMAX, ROUTE_SIGMOID_GROUP = 0, 1, 2
 OUT_BF16, OUT_F32 = 0, 1
 
 FORMATS = {"awq_int4_g128": FMT_AWQ_INT4_G128, "fp8_b128": FMT_FP8_E4M3_B128}
+LAYOUTS = {"rows": LAYOUT_ROWS, "frags": LAYOUT_FRAGS}
 ROUTING = {"softmax_topk": ROUTE_SOFTMAX_TOPK, "topk_softmax": ROUTE_TOPK_SOFTMAX, "sigmoid_group": ROUTE_SIGMOID_GROUP}
 
 _vp, _sz, _i, _f = C.c_void_p, C.c_size_t, C.c_int, C.c_float
@@ -37,7 +39,7 @@ class RouteParams(C.Structure):
 
 class MoeLayerDesc(C.Structure):
     _fields_ = [
-        ("format", _i), ("hidden", _i), ("inter", _i), ("num_experts", _i),
+        ("format", _i), ("layout", _i), ("hidden", _i), ("inter", _i), ("num_experts", _i),
         ("num_shared_slices", _i), ("shared_gate", _f),
         ("w13", _vp), ("w2", _vp), ("router", _vp),
     ]
@@ -50,8 +52,8 @@ SIGNATURES: dict[str, tuple] = {
     "ccut_packed_matrix_bytes": (_sz, [_i, _i, _i]),
     "ccut_w13_bytes": (_sz, [_i, _i, _i]),
     "ccut_w2_bytes": (_sz, [_i, _i, _i]),
-    "ccut_pack_matrix": (_i, [_i, _vp, _vp, _vp, _i, _i, _i, _vp, _i, _i, _vp]),
-    "ccut_dequant_matrix": (_i, [_i, _vp, _i, _i, _i, _i, _vp, _vp]),
+    "ccut_pack_matrix": (_i, [_i, _i, _vp, _vp, _vp, _i, _i, _i, _vp, _i, _i, _vp]),
+    "ccut_dequant_matrix": (_i, [_i, _i, _vp, _i, _i, _i, _i, _vp, _vp]),
     "ccut_route_workspace_bytes": (_sz, [_i, _i, _i]),
     "ccut_moe_route": (_i, [_vp, _vp, _i, _i, _i, C.POINTER(RouteParams), _vp, _vp, _vp, _vp, _sz, _vp]),
     "ccut_moe_topk": (_i, [_vp, _i, _i, C.POINTER(RouteParams), _vp, _vp, _vp]),
@@ -69,7 +71,7 @@ SIGNATURES: dict[str, tuple] = {
     "ccut_moe_forward": (_i, [C.POINTER(MoeLayerDesc), C.POINTER(RouteParams), _vp, _i, _vp, _i, _vp, _vp, _vp, _sz,
                               _vp]),
     "ccut_quant_linear_workspace_bytes": (_sz, [_i, _i, _i]),
-    "ccut_quant_linear": (_i, [_i, _vp, _i, _i, _vp, _i, _vp, _vp, _sz, _vp]),
+    "ccut_quant_linear": (_i, [_i, _i, _vp, _i, _i, _vp, _i, _vp, _vp, _sz, _vp]),
     "ccut_workspace_status": (_i, [_vp, _vp]),
 }
 

@@ -41,6 +41,7 @@ bool valid_fmt(int f) { return f == CCUT_FMT_AWQ_INT4_G128 || f == CCUT_FMT_FP8_
 int check_layer(const ccut_moe_layer* L) {
   if (!L) return CCUT_ERR_INVALID;
   if (!valid_fmt(L->format)) return CCUT_ERR_UNSUPPORTED;
+  if (L->layout != CCUT_LAYOUT_ROWS && L->layout != CCUT_LAYOUT_FRAGS) return CCUT_ERR_UNSUPPORTED;
   if (L->hidden <= 0 || L->inter <= 0 || L->hidden % 128 || L->inter % 128) return CCUT_ERR_INVALID;
   if (L->num_experts < 1 || L->num_experts > kMaxRoutedExperts) return CCUT_ERR_UNSUPPORTED;
   if (L->num_shared_slices < 0 || L->num_experts + L->num_shared_slices > kMaxExperts) return CCUT_ERR_UNSUPPORTED;
@@ -67,16 +68,24 @@ int pick_mt(int T, int k, int E) {
   return rows_per_expert <= 24 ? 32 : 64;
 }
 
-// Expert-FFN scratch: f16 copy of x (FP8), intermediate rows.
+// Expert-FFN scratch.  Row layout (tcgen05): xp = f16 activations gathered in expert
+// order [R, H].  Fragment layout (mma.sync): x16 = f16 copy of x [T, H] for FP8 only.
+// Both: intermediate rows [R, I] (16-bit).
 struct FfnScratch {
   uint16_t* x16;
+  uint16_t* xp;
   uint16_t* hbuf;
 };
 
-FfnScratch carve_ffn(Carver& c, const ccut_moe_layer* L, int T, int k, bool need_x16) {
-  const size_t R = (size_t)T * k + (size_t)L->num_shared_slices * T;
-  FfnScratch s;
-  s.x16 = need_x16 ? c.take<uint16_t>((size_t)T * L->hidden) : nullptr;
+size_t rows_of(const ccut_moe_layer* L, int T, int k) { return (size_t)T * k + (size_t)L->num_shared_slices * T; }
+
+FfnScratch carve_ffn(Carver& c, const ccut_moe_layer* L, int T, int k, bool with_input) {
+  const size_t R = rows_of(L, T, k);
+  FfnScratch s{nullptr, nullptr, nullptr};
+  if (with_input) {
+    if (L->layout == CCUT_LAYOUT_ROWS) s.xp = c.take<uint16_t>(R * L->hidden);
+    else if (L->format == CCUT_FMT_FP8_E4M3_B128) s.x16 = c.take<uint16_t>((size_t)T * L->hidden);
+  }
   s.hbuf = c.take<uint16_t>(R * L->inter);
   return s;
 }
@@ -108,23 +117,43 @@ FwdScratch carve_fwd(Carver& c, const ccut_moe_layer* L, int T, int k) {
   s.row_token = c.take<int32_t>(R);
   s.row_weight = c.take<float>(R);
   s.pair_row = c.take<int32_t>((size_t)T * k);
-  s.ffn = carve_ffn(c, L, T, k, L->format == CCUT_FMT_FP8_E4M3_B128);
+  s.ffn = carve_ffn(c, L, T, k, true);
   s.ybuf = c.take<float>(R * H);
   return s;
 }
 
-int run_gate_up(const ccut_moe_layer* L, const uint16_t* xa, int T, int k, const int32_t* offsets,
-                const int32_t* row_token, uint16_t* hbuf, int* status, cudaStream_t st) {
+int token_tile(const ccut_moe_layer* L, int T, int k) {
+  const long per_expert = (long)T * k / (L->num_experts > 0 ? L->num_experts : 1);
+  return tc_token_tile(static_cast<int>(per_expert));
+}
+
+// gate/up: h rows [R, I] from x.  `x16` is the fragment path's f16 copy of x (FP8 only);
+// `xp` the row path's gather buffer.
+int run_gate_up(const ccut_moe_layer* L, const uint16_t* x, const uint16_t* x16, uint16_t* xp, int T, int k,
+                const int32_t* offsets, const int32_t* row_token, uint16_t* hbuf, int* status, cudaStream_t st) {
   const int fmt = L->format;
+  const int ne = L->num_experts + L->num_shared_slices;
+  if (L->layout == CCUT_LAYOUT_ROWS) {
+    const int R = static_cast<int>(rows_of(L, T, k));
+    int rc = launch_gather_f16(x, row_token, R, L->hidden, xp, st);
+    if (rc) return rc;
+    const int nt = token_tile(L, T, k);
+    CUtensorMap map;
+    rc = encode_rows_map(&map, xp, R, L->hidden, nt);
+    if (rc) return rc;
+    TcArgs a{static_cast<const uint8_t*>(L->w13), ccut_w13_bytes(fmt, L->hidden, L->inter), L->hidden, L->inter,
+             offsets, ne, hbuf, L->inter, nullptr, status};
+    return launch_tc_gemm(fmt, kFfn1, nt, map, a, num_sms(), st);
+  }
   GemmArgs a{static_cast<const uint8_t*>(L->w13),
              ccut_w13_bytes(fmt, L->hidden, L->inter),
              L->hidden,
              L->inter,
-             xa,
+             fmt == CCUT_FMT_FP8_E4M3_B128 ? x16 : x,
              L->hidden,
              row_token,
              offsets,
-             L->num_experts + L->num_shared_slices,
+             ne,
              hbuf,
              L->inter,
              nullptr,
@@ -135,6 +164,17 @@ int run_gate_up(const ccut_moe_layer* L, const uint16_t* xa, int T, int k, const
 int run_down(const ccut_moe_layer* L, const uint16_t* hbuf, int T, int k, const int32_t* offsets,
              const float* row_weight, float* y_rows, int* status, cudaStream_t st) {
   const int fmt = L->format;
+  const int ne = L->num_experts + L->num_shared_slices;
+  if (L->layout == CCUT_LAYOUT_ROWS) {
+    const int R = static_cast<int>(rows_of(L, T, k));
+    const int nt = token_tile(L, T, k);
+    CUtensorMap map;
+    int rc = encode_rows_map(&map, hbuf, R, L->inter, nt);
+    if (rc) return rc;
+    TcArgs a{static_cast<const uint8_t*>(L->w2), ccut_w2_bytes(fmt, L->hidden, L->inter), L->inter, L->hidden,
+             offsets, ne, y_rows, L->hidden, row_weight, status};
+    return launch_tc_gemm(fmt, kFfn2, nt, map, a, num_sms(), st);
+  }
   GemmArgs a{static_cast<const uint8_t*>(L->w2),
              ccut_w2_bytes(fmt, L->hidden, L->inter),
              L->inter,
@@ -143,7 +183,7 @@ int run_down(const ccut_moe_layer* L, const uint16_t* hbuf, int T, int k, const 
              L->inter,
              nullptr,
              offsets,
-             L->num_experts + L->num_shared_slices,
+             ne,
              y_rows,
              L->hidden,
              row_weight,
@@ -151,13 +191,11 @@ int run_down(const ccut_moe_layer* L, const uint16_t* hbuf, int T, int k, const 
   return launch_gemm(fmt, kFfn2, pick_mt(T, k, L->num_experts), a, num_sms(), st);
 }
 
-int run_ffn(const ccut_moe_layer* L, const uint16_t* x, const uint16_t* x16, int T, int k, const int32_t* offsets,
-            const int32_t* row_token, const float* row_weight, float* y_rows, uint16_t* hbuf, int* status,
-            cudaStream_t st) {
-  const uint16_t* xa = L->format == CCUT_FMT_FP8_E4M3_B128 ? x16 : x;
-  int rc = run_gate_up(L, xa, T, k, offsets, row_token, hbuf, status, st);
+int run_ffn(const ccut_moe_layer* L, const uint16_t* x, const FfnScratch& s, int T, int k, const int32_t* offsets,
+            const int32_t* row_token, const float* row_weight, float* y_rows, int* status, cudaStream_t st) {
+  int rc = run_gate_up(L, x, s.x16, s.xp, T, k, offsets, row_token, s.hbuf, status, st);
   if (rc) return rc;
-  return run_down(L, hbuf, T, k, offsets, row_weight, y_rows, status, st);
+  return run_down(L, s.hbuf, T, k, offsets, row_weight, y_rows, status, st);
 }
 
 }  // namespace
@@ -191,24 +229,26 @@ size_t ccut_w13_bytes(int format, int hidden, int inter) { return 2 * ccut_packe
 
 size_t ccut_w2_bytes(int format, int hidden, int inter) { return ccut_packed_matrix_bytes(format, inter, hidden); }
 
-int ccut_pack_matrix(int format, const void* q, const void* z, const void* s, int K, int N, int nibble_order,
-                     void* dst, int nmat, int slot, ccut_stream_t stream) {
+int ccut_pack_matrix(int format, int layout, const void* q, const void* z, const void* s, int K, int N,
+                     int nibble_order, void* dst, int nmat, int slot, ccut_stream_t stream) {
   if (!valid_fmt(format)) return CCUT_ERR_UNSUPPORTED;
+  if (layout != CCUT_LAYOUT_ROWS && layout != CCUT_LAYOUT_FRAGS) return CCUT_ERR_UNSUPPORTED;
   if (!q || !s || !dst || K <= 0 || N <= 0 || K % 128 || N % 128) return CCUT_ERR_INVALID;
   if (nmat < 1 || nmat > 2 || slot < 0 || slot >= nmat) return CCUT_ERR_INVALID;
   if (format == CCUT_FMT_AWQ_INT4_G128) {
     if (!z) return CCUT_ERR_INVALID;
     if (nibble_order != CCUT_NIBBLES_AWQ && nibble_order != CCUT_NIBBLES_SEQUENTIAL) return CCUT_ERR_INVALID;
   }
-  return launch_pack(format, q, z, s, K, N, nibble_order, dst, nmat, slot, stream);
+  return launch_pack(format, layout, q, z, s, K, N, nibble_order, dst, nmat, slot, stream);
 }
 
-int ccut_dequant_matrix(int format, const void* packed, int K, int N, int nmat, int slot, float* out,
+int ccut_dequant_matrix(int format, int layout, const void* packed, int K, int N, int nmat, int slot, float* out,
                         ccut_stream_t stream) {
   if (!valid_fmt(format)) return CCUT_ERR_UNSUPPORTED;
+  if (layout != CCUT_LAYOUT_ROWS && layout != CCUT_LAYOUT_FRAGS) return CCUT_ERR_UNSUPPORTED;
   if (!packed || !out || K <= 0 || N <= 0 || K % 128 || N % 128) return CCUT_ERR_INVALID;
   if (nmat < 1 || nmat > 2 || slot < 0 || slot >= nmat) return CCUT_ERR_INVALID;
-  return launch_dequant(format, packed, K, N, nmat, slot, out, stream);
+  return launch_dequant(format, layout, packed, K, N, nmat, slot, out, stream);
 }
 
 size_t ccut_route_workspace_bytes(int T, int E, int H) {
@@ -275,7 +315,7 @@ size_t ccut_expert_ffn_workspace_bytes(const ccut_moe_layer* L, int T, int k) {
   if (check_layer(L) || T < 0 || k < 1) return 0;
   Carver c(nullptr);
   c.take<int>(64);
-  carve_ffn(c, L, T, k, L->format == CCUT_FMT_FP8_E4M3_B128);
+  carve_ffn(c, L, T, k, true);
   return c.off;
 }
 
@@ -290,13 +330,12 @@ int ccut_moe_expert_ffn(const ccut_moe_layer* L, const uint16_t* x, int T, int k
   if (ws_bytes < ccut_expert_ffn_workspace_bytes(L, T, k)) return CCUT_ERR_WORKSPACE;
   Carver c(workspace);
   int* status = c.take<int>(64);
-  const bool fp8 = L->format == CCUT_FMT_FP8_E4M3_B128;
-  FfnScratch s = carve_ffn(c, L, T, k, fp8);
-  if (fp8) {
+  FfnScratch s = carve_ffn(c, L, T, k, true);
+  if (s.x16) {
     rc = launch_bf16_to_f16(x, s.x16, (size_t)T * L->hidden, stream);
     if (rc) return rc;
   }
-  return run_ffn(L, x, s.x16, T, k, offsets, row_token, row_weight, y_rows, s.hbuf, status, stream);
+  return run_ffn(L, x, s, T, k, offsets, row_token, row_weight, y_rows, status, stream);
 }
 
 int ccut_moe_expert_ffn_w4a16(const ccut_moe_layer* L, const uint16_t* x, int T, int k, const int32_t* offsets,
@@ -317,7 +356,9 @@ size_t ccut_gate_up_workspace_bytes(const ccut_moe_layer* L, int T) {
   if (check_layer(L) || T < 0) return 0;
   Carver c(nullptr);
   c.take<int>(64);
-  if (L->format == CCUT_FMT_FP8_E4M3_B128) c.take<uint16_t>((size_t)T * L->hidden);
+  // sized for the largest top_k so that one workspace serves any call
+  if (L->layout == CCUT_LAYOUT_ROWS) c.take<uint16_t>(rows_of(L, T, kMaxTopK) * L->hidden);
+  else if (L->format == CCUT_FMT_FP8_E4M3_B128) c.take<uint16_t>((size_t)T * L->hidden);
   return c.off;
 }
 
@@ -332,14 +373,16 @@ int ccut_moe_gate_up(const ccut_moe_layer* L, const uint16_t* x, int T, int k, c
   if (ws_bytes < ccut_gate_up_workspace_bytes(L, T)) return CCUT_ERR_WORKSPACE;
   Carver c(workspace);
   int* status = c.take<int>(64);
-  const uint16_t* xa = x;
-  if (L->format == CCUT_FMT_FP8_E4M3_B128) {
-    uint16_t* x16 = c.take<uint16_t>((size_t)T * L->hidden);
+  uint16_t* xp = nullptr;
+  uint16_t* x16 = nullptr;
+  if (L->layout == CCUT_LAYOUT_ROWS) {
+    xp = c.take<uint16_t>(rows_of(L, T, kMaxTopK) * L->hidden);
+  } else if (L->format == CCUT_FMT_FP8_E4M3_B128) {
+    x16 = c.take<uint16_t>((size_t)T * L->hidden);
     rc = launch_bf16_to_f16(x, x16, (size_t)T * L->hidden, stream);
     if (rc) return rc;
-    xa = x16;
   }
-  return run_gate_up(L, xa, T, k, offsets, row_token, h_rows, status, stream);
+  return run_gate_up(L, x, x16, xp, T, k, offsets, row_token, h_rows, status, stream);
 }
 
 int ccut_moe_down(const ccut_moe_layer* L, const uint16_t* h_rows, int T, int k, const int32_t* offsets,
@@ -387,13 +430,13 @@ int ccut_moe_forward(const ccut_moe_layer* L, const ccut_route_params* rp, const
   Carver c(workspace);
   FwdScratch s = carve_fwd(c, L, T, k);
   cudaStream_t st = stream;
-  rc = launch_route(x, L->router, T, H, E, *rp, s.ids, s.wts, nullptr, s.part, s.counts, s.ffn.x16, st);
+  rc = launch_route(x, L->router, T, H, E, *rp, s.ids, s.wts, nullptr, s.part, s.counts, s.ffn.x16, st);  // x16: FP8 fragment path
   if (rc) return rc;
   if (cudaMemsetAsync(s.pair_row, 0xFF, sizeof(int32_t) * (size_t)T * k, st) != cudaSuccess) return CCUT_ERR_CUDA;
   rc = launch_permute(s.ids, s.wts, T, k, E, L->num_shared_slices, L->shared_gate, s.counts, s.offsets, s.row_token,
                       s.row_weight, s.pair_row, st);
   if (rc) return rc;
-  rc = run_ffn(L, x, s.ffn.x16, T, k, s.offsets, s.row_token, s.row_weight, s.ybuf, s.ffn.hbuf, s.status, st);
+  rc = run_ffn(L, x, s.ffn, T, k, s.offsets, s.row_token, s.row_weight, s.ybuf, s.status, st);
   if (rc) return rc;
   rc = launch_combine(s.ybuf, s.pair_row, T, k, H, L->num_shared_slices, out, out_dtype, st);
   if (rc) return rc;
@@ -410,13 +453,14 @@ size_t ccut_quant_linear_workspace_bytes(int format, int M, int K) {
   Carver c(nullptr);
   c.take<int>(64);
   c.take<int32_t>(2);
-  if (format == CCUT_FMT_FP8_E4M3_B128) c.take<uint16_t>((size_t)M * K);
+  c.take<uint16_t>((size_t)(M > 0 ? M : 1) * K);  // f16 activations (both layouts' FP8, row layout's AWQ)
   return c.off;
 }
 
-int ccut_quant_linear(int format, const void* packed, int K, int N, const uint16_t* x, int M, float* y,
+int ccut_quant_linear(int format, int layout, const void* packed, int K, int N, const uint16_t* x, int M, float* y,
                       void* workspace, size_t ws_bytes, ccut_stream_t stream) {
   if (!valid_fmt(format)) return CCUT_ERR_UNSUPPORTED;
+  if (layout != CCUT_LAYOUT_ROWS && layout != CCUT_LAYOUT_FRAGS) return CCUT_ERR_UNSUPPORTED;
   if (K <= 0 || N <= 0 || K % 128 || N % 128 || M < 0) return CCUT_ERR_INVALID;
   if (M == 0) return CCUT_OK;
   if (!packed || !x || !y || !workspace) return CCUT_ERR_INVALID;
@@ -424,17 +468,27 @@ int ccut_quant_linear(int format, const void* packed, int K, int N, const uint16
   Carver c(workspace);
   int* status = c.take<int>(64);
   int32_t* off = c.take<int32_t>(2);
-  const uint16_t* xa = x;
+  uint16_t* x16 = c.take<uint16_t>((size_t)M * K);
   int rc = launch_fill_offsets(off, M, stream);
   if (rc) return rc;
+  if (layout == CCUT_LAYOUT_ROWS) {
+    rc = launch_gather_f16(x, nullptr, M, K, x16, stream);
+    if (rc) return rc;
+    const int nt = tc_token_tile(M);
+    CUtensorMap map;
+    rc = encode_rows_map(&map, x16, M, K, nt);
+    if (rc) return rc;
+    TcArgs a{static_cast<const uint8_t*>(packed), 0, K, N, off, 1, y, N, nullptr, status};
+    return launch_tc_gemm(format, kFfn2, nt, map, a, num_sms(), stream);
+  }
+  const uint16_t* xa = x;
   if (format == CCUT_FMT_FP8_E4M3_B128) {
-    uint16_t* x16 = c.take<uint16_t>((size_t)M * K);
     rc = launch_bf16_to_f16(x, x16, (size_t)M * K, stream);
     if (rc) return rc;
     xa = x16;
   }
   GemmArgs a{static_cast<const uint8_t*>(packed), 0, K, N, xa, K, nullptr, off, 1, y, N, nullptr, status};
-  return launch_gemm(format, 1, M <= 32 ? 32 : 64, a, num_sms(), stream);
+  return launch_gemm(format, kFfn2, M <= 32 ? 32 : 64, a, num_sms(), stream);
 }
 
 int ccut_workspace_status(void* workspace, ccut_stream_t stream) {

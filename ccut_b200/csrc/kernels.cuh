@@ -22,10 +22,35 @@ struct GemmArgs {
   int* status;
 };
 
+// Arguments of the tcgen05 grouped GEMM (tc_gemm.cu); the activation operand arrives
+// through a TMA tensor map passed separately.
+struct TcArgs {
+  const uint8_t* w;      // packed weights (row layout) of expert 0
+  size_t expert_stride;  // bytes between experts
+  int K, N;              // inputs, outputs of one matrix
+  const int* offsets;    // [num_e + 1] first GEMM row of each expert
+  int num_e;
+  void* out;
+  int out_ld;
+  const float* row_weight;
+  int* status;
+};
+
+// tc_gemm.cu
+int tc_token_tile(int rows_per_expert);
+int launch_tc_gemm(int fmt, int mode, int nt_tokens, const CUtensorMap& map, const TcArgs& a, int num_sms,
+                   cudaStream_t st);
+// tmap.cu: 2-D f16 tensor map over a row-major [rows, cols] buffer, boxes of 64 x box_rows,
+// 128-byte swizzle (host side)
+int encode_rows_map(CUtensorMap* map, const void* base, int rows, int cols, int box_rows);
+int launch_gather_f16(const uint16_t* x_bf16, const int32_t* row_token, int R, int H, uint16_t* xp,
+                      cudaStream_t st);
+
 // pack.cu
-int launch_pack(int fmt, const void* q, const void* z, const void* s, int K, int N, int nibble_order, void* dst,
-                int nmat, int slot, cudaStream_t st);
-int launch_dequant(int fmt, const void* packed, int K, int N, int nmat, int slot, float* out, cudaStream_t st);
+int launch_pack(int fmt, int layout, const void* q, const void* z, const void* s, int K, int N, int nibble_order,
+                void* dst, int nmat, int slot, cudaStream_t st);
+int launch_dequant(int fmt, int layout, const void* packed, int K, int N, int nmat, int slot, float* out,
+                   cudaStream_t st);
 // route.cu
 int route_hsplit(int T, int E, int H);
 int launch_route(const uint16_t* x, const float* router, int T, int H, int E, const ccut_route_params& rp,

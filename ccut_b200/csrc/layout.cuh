@@ -22,6 +22,18 @@
 //                             [16384, 16388) fp32 block scale, 12 bytes padding
 //     bytes [8j, 8j+8) of a lane cover k-step j; byte b is A-tile element
 //     (row g + 8*((b>>1)&1), col 2t + 8*(b>>2) + (b&1)), i.e. byte pair r is A register r.
+//
+// Row layout (CCUT_LAYOUT_ROWS, used by the tcgen05 kernel): the same block sizes, but the
+// weights of each block are stored one output channel per row, so that one dequant thread
+// owns one row (one TMEM lane of the A operand):
+//   AWQ int4: [0, 8192) 128 rows x 64 B; 16-byte chunk c of row r sits at
+//             r*64 + 16*(c ^ ((r >> 1) & 3)); word j of a row covers k = 8j..8j+7 with
+//             nibble slot p holding k = 8j + {0,2,4,6,1,3,5,7}[p], so (w >> 4i) & 0x000F000F
+//             is the pair (8j+2i, 8j+2i+1).  Scales / zero-points as above.
+//   FP8:      [0, 16384) 128 rows x 128 B; chunk c of row r at r*128 + 16*(c ^ (r & 7));
+//             byte b of a row is k = b.  Scale as above.
+// The XOR swizzle makes the eight rows read by each quarter-warp hit eight distinct bank
+// groups.
 #pragma once
 
 #include "common.cuh"
@@ -31,6 +43,23 @@ namespace ccut {
 constexpr int kTileN = 128;  // output channels per block
 constexpr int kTileK = 128;  // inputs per block (= AWQ group = FP8 block)
 constexpr int kMaxExperts = 512;
+
+enum { kLayoutRows = 0, kLayoutFrags = 1 };
+
+// Byte offset, inside a row-layout AWQ block, of the 32-bit word holding element k of row r.
+inline __host__ __device__ int rows_awq_word(int r, int k) {
+  const int j = k >> 3;   // word index within the row
+  const int c = j >> 2;   // 16-byte chunk (4 words)
+  return r * 64 + 16 * (c ^ ((r >> 1) & 3)) + 4 * (j & 3);
+}
+inline __host__ __device__ int rows_awq_slot(int k) {  // nibble slot inside the word
+  const int kk = k & 7;
+  return (kk & 1) ? 4 + (kk >> 1) : (kk >> 1);
+}
+inline __host__ __device__ int rows_fp8_byte(int r, int k) {
+  const int c = k >> 4;
+  return r * 128 + 16 * (c ^ (r & 7)) + (k & 15);
+}
 
 template <int FMT>
 struct Blk;

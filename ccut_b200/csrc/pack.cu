@@ -173,6 +173,112 @@ __global__ void dequant_fp8_kernel(const uint8_t* __restrict__ src, int K, int N
   }
 }
 
+// ---- row layout (tcgen05 kernel) ------------------------------------------------------
+__global__ void pack_awq_rows_kernel(const int32_t* __restrict__ qweight, int K, int N, NibbleOrder ord,
+                                     uint8_t* __restrict__ dst, int nmat, int slot) {
+  constexpr int kWordsPerBlock = kTileN * 16;  // 128 rows x 16 words
+  const int ktiles = K / kTileK;
+  const size_t total = (size_t)(N / kTileN) * ktiles * kWordsPerBlock;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int widx = static_cast<int>(i % kWordsPerBlock);
+    const size_t blk = i / kWordsPerBlock;
+    const int kt = static_cast<int>(blk % ktiles);
+    const int nt = static_cast<int>(blk / ktiles);
+    const int r = widx >> 4, j = widx & 15;
+    const int n = nt * kTileN + r;
+    uint32_t word = 0;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const int k = kt * kTileK + 8 * j + kk;
+      word |= awq_get(qweight, N / 8, k, n, ord.slot_of_col) << (4 * rows_awq_slot(kk));
+    }
+    uint8_t* b = dst + block_offset(CCUT_FMT_AWQ_INT4_G128, nt, kt, slot, ktiles, nmat);
+    *reinterpret_cast<uint32_t*>(b + rows_awq_word(r, 8 * j)) = word;
+  }
+}
+
+__global__ void pack_fp8_rows_kernel(const uint8_t* __restrict__ w, const float* __restrict__ scale, int K, int N,
+                                     uint8_t* __restrict__ dst, int nmat, int slot) {
+  using B = Blk<CCUT_FMT_FP8_E4M3_B128>;
+  constexpr int kChunksPerBlock = kTileN * 8;  // 128 rows x 8 chunks of 16 bytes
+  const int ktiles = K / kTileK;
+  const size_t total = (size_t)(N / kTileN) * ktiles * kChunksPerBlock;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int cidx = static_cast<int>(i % kChunksPerBlock);
+    const size_t blk = i / kChunksPerBlock;
+    const int kt = static_cast<int>(blk % ktiles);
+    const int nt = static_cast<int>(blk / ktiles);
+    const int r = cidx >> 3, c = cidx & 7;
+    const int n = nt * kTileN + r;
+    const uint4 v = *reinterpret_cast<const uint4*>(w + (size_t)n * K + kt * kTileK + 16 * c);
+    uint8_t* b = dst + block_offset(CCUT_FMT_FP8_E4M3_B128, nt, kt, slot, ktiles, nmat);
+    *reinterpret_cast<uint4*>(b + rows_fp8_byte(r, 16 * c)) = v;
+    if (cidx == 0) {
+      float* s = reinterpret_cast<float*>(b + B::kScaleOff);
+      s[0] = scale[(size_t)nt * ktiles + kt];
+      s[1] = 0.f;
+      s[2] = 0.f;
+      s[3] = 0.f;
+    }
+  }
+}
+
+__global__ void dequant_awq_rows_kernel(const uint8_t* __restrict__ src, int K, int N, int nmat, int slot,
+                                        float* __restrict__ out) {
+  using B = Blk<CCUT_FMT_AWQ_INT4_G128>;
+  constexpr int kWordsPerBlock = kTileN * 16;
+  const int ktiles = K / kTileK;
+  const size_t total = (size_t)(N / kTileN) * ktiles * kWordsPerBlock;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int widx = static_cast<int>(i % kWordsPerBlock);
+    const size_t blk = i / kWordsPerBlock;
+    const int kt = static_cast<int>(blk % ktiles);
+    const int nt = static_cast<int>(blk / ktiles);
+    const int r = widx >> 4, j = widx & 15;
+    const uint8_t* b = src + block_offset(CCUT_FMT_AWQ_INT4_G128, nt, kt, slot, ktiles, nmat);
+    const uint32_t word = *reinterpret_cast<const uint32_t*>(b + rows_awq_word(r, 8 * j));
+    const uint32_t z = (b[B::kZeroOff + (r >> 1)] >> (4 * (r & 1))) & 0xF;
+    const float s = __half2float(__ushort_as_half(reinterpret_cast<const uint16_t*>(b + B::kScaleOff)[r]));
+    const int n = nt * kTileN + r;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const uint32_t q = (word >> (4 * rows_awq_slot(kk))) & 0xF;
+      const int k = kt * kTileK + 8 * j + kk;
+      out[(size_t)k * N + n] = __fmul_rn(__fsub_rn((float)q, (float)z), s);
+    }
+  }
+}
+
+__global__ void dequant_fp8_rows_kernel(const uint8_t* __restrict__ src, int K, int N, int nmat, int slot,
+                                        float* __restrict__ out) {
+  using B = Blk<CCUT_FMT_FP8_E4M3_B128>;
+  constexpr int kChunksPerBlock = kTileN * 8;
+  const int ktiles = K / kTileK;
+  const size_t total = (size_t)(N / kTileN) * ktiles * kChunksPerBlock;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int cidx = static_cast<int>(i % kChunksPerBlock);
+    const size_t blk = i / kChunksPerBlock;
+    const int kt = static_cast<int>(blk % ktiles);
+    const int nt = static_cast<int>(blk / ktiles);
+    const int r = cidx >> 3, c = cidx & 7;
+    const uint8_t* b = src + block_offset(CCUT_FMT_FP8_E4M3_B128, nt, kt, slot, ktiles, nmat);
+    const uint4 v = *reinterpret_cast<const uint4*>(b + rows_fp8_byte(r, 16 * c));
+    const float s = reinterpret_cast<const float*>(b + B::kScaleOff)[0];
+    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+    const int n = nt * kTileN + r;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const uint32_t h2 = e4m3x2_to_f16x2(static_cast<uint16_t>(w4[q >> 1] >> (16 * (q & 1))));
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int k = kt * kTileK + 16 * c + 2 * q + e;
+        const float val = __half2float(__ushort_as_half(static_cast<uint16_t>(h2 >> (16 * e))));
+        out[(size_t)k * N + n] = __fmul_rn(val, s);
+      }
+    }
+  }
+}
+
 static int grid_for(size_t total, int threads) {
   size_t g = (total + threads - 1) / threads;
   if (g > 148 * 32) g = 148 * 32;
@@ -186,10 +292,28 @@ static NibbleOrder make_order(int nibble_order) {
   return o;
 }
 
-int launch_pack(int fmt, const void* q, const void* z, const void* s, int K, int N, int nibble_order, void* dst,
-                int nmat, int slot, cudaStream_t st) {
+int launch_pack(int fmt, int layout, const void* q, const void* z, const void* s, int K, int N, int nibble_order,
+                void* dst, int nmat, int slot, cudaStream_t st) {
   const int threads = 256;
   const int ktiles = K / kTileK, ntiles = N / kTileN;
+  if (layout == kLayoutRows) {
+    if (fmt == CCUT_FMT_AWQ_INT4_G128) {
+      NibbleOrder o = make_order(nibble_order);
+      size_t t1 = (size_t)ntiles * ktiles * kTileN * 16;
+      pack_awq_rows_kernel<<<grid_for(t1, threads), threads, 0, st>>>(static_cast<const int32_t*>(q), K, N, o,
+                                                                       static_cast<uint8_t*>(dst), nmat, slot);
+      size_t t2 = (size_t)ntiles * ktiles * (kTileN / 2);
+      pack_awq_meta_kernel<<<grid_for(t2, threads), threads, 0, st>>>(
+          static_cast<const int32_t*>(z), static_cast<const uint16_t*>(s), K, N, o, static_cast<uint8_t*>(dst), nmat,
+          slot);
+    } else {
+      size_t t1 = (size_t)ntiles * ktiles * kTileN * 8;
+      pack_fp8_rows_kernel<<<grid_for(t1, threads), threads, 0, st>>>(static_cast<const uint8_t*>(q),
+                                                                       static_cast<const float*>(s), K, N,
+                                                                       static_cast<uint8_t*>(dst), nmat, slot);
+    }
+    return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
+  }
   if (fmt == CCUT_FMT_AWQ_INT4_G128) {
     NibbleOrder o = make_order(nibble_order);
     size_t t1 = (size_t)ntiles * ktiles * (Blk<CCUT_FMT_AWQ_INT4_G128>::kAtomBytes / 4);
@@ -208,9 +332,22 @@ int launch_pack(int fmt, const void* q, const void* z, const void* s, int K, int
   return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
 }
 
-int launch_dequant(int fmt, const void* packed, int K, int N, int nmat, int slot, float* out, cudaStream_t st) {
+int launch_dequant(int fmt, int layout, const void* packed, int K, int N, int nmat, int slot, float* out,
+                   cudaStream_t st) {
   const int threads = 256;
   const int ktiles = K / kTileK, ntiles = N / kTileN;
+  if (layout == kLayoutRows) {
+    if (fmt == CCUT_FMT_AWQ_INT4_G128) {
+      size_t t = (size_t)ntiles * ktiles * kTileN * 16;
+      dequant_awq_rows_kernel<<<grid_for(t, threads), threads, 0, st>>>(static_cast<const uint8_t*>(packed), K, N,
+                                                                        nmat, slot, out);
+    } else {
+      size_t t = (size_t)ntiles * ktiles * kTileN * 8;
+      dequant_fp8_rows_kernel<<<grid_for(t, threads), threads, 0, st>>>(static_cast<const uint8_t*>(packed), K, N,
+                                                                        nmat, slot, out);
+    }
+    return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
+  }
   if (fmt == CCUT_FMT_AWQ_INT4_G128) {
     size_t t = (size_t)ntiles * ktiles * (Blk<CCUT_FMT_AWQ_INT4_G128>::kAtomBytes / 4);
     dequant_awq_kernel<<<grid_for(t, threads), threads, 0, st>>>(static_cast<const uint8_t*>(packed), K, N, nmat,

@@ -13,9 +13,10 @@
 
 namespace ccut {
 
-constexpr int kRtTok = 16;  // tokens per logits CTA
+constexpr int kRtTok = 64;  // tokens per logits CTA
 constexpr int kRtExp = 64;  // experts per logits CTA
-constexpr int kRtH = 64;    // h per smem chunk
+constexpr int kRtH = 32;    // h per shared-memory chunk
+constexpr int kRtPad = 68;  // padded row (floats): 16-byte aligned float4 reads
 
 // Number of H splits: enough CTAs to cover the SMs at small T, one split at large T.
 int route_hsplit(int T, int E, int H) {
@@ -28,49 +29,87 @@ int route_hsplit(int T, int E, int H) {
   return hs;
 }
 
-// part[hs][t][e]; also zeroes counts[E] and writes x16 (f16 copy of x) when requested.
+// part[hs][t][e] = sum over this split's h of x[t, h] * router[e, h] (fp32).  Also zeroes
+// counts[E] and writes x16 (f16 copy of x) when requested.
 __global__ void __launch_bounds__(256) route_logits_kernel(const uint16_t* __restrict__ x,
                                                            const float* __restrict__ router, int T, int H, int E,
                                                            int hsplit, float* __restrict__ part,
                                                            int* __restrict__ counts, uint16_t* __restrict__ x16) {
-  __shared__ float xs[kRtTok][kRtH];
-  __shared__ float ws[kRtExp][kRtH + 1];
+  __shared__ __align__(16) float xs[kRtH][kRtPad];  // [h][token]
+  __shared__ __align__(16) float ws[kRtH][kRtPad];  // [h][expert]
   const int t0 = blockIdx.x * kRtTok, e0 = blockIdx.y * kRtExp, hs = blockIdx.z;
   const int hlen = H / hsplit, hbeg = hs * hlen;
   const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
   if (counts && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
     for (int e = tid; e < E; e += blockDim.x) counts[e] = 0;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  const int lr = tid >> 2, lseg = tid & 3;  // loader: row (token / expert), 8-wide h segment
   for (int h0 = hbeg; h0 < hbeg + hlen; h0 += kRtH) {
-    for (int i = tid; i < kRtTok * kRtH; i += 256) {
-      const int r = i / kRtH, c = i % kRtH, t = t0 + r;
-      float v = 0.f;
+    {
+      const int t = t0 + lr;
+      float v[8];
       if (t < T) {
-        const uint16_t b = x[(size_t)t * H + h0 + c];
-        v = __uint_as_float(static_cast<uint32_t>(b) << 16);
-        if (x16 && blockIdx.y == 0) x16[(size_t)t * H + h0 + c] = __half_as_ushort(__float2half_rn(v));
+        const uint4 raw = *reinterpret_cast<const uint4*>(x + (size_t)t * H + h0 + lseg * 8);
+        const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          v[2 * j] = __uint_as_float(w4[j] << 16);
+          v[2 * j + 1] = __uint_as_float(w4[j] & 0xffff0000u);
+        }
+        if (x16 && blockIdx.y == 0) {
+          uint32_t o[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const __half2 hh = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+            o[j] = *reinterpret_cast<const uint32_t*>(&hh);
+          }
+          *reinterpret_cast<uint4*>(x16 + (size_t)t * H + h0 + lseg * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = 0.f;
       }
-      xs[r][c] = v;
-    }
-    for (int i = tid; i < kRtExp * kRtH; i += 256) {
-      const int r = i / kRtH, c = i % kRtH, e = e0 + r;
-      ws[r][c] = e < E ? router[(size_t)e * H + h0 + c] : 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) xs[lseg * 8 + j][lr] = v[j];
+      const int e = e0 + lr;
+      float w[8];
+      if (e < E) {
+        const float4 a = *reinterpret_cast<const float4*>(router + (size_t)e * H + h0 + lseg * 8);
+        const float4 b = *reinterpret_cast<const float4*>(router + (size_t)e * H + h0 + lseg * 8 + 4);
+        w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w; w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) w[j] = 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ws[lseg * 8 + j][lr] = w[j];
     }
     __syncthreads();
 #pragma unroll 8
-    for (int c = 0; c < kRtH; ++c) {
-      const float xv = xs[ty][c];
+    for (int h = 0; h < kRtH; ++h) {
+      const float4 xv = *reinterpret_cast<const float4*>(&xs[h][ty * 4]);
+      const float4 wv = *reinterpret_cast<const float4*>(&ws[h][tx * 4]);
+      const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
+      const float wa[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-      for (int j = 0; j < 4; ++j) acc[j] = fmaf(xv, ws[tx + 16 * j][c], acc[j]);
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xa[i], wa[j], acc[i][j]);
     }
     __syncthreads();
   }
-  const int t = t0 + ty;
-  if (t < T) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int t = t0 + ty * 4 + i;
+    if (t >= T) continue;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int e = e0 + tx + 16 * j;
-      if (e < E) part[((size_t)hs * T + t) * E + e] = acc[j];
+      const int e = e0 + tx * 4 + j;
+      if (e < E) part[((size_t)hs * T + t) * E + e] = acc[i][j];
     }
   }
 }
@@ -253,13 +292,18 @@ __global__ void __launch_bounds__(256) route_topk_kernel(const float* __restrict
   }
 }
 
-// One warp per expert: stable compaction of the pairs routed to it.
+// One warp per expert: stable compaction of the pairs routed to it.  The ids are staged
+// through shared memory in chunks so that each warp's scan runs at shared-memory speed
+// instead of waiting on one dependent global load per 32 pairs.
+constexpr int kPermChunk = 8192;
+
 __global__ void __launch_bounds__(256) permute_kernel(const int32_t* __restrict__ ids,
                                                       const float* __restrict__ weights, int T, int k, int E,
                                                       int slices, float shared_gate, const int* __restrict__ counts,
                                                       int32_t* __restrict__ offsets, int32_t* __restrict__ row_token,
                                                       float* __restrict__ row_weight, int32_t* __restrict__ pair_row) {
   __shared__ int cnt[kMaxExperts];
+  __shared__ int16_t sid[kPermChunk];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = counts[e];
   __syncthreads();
@@ -282,24 +326,33 @@ __global__ void __launch_bounds__(256) permute_kernel(const int32_t* __restrict_
     if (lane == 0)
       for (int s = 0; s <= slices; ++s) offsets[E + s] = tk + s * T;
   }
+  int base = 0;
   if (e < E) {
-    int base = 0;
     for (int i = lane; i < e; i += 32) base += cnt[i];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) base += __shfl_xor_sync(0xffffffffu, base, o);
-    int pos = 0;
-    const unsigned lt = (1u << lane) - 1u;
-    for (int i0 = 0; i0 < tk; i0 += 32) {
-      const int i = i0 + lane;
-      const bool m = i < tk && ids[i] == e;
-      const unsigned bal = __ballot_sync(0xffffffffu, m);
-      if (m) {
-        const int p = base + pos + __popc(bal & lt);
-        row_token[p] = i / k;
-        row_weight[p] = weights[i];
-        pair_row[i] = p;
+  }
+  int pos = 0;
+  const unsigned lt = (1u << lane) - 1u;
+  for (int c0 = 0; c0 < tk; c0 += kPermChunk) {
+    const int n = min(kPermChunk, tk - c0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) sid[i] = static_cast<int16_t>(ids[c0 + i]);
+    __syncthreads();
+    if (e < E) {
+      for (int i0 = 0; i0 < n; i0 += 32) {
+        const int i = i0 + lane;
+        const bool m = i < n && sid[i] == e;
+        const unsigned bal = __ballot_sync(0xffffffffu, m);
+        if (m) {
+          const int p = base + pos + __popc(bal & lt);
+          const int gi = c0 + i;
+          row_token[p] = gi / k;
+          row_weight[p] = weights[gi];
+          pair_row[gi] = p;
+        }
+        pos += __popc(bal);
       }
-      pos += __popc(bal);
     }
   }
   // shared-expert rows: every token once per slice

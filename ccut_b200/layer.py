@@ -91,6 +91,7 @@ class MoeLayer:
         routed_scaling: float = 1.0,
         bias: np.ndarray | torch.Tensor | None = None,
         nibble_order: str = "awq",
+        layout: str = "rows",
         device: str | torch.device = "cuda",
     ):
         if fmt not in _lib.FORMATS:
@@ -101,8 +102,11 @@ class MoeLayer:
             raise ValueError("hidden and inter must be multiples of 128")
         if len(experts) != num_experts:
             raise ValueError(f"expected {num_experts} experts, got {len(experts)}")
+        if layout not in _lib.LAYOUTS:
+            raise NotImplementedError(f"packed layout {layout!r} is not supported (have {sorted(_lib.LAYOUTS)})")
         self.lib = _lib.load()
         self.fmt, self.fmt_code = fmt, _lib.FORMATS[fmt]
+        self.layout, self.layout_code = layout, _lib.LAYOUTS[layout]
         self.hidden, self.inter, self.num_experts, self.top_k = hidden, inter, num_experts, top_k
         self.routing = routing
         self.device = torch.device(device)
@@ -135,7 +139,7 @@ class MoeLayer:
                     self._pack_expert(num_experts + j * self.slices_per_shared + s, sw, s * inter, inter)
             torch.cuda.current_stream().synchronize()
         self.desc = _lib.MoeLayerDesc(
-            self.fmt_code, hidden, inter, num_experts, self.num_slices, self.shared_gate,
+            self.fmt_code, self.layout_code, hidden, inter, num_experts, self.num_slices, self.shared_gate,
             _ptr(self.w13), _ptr(self.w2), _ptr(self.router),
         )
         self._ws: dict[str, torch.Tensor] = {}
@@ -164,7 +168,7 @@ class MoeLayer:
             qd, zd, sd = _dev(q, self.device, torch.uint8), None, _dev(s, self.device, torch.float32)
             if tuple(qd.shape) != (N, K) or tuple(sd.shape) != (N // 128, K // 128):
                 raise ValueError(f"{role}: FP8 tensors have shapes w{tuple(qd.shape)} s{tuple(sd.shape)} for K={K} N={N}")
-        _lib.call("ccut_pack_matrix", self.fmt_code, _ptr(qd), _ptr(zd), _ptr(sd), K, N, self.nibbles,
+        _lib.call("ccut_pack_matrix", self.fmt_code, self.layout_code, _ptr(qd), _ptr(zd), _ptr(sd), K, N, self.nibbles,
                   _ptr(dst), nmat, slot, _stream())
 
     def _pack_expert(self, e: int, ew, lo: int, width: int):
@@ -309,5 +313,5 @@ class MoeLayer:
             src = self.w2[expert * self.w2_bytes:(expert + 1) * self.w2_bytes]
             K, N, nmat, slot = I, H, 1, 0
         out = torch.empty((K, N), dtype=torch.float32, device=self.device)
-        _lib.call("ccut_dequant_matrix", self.fmt_code, _ptr(src), K, N, nmat, slot, _ptr(out), _stream())
+        _lib.call("ccut_dequant_matrix", self.fmt_code, self.layout_code, _ptr(src), K, N, nmat, slot, _ptr(out), _stream())
         return out

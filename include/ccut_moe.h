@@ -55,6 +55,11 @@ enum {
   CCUT_FMT_FP8_E4M3_B128 = 2  /* DeepSeek fp8: weight e4m3 [N,K], scale fp32 [N/128,K/128] */
 };
 
+/* Packed tile layouts (same byte size).  ROWS feeds the tcgen05 kernel (one output channel
+ * per row, dequantized into tensor memory); FRAGS feeds the mma.sync kernel (pre-arranged
+ * register fragments). */
+enum { CCUT_LAYOUT_ROWS = 0, CCUT_LAYOUT_FRAGS = 1 };
+
 /* AWQ nibble order inside a 32-bit word. */
 enum { CCUT_NIBBLES_AWQ = 0, CCUT_NIBBLES_SEQUENTIAL = 1 };
 
@@ -82,6 +87,7 @@ typedef struct {
  * stored after the routed ones as `num_shared_slices` slices of width `inter` each. */
 typedef struct {
   int format;            /* CCUT_FMT_* */
+  int layout;            /* CCUT_LAYOUT_* of w13 / w2 */
   int hidden;            /* H */
   int inter;             /* I, routed expert intermediate size */
   int num_experts;       /* E */
@@ -108,14 +114,14 @@ CCUT_API size_t ccut_w2_bytes(int format, int hidden, int inter);
  * AWQ: q = qweight [K, N/8], z = qzeros [K/128, N/8], s = scales fp16 [K/128, N].
  * FP8: q = weight e4m3 [N, K], z unused (NULL), s = scale fp32 [N/128, K/128].
  * Replaces the load-time layout handling of ccut/quant/method.py:35-43 (create_weights). */
-CCUT_API int ccut_pack_matrix(int format, const void* q, const void* z, const void* s, int K, int N,
-                     int nibble_order, void* dst, int nmat, int slot, ccut_stream_t stream);
+CCUT_API int ccut_pack_matrix(int format, int layout, const void* q, const void* z, const void* s, int K,
+                              int N, int nibble_order, void* dst, int nmat, int slot, ccut_stream_t stream);
 
 /* Debug export: packed matrix -> fp32 [K, N] (in, out), bit-identical to the checkpoint
  * dequant ((q - z) * s for AWQ; e4m3 * scale for FP8, NaN codes -> NaN).
  * Replaces ccut/quant/kernels.py:150-171 (fp8_dequant_mat) / :276-295 (int4_dequant_row). */
-CCUT_API int ccut_dequant_matrix(int format, const void* packed, int K, int N, int nmat, int slot,
-                        float* out, ccut_stream_t stream);
+CCUT_API int ccut_dequant_matrix(int format, int layout, const void* packed, int K, int N, int nmat,
+                                 int slot, float* out, ccut_stream_t stream);
 
 /* ---- routing (ccut/models/generic.py:361-362, ccut/blocks/moe.py:46-89) ----------- */
 /* Workspace bytes for ccut_moe_route / ccut_moe_topk with T tokens and E experts. */
@@ -193,8 +199,9 @@ CCUT_API int ccut_moe_forward(const ccut_moe_layer* L, const ccut_route_params* 
 /* ---- quant linear (ccut/quant/method.py:45-58, QuantizeMethodBase.apply) ----------- */
 /* y fp32 [M, N] = x [M, K] @ W, W a packed (nmat = 1) matrix; x bf16 [M, K]. */
 CCUT_API size_t ccut_quant_linear_workspace_bytes(int format, int M, int K);
-CCUT_API int ccut_quant_linear(int format, const void* packed, int K, int N, const uint16_t* x, int M,
-                      float* y, void* workspace, size_t ws_bytes, ccut_stream_t stream);
+CCUT_API int ccut_quant_linear(int format, int layout, const void* packed, int K, int N,
+                               const uint16_t* x, int M, float* y, void* workspace, size_t ws_bytes,
+                               ccut_stream_t stream);
 
 /* ---- diagnostics ------------------------------------------------------------------- */
 /* Device-side status word kept at the start of every workspace: a kernel whose bounded

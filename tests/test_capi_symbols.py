@@ -60,4 +60,4 @@ def test_argument_errors_map_to_reference_exceptions(lib):
     with pytest.raises(NotImplementedError):
         _lib.call("ccut_moe_topk", ctypes.c_void_p(0), 4, 64, ctypes.byref(rp), None, None, None)
     with pytest.raises(NotImplementedError):
-        _lib.call("ccut_pack_matrix", 9, None, None, None, 128, 128, 0, None, 1, 0, None)
+        _lib.call("ccut_pack_matrix", 9, 0, None, None, None, 128, 128, 0, None, 1, 0, None)
