@@ -123,9 +123,9 @@ CCUT_DEVICE void mma_16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1
 // subtraction of 128 + z is exact as well.
 CCUT_DEVICE uint32_t nib2_to_bf16x2_minus(uint32_t w, uint32_t zpair) {
   uint32_t v;
-  asm volatile("lop3.b32 %0, %1, 0x000F000F, 0x43004300, 0xEA;" : "=r"(v) : "r"(w));  // (a & b) | c
+  asm("lop3.b32 %0, %1, 0x000F000F, 0x43004300, 0xEA;" : "=r"(v) : "r"(w));  // (a & b) | c
   uint32_t r;
-  asm volatile("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(zpair));
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(zpair));
   return r;
 }
 
@@ -138,7 +138,7 @@ CCUT_DEVICE uint32_t zero_pair_bf16(uint32_t z) {
 // Two e4m3 bytes (low byte = element 0) -> f16x2, exact (NaN codes -> NaN).
 CCUT_DEVICE uint32_t e4m3x2_to_f16x2(uint16_t v) {
   uint32_t r;
-  asm volatile("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(v));
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(v));
   return r;
 }
 

@@ -6,16 +6,17 @@
 //   D[channel, token] (+)= A[channel, k] * B[token, k]      (tcgen05.mma kind::f16, M=128)
 //
 // Work item = (expert, token tile of NT rows, 128-channel tile); one persistent CTA per SM
-// walks the items.  Warp roles inside the CTA (16 warps):
+// walks the items.  Warp roles inside the CTA (24 warps):
 //   warp 0        producer: per 128-k stage one bulk copy of the packed weight block(s)
 //                 and two 128-byte-swizzled TMA tile loads of the activation rows
 //   warp 1        MMA issuer (one thread) and tensor-memory owner
 //   warp 2        builds the item prefix, then idles
-//   warps 4..11   two dequant warpgroups: each thread owns one weight row (channel),
-//                 converts its 128-k slice to f16 with the group/block scale applied
-//                 ((q - z) * s for AWQ, e4m3 * S for FP8) and stores it to tensor memory
-//                 as the A operand of the next MMAs
-//   warps 12..15  epilogue warpgroup: tensor memory -> registers -> silu(gate) * up as
+//   warps 4..19   four dequant warpgroups: each thread owns one weight row (channel) and
+//                 converts a k-slice of it to f16 with the group/block scale applied
+//                 ((q - z) * s for AWQ, e4m3 * S for FP8), storing it to tensor memory as
+//                 the A operand of the next MMAs (gate/up: warpgroup g converts matrix g/2,
+//                 k half g%2; down: k quarter g)
+//   warps 20..23  epilogue warpgroup: tensor memory -> registers -> silu(gate) * up as
 //                 f16 rows (gate/up), or row_weight * acc as fp32 rows (down)
 // Stages are guarded by mbarriers (full: copies landed; empty: dequant done reading and
 // the MMAs that read the activations completed); A buffers and accumulators are
@@ -29,6 +30,16 @@
 
 namespace ccut {
 
+// Debug-only per-CTA cycle counters of the role waits (built only with -DCCUT_TC_PROFILE).
+#ifdef CCUT_TC_PROFILE
+__device__ unsigned long long g_tc_prof[1024][12];
+#define TC_PROF_START(v) const long long v = clock64()
+#define TC_PROF_ADD(slot, v) atomicAdd(&g_tc_prof[blockIdx.x & 1023][slot], (unsigned long long)(clock64() - (v)))
+#else
+#define TC_PROF_START(v)
+#define TC_PROF_ADD(slot, v)
+#endif
+
 template <int FMT, int MODE, int NT>
 struct TcCfg {
   static constexpr int kNMat = MODE == kFfn1 ? 2 : 1;
@@ -39,20 +50,28 @@ struct TcCfg {
   static constexpr int kStageBytes = kWPad + kBBytes;
   static constexpr int kStages0 = (200 * 1024) / kStageBytes;
   static constexpr int kStages = kStages0 > 8 ? 8 : kStages0;
-  static constexpr int kND = MODE == kFfn1 ? 1 : 2;  // accumulator buffers
-  static constexpr int kThreads = 512;
-  static constexpr int kNBar = 2 * kStages + 9;
+  // Tensor memory (512 columns): accumulators D [kND x kNMat x NT] first, then a ring of
+  // kNA A-operand buffers [kNMat x 64 columns] (one 128-k stage of f16 weights).
+  static constexpr int kND = (2 * kNMat * NT + kNMat * 128 <= 512) ? 2 : 1;  // accumulator buffers
+  static constexpr int kDCols = kND * kNMat * NT;
+  static constexpr int kNA0 = (512 - kDCols) / (kNMat * 64);
+  static constexpr int kNA = kNA0 > 4 ? 4 : kNA0;  // A-operand buffers
+  static constexpr int kThreads = 768;
+  static constexpr int kDeqWarps = 16;
+  static constexpr int kNBar = 2 * kStages + 2 * 4 + 2 * 2 + 1;
   static constexpr int kHeader = kNBar * 8 + 16 + 4 * (kMaxExperts + 1);
   static constexpr int kHeaderAligned = (kHeader + 1023) / 1024 * 1024;
   static constexpr int kSmem = kHeaderAligned + kStages * kStageBytes + 1024;  // +1024: runtime alignment slack
   static_assert(kStages >= 2, "stage does not fit");
   static_assert(NT % 16 == 0 && NT >= 16 && NT <= 128, "token tile must be 16..128, multiple of 16");
-  static_assert(kND * kNMat * 128 <= 256, "accumulators exceed their tensor-memory region");
+  static_assert(kNA >= 2 && kDCols + kNA * kNMat * 64 <= 512, "tensor-memory budget");
   static_assert(kSmem <= 227 * 1024, "shared memory budget");
 };
 
-__device__ __forceinline__ uint32_t dcol(int db, int m, int nmat) { return (uint32_t)((db * nmat + m) * 128); }
-__device__ __forceinline__ uint32_t acol(int a, int m) { return (uint32_t)(256 + (a * 2 + m) * 64); }
+template <class C, int NT>
+__device__ __forceinline__ uint32_t dcol(int db, int m) { return (uint32_t)((db * C::kNMat + m) * NT); }
+template <class C>
+__device__ __forceinline__ uint32_t acol(int a, int m) { return (uint32_t)(C::kDCols + (a * C::kNMat + m) * 64); }
 
 template <int NT>
 __device__ __forceinline__ void tc_decode_item(int item, const int* tprefix, int num_e, const int* offsets,
@@ -90,15 +109,15 @@ __device__ __forceinline__ uint32_t nib2_f16_1024(uint32_t w) {  // (1024 + q_lo
   return v;
 }
 
-// Dequantize k in [64h, 64h+64) of row r of a row-layout block into 32 f16x2 registers
-// (register i = k 64h+2i, 64h+2i+1).
-template <int FMT>
-__device__ __forceinline__ void dequant_half(const uint8_t* blk, int r, int h, uint32_t zz, uint32_t ss,
-                                             uint32_t (&v)[32]) {
+// Dequantize k in [kbase, kbase + 2*NREG) of row r of a row-layout block into NREG f16x2
+// registers (register i = k kbase+2i, kbase+2i+1); kbase is a multiple of 32.
+template <int FMT, int NREG>
+__device__ __forceinline__ void dequant_slice(const uint8_t* blk, int r, int kbase, uint32_t zz, uint32_t ss,
+                                              uint32_t (&v)[NREG]) {
   if constexpr (FMT == CCUT_FMT_FP8_E4M3_B128) {
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const int cc = 4 * h + c;
+    for (int c = 0; c < NREG / 8; ++c) {  // 16-byte chunks of 16 e4m3 values
+      const int cc = kbase / 16 + c;
       const uint4 q = *reinterpret_cast<const uint4*>(blk + r * 128 + 16 * (cc ^ (r & 7)));
       const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
@@ -107,8 +126,8 @@ __device__ __forceinline__ void dequant_half(const uint8_t* blk, int r, int h, u
     }
   } else {
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      const int cc = 2 * h + c;
+    for (int c = 0; c < NREG / 16; ++c) {  // 16-byte chunks of 32 nibbles
+      const int cc = kbase / 32 + c;
       const uint4 q = *reinterpret_cast<const uint4*>(blk + r * 64 + 16 * (cc ^ ((r >> 1) & 3)));
       const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
@@ -121,7 +140,7 @@ __device__ __forceinline__ void dequant_half(const uint8_t* blk, int r, int h, u
 }
 
 template <int FMT, int MODE, int NT>
-__global__ void __launch_bounds__(512, 1) tc_gemm_kernel(const __grid_constant__ CUtensorMap bmap, TcArgs a) {
+__global__ void __launch_bounds__(768, 1) tc_gemm_kernel(const __grid_constant__ CUtensorMap bmap, TcArgs a) {
   using C = TcCfg<FMT, MODE, NT>;
   using BK = Blk<FMT>;
   constexpr int S = C::kStages;
@@ -134,8 +153,8 @@ __global__ void __launch_bounds__(512, 1) tc_gemm_kernel(const __grid_constant__
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* afull = bars + 2 * S;
-  uint64_t* aempty = afull + 2;
-  uint64_t* dfull = aempty + 2;
+  uint64_t* aempty = afull + 4;
+  uint64_t* dfull = aempty + 4;
   uint64_t* dempty = dfull + 2;
   uint64_t* drain = dempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNBar);
@@ -144,6 +163,7 @@ __global__ void __launch_bounds__(512, 1) tc_gemm_kernel(const __grid_constant__
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntiles = a.N / kTileN, ktiles = a.K / kTileK;
+  TC_PROF_START(t_kernel);
 
   if (warp == 1) {
     tc::tmem_alloc(tmem_slot, 512);
@@ -152,11 +172,13 @@ __global__ void __launch_bounds__(512, 1) tc_gemm_kernel(const __grid_constant__
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 8 + 1);
+      mbar_init(&empty[s], C::kDeqWarps + 1);
+    }
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&afull[i], C::kDeqWarps);
+      mbar_init(&aempty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&afull[i], 8);
-      mbar_init(&aempty[i], 1);
       mbar_init(&dfull[i], 1);
       mbar_init(&dempty[i], 4);
     }
@@ -199,10 +221,12 @@ __global__ void __launch_bounds__(512, 1) tc_gemm_kernel(const __grid_constant__
         const uint8_t* wb = a.w + (size_t)e * a.expert_stride + (size_t)nt * ktiles * C::kWBytes;
         for (int kt = 0; kt < ktiles; ++kt, ++use) {
           const int s = use % S;
+          TC_PROF_START(p0);
           if (!mbar_wait(&empty[s], ((use / S) & 1) ^ 1, a.status)) {
             ok = false;
             break;
           }
+          TC_PROF_ADD(0, p0);
           uint8_t* st = stages + s * C::kStageBytes;
           mbar_arrive_expect_tx(&full[s], C::kWBytes + C::kBBytes);
           bulk_g2s(st, wb + (size_t)kt * C::kWBytes, C::kWBytes, &full[s]);
@@ -221,14 +245,21 @@ __global__ void __launch_bounds__(512, 1) tc_gemm_kernel(const __grid_constant__
       bool ok = true;
       for (int item = blockIdx.x; item < total && ok; item += gridDim.x, ++it) {
         const int db = it % ND;
+        TC_PROF_START(m0);
         if (!mbar_wait(&dempty[db], ((it / ND) & 1) ^ 1, a.status)) break;
+        TC_PROF_ADD(3, m0);
         tc::fence_after_sync();
         for (int kt = 0; kt < ktiles; ++kt, ++use) {
-          const int s = use % S, ab = use & 1;
-          if (!mbar_wait(&full[s], (use / S) & 1, a.status) || !mbar_wait(&afull[ab], (use >> 1) & 1, a.status)) {
+          const int s = use % S, ab = use % C::kNA;
+          TC_PROF_START(m1);
+          const bool okf = mbar_wait(&full[s], (use / S) & 1, a.status);
+          TC_PROF_ADD(1, m1);
+          TC_PROF_START(m2);
+          if (!okf || !mbar_wait(&afull[ab], (use / C::kNA) & 1, a.status)) {
             ok = false;
             break;
           }
+          TC_PROF_ADD(2, m2);
           tc::fence_after_sync();
           const uint32_t bbase = smem_u32(stages + s * C::kStageBytes + C::kWPad);
 #pragma unroll
@@ -236,7 +267,7 @@ __global__ void __launch_bounds__(512, 1) tc_gemm_kernel(const __grid_constant__
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks) {
               const uint64_t bd = tc::sdesc_sw128(bbase + (ks >> 2) * (NT * 128) + (ks & 3) * 32);
-              tc::mma_ts(tmem + dcol(db, m, NM), tmem + acol(ab, m) + ks * 8, bd, idesc, (kt | ks) != 0);
+              tc::mma_ts(tmem + dcol<C, NT>(db, m), tmem + acol<C>(ab, m) + ks * 8, bd, idesc, (kt | ks) != 0);
             }
           tc::commit(&aempty[ab]);
           tc::commit(&empty[s]);
@@ -246,22 +277,32 @@ __global__ void __launch_bounds__(512, 1) tc_gemm_kernel(const __grid_constant__
       tc::commit(drain);  // all MMAs issued above have completed once this lands
       mbar_wait(drain, 0, a.status);
     }
-  } else if (warp >= 4 && warp < 12) {
+  } else if (warp >= 4 && warp < 20) {
     // ------------------------------------------------------------ dequant warpgroups
     const int wg = (warp - 4) >> 2;
-    const int q = warp & 3;  // tensor-memory lane quarter
+    const int q = warp & 3;       // tensor-memory lane quarter
     const int r = q * 32 + lane;  // weight row (output channel) of this thread
-    const int mat = NM == 2 ? wg : 0;
-    const int h0 = NM == 2 ? 0 : wg, h1 = NM == 2 ? 2 : wg + 1;  // 64-k halves this group converts
+    const int mat = NM == 2 ? (wg >> 1) : 0;
+    constexpr int kSliceK = NM == 2 ? 64 : 32;  // k handled per warpgroup and stage
+    const int kbase = NM == 2 ? 64 * (wg & 1) : 32 * wg;
+    const uint32_t tlane = (uint32_t)(q * 32) << 16;
     int use = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
       for (int kt = 0; kt < ktiles; ++kt, ++use) {
-        const int s = use % S, ab = use & 1;
-        if (!mbar_wait(&full[s], (use / S) & 1, a.status) || !mbar_wait(&aempty[ab], ((use >> 1) & 1) ^ 1, a.status)) {
+        const int s = use % S, ab = use % C::kNA;
+        const bool rec = (warp == 4 && lane == 0);
+        (void)rec;
+        TC_PROF_START(d0);
+        const bool okf = mbar_wait(&full[s], (use / S) & 1, a.status);
+        if (rec) TC_PROF_ADD(4, d0);
+        TC_PROF_START(d1);
+        if (!okf || !mbar_wait(&aempty[ab], ((use / C::kNA) & 1) ^ 1, a.status)) {
           ok = false;
           break;
         }
+        if (rec) TC_PROF_ADD(5, d1);
+        TC_PROF_START(d2);
         tc::fence_after_sync();
         const uint8_t* blk = stages + s * C::kStageBytes + mat * C::kBlk;
         uint32_t zz = 0, ss;
@@ -274,12 +315,20 @@ __global__ void __launch_bounds__(512, 1) tc_gemm_kernel(const __grid_constant__
           const __half2 s2 = __float2half2_rn(reinterpret_cast<const float*>(blk + BK::kScaleOff)[0]);
           ss = *reinterpret_cast<const uint32_t*>(&s2);
         }
-        for (int h = h0; h < h1; ++h) {
+        const uint32_t taddr = tmem + tlane + acol<C>(ab, mat) + kbase / 2;
+        if constexpr (kSliceK == 64) {
           uint32_t v[32];
-          dequant_half<FMT>(blk, r, h, zz, ss, v);
-          tc::st_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + acol(ab, mat) + 32 * h, v);
+          dequant_slice<FMT, 32>(blk, r, kbase, zz, ss, v);
+          tc::st_32x32b_x32(taddr, v);
+        } else {
+          uint32_t v[16];
+          dequant_slice<FMT, 16>(blk, r, kbase, zz, ss, v);
+          tc::st_32x32b_x16(taddr, v);
         }
+        if (rec) TC_PROF_ADD(6, d2);
+        TC_PROF_START(d3);
         tc::wait_st();
+        if (rec) TC_PROF_ADD(10, d3);
         tc::fence_before_sync();
         __syncwarp();
         if (lane == 0) {
@@ -288,7 +337,7 @@ __global__ void __launch_bounds__(512, 1) tc_gemm_kernel(const __grid_constant__
         }
       }
     }
-  } else if (warp >= 12) {
+  } else if (warp >= 20) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
     const int c = q * 32 + lane;  // channel within the 128-tile
@@ -296,47 +345,62 @@ __global__ void __launch_bounds__(512, 1) tc_gemm_kernel(const __grid_constant__
     int it = 0;
     for (int item = blockIdx.x; item < total; item += gridDim.x, ++it) {
       const int db = it % ND;
-      if (!mbar_wait(&dfull[db], (it / ND) & 1, a.status)) break;
-      tc::fence_after_sync();
+      // item metadata and routing weights first: their latency overlaps the MMAs
       int e, nt, m0, rows;
       tc_decode_item<NT>(item, tprefix, a.num_e, a.offsets, e, nt, m0, rows);
       const int row0 = a.offsets[e] + m0;
+      float wl[NT / 32];  // routing weight of token 32*i + lane
+#pragma unroll
+      for (int i = 0; i < NT / 32; ++i) {
+        const int tok = 32 * i + lane;
+        wl[i] = (MODE == kFfn2 && a.row_weight && tok < rows) ? a.row_weight[row0 + tok] : 1.f;
+      }
+      TC_PROF_START(e0);
+      if (!mbar_wait(&dfull[db], (it / ND) & 1, a.status)) break;
+      if (warp == 20 && lane == 0) TC_PROF_ADD(7, e0);
+      TC_PROF_START(e1);
+      tc::fence_after_sync();
       const int n = nt * kTileN + c;
-      for (int c0 = 0; c0 < rows; c0 += 32) {
-        if constexpr (MODE == kFfn1) {
-          uint32_t g[32], u[32];
-          tc::ld_32x32b_x32(tmem + lane_base + dcol(db, 0, NM) + c0, g);
-          tc::ld_32x32b_x32(tmem + lane_base + dcol(db, 1, NM) + c0, u);
-          tc::wait_ld();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (c0 + j < rows) {
-              const float hv = silu(__uint_as_float(g[j])) * __uint_as_float(u[j]);
-              static_cast<uint16_t*>(a.out)[(size_t)(row0 + c0 + j) * a.out_ld + n] =
-                  __half_as_ushort(__float2half_rn(hv));
+      for (int c0 = 0; c0 < NT; c0 += 16) {
+        if (c0 < rows) {
+          if constexpr (MODE == kFfn1) {
+            uint32_t g[16], u[16];
+            tc::ld_32x32b_x16(tmem + lane_base + dcol<C, NT>(db, 0) + c0, g);
+            tc::ld_32x32b_x16(tmem + lane_base + dcol<C, NT>(db, 1) + c0, u);
+            tc::wait_ld();
+            uint16_t* orow = static_cast<uint16_t*>(a.out) + (size_t)(row0 + c0) * a.out_ld + n;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              if (c0 + j < rows) {
+                const float gv = __uint_as_float(g[j]);
+                const float hv = __fdividef(gv, 1.0f + __expf(-gv)) * __uint_as_float(u[j]);
+                orow[(size_t)j * a.out_ld] = __half_as_ushort(__float2half_rn(hv));
+              }
             }
-          }
-        } else {
-          uint32_t d[32];
-          tc::ld_32x32b_x32(tmem + lane_base + dcol(db, 0, NM) + c0, d);
-          tc::wait_ld();
+          } else {
+            uint32_t d[16];
+            tc::ld_32x32b_x16(tmem + lane_base + dcol<C, NT>(db, 0) + c0, d);
+            tc::wait_ld();
+            float* orow = static_cast<float*>(a.out) + (size_t)(row0 + c0) * a.out_ld + n;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (c0 + j < rows) {
-              const float wr = a.row_weight ? a.row_weight[row0 + c0 + j] : 1.f;
-              static_cast<float*>(a.out)[(size_t)(row0 + c0 + j) * a.out_ld + n] = __uint_as_float(d[j]) * wr;
+            for (int j = 0; j < 16; ++j) {
+              const float wr = __shfl_sync(0xffffffffu, wl[(c0 + j) / 32], (c0 + j) % 32);
+              if (c0 + j < rows) orow[(size_t)j * a.out_ld] = __uint_as_float(d[j]) * wr;
             }
           }
         }
       }
       tc::fence_before_sync();
       __syncwarp();
+      if (warp == 20 && lane == 0) TC_PROF_ADD(8, e1);
       if (lane == 0) mbar_arrive(&dempty[db]);
     }
   }
 
   tc::fence_before_sync();
   __syncthreads();
+  if (threadIdx.x == 0) TC_PROF_ADD(9, t_kernel);
   if (warp == 1) {
     __syncwarp();
     tc::fence_after_sync();
@@ -365,6 +429,17 @@ static int launch_tc_fmt(int fmt, const CUtensorMap& map, const TcArgs& a, int n
   if (fmt == CCUT_FMT_AWQ_INT4_G128) return launch_tc_t<CCUT_FMT_AWQ_INT4_G128, MODE, NT>(map, a, num_sms, st);
   return launch_tc_t<CCUT_FMT_FP8_E4M3_B128, MODE, NT>(map, a, num_sms, st);
 }
+
+#ifdef CCUT_TC_PROFILE
+extern "C" __attribute__((visibility("default"))) int ccut_debug_tc_prof(unsigned long long* host, int clear) {
+  if (cudaMemcpyFromSymbol(host, g_tc_prof, sizeof(g_tc_prof)) != cudaSuccess) return CCUT_ERR_CUDA;
+  if (clear) {
+    static unsigned long long zeros[1024][12];
+    if (cudaMemcpyToSymbol(g_tc_prof, zeros, sizeof(zeros)) != cudaSuccess) return CCUT_ERR_CUDA;
+  }
+  return CCUT_OK;
+}
+#endif
 
 int tc_token_tile(int rows_per_expert) { return rows_per_expert <= 16 ? 32 : rows_per_expert <= 48 ? 64 : 128; }
 
