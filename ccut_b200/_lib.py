@@ -25,6 +25,8 @@ OUT_BF16, OUT_F32 = 0, 1
 
 FORMATS = {"awq_int4_g128": FMT_AWQ_INT4_G128, "fp8_b128": FMT_FP8_E4M3_B128}
 LAYOUTS = {"rows": LAYOUT_ROWS, "frags": LAYOUT_FRAGS}
+KERNEL_AUTO, KERNEL_TC, KERNEL_MMA = 0, 1, 2
+KERNELS = {"auto": KERNEL_AUTO, "tc": KERNEL_TC, "mma": KERNEL_MMA}
 ROUTING = {"softmax_topk": ROUTE_SOFTMAX_TOPK, "topk_softmax": ROUTE_TOPK_SOFTMAX, "sigmoid_group": ROUTE_SIGMOID_GROUP}
 
 _vp, _sz, _i, _f = C.c_void_p, C.c_size_t, C.c_int, C.c_float
@@ -39,9 +41,9 @@ class RouteParams(C.Structure):
 
 class MoeLayerDesc(C.Structure):
     _fields_ = [
-        ("format", _i), ("layout", _i), ("hidden", _i), ("inter", _i), ("num_experts", _i),
+        ("format", _i), ("kernel", _i), ("hidden", _i), ("inter", _i), ("num_experts", _i),
         ("num_shared_slices", _i), ("shared_gate", _f),
-        ("w13", _vp), ("w2", _vp), ("router", _vp),
+        ("w13", _vp), ("w2", _vp), ("w13_frags", _vp), ("w2_frags", _vp), ("router", _vp),
     ]
 
 

@@ -41,7 +41,9 @@ bool valid_fmt(int f) { return f == CCUT_FMT_AWQ_INT4_G128 || f == CCUT_FMT_FP8_
 int check_layer(const ccut_moe_layer* L) {
   if (!L) return CCUT_ERR_INVALID;
   if (!valid_fmt(L->format)) return CCUT_ERR_UNSUPPORTED;
-  if (L->layout != CCUT_LAYOUT_ROWS && L->layout != CCUT_LAYOUT_FRAGS) return CCUT_ERR_UNSUPPORTED;
+  if (L->kernel != CCUT_KERNEL_AUTO && L->kernel != CCUT_KERNEL_TC && L->kernel != CCUT_KERNEL_MMA)
+    return CCUT_ERR_UNSUPPORTED;
+  if (L->kernel == CCUT_KERNEL_MMA && (!L->w13_frags || !L->w2_frags)) return CCUT_ERR_INVALID;
   if (L->hidden <= 0 || L->inter <= 0 || L->hidden % 128 || L->inter % 128) return CCUT_ERR_INVALID;
   if (L->num_experts < 1 || L->num_experts > kMaxRoutedExperts) return CCUT_ERR_UNSUPPORTED;
   if (L->num_shared_slices < 0 || L->num_experts + L->num_shared_slices > kMaxExperts) return CCUT_ERR_UNSUPPORTED;
@@ -68,6 +70,15 @@ int pick_mt(int T, int k, int E) {
   return rows_per_expert <= 24 ? 32 : 64;
 }
 
+// Kernel choice for a call with T tokens and top_k k.
+bool use_tc(const ccut_moe_layer* L, int T, int k) {
+  if (L->kernel == CCUT_KERNEL_TC) return true;
+  if (L->kernel == CCUT_KERNEL_MMA) return false;
+  if (!L->w13_frags || !L->w2_frags) return true;
+  const long per_expert = (long)T * k / (L->num_experts > 0 ? L->num_experts : 1);
+  return per_expert >= CCUT_TC_MIN_ROWS;
+}
+
 // Expert-FFN scratch.  Row layout (tcgen05): xp = f16 activations gathered in expert
 // order [R, H].  Fragment layout (mma.sync): x16 = f16 copy of x [T, H] for FP8 only.
 // Both: intermediate rows [R, I] (16-bit).
@@ -82,9 +93,9 @@ size_t rows_of(const ccut_moe_layer* L, int T, int k) { return (size_t)T * k + (
 FfnScratch carve_ffn(Carver& c, const ccut_moe_layer* L, int T, int k, bool with_input) {
   const size_t R = rows_of(L, T, k);
   FfnScratch s{nullptr, nullptr, nullptr};
-  if (with_input) {
-    if (L->layout == CCUT_LAYOUT_ROWS) s.xp = c.take<uint16_t>(R * L->hidden);
-    else if (L->format == CCUT_FMT_FP8_E4M3_B128) s.x16 = c.take<uint16_t>((size_t)T * L->hidden);
+  if (with_input) {  // sized for either kernel so that one workspace serves both
+    s.xp = c.take<uint16_t>(R * L->hidden);
+    if (L->format == CCUT_FMT_FP8_E4M3_B128) s.x16 = c.take<uint16_t>((size_t)T * L->hidden);
   }
   s.hbuf = c.take<uint16_t>(R * L->inter);
   return s;
@@ -127,13 +138,13 @@ int token_tile(const ccut_moe_layer* L, int T, int k) {
   return tc_token_tile(static_cast<int>(per_expert));
 }
 
-// gate/up: h rows [R, I] from x.  `x16` is the fragment path's f16 copy of x (FP8 only);
-// `xp` the row path's gather buffer.
+// gate/up: h rows [R, I] from x.  `x16` is the mma.sync path's f16 copy of x (FP8 only);
+// `xp` the tcgen05 path's gather buffer.
 int run_gate_up(const ccut_moe_layer* L, const uint16_t* x, const uint16_t* x16, uint16_t* xp, int T, int k,
                 const int32_t* offsets, const int32_t* row_token, uint16_t* hbuf, int* status, cudaStream_t st) {
   const int fmt = L->format;
   const int ne = L->num_experts + L->num_shared_slices;
-  if (L->layout == CCUT_LAYOUT_ROWS) {
+  if (use_tc(L, T, k)) {
     const int R = static_cast<int>(rows_of(L, T, k));
     int rc = launch_gather_f16(x, row_token, R, L->hidden, xp, st);
     if (rc) return rc;
@@ -141,11 +152,13 @@ int run_gate_up(const ccut_moe_layer* L, const uint16_t* x, const uint16_t* x16,
     CUtensorMap map;
     rc = encode_rows_map(&map, xp, R, L->hidden, nt);
     if (rc) return rc;
-    TcArgs a{static_cast<const uint8_t*>(L->w13), ccut_w13_bytes(fmt, L->hidden, L->inter), L->hidden, L->inter,
-             offsets, ne, hbuf, L->inter, nullptr, status};
+    // fused gate/up rows: 2I packed rows, intermediate rows of I channels out
+    TcArgs a{static_cast<const uint8_t*>(L->w13), ccut_w13_bytes(fmt, L->hidden, L->inter), L->hidden,
+             2 * L->inter, offsets, ne, hbuf, L->inter, nullptr, status};
     return launch_tc_gemm(fmt, kFfn1, nt, map, a, num_sms(), st);
   }
-  GemmArgs a{static_cast<const uint8_t*>(L->w13),
+  if (fmt == CCUT_FMT_FP8_E4M3_B128 && !x16) return CCUT_ERR_INVALID;
+  GemmArgs a{static_cast<const uint8_t*>(L->w13_frags),
              ccut_w13_bytes(fmt, L->hidden, L->inter),
              L->hidden,
              L->inter,
@@ -165,7 +178,7 @@ int run_down(const ccut_moe_layer* L, const uint16_t* hbuf, int T, int k, const 
              const float* row_weight, float* y_rows, int* status, cudaStream_t st) {
   const int fmt = L->format;
   const int ne = L->num_experts + L->num_shared_slices;
-  if (L->layout == CCUT_LAYOUT_ROWS) {
+  if (use_tc(L, T, k)) {
     const int R = static_cast<int>(rows_of(L, T, k));
     const int nt = token_tile(L, T, k);
     CUtensorMap map;
@@ -175,7 +188,7 @@ int run_down(const ccut_moe_layer* L, const uint16_t* hbuf, int T, int k, const 
              offsets, ne, y_rows, L->hidden, row_weight, status};
     return launch_tc_gemm(fmt, kFfn2, nt, map, a, num_sms(), st);
   }
-  GemmArgs a{static_cast<const uint8_t*>(L->w2),
+  GemmArgs a{static_cast<const uint8_t*>(L->w2_frags),
              ccut_w2_bytes(fmt, L->hidden, L->inter),
              L->inter,
              L->hidden,
@@ -331,7 +344,7 @@ int ccut_moe_expert_ffn(const ccut_moe_layer* L, const uint16_t* x, int T, int k
   Carver c(workspace);
   int* status = c.take<int>(64);
   FfnScratch s = carve_ffn(c, L, T, k, true);
-  if (s.x16) {
+  if (s.x16 && !use_tc(L, T, k)) {
     rc = launch_bf16_to_f16(x, s.x16, (size_t)T * L->hidden, stream);
     if (rc) return rc;
   }
@@ -356,9 +369,9 @@ size_t ccut_gate_up_workspace_bytes(const ccut_moe_layer* L, int T) {
   if (check_layer(L) || T < 0) return 0;
   Carver c(nullptr);
   c.take<int>(64);
-  // sized for the largest top_k so that one workspace serves any call
-  if (L->layout == CCUT_LAYOUT_ROWS) c.take<uint16_t>(rows_of(L, T, kMaxTopK) * L->hidden);
-  else if (L->format == CCUT_FMT_FP8_E4M3_B128) c.take<uint16_t>((size_t)T * L->hidden);
+  // sized for the largest top_k and either kernel so that one workspace serves any call
+  c.take<uint16_t>(rows_of(L, T, kMaxTopK) * L->hidden);
+  if (L->format == CCUT_FMT_FP8_E4M3_B128) c.take<uint16_t>((size_t)T * L->hidden);
   return c.off;
 }
 
@@ -373,14 +386,14 @@ int ccut_moe_gate_up(const ccut_moe_layer* L, const uint16_t* x, int T, int k, c
   if (ws_bytes < ccut_gate_up_workspace_bytes(L, T)) return CCUT_ERR_WORKSPACE;
   Carver c(workspace);
   int* status = c.take<int>(64);
-  uint16_t* xp = nullptr;
+  uint16_t* xp = c.take<uint16_t>(rows_of(L, T, kMaxTopK) * L->hidden);
   uint16_t* x16 = nullptr;
-  if (L->layout == CCUT_LAYOUT_ROWS) {
-    xp = c.take<uint16_t>(rows_of(L, T, kMaxTopK) * L->hidden);
-  } else if (L->format == CCUT_FMT_FP8_E4M3_B128) {
+  if (L->format == CCUT_FMT_FP8_E4M3_B128) {
     x16 = c.take<uint16_t>((size_t)T * L->hidden);
-    rc = launch_bf16_to_f16(x, x16, (size_t)T * L->hidden, stream);
-    if (rc) return rc;
+    if (!use_tc(L, T, k)) {
+      rc = launch_bf16_to_f16(x, x16, (size_t)T * L->hidden, stream);
+      if (rc) return rc;
+    }
   }
   return run_gate_up(L, x, x16, xp, T, k, offsets, row_token, h_rows, status, stream);
 }
@@ -430,7 +443,8 @@ int ccut_moe_forward(const ccut_moe_layer* L, const ccut_route_params* rp, const
   Carver c(workspace);
   FwdScratch s = carve_fwd(c, L, T, k);
   cudaStream_t st = stream;
-  rc = launch_route(x, L->router, T, H, E, *rp, s.ids, s.wts, nullptr, s.part, s.counts, s.ffn.x16, st);  // x16: FP8 fragment path
+  rc = launch_route(x, L->router, T, H, E, *rp, s.ids, s.wts, nullptr, s.part, s.counts,
+                    use_tc(L, T, k) ? nullptr : s.ffn.x16, st);  // x16: FP8 operands of the mma.sync kernel
   if (rc) return rc;
   if (cudaMemsetAsync(s.pair_row, 0xFF, sizeof(int32_t) * (size_t)T * k, st) != cudaSuccess) return CCUT_ERR_CUDA;
   rc = launch_permute(s.ids, s.wts, T, k, E, L->num_shared_slices, L->shared_gate, s.counts, s.offsets, s.row_token,

@@ -76,6 +76,32 @@ CCUT_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
   return true;
 }
 
+CCUT_DEVICE bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded busy wait (non-suspending test_wait) for single-thread roles whose wake-up
+// latency is on the critical path (MMA issue, TMA producer).
+CCUT_DEVICE bool mbar_spin(uint64_t* bar, uint32_t parity, int* status) {
+  if (mbar_test_wait(bar, parity)) return true;
+  long long t0 = clock64();
+  while (!mbar_test_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitBudgetCycles) {
+      record_error(status, CCUT_ERR_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
 // ---- bulk async copy global -> shared (no tensor map, no multicast) ----------------
 // dst and src 16-byte aligned, bytes a multiple of 16.
 CCUT_DEVICE void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

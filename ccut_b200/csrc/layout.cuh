@@ -23,17 +23,21 @@
 //     bytes [8j, 8j+8) of a lane cover k-step j; byte b is A-tile element
 //     (row g + 8*((b>>1)&1), col 2t + 8*(b>>2) + (b&1)), i.e. byte pair r is A register r.
 //
-// Row layout (CCUT_LAYOUT_ROWS, used by the tcgen05 kernel): the same block sizes, but the
-// weights of each block are stored one output channel per row, so that one dequant thread
-// owns one row (one TMEM lane of the A operand):
-//   AWQ int4: [0, 8192) 128 rows x 64 B; 16-byte chunk c of row r sits at
-//             r*64 + 16*(c ^ ((r >> 1) & 3)); word j of a row covers k = 8j..8j+7 with
-//             nibble slot p holding k = 8j + {0,2,4,6,1,3,5,7}[p], so (w >> 4i) & 0x000F000F
-//             is the pair (8j+2i, 8j+2i+1).  Scales / zero-points as above.
-//   FP8:      [0, 16384) 128 rows x 128 B; chunk c of row r at r*128 + 16*(c ^ (r & 7));
-//             byte b of a row is k = b.  Scale as above.
+// Row layout (used by the tcgen05 kernel): the same block sizes, but each block holds one
+// output channel per row (one tensor-memory lane of the A operand) and is split into two
+// contiguous 64-k halves, so that one pipeline stage (64 k) is one contiguous copy:
+//   AWQ int4: half h at [4096 h, 4096 h + 4096): 128 rows x 32 B; 16-byte chunk c (0..1) of
+//             row r at r*32 + 16*(c ^ ((r >> 2) & 1)); word j (0..3) of a chunk covers
+//             k = 64h + 32c + 8j .. +7 with nibble slot p holding k offset {0,2,4,6,1,3,5,7}[p],
+//             so (w >> 4i) & 0x000F000F is the pair (2i, 2i+1).  Scales at 8192, zero-point
+//             nibbles at 8448, per row, as above.
+//   FP8:      half h at [8192 h, 8192 h + 8192): 128 rows x 64 B; chunk c (0..3) of row r at
+//             r*64 + 16*(c ^ ((r >> 1) & 3)); byte b of a chunk is k = 64h + 16c + b.  Scale at
+//             16384 (a fused gate/up block: gate scale at 16384, up scale at 16388).
 // The XOR swizzle makes the eight rows read by each quarter-warp hit eight distinct bank
-// groups.
+// groups.  A lone matrix (down projection) uses blocks of 128 channels; the gate and up
+// matrices are fused: block t holds gate channels [64t, 64t+64) in rows 0..63 and the same
+// up channels in rows 64..127, so that one 128-row MMA tile yields both halves of SwiGLU.
 #pragma once
 
 #include "common.cuh"
@@ -48,18 +52,25 @@ enum { kLayoutRows = 0, kLayoutFrags = 1 };
 
 // Byte offset, inside a row-layout AWQ block, of the 32-bit word holding element k of row r.
 inline __host__ __device__ int rows_awq_word(int r, int k) {
-  const int j = k >> 3;   // word index within the row
-  const int c = j >> 2;   // 16-byte chunk (4 words)
-  return r * 64 + 16 * (c ^ ((r >> 1) & 3)) + 4 * (j & 3);
+  const int h = k >> 6, c = (k >> 5) & 1, j = (k >> 3) & 3;
+  return h * 4096 + r * 32 + 16 * (c ^ ((r >> 2) & 1)) + 4 * j;
 }
 inline __host__ __device__ int rows_awq_slot(int k) {  // nibble slot inside the word
   const int kk = k & 7;
   return (kk & 1) ? 4 + (kk >> 1) : (kk >> 1);
 }
 inline __host__ __device__ int rows_fp8_byte(int r, int k) {
-  const int c = k >> 4;
-  return r * 128 + 16 * (c ^ (r & 7)) + (k & 15);
+  const int h = k >> 6, c = (k >> 4) & 3;
+  return h * 8192 + r * 64 + 16 * (c ^ ((r >> 1) & 3)) + (k & 15);
 }
+// Source channel of row r of row-layout block `nt` for matrix `slot` (-1: the row belongs to
+// the other matrix of a fused gate/up block).
+inline __host__ __device__ int rows_channel(int nt, int r, int nmat, int slot) {
+  if (nmat == 1) return nt * 128 + r;
+  return (r >> 6) == slot ? nt * 64 + (r & 63) : -1;
+}
+// Row-layout blocks along the channel axis of a matrix with N channels.
+inline __host__ __device__ int rows_nblocks(int N, int nmat) { return nmat == 1 ? N / 128 : N / 64; }
 
 template <int FMT>
 struct Blk;

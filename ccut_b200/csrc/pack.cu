@@ -174,51 +174,69 @@ __global__ void dequant_fp8_kernel(const uint8_t* __restrict__ src, int K, int N
 }
 
 // ---- row layout (tcgen05 kernel) ------------------------------------------------------
-__global__ void pack_awq_rows_kernel(const int32_t* __restrict__ qweight, int K, int N, NibbleOrder ord,
+// Block (nt, kt) of a row-layout buffer sits at (nt * ktiles + kt) * block_bytes; fused
+// gate/up buffers (nmat = 2) hold both matrices in every block.
+__global__ void pack_awq_rows_kernel(const int32_t* __restrict__ qweight, const int32_t* __restrict__ qzeros,
+                                     const uint16_t* __restrict__ scales, int K, int N, NibbleOrder ord,
                                      uint8_t* __restrict__ dst, int nmat, int slot) {
-  constexpr int kWordsPerBlock = kTileN * 16;  // 128 rows x 16 words
-  const int ktiles = K / kTileK;
-  const size_t total = (size_t)(N / kTileN) * ktiles * kWordsPerBlock;
+  using B = Blk<CCUT_FMT_AWQ_INT4_G128>;
+  constexpr int kWordsPerRow = kTileK / 8;  // 16
+  const int ktiles = K / kTileK, nblk = rows_nblocks(N, nmat);
+  const size_t total = (size_t)nblk * ktiles * kTileN * (kWordsPerRow + 1);
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-    const int widx = static_cast<int>(i % kWordsPerBlock);
-    const size_t blk = i / kWordsPerBlock;
+    const int widx = static_cast<int>(i % (kTileN * (kWordsPerRow + 1)));
+    const size_t blk = i / (kTileN * (kWordsPerRow + 1));
     const int kt = static_cast<int>(blk % ktiles);
     const int nt = static_cast<int>(blk / ktiles);
-    const int r = widx >> 4, j = widx & 15;
-    const int n = nt * kTileN + r;
-    uint32_t word = 0;
+    const int r = widx / (kWordsPerRow + 1), j = widx % (kWordsPerRow + 1);
+    const int n = rows_channel(nt, r, nmat, slot);
+    if (n < 0) continue;
+    uint8_t* b = dst + ((size_t)nt * ktiles + kt) * B::kBytes;
+    if (j < kWordsPerRow) {
+      uint32_t word = 0;
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      const int k = kt * kTileK + 8 * j + kk;
-      word |= awq_get(qweight, N / 8, k, n, ord.slot_of_col) << (4 * rows_awq_slot(kk));
+      for (int kk = 0; kk < 8; ++kk) {
+        const int k = kt * kTileK + 8 * j + kk;
+        word |= awq_get(qweight, N / 8, k, n, ord.slot_of_col) << (4 * rows_awq_slot(kk));
+      }
+      *reinterpret_cast<uint32_t*>(b + rows_awq_word(r, 8 * j)) = word;
+    } else if ((r & 1) == 0) {  // metadata of rows r, r+1 (same matrix: halves are 64 rows)
+      uint16_t* sc = reinterpret_cast<uint16_t*>(b + B::kScaleOff);
+      sc[r] = scales[(size_t)kt * N + n];
+      sc[r + 1] = scales[(size_t)kt * N + n + 1];
+      const uint32_t z0 = awq_get(qzeros, N / 8, kt, n, ord.slot_of_col);
+      const uint32_t z1 = awq_get(qzeros, N / 8, kt, n + 1, ord.slot_of_col);
+      b[B::kZeroOff + (r >> 1)] = static_cast<uint8_t>(z0 | (z1 << 4));
     }
-    uint8_t* b = dst + block_offset(CCUT_FMT_AWQ_INT4_G128, nt, kt, slot, ktiles, nmat);
-    *reinterpret_cast<uint32_t*>(b + rows_awq_word(r, 8 * j)) = word;
   }
 }
 
 __global__ void pack_fp8_rows_kernel(const uint8_t* __restrict__ w, const float* __restrict__ scale, int K, int N,
                                      uint8_t* __restrict__ dst, int nmat, int slot) {
   using B = Blk<CCUT_FMT_FP8_E4M3_B128>;
-  constexpr int kChunksPerBlock = kTileN * 8;  // 128 rows x 8 chunks of 16 bytes
-  const int ktiles = K / kTileK;
-  const size_t total = (size_t)(N / kTileN) * ktiles * kChunksPerBlock;
+  constexpr int kChunksPerRow = kTileK / 16;  // 8
+  const int ktiles = K / kTileK, nblk = rows_nblocks(N, nmat);
+  const size_t total = (size_t)nblk * ktiles * kTileN * kChunksPerRow;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-    const int cidx = static_cast<int>(i % kChunksPerBlock);
-    const size_t blk = i / kChunksPerBlock;
+    const int cidx = static_cast<int>(i % (kTileN * kChunksPerRow));
+    const size_t blk = i / (kTileN * kChunksPerRow);
     const int kt = static_cast<int>(blk % ktiles);
     const int nt = static_cast<int>(blk / ktiles);
     const int r = cidx >> 3, c = cidx & 7;
-    const int n = nt * kTileN + r;
+    const int n = rows_channel(nt, r, nmat, slot);
+    if (n < 0) continue;
     const uint4 v = *reinterpret_cast<const uint4*>(w + (size_t)n * K + kt * kTileK + 16 * c);
-    uint8_t* b = dst + block_offset(CCUT_FMT_FP8_E4M3_B128, nt, kt, slot, ktiles, nmat);
+    uint8_t* b = dst + ((size_t)nt * ktiles + kt) * B::kBytes;
     *reinterpret_cast<uint4*>(b + rows_fp8_byte(r, 16 * c)) = v;
-    if (cidx == 0) {
+    if (c == 0 && (r & 63) == 0 && (nmat == 2 || r == 0)) {
+      // block scale(s): a fused gate/up block keeps the gate scale at [0], the up scale at [1]
       float* s = reinterpret_cast<float*>(b + B::kScaleOff);
-      s[0] = scale[(size_t)nt * ktiles + kt];
-      s[1] = 0.f;
-      s[2] = 0.f;
-      s[3] = 0.f;
+      s[nmat == 2 ? slot : 0] = scale[(size_t)(n / 128) * ktiles + kt];
+      if (slot == 0) {
+        if (nmat == 1) s[1] = 0.f;
+        s[2] = 0.f;
+        s[3] = 0.f;
+      }
     }
   }
 }
@@ -226,20 +244,21 @@ __global__ void pack_fp8_rows_kernel(const uint8_t* __restrict__ w, const float*
 __global__ void dequant_awq_rows_kernel(const uint8_t* __restrict__ src, int K, int N, int nmat, int slot,
                                         float* __restrict__ out) {
   using B = Blk<CCUT_FMT_AWQ_INT4_G128>;
-  constexpr int kWordsPerBlock = kTileN * 16;
-  const int ktiles = K / kTileK;
-  const size_t total = (size_t)(N / kTileN) * ktiles * kWordsPerBlock;
+  constexpr int kWordsPerRow = kTileK / 8;
+  const int ktiles = K / kTileK, nblk = rows_nblocks(N, nmat);
+  const size_t total = (size_t)nblk * ktiles * kTileN * kWordsPerRow;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-    const int widx = static_cast<int>(i % kWordsPerBlock);
-    const size_t blk = i / kWordsPerBlock;
+    const int widx = static_cast<int>(i % (kTileN * kWordsPerRow));
+    const size_t blk = i / (kTileN * kWordsPerRow);
     const int kt = static_cast<int>(blk % ktiles);
     const int nt = static_cast<int>(blk / ktiles);
-    const int r = widx >> 4, j = widx & 15;
-    const uint8_t* b = src + block_offset(CCUT_FMT_AWQ_INT4_G128, nt, kt, slot, ktiles, nmat);
+    const int r = widx / kWordsPerRow, j = widx % kWordsPerRow;
+    const int n = rows_channel(nt, r, nmat, slot);
+    if (n < 0) continue;
+    const uint8_t* b = src + ((size_t)nt * ktiles + kt) * B::kBytes;
     const uint32_t word = *reinterpret_cast<const uint32_t*>(b + rows_awq_word(r, 8 * j));
     const uint32_t z = (b[B::kZeroOff + (r >> 1)] >> (4 * (r & 1))) & 0xF;
     const float s = __half2float(__ushort_as_half(reinterpret_cast<const uint16_t*>(b + B::kScaleOff)[r]));
-    const int n = nt * kTileN + r;
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) {
       const uint32_t q = (word >> (4 * rows_awq_slot(kk))) & 0xF;
@@ -252,20 +271,21 @@ __global__ void dequant_awq_rows_kernel(const uint8_t* __restrict__ src, int K, 
 __global__ void dequant_fp8_rows_kernel(const uint8_t* __restrict__ src, int K, int N, int nmat, int slot,
                                         float* __restrict__ out) {
   using B = Blk<CCUT_FMT_FP8_E4M3_B128>;
-  constexpr int kChunksPerBlock = kTileN * 8;
-  const int ktiles = K / kTileK;
-  const size_t total = (size_t)(N / kTileN) * ktiles * kChunksPerBlock;
+  constexpr int kChunksPerRow = kTileK / 16;
+  const int ktiles = K / kTileK, nblk = rows_nblocks(N, nmat);
+  const size_t total = (size_t)nblk * ktiles * kTileN * kChunksPerRow;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-    const int cidx = static_cast<int>(i % kChunksPerBlock);
-    const size_t blk = i / kChunksPerBlock;
+    const int cidx = static_cast<int>(i % (kTileN * kChunksPerRow));
+    const size_t blk = i / (kTileN * kChunksPerRow);
     const int kt = static_cast<int>(blk % ktiles);
     const int nt = static_cast<int>(blk / ktiles);
     const int r = cidx >> 3, c = cidx & 7;
-    const uint8_t* b = src + block_offset(CCUT_FMT_FP8_E4M3_B128, nt, kt, slot, ktiles, nmat);
+    const int n = rows_channel(nt, r, nmat, slot);
+    if (n < 0) continue;
+    const uint8_t* b = src + ((size_t)nt * ktiles + kt) * B::kBytes;
     const uint4 v = *reinterpret_cast<const uint4*>(b + rows_fp8_byte(r, 16 * c));
-    const float s = reinterpret_cast<const float*>(b + B::kScaleOff)[0];
+    const float s = reinterpret_cast<const float*>(b + B::kScaleOff)[nmat == 2 ? slot : 0];
     const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-    const int n = nt * kTileN + r;
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       const uint32_t h2 = e4m3x2_to_f16x2(static_cast<uint16_t>(w4[q >> 1] >> (16 * (q & 1))));
@@ -297,17 +317,15 @@ int launch_pack(int fmt, int layout, const void* q, const void* z, const void* s
   const int threads = 256;
   const int ktiles = K / kTileK, ntiles = N / kTileN;
   if (layout == kLayoutRows) {
+    const int nblk = rows_nblocks(N, nmat);
     if (fmt == CCUT_FMT_AWQ_INT4_G128) {
       NibbleOrder o = make_order(nibble_order);
-      size_t t1 = (size_t)ntiles * ktiles * kTileN * 16;
-      pack_awq_rows_kernel<<<grid_for(t1, threads), threads, 0, st>>>(static_cast<const int32_t*>(q), K, N, o,
-                                                                       static_cast<uint8_t*>(dst), nmat, slot);
-      size_t t2 = (size_t)ntiles * ktiles * (kTileN / 2);
-      pack_awq_meta_kernel<<<grid_for(t2, threads), threads, 0, st>>>(
-          static_cast<const int32_t*>(z), static_cast<const uint16_t*>(s), K, N, o, static_cast<uint8_t*>(dst), nmat,
-          slot);
+      size_t t1 = (size_t)nblk * ktiles * kTileN * 17;
+      pack_awq_rows_kernel<<<grid_for(t1, threads), threads, 0, st>>>(
+          static_cast<const int32_t*>(q), static_cast<const int32_t*>(z), static_cast<const uint16_t*>(s), K, N, o,
+          static_cast<uint8_t*>(dst), nmat, slot);
     } else {
-      size_t t1 = (size_t)ntiles * ktiles * kTileN * 8;
+      size_t t1 = (size_t)nblk * ktiles * kTileN * 8;
       pack_fp8_rows_kernel<<<grid_for(t1, threads), threads, 0, st>>>(static_cast<const uint8_t*>(q),
                                                                        static_cast<const float*>(s), K, N,
                                                                        static_cast<uint8_t*>(dst), nmat, slot);
@@ -337,12 +355,13 @@ int launch_dequant(int fmt, int layout, const void* packed, int K, int N, int nm
   const int threads = 256;
   const int ktiles = K / kTileK, ntiles = N / kTileN;
   if (layout == kLayoutRows) {
+    const int nblk = rows_nblocks(N, nmat);
     if (fmt == CCUT_FMT_AWQ_INT4_G128) {
-      size_t t = (size_t)ntiles * ktiles * kTileN * 16;
+      size_t t = (size_t)nblk * ktiles * kTileN * 16;
       dequant_awq_rows_kernel<<<grid_for(t, threads), threads, 0, st>>>(static_cast<const uint8_t*>(packed), K, N,
                                                                         nmat, slot, out);
     } else {
-      size_t t = (size_t)ntiles * ktiles * kTileN * 8;
+      size_t t = (size_t)nblk * ktiles * kTileN * 8;
       dequant_fp8_rows_kernel<<<grid_for(t, threads), threads, 0, st>>>(static_cast<const uint8_t*>(packed), K, N,
                                                                         nmat, slot, out);
     }

@@ -71,7 +71,9 @@ class MoeLayer:
 
     ``fmt``: ``"awq_int4_g128"`` or ``"fp8_b128"``; ``routing``: ``"softmax_topk"``
     (``norm_topk_prob=False``), ``"topk_softmax"`` (``norm_topk_prob=True``) or
-    ``"sigmoid_group"``."""
+    ``"sigmoid_group"``.  ``kernel``: ``"auto"`` keeps both packed layouts resident and runs
+    the mma.sync kernel for decode-sized batches and the tcgen05 kernel otherwise; ``"tc"``
+    keeps only the tcgen05 layout; ``"mma"`` forces the mma.sync kernel."""
 
     def __init__(
         self,
@@ -91,7 +93,7 @@ class MoeLayer:
         routed_scaling: float = 1.0,
         bias: np.ndarray | torch.Tensor | None = None,
         nibble_order: str = "awq",
-        layout: str = "rows",
+        kernel: str = "auto",
         device: str | torch.device = "cuda",
     ):
         if fmt not in _lib.FORMATS:
@@ -102,11 +104,11 @@ class MoeLayer:
             raise ValueError("hidden and inter must be multiples of 128")
         if len(experts) != num_experts:
             raise ValueError(f"expected {num_experts} experts, got {len(experts)}")
-        if layout not in _lib.LAYOUTS:
-            raise NotImplementedError(f"packed layout {layout!r} is not supported (have {sorted(_lib.LAYOUTS)})")
+        if kernel not in _lib.KERNELS:
+            raise NotImplementedError(f"kernel policy {kernel!r} is not supported (have {sorted(_lib.KERNELS)})")
         self.lib = _lib.load()
         self.fmt, self.fmt_code = fmt, _lib.FORMATS[fmt]
-        self.layout, self.layout_code = layout, _lib.LAYOUTS[layout]
+        self.kernel = kernel
         self.hidden, self.inter, self.num_experts, self.top_k = hidden, inter, num_experts, top_k
         self.routing = routing
         self.device = torch.device(device)
@@ -129,18 +131,26 @@ class MoeLayer:
         self.w13_bytes = L.ccut_w13_bytes(self.fmt_code, hidden, inter)
         self.w2_bytes = L.ccut_w2_bytes(self.fmt_code, hidden, inter)
         ne = num_experts + self.num_slices
-        self.w13 = torch.empty(ne * self.w13_bytes, dtype=torch.uint8, device=self.device)
-        self.w2 = torch.empty(ne * self.w2_bytes, dtype=torch.uint8, device=self.device)
+        self.packed = {}  # layout name -> (w13, w2)
+        layouts = ["rows"] + ([] if kernel == "tc" else ["frags"])
         with torch.cuda.device(self.device):
-            for e, ew in enumerate(experts):
-                self._pack_expert(e, ew, 0, inter)
-            for j, sw in enumerate(shared):
-                for s in range(self.slices_per_shared):
-                    self._pack_expert(num_experts + j * self.slices_per_shared + s, sw, s * inter, inter)
+            for lay in layouts:
+                w13 = torch.empty(ne * self.w13_bytes, dtype=torch.uint8, device=self.device)
+                w2 = torch.empty(ne * self.w2_bytes, dtype=torch.uint8, device=self.device)
+                code = _lib.LAYOUTS[lay]
+                for e, ew in enumerate(experts):
+                    self._pack_expert(code, w13, w2, e, ew, 0, inter)
+                for j, sw in enumerate(shared):
+                    for s in range(self.slices_per_shared):
+                        self._pack_expert(code, w13, w2, num_experts + j * self.slices_per_shared + s, sw,
+                                          s * inter, inter)
+                self.packed[lay] = (w13, w2)
             torch.cuda.current_stream().synchronize()
+        self.w13, self.w2 = self.packed["rows"]
+        w13f, w2f = self.packed.get("frags", (None, None))
         self.desc = _lib.MoeLayerDesc(
-            self.fmt_code, self.layout_code, hidden, inter, num_experts, self.num_slices, self.shared_gate,
-            _ptr(self.w13), _ptr(self.w2), _ptr(self.router),
+            self.fmt_code, _lib.KERNELS[kernel], hidden, inter, num_experts, self.num_slices, self.shared_gate,
+            _ptr(self.w13), _ptr(self.w2), _ptr(w13f), _ptr(w2f), _ptr(self.router),
         )
         self._ws: dict[str, torch.Tensor] = {}
 
@@ -157,7 +167,7 @@ class MoeLayer:
             return w[lo:lo + width], None, sc[lo // 128:(lo + width) // 128]
         return w[:, lo:lo + width], None, sc[:, lo // 128:(lo + width) // 128]
 
-    def _pack_one(self, mat, role, lo, width, K, N, dst: torch.Tensor, nmat: int, slot: int):
+    def _pack_one(self, layout_code, mat, role, lo, width, K, N, dst: torch.Tensor, nmat: int, slot: int):
         q, z, s = self._slice(mat, role, lo, width)
         if self.fmt == "awq_int4_g128":
             qd, zd, sd = _dev(q, self.device, torch.int32), _dev(z, self.device, torch.int32), _dev(s, self.device,
@@ -168,16 +178,16 @@ class MoeLayer:
             qd, zd, sd = _dev(q, self.device, torch.uint8), None, _dev(s, self.device, torch.float32)
             if tuple(qd.shape) != (N, K) or tuple(sd.shape) != (N // 128, K // 128):
                 raise ValueError(f"{role}: FP8 tensors have shapes w{tuple(qd.shape)} s{tuple(sd.shape)} for K={K} N={N}")
-        _lib.call("ccut_pack_matrix", self.fmt_code, self.layout_code, _ptr(qd), _ptr(zd), _ptr(sd), K, N, self.nibbles,
+        _lib.call("ccut_pack_matrix", self.fmt_code, layout_code, _ptr(qd), _ptr(zd), _ptr(sd), K, N, self.nibbles,
                   _ptr(dst), nmat, slot, _stream())
 
-    def _pack_expert(self, e: int, ew, lo: int, width: int):
+    def _pack_expert(self, code, w13_all, w2_all, e: int, ew, lo: int, width: int):
         H, I = self.hidden, self.inter
-        w13 = self.w13[e * self.w13_bytes:(e + 1) * self.w13_bytes]
-        w2 = self.w2[e * self.w2_bytes:(e + 1) * self.w2_bytes]
-        self._pack_one(_get(ew, "gate"), "gate", lo, width, H, I, w13, 2, 0)
-        self._pack_one(_get(ew, "up"), "up", lo, width, H, I, w13, 2, 1)
-        self._pack_one(_get(ew, "down"), "down", lo, width, I, H, w2, 1, 0)
+        w13 = w13_all[e * self.w13_bytes:(e + 1) * self.w13_bytes]
+        w2 = w2_all[e * self.w2_bytes:(e + 1) * self.w2_bytes]
+        self._pack_one(code, _get(ew, "gate"), "gate", lo, width, H, I, w13, 2, 0)
+        self._pack_one(code, _get(ew, "up"), "up", lo, width, H, I, w13, 2, 1)
+        self._pack_one(code, _get(ew, "down"), "down", lo, width, I, H, w2, 1, 0)
 
     # ---- workspace ------------------------------------------------------------------
     def _workspace(self, key: str, nbytes: int) -> torch.Tensor:
@@ -303,15 +313,17 @@ class MoeLayer:
                   _ptr(out), od, _stream())
         return out
 
-    def dequant(self, expert: int, which: str) -> torch.Tensor:
+    def dequant(self, expert: int, which: str, layout: str = "rows") -> torch.Tensor:
         """fp32 [K, N] ([in, out]) export of one packed matrix ("gate" | "up" | "down")."""
         H, I = self.hidden, self.inter
+        w13_all, w2_all = self.packed[layout]
         if which in ("gate", "up"):
-            src = self.w13[expert * self.w13_bytes:(expert + 1) * self.w13_bytes]
+            src = w13_all[expert * self.w13_bytes:(expert + 1) * self.w13_bytes]
             K, N, nmat, slot = H, I, 2, 0 if which == "gate" else 1
         else:
-            src = self.w2[expert * self.w2_bytes:(expert + 1) * self.w2_bytes]
+            src = w2_all[expert * self.w2_bytes:(expert + 1) * self.w2_bytes]
             K, N, nmat, slot = I, H, 1, 0
         out = torch.empty((K, N), dtype=torch.float32, device=self.device)
-        _lib.call("ccut_dequant_matrix", self.fmt_code, self.layout_code, _ptr(src), K, N, nmat, slot, _ptr(out), _stream())
+        _lib.call("ccut_dequant_matrix", self.fmt_code, _lib.LAYOUTS[layout], _ptr(src), K, N, nmat, slot,
+                  _ptr(out), _stream())
         return out

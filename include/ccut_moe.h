@@ -56,9 +56,16 @@ enum {
 };
 
 /* Packed tile layouts (same byte size).  ROWS feeds the tcgen05 kernel (one output channel
- * per row, dequantized into tensor memory); FRAGS feeds the mma.sync kernel (pre-arranged
- * register fragments). */
+ * per row, dequantized into tensor memory; the gate and up matrices of w13 are fused into
+ * shared 128-row blocks); FRAGS feeds the mma.sync kernel (pre-arranged register fragments). */
 enum { CCUT_LAYOUT_ROWS = 0, CCUT_LAYOUT_FRAGS = 1 };
+
+/* Expert-GEMM kernel policy.  TC: tcgen05 (tensor-memory) kernel on the ROWS layout, best
+ * when many rows share an expert (prefill).  MMA: mma.sync kernel on the FRAGS layout, best
+ * for decode-sized batches.  AUTO: MMA when FRAGS weights are present and the batch gives
+ * fewer than CCUT_TC_MIN_ROWS rows per routed expert, else TC. */
+enum { CCUT_KERNEL_AUTO = 0, CCUT_KERNEL_TC = 1, CCUT_KERNEL_MMA = 2 };
+#define CCUT_TC_MIN_ROWS 64
 
 /* AWQ nibble order inside a 32-bit word. */
 enum { CCUT_NIBBLES_AWQ = 0, CCUT_NIBBLES_SEQUENTIAL = 1 };
@@ -87,14 +94,16 @@ typedef struct {
  * stored after the routed ones as `num_shared_slices` slices of width `inter` each. */
 typedef struct {
   int format;            /* CCUT_FMT_* */
-  int layout;            /* CCUT_LAYOUT_* of w13 / w2 */
+  int kernel;            /* CCUT_KERNEL_* */
   int hidden;            /* H */
   int inter;             /* I, routed expert intermediate size */
   int num_experts;       /* E */
   int num_shared_slices; /* shared-expert intermediate / I (0 = no shared expert) */
   float shared_gate;     /* multiplier of the shared-expert output (ccut/blocks/moe.py:177-179) */
-  const void* w13;       /* packed gate/up of E + slices experts, ccut_w13_bytes() each */
-  const void* w2;        /* packed down of E + slices experts, ccut_w2_bytes() each */
+  const void* w13;       /* ROWS layout: packed gate/up of E + slices experts, ccut_w13_bytes() each */
+  const void* w2;        /* ROWS layout: packed down, ccut_w2_bytes() each */
+  const void* w13_frags; /* FRAGS layout of the same weights, or NULL (then only the TC kernel runs) */
+  const void* w2_frags;
   const float* router;   /* fp32 [E, H] router weight (gate_w in ccut/models/generic.py:361) */
 } ccut_moe_layer;
 
@@ -109,8 +118,9 @@ CCUT_API size_t ccut_packed_matrix_bytes(int format, int K, int N);
 CCUT_API size_t ccut_w13_bytes(int format, int hidden, int inter);
 CCUT_API size_t ccut_w2_bytes(int format, int hidden, int inter);
 
-/* Pack one matrix.  `nmat` = 2 interleaves two matrices (gate = slot 0, up = slot 1)
- * in one buffer of 2 * ccut_packed_matrix_bytes(); `nmat` = 1 packs a lone matrix.
+/* Pack one matrix.  `nmat` = 2 packs gate (slot 0) and up (slot 1) into one buffer of
+ * 2 * ccut_packed_matrix_bytes() (FRAGS: interleaved blocks; ROWS: fused 128-row blocks of
+ * 64 gate + 64 up channels); `nmat` = 1 packs a lone matrix.
  * AWQ: q = qweight [K, N/8], z = qzeros [K/128, N/8], s = scales fp16 [K/128, N].
  * FP8: q = weight e4m3 [N, K], z unused (NULL), s = scale fp32 [N/128, K/128].
  * Replaces the load-time layout handling of ccut/quant/method.py:35-43 (create_weights). */

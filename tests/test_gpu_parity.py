@@ -30,6 +30,7 @@ def _cuda():
 
 # ---------------------------------------------------------------- dequant export
 LAYOUTS = ["rows", "frags"]
+KERNELS = ["tc", "mma"]
 
 
 @pytest.mark.parametrize("layout", LAYOUTS)
@@ -45,15 +46,15 @@ def test_dequant_export_bit_exact(fmt, order, layout):
             for m in (ew.gate, ew.up, ew.down):
                 m.qweight = formats.awq_pack(formats.awq_unpack(m.qweight, "awq"), "sequential")
                 m.qzeros = formats.awq_pack(formats.awq_unpack(m.qzeros, "awq"), "sequential")
-        L = gpu_layer(lw, nibble_order="sequential", layout=layout)
+        L = gpu_layer(lw, nibble_order="sequential")
         deq = lambda m: formats.awq_dequant(m.qweight, m.qzeros, m.scales, order="sequential")  # noqa: E731
     else:
-        L = gpu_layer(lw, layout=layout)
+        L = gpu_layer(lw)
         deq = inputs.dequant
     for e, ew in enumerate(lw.experts + lw.shared):
         for which in ("gate", "up", "down"):
             ref = deq(getattr(ew, which)).astype(np.float32)
-            got = L.dequant(e, which).cpu().numpy()
+            got = L.dequant(e, which, layout=layout).cpu().numpy()
             assert got.shape == ref.shape
             assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), f"expert {e} {which}"
 
@@ -185,13 +186,13 @@ CASES = [
 ]
 
 
-@pytest.mark.parametrize("layout", LAYOUTS)
+@pytest.mark.parametrize("kernel", KERNELS)
 @pytest.mark.parametrize("fmt,mode,E,k,S,H,I,Ts", CASES)
-def test_forward_matches_oracle(fmt, mode, E, k, S, H, I, Ts, layout):
+def test_forward_matches_oracle(fmt, mode, E, k, S, H, I, Ts, kernel):
     kw = dict(n_group=4, topk_group=2, routed_scaling=2.5) if mode == "sigmoid_group" else {}
     cfg = small_cfg(fmt, mode, hidden=H, inter=I, experts=E, top_k=k, shared=S, **kw)
     lw = inputs.make_layer(cfg, seed=E + k + S)
-    L = gpu_layer(lw, layout=layout)
+    L = gpu_layer(lw, kernel=kernel)
     for T in Ts:
         xb = lw.make_x(T)
         out, r = L.forward(x_device(xb), out_dtype=torch.float32, return_routing=True)
@@ -207,8 +208,8 @@ def test_forward_matches_oracle(fmt, mode, E, k, S, H, I, Ts, layout):
     assert L.workspace_status() == 0
 
 
-@pytest.mark.parametrize("layout", LAYOUTS)
-def test_forward_matches_reference_moe_forward_as_is(golden_dir, layout):
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_forward_matches_reference_moe_forward_as_is(golden_dir, kernel):
     """Against the reference's own moe_forward (FP8 per-row scales) on equivalent weights."""
     g = np.load(golden_dir / "moe_forward_fp8.npz")
     for norm in (False, True):
@@ -217,31 +218,31 @@ def test_forward_matches_reference_moe_forward_as_is(golden_dir, layout):
         for ew in lw.experts:
             for m in (ew.gate, ew.up, ew.down):
                 m.scale[:] = m.scale[0:1, :]
-        L = gpu_layer(lw, layout=layout)
+        L = gpu_layer(lw, kernel=kernel)
         for T in (1, 5, 17):
             xb = g[f"x_T{T}"]
             out = L.forward(x_device(xb), out_dtype=torch.float32).cpu().numpy()
             assert rel_err_rows(out, g[f"y_norm{int(norm)}_T{T}"]) <= TOL
 
 
-@pytest.mark.parametrize("layout", LAYOUTS)
+@pytest.mark.parametrize("kernel", KERNELS)
 @pytest.mark.parametrize("fmt", FMTS)
-def test_forward_matches_reference_combine(golden_dir, fmt, layout):
+def test_forward_matches_reference_combine(golden_dir, fmt, kernel):
     g = np.load(golden_dir / f"combine_{fmt}.npz")
     cfg = small_cfg(fmt, str(g["routing"]), top_k=int(g["top_k"]))
     lw = inputs.make_layer(cfg, seed=int(g["seed"]))
-    L = gpu_layer(lw, layout=layout)
+    L = gpu_layer(lw, kernel=kernel)
     for T in (1, 5, 17):
         out, r = L.forward(x_device(g[f"x_T{T}"]), out_dtype=torch.float32, return_routing=True)
         assert np.array_equal(r.ids.cpu().numpy().astype(np.int64), g[f"ids_T{T}"])
         assert rel_err_rows(out.cpu().numpy(), g[f"y_T{T}"]) <= TOL
 
 
-@pytest.mark.parametrize("layout", LAYOUTS)
-def test_stages_compose_to_forward(layout):
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_stages_compose_to_forward(kernel):
     cfg = small_cfg("awq_int4_g128", "softmax_topk", experts=8, top_k=2, shared=1)
     lw = inputs.make_layer(cfg, seed=8)
-    L = gpu_layer(lw, layout=layout)
+    L = gpu_layer(lw, kernel=kernel)
     x = x_device(lw.make_x(37))
     r = L.route(x)
     p = L.permute(r)
@@ -259,14 +260,14 @@ def test_empty_batch():
     assert out.shape == (0, 256)
 
 
-@pytest.mark.parametrize("layout", LAYOUTS)
+@pytest.mark.parametrize("kernel", KERNELS)
 @pytest.mark.parametrize("fmt", FMTS)
-def test_all_tokens_on_one_expert_and_empty_experts(fmt, layout):
+def test_all_tokens_on_one_expert_and_empty_experts(fmt, kernel):
     cfg = small_cfg(fmt, "topk_softmax", experts=8, top_k=1, shared=1)
     lw = inputs.make_layer(cfg, seed=10)
     lw.router[:] = 0.0
     lw.router[5, :] = 0.05  # every token routes to expert 5 (x>0 dominated rows aside)
-    L = gpu_layer(lw, layout=layout)
+    L = gpu_layer(lw, kernel=kernel)
     xb = formats.bf16_bits_from_f32(np.abs(formats.bf16_bits_to_f32(lw.make_x(150))) + 0.1)
     out, r = L.forward(x_device(xb), out_dtype=torch.float32, return_routing=True)
     ids = r.ids.cpu().numpy().astype(np.int64)
