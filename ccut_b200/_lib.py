@@ -61,6 +61,7 @@ SIGNATURES: dict[str, tuple] = {
     "ccut_moe_topk": (_i, [_vp, _i, _i, C.POINTER(RouteParams), _vp, _vp, _vp]),
     "ccut_permute_workspace_bytes": (_sz, [_i]),
     "ccut_moe_permute": (_i, [_vp, _vp, _i, _i, _i, _i, _f, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "ccut_moe_permute_static": (_i, [_vp, _vp, _i, _i, _i, _i, _f, _vp, _vp, _vp, _vp, _vp]),
     "ccut_expert_ffn_workspace_bytes": (_sz, [C.POINTER(MoeLayerDesc), _i, _i]),
     "ccut_moe_expert_ffn": (_i, [C.POINTER(MoeLayerDesc), _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "ccut_moe_expert_ffn_w4a16": (_i, [C.POINTER(MoeLayerDesc), _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),

@@ -161,6 +161,20 @@ CCUT_API int ccut_moe_permute(const int32_t* ids, const float* weights, int T, i
                      int32_t* row_token, float* row_weight, int32_t* pair_row,
                      void* workspace, size_t ws_bytes, ccut_stream_t stream);
 
+/* No reference counterpart: ccut_moe_permute with no workspace argument, for hosts that
+ * cannot allocate device memory (a C / FFI caller with no device allocator, or a fixed
+ * memory plan that forbids allocation while steps run).  Its per-expert counters live in
+ * a file-scope device array of CCUT_PERMUTE_STATIC_MAX_EXPERTS int32 per device; it
+ * allocates nothing.  E above that limit fails with CCUT_ERR_UNSUPPORTED.  Outputs and
+ * errors are otherwise those of ccut_moe_permute.  The first call on a device (that device
+ * current) looks up the array's address; make it before any stream capture.  Calls that
+ * overlap on one device share the array and race: serialise them. */
+#define CCUT_PERMUTE_STATIC_MAX_EXPERTS 256
+CCUT_API int ccut_moe_permute_static(const int32_t* ids, const float* weights, int T, int k, int E,
+                            int num_shared_slices, float shared_gate, int32_t* offsets,
+                            int32_t* row_token, float* row_weight, int32_t* pair_row,
+                            ccut_stream_t stream);
+
 /* ---- expert FFN (ccut/blocks/moe.py:122-141, ccut/quant/kernels.py:219-231) ------- */
 /* Workspace bytes of ccut_moe_expert_ffn (intermediate activations) for R rows. */
 CCUT_API size_t ccut_expert_ffn_workspace_bytes(const ccut_moe_layer* L, int T, int k);
