@@ -3,6 +3,8 @@
 // Argument checks happen here, on the host, before anything is enqueued; kernels never
 // see a shape they were not written for.  Workspaces are carved into 256-byte aligned
 // regions; the first region is the device status word of ccut_workspace_status().
+#include <cstdlib>
+
 #include "kernels.cuh"
 
 namespace ccut {
@@ -65,9 +67,17 @@ int check_route(const ccut_route_params* rp, int E) {
   return CCUT_OK;
 }
 
+// Token-tile height of the mma.sync kernel from the mean rows per routed expert.
+// CCUT_MMA_TOKEN_TILE (16, 32 or 64) overrides it, for measurement.
 int pick_mt(int T, int k, int E) {
+  static const int forced = [] {
+    const char* v = getenv("CCUT_MMA_TOKEN_TILE");
+    const int t = v ? atoi(v) : 0;
+    return (t == 16 || t == 32 || t == 64) ? t : 0;
+  }();
+  if (forced) return forced;
   const long rows_per_expert = (long)T * k / (E > 0 ? E : 1);
-  return rows_per_expert <= 24 ? 32 : 64;
+  return rows_per_expert <= 10 ? 16 : rows_per_expert <= 24 ? 32 : 64;
 }
 
 // Kernel choice for a call with T tokens and top_k k.
@@ -502,7 +512,7 @@ int ccut_quant_linear(int format, int layout, const void* packed, int K, int N, 
     xa = x16;
   }
   GemmArgs a{static_cast<const uint8_t*>(packed), 0, K, N, xa, K, nullptr, off, 1, y, N, nullptr, status};
-  return launch_gemm(format, kFfn2, M <= 32 ? 32 : 64, a, num_sms(), stream);
+  return launch_gemm(format, kFfn2, M <= 16 ? 16 : M <= 32 ? 32 : 64, a, num_sms(), stream);
 }
 
 int ccut_workspace_status(void* workspace, ccut_stream_t stream) {

@@ -32,7 +32,10 @@ struct GemmCfg {
   static constexpr int kXRow = kTileK * 2 + 16;  // padded row: conflict-free ldmatrix
   static constexpr int kXBytes = MT * kXRow;
   static constexpr int kStageBytes = kWBytes + kXBytes;
-  static constexpr int kBudget = 200 * 1024;
+  // 16-row tiles (decode) run two CTAs per SM: twice the warps to hide the dequant and
+  // shared-memory latencies, each with half of the shared memory.
+  static constexpr int kMinBlocks = MT <= 16 ? 2 : 1;
+  static constexpr int kBudget = MT <= 16 ? 100 * 1024 : 200 * 1024;
   static constexpr int kStages0 = kBudget / kStageBytes;
   static constexpr int kStages = kStages0 > 8 ? 8 : kStages0;
   static constexpr int kHeader = 2 * 8 * kStages + 4 * (kMaxExperts + 1);
@@ -63,7 +66,8 @@ __device__ __forceinline__ void decode_item(int item, const int* tprefix, int nu
 }
 
 template <int FMT, int MODE, int MT>
-__global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, 1) moe_gemm_kernel(GemmArgs a) {
+__global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT, MODE, MT>::kMinBlocks)
+    moe_gemm_kernel(GemmArgs a) {
   using C = GemmCfg<FMT, MODE, MT>;
   using B = typename C::B;
   constexpr int S = C::kStages;
@@ -172,8 +176,9 @@ __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, 1) moe_gemm_
       for (int m = 0; m < C::kNMat; ++m)
 #pragma unroll
         for (int b = 0; b < MT / 8; ++b)
+          if (b < nblk)
 #pragma unroll
-          for (int i = 0; i < 4; ++i) part[m][b][i] = 0.f;
+            for (int i = 0; i < 4; ++i) part[m][b][i] = 0.f;
 
       // per-stage scale (and AWQ zero-point) of this lane's two channels
       float sc_lo[C::kNMat], sc_hi[C::kNMat];
@@ -243,6 +248,7 @@ __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, 1) moe_gemm_
       for (int m = 0; m < C::kNMat; ++m)
 #pragma unroll
         for (int b = 0; b < MT / 8; ++b) {
+          if (b >= nblk) continue;
           acc[m][b][0] = fmaf(sc_lo[m], part[m][b][0], acc[m][b][0]);
           acc[m][b][1] = fmaf(sc_lo[m], part[m][b][1], acc[m][b][1]);
           acc[m][b][2] = fmaf(sc_hi[m], part[m][b][2], acc[m][b][2]);
@@ -287,23 +293,25 @@ static int launch_gemm_t(const GemmArgs& a, int num_sms, cudaStream_t st) {
       return CCUT_ERR_CUDA;
     attr_done = true;
   }
-  kern<<<num_sms, C::kThreads, C::kSmem, st>>>(a);
+  kern<<<num_sms * C::kMinBlocks, C::kThreads, C::kSmem, st>>>(a);
   return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
 }
 
-// Token-tile height: 32 covers decode batches in one tile; 64 halves weight re-reads for
-// larger batches.
+template <int FMT, int MODE>
+static int launch_gemm_mt(int mt, const GemmArgs& a, int num_sms, cudaStream_t st) {
+  if (mt <= 16) return launch_gemm_t<FMT, MODE, 16>(a, num_sms, st);
+  if (mt <= 32) return launch_gemm_t<FMT, MODE, 32>(a, num_sms, st);
+  return launch_gemm_t<FMT, MODE, 64>(a, num_sms, st);
+}
+
+// Token-tile height: 16 (two CTAs per SM) and 32 cover decode batches in one tile; 64
+// halves weight re-reads for larger batches.
 int launch_gemm(int fmt, int mode, int mt, const GemmArgs& a, int num_sms, cudaStream_t st) {
-  if (fmt == CCUT_FMT_AWQ_INT4_G128) {
-    if (mode == kFfn1) return mt <= 32 ? launch_gemm_t<CCUT_FMT_AWQ_INT4_G128, kFfn1, 32>(a, num_sms, st)
-                                       : launch_gemm_t<CCUT_FMT_AWQ_INT4_G128, kFfn1, 64>(a, num_sms, st);
-    return mt <= 32 ? launch_gemm_t<CCUT_FMT_AWQ_INT4_G128, kFfn2, 32>(a, num_sms, st)
-                    : launch_gemm_t<CCUT_FMT_AWQ_INT4_G128, kFfn2, 64>(a, num_sms, st);
-  }
-  if (mode == kFfn1) return mt <= 32 ? launch_gemm_t<CCUT_FMT_FP8_E4M3_B128, kFfn1, 32>(a, num_sms, st)
-                                     : launch_gemm_t<CCUT_FMT_FP8_E4M3_B128, kFfn1, 64>(a, num_sms, st);
-  return mt <= 32 ? launch_gemm_t<CCUT_FMT_FP8_E4M3_B128, kFfn2, 32>(a, num_sms, st)
-                  : launch_gemm_t<CCUT_FMT_FP8_E4M3_B128, kFfn2, 64>(a, num_sms, st);
+  if (fmt == CCUT_FMT_AWQ_INT4_G128)
+    return mode == kFfn1 ? launch_gemm_mt<CCUT_FMT_AWQ_INT4_G128, kFfn1>(mt, a, num_sms, st)
+                         : launch_gemm_mt<CCUT_FMT_AWQ_INT4_G128, kFfn2>(mt, a, num_sms, st);
+  return mode == kFfn1 ? launch_gemm_mt<CCUT_FMT_FP8_E4M3_B128, kFfn1>(mt, a, num_sms, st)
+                       : launch_gemm_mt<CCUT_FMT_FP8_E4M3_B128, kFfn2>(mt, a, num_sms, st);
 }
 
 }  // namespace ccut

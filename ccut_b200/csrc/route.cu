@@ -292,72 +292,93 @@ __global__ void __launch_bounds__(256) route_topk_kernel(const float* __restrict
   }
 }
 
-// One warp per expert: stable compaction of the pairs routed to it.  The ids are staged
-// through shared memory in chunks so that each warp's scan runs at shared-memory speed
-// instead of waiting on one dependent global load per 32 pairs.
-constexpr int kPermChunk = 8192;
+// Stable counting sort of the T*k (token, slot) pairs by expert, one CTA per contiguous
+// chunk of pairs.  A pair's row is offsets[e] + (pairs of expert e before its chunk) +
+// (pairs of expert e before it inside the chunk).  The first term is an exclusive scan of
+// `counts`; the second a shared-memory histogram of the pairs before the chunk (or, for the
+// later half of the chunks, `counts` minus the histogram of the pairs from the chunk on);
+// the third comes from rounds of 256 pairs: __match_any_sync ranks a pair inside its warp
+// and per-warp counters in shared memory rank the warps.  Pair ids outside [0, E) take no
+// row (their pair_row keeps the caller's -1).
+constexpr int kPermThreads = 256;
+constexpr int kPermWarps = kPermThreads / 32;
 
-__global__ void __launch_bounds__(256) permute_kernel(const int32_t* __restrict__ ids,
-                                                      const float* __restrict__ weights, int T, int k, int E,
-                                                      int slices, float shared_gate, const int* __restrict__ counts,
-                                                      int32_t* __restrict__ offsets, int32_t* __restrict__ row_token,
-                                                      float* __restrict__ row_weight, int32_t* __restrict__ pair_row) {
-  __shared__ int cnt[kMaxExperts];
-  __shared__ int16_t sid[kPermChunk];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = counts[e];
-  __syncthreads();
+__global__ void __launch_bounds__(kPermThreads) permute_kernel(
+    const int32_t* __restrict__ ids, const float* __restrict__ weights, int T, int k, int E, int slices,
+    float shared_gate, const int* __restrict__ counts, int chunk, int32_t* __restrict__ offsets,
+    int32_t* __restrict__ row_token, float* __restrict__ row_weight, int32_t* __restrict__ pair_row) {
+  __shared__ int base[kMaxExperts];
+  __shared__ int hist[kMaxExperts];
+  __shared__ int wcnt[kPermWarps][kMaxExperts];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tk = T * k;
-  const int e = blockIdx.x * 8 + warp;
-  if (blockIdx.x == 0 && warp == 0) {
+  const int c0 = min(tk, blockIdx.x * chunk), c1 = min(tk, c0 + chunk);
+  for (int e = tid; e < E; e += kPermThreads) {
+    hist[e] = 0;
+#pragma unroll
+    for (int w = 0; w < kPermWarps; ++w) wcnt[w][e] = 0;
+  }
+  if (warp == 0) {  // exclusive scan of counts -> base (= offsets)
     int carry = 0;
     for (int b = 0; b < E; b += 32) {
-      const int ee = b + lane;
-      int c = ee < E ? cnt[ee] : 0;
+      const int e = b + lane;
+      const int c = e < E ? counts[e] : 0;
       int inc = c;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int u = __shfl_up_sync(0xffffffffu, inc, o);
         if (lane >= o) inc += u;
       }
-      if (ee < E) offsets[ee] = carry + inc - c;
+      if (e < E) base[e] = carry + inc - c;
       carry += __shfl_sync(0xffffffffu, inc, 31);
     }
-    if (lane == 0)
-      for (int s = 0; s <= slices; ++s) offsets[E + s] = tk + s * T;
   }
-  int base = 0;
-  if (e < E) {
-    for (int i = lane; i < e; i += 32) base += cnt[i];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) base += __shfl_xor_sync(0xffffffffu, base, o);
+  __syncthreads();
+  if (blockIdx.x == 0) {
+    for (int e = tid; e < E; e += kPermThreads) offsets[e] = base[e];
+    for (int s = tid; s <= slices; s += kPermThreads) offsets[E + s] = tk + s * T;
   }
-  int pos = 0;
+  // pairs of each expert before the chunk
+  const bool from_front = c0 <= tk - c0;
+  const int h0 = from_front ? 0 : c0, h1 = from_front ? c0 : tk;
+  for (int i = h0 + tid; i < h1; i += kPermThreads) {
+    const int e = ids[i];
+    if (e >= 0 && e < E) atomicAdd(&hist[e], 1);
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += kPermThreads) base[e] += from_front ? hist[e] : counts[e] - hist[e];
+  __syncthreads();
   const unsigned lt = (1u << lane) - 1u;
-  for (int c0 = 0; c0 < tk; c0 += kPermChunk) {
-    const int n = min(kPermChunk, tk - c0);
+  for (int r0 = c0; r0 < c1; r0 += kPermThreads) {
+    const int i = r0 + tid;
+    int e = i < c1 ? ids[i] : -1;
+    if (e >= E) e = -1;
+    const float wt = e >= 0 ? weights[i] : 0.f;
+    const unsigned same = __match_any_sync(0xffffffffu, e);
+    if (e >= 0 && (same & lt) == 0) wcnt[warp][e] = __popc(same);
     __syncthreads();
-    for (int i = threadIdx.x; i < n; i += blockDim.x) sid[i] = static_cast<int16_t>(ids[c0 + i]);
-    __syncthreads();
-    if (e < E) {
-      for (int i0 = 0; i0 < n; i0 += 32) {
-        const int i = i0 + lane;
-        const bool m = i < n && sid[i] == e;
-        const unsigned bal = __ballot_sync(0xffffffffu, m);
-        if (m) {
-          const int p = base + pos + __popc(bal & lt);
-          const int gi = c0 + i;
-          row_token[p] = gi / k;
-          row_weight[p] = weights[gi];
-          pair_row[gi] = p;
-        }
-        pos += __popc(bal);
-      }
+    if (e >= 0) {
+      int p = base[e] + __popc(same & lt);
+      for (int w = 0; w < warp; ++w) p += wcnt[w][e];
+      row_token[p] = i / k;
+      row_weight[p] = wt;
+      pair_row[i] = p;
     }
+    __syncthreads();
+    for (int ee = tid; ee < E; ee += kPermThreads) {
+      int add = 0;
+#pragma unroll
+      for (int w = 0; w < kPermWarps; ++w) {
+        add += wcnt[w][ee];
+        wcnt[w][ee] = 0;
+      }
+      base[ee] += add;
+    }
+    __syncthreads();
   }
   // shared-expert rows: every token once per slice
   const int nsh = slices * T;
-  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < nsh; r += gridDim.x * blockDim.x) {
+  for (int r = blockIdx.x * kPermThreads + tid; r < nsh; r += gridDim.x * kPermThreads) {
     row_token[tk + r] = r % T;
     row_weight[tk + r] = shared_gate;
   }
@@ -382,9 +403,15 @@ int launch_topk(const float* logits, int T, int E, const ccut_route_params& rp, 
 int launch_permute(const int32_t* ids, const float* weights, int T, int k, int E, int slices, float shared_gate,
                    const int* counts, int32_t* offsets, int32_t* row_token, float* row_weight, int32_t* pair_row,
                    cudaStream_t st) {
-  const int blocks = (E + 7) / 8;
-  permute_kernel<<<blocks, 256, 0, st>>>(ids, weights, T, k, E, slices, shared_gate, counts, offsets, row_token,
-                                         row_weight, pair_row);
+  // about one wave of CTAs; chunks are whole rounds of kPermThreads pairs
+  const int tk = T * k;
+  const int per = (tk + 147) / 148;
+  const int chunk = (per + kPermThreads - 1) / kPermThreads * kPermThreads;
+  int blocks = chunk > 0 ? (tk + chunk - 1) / chunk : 1;
+  if (blocks < 1) blocks = 1;
+  permute_kernel<<<blocks, kPermThreads, 0, st>>>(ids, weights, T, k, E, slices, shared_gate, counts,
+                                                  chunk > 0 ? chunk : kPermThreads, offsets, row_token, row_weight,
+                                                  pair_row);
   return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
 }
 
