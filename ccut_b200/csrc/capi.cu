@@ -48,7 +48,9 @@ int check_layer(const ccut_moe_layer* L) {
   if (L->kernel == CCUT_KERNEL_MMA && (!L->w13_frags || !L->w2_frags)) return CCUT_ERR_INVALID;
   if (L->hidden <= 0 || L->inter <= 0 || L->hidden % 128 || L->inter % 128) return CCUT_ERR_INVALID;
   if (L->num_experts < 1 || L->num_experts > kMaxRoutedExperts) return CCUT_ERR_UNSUPPORTED;
-  if (L->num_shared_slices < 0 || L->num_experts + L->num_shared_slices > kMaxExperts) return CCUT_ERR_UNSUPPORTED;
+  if (L->num_shared_slices < 0 || L->num_shared_slices > CCUT_MAX_SHARED_SLICES ||
+      L->num_experts + L->num_shared_slices > kMaxExperts)
+    return CCUT_ERR_UNSUPPORTED;
   if (!L->w13 || !L->w2) return CCUT_ERR_INVALID;
   return CCUT_OK;
 }
@@ -90,7 +92,7 @@ bool use_tc(const ccut_moe_layer* L, int T, int k) {
 }
 
 // Expert-FFN scratch.  Row layout (tcgen05): xp = f16 activations gathered in expert
-// order [R, H].  Fragment layout (mma.sync): x16 = f16 copy of x [T, H] for FP8 only.
+// order [R, H].  Fragment layout (mma.sync): x16 = f16 copy of x [T, H].
 // Both: intermediate rows [R, I] (16-bit).
 struct FfnScratch {
   uint16_t* x16;
@@ -105,7 +107,7 @@ FfnScratch carve_ffn(Carver& c, const ccut_moe_layer* L, int T, int k, bool with
   FfnScratch s{nullptr, nullptr, nullptr};
   if (with_input) {  // sized for either kernel so that one workspace serves both
     s.xp = c.take<uint16_t>(R * L->hidden);
-    if (L->format == CCUT_FMT_FP8_E4M3_B128) s.x16 = c.take<uint16_t>((size_t)T * L->hidden);
+    s.x16 = c.take<uint16_t>((size_t)T * L->hidden);
   }
   s.hbuf = c.take<uint16_t>(R * L->inter);
   return s;
@@ -148,7 +150,7 @@ int token_tile(const ccut_moe_layer* L, int T, int k) {
   return tc_token_tile(static_cast<int>(per_expert));
 }
 
-// gate/up: h rows [R, I] from x.  `x16` is the mma.sync path's f16 copy of x (FP8 only);
+// gate/up: h rows [R, I] (f16) from x.  `x16` is the mma.sync path's f16 copy of x;
 // `xp` the tcgen05 path's gather buffer.
 int run_gate_up(const ccut_moe_layer* L, const uint16_t* x, const uint16_t* x16, uint16_t* xp, int T, int k,
                 const int32_t* offsets, const int32_t* row_token, uint16_t* hbuf, int* status, cudaStream_t st) {
@@ -167,12 +169,12 @@ int run_gate_up(const ccut_moe_layer* L, const uint16_t* x, const uint16_t* x16,
              2 * L->inter, offsets, ne, hbuf, L->inter, nullptr, status};
     return launch_tc_gemm(fmt, kFfn1, nt, map, a, num_sms(), st);
   }
-  if (fmt == CCUT_FMT_FP8_E4M3_B128 && !x16) return CCUT_ERR_INVALID;
+  if (!x16) return CCUT_ERR_INVALID;
   GemmArgs a{static_cast<const uint8_t*>(L->w13_frags),
              ccut_w13_bytes(fmt, L->hidden, L->inter),
              L->hidden,
              L->inter,
-             fmt == CCUT_FMT_FP8_E4M3_B128 ? x16 : x,
+             x16,
              L->hidden,
              row_token,
              offsets,
@@ -381,7 +383,7 @@ size_t ccut_gate_up_workspace_bytes(const ccut_moe_layer* L, int T) {
   c.take<int>(64);
   // sized for the largest top_k and either kernel so that one workspace serves any call
   c.take<uint16_t>(rows_of(L, T, kMaxTopK) * L->hidden);
-  if (L->format == CCUT_FMT_FP8_E4M3_B128) c.take<uint16_t>((size_t)T * L->hidden);
+  c.take<uint16_t>((size_t)T * L->hidden);
   return c.off;
 }
 
@@ -397,13 +399,10 @@ int ccut_moe_gate_up(const ccut_moe_layer* L, const uint16_t* x, int T, int k, c
   Carver c(workspace);
   int* status = c.take<int>(64);
   uint16_t* xp = c.take<uint16_t>(rows_of(L, T, kMaxTopK) * L->hidden);
-  uint16_t* x16 = nullptr;
-  if (L->format == CCUT_FMT_FP8_E4M3_B128) {
-    x16 = c.take<uint16_t>((size_t)T * L->hidden);
-    if (!use_tc(L, T, k)) {
-      rc = launch_bf16_to_f16(x, x16, (size_t)T * L->hidden, stream);
-      if (rc) return rc;
-    }
+  uint16_t* x16 = c.take<uint16_t>((size_t)T * L->hidden);
+  if (!use_tc(L, T, k)) {
+    rc = launch_bf16_to_f16(x, x16, (size_t)T * L->hidden, stream);
+    if (rc) return rc;
   }
   return run_gate_up(L, x, x16, xp, T, k, offsets, row_token, h_rows, status, stream);
 }
@@ -422,6 +421,7 @@ int ccut_moe_down(const ccut_moe_layer* L, const uint16_t* h_rows, int T, int k,
 int ccut_moe_combine(const float* y_rows, const int32_t* pair_row, int T, int k, int H, int num_shared_slices,
                      void* out, int out_dtype, ccut_stream_t stream) {
   if (T < 0 || k < 1 || k > kMaxTopK || H <= 0 || H % 4 || num_shared_slices < 0) return CCUT_ERR_INVALID;
+  if (num_shared_slices > CCUT_MAX_SHARED_SLICES) return CCUT_ERR_UNSUPPORTED;
   if (out_dtype != CCUT_OUT_BF16 && out_dtype != CCUT_OUT_F32) return CCUT_ERR_INVALID;
   if (T == 0) return CCUT_OK;
   if (!y_rows || !pair_row || !out) return CCUT_ERR_INVALID;
@@ -454,7 +454,7 @@ int ccut_moe_forward(const ccut_moe_layer* L, const ccut_route_params* rp, const
   FwdScratch s = carve_fwd(c, L, T, k);
   cudaStream_t st = stream;
   rc = launch_route(x, L->router, T, H, E, *rp, s.ids, s.wts, nullptr, s.part, s.counts,
-                    use_tc(L, T, k) ? nullptr : s.ffn.x16, st);  // x16: FP8 operands of the mma.sync kernel
+                    use_tc(L, T, k) ? nullptr : s.ffn.x16, st);  // x16: f16 operands of the mma.sync kernel
   if (rc) return rc;
   if (cudaMemsetAsync(s.pair_row, 0xFF, sizeof(int32_t) * (size_t)T * k, st) != cudaSuccess) return CCUT_ERR_CUDA;
   rc = launch_permute(s.ids, s.wts, T, k, E, L->num_shared_slices, L->shared_gate, s.counts, s.offsets, s.row_token,
@@ -477,7 +477,7 @@ size_t ccut_quant_linear_workspace_bytes(int format, int M, int K) {
   Carver c(nullptr);
   c.take<int>(64);
   c.take<int32_t>(2);
-  c.take<uint16_t>((size_t)(M > 0 ? M : 1) * K);  // f16 activations (both layouts' FP8, row layout's AWQ)
+  c.take<uint16_t>((size_t)(M > 0 ? M : 1) * K);  // f16 activations
   return c.off;
 }
 
@@ -505,13 +505,9 @@ int ccut_quant_linear(int format, int layout, const void* packed, int K, int N, 
     TcArgs a{static_cast<const uint8_t*>(packed), 0, K, N, off, 1, y, N, nullptr, status};
     return launch_tc_gemm(format, kFfn2, nt, map, a, num_sms(), stream);
   }
-  const uint16_t* xa = x;
-  if (format == CCUT_FMT_FP8_E4M3_B128) {
-    rc = launch_bf16_to_f16(x, x16, (size_t)M * K, stream);
-    if (rc) return rc;
-    xa = x16;
-  }
-  GemmArgs a{static_cast<const uint8_t*>(packed), 0, K, N, xa, K, nullptr, off, 1, y, N, nullptr, status};
+  rc = launch_bf16_to_f16(x, x16, (size_t)M * K, stream);
+  if (rc) return rc;
+  GemmArgs a{static_cast<const uint8_t*>(packed), 0, K, N, x16, K, nullptr, off, 1, y, N, nullptr, status};
   return launch_gemm(format, kFfn2, M <= 16 ? 16 : M <= 32 ? 32 : 64, a, num_sms(), stream);
 }
 

@@ -8,51 +8,65 @@
 
 namespace ccut {
 
+constexpr int kCombThreads = 256;
+constexpr int kCombMaxRows = 16 + CCUT_MAX_SHARED_SLICES;  // top-k + shared slices
+
+// One CTA per (token, 1024-column chunk).  The token's source rows are staged in shared
+// memory first, so every lane's row loads are independent of one another; the sum runs in
+// the fixed order j = 0..k-1, then the shared slices.
 template <bool kBf16Out>
-__global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ pair_row,
-                                                      int T, int k, int H, int slices, void* __restrict__ out) {
+__global__ void __launch_bounds__(kCombThreads) combine_kernel(const float* __restrict__ y,
+                                                               const int32_t* __restrict__ pair_row, int T, int k,
+                                                               int H, int slices, void* __restrict__ out) {
+  __shared__ int rows[kCombMaxRows];
   const int t = blockIdx.x;
   const int tk = T * k;
   const int R = tk + slices * T;
+  if (threadIdx.x < k) {
+    const int p = pair_row[(size_t)t * k + threadIdx.x];
+    rows[threadIdx.x] = (p >= 0 && p < R) ? p : -1;
+  } else if (threadIdx.x < k + slices) {
+    rows[threadIdx.x] = tk + (threadIdx.x - k) * T + t;
+  }
+  __syncthreads();
+  const int n = k + slices;
   const int h4n = H / 4;
-  for (int h4 = threadIdx.x; h4 < h4n; h4 += blockDim.x) {
-    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int j = 0; j < k; ++j) {
-      const int p = pair_row[(size_t)t * k + j];
-      if (p >= 0 && p < R) {
-        const float4 v = reinterpret_cast<const float4*>(y + (size_t)p * H)[h4];
-        s.x += v.x;
-        s.y += v.y;
-        s.z += v.z;
-        s.w += v.w;
-      }
-    }
-    for (int sl = 0; sl < slices; ++sl) {
-      const float4 v = reinterpret_cast<const float4*>(y + (size_t)(tk + sl * T + t) * H)[h4];
+  const int h4 = blockIdx.y * kCombThreads + threadIdx.x;
+  if (h4 >= h4n) return;
+  const float4* y4 = reinterpret_cast<const float4*>(y);
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+  for (int j = 0; j < n; ++j) {
+    const int p = rows[j];
+    if (p >= 0) {
+      const float4 v = y4[(size_t)p * h4n + h4];
       s.x += v.x;
       s.y += v.y;
       s.z += v.z;
       s.w += v.w;
     }
-    if constexpr (kBf16Out) {
-      __nv_bfloat162 a = __floats2bfloat162_rn(s.x, s.y);
-      __nv_bfloat162 b = __floats2bfloat162_rn(s.z, s.w);
-      uint2 pk;
-      pk.x = *reinterpret_cast<uint32_t*>(&a);
-      pk.y = *reinterpret_cast<uint32_t*>(&b);
-      reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + (size_t)t * H)[h4] = pk;
-    } else {
-      reinterpret_cast<float4*>(static_cast<float*>(out) + (size_t)t * H)[h4] = s;
-    }
+  }
+  if constexpr (kBf16Out) {
+    __nv_bfloat162 a = __floats2bfloat162_rn(s.x, s.y);
+    __nv_bfloat162 b = __floats2bfloat162_rn(s.z, s.w);
+    uint2 pk;
+    pk.x = *reinterpret_cast<uint32_t*>(&a);
+    pk.y = *reinterpret_cast<uint32_t*>(&b);
+    reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + (size_t)t * H)[h4] = pk;
+  } else {
+    reinterpret_cast<float4*>(static_cast<float*>(out) + (size_t)t * H)[h4] = s;
   }
 }
 
 int launch_combine(const float* y, const int32_t* pair_row, int T, int k, int H, int slices, void* out,
                    int out_dtype, cudaStream_t st) {
+  if (k < 1 || slices < 0 || k + slices > kCombMaxRows || H % 4) return CCUT_ERR_UNSUPPORTED;
+  if (T == 0) return CCUT_OK;
+  const dim3 grid(T, (H / 4 + kCombThreads - 1) / kCombThreads);
   if (out_dtype == CCUT_OUT_BF16)
-    combine_kernel<true><<<T, 256, 0, st>>>(y, pair_row, T, k, H, slices, out);
+    combine_kernel<true><<<grid, kCombThreads, 0, st>>>(y, pair_row, T, k, H, slices, out);
   else
-    combine_kernel<false><<<T, 256, 0, st>>>(y, pair_row, T, k, H, slices, out);
+    combine_kernel<false><<<grid, kCombThreads, 0, st>>>(y, pair_row, T, k, H, slices, out);
   return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
 }
 

@@ -144,20 +144,29 @@ CCUT_DEVICE void mma_16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1
 }
 
 // ---- dequant primitives ----------------------------------------------------------------
-// Two unsigned nibbles at bits [0,4) and [16,20) of (w >> shift) -> bf16x2 (q - z):
-// OR-ing a nibble into the mantissa of bf16 128.0 (0x4300) gives 128 + q exactly; the
-// subtraction of 128 + z is exact as well.
-CCUT_DEVICE uint32_t nib2_to_bf16x2_minus(uint32_t w, uint32_t zpair) {
-  uint32_t v;
-  asm("lop3.b32 %0, %1, 0x000F000F, 0x43004300, 0xEA;" : "=r"(v) : "r"(w));  // (a & b) | c
-  uint32_t r;
-  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(zpair));
+// AWQ nibbles -> f16x2 without shifting them down: OR-ing the nibbles at bits [0,4) and
+// [16,20) into the mantissa of f16 1024.0 (0x6400) gives 1024 + q, the nibbles at bits
+// [4,8) and [20,24) give 1024 + 16 q.  Then (1024 + q) - (1024 + z) and
+// (1024 + 16 q) * 1/16 - (64 + z) are q - z, exact (one rounding of an exact result).
+CCUT_DEVICE uint32_t nib_lo_to_f16x2_minus(uint32_t w, uint32_t z1024) {
+  uint32_t v, r;
+  asm("lop3.b32 %0, %1, 0x000F000F, 0x64006400, 0xEA;" : "=r"(v) : "r"(w));
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(z1024));
   return r;
 }
-
-// bf16x2 holding (128 + z, 128 + z).
-CCUT_DEVICE uint32_t zero_pair_bf16(uint32_t z) {
-  uint32_t h = 0x4300u | (z & 0xFu);
+CCUT_DEVICE uint32_t nib_hi_to_f16x2_minus(uint32_t w, uint32_t neg_z64) {
+  uint32_t v, r;
+  asm("lop3.b32 %0, %1, 0x00F000F0, 0x64006400, 0xEA;" : "=r"(v) : "r"(w));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(v), "r"(0x2C002C00u), "r"(neg_z64));  // 0x2C00 = 1/16
+  return r;
+}
+// f16x2 (1024 + z, 1024 + z) and (-(64 + z), -(64 + z)) for a zero-point z in [0, 16).
+CCUT_DEVICE uint32_t zero_pair_f16_1024(uint32_t z) {
+  const uint32_t h = 0x6400u | (z & 0xFu);
+  return h | (h << 16);
+}
+CCUT_DEVICE uint32_t zero_pair_f16_neg64(uint32_t z) {
+  const uint32_t h = 0xD400u + ((z & 0xFu) << 4);
   return h | (h << 16);
 }
 

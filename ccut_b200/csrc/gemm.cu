@@ -6,13 +6,14 @@
 //     one bulk async copy and the MT activation row chunks (gathered through row_src) with
 //     one bulk copy each, into a ring of shared-memory stages guarded by mbarriers;
 //   * warps 0..7 (consumers) each own 16 output channels: they load their A fragments
-//     with 128-bit shared loads, dequantize in registers (AWQ: nibble -> bf16 (q - z),
-//     exact; FP8: e4m3 -> f16, exact), read the activations with ldmatrix and issue
+//     with 128-bit shared loads, dequantize in registers (AWQ: nibble -> f16 (q - z),
+//     exact, one shift + four lop3 + four f16x2 ops per eight weights; FP8: e4m3 -> f16,
+//     exact), read the f16 activations with ldmatrix and issue
 //     m16n8k16 tensor-core MMAs into a per-stage fp32 partial, which is then scaled by the
 //     stage's group/block scale and added to the fp32 accumulator.  The weight operand is
-//     therefore never rounded: (q - z) and e4m3 values are exact in bf16/f16, and the
+//     therefore never rounded: (q - z) and e4m3 values are exact in f16, and the
 //     scale is applied in fp32 once per 128-k group (AWQ per channel, FP8 per block).
-// Epilogues: FFN1 writes silu(gate) * up as bf16 (AWQ) / f16 (FP8) rows; FFN2 writes
+// Epilogues: FFN1 writes silu(gate) * up as f16 rows; FFN2 writes
 // row_weight[row] * acc as fp32 rows.
 //
 // Follows ccut/blocks/moe.py:122-141 (expert_ffn), ccut/quant/kernels.py:219-231 (SiLU),
@@ -21,6 +22,16 @@
 #include "kernels.cuh"
 
 namespace ccut {
+
+// Debug-only per-CTA cycle counters of the role waits (built only with -DCCUT_GEMM_PROFILE).
+#ifdef CCUT_GEMM_PROFILE
+__device__ unsigned long long g_gemm_prof[1024][8];
+#define GM_PROF_START(v) const long long v = clock64()
+#define GM_PROF_ADD(slot, v) atomicAdd(&g_gemm_prof[blockIdx.x & 1023][slot], (unsigned long long)(clock64() - (v)))
+#else
+#define GM_PROF_START(v)
+#define GM_PROF_ADD(slot, v)
+#endif
 
 template <int FMT, int MODE, int MT>
 struct GemmCfg {
@@ -79,6 +90,7 @@ __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT,
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntiles = a.N / kTileN, ktiles = a.K / kTileK;
+  GM_PROF_START(t_kernel);
 
   if (warp == 0) {  // item prefix over experts: tiles(e) = ceil(M_e / MT) * ntiles
     int carry = 0;
@@ -125,10 +137,12 @@ __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT,
       for (int kt = 0; kt < ktiles; ++kt, ++use) {
         const int s = use % S;
         const uint32_t ph = (use / S) & 1;
+        GM_PROF_START(p0);
         if (!mbar_wait(&empty[s], ph ^ 1, a.status)) {
           ok = false;
           break;
         }
+        if (lane == 0) GM_PROF_ADD(0, p0);
         uint8_t* st = stages + s * C::kStageBytes;
         if (lane == 0) {
           mbar_arrive_expect_tx(&full[s], C::kWBytes + rows * (kTileK * 2));
@@ -168,7 +182,10 @@ __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT,
 
     for (int kt = 0; kt < ktiles; ++kt, ++use) {
       const int s = use % S;
+      GM_PROF_START(c0);
       if (!mbar_wait(&full[s], (use / S) & 1, a.status)) return;
+      if (threadIdx.x == 0) GM_PROF_ADD(1, c0);
+      GM_PROF_START(c1);
       const uint8_t* st = stages + s * C::kStageBytes;
       const uint8_t* xs = st + C::kWBytes;
       float part[C::kNMat][MT / 8][4];
@@ -182,7 +199,7 @@ __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT,
 
       // per-stage scale (and AWQ zero-point) of this lane's two channels
       float sc_lo[C::kNMat], sc_hi[C::kNMat];
-      uint32_t zp_lo[C::kNMat], zp_hi[C::kNMat];
+      uint32_t zp_lo[C::kNMat], zp_hi[C::kNMat];  // AWQ: f16x2 1024 + z (lo), -(64 + z) (hi)
 #pragma unroll
       for (int m = 0; m < C::kNMat; ++m) {
         const uint8_t* blk = st + m * B::kBytes;
@@ -190,8 +207,8 @@ __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT,
           const uint16_t* sc = reinterpret_cast<const uint16_t*>(blk + B::kScaleOff);
           sc_lo[m] = __half2float(__ushort_as_half(sc[ch_lo]));
           sc_hi[m] = __half2float(__ushort_as_half(sc[ch_hi]));
-          zp_lo[m] = zero_pair_bf16(blk[B::kZeroOff + (ch_lo >> 1)] >> (4 * (ch_lo & 1)));
-          zp_hi[m] = zero_pair_bf16(blk[B::kZeroOff + (ch_hi >> 1)] >> (4 * (ch_hi & 1)));
+          zp_lo[m] = zero_pair_f16_1024(blk[B::kZeroOff + (ch_lo >> 1)] >> (4 * (ch_lo & 1)));
+          zp_hi[m] = zero_pair_f16_neg64(blk[B::kZeroOff + (ch_hi >> 1)] >> (4 * (ch_hi & 1)));
         } else {
           sc_lo[m] = sc_hi[m] = reinterpret_cast<const float*>(blk + B::kScaleOff)[0];
           zp_lo[m] = zp_hi[m] = 0;
@@ -211,10 +228,11 @@ __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT,
           for (int m = 0; m < C::kNMat; ++m) {
             if constexpr (FMT == CCUT_FMT_AWQ_INT4_G128) {
               const uint32_t wd = j == 0 ? raw[m].x : j == 1 ? raw[m].y : j == 2 ? raw[m].z : raw[m].w;
-              af[m][0] = nib2_to_bf16x2_minus(wd, zp_lo[m]);
-              af[m][1] = nib2_to_bf16x2_minus(wd >> 4, zp_hi[m]);
-              af[m][2] = nib2_to_bf16x2_minus(wd >> 8, zp_lo[m]);
-              af[m][3] = nib2_to_bf16x2_minus(wd >> 12, zp_hi[m]);
+              // a0/a2: channel ch_lo (nibbles 0,4 / 2,6); a1/a3: ch_hi (nibbles 1,5 / 3,7)
+              af[m][0] = nib_lo_to_f16x2_minus(wd, zp_lo[m]);
+              af[m][1] = nib_hi_to_f16x2_minus(wd, zp_hi[m]);
+              af[m][2] = nib_lo_to_f16x2_minus(wd >> 8, zp_lo[m]);
+              af[m][3] = nib_hi_to_f16x2_minus(wd >> 8, zp_hi[m]);
             } else {
               const uint32_t w0 = j == 0 ? raw[m].x : raw[m].z;
               const uint32_t w1 = j == 0 ? raw[m].y : raw[m].w;
@@ -243,6 +261,7 @@ __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT,
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
+      if (threadIdx.x == 0) GM_PROF_ADD(2, c1);
       // promote: acc += scale * partial (fp32)
 #pragma unroll
       for (int m = 0; m < C::kNMat; ++m)
@@ -257,6 +276,7 @@ __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT,
     }
 
     // ---------------- epilogue ----------------
+    GM_PROF_START(c2);
     const int row0 = a.offsets[e] + m0;
     const int n_lo = nt * kTileN + ch_lo, n_hi = n_lo + 8;
 #pragma unroll
@@ -280,8 +300,21 @@ __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT,
         }
       }
     }
+    if (threadIdx.x == 0) GM_PROF_ADD(3, c2);
   }
+  if (threadIdx.x == 0) GM_PROF_ADD(4, t_kernel);
 }
+
+#ifdef CCUT_GEMM_PROFILE
+extern "C" __attribute__((visibility("default"))) int ccut_debug_gemm_prof(unsigned long long* host, int clear) {
+  if (cudaMemcpyFromSymbol(host, g_gemm_prof, sizeof(g_gemm_prof)) != cudaSuccess) return CCUT_ERR_CUDA;
+  if (clear) {
+    static unsigned long long zeros[1024][8];
+    if (cudaMemcpyToSymbol(g_gemm_prof, zeros, sizeof(zeros)) != cudaSuccess) return CCUT_ERR_CUDA;
+  }
+  return CCUT_OK;
+}
+#endif
 
 template <int FMT, int MODE, int MT>
 static int launch_gemm_t(const GemmArgs& a, int num_sms, cudaStream_t st) {

@@ -84,7 +84,7 @@ struct Blk<CCUT_FMT_AWQ_INT4_G128> {
   static constexpr int kScaleOff = 8192;
   static constexpr int kZeroOff = 8448;
   static constexpr int kBytes = 8512;
-  static constexpr bool kBf16 = true;  // MMA operand type
+  static constexpr bool kBf16 = false;  // f16 operands ((q - z) is exact in f16)
 };
 
 template <>

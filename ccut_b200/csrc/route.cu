@@ -163,8 +163,17 @@ __global__ void __launch_bounds__(256) route_topk_kernel(const float* __restrict
       if (logits_in) {
         val = logits_in[(size_t)t * E + e];
       } else {
-        val = 0.f;
-        for (int s = 0; s < hsplit; ++s) val += part[((size_t)s * T + t) * E + e];
+        // eight independent partial sums keep eight loads in flight per lane
+        const float* pp = part + (size_t)t * E + e;
+        const size_t ps = (size_t)T * E;
+        float a8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        int s = 0;
+        for (; s + 8 <= hsplit; s += 8) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) a8[j] += pp[(size_t)(s + j) * ps];
+        }
+        for (; s < hsplit; ++s) a8[0] += pp[(size_t)s * ps];
+        val = ((a8[0] + a8[1]) + (a8[2] + a8[3])) + ((a8[4] + a8[5]) + (a8[6] + a8[7]));
       }
       if (logits_out) logits_out[(size_t)t * E + e] = val;
     }

@@ -92,13 +92,15 @@ typedef struct {
  * ccut/experts/reader.py:86-334, and the per-call segment reads of
  * ccut/models/generic.py:389-400).  Shared experts (ccut/models/generic.py:380-385) are
  * stored after the routed ones as `num_shared_slices` slices of width `inter` each. */
+#define CCUT_MAX_SHARED_SLICES 32
+
 typedef struct {
   int format;            /* CCUT_FMT_* */
   int kernel;            /* CCUT_KERNEL_* */
   int hidden;            /* H */
   int inter;             /* I, routed expert intermediate size */
   int num_experts;       /* E */
-  int num_shared_slices; /* shared-expert intermediate / I (0 = no shared expert) */
+  int num_shared_slices; /* shared-expert intermediate / I (0 = no shared expert), <= CCUT_MAX_SHARED_SLICES */
   float shared_gate;     /* multiplier of the shared-expert output (ccut/blocks/moe.py:177-179) */
   const void* w13;       /* ROWS layout: packed gate/up of E + slices experts, ccut_w13_bytes() each */
   const void* w2;        /* ROWS layout: packed down, ccut_w2_bytes() each */
@@ -195,7 +197,7 @@ CCUT_API int ccut_moe_expert_ffn_fp8b128(const ccut_moe_layer* L, const uint16_t
                                 size_t ws_bytes, ccut_stream_t stream);
 
 /* The two halves of ccut_moe_expert_ffn, for callers that schedule them separately.
- * gate/up: h_rows [R, I] = silu(x_r @ Wg) * (x_r @ Wu), 16-bit (bf16 for AWQ, f16 for FP8)
+ * gate/up: h_rows [R, I] = silu(x_r @ Wg) * (x_r @ Wu), f16 (both formats)
  * (ccut/blocks/moe.py:128-136); down: y_rows fp32 [R, H] = row_weight[r] * h_r @ Wd
  * (ccut/blocks/moe.py:137, ccut/models/generic.py:377-378). */
 CCUT_API size_t ccut_gate_up_workspace_bytes(const ccut_moe_layer* L, int T);
