@@ -75,6 +75,15 @@ SIGNATURES: dict[str, tuple] = {
                               _vp]),
     "ccut_quant_linear_workspace_bytes": (_sz, [_i, _i, _i]),
     "ccut_quant_linear": (_i, [_i, _i, _vp, _i, _i, _vp, _i, _vp, _vp, _sz, _vp]),
+    "ccut_ep_unique_id_bytes": (_sz, []),
+    "ccut_ep_unique_id": (_i, [_vp]),
+    "ccut_ep_init": (_i, [_vp, _i, _i, C.c_double, C.POINTER(_vp)]),
+    "ccut_ep_destroy": (_i, [_vp]),
+    "ccut_moe_ep_dispatch": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp]),
+    "ccut_moe_ep_combine": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
+    "ccut_moe_ep_forward_workspace_bytes": (_sz, [C.POINTER(MoeLayerDesc), _i, _i, _i, _i]),
+    "ccut_moe_ep_forward": (_i, [_vp, C.POINTER(MoeLayerDesc), _i, _i, C.POINTER(RouteParams), _vp, _i, _vp, _i,
+                                 _vp, _sz, _vp]),
     "ccut_workspace_status": (_i, [_vp, _vp]),
 }
 

@@ -74,7 +74,7 @@ def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | N
     with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         objs = list(ex.map(compile_one, sources()))
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [cc, *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-lcudart"]
+    cmd = [cc, *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-lcudart", "-lnccl"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -5,13 +5,9 @@
 // regions; the first region is the device status word of ccut_workspace_status().
 #include <cstdlib>
 
-#include "kernels.cuh"
+#include "host.cuh"
 
 namespace ccut {
-namespace {
-
-constexpr int kMaxTopK = 16;
-constexpr int kMaxRoutedExperts = 256;
 
 int num_sms() {
   static int cache[64] = {0};
@@ -24,19 +20,6 @@ int num_sms() {
   }
   return cache[dev];
 }
-
-struct Carver {
-  uint8_t* base;
-  size_t off = 0;
-  explicit Carver(void* b) : base(static_cast<uint8_t*>(b)) {}
-  template <class T>
-  T* take(size_t n) {
-    off = (off + 255) / 256 * 256;
-    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
-    off += n * sizeof(T);
-    return p;
-  }
-};
 
 bool valid_fmt(int f) { return f == CCUT_FMT_AWQ_INT4_G128 || f == CCUT_FMT_FP8_E4M3_B128; }
 
@@ -71,34 +54,27 @@ int check_route(const ccut_route_params* rp, int E) {
 
 // Token-tile height of the mma.sync kernel from the mean rows per routed expert.
 // CCUT_MMA_TOKEN_TILE (16, 32 or 64) overrides it, for measurement.
-int pick_mt(int T, int k, int E) {
+int pick_mt(long rows_per_expert) {
   static const int forced = [] {
     const char* v = getenv("CCUT_MMA_TOKEN_TILE");
     const int t = v ? atoi(v) : 0;
     return (t == 16 || t == 32 || t == 64) ? t : 0;
   }();
   if (forced) return forced;
-  const long rows_per_expert = (long)T * k / (E > 0 ? E : 1);
   return rows_per_expert <= 10 ? 16 : rows_per_expert <= 24 ? 32 : 64;
 }
 
 // Kernel choice for a call with T tokens and top_k k.
-bool use_tc(const ccut_moe_layer* L, int T, int k) {
+long mean_rows(const ccut_moe_layer* L, int T, int k) {
+  return (long)T * k / (L->num_experts > 0 ? L->num_experts : 1);
+}
+
+bool use_tc(const ccut_moe_layer* L, long per_expert) {
   if (L->kernel == CCUT_KERNEL_TC) return true;
   if (L->kernel == CCUT_KERNEL_MMA) return false;
   if (!L->w13_frags || !L->w2_frags) return true;
-  const long per_expert = (long)T * k / (L->num_experts > 0 ? L->num_experts : 1);
   return per_expert >= CCUT_TC_MIN_ROWS;
 }
-
-// Expert-FFN scratch.  Row layout (tcgen05): xp = f16 activations gathered in expert
-// order [R, H].  Fragment layout (mma.sync): x16 = f16 copy of x [T, H].
-// Both: intermediate rows [R, I] (16-bit).
-struct FfnScratch {
-  uint16_t* x16;
-  uint16_t* xp;
-  uint16_t* hbuf;
-};
 
 size_t rows_of(const ccut_moe_layer* L, int T, int k) { return (size_t)T * k + (size_t)L->num_shared_slices * T; }
 
@@ -145,22 +121,19 @@ FwdScratch carve_fwd(Carver& c, const ccut_moe_layer* L, int T, int k) {
   return s;
 }
 
-int token_tile(const ccut_moe_layer* L, int T, int k) {
-  const long per_expert = (long)T * k / (L->num_experts > 0 ? L->num_experts : 1);
-  return tc_token_tile(static_cast<int>(per_expert));
-}
 
 // gate/up: h rows [R, I] (f16) from x.  `x16` is the mma.sync path's f16 copy of x;
 // `xp` the tcgen05 path's gather buffer.
-int run_gate_up(const ccut_moe_layer* L, const uint16_t* x, const uint16_t* x16, uint16_t* xp, int T, int k,
+int run_gate_up(const ccut_moe_layer* L, long per_expert, const uint16_t* x, const uint16_t* x16, uint16_t* xp,
+                int T, int k,
                 const int32_t* offsets, const int32_t* row_token, uint16_t* hbuf, int* status, cudaStream_t st) {
   const int fmt = L->format;
   const int ne = L->num_experts + L->num_shared_slices;
-  if (use_tc(L, T, k)) {
+  if (use_tc(L, per_expert)) {
     const int R = static_cast<int>(rows_of(L, T, k));
-    int rc = launch_gather_f16(x, row_token, R, L->hidden, xp, st);
+    int rc = launch_gather_f16(x, row_token, R, offsets + ne, L->hidden, xp, st);
     if (rc) return rc;
-    const int nt = token_tile(L, T, k);
+    const int nt = tc_token_tile(static_cast<int>(per_expert));
     CUtensorMap map;
     rc = encode_rows_map(&map, xp, R, L->hidden, nt);
     if (rc) return rc;
@@ -183,16 +156,16 @@ int run_gate_up(const ccut_moe_layer* L, const uint16_t* x, const uint16_t* x16,
              L->inter,
              nullptr,
              status};
-  return launch_gemm(fmt, kFfn1, pick_mt(T, k, L->num_experts), a, num_sms(), st);
+  return launch_gemm(fmt, kFfn1, pick_mt(per_expert), a, num_sms(), st);
 }
 
-int run_down(const ccut_moe_layer* L, const uint16_t* hbuf, int T, int k, const int32_t* offsets,
+int run_down(const ccut_moe_layer* L, long per_expert, const uint16_t* hbuf, int T, int k, const int32_t* offsets,
              const float* row_weight, float* y_rows, int* status, cudaStream_t st) {
   const int fmt = L->format;
   const int ne = L->num_experts + L->num_shared_slices;
-  if (use_tc(L, T, k)) {
+  if (use_tc(L, per_expert)) {
     const int R = static_cast<int>(rows_of(L, T, k));
-    const int nt = token_tile(L, T, k);
+    const int nt = tc_token_tile(static_cast<int>(per_expert));
     CUtensorMap map;
     int rc = encode_rows_map(&map, hbuf, R, L->inter, nt);
     if (rc) return rc;
@@ -213,17 +186,17 @@ int run_down(const ccut_moe_layer* L, const uint16_t* hbuf, int T, int k, const 
              L->hidden,
              row_weight,
              status};
-  return launch_gemm(fmt, kFfn2, pick_mt(T, k, L->num_experts), a, num_sms(), st);
+  return launch_gemm(fmt, kFfn2, pick_mt(per_expert), a, num_sms(), st);
 }
 
-int run_ffn(const ccut_moe_layer* L, const uint16_t* x, const FfnScratch& s, int T, int k, const int32_t* offsets,
+int run_ffn(const ccut_moe_layer* L, long per_expert, const uint16_t* x, const FfnScratch& s, int T, int k,
+            const int32_t* offsets,
             const int32_t* row_token, const float* row_weight, float* y_rows, int* status, cudaStream_t st) {
-  int rc = run_gate_up(L, x, s.x16, s.xp, T, k, offsets, row_token, s.hbuf, status, st);
+  int rc = run_gate_up(L, per_expert, x, s.x16, s.xp, T, k, offsets, row_token, s.hbuf, status, st);
   if (rc) return rc;
-  return run_down(L, s.hbuf, T, k, offsets, row_weight, y_rows, status, st);
+  return run_down(L, per_expert, s.hbuf, T, k, offsets, row_weight, y_rows, status, st);
 }
 
-}  // namespace
 }  // namespace ccut
 
 using namespace ccut;
@@ -356,11 +329,11 @@ int ccut_moe_expert_ffn(const ccut_moe_layer* L, const uint16_t* x, int T, int k
   Carver c(workspace);
   int* status = c.take<int>(64);
   FfnScratch s = carve_ffn(c, L, T, k, true);
-  if (s.x16 && !use_tc(L, T, k)) {
+  if (s.x16 && !use_tc(L, mean_rows(L, T, k))) {
     rc = launch_bf16_to_f16(x, s.x16, (size_t)T * L->hidden, stream);
     if (rc) return rc;
   }
-  return run_ffn(L, x, s, T, k, offsets, row_token, row_weight, y_rows, status, stream);
+  return run_ffn(L, mean_rows(L, T, k), x, s, T, k, offsets, row_token, row_weight, y_rows, status, stream);
 }
 
 int ccut_moe_expert_ffn_w4a16(const ccut_moe_layer* L, const uint16_t* x, int T, int k, const int32_t* offsets,
@@ -400,11 +373,11 @@ int ccut_moe_gate_up(const ccut_moe_layer* L, const uint16_t* x, int T, int k, c
   int* status = c.take<int>(64);
   uint16_t* xp = c.take<uint16_t>(rows_of(L, T, kMaxTopK) * L->hidden);
   uint16_t* x16 = c.take<uint16_t>((size_t)T * L->hidden);
-  if (!use_tc(L, T, k)) {
+  if (!use_tc(L, mean_rows(L, T, k))) {
     rc = launch_bf16_to_f16(x, x16, (size_t)T * L->hidden, stream);
     if (rc) return rc;
   }
-  return run_gate_up(L, x, x16, xp, T, k, offsets, row_token, h_rows, status, stream);
+  return run_gate_up(L, mean_rows(L, T, k), x, x16, xp, T, k, offsets, row_token, h_rows, status, stream);
 }
 
 int ccut_moe_down(const ccut_moe_layer* L, const uint16_t* h_rows, int T, int k, const int32_t* offsets,
@@ -415,7 +388,8 @@ int ccut_moe_down(const ccut_moe_layer* L, const uint16_t* h_rows, int T, int k,
   if (T == 0) return CCUT_OK;
   if (!h_rows || !offsets || !row_weight || !y_rows || !workspace) return CCUT_ERR_INVALID;
   if (ws_bytes < 256) return CCUT_ERR_WORKSPACE;
-  return run_down(L, h_rows, T, k, offsets, row_weight, y_rows, static_cast<int*>(workspace), stream);
+  return run_down(L, mean_rows(L, T, k), h_rows, T, k, offsets, row_weight, y_rows, static_cast<int*>(workspace),
+                  stream);
 }
 
 int ccut_moe_combine(const float* y_rows, const int32_t* pair_row, int T, int k, int H, int num_shared_slices,
@@ -425,7 +399,7 @@ int ccut_moe_combine(const float* y_rows, const int32_t* pair_row, int T, int k,
   if (out_dtype != CCUT_OUT_BF16 && out_dtype != CCUT_OUT_F32) return CCUT_ERR_INVALID;
   if (T == 0) return CCUT_OK;
   if (!y_rows || !pair_row || !out) return CCUT_ERR_INVALID;
-  return launch_combine(y_rows, pair_row, T, k, H, num_shared_slices, out, out_dtype, stream);
+  return launch_combine(y_rows, pair_row, T, k, H, num_shared_slices, -1, out, out_dtype, stream);
 }
 
 size_t ccut_moe_forward_workspace_bytes(const ccut_moe_layer* L, int T, int top_k) {
@@ -454,15 +428,15 @@ int ccut_moe_forward(const ccut_moe_layer* L, const ccut_route_params* rp, const
   FwdScratch s = carve_fwd(c, L, T, k);
   cudaStream_t st = stream;
   rc = launch_route(x, L->router, T, H, E, *rp, s.ids, s.wts, nullptr, s.part, s.counts,
-                    use_tc(L, T, k) ? nullptr : s.ffn.x16, st);  // x16: f16 operands of the mma.sync kernel
+                    use_tc(L, mean_rows(L, T, k)) ? nullptr : s.ffn.x16, st);  // x16: mma.sync operands
   if (rc) return rc;
   if (cudaMemsetAsync(s.pair_row, 0xFF, sizeof(int32_t) * (size_t)T * k, st) != cudaSuccess) return CCUT_ERR_CUDA;
   rc = launch_permute(s.ids, s.wts, T, k, E, L->num_shared_slices, L->shared_gate, s.counts, s.offsets, s.row_token,
                       s.row_weight, s.pair_row, st);
   if (rc) return rc;
-  rc = run_ffn(L, x, s.ffn, T, k, s.offsets, s.row_token, s.row_weight, s.ybuf, s.status, st);
+  rc = run_ffn(L, mean_rows(L, T, k), x, s.ffn, T, k, s.offsets, s.row_token, s.row_weight, s.ybuf, s.status, st);
   if (rc) return rc;
-  rc = launch_combine(s.ybuf, s.pair_row, T, k, H, L->num_shared_slices, out, out_dtype, st);
+  rc = launch_combine(s.ybuf, s.pair_row, T, k, H, L->num_shared_slices, -1, out, out_dtype, st);
   if (rc) return rc;
   if (ids && cudaMemcpyAsync(ids, s.ids, sizeof(int32_t) * (size_t)T * k, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
     return CCUT_ERR_CUDA;
@@ -496,7 +470,7 @@ int ccut_quant_linear(int format, int layout, const void* packed, int K, int N, 
   int rc = launch_fill_offsets(off, M, stream);
   if (rc) return rc;
   if (layout == CCUT_LAYOUT_ROWS) {
-    rc = launch_gather_f16(x, nullptr, M, K, x16, stream);
+    rc = launch_gather_f16(x, nullptr, M, nullptr, K, x16, stream);
     if (rc) return rc;
     const int nt = tc_token_tile(M);
     CUtensorMap map;

@@ -17,16 +17,16 @@ constexpr int kCombMaxRows = 16 + CCUT_MAX_SHARED_SLICES;  // top-k + shared sli
 template <bool kBf16Out>
 __global__ void __launch_bounds__(kCombThreads) combine_kernel(const float* __restrict__ y,
                                                                const int32_t* __restrict__ pair_row, int T, int k,
-                                                               int H, int slices, void* __restrict__ out) {
+                                                               int H, int slices, int shared_base,
+                                                               void* __restrict__ out) {
   __shared__ int rows[kCombMaxRows];
   const int t = blockIdx.x;
-  const int tk = T * k;
-  const int R = tk + slices * T;
+  const int R = shared_base + slices * T;
   if (threadIdx.x < k) {
     const int p = pair_row[(size_t)t * k + threadIdx.x];
     rows[threadIdx.x] = (p >= 0 && p < R) ? p : -1;
   } else if (threadIdx.x < k + slices) {
-    rows[threadIdx.x] = tk + (threadIdx.x - k) * T + t;
+    rows[threadIdx.x] = shared_base + (threadIdx.x - k) * T + t;
   }
   __syncthreads();
   const int n = k + slices;
@@ -58,15 +58,16 @@ __global__ void __launch_bounds__(kCombThreads) combine_kernel(const float* __re
   }
 }
 
-int launch_combine(const float* y, const int32_t* pair_row, int T, int k, int H, int slices, void* out,
-                   int out_dtype, cudaStream_t st) {
+int launch_combine(const float* y, const int32_t* pair_row, int T, int k, int H, int slices, int shared_base,
+                   void* out, int out_dtype, cudaStream_t st) {
   if (k < 1 || slices < 0 || k + slices > kCombMaxRows || H % 4) return CCUT_ERR_UNSUPPORTED;
   if (T == 0) return CCUT_OK;
+  if (shared_base < 0) shared_base = T * k;
   const dim3 grid(T, (H / 4 + kCombThreads - 1) / kCombThreads);
   if (out_dtype == CCUT_OUT_BF16)
-    combine_kernel<true><<<grid, kCombThreads, 0, st>>>(y, pair_row, T, k, H, slices, out);
+    combine_kernel<true><<<grid, kCombThreads, 0, st>>>(y, pair_row, T, k, H, slices, shared_base, out);
   else
-    combine_kernel<false><<<grid, kCombThreads, 0, st>>>(y, pair_row, T, k, H, slices, out);
+    combine_kernel<false><<<grid, kCombThreads, 0, st>>>(y, pair_row, T, k, H, slices, shared_base, out);
   return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
 }
 

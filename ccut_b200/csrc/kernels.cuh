@@ -43,8 +43,9 @@ int launch_tc_gemm(int fmt, int mode, int nt_tokens, const CUtensorMap& map, con
 // tmap.cu: 2-D f16 tensor map over a row-major [rows, cols] buffer, boxes of 64 x box_rows,
 // 128-byte swizzle (host side)
 int encode_rows_map(CUtensorMap* map, const void* base, int rows, int cols, int box_rows);
-int launch_gather_f16(const uint16_t* x_bf16, const int32_t* row_token, int R, int H, uint16_t* xp,
-                      cudaStream_t st);
+// nrows: device row count bound (rows >= *nrows are left alone), or null
+int launch_gather_f16(const uint16_t* x_bf16, const int32_t* row_token, int R, const int* nrows, int H,
+                      uint16_t* xp, cudaStream_t st);
 
 // pack.cu
 int launch_pack(int fmt, int layout, const void* q, const void* z, const void* s, int K, int N, int nibble_order,
@@ -65,8 +66,9 @@ int launch_count(const int32_t* ids, int n, int E, int* counts, cudaStream_t st)
 // gemm.cu
 int launch_gemm(int fmt, int mode, int mt, const GemmArgs& a, int num_sms, cudaStream_t st);
 // combine.cu
-int launch_combine(const float* y, const int32_t* pair_row, int T, int k, int H, int slices, void* out,
-                   int out_dtype, cudaStream_t st);
+// shared rows of slice s sit at shared_base + s * T (shared_base < 0: T * k)
+int launch_combine(const float* y, const int32_t* pair_row, int T, int k, int H, int slices, int shared_base,
+                   void* out, int out_dtype, cudaStream_t st);
 int launch_bf16_to_f16(const uint16_t* in, uint16_t* out, size_t n, cudaStream_t st);
 int launch_fill_offsets(int32_t* off, int m, cudaStream_t st);
 

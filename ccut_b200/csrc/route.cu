@@ -308,7 +308,8 @@ __global__ void __launch_bounds__(256) route_topk_kernel(const float* __restrict
 // later half of the chunks, `counts` minus the histogram of the pairs from the chunk on);
 // the third comes from rounds of 256 pairs: __match_any_sync ranks a pair inside its warp
 // and per-warp counters in shared memory rank the warps.  Pair ids outside [0, E) take no
-// row (their pair_row keeps the caller's -1).
+// row (their pair_row keeps the caller's -1), so the V valid pairs fill rows [0, V) and the
+// shared-expert slices follow at V + s * T (V = T * k when every id is valid).
 constexpr int kPermThreads = 256;
 constexpr int kPermWarps = kPermThreads / 32;
 
@@ -319,6 +320,7 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(
   __shared__ int base[kMaxExperts];
   __shared__ int hist[kMaxExperts];
   __shared__ int wcnt[kPermWarps][kMaxExperts];
+  __shared__ int s_valid;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tk = T * k;
   const int c0 = min(tk, blockIdx.x * chunk), c1 = min(tk, c0 + chunk);
@@ -341,11 +343,13 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(
       if (e < E) base[e] = carry + inc - c;
       carry += __shfl_sync(0xffffffffu, inc, 31);
     }
+    if (lane == 0) s_valid = carry;
   }
   __syncthreads();
+  const int valid = s_valid;
   if (blockIdx.x == 0) {
     for (int e = tid; e < E; e += kPermThreads) offsets[e] = base[e];
-    for (int s = tid; s <= slices; s += kPermThreads) offsets[E + s] = tk + s * T;
+    for (int s = tid; s <= slices; s += kPermThreads) offsets[E + s] = valid + s * T;
   }
   // pairs of each expert before the chunk
   const bool from_front = c0 <= tk - c0;
@@ -388,8 +392,8 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(
   // shared-expert rows: every token once per slice
   const int nsh = slices * T;
   for (int r = blockIdx.x * kPermThreads + tid; r < nsh; r += gridDim.x * kPermThreads) {
-    row_token[tk + r] = r % T;
-    row_weight[tk + r] = shared_gate;
+    row_token[valid + r] = r % T;
+    row_weight[valid + r] = shared_gate;
   }
 }
 

@@ -36,8 +36,9 @@ int encode_rows_map(CUtensorMap* map, const void* base, int rows, int cols, int 
 }
 
 __global__ void gather_f16_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ row_token, int R,
-                                  int H, uint16_t* __restrict__ xp) {
+                                  const int* __restrict__ nrows, int H, uint16_t* __restrict__ xp) {
   const int per_row = H / 8;
+  if (nrows && *nrows < R) R = *nrows;  // rows the permutation actually produced
   const size_t total = (size_t)R * per_row;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const int r = static_cast<int>(i / per_row), c = static_cast<int>(i % per_row);
@@ -54,12 +55,13 @@ __global__ void gather_f16_kernel(const uint16_t* __restrict__ x, const int32_t*
   }
 }
 
-int launch_gather_f16(const uint16_t* x_bf16, const int32_t* row_token, int R, int H, uint16_t* xp, cudaStream_t st) {
+int launch_gather_f16(const uint16_t* x_bf16, const int32_t* row_token, int R, const int* nrows, int H, uint16_t* xp,
+                      cudaStream_t st) {
   size_t total = (size_t)R * (H / 8);
   size_t blocks = (total + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
   if (blocks < 1) blocks = 1;
-  gather_f16_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(x_bf16, row_token, R, H, xp);
+  gather_f16_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(x_bf16, row_token, R, nrows, H, xp);
   return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
 }
 

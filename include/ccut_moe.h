@@ -235,6 +235,41 @@ CCUT_API int ccut_quant_linear(int format, int layout, const void* packed, int K
  * `stream`) and clears it. */
 CCUT_API int ccut_workspace_status(void* workspace, ccut_stream_t stream);
 
+/* ---- expert parallelism over NCCL (no reference counterpart: the reference runs a
+ * layer's experts in one process, ccut/models/generic.py:364-385,
+ * ccut/experts/pipeline.py:123-190) -------------------------------------------------- */
+/* One process per GPU.  Rank r holds routed experts [expert_lo, expert_lo + E_r) and every
+ * shared expert; all ranks pass the same T_local.  The communicator is non-blocking: init
+ * and every collective wait at most `timeout_s` seconds and then fail with
+ * CCUT_ERR_TIMEOUT instead of hanging. */
+typedef struct ccut_ep ccut_ep;
+/* Size of the NCCL unique id (host bytes) that rank 0 creates and every rank passes to
+ * ccut_ep_init. */
+CCUT_API size_t ccut_ep_unique_id_bytes(void);
+CCUT_API int ccut_ep_unique_id(void* id_out);
+/* Collective over `world` ranks; uses the current CUDA device. */
+CCUT_API int ccut_ep_init(const void* unique_id, int rank, int world, double timeout_s, ccut_ep** out);
+CCUT_API int ccut_ep_destroy(ccut_ep* ep);
+/* Dispatch: all-gather of the local tokens x bf16 [T_local, H], ids int32 [T_local, k] and
+ * routing weights fp32 [T_local, k] into [world * T_local, ...] (rank-major). */
+CCUT_API int ccut_moe_ep_dispatch(ccut_ep* ep, const uint16_t* x, const int32_t* ids,
+                                  const float* weights, int T_local, int H, int k, uint16_t* x_all,
+                                  int32_t* ids_all, float* w_all, ccut_stream_t stream);
+/* Combine: y_local fp32 [T_local, H] = sum over ranks of their partial outputs for this
+ * rank's tokens, from y_part fp32 [world * T_local, H] (reduce-scatter). */
+CCUT_API int ccut_moe_ep_combine(ccut_ep* ep, const float* y_part, int T_local, int H,
+                                 float* y_local, ccut_stream_t stream);
+/* Whole expert-parallel layer: route (against L->router, fp32 [E_global, H]), dispatch,
+ * local grouped FFN, combine, shared experts; out [T_local, H] bf16 or fp32.  L describes
+ * this rank's experts: num_experts = E_r routed experts (global ids expert_lo..), then the
+ * shared slices.  Every rank must call it, also with T_local = 0. */
+CCUT_API size_t ccut_moe_ep_forward_workspace_bytes(const ccut_moe_layer* L, int num_experts_global,
+                                                    int world, int T_local, int top_k);
+CCUT_API int ccut_moe_ep_forward(ccut_ep* ep, const ccut_moe_layer* L, int expert_lo,
+                                 int num_experts_global, const ccut_route_params* rp,
+                                 const uint16_t* x, int T_local, void* out, int out_dtype,
+                                 void* workspace, size_t ws_bytes, ccut_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
