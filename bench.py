@@ -192,6 +192,126 @@ def workload_config(wl: str, n: int, parallelism: str) -> dict:
 
 
 # ------------------------------------------------------------------ GPU leg
+# Kernels of this library per staged single-GPU step: route (logits, top-k), permute
+# (count, permute), gate/up (gather or f16 convert, GEMM), down (GEMM), combine.
+LAUNCHES_SINGLE = 8
+
+
+def ep_launches(cfg) -> int:
+    """Kernels of this library per expert-parallel step (NCCL's own kernels not counted):
+    route 2, localize 1, count 1, permute 1, routed FFN 3, combine 1, add/cast 1, and for
+    shared experts permute 1, FFN 3, combine 1."""
+    return 10 + (5 if cfg.num_shared else 0)
+
+
+def run_ep(args, wl, world: int, rank: int, local: int) -> None:
+    """Expert-parallel layer over `world` GPUs: the workload's tokens split evenly over the
+    ranks (strong scaling), routed experts sharded, NCCL all-gather / reduce-scatter."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from ccut_b200 import build
+    from ccut_b200.ep import ExpertParallelMoeLayer
+    from ccut_b200.synthetic import make_layer
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    if rank == 0:  # compile (if stale) once, before the other ranks load the library
+        build.build()
+    dist.barrier()
+    build.build()
+    cfg_name, T, bound = WORKLOADS[wl]
+    if T % world:
+        raise SystemExit(f"{T} tokens do not split over {world} ranks")
+    Tl = T // world
+    lw = make_layer(cfg_name, seed=0)
+    c = lw.cfg
+    ep = ExpertParallelMoeLayer(c.fmt, c.hidden, c.inter, c.num_experts, c.top_k, c.routing, lw.router, lw.experts,
+                                shared=lw.shared, shared_inter=c.shared_inter, n_group=c.n_group,
+                                topk_group=c.topk_group, routed_scaling=c.routed_scaling, device=dev, rank=rank,
+                                world=world, timeout_s=120.0)
+    xb = lw.make_x(T)[rank * Tl:(rank + 1) * Tl]
+    x = torch.from_numpy(xb.view(np.int16)).to(dev).view(torch.bfloat16)
+    del lw
+    for _ in range(max(args.warmup, 3)):
+        ep.forward(x)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    t_soak = time.perf_counter()
+    while time.perf_counter() - t_soak < args.soak:
+        ep.forward(x)
+        torch.cuda.synchronize()
+    K = args.steps
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist.barrier()
+    torch.cuda.synchronize()
+    start.record()
+    for _ in range(K):
+        ep.forward(x)
+    end.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = start.elapsed_time(end)
+    # end to end: pinned host tokens in, host bf16 out, every step
+    x_pin = torch.from_numpy(xb.view(np.int16)).view(torch.bfloat16).pin_memory()
+    out_pin = torch.empty((Tl, c.hidden), dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty_like(x)
+    for _ in range(2):
+        xd.copy_(x_pin, non_blocking=True)
+        out_pin.copy_(ep.forward(xd), non_blocking=True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(K):
+        xd.copy_(x_pin, non_blocking=True)
+        out_pin.copy_(ep.forward(xd), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    status = ep.workspace_status()
+    t = torch.tensor([ms, e2e_ms, float(status != 0)], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms, bad = float(t[0]), float(t[1]), float(t[2])
+    if rank == 0:
+        if bad:
+            raise SystemExit("device status word reports an expired wait")
+        pk, src = peaks()
+        flops_rank = layer_flops(c, T) / world
+        achieved = flops_rank * K / (ms * 1e-3) / 1e12
+        peak = pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+        roof = {"bound": "tensor" if bound == "tensor" else "hbm", "achieved": achieved, "peak": peak,
+                "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+                "kernel": "ccut_moe_ep_forward (whole layer per rank, collectives included)",
+                "algorithmic_flops_per_rank_step": flops_rank,
+                "peak_source": f"{src} (MEASURED_PEAKS.json)" if src == "measured" else "fallback"}
+        cfgd = workload_config(wl, 1, f"ep{world}")
+        cfgd["tokens_per_gpu"] = Tl
+        cfgd["global_tokens"] = T
+        cfgd["experts_per_gpu"] = c.num_experts // world
+        line = {
+            "metric": METRIC, "value": T * K / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16" if c.fmt == "awq_int4_g128" else "f16", "data": "synthetic",
+            "config": cfgd, "roofline": roof,
+            "e2e": {"value": T * K / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": T * c.hidden * 2,
+                    "d2h_bytes_per_step": T * c.hidden * 2},
+            "gpu_launches": ep_launches(c) * K,
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]},
+            "layer_tflops": layer_flops(c, T) * K / (ms * 1e-3) / 1e12,
+        }
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    ep.close()
+    dist.destroy_process_group()
+
+
 def run_ours(args, wl) -> None:
     import torch
     import torch.distributed as dist
@@ -204,12 +324,10 @@ def run_ours(args, wl) -> None:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if world > 1:
+        return run_ep(args, wl, world, rank, local)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-
-        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
     build.build()
     cfg_name, T, bound = WORKLOADS[wl]
     lw = make_layer(cfg_name, seed=0)
@@ -217,15 +335,14 @@ def run_ours(args, wl) -> None:
     L = MoeLayer(c.fmt, c.hidden, c.inter, c.num_experts, c.top_k, c.routing, lw.router, lw.experts,
                  shared=lw.shared, shared_inter=c.shared_inter, n_group=c.n_group, topk_group=c.topk_group,
                  routed_scaling=c.routed_scaling, device=dev)
-    xb_all = lw.make_x(T * world)
-    xb = xb_all[rank * T:(rank + 1) * T]
+    xb = lw.make_x(T)
     x = torch.from_numpy(xb.view(np.int16)).to(dev).view(torch.bfloat16)
     del lw
     use_graph = args.graph == "on" or (args.graph == "auto" and T <= 256)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
+    # the gate/up launch timed between ev0 and ev1: tcgen05 kernel (plus its activation
+    # gather) at >= CCUT_TC_MIN_ROWS mean rows per expert, else mma.sync (plus f16 convert)
+    tc_path = T * c.top_k / c.num_experts >= 64
+    kname = "tc_gemm_kernel<gate/up>" if tc_path else "moe_gemm_kernel<gate/up>"
 
     def step(ev0=None, ev1=None):
         r = L.route(x)
@@ -273,7 +390,6 @@ def run_ours(args, wl) -> None:
             step()
         torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
     torch.cuda.synchronize()
     start.record()
     if graph is not None:
@@ -283,7 +399,6 @@ def run_ours(args, wl) -> None:
             step(ev0[i], ev1[i])
     end.record()
     torch.cuda.synchronize()
-    barrier()
     ms = start.elapsed_time(end)
     kern_ms = [a.elapsed_time(b) for a, b in zip(ev0, ev1)]
 
@@ -296,7 +411,6 @@ def run_ours(args, wl) -> None:
         out_pin.copy_(L.forward(xd), non_blocking=True)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
     torch.cuda.synchronize()
     e0.record()
     for _ in range(K):
@@ -304,22 +418,12 @@ def run_ours(args, wl) -> None:
         out_pin.copy_(L.forward(xd), non_blocking=True)
     e1.record()
     torch.cuda.synchronize()
-    barrier()
     e2e_ms = e0.elapsed_time(e1)
     clk = clocks.stop()
     if L.workspace_status() != 0:
         raise SystemExit("device status word reports an expired wait")
 
-    if world > 1:
-        t = torch.tensor([ms, e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_ms = float(t[0]), float(t[1])
-        kt = torch.tensor([statistics.mean(kern_ms)], device=dev)
-        dist.all_reduce(kt, op=dist.ReduceOp.MAX)
-        kmean = float(kt[0])
-    else:
-        kmean = statistics.mean(kern_ms)
-
+    kmean = statistics.mean(kern_ms)
     if rank == 0:
         pk, src = peaks()
         byts, flops = gate_up_counts(c, offsets)
@@ -327,37 +431,34 @@ def run_ours(args, wl) -> None:
             achieved = byts / (kmean * 1e-3) / 1e9
             peak = pk.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
             roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                    "traffic": None, "kernel": "moe_gemm_kernel<gate/up>", "algorithmic_bytes_per_launch": byts}
+                    "traffic": None, "kernel": kname, "algorithmic_bytes_per_launch": byts}
         else:
             achieved = flops / (kmean * 1e-3) / 1e12
             peak = pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
             roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                    "frac": achieved / peak, "traffic": None, "kernel": "moe_gemm_kernel<gate/up>",
+                    "frac": achieved / peak, "traffic": None, "kernel": kname,
                     "algorithmic_flops_per_launch": flops}
         roof["peak_source"] = f"{src} (MEASURED_PEAKS.json)" if src == "measured" else "fallback"
         roof["kernel_ms"] = kmean
-        launches_per_step = 7 + (1 if c.fmt == "fp8_b128" else 0)
         line = {
-            "metric": METRIC, "value": world * T * K / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": K,
+            "metric": METRIC, "value": T * K / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": K,
             "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16" if c.fmt == "awq_int4_g128" else "f16", "data": "synthetic",
-            "config": workload_config(wl, world, "replicas" if world > 1 else "single"),
+            "config": workload_config(wl, 1, "single"),
             "roofline": roof,
-            "e2e": {"value": world * T * K / (e2e_ms * 1e-3), "unit": "tokens/s",
+            "e2e": {"value": T * K / (e2e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": T * c.hidden * 2, "d2h_bytes_per_step": T * c.hidden * 2},
-            "gpu_launches": launches_per_step * K,
+            "gpu_launches": LAUNCHES_SINGLE * K,
             "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]},
-            "layer_tflops": layer_flops(c, T) * world * K / (ms * 1e-3) / 1e12,
+            "layer_tflops": layer_flops(c, T) * K / (ms * 1e-3) / 1e12,
             "cuda_graph": use_graph,
         }
-        if world == 1 and not args.no_cpu_baseline:
+        if not args.no_cpu_baseline:
             r = cpu_sample_run(cfg_name, T, min(T, args.cpu_sample), 1, args.cpu_budget)
             line["cpu_baseline"] = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
         print(json.dumps(line), flush=True)
     if graph is not None:
         del graph
-    if world > 1:
-        dist.destroy_process_group()
 
 
 def main(argv=None) -> int:

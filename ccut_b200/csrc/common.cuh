@@ -102,7 +102,7 @@ CCUT_DEVICE bool mbar_spin(uint64_t* bar, uint32_t parity, int* status) {
   return true;
 }
 
-// ---- bulk async copy global -> shared (no tensor map, no multicast) ----------------
+// ---- bulk async copy global -> shared (no tensor map, one destination CTA) ---------
 // dst and src 16-byte aligned, bytes a multiple of 16.
 CCUT_DEVICE void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(

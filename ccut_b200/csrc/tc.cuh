@@ -108,7 +108,7 @@ CCUT_DEVICE void commit(uint64_t* bar) {
                : "memory");
 }
 
-// ---- TMA tiled load (no multicast) ----------------------------------------------------------
+// ---- TMA tiled load into this CTA only ------------------------------------------------------
 CCUT_DEVICE void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
