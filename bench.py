@@ -191,6 +191,11 @@ def workload_config(wl: str, n: int, parallelism: str) -> dict:
     }
 
 
+# DRAM bytes (read + write) of one gate/up launch from an ncu capture of the same workload
+# (profiles/tc_gemm_kernel_cfg1_prefill.md, profiles/moe_gemm_kernel_cfg0_decode.md);
+# workloads without a capture report null.
+NCU_TRAFFIC = {"cfg1_prefill": 482.6e6, "cfg0_decode": 202.3e6}
+
 # ------------------------------------------------------------------ GPU leg
 # Kernels of this library per staged single-GPU step: route (logits, top-k), permute
 # (count, permute), gate/up (gather or f16 convert, GEMM), down (GEMM), combine.
@@ -431,12 +436,12 @@ def run_ours(args, wl) -> None:
             achieved = byts / (kmean * 1e-3) / 1e9
             peak = pk.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
             roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                    "traffic": None, "kernel": kname, "algorithmic_bytes_per_launch": byts}
+                    "traffic": NCU_TRAFFIC.get(wl), "kernel": kname, "algorithmic_bytes_per_launch": byts}
         else:
             achieved = flops / (kmean * 1e-3) / 1e12
             peak = pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
             roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                    "frac": achieved / peak, "traffic": None, "kernel": kname,
+                    "frac": achieved / peak, "traffic": NCU_TRAFFIC.get(wl), "kernel": kname,
                     "algorithmic_flops_per_launch": flops}
         roof["peak_source"] = f"{src} (MEASURED_PEAKS.json)" if src == "measured" else "fallback"
         roof["kernel_ms"] = kmean

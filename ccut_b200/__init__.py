@@ -7,7 +7,9 @@ There is no CPU fallback: a missing library raises.
 Public entry points
 -------------------
 ``MoeLayer``                 HBM-resident MoE layer: ``forward``, ``route``, ``topk``,
-                             ``permute``, ``expert_ffn``, ``combine``, ``dequant``
+                             ``permute``, ``expert_ffn``, ``gate_up``, ``down``, ``combine``,
+                             ``dequant``
+``ep.ExpertParallelMoeLayer`` the same layer with routed experts sharded over GPUs (NCCL)
 ``blocks.moe``               drop-ins for ``ccut.blocks.moe`` / ``ccut.models.generic.moe_forward``
 ``quant``                    ``QuantizeMethodBase``-compatible AWQ-int4-g128 / FP8-block-128 methods
 """

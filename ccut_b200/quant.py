@@ -1,0 +1,152 @@
+"""``QuantizeMethodBase``-compatible linear methods for the two new weight formats.
+
+Mirrors the reference's method interface (``ccut/quant/method.py:27-62``):
+``create_weights(spec)`` checks the scale tensors once, ``apply(weight_bytes, scales, x)``
+returns ``y = x @ dequant(W)`` as fp32 ``[batch, out]``, and
+``process_weights_after_loading()`` is a hook.  ``apply`` packs the weight into the kernel
+tile layout on its first call (cached per weight buffer) and then runs
+``ccut_quant_linear`` on the GPU.  numpy in gives numpy out; torch in gives torch out.
+
+Formats (no reference implementation; the nearest reference methods are
+``ccut/quant/weight_only.py:37-54`` and ``ccut/quant/fp8.py:37-51``):
+  AWQ int4 g128    weight = qweight int32 [in, out/8]; scales = {"scales": fp16 [in/128, out],
+                   "qzeros": int32 [in/128, out/8]}
+  FP8 e4m3 b128    weight = e4m3 bytes [out, in]; scales = {"weight_scale_inv" (or "scale"):
+                   fp32 [out/128, in/128]}
+Missing scales raise ``ValueError`` and unknown formats ``NotImplementedError``, as in the
+reference.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+
+from ccut_b200 import _lib
+from ccut_b200.layer import _dev, _ptr, _stream
+
+__all__ = ["QuantizeMethodBase", "AwqInt4G128Method", "Fp8Block128Method", "make_method"]
+
+
+class QuantizeMethodBase:
+    """Interface of the reference's quantize methods."""
+
+    compute_path = "bf16"
+
+    def create_weights(self, spec=None) -> None:
+        return None
+
+    def apply(self, weight_bytes, scales: dict, x):
+        raise NotImplementedError
+
+    def process_weights_after_loading(self) -> None:
+        return None
+
+
+class _PackedLinear(QuantizeMethodBase):
+    fmt = ""
+    scale_names: tuple[tuple[str, ...], ...] = ()
+
+    def __init__(self, in_features: int, out_features: int, layout: str = "frags", device="cuda"):
+        if in_features % 128 or out_features % 128:
+            raise ValueError("in_features and out_features must be multiples of 128")
+        if layout not in _lib.LAYOUTS:
+            raise NotImplementedError(f"layout {layout!r} is not supported (have {sorted(_lib.LAYOUTS)})")
+        self.K, self.N = int(in_features), int(out_features)
+        self.layout = layout
+        self.device = torch.device(device)
+        self.lib = _lib.load()
+        self.code = _lib.FORMATS[self.fmt]
+        self._packed: dict = {}
+        self._ws: torch.Tensor | None = None
+
+    def create_weights(self, spec=None) -> None:
+        names = getattr(spec, "scales", None)
+        if spec is not None and not names:
+            raise ValueError(f"{getattr(spec, 'layer_name', 'layer')}: quantized layer has no scale tensors")
+
+    def _scale(self, scales: dict, names: tuple[str, ...]):
+        for n in names:
+            if n in scales:
+                return scales[n]
+        raise ValueError(f"missing scale tensor (one of {names})")
+
+    def _pack(self, weight_bytes, scales: dict) -> torch.Tensor:
+        key = (id(weight_bytes), tuple(id(scales.get(n)) for group in self.scale_names for n in group))
+        hit = self._packed.get(key)
+        if hit is not None:
+            return hit[0]
+        q, z, s = self._tensors(weight_bytes, scales)
+        packed = torch.empty(self.lib.ccut_packed_matrix_bytes(self.code, self.K, self.N), dtype=torch.uint8,
+                             device=self.device)
+        with torch.cuda.device(self.device):
+            _lib.call("ccut_pack_matrix", self.code, _lib.LAYOUTS[self.layout], _ptr(q), _ptr(z), _ptr(s), self.K,
+                      self.N, _lib.NIBBLES_AWQ, _ptr(packed), 1, 0, _stream())
+        self._packed[key] = (packed, weight_bytes)  # keep the source alive: its id is the key
+        return packed
+
+    def apply(self, weight_bytes, scales: dict, x):
+        packed = self._pack(weight_bytes, scales)
+        was_np = not isinstance(x, torch.Tensor)
+        xt = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)) if was_np else x
+        if xt.dim() != 2 or xt.shape[1] != self.K:
+            raise ValueError(f"x must be [batch, {self.K}], got {tuple(xt.shape)}")
+        xb = xt.to(self.device, torch.bfloat16).contiguous()
+        M = xb.shape[0]
+        y = torch.empty((M, self.N), dtype=torch.float32, device=self.device)
+        if M:
+            nbytes = self.lib.ccut_quant_linear_workspace_bytes(self.code, M, self.K)
+            if self._ws is None or self._ws.numel() < nbytes:
+                self._ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+            with torch.cuda.device(self.device):
+                _lib.call("ccut_quant_linear", self.code, _lib.LAYOUTS[self.layout], _ptr(packed), self.K, self.N,
+                          _ptr(xb), M, _ptr(y), _ptr(self._ws), self._ws.numel(), _stream())
+        return y.cpu().numpy() if was_np else y
+
+
+class AwqInt4G128Method(_PackedLinear):
+    """W4A16: unsigned int4 weights, group-128 zero-points and fp16 scales along the input."""
+
+    compute_path = "w4a16"
+    fmt = "awq_int4_g128"
+    scale_names = (("scales",), ("qzeros", "zeros"))
+
+    def _tensors(self, weight_bytes, scales):
+        q = _as_array(weight_bytes, np.int32).reshape(self.K, self.N // 8)
+        s = np.asarray(self._scale(scales, ("scales",)), dtype=np.float16).reshape(self.K // 128, self.N)
+        z = np.asarray(self._scale(scales, ("qzeros", "zeros")), dtype=np.int32).reshape(self.K // 128, self.N // 8)
+        return (_dev(q, self.device, torch.int32), _dev(z, self.device, torch.int32),
+                _dev(s, self.device, torch.float16))
+
+
+class Fp8Block128Method(_PackedLinear):
+    """W8A16: e4m3 weights with one fp32 scale per 128 x 128 block."""
+
+    compute_path = "w8a16"
+    fmt = "fp8_b128"
+    scale_names = (("weight_scale_inv", "scale"),)
+
+    def _tensors(self, weight_bytes, scales):
+        w = _as_array(weight_bytes, np.uint8).reshape(self.N, self.K)
+        s = np.asarray(self._scale(scales, ("weight_scale_inv", "scale")), dtype=np.float32).reshape(
+            self.N // 128, self.K // 128)
+        return _dev(w, self.device, torch.uint8), None, _dev(s, self.device, torch.float32)
+
+
+def _as_array(b, dtype) -> np.ndarray:
+    if isinstance(b, torch.Tensor):
+        return b.detach().cpu().numpy().view(dtype)
+    if isinstance(b, (bytes, bytearray, memoryview)):
+        return np.frombuffer(b, dtype=dtype).copy()
+    return np.asarray(b).view(dtype)
+
+
+def make_method(fmt: str, in_features: int, out_features: int, **kw) -> QuantizeMethodBase:
+    """Format name -> method (``"awq_int4_g128"`` | ``"fp8_b128"``)."""
+    if fmt == "awq_int4_g128":
+        return AwqInt4G128Method(in_features, out_features, **kw)
+    if fmt == "fp8_b128":
+        return Fp8Block128Method(in_features, out_features, **kw)
+    raise NotImplementedError(f"weight format {fmt!r} is not supported")
