@@ -28,9 +28,9 @@
 //                 warp loads its next chunk from tensor memory before storing the current one
 // The weight ring has its own full/empty barriers (released by the dequant warps); a stage's
 // A buffer and activation tile share one "ready" barrier (dequant arrivals plus the TMA's
-// bytes) and one "done" barrier (a single MMA commit), because every extra commit or wait
-// in the single MMA-issuing thread costs tensor throughput.  Accumulators have their own
-// pair.  Every wait is bounded.
+// bytes) and one "done" barrier (one MMA commit per issuer), because every extra commit or
+// wait in an MMA-issuing thread costs tensor throughput.  Accumulators have their own pair.
+// Every wait is bounded.
 //
 // Follows ccut/blocks/moe.py:122-141 (expert_ffn), ccut/quant/kernels.py:219-231 (SiLU),
 // the dequant of ccut/quant/kernels.py:150-171 / :276-295 (restated for the group-128 /
