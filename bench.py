@@ -204,9 +204,9 @@ LAUNCHES_SINGLE = 8
 
 def ep_launches(cfg) -> int:
     """Kernels of this library per expert-parallel step (NCCL's own kernels not counted):
-    route 2, localize 1, count 1, permute 1, routed FFN 3, combine 1, add/cast 1, and for
+    route 2, localize + count 1, permute 1, routed FFN 3, combine 1, add/cast 1, and for
     shared experts permute 1, FFN 3, combine 1."""
-    return 10 + (5 if cfg.num_shared else 0)
+    return 9 + (5 if cfg.num_shared else 0)
 
 
 def run_ep(args, wl, world: int, rank: int, local: int) -> None:
@@ -244,18 +244,44 @@ def run_ep(args, wl, world: int, rank: int, local: int) -> None:
     for _ in range(max(args.warmup, 3)):
         ep.forward(x)
     torch.cuda.synchronize()
+    K = args.steps
+    # The K timed steps replay as one CUDA graph, NCCL calls included: a step enqueues ~25
+    # operations, which the host issues no faster than 4-8 GPUs finish them.  The graph is
+    # reset before the communicator is destroyed.
+    graph = None
+    if args.graph in ("auto", "on"):
+        graph = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream(device=dev)
+        cap.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(cap):
+            ep.forward(x)
+            torch.cuda.synchronize()
+            with torch.cuda.graph(graph, stream=cap):
+                for _ in range(K):
+                    ep.forward(x)
+        torch.cuda.current_stream().wait_stream(cap)
+        torch.cuda.synchronize()
+        dist.barrier()
+        graph.replay()
+        torch.cuda.synchronize()
+
+    def timed_steps():
+        if graph is not None:
+            graph.replay()
+        else:
+            for _ in range(K):
+                ep.forward(x)
+
     clocks = ClockSampler(local)
     t_soak = time.perf_counter()
     while time.perf_counter() - t_soak < args.soak:
-        ep.forward(x)
+        timed_steps()
         torch.cuda.synchronize()
-    K = args.steps
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     dist.barrier()
     torch.cuda.synchronize()
     start.record()
-    for _ in range(K):
-        ep.forward(x)
+    timed_steps()
     end.record()
     torch.cuda.synchronize()
     dist.barrier()
@@ -310,8 +336,13 @@ def run_ep(args, wl, world: int, rank: int, local: int) -> None:
             "gpu_launches": ep_launches(c) * K,
             "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]},
             "layer_tflops": layer_flops(c, T) * K / (ms * 1e-3) / 1e12,
+            "cuda_graph": graph is not None,
         }
         print(json.dumps(line), flush=True)
+    if graph is not None:
+        graph.reset()  # drop the captured NCCL work before the communicator goes
+        graph = None
+    torch.cuda.synchronize()
     dist.barrier()
     ep.close()
     dist.destroy_process_group()

@@ -9,11 +9,11 @@
 //      row), permute them by local expert and run the grouped expert FFN on them only;
 //   4. combine the local rows per token (fp32 [T, H], zero for tokens with no local
 //      expert) and reduce-scatter it: rank r receives the sum over ranks of its T_r rows;
-//   5. shared experts run data-parallel on the local tokens and are added in.
+//   5. shared experts run data-parallel on the local tokens and are added in; they only need
+//      the local tokens, so they run on a second stream while the dispatch is in flight.
 // The reference runs the experts of one layer in a single process
 // (ccut/models/generic.py:364-385, ccut/experts/pipeline.py:123-190); the partitioning is
-// new.  NCCL communicators are created non-blocking so that init and every call wait on a
-// time limit instead of hanging.
+// new.  One blocking NCCL communicator per layer handle carries the collectives.
 #include <nccl.h>
 
 #include <chrono>
@@ -28,6 +28,8 @@ struct ccut_ep {
   int rank;
   int world;
   double timeout_s;
+  cudaStream_t side;  // shared experts run here, beside the dispatch collective
+  cudaEvent_t fork, join;
 };
 
 namespace ccut {
@@ -45,14 +47,26 @@ int nccl_settle(ncclComm_t comm, ncclResult_t r, double budget_s) {
   return r == ncclSuccess ? CCUT_OK : CCUT_ERR_NCCL;
 }
 
-// ids_loc[i] = ids[i] - lo when expert ids[i] is local, else -1; weights copied.
-__global__ void localize_kernel(const int32_t* __restrict__ ids, const float* __restrict__ w, int n, int lo,
-                                int e_local, int32_t* __restrict__ ids_loc, float* __restrict__ w_loc) {
+// ids_loc[i] = ids[i] - lo when expert ids[i] is local, else -1; weights copied; counts[e]
+// of the local experts accumulated (shared-memory histogram, then one atomic per expert
+// and CTA).  counts must start at zero.
+__global__ void __launch_bounds__(256) localize_count_kernel(const int32_t* __restrict__ ids,
+                                                             const float* __restrict__ w, int n, int lo, int e_local,
+                                                             int32_t* __restrict__ ids_loc,
+                                                             float* __restrict__ w_loc, int* __restrict__ counts) {
+  __shared__ int hist[kMaxExperts];
+  for (int e = threadIdx.x; e < e_local; e += blockDim.x) hist[e] = 0;
+  __syncthreads();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const int e = ids[i] - lo;
-    ids_loc[i] = (e >= 0 && e < e_local) ? e : -1;
+    const bool mine = e >= 0 && e < e_local;
+    ids_loc[i] = mine ? e : -1;
     w_loc[i] = w[i];
+    if (mine) atomicAdd(&hist[e], 1);
   }
+  __syncthreads();
+  for (int e = threadIdx.x; e < e_local; e += blockDim.x)
+    if (hist[e]) atomicAdd(&counts[e], hist[e]);
 }
 
 // out = a (+ b), fp32 -> bf16 or fp32.
@@ -231,20 +245,24 @@ int ccut_ep_init(const void* unique_id, int rank, int world, double timeout_s, c
   *out = nullptr;
   ncclUniqueId id;
   std::memcpy(&id, unique_id, sizeof(id));
-  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
-  cfg.blocking = 0;
+  // A blocking communicator: init returns once every rank has joined (the caller bounds
+  // that wait: the unique id reaches the ranks through a collective with a timeout, and the
+  // process has its own limit); collectives are enqueued without host polling.
   ncclComm_t comm = nullptr;
-  ncclResult_t r = ncclCommInitRankConfig(&comm, world, id, rank, &cfg);
-  if (r != ncclSuccess && r != ncclInProgress) return CCUT_ERR_NCCL;
-  const int rc = nccl_settle(comm, r, timeout_s);
-  if (rc) {
+  if (ncclCommInitRank(&comm, world, id, rank) != ncclSuccess) {
     if (comm) ncclCommAbort(comm);
-    return rc;
+    return CCUT_ERR_NCCL;
   }
-  ccut_ep* ep = new (std::nothrow) ccut_ep{comm, rank, world, timeout_s};
+  ccut_ep* ep = new (std::nothrow) ccut_ep{comm, rank, world, timeout_s, nullptr, nullptr, nullptr};
   if (!ep) {
     ncclCommAbort(comm);
     return CCUT_ERR_INVALID;
+  }
+  if (cudaStreamCreateWithFlags(&ep->side, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&ep->fork, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&ep->join, cudaEventDisableTiming) != cudaSuccess) {
+    ccut_ep_destroy(ep);
+    return CCUT_ERR_CUDA;
   }
   *out = ep;
   return CCUT_OK;
@@ -261,6 +279,9 @@ int ccut_ep_destroy(ccut_ep* ep) {
       ncclCommAbort(ep->comm);
     }
   }
+  if (ep->side) cudaStreamDestroy(ep->side);
+  if (ep->fork) cudaEventDestroy(ep->fork);
+  if (ep->join) cudaEventDestroy(ep->join);
   delete ep;
   return rc;
 }
@@ -319,6 +340,31 @@ int ccut_moe_ep_forward(ccut_ep* ep, const ccut_moe_layer* L, int expert_lo, int
   Carver c(workspace);
   EpScratch s = carve_ep(c, L, num_experts_global, ep->world, T_local, k);
 
+  // 5 (forked). shared experts on the local tokens, on the side stream: no routed pair is
+  //    valid there, so every row belongs to a shared slice (rows s * T_local + t)
+  const bool shared = S > 0 && T_local > 0;
+  if (shared) {
+    cudaStream_t ss = ep->side;
+    if (cudaEventRecord(ep->fork, st) != cudaSuccess || cudaStreamWaitEvent(ss, ep->fork, 0) != cudaSuccess)
+      return CCUT_ERR_CUDA;
+    if (cudaMemsetAsync(s.sh_ids, 0xFF, sizeof(int32_t) * T_local, ss) != cudaSuccess) return CCUT_ERR_CUDA;
+    if (cudaMemsetAsync(s.sh_pair_row, 0xFF, sizeof(int32_t) * T_local, ss) != cudaSuccess) return CCUT_ERR_CUDA;
+    if (cudaMemsetAsync(s.sh_counts, 0, sizeof(int), ss) != cudaSuccess) return CCUT_ERR_CUDA;
+    rc = launch_permute(s.sh_ids, s.sh_w, T_local, 1, 1, S, L->shared_gate, s.sh_counts, s.sh_offsets,
+                        s.sh_row_token, s.sh_row_weight, s.sh_pair_row, ss);
+    if (rc) return rc;
+    const ccut_moe_layer sv = with_policy(shared_view(L), T_local);
+    if (sv.kernel == CCUT_KERNEL_MMA) {
+      rc = launch_bf16_to_f16(x, s.sh_ffn.x16, (size_t)T_local * H, ss);
+      if (rc) return rc;
+    }
+    rc = run_ffn(&sv, T_local, x, s.sh_ffn, T_local, 1, s.sh_offsets, s.sh_row_token, s.sh_row_weight, s.sh_ybuf,
+                 s.status, ss);
+    if (rc) return rc;
+    rc = launch_combine(s.sh_ybuf, s.sh_pair_row, T_local, 1, H, S, 0, s.y_sh, CCUT_OUT_F32, ss);
+    if (rc) return rc;
+    if (cudaEventRecord(ep->join, ss) != cudaSuccess) return CCUT_ERR_CUDA;
+  }
   // 1. route the local tokens (global expert ids)
   if (T_local > 0) {
     rc = launch_route(x, L->router, T_local, H, num_experts_global, *rp, s.ids_l, s.w_l, nullptr, s.part,
@@ -329,12 +375,11 @@ int ccut_moe_ep_forward(ccut_ep* ep, const ccut_moe_layer* L, int expert_lo, int
   rc = ep_allgather(ep, x, s.ids_l, s.w_l, T_local, H, k, s.x_all, s.ids_all, s.w_all, st);
   if (rc) return rc;
   // 3. local pairs -> permutation -> grouped FFN over the local experts
-  localize_kernel<<<grid_for((size_t)T * k, 256), 256, 0, st>>>(s.ids_all, s.w_all, T * k, expert_lo, E_l,
-                                                                  s.ids_loc, s.w_loc);
+  if (cudaMemsetAsync(s.counts, 0, sizeof(int) * E_l, st) != cudaSuccess) return CCUT_ERR_CUDA;
+  localize_count_kernel<<<grid_for((size_t)T * k, 256 * 4), 256, 0, st>>>(s.ids_all, s.w_all, T * k, expert_lo,
+                                                                          E_l, s.ids_loc, s.w_loc, s.counts);
   if (cudaPeekAtLastError() != cudaSuccess) return CCUT_ERR_CUDA;
   if (cudaMemsetAsync(s.pair_row, 0xFF, sizeof(int32_t) * (size_t)T * k, st) != cudaSuccess) return CCUT_ERR_CUDA;
-  rc = launch_count(s.ids_loc, T * k, E_l, s.counts, st);
-  if (rc) return rc;
   rc = launch_permute(s.ids_loc, s.w_loc, T, k, E_l, 0, 0.f, s.counts, s.offsets, s.row_token, s.row_weight,
                       s.pair_row, st);
   if (rc) return rc;
@@ -352,29 +397,10 @@ int ccut_moe_ep_forward(ccut_ep* ep, const ccut_moe_layer* L, int expert_lo, int
   rc = ep_reduce_scatter(ep, s.y_part, T_local, H, s.y_loc, st);
   if (rc) return rc;
   if (T_local == 0) return CCUT_OK;
-  // 5. shared experts on the local tokens: no routed pair is valid, so every row belongs to
-  //    a shared slice (rows s * T_local + t)
-  if (S > 0) {
-    if (cudaMemsetAsync(s.sh_ids, 0xFF, sizeof(int32_t) * T_local, st) != cudaSuccess) return CCUT_ERR_CUDA;
-    if (cudaMemsetAsync(s.sh_pair_row, 0xFF, sizeof(int32_t) * T_local, st) != cudaSuccess) return CCUT_ERR_CUDA;
-    if (cudaMemsetAsync(s.sh_counts, 0, sizeof(int), st) != cudaSuccess) return CCUT_ERR_CUDA;
-    rc = launch_permute(s.sh_ids, s.sh_w, T_local, 1, 1, S, L->shared_gate, s.sh_counts, s.sh_offsets,
-                        s.sh_row_token, s.sh_row_weight, s.sh_pair_row, st);
-    if (rc) return rc;
-    const ccut_moe_layer sv = with_policy(shared_view(L), T_local);
-    if (sv.kernel == CCUT_KERNEL_MMA) {
-      rc = launch_bf16_to_f16(x, s.sh_ffn.x16, (size_t)T_local * H, st);
-      if (rc) return rc;
-    }
-    rc = run_ffn(&sv, T_local, x, s.sh_ffn, T_local, 1, s.sh_offsets, s.sh_row_token, s.sh_row_weight, s.sh_ybuf,
-                 s.status, st);
-    if (rc) return rc;
-    rc = launch_combine(s.sh_ybuf, s.sh_pair_row, T_local, 1, H, S, 0, s.y_sh, CCUT_OUT_F32, st);
-    if (rc) return rc;
-  }
+  if (shared && cudaStreamWaitEvent(st, ep->join, 0) != cudaSuccess) return CCUT_ERR_CUDA;
   const size_t n4 = (size_t)T_local * H / 4;
   add_cast_kernel<<<grid_for(n4, 256), 256, 0, st>>>(reinterpret_cast<const float4*>(s.y_loc),
-                                                      S > 0 ? reinterpret_cast<const float4*>(s.y_sh) : nullptr, n4,
+                                                      shared ? reinterpret_cast<const float4*>(s.y_sh) : nullptr, n4,
                                                       out, out_dtype);
   return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
 }

@@ -239,9 +239,10 @@ CCUT_API int ccut_workspace_status(void* workspace, ccut_stream_t stream);
  * layer's experts in one process, ccut/models/generic.py:364-385,
  * ccut/experts/pipeline.py:123-190) -------------------------------------------------- */
 /* One process per GPU.  Rank r holds routed experts [expert_lo, expert_lo + E_r) and every
- * shared expert; all ranks pass the same T_local.  The communicator is non-blocking: init
- * and every collective wait at most `timeout_s` seconds and then fail with
- * CCUT_ERR_TIMEOUT instead of hanging. */
+ * shared expert; all ranks pass the same T_local.  ccut_ep_init is collective and returns
+ * once every rank has joined: distribute the unique id through a channel with a timeout
+ * (e.g. a torch.distributed broadcast) so that a missing rank fails there.  `timeout_s`
+ * bounds the host waits of ccut_ep_destroy. */
 typedef struct ccut_ep ccut_ep;
 /* Size of the NCCL unique id (host bytes) that rank 0 creates and every rank passes to
  * ccut_ep_init. */
