@@ -76,6 +76,117 @@ __device__ __forceinline__ void decode_item(int item, const int* tprefix, int nu
   rows = min(MT, me - m0);
 }
 
+// The k loop of one item: per 128-k stage wait for the staged block(s), dequantize, issue
+// the MMAs of the NB active 8-token column blocks (NB = 0: the runtime count nblk), release
+// the stage and promote the scaled partial into acc.  A compile-time NB leaves no
+// predicated-off MMAs in the unrolled loop.  Returns false when a bounded wait expired.
+template <int FMT, int MODE, int MT, int NB>
+__device__ __forceinline__ bool consume_item(const GemmArgs& a, uint8_t* stages, uint64_t* full, uint64_t* empty,
+                                             int ktiles, int nblk, int warp, int lane, int ch_lo, int ch_hi,
+                                             int& use,
+                                             float (&acc)[GemmCfg<FMT, MODE, MT>::kNMat][MT / 8][4]) {
+  using C = GemmCfg<FMT, MODE, MT>;
+  using B = typename C::B;
+  constexpr int S = C::kStages;
+  const int nb = NB > 0 ? NB : nblk;
+  for (int kt = 0; kt < ktiles; ++kt, ++use) {
+    const int s = use % S;
+    GM_PROF_START(c0);
+    if (!mbar_wait(&full[s], (use / S) & 1, a.status)) return false;
+    if (threadIdx.x == 0) GM_PROF_ADD(1, c0);
+    GM_PROF_START(c1);
+    const uint8_t* st = stages + s * C::kStageBytes;
+    const uint8_t* xs = st + C::kWBytes;
+    float part[C::kNMat][MT / 8][4];
+#pragma unroll
+    for (int m = 0; m < C::kNMat; ++m)
+#pragma unroll
+      for (int b = 0; b < MT / 8; ++b)
+        if (b < nb)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) part[m][b][i] = 0.f;
+
+    // per-stage scale (and AWQ zero-point) of this lane's two channels
+    float sc_lo[C::kNMat], sc_hi[C::kNMat];
+    uint32_t zp_lo[C::kNMat], zp_hi[C::kNMat];  // AWQ: f16x2 1024 + z (lo), -(64 + z) (hi)
+#pragma unroll
+    for (int m = 0; m < C::kNMat; ++m) {
+      const uint8_t* blk = st + m * B::kBytes;
+      if constexpr (FMT == CCUT_FMT_AWQ_INT4_G128) {
+        const uint16_t* sc = reinterpret_cast<const uint16_t*>(blk + B::kScaleOff);
+        sc_lo[m] = __half2float(__ushort_as_half(sc[ch_lo]));
+        sc_hi[m] = __half2float(__ushort_as_half(sc[ch_hi]));
+        zp_lo[m] = zero_pair_f16_1024(blk[B::kZeroOff + (ch_lo >> 1)] >> (4 * (ch_lo & 1)));
+        zp_hi[m] = zero_pair_f16_neg64(blk[B::kZeroOff + (ch_hi >> 1)] >> (4 * (ch_hi & 1)));
+      } else {
+        sc_lo[m] = sc_hi[m] = reinterpret_cast<const float*>(blk + B::kScaleOff)[0];
+        zp_lo[m] = zp_hi[m] = 0;
+      }
+    }
+
+#pragma unroll
+    for (int kc = 0; kc < B::kChunks; ++kc) {
+      uint4 raw[C::kNMat];
+#pragma unroll
+      for (int m = 0; m < C::kNMat; ++m)
+        raw[m] = *reinterpret_cast<const uint4*>(st + m * B::kBytes + ((warp * B::kChunks + kc) * 32 + lane) * 16);
+#pragma unroll
+      for (int j = 0; j < B::kStepsPerChunk; ++j) {
+        uint32_t af[C::kNMat][4];
+#pragma unroll
+        for (int m = 0; m < C::kNMat; ++m) {
+          if constexpr (FMT == CCUT_FMT_AWQ_INT4_G128) {
+            const uint32_t wd = j == 0 ? raw[m].x : j == 1 ? raw[m].y : j == 2 ? raw[m].z : raw[m].w;
+            // a0/a2: channel ch_lo (nibbles 0,4 / 2,6); a1/a3: ch_hi (nibbles 1,5 / 3,7)
+            af[m][0] = nib_lo_to_f16x2_minus(wd, zp_lo[m]);
+            af[m][1] = nib_hi_to_f16x2_minus(wd, zp_hi[m]);
+            af[m][2] = nib_lo_to_f16x2_minus(wd >> 8, zp_lo[m]);
+            af[m][3] = nib_hi_to_f16x2_minus(wd >> 8, zp_hi[m]);
+          } else {
+            const uint32_t w0 = j == 0 ? raw[m].x : raw[m].z;
+            const uint32_t w1 = j == 0 ? raw[m].y : raw[m].w;
+            af[m][0] = e4m3x2_to_f16x2(static_cast<uint16_t>(w0));
+            af[m][1] = e4m3x2_to_f16x2(static_cast<uint16_t>(w0 >> 16));
+            af[m][2] = e4m3x2_to_f16x2(static_cast<uint16_t>(w1));
+            af[m][3] = e4m3x2_to_f16x2(static_cast<uint16_t>(w1 >> 16));
+          }
+        }
+        const int koff = kc * B::kChunkK + j * 16;
+#pragma unroll
+        for (int b = 0; b < MT / 8; b += 2) {
+          if (b < nb) {
+            const int tok = 8 * (b + (lane >> 4)) + (lane & 7);
+            const int kk = koff + ((lane >> 3) & 1) * 8;
+            uint32_t r0, r1, r2, r3;
+            ldmatrix_x4(r0, r1, r2, r3, xs + tok * C::kXRow + kk * 2);
+#pragma unroll
+            for (int m = 0; m < C::kNMat; ++m) {
+              mma_16816<B::kBf16>(part[m][b], af[m], r0, r1);
+              if (b + 1 < nb) mma_16816<B::kBf16>(part[m][b + 1], af[m], r2, r3);
+            }
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    if (threadIdx.x == 0) GM_PROF_ADD(2, c1);
+    // promote: acc += scale * partial (fp32)
+#pragma unroll
+    for (int m = 0; m < C::kNMat; ++m)
+#pragma unroll
+      for (int b = 0; b < MT / 8; ++b) {
+        if (b >= nb) continue;
+        acc[m][b][0] = fmaf(sc_lo[m], part[m][b][0], acc[m][b][0]);
+        acc[m][b][1] = fmaf(sc_lo[m], part[m][b][1], acc[m][b][1]);
+        acc[m][b][2] = fmaf(sc_hi[m], part[m][b][2], acc[m][b][2]);
+        acc[m][b][3] = fmaf(sc_hi[m], part[m][b][3], acc[m][b][3]);
+      }
+  }
+
+  return true;
+}
+
 template <int FMT, int MODE, int MT>
 __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT, MODE, MT>::kMinBlocks)
     moe_gemm_kernel(GemmArgs a) {
@@ -180,100 +291,19 @@ __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT,
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[m][b][i] = 0.f;
 
-    for (int kt = 0; kt < ktiles; ++kt, ++use) {
-      const int s = use % S;
-      GM_PROF_START(c0);
-      if (!mbar_wait(&full[s], (use / S) & 1, a.status)) return;
-      if (threadIdx.x == 0) GM_PROF_ADD(1, c0);
-      GM_PROF_START(c1);
-      const uint8_t* st = stages + s * C::kStageBytes;
-      const uint8_t* xs = st + C::kWBytes;
-      float part[C::kNMat][MT / 8][4];
-#pragma unroll
-      for (int m = 0; m < C::kNMat; ++m)
-#pragma unroll
-        for (int b = 0; b < MT / 8; ++b)
-          if (b < nblk)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) part[m][b][i] = 0.f;
-
-      // per-stage scale (and AWQ zero-point) of this lane's two channels
-      float sc_lo[C::kNMat], sc_hi[C::kNMat];
-      uint32_t zp_lo[C::kNMat], zp_hi[C::kNMat];  // AWQ: f16x2 1024 + z (lo), -(64 + z) (hi)
-#pragma unroll
-      for (int m = 0; m < C::kNMat; ++m) {
-        const uint8_t* blk = st + m * B::kBytes;
-        if constexpr (FMT == CCUT_FMT_AWQ_INT4_G128) {
-          const uint16_t* sc = reinterpret_cast<const uint16_t*>(blk + B::kScaleOff);
-          sc_lo[m] = __half2float(__ushort_as_half(sc[ch_lo]));
-          sc_hi[m] = __half2float(__ushort_as_half(sc[ch_hi]));
-          zp_lo[m] = zero_pair_f16_1024(blk[B::kZeroOff + (ch_lo >> 1)] >> (4 * (ch_lo & 1)));
-          zp_hi[m] = zero_pair_f16_neg64(blk[B::kZeroOff + (ch_hi >> 1)] >> (4 * (ch_hi & 1)));
-        } else {
-          sc_lo[m] = sc_hi[m] = reinterpret_cast<const float*>(blk + B::kScaleOff)[0];
-          zp_lo[m] = zp_hi[m] = 0;
-        }
-      }
-
-#pragma unroll
-      for (int kc = 0; kc < B::kChunks; ++kc) {
-        uint4 raw[C::kNMat];
-#pragma unroll
-        for (int m = 0; m < C::kNMat; ++m)
-          raw[m] = *reinterpret_cast<const uint4*>(st + m * B::kBytes + ((warp * B::kChunks + kc) * 32 + lane) * 16);
-#pragma unroll
-        for (int j = 0; j < B::kStepsPerChunk; ++j) {
-          uint32_t af[C::kNMat][4];
-#pragma unroll
-          for (int m = 0; m < C::kNMat; ++m) {
-            if constexpr (FMT == CCUT_FMT_AWQ_INT4_G128) {
-              const uint32_t wd = j == 0 ? raw[m].x : j == 1 ? raw[m].y : j == 2 ? raw[m].z : raw[m].w;
-              // a0/a2: channel ch_lo (nibbles 0,4 / 2,6); a1/a3: ch_hi (nibbles 1,5 / 3,7)
-              af[m][0] = nib_lo_to_f16x2_minus(wd, zp_lo[m]);
-              af[m][1] = nib_hi_to_f16x2_minus(wd, zp_hi[m]);
-              af[m][2] = nib_lo_to_f16x2_minus(wd >> 8, zp_lo[m]);
-              af[m][3] = nib_hi_to_f16x2_minus(wd >> 8, zp_hi[m]);
-            } else {
-              const uint32_t w0 = j == 0 ? raw[m].x : raw[m].z;
-              const uint32_t w1 = j == 0 ? raw[m].y : raw[m].w;
-              af[m][0] = e4m3x2_to_f16x2(static_cast<uint16_t>(w0));
-              af[m][1] = e4m3x2_to_f16x2(static_cast<uint16_t>(w0 >> 16));
-              af[m][2] = e4m3x2_to_f16x2(static_cast<uint16_t>(w1));
-              af[m][3] = e4m3x2_to_f16x2(static_cast<uint16_t>(w1 >> 16));
-            }
-          }
-          const int koff = kc * B::kChunkK + j * 16;
-#pragma unroll
-          for (int b = 0; b < MT / 8; b += 2) {
-            if (b < nblk) {
-              const int tok = 8 * (b + (lane >> 4)) + (lane & 7);
-              const int kk = koff + ((lane >> 3) & 1) * 8;
-              uint32_t r0, r1, r2, r3;
-              ldmatrix_x4(r0, r1, r2, r3, xs + tok * C::kXRow + kk * 2);
-#pragma unroll
-              for (int m = 0; m < C::kNMat; ++m) {
-                mma_16816<B::kBf16>(part[m][b], af[m], r0, r1);
-                if (b + 1 < nblk) mma_16816<B::kBf16>(part[m][b + 1], af[m], r2, r3);
-              }
-            }
-          }
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-      if (threadIdx.x == 0) GM_PROF_ADD(2, c1);
-      // promote: acc += scale * partial (fp32)
-#pragma unroll
-      for (int m = 0; m < C::kNMat; ++m)
-#pragma unroll
-        for (int b = 0; b < MT / 8; ++b) {
-          if (b >= nblk) continue;
-          acc[m][b][0] = fmaf(sc_lo[m], part[m][b][0], acc[m][b][0]);
-          acc[m][b][1] = fmaf(sc_lo[m], part[m][b][1], acc[m][b][1]);
-          acc[m][b][2] = fmaf(sc_hi[m], part[m][b][2], acc[m][b][2]);
-          acc[m][b][3] = fmaf(sc_hi[m], part[m][b][3], acc[m][b][3]);
-        }
+    bool alive;
+    if constexpr (MT == 16) {  // one or two active column blocks
+      alive = nblk == 1
+                  ? consume_item<FMT, MODE, MT, 1>(a, stages, full, empty, ktiles, nblk, warp, lane, ch_lo, ch_hi, use, acc)
+                  : consume_item<FMT, MODE, MT, 2>(a, stages, full, empty, ktiles, nblk, warp, lane, ch_lo, ch_hi, use, acc);
+    } else if constexpr (MT == 32) {
+      alive = nblk == 1
+                  ? consume_item<FMT, MODE, MT, 1>(a, stages, full, empty, ktiles, nblk, warp, lane, ch_lo, ch_hi, use, acc)
+                  : consume_item<FMT, MODE, MT, 0>(a, stages, full, empty, ktiles, nblk, warp, lane, ch_lo, ch_hi, use, acc);
+    } else {
+      alive = consume_item<FMT, MODE, MT, 0>(a, stages, full, empty, ktiles, nblk, warp, lane, ch_lo, ch_hi, use, acc);
     }
+    if (!alive) return;
 
     // ---------------- epilogue ----------------
     GM_PROF_START(c2);
