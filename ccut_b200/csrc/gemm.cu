@@ -39,8 +39,13 @@ struct GemmCfg {
   static constexpr int kNWarps = 8;
   static constexpr int kThreads = (kNWarps + 1) * 32;
   static constexpr int kNMat = MODE == kFfn1 ? 2 : 1;
-  static constexpr int kWBytes = kNMat * B::kBytes;
-  static constexpr int kXRow = kTileK * 2 + 16;  // padded row: conflict-free ldmatrix
+  // AWQ down blocks are half the size of the other stages: stage two 128-k groups at once so
+  // that the per-stage work (barriers, scales, partial promotion) covers as many bytes
+  static constexpr int kKG = (FMT == CCUT_FMT_AWQ_INT4_G128 && MODE == kFfn2) ? 2 : 1;
+  static constexpr int kNBlk = kNMat * kKG;  // packed blocks per stage (slots)
+  static constexpr int kStageK = kTileK * kKG;
+  static constexpr int kWBytes = kNBlk * B::kBytes;
+  static constexpr int kXRow = kStageK * 2 + 16;  // padded row: conflict-free ldmatrix
   static constexpr int kXBytes = MT * kXRow;
   static constexpr int kStageBytes = kWBytes + kXBytes;
   // 16-row tiles (decode) run two CTAs per SM: twice the warps to hide the dequant and
@@ -89,17 +94,20 @@ __device__ __forceinline__ bool consume_item(const GemmArgs& a, uint8_t* stages,
   using B = typename C::B;
   constexpr int S = C::kStages;
   const int nb = NB > 0 ? NB : nblk;
-  for (int kt = 0; kt < ktiles; ++kt, ++use) {
+  constexpr int Q = C::kNBlk;  // slots: the two matrices (gate/up) or the k groups of a stage
+  const int nstages = (ktiles + C::kKG - 1) / C::kKG;
+  for (int kt = 0; kt < nstages; ++kt, ++use) {
     const int s = use % S;
+    const int nq = C::kKG > 1 ? min(C::kKG, ktiles - kt * C::kKG) : Q;  // slots staged
     GM_PROF_START(c0);
     if (!mbar_wait(&full[s], (use / S) & 1, a.status)) return false;
     if (threadIdx.x == 0) GM_PROF_ADD(1, c0);
     GM_PROF_START(c1);
     const uint8_t* st = stages + s * C::kStageBytes;
     const uint8_t* xs = st + C::kWBytes;
-    float part[C::kNMat][MT / 8][4];
+    float part[Q][MT / 8][4];
 #pragma unroll
-    for (int m = 0; m < C::kNMat; ++m)
+    for (int m = 0; m < Q; ++m)
 #pragma unroll
       for (int b = 0; b < MT / 8; ++b)
         if (b < nb)
@@ -107,11 +115,11 @@ __device__ __forceinline__ bool consume_item(const GemmArgs& a, uint8_t* stages,
           for (int i = 0; i < 4; ++i) part[m][b][i] = 0.f;
 
     // per-stage scale (and AWQ zero-point) of this lane's two channels
-    float sc_lo[C::kNMat], sc_hi[C::kNMat];
-    uint32_t zp_lo[C::kNMat], zp_hi[C::kNMat];  // AWQ: f16x2 1024 + z (lo), -(64 + z) (hi)
+    float sc_lo[Q], sc_hi[Q];
+    uint32_t zp_lo[Q], zp_hi[Q];  // AWQ: f16x2 1024 + z (lo), -(64 + z) (hi)
 #pragma unroll
-    for (int m = 0; m < C::kNMat; ++m) {
-      const uint8_t* blk = st + m * B::kBytes;
+    for (int m = 0; m < Q; ++m) {
+      const uint8_t* blk = st + (m < nq ? m : 0) * B::kBytes;
       if constexpr (FMT == CCUT_FMT_AWQ_INT4_G128) {
         const uint16_t* sc = reinterpret_cast<const uint16_t*>(blk + B::kScaleOff);
         sc_lo[m] = __half2float(__ushort_as_half(sc[ch_lo]));
@@ -126,15 +134,16 @@ __device__ __forceinline__ bool consume_item(const GemmArgs& a, uint8_t* stages,
 
 #pragma unroll
     for (int kc = 0; kc < B::kChunks; ++kc) {
-      uint4 raw[C::kNMat];
+      uint4 raw[Q];
 #pragma unroll
-      for (int m = 0; m < C::kNMat; ++m)
-        raw[m] = *reinterpret_cast<const uint4*>(st + m * B::kBytes + ((warp * B::kChunks + kc) * 32 + lane) * 16);
+      for (int m = 0; m < Q; ++m)
+        if (m < nq)
+          raw[m] = *reinterpret_cast<const uint4*>(st + m * B::kBytes + ((warp * B::kChunks + kc) * 32 + lane) * 16);
 #pragma unroll
       for (int j = 0; j < B::kStepsPerChunk; ++j) {
-        uint32_t af[C::kNMat][4];
+        uint32_t af[Q][4];
 #pragma unroll
-        for (int m = 0; m < C::kNMat; ++m) {
+        for (int m = 0; m < Q; ++m) {
           if constexpr (FMT == CCUT_FMT_AWQ_INT4_G128) {
             const uint32_t wd = j == 0 ? raw[m].x : j == 1 ? raw[m].y : j == 2 ? raw[m].z : raw[m].w;
             // a0/a2: channel ch_lo (nibbles 0,4 / 2,6); a1/a3: ch_hi (nibbles 1,5 / 3,7)
@@ -157,12 +166,24 @@ __device__ __forceinline__ bool consume_item(const GemmArgs& a, uint8_t* stages,
           if (b < nb) {
             const int tok = 8 * (b + (lane >> 4)) + (lane & 7);
             const int kk = koff + ((lane >> 3) & 1) * 8;
-            uint32_t r0, r1, r2, r3;
-            ldmatrix_x4(r0, r1, r2, r3, xs + tok * C::kXRow + kk * 2);
+            if constexpr (C::kKG == 1) {  // both matrices read the same activation k range
+              uint32_t r0, r1, r2, r3;
+              ldmatrix_x4(r0, r1, r2, r3, xs + tok * C::kXRow + kk * 2);
 #pragma unroll
-            for (int m = 0; m < C::kNMat; ++m) {
-              mma_16816<B::kBf16>(part[m][b], af[m], r0, r1);
-              if (b + 1 < nb) mma_16816<B::kBf16>(part[m][b + 1], af[m], r2, r3);
+              for (int m = 0; m < Q; ++m) {
+                mma_16816<B::kBf16>(part[m][b], af[m], r0, r1);
+                if (b + 1 < nb) mma_16816<B::kBf16>(part[m][b + 1], af[m], r2, r3);
+              }
+            } else {  // slot m is the m-th 128-k group of the stage
+#pragma unroll
+              for (int m = 0; m < Q; ++m) {
+                if (m < nq) {
+                  uint32_t r0, r1, r2, r3;
+                  ldmatrix_x4(r0, r1, r2, r3, xs + tok * C::kXRow + (kk + m * kTileK) * 2);
+                  mma_16816<B::kBf16>(part[m][b], af[m], r0, r1);
+                  if (b + 1 < nb) mma_16816<B::kBf16>(part[m][b + 1], af[m], r2, r3);
+                }
+              }
             }
           }
         }
@@ -171,16 +192,17 @@ __device__ __forceinline__ bool consume_item(const GemmArgs& a, uint8_t* stages,
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
     if (threadIdx.x == 0) GM_PROF_ADD(2, c1);
-    // promote: acc += scale * partial (fp32)
+    // promote: acc += scale * partial (fp32); k-group slots share one accumulator
 #pragma unroll
-    for (int m = 0; m < C::kNMat; ++m)
+    for (int m = 0; m < Q; ++m)
 #pragma unroll
       for (int b = 0; b < MT / 8; ++b) {
-        if (b >= nb) continue;
-        acc[m][b][0] = fmaf(sc_lo[m], part[m][b][0], acc[m][b][0]);
-        acc[m][b][1] = fmaf(sc_lo[m], part[m][b][1], acc[m][b][1]);
-        acc[m][b][2] = fmaf(sc_hi[m], part[m][b][2], acc[m][b][2]);
-        acc[m][b][3] = fmaf(sc_hi[m], part[m][b][3], acc[m][b][3]);
+        if (b >= nb || m >= nq) continue;
+        const int ma = C::kKG > 1 ? 0 : m;
+        acc[ma][b][0] = fmaf(sc_lo[m], part[m][b][0], acc[ma][b][0]);
+        acc[ma][b][1] = fmaf(sc_lo[m], part[m][b][1], acc[ma][b][1]);
+        acc[ma][b][2] = fmaf(sc_hi[m], part[m][b][2], acc[ma][b][2]);
+        acc[ma][b][3] = fmaf(sc_hi[m], part[m][b][3], acc[ma][b][3]);
       }
   }
 
@@ -244,8 +266,11 @@ __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT,
         const int r = lane + 32 * i;
         src[i] = r < rows ? (a.row_src ? a.row_src[row0 + r] : row0 + r) : 0;
       }
-      const uint8_t* wb = a.w + (size_t)e * a.expert_stride + (size_t)nt * ktiles * C::kWBytes;
-      for (int kt = 0; kt < ktiles; ++kt, ++use) {
+      const uint8_t* wb = a.w + (size_t)e * a.expert_stride + (size_t)nt * ktiles * C::kNMat * B::kBytes;
+      const int nstages = (ktiles + C::kKG - 1) / C::kKG;
+      for (int kt = 0; kt < nstages; ++kt, ++use) {
+        const int nq = C::kKG > 1 ? min(C::kKG, ktiles - kt * C::kKG) : 1;  // k groups staged
+        const uint32_t wbytes = nq * C::kNMat * B::kBytes, xbytes = nq * kTileK * 2;
         const int s = use % S;
         const uint32_t ph = (use / S) & 1;
         GM_PROF_START(p0);
@@ -256,15 +281,15 @@ __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT,
         if (lane == 0) GM_PROF_ADD(0, p0);
         uint8_t* st = stages + s * C::kStageBytes;
         if (lane == 0) {
-          mbar_arrive_expect_tx(&full[s], C::kWBytes + rows * (kTileK * 2));
-          bulk_g2s(st, wb + (size_t)kt * C::kWBytes, C::kWBytes, &full[s]);
+          mbar_arrive_expect_tx(&full[s], wbytes + rows * xbytes);
+          bulk_g2s(st, wb + (size_t)kt * C::kWBytes, wbytes, &full[s]);
         }
         __syncwarp();
 #pragma unroll
         for (int i = 0; i * 32 < MT; ++i) {
           const int r = lane + 32 * i;
           if (r < rows)
-            bulk_g2s(st + C::kWBytes + r * C::kXRow, a.x + (size_t)src[i] * a.x_ld + kt * kTileK, kTileK * 2,
+            bulk_g2s(st + C::kWBytes + r * C::kXRow, a.x + (size_t)src[i] * a.x_ld + kt * C::kStageK, xbytes,
                      &full[s]);
         }
       }
