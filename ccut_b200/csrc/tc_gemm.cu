@@ -507,8 +507,11 @@ extern "C" __attribute__((visibility("default"))) int ccut_debug_tc_prof(unsigne
 }
 #endif
 
-// Token tile: the smallest of 64 / 128 / 192 covering the typical expert's rows; 192 above
-// (two 192-column accumulators still fit tensor memory, so the epilogue overlaps the MMAs).
+// Token tile: the smallest of 64 / 128 / 256 covering the typical expert's rows (one tile
+// per expert: an MMA costs the same at any N up to 256, and at 256 the A ring is eight
+// deep); 192 above (two 192-column accumulators still fit tensor memory, so the epilogue of
+// one tile overlaps the MMAs of the next).  Measured on B200: 192 rows per expert run
+// 5-9% faster at 256 than at 192, 384 rows faster at 192 than at 256.
 // CCUT_TC_TOKEN_TILE (64, 128, 192 or 256) overrides the choice for tuning.
 int tc_token_tile(int rows_per_expert) {
   static int forced = -1;
@@ -518,7 +521,7 @@ int tc_token_tile(int rows_per_expert) {
     forced = (v == 64 || v == 128 || v == 192 || v == 256) ? v : 0;
   }
   if (forced) return forced;
-  return rows_per_expert <= 64 ? 64 : rows_per_expert <= 128 ? 128 : 192;
+  return rows_per_expert <= 64 ? 64 : rows_per_expert <= 128 ? 128 : rows_per_expert <= 256 ? 256 : 192;
 }
 
 int launch_tc_gemm(int fmt, int mode, int nt_tokens, const CUtensorMap& map, const TcArgs& a, int num_sms,
