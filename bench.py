@@ -194,7 +194,7 @@ def workload_config(wl: str, n: int, parallelism: str) -> dict:
 # DRAM bytes (read + write) of one gate/up launch from an ncu capture of the same workload
 # (profiles/tc_gemm_kernel_cfg1_prefill.md, profiles/moe_gemm_kernel_cfg0_decode.md);
 # workloads without a capture report null.
-NCU_TRAFFIC = {"cfg1_prefill": 482.6e6, "cfg0_decode": 202.3e6}
+NCU_TRAFFIC = {"cfg1_prefill": 480.6e6, "cfg0_decode": 202.3e6}
 
 # ------------------------------------------------------------------ GPU leg
 # Kernels of this library per staged single-GPU step: route (logits, top-k), permute
