@@ -67,6 +67,7 @@ SIGNATURES: dict[str, tuple] = {
     "ccut_moe_expert_ffn_w4a16": (_i, [C.POINTER(MoeLayerDesc), _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "ccut_moe_expert_ffn_fp8b128": (_i, [C.POINTER(MoeLayerDesc), _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "ccut_gate_up_workspace_bytes": (_sz, [C.POINTER(MoeLayerDesc), _i]),
+    "ccut_down_workspace_bytes": (_sz, [C.POINTER(MoeLayerDesc)]),
     "ccut_moe_gate_up": (_i, [C.POINTER(MoeLayerDesc), _vp, _i, _i, _vp, _vp, _vp, _vp, _sz, _vp]),
     "ccut_moe_down": (_i, [C.POINTER(MoeLayerDesc), _vp, _i, _i, _vp, _vp, _vp, _vp, _sz, _vp]),
     "ccut_moe_combine": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _i, _vp]),

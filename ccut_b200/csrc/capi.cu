@@ -78,9 +78,9 @@ bool use_tc(const ccut_moe_layer* L, long per_expert) {
 
 size_t rows_of(const ccut_moe_layer* L, int T, int k) { return (size_t)T * k + (size_t)L->num_shared_slices * T; }
 
-FfnScratch carve_ffn(Carver& c, const ccut_moe_layer* L, int T, int k, bool with_input) {
+FfnScratch carve_ffn(Carver& c, const ccut_moe_layer* L, int T, int k, bool with_input, int* sched) {
   const size_t R = rows_of(L, T, k);
-  FfnScratch s{nullptr, nullptr, nullptr};
+  FfnScratch s{nullptr, nullptr, nullptr, sched};
   if (with_input) {  // sized for either kernel so that one workspace serves both
     s.xp = c.take<uint16_t>(R * L->hidden);
     s.x16 = c.take<uint16_t>((size_t)T * L->hidden);
@@ -89,8 +89,19 @@ FfnScratch carve_ffn(Carver& c, const ccut_moe_layer* L, int T, int k, bool with
   return s;
 }
 
+// Work counters of a mma.sync launch (static schedule when null).
+// CCUT_DYNAMIC_SCHEDULE=0 selects the static schedule, for measurement.
+static void set_sched(GemmArgs& a, int* sched) {
+  static const bool off = [] {
+    const char* v = getenv("CCUT_DYNAMIC_SCHEDULE");
+    return v && v[0] == '0';
+  }();
+  a.sched = off ? nullptr : sched;
+}
+
 struct FwdScratch {
   int* status;
+  int* sched;
   float* part;
   int* counts;
   int32_t* offsets;
@@ -108,6 +119,7 @@ FwdScratch carve_fwd(Carver& c, const ccut_moe_layer* L, int T, int k) {
   const size_t R = (size_t)T * k + (size_t)S * T;
   FwdScratch s;
   s.status = c.take<int>(64);
+  s.sched = take_sched(c);
   s.part = c.take<float>((size_t)route_hsplit(T, E, H) * T * E);
   s.counts = c.take<int>(E);
   s.offsets = c.take<int32_t>(E + S + 1);
@@ -116,7 +128,7 @@ FwdScratch carve_fwd(Carver& c, const ccut_moe_layer* L, int T, int k) {
   s.row_token = c.take<int32_t>(R);
   s.row_weight = c.take<float>(R);
   s.pair_row = c.take<int32_t>((size_t)T * k);
-  s.ffn = carve_ffn(c, L, T, k, true);
+  s.ffn = carve_ffn(c, L, T, k, true, s.sched);
   s.ybuf = c.take<float>(R * H);
   return s;
 }
@@ -125,8 +137,8 @@ FwdScratch carve_fwd(Carver& c, const ccut_moe_layer* L, int T, int k) {
 // gate/up: h rows [R, I] (f16) from x.  `x16` is the mma.sync path's f16 copy of x;
 // `xp` the tcgen05 path's gather buffer.
 int run_gate_up(const ccut_moe_layer* L, long per_expert, const uint16_t* x, const uint16_t* x16, uint16_t* xp,
-                int T, int k,
-                const int32_t* offsets, const int32_t* row_token, uint16_t* hbuf, int* status, cudaStream_t st) {
+                int T, int k, const int32_t* offsets, const int32_t* row_token, uint16_t* hbuf, int* sched, int* status,
+                cudaStream_t st) {
   const int fmt = L->format;
   const int ne = L->num_experts + L->num_shared_slices;
   if (use_tc(L, per_expert)) {
@@ -156,11 +168,12 @@ int run_gate_up(const ccut_moe_layer* L, long per_expert, const uint16_t* x, con
              L->inter,
              nullptr,
              status};
+  set_sched(a, sched);
   return launch_gemm(fmt, kFfn1, pick_mt(per_expert), a, num_sms(), st);
 }
 
 int run_down(const ccut_moe_layer* L, long per_expert, const uint16_t* hbuf, int T, int k, const int32_t* offsets,
-             const float* row_weight, float* y_rows, int* status, cudaStream_t st) {
+             const float* row_weight, float* y_rows, int* sched, int* status, cudaStream_t st) {
   const int fmt = L->format;
   const int ne = L->num_experts + L->num_shared_slices;
   if (use_tc(L, per_expert)) {
@@ -186,15 +199,16 @@ int run_down(const ccut_moe_layer* L, long per_expert, const uint16_t* hbuf, int
              L->hidden,
              row_weight,
              status};
+  set_sched(a, sched);
   return launch_gemm(fmt, kFfn2, pick_mt(per_expert), a, num_sms(), st);
 }
 
 int run_ffn(const ccut_moe_layer* L, long per_expert, const uint16_t* x, const FfnScratch& s, int T, int k,
             const int32_t* offsets,
             const int32_t* row_token, const float* row_weight, float* y_rows, int* status, cudaStream_t st) {
-  int rc = run_gate_up(L, per_expert, x, s.x16, s.xp, T, k, offsets, row_token, s.hbuf, status, st);
+  int rc = run_gate_up(L, per_expert, x, s.x16, s.xp, T, k, offsets, row_token, s.hbuf, s.sched, status, st);
   if (rc) return rc;
-  return run_down(L, per_expert, s.hbuf, T, k, offsets, row_weight, y_rows, status, st);
+  return run_down(L, per_expert, s.hbuf, T, k, offsets, row_weight, y_rows, s.sched, status, st);
 }
 
 }  // namespace ccut
@@ -313,7 +327,8 @@ size_t ccut_expert_ffn_workspace_bytes(const ccut_moe_layer* L, int T, int k) {
   if (check_layer(L) || T < 0 || k < 1) return 0;
   Carver c(nullptr);
   c.take<int>(64);
-  carve_ffn(c, L, T, k, true);
+  take_sched(c);
+  carve_ffn(c, L, T, k, true, nullptr);
   return c.off;
 }
 
@@ -328,7 +343,8 @@ int ccut_moe_expert_ffn(const ccut_moe_layer* L, const uint16_t* x, int T, int k
   if (ws_bytes < ccut_expert_ffn_workspace_bytes(L, T, k)) return CCUT_ERR_WORKSPACE;
   Carver c(workspace);
   int* status = c.take<int>(64);
-  FfnScratch s = carve_ffn(c, L, T, k, true);
+  int* sched = take_sched(c);
+  FfnScratch s = carve_ffn(c, L, T, k, true, sched);
   if (s.x16 && !use_tc(L, mean_rows(L, T, k))) {
     rc = launch_bf16_to_f16(x, s.x16, (size_t)T * L->hidden, stream);
     if (rc) return rc;
@@ -354,6 +370,7 @@ size_t ccut_gate_up_workspace_bytes(const ccut_moe_layer* L, int T) {
   if (check_layer(L) || T < 0) return 0;
   Carver c(nullptr);
   c.take<int>(64);
+  take_sched(c);
   // sized for the largest top_k and either kernel so that one workspace serves any call
   c.take<uint16_t>(rows_of(L, T, kMaxTopK) * L->hidden);
   c.take<uint16_t>((size_t)T * L->hidden);
@@ -371,13 +388,22 @@ int ccut_moe_gate_up(const ccut_moe_layer* L, const uint16_t* x, int T, int k, c
   if (ws_bytes < ccut_gate_up_workspace_bytes(L, T)) return CCUT_ERR_WORKSPACE;
   Carver c(workspace);
   int* status = c.take<int>(64);
+  int* sched = take_sched(c);
   uint16_t* xp = c.take<uint16_t>(rows_of(L, T, kMaxTopK) * L->hidden);
   uint16_t* x16 = c.take<uint16_t>((size_t)T * L->hidden);
   if (!use_tc(L, mean_rows(L, T, k))) {
     rc = launch_bf16_to_f16(x, x16, (size_t)T * L->hidden, stream);
     if (rc) return rc;
   }
-  return run_gate_up(L, mean_rows(L, T, k), x, x16, xp, T, k, offsets, row_token, h_rows, status, stream);
+  return run_gate_up(L, mean_rows(L, T, k), x, x16, xp, T, k, offsets, row_token, h_rows, sched, status, stream);
+}
+
+size_t ccut_down_workspace_bytes(const ccut_moe_layer* L) {
+  if (check_layer(L)) return 0;
+  Carver c(nullptr);
+  c.take<int>(64);
+  take_sched(c);
+  return c.off;
 }
 
 int ccut_moe_down(const ccut_moe_layer* L, const uint16_t* h_rows, int T, int k, const int32_t* offsets,
@@ -388,8 +414,14 @@ int ccut_moe_down(const ccut_moe_layer* L, const uint16_t* h_rows, int T, int k,
   if (T == 0) return CCUT_OK;
   if (!h_rows || !offsets || !row_weight || !y_rows || !workspace) return CCUT_ERR_INVALID;
   if (ws_bytes < 256) return CCUT_ERR_WORKSPACE;
-  return run_down(L, mean_rows(L, T, k), h_rows, T, k, offsets, row_weight, y_rows, static_cast<int*>(workspace),
-                  stream);
+  int* sched = nullptr;
+  if (ws_bytes >= ccut_down_workspace_bytes(L)) {  // else the static schedule (status word only)
+    Carver c(workspace);
+    c.take<int>(64);
+    sched = take_sched(c);
+  }
+  return run_down(L, mean_rows(L, T, k), h_rows, T, k, offsets, row_weight, y_rows, sched,
+                  static_cast<int*>(workspace), stream);
 }
 
 int ccut_moe_combine(const float* y_rows, const int32_t* pair_row, int T, int k, int H, int num_shared_slices,

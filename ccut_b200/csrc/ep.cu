@@ -130,6 +130,8 @@ ccut_moe_layer with_policy(ccut_moe_layer v, long per_expert) {
 
 struct EpScratch {
   int* status;
+  int* sched;     // GEMM work counters of the routed FFN
+  int* sh_sched;  // and of the shared-expert FFN (runs concurrently on the side stream)
   float* part;
   int* counts_g;
   int32_t* ids_l;
@@ -167,6 +169,8 @@ EpScratch carve_ep(Carver& c, const ccut_moe_layer* L, int E_global, int world, 
   const ccut_moe_layer rv = routed_view(L);
   EpScratch s{};
   s.status = c.take<int>(64);
+  s.sched = take_sched(c);
+  s.sh_sched = take_sched(c);
   s.part = c.take<float>((size_t)route_hsplit(T_l, E_global, H) * T_l * E_global);
   s.counts_g = c.take<int>(E_global);
   s.ids_l = c.take<int32_t>((size_t)T_l * k);
@@ -181,7 +185,7 @@ EpScratch carve_ep(Carver& c, const ccut_moe_layer* L, int E_global, int world, 
   s.row_token = c.take<int32_t>((size_t)T * k);
   s.row_weight = c.take<float>((size_t)T * k);
   s.pair_row = c.take<int32_t>((size_t)T * k);
-  s.ffn = carve_ffn(c, &rv, T, k, true);
+  s.ffn = carve_ffn(c, &rv, T, k, true, s.sched);
   s.ybuf = c.take<float>((size_t)T * k * H);
   s.y_part = c.take<float>((size_t)T * H);
   s.y_loc = c.take<float>((size_t)T_l * H);
@@ -195,7 +199,7 @@ EpScratch carve_ep(Carver& c, const ccut_moe_layer* L, int E_global, int world, 
     s.sh_row_token = c.take<int32_t>(R);
     s.sh_row_weight = c.take<float>(R);
     s.sh_pair_row = c.take<int32_t>(T_l);
-    s.sh_ffn = carve_ffn(c, &sv, T_l, 1, true);
+    s.sh_ffn = carve_ffn(c, &sv, T_l, 1, true, s.sh_sched);
     s.sh_ybuf = c.take<float>(R * H);
     s.y_sh = c.take<float>((size_t)T_l * H);
   }

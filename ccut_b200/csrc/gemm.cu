@@ -54,7 +54,8 @@ struct GemmCfg {
   static constexpr int kBudget = MT <= 16 ? 100 * 1024 : 200 * 1024;
   static constexpr int kStages0 = kBudget / kStageBytes;
   static constexpr int kStages = kStages0 > 8 ? 8 : kStages0;
-  static constexpr int kHeader = 2 * 8 * kStages + 4 * (kMaxExperts + 1);
+  // barriers, the work item of each stage slot, the item prefix over experts
+  static constexpr int kHeader = 2 * 8 * kStages + 4 * kStages + 4 * (kMaxExperts + 1);
   static constexpr int kHeaderAligned = (kHeader + 127) / 128 * 128;
   static constexpr int kSmem = kHeaderAligned + kStages * kStageBytes;
   static_assert(kStages >= 2, "stage does not fit");
@@ -218,7 +219,8 @@ __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT,
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + S;
-  int* tprefix = reinterpret_cast<int*>(smem + 16 * S);
+  volatile int* slot_item = reinterpret_cast<int*>(smem + 16 * S);  // item whose first stage the slot holds
+  int* tprefix = reinterpret_cast<int*>(smem + 20 * S);
   uint8_t* stages = smem + C::kHeaderAligned;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -254,9 +256,20 @@ __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT,
 
   if (warp == C::kNWarps) {
     // ---------------- producer ----------------
+    // Work items go out in increasing order: CTA c takes item c, then either fetches the
+    // next one from the counter a.sched[0] (dynamic: CTAs that finish early take more, so
+    // the SMs end at about the same time whatever their speed or item count) or takes
+    // c + grid, c + 2 grid, ... (static).
+    // The item id travels to the consumers in the slot of the item's first stage, published
+    // by that stage's full-barrier arrival; -1 ends the walk.
     int use = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
+    // The first wave is static (CTA c starts with item c, so a small launch spreads over
+    // distinct SMs rather than pairing up on the first CTAs to fetch).
+    int item = (int)blockIdx.x;
+    while (ok && item < total) {
+      int next = 0;  // lane 0: the next item, fetched now and read after this item's stages
+      if (a.sched != nullptr && lane == 0) next = (int)gridDim.x + atomicAdd(&a.sched[0], 1);
       int e, nt, m0, rows;
       decode_item<MT>(item, tprefix, a.num_e, a.offsets, ntiles, e, nt, m0, rows);
       const int row0 = a.offsets[e] + m0;
@@ -281,6 +294,7 @@ __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT,
         if (lane == 0) GM_PROF_ADD(0, p0);
         uint8_t* st = stages + s * C::kStageBytes;
         if (lane == 0) {
+          if (kt == 0) slot_item[s] = item;
           mbar_arrive_expect_tx(&full[s], wbytes + rows * xbytes);
           bulk_g2s(st, wb + (size_t)kt * C::kWBytes, wbytes, &full[s]);
         }
@@ -293,9 +307,26 @@ __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT,
                      &full[s]);
         }
       }
+      item = a.sched != nullptr ? __shfl_sync(0xffffffffu, next, 0) : item + (int)gridDim.x;
+    }
+    if (ok) {  // end marker: the next slot carries item -1 and no bytes
+      const int s = use % S;
+      if (mbar_wait(&empty[s], ((use / S) & 1) ^ 1, a.status)) {
+        if (lane == 0) {
+          slot_item[s] = -1;
+          mbar_arrive(&full[s]);
+        }
+      } else {
+        ok = false;
+      }
     }
     if (!ok && lane == 0) {  // let the copies already issued land before the CTA exits
       for (int u = use > S ? use - S : 0; u < use; ++u) mbar_wait(&full[u % S], (u / S) & 1, nullptr);
+    }
+    // The last CTA to finish fetching leaves the counters zero for the next launch.
+    if (a.sched != nullptr && lane == 0 && atomicAdd(&a.sched[1], 1) == (int)gridDim.x - 1) {
+      a.sched[0] = 0;
+      a.sched[1] = 0;
     }
     return;
   }
@@ -304,7 +335,13 @@ __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT,
   const int g = lane >> 2, t = lane & 3;
   const int ch_lo = warp * 16 + g, ch_hi = ch_lo + 8;  // channels within the 128-tile
   int use = 0;
-  for (int item = blockIdx.x; item < total; item += gridDim.x) {
+  while (true) {
+    {  // the item of the next stage (its full barrier completes before the slot is read)
+      const int s = use % S;
+      if (!mbar_wait(&full[s], (use / S) & 1, a.status)) return;
+    }
+    const int item = slot_item[use % S];
+    if (item < 0) break;
     int e, nt, m0, rows;
     decode_item<MT>(item, tprefix, a.num_e, a.offsets, ntiles, e, nt, m0, rows);
     const int nblk = (rows + 7) >> 3;  // 8-token MMA column blocks in use

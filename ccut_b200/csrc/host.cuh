@@ -30,7 +30,16 @@ struct FfnScratch {
   uint16_t* x16;
   uint16_t* xp;
   uint16_t* hbuf;
+  int* sched;  // work counters of the mma.sync GEMM (null: static schedule)
 };
+
+// Work counters of the mma.sync grouped GEMM's dynamic schedule (gemm.cu).  Every workspace
+// that runs that GEMM keeps them right after its status word, at an offset that does not
+// depend on the call's shapes, so that a workspace reused for other shapes still finds them
+// zero: the caller zero-fills a workspace before its first use and every launch leaves the
+// counters zero.
+constexpr int kSchedInts = 64;
+inline int* take_sched(Carver& c) { return c.take<int>(kSchedInts); }
 
 int num_sms();
 bool valid_fmt(int f);
@@ -41,7 +50,8 @@ long mean_rows(const ccut_moe_layer* L, int T, int k);
 // Kernel policy: tcgen05 (true) or mma.sync (false) for a mean of per_expert rows.
 bool use_tc(const ccut_moe_layer* L, long per_expert);
 size_t rows_of(const ccut_moe_layer* L, int T, int k);
-FfnScratch carve_ffn(Carver& c, const ccut_moe_layer* L, int T, int k, bool with_input);
+// sched: this FFN's GEMM work counters (take_sched), or null for the static schedule.
+FfnScratch carve_ffn(Carver& c, const ccut_moe_layer* L, int T, int k, bool with_input, int* sched);
 // gate/up then down over the rows of a permutation; x16 must already hold x in f16 when
 // the mma.sync kernel runs.
 int run_ffn(const ccut_moe_layer* L, long per_expert, const uint16_t* x, const FfnScratch& s, int T, int k,

@@ -20,6 +20,9 @@ struct GemmArgs {
   int out_ld;
   const float* row_weight;  // FFN2: per-row multiplier (null -> 1)
   int* status;
+  // Dynamic scheduling (gemm.cu): sched[0] hands out work items, sched[1] counts the CTAs
+  // done; both zero on entry, left zero on exit.  Null: static item striding.
+  int* sched;
 };
 
 // Arguments of the tcgen05 grouped GEMM (tc_gemm.cu); the activation operand arrives

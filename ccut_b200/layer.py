@@ -299,7 +299,7 @@ class MoeLayer:
         k = k or self.top_k
         R = T * k + self.num_slices * T
         y = torch.empty((max(R, 1), self.hidden), dtype=torch.float32, device=self.device)
-        ws = self._workspace("down", 256)
+        ws = self._workspace("down", self.lib.ccut_down_workspace_bytes(C.byref(self.desc)))
         _lib.call("ccut_moe_down", C.byref(self.desc), _ptr(h), T, k, _ptr(perm.offsets), _ptr(perm.row_weight),
                   _ptr(y), _ptr(ws), ws.numel(), _stream())
         return y[:R]

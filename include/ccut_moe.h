@@ -12,6 +12,10 @@
  *   - Work is enqueued on `stream` (a cudaStream_t); nothing synchronises the host unless
  *     stated.  Calls on the same stream are ordered; calls that share a workspace must not
  *     overlap on different streams.
+ *   - Workspaces are caller-allocated, sized by the matching *_workspace_bytes function.
+ *     Zero-fill a workspace before its first use and keep it for one entry point: its first
+ *     bytes hold the status word and the work counters of the decode GEMM's dynamic
+ *     schedule, which every call leaves at zero.
  *   - Activations are bf16 bit patterns (uint16_t); routing ids are int32.
  *   - Hidden, intermediate and every matrix dimension must be multiples of 128.
  */
@@ -204,6 +208,10 @@ CCUT_API size_t ccut_gate_up_workspace_bytes(const ccut_moe_layer* L, int T);
 CCUT_API int ccut_moe_gate_up(const ccut_moe_layer* L, const uint16_t* x, int T, int k,
                               const int32_t* offsets, const int32_t* row_token, uint16_t* h_rows,
                               void* workspace, size_t ws_bytes, ccut_stream_t stream);
+/* Workspace bytes that let ccut_moe_down balance its work over the SMs (dynamic
+ * schedule of the decode GEMM); a smaller workspace (at least 256 bytes) runs the static
+ * schedule. */
+CCUT_API size_t ccut_down_workspace_bytes(const ccut_moe_layer* L);
 CCUT_API int ccut_moe_down(const ccut_moe_layer* L, const uint16_t* h_rows, int T, int k,
                            const int32_t* offsets, const float* row_weight, float* y_rows,
                            void* workspace, size_t ws_bytes, ccut_stream_t stream);

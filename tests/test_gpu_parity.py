@@ -252,6 +252,42 @@ def test_stages_compose_to_forward(kernel):
     assert torch.equal(out, full)
 
 
+@pytest.mark.parametrize("fmt", FMTS)
+def test_dynamic_schedule_matches_static(fmt):
+    """The decode GEMM hands out work items from a counter in the workspace (dynamic
+    schedule) or by CTA index (static, chosen by a workspace too small for the counters);
+    both compute every item whole, so the down projection is bit-identical either way, and
+    every call leaves the counters at zero for the next one.  The whole layer stays within
+    tolerance of the oracle."""
+    import ctypes as C
+
+    from ccut_b200 import _lib
+    from ccut_b200.layer import _ptr, _stream
+
+    cfg = small_cfg(fmt, "softmax_topk", hidden=1024, inter=512, experts=16, top_k=4, shared=1)
+    lw = inputs.make_layer(cfg, seed=21)
+    L = gpu_layer(lw, kernel="mma")
+    for T in (1, 7, 64):
+        xb = lw.make_x(T)
+        x = x_device(xb)
+        p = L.permute(L.route(x))
+        h = L.gate_up(x, p)
+        assert torch.equal(L.gate_up(x, p), h)
+        y_dyn = L.down(h, p, T)
+        ws_dyn = L._ws["down"]
+        assert int(ws_dyn[256:512].count_nonzero()) == 0  # counters back at zero
+        y_st = torch.empty_like(y_dyn)
+        ws = torch.zeros(256, dtype=torch.uint8, device="cuda")
+        _lib.call("ccut_moe_down", C.byref(L.desc), _ptr(h), T, L.top_k, _ptr(p.offsets), _ptr(p.row_weight),
+                  _ptr(y_st), _ptr(ws), ws.numel(), _stream())
+        R = T * L.top_k + T
+        assert torch.equal(y_dyn[:R], y_st[:R])
+        out, r = L.forward(x, out_dtype=torch.float32, return_routing=True)
+        ref, _, _ = oracle_forward(lw, xb, ids=r.ids.cpu().numpy().astype(np.int64), weights=r.weights.cpu().numpy())
+        assert rel_err_rows(out.cpu().numpy(), ref) <= TOL
+    assert L.workspace_status() == 0
+
+
 # ---------------------------------------------------------------- edge cases
 def test_empty_batch():
     lw = inputs.make_layer(small_cfg("fp8_b128"), seed=9)
