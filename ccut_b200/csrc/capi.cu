@@ -21,6 +21,16 @@ int num_sms() {
   return cache[dev];
 }
 
+thread_local bool g_pdl_on = false;
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("CCUT_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 bool valid_fmt(int f) { return f == CCUT_FMT_AWQ_INT4_G128 || f == CCUT_FMT_FP8_E4M3_B128; }
 
 int check_layer(const ccut_moe_layer* L) {
@@ -274,6 +284,7 @@ size_t ccut_route_workspace_bytes(int T, int E, int H) {
 int ccut_moe_route(const uint16_t* x, const float* router, int T, int H, int E, const ccut_route_params* rp,
                    int32_t* ids, float* weights, float* logits, void* workspace, size_t ws_bytes,
                    ccut_stream_t stream) {
+  PdlScope pdl_scope(T);  // PDL for decode-sized calls
   int rc = check_route(rp, E);
   if (rc) return rc;
   if (T < 0 || H <= 0 || H % 128) return CCUT_ERR_INVALID;
@@ -288,6 +299,7 @@ int ccut_moe_route(const uint16_t* x, const float* router, int T, int H, int E, 
 
 int ccut_moe_topk(const float* logits, int T, int E, const ccut_route_params* rp, int32_t* ids, float* weights,
                   ccut_stream_t stream) {
+  PdlScope pdl_scope(T);  // PDL for decode-sized calls
   int rc = check_route(rp, E);
   if (rc) return rc;
   if (T < 0) return CCUT_ERR_INVALID;
@@ -306,6 +318,7 @@ size_t ccut_permute_workspace_bytes(int E) {
 int ccut_moe_permute(const int32_t* ids, const float* weights, int T, int k, int E, int num_shared_slices,
                      float shared_gate, int32_t* offsets, int32_t* row_token, float* row_weight, int32_t* pair_row,
                      void* workspace, size_t ws_bytes, ccut_stream_t stream) {
+  PdlScope pdl_scope(T);  // PDL for decode-sized calls
   if (T < 0 || k < 1 || k > kMaxTopK || E < 1 || E > kMaxRoutedExperts || num_shared_slices < 0 ||
       E + num_shared_slices > kMaxExperts)
     return CCUT_ERR_INVALID;
@@ -315,8 +328,6 @@ int ccut_moe_permute(const int32_t* ids, const float* weights, int T, int k, int
   Carver c(workspace);
   c.take<int>(64);
   int* counts = c.take<int>(E);
-  if (T > 0 && cudaMemsetAsync(pair_row, 0xFF, sizeof(int32_t) * (size_t)T * k, stream) != cudaSuccess)
-    return CCUT_ERR_CUDA;
   int rc = launch_count(ids, T * k, E, counts, stream);
   if (rc) return rc;
   return launch_permute(ids, weights, T, k, E, num_shared_slices, shared_gate, counts, offsets, row_token,
@@ -335,6 +346,7 @@ size_t ccut_expert_ffn_workspace_bytes(const ccut_moe_layer* L, int T, int k) {
 int ccut_moe_expert_ffn(const ccut_moe_layer* L, const uint16_t* x, int T, int k, const int32_t* offsets,
                         const int32_t* row_token, const float* row_weight, float* y_rows, void* workspace,
                         size_t ws_bytes, ccut_stream_t stream) {
+  PdlScope pdl_scope(T);  // PDL for decode-sized calls
   int rc = check_layer(L);
   if (rc) return rc;
   if (T < 0 || k < 1 || k > kMaxTopK || k > L->num_experts) return CCUT_ERR_INVALID;
@@ -380,6 +392,7 @@ size_t ccut_gate_up_workspace_bytes(const ccut_moe_layer* L, int T) {
 int ccut_moe_gate_up(const ccut_moe_layer* L, const uint16_t* x, int T, int k, const int32_t* offsets,
                      const int32_t* row_token, uint16_t* h_rows, void* workspace, size_t ws_bytes,
                      ccut_stream_t stream) {
+  PdlScope pdl_scope(T);  // PDL for decode-sized calls
   int rc = check_layer(L);
   if (rc) return rc;
   if (T < 0 || k < 1 || k > kMaxTopK || k > L->num_experts) return CCUT_ERR_INVALID;
@@ -408,6 +421,7 @@ size_t ccut_down_workspace_bytes(const ccut_moe_layer* L) {
 
 int ccut_moe_down(const ccut_moe_layer* L, const uint16_t* h_rows, int T, int k, const int32_t* offsets,
                   const float* row_weight, float* y_rows, void* workspace, size_t ws_bytes, ccut_stream_t stream) {
+  PdlScope pdl_scope(T);  // PDL for decode-sized calls
   int rc = check_layer(L);
   if (rc) return rc;
   if (T < 0 || k < 1 || k > kMaxTopK || k > L->num_experts) return CCUT_ERR_INVALID;
@@ -426,6 +440,7 @@ int ccut_moe_down(const ccut_moe_layer* L, const uint16_t* h_rows, int T, int k,
 
 int ccut_moe_combine(const float* y_rows, const int32_t* pair_row, int T, int k, int H, int num_shared_slices,
                      void* out, int out_dtype, ccut_stream_t stream) {
+  PdlScope pdl_scope(T);  // PDL for decode-sized calls
   if (T < 0 || k < 1 || k > kMaxTopK || H <= 0 || H % 4 || num_shared_slices < 0) return CCUT_ERR_INVALID;
   if (num_shared_slices > CCUT_MAX_SHARED_SLICES) return CCUT_ERR_UNSUPPORTED;
   if (out_dtype != CCUT_OUT_BF16 && out_dtype != CCUT_OUT_F32) return CCUT_ERR_INVALID;
@@ -445,6 +460,7 @@ size_t ccut_moe_forward_workspace_bytes(const ccut_moe_layer* L, int T, int top_
 int ccut_moe_forward(const ccut_moe_layer* L, const ccut_route_params* rp, const uint16_t* x, int T, void* out,
                      int out_dtype, int32_t* ids, float* weights, void* workspace, size_t ws_bytes,
                      ccut_stream_t stream) {
+  PdlScope pdl_scope(T);  // PDL for decode-sized calls
   int rc = check_layer(L);
   if (rc) return rc;
   if (!L->router) return CCUT_ERR_INVALID;
@@ -462,7 +478,6 @@ int ccut_moe_forward(const ccut_moe_layer* L, const ccut_route_params* rp, const
   rc = launch_route(x, L->router, T, H, E, *rp, s.ids, s.wts, nullptr, s.part, s.counts,
                     use_tc(L, mean_rows(L, T, k)) ? nullptr : s.ffn.x16, st);  // x16: mma.sync operands
   if (rc) return rc;
-  if (cudaMemsetAsync(s.pair_row, 0xFF, sizeof(int32_t) * (size_t)T * k, st) != cudaSuccess) return CCUT_ERR_CUDA;
   rc = launch_permute(s.ids, s.wts, T, k, E, L->num_shared_slices, L->shared_gate, s.counts, s.offsets, s.row_token,
                       s.row_weight, s.pair_row, st);
   if (rc) return rc;
@@ -489,6 +504,7 @@ size_t ccut_quant_linear_workspace_bytes(int format, int M, int K) {
 
 int ccut_quant_linear(int format, int layout, const void* packed, int K, int N, const uint16_t* x, int M, float* y,
                       void* workspace, size_t ws_bytes, ccut_stream_t stream) {
+  PdlScope pdl_scope(M);  // PDL for decode-sized calls
   if (!valid_fmt(format)) return CCUT_ERR_UNSUPPORTED;
   if (layout != CCUT_LAYOUT_ROWS && layout != CCUT_LAYOUT_FRAGS) return CCUT_ERR_UNSUPPORTED;
   if (K <= 0 || N <= 0 || K % 128 || N % 128 || M < 0) return CCUT_ERR_INVALID;

@@ -4,6 +4,7 @@
 // so this is a fixed-order fp32 sum per token: deterministic, no atomics.  Follows the
 // scatter-add of ccut/models/generic.py:377-378 and the shared-expert add of
 // ccut/models/generic.py:380-385.
+#include "launch.cuh"
 #include "layout.cuh"
 
 namespace ccut {
@@ -19,6 +20,8 @@ __global__ void __launch_bounds__(kCombThreads) combine_kernel(const float* __re
                                                                const int32_t* __restrict__ pair_row, int T, int k,
                                                                int H, int slices, int shared_base,
                                                                void* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int rows[kCombMaxRows];
   const int t = blockIdx.x;
   const int R = shared_base + slices * T;
@@ -64,15 +67,14 @@ int launch_combine(const float* y, const int32_t* pair_row, int T, int k, int H,
   if (T == 0) return CCUT_OK;
   if (shared_base < 0) shared_base = T * k;
   const dim3 grid(T, (H / 4 + kCombThreads - 1) / kCombThreads);
-  if (out_dtype == CCUT_OUT_BF16)
-    combine_kernel<true><<<grid, kCombThreads, 0, st>>>(y, pair_row, T, k, H, slices, shared_base, out);
-  else
-    combine_kernel<false><<<grid, kCombThreads, 0, st>>>(y, pair_row, T, k, H, slices, shared_base, out);
-  return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
+  return launch_k(out_dtype == CCUT_OUT_BF16 ? combine_kernel<true> : combine_kernel<false>, grid, dim3(kCombThreads),
+                  0, st, y, pair_row, T, k, H, slices, shared_base, out);
 }
 
 // bf16 -> f16 copy (FP8 path operands are f16).
 __global__ void bf16_to_f16_kernel(const uint16_t* __restrict__ in, uint16_t* __restrict__ out, size_t n) {
+  pdl_wait();
+  pdl_trigger();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     const float v = __uint_as_float(static_cast<uint32_t>(in[i]) << 16);
     out[i] = __half_as_ushort(__float2half_rn(v));
@@ -83,18 +85,18 @@ int launch_bf16_to_f16(const uint16_t* in, uint16_t* out, size_t n, cudaStream_t
   size_t blocks = (n + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
   if (blocks < 1) blocks = 1;
-  bf16_to_f16_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(in, out, n);
-  return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
+  return launch_k(bf16_to_f16_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st, in, out, n);
 }
 
 __global__ void fill_offsets_kernel(int32_t* off, int m) {
+  pdl_wait();
+  pdl_trigger();
   off[0] = 0;
   off[1] = m;
 }
 
 int launch_fill_offsets(int32_t* off, int m, cudaStream_t st) {
-  fill_offsets_kernel<<<1, 1, 0, st>>>(off, m);
-  return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
+  return launch_k(fill_offsets_kernel, dim3(1), dim3(1), 0, st, off, m);
 }
 
 }  // namespace ccut

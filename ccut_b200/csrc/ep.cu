@@ -54,6 +54,8 @@ __global__ void __launch_bounds__(256) localize_count_kernel(const int32_t* __re
                                                              const float* __restrict__ w, int n, int lo, int e_local,
                                                              int32_t* __restrict__ ids_loc,
                                                              float* __restrict__ w_loc, int* __restrict__ counts) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int hist[kMaxExperts];
   for (int e = threadIdx.x; e < e_local; e += blockDim.x) hist[e] = 0;
   __syncthreads();
@@ -72,6 +74,8 @@ __global__ void __launch_bounds__(256) localize_count_kernel(const int32_t* __re
 // out = a (+ b), fp32 -> bf16 or fp32.
 __global__ void add_cast_kernel(const float4* __restrict__ a, const float4* __restrict__ b, size_t n4, void* out,
                                 int out_dtype) {
+  pdl_wait();
+  pdl_trigger();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
     float4 v = a[i];
     if (b) {
@@ -322,6 +326,7 @@ int ccut_moe_ep_forward(ccut_ep* ep, const ccut_moe_layer* L, int expert_lo, int
                         void* workspace, size_t ws_bytes, ccut_stream_t stream) {
   int rc = check_ep(ep);
   if (rc) return rc;
+  PdlScope pdl_scope((long)T_local * ep->world);  // PDL for decode-sized calls (all ranks' tokens)
   rc = check_layer(L);
   if (rc) return rc;
   if (!L->router) return CCUT_ERR_INVALID;
@@ -380,10 +385,9 @@ int ccut_moe_ep_forward(ccut_ep* ep, const ccut_moe_layer* L, int expert_lo, int
   if (rc) return rc;
   // 3. local pairs -> permutation -> grouped FFN over the local experts
   if (cudaMemsetAsync(s.counts, 0, sizeof(int) * E_l, st) != cudaSuccess) return CCUT_ERR_CUDA;
-  localize_count_kernel<<<grid_for((size_t)T * k, 256 * 4), 256, 0, st>>>(s.ids_all, s.w_all, T * k, expert_lo,
-                                                                          E_l, s.ids_loc, s.w_loc, s.counts);
-  if (cudaPeekAtLastError() != cudaSuccess) return CCUT_ERR_CUDA;
-  if (cudaMemsetAsync(s.pair_row, 0xFF, sizeof(int32_t) * (size_t)T * k, st) != cudaSuccess) return CCUT_ERR_CUDA;
+  rc = launch_k(localize_count_kernel, dim3(grid_for((size_t)T * k, 256 * 4)), dim3(256), 0, st,
+                (const int32_t*)s.ids_all, (const float*)s.w_all, T * k, expert_lo, E_l, s.ids_loc, s.w_loc, s.counts);
+  if (rc) return rc;
   rc = launch_permute(s.ids_loc, s.w_loc, T, k, E_l, 0, 0.f, s.counts, s.offsets, s.row_token, s.row_weight,
                       s.pair_row, st);
   if (rc) return rc;
@@ -403,10 +407,8 @@ int ccut_moe_ep_forward(ccut_ep* ep, const ccut_moe_layer* L, int expert_lo, int
   if (T_local == 0) return CCUT_OK;
   if (shared && cudaStreamWaitEvent(st, ep->join, 0) != cudaSuccess) return CCUT_ERR_CUDA;
   const size_t n4 = (size_t)T_local * H / 4;
-  add_cast_kernel<<<grid_for(n4, 256), 256, 0, st>>>(reinterpret_cast<const float4*>(s.y_loc),
-                                                      shared ? reinterpret_cast<const float4*>(s.y_sh) : nullptr, n4,
-                                                      out, out_dtype);
-  return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
+  return launch_k(add_cast_kernel, dim3(grid_for(n4, 256)), dim3(256), 0, st, reinterpret_cast<const float4*>(s.y_loc),
+                  shared ? reinterpret_cast<const float4*>(s.y_sh) : nullptr, n4, out, out_dtype);
 }
 
 }  // extern "C"

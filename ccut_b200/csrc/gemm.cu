@@ -213,6 +213,8 @@ __device__ __forceinline__ bool consume_item(const GemmArgs& a, uint8_t* stages,
 template <int FMT, int MODE, int MT>
 __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT, MODE, MT>::kMinBlocks)
     moe_gemm_kernel(GemmArgs a) {
+  pdl_wait();
+  pdl_trigger();
   using C = GemmCfg<FMT, MODE, MT>;
   using B = typename C::B;
   constexpr int S = C::kStages;
@@ -418,8 +420,7 @@ static int launch_gemm_t(const GemmArgs& a, int num_sms, cudaStream_t st) {
       return CCUT_ERR_CUDA;
     attr_done = true;
   }
-  kern<<<num_sms * C::kMinBlocks, C::kThreads, C::kSmem, st>>>(a);
-  return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
+  return launch_k(kern, dim3(num_sms * C::kMinBlocks), dim3(C::kThreads), C::kSmem, st, a);
 }
 
 template <int FMT, int MODE>

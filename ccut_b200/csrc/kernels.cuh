@@ -1,6 +1,7 @@
 // kernels.cuh -- host-side launchers implemented in the .cu files, used by capi.cu.
 #pragma once
 
+#include "launch.cuh"
 #include "layout.cuh"
 
 namespace ccut {

@@ -9,6 +9,7 @@
 // deterministic run to run.
 #include <math.h>
 
+#include "launch.cuh"
 #include "layout.cuh"
 
 namespace ccut {
@@ -35,6 +36,8 @@ __global__ void __launch_bounds__(256) route_logits_kernel(const uint16_t* __res
                                                            const float* __restrict__ router, int T, int H, int E,
                                                            int hsplit, float* __restrict__ part,
                                                            int* __restrict__ counts, uint16_t* __restrict__ x16) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ __align__(16) float xs[kRtH][kRtPad];  // [h][token]
   __shared__ __align__(16) float ws[kRtH][kRtPad];  // [h][expert]
   const int t0 = blockIdx.x * kRtTok, e0 = blockIdx.y * kRtExp, hs = blockIdx.z;
@@ -150,6 +153,8 @@ __global__ void __launch_bounds__(256) route_topk_kernel(const float* __restrict
                                                          ccut_route_params rp, int32_t* __restrict__ ids,
                                                          float* __restrict__ weights, float* __restrict__ logits_out,
                                                          int* __restrict__ counts) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + warp;
   if (t >= T) return;
@@ -308,8 +313,8 @@ __global__ void __launch_bounds__(256) route_topk_kernel(const float* __restrict
 // later half of the chunks, `counts` minus the histogram of the pairs from the chunk on);
 // the third comes from rounds of 256 pairs: __match_any_sync ranks a pair inside its warp
 // and per-warp counters in shared memory rank the warps.  Pair ids outside [0, E) take no
-// row (their pair_row keeps the caller's -1), so the V valid pairs fill rows [0, V) and the
-// shared-expert slices follow at V + s * T (V = T * k when every id is valid).
+// row (their pair_row is -1), so the V valid pairs fill rows [0, V) and the shared-expert
+// slices follow at V + s * T (V = T * k when every id is valid).
 constexpr int kPermThreads = 256;
 constexpr int kPermWarps = kPermThreads / 32;
 
@@ -317,6 +322,8 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(
     const int32_t* __restrict__ ids, const float* __restrict__ weights, int T, int k, int E, int slices,
     float shared_gate, const int* __restrict__ counts, int chunk, int32_t* __restrict__ offsets,
     int32_t* __restrict__ row_token, float* __restrict__ row_weight, int32_t* __restrict__ pair_row) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int base[kMaxExperts];
   __shared__ int hist[kMaxExperts];
   __shared__ int wcnt[kPermWarps][kMaxExperts];
@@ -376,6 +383,8 @@ __global__ void __launch_bounds__(kPermThreads) permute_kernel(
       row_token[p] = i / k;
       row_weight[p] = wt;
       pair_row[i] = p;
+    } else if (i < c1) {
+      pair_row[i] = -1;
     }
     __syncthreads();
     for (int ee = tid; ee < E; ee += kPermThreads) {
@@ -402,15 +411,16 @@ int launch_route(const uint16_t* x, const float* router, int T, int H, int E, co
                  cudaStream_t st) {
   const int hs = route_hsplit(T, E, H);
   dim3 g1((T + kRtTok - 1) / kRtTok, (E + kRtExp - 1) / kRtExp, hs);
-  route_logits_kernel<<<g1, 256, 0, st>>>(x, router, T, H, E, hs, part, counts, x16);
-  route_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(part, hs, nullptr, T, E, rp, ids, weights, logits, counts);
-  return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
+  int rc = launch_k(route_logits_kernel, g1, dim3(256), 0, st, x, router, T, H, E, hs, part, counts, x16);
+  if (rc) return rc;
+  return launch_k(route_topk_kernel, dim3((T + 7) / 8), dim3(256), 0, st, (const float*)part, hs,
+                  (const float*)nullptr, T, E, rp, ids, weights, logits, counts);
 }
 
 int launch_topk(const float* logits, int T, int E, const ccut_route_params& rp, int32_t* ids, float* weights,
                 cudaStream_t st) {
-  route_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(nullptr, 0, logits, T, E, rp, ids, weights, nullptr, nullptr);
-  return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
+  return launch_k(route_topk_kernel, dim3((T + 7) / 8), dim3(256), 0, st, (const float*)nullptr, 0, logits, T, E, rp,
+                  ids, weights, (float*)nullptr, (int*)nullptr);
 }
 
 int launch_permute(const int32_t* ids, const float* weights, int T, int k, int E, int slices, float shared_gate,
@@ -422,14 +432,14 @@ int launch_permute(const int32_t* ids, const float* weights, int T, int k, int E
   const int chunk = (per + kPermThreads - 1) / kPermThreads * kPermThreads;
   int blocks = chunk > 0 ? (tk + chunk - 1) / chunk : 1;
   if (blocks < 1) blocks = 1;
-  permute_kernel<<<blocks, kPermThreads, 0, st>>>(ids, weights, T, k, E, slices, shared_gate, counts,
-                                                  chunk > 0 ? chunk : kPermThreads, offsets, row_token, row_weight,
-                                                  pair_row);
-  return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
+  return launch_k(permute_kernel, dim3(blocks), dim3(kPermThreads), 0, st, ids, weights, T, k, E, slices, shared_gate,
+                  counts, chunk > 0 ? chunk : kPermThreads, offsets, row_token, row_weight, pair_row);
 }
 
 // counts[e] from ids (used when the caller supplies its own routing).
 __global__ void count_kernel(const int32_t* __restrict__ ids, int n, int E, int* __restrict__ counts) {
+  pdl_wait();
+  pdl_trigger();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const int e = ids[i];
     if (e >= 0 && e < E) atomicAdd(&counts[e], 1);
@@ -441,8 +451,7 @@ int launch_count(const int32_t* ids, int n, int E, int* counts, cudaStream_t st)
   int blocks = (n + 255) / 256;
   if (blocks > 1024) blocks = 1024;
   if (blocks < 1) blocks = 1;
-  count_kernel<<<blocks, 256, 0, st>>>(ids, n, E, counts);
-  return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
+  return launch_k(count_kernel, dim3(blocks), dim3(256), 0, st, ids, n, E, counts);
 }
 
 }  // namespace ccut

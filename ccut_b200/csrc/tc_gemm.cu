@@ -168,6 +168,8 @@ __device__ __forceinline__ void named_bar(int id, int nthreads) {
 
 template <int FMT, int MODE, int NT>
 __global__ void __launch_bounds__(896, 1) tc_gemm_kernel(const __grid_constant__ CUtensorMap bmap, TcArgs a) {
+  pdl_wait();
+  pdl_trigger();
   using C = TcCfg<FMT, MODE, NT>;
   using BK = Blk<FMT>;
   constexpr int SB = C::kSB;
@@ -486,8 +488,7 @@ static int launch_tc_t(const CUtensorMap& map, const TcArgs& a, int num_sms, cud
       return CCUT_ERR_CUDA;
     attr_done = dev;
   }
-  kern<<<num_sms, C::kThreads, C::kSmem, st>>>(map, a);
-  return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
+  return launch_k(kern, dim3(num_sms), dim3(C::kThreads), C::kSmem, st, map, a);
 }
 
 template <int MODE, int NT>

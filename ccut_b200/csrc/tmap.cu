@@ -37,6 +37,8 @@ int encode_rows_map(CUtensorMap* map, const void* base, int rows, int cols, int 
 
 __global__ void gather_f16_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ row_token, int R,
                                   const int* __restrict__ nrows, int H, uint16_t* __restrict__ xp) {
+  pdl_wait();
+  pdl_trigger();
   const int per_row = H / 8;
   if (nrows && *nrows < R) R = *nrows;  // rows the permutation actually produced
   const size_t total = (size_t)R * per_row;
@@ -61,8 +63,8 @@ int launch_gather_f16(const uint16_t* x_bf16, const int32_t* row_token, int R, c
   size_t blocks = (total + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
   if (blocks < 1) blocks = 1;
-  gather_f16_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(x_bf16, row_token, R, nrows, H, xp);
-  return cudaPeekAtLastError() == cudaSuccess ? CCUT_OK : CCUT_ERR_CUDA;
+  return launch_k(gather_f16_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st, x_bf16, row_token, R,
+                  nrows, H, xp);
 }
 
 }  // namespace ccut
