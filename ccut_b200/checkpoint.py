@@ -1,0 +1,366 @@
+"""Checkpoint loader: one MoE layer's experts from safetensors shards into HBM.
+
+The reference streams experts from disk at every step: ``ccut/experts/index.py:145-248``
+parses the shard headers into a ``(layer, expert) -> segment`` index,
+``ccut/experts/reader.py:86-334`` reads those segments on demand, and
+``ccut/io_/safetensors_io.py:88-218`` is its shard reader.  Here the same headers are
+parsed once, and every routed and shared expert of a layer is read through ``mmap`` and
+packed into the layer's HBM tile layout (``MoeLayer``), where it stays for the life of
+the layer.
+
+Checkpoint formats (the ``quantization_config`` of ``config.json``, resolved by
+``quant_method`` as in ``ccut/quant/registry.py:107-153``):
+
+* AWQ GEMM (``"awq"``, 4 bits, group size 128, zero points):
+  ``<proj>.qweight`` int32 ``[in, out/8]``, ``<proj>.qzeros`` int32 ``[in/128, out/8]``,
+  ``<proj>.scales`` fp16 ``[in/128, out]``;
+* FP8 block (``"fp8"``, e4m3, ``weight_block_size [128, 128]``):
+  ``<proj>.weight`` F8_E4M3 ``[out, in]``, ``<proj>.weight_scale_inv`` fp32
+  ``[out/128, in/128]``.
+
+MoE shape keys follow ``ccut/models/spec.py:159-170`` (``num_experts`` or
+``n_routed_experts``, ``num_experts_per_tok``, ``moe_intermediate_size``,
+``norm_topk_prob``, ``n_shared_experts`` or ``moe_shared_expert_intermediate_size``),
+plus the DeepSeek-V3 routing keys (``scoring_func``, ``n_group``, ``topk_group``,
+``routed_scaling_factor``).  Missing tensors raise ``KeyError``, malformed files and
+missing scales ``ValueError``, formats this path does not run ``NotImplementedError``,
+as the reference's reader and quant methods do.
+"""
+
+from __future__ import annotations
+
+import json
+import mmap
+import re
+import struct
+from dataclasses import dataclass
+from pathlib import Path
+
+import numpy as np
+
+__all__ = [
+    "SafetensorsShard",
+    "CheckpointReader",
+    "MoeCheckpointSpec",
+    "NameTemplates",
+    "expert_pattern",
+    "quant_format",
+    "moe_spec_from_config",
+    "load_layer_weights",
+    "load_moe_layer",
+]
+
+# safetensors dtype -> numpy dtype of the stored bytes (BF16 and FP8 stay as raw bits)
+_DTYPES = {
+    "F64": np.float64, "F32": np.float32, "F16": np.float16, "BF16": np.uint16,
+    "I64": np.int64, "U64": np.uint64, "I32": np.int32, "U32": np.uint32, "I16": np.int16, "U16": np.uint16,
+    "I8": np.int8, "U8": np.uint8, "BOOL": np.bool_, "F8_E4M3": np.uint8, "F8_E5M2": np.uint8,
+}
+_MAX_HEADER = 100 * 1024 * 1024
+
+
+@dataclass(frozen=True)
+class TensorInfo:
+    dtype: str
+    shape: tuple[int, ...]
+    begin: int  # byte offsets inside the data section
+    end: int
+
+
+class SafetensorsShard:
+    """One safetensors file: an 8-byte little-endian header length, a JSON header mapping
+    tensor names to ``dtype`` / ``shape`` / ``data_offsets``, then the tensor bytes.
+    Tensors are read as read-only views of an ``mmap`` of the file."""
+
+    def __init__(self, path: str | Path):
+        self.path = Path(path)
+        with open(self.path, "rb") as fh:
+            head = fh.read(8)
+            if len(head) < 8:
+                raise ValueError(f"{self.path}: too short for a safetensors file")
+            (n,) = struct.unpack("<Q", head)
+            if n > _MAX_HEADER:
+                raise ValueError(f"{self.path}: header of {n} bytes, file corrupt")
+            raw = fh.read(n)
+            if len(raw) < n:
+                raise ValueError(f"{self.path}: truncated header")
+        try:
+            meta = json.loads(raw.decode("utf-8"))
+        except (UnicodeDecodeError, json.JSONDecodeError) as e:
+            raise ValueError(f"{self.path}: header is not JSON ({e})") from None
+        self.metadata = meta.pop("__metadata__", {}) or {}
+        self.data_start = 8 + n
+        size = self.path.stat().st_size
+        self.tensors: dict[str, TensorInfo] = {}
+        for name, d in meta.items():
+            if d.get("dtype") not in _DTYPES:
+                raise NotImplementedError(f"{self.path}: tensor {name!r} has unsupported dtype {d.get('dtype')!r}")
+            shape = tuple(int(v) for v in d["shape"])
+            b, e = (int(v) for v in d["data_offsets"])
+            count = int(np.prod(shape, dtype=np.int64)) if shape else 1
+            if e - b != count * np.dtype(_DTYPES[d["dtype"]]).itemsize or b < 0 or self.data_start + e > size:
+                raise ValueError(f"{self.path}: tensor {name!r} offsets [{b}, {e}) disagree with its shape or the file")
+            self.tensors[name] = TensorInfo(d["dtype"], shape, b, e)
+        self._mm: mmap.mmap | None = None
+
+    @property
+    def names(self) -> list[str]:
+        return list(self.tensors)
+
+    def __contains__(self, name: str) -> bool:
+        return name in self.tensors
+
+    def info(self, name: str) -> TensorInfo:
+        try:
+            return self.tensors[name]
+        except KeyError:
+            raise KeyError(f"{self.path}: no tensor {name!r}") from None
+
+    def array(self, name: str) -> np.ndarray:
+        """Read-only view of a tensor's bytes with its shape (BF16 / FP8 as raw bits)."""
+        t = self.info(name)
+        if self._mm is None:
+            with open(self.path, "rb") as fh:
+                self._mm = mmap.mmap(fh.fileno(), 0, access=mmap.ACCESS_READ)
+        dt = np.dtype(_DTYPES[t.dtype])
+        a = np.frombuffer(self._mm, dtype=dt, count=(t.end - t.begin) // dt.itemsize, offset=self.data_start + t.begin)
+        return a.reshape(t.shape)
+
+    def close(self) -> None:
+        self._mm = None  # the views keep the mapping alive while they exist
+
+
+class CheckpointReader:
+    """A model directory: ``config.json`` plus one ``model.safetensors`` or the shards
+    listed in ``model.safetensors.index.json`` (``weight_map``: tensor -> shard file)."""
+
+    def __init__(self, model_dir: str | Path):
+        self.dir = Path(model_dir)
+        cfg = self.dir / "config.json"
+        if not cfg.exists():
+            raise FileNotFoundError(f"{cfg}: no config.json")
+        self.config = json.loads(cfg.read_text())
+        index = self.dir / "model.safetensors.index.json"
+        self._shards: dict[str, SafetensorsShard] = {}
+        self.weight_map: dict[str, str] = {}
+        if index.exists():
+            wm = json.loads(index.read_text()).get("weight_map")
+            if not isinstance(wm, dict):
+                raise ValueError(f"{index}: no weight_map")
+            self.weight_map = {str(k): str(v) for k, v in wm.items()}
+        else:
+            files = sorted(self.dir.glob("*.safetensors"))
+            if not files:
+                raise FileNotFoundError(f"{self.dir}: no safetensors files")
+            for f in files:
+                for name in self._shard(f.name).names:
+                    self.weight_map[name] = f.name
+
+    def _shard(self, fname: str) -> SafetensorsShard:
+        sh = self._shards.get(fname)
+        if sh is None:
+            sh = self._shards[fname] = SafetensorsShard(self.dir / fname)
+        return sh
+
+    @property
+    def text_config(self) -> dict:
+        return self.config.get("text_config", self.config)
+
+    def has(self, name: str) -> bool:
+        return name in self.weight_map
+
+    def tensor(self, name: str) -> np.ndarray:
+        if name not in self.weight_map:
+            raise KeyError(f"{self.dir}: no tensor {name!r} in the checkpoint")
+        return self._shard(self.weight_map[name]).array(name)
+
+    def dtype(self, name: str) -> str:
+        if name not in self.weight_map:
+            raise KeyError(f"{self.dir}: no tensor {name!r} in the checkpoint")
+        return self._shard(self.weight_map[name]).info(name).dtype
+
+
+# ---------------------------------------------------------------- config
+def quant_format(config: dict) -> str:
+    """Weight format of this path for a checkpoint's ``quantization_config``."""
+    tc = config.get("text_config", config)
+    q = tc.get("quantization_config") or config.get("quantization_config")
+    if not q:
+        raise NotImplementedError("unquantized checkpoint: this path runs AWQ int4 g128 or FP8 e4m3 128x128 weights")
+    method = str(q.get("quant_method", "")).lower()
+    if method == "awq":
+        bits, group = int(q.get("bits", q.get("w_bit", 4))), int(q.get("group_size", q.get("q_group_size", 128)))
+        version = str(q.get("version", "gemm")).lower()
+        if bits != 4 or group != 128 or not q.get("zero_point", True) or version != "gemm":
+            raise NotImplementedError(f"AWQ variant bits={bits} group_size={group} version={version!r} is not supported"
+                                      " (4-bit, group 128, zero points, GEMM packing)")
+        return "awq_int4_g128"
+    if method == "fp8":
+        block = q.get("weight_block_size")
+        fmt = str(q.get("fmt", "e4m3")).lower()
+        if block is None or [int(v) for v in block] != [128, 128] or fmt != "e4m3":
+            raise NotImplementedError(f"FP8 variant fmt={fmt!r} weight_block_size={block} is not supported"
+                                      " (e4m3, 128 x 128 blocks)")
+        return "fp8_b128"
+    raise NotImplementedError(f"quant_method {method!r} is not supported (have 'awq', 'fp8')")
+
+
+@dataclass(frozen=True)
+class MoeCheckpointSpec:
+    fmt: str
+    hidden: int
+    inter: int
+    num_experts: int
+    top_k: int
+    routing: str  # "softmax_topk" | "topk_softmax" | "sigmoid_group"
+    shared_inter: int  # 0: no shared expert
+    n_group: int = 1
+    topk_group: int = 1
+    routed_scaling: float = 1.0
+
+
+def moe_spec_from_config(config: dict) -> MoeCheckpointSpec:
+    """MoE layer shape and routing of a ``config.json``."""
+    tc = config.get("text_config", config)
+    E = int(tc.get("num_experts") or tc.get("n_routed_experts") or 0)
+    if E < 1:
+        raise ValueError("config has no routed experts (num_experts / n_routed_experts)")
+    I = int(tc.get("moe_intermediate_size", 0))
+    if I < 1:
+        raise ValueError("config has no moe_intermediate_size")
+    shared = int(tc.get("moe_shared_expert_intermediate_size", 0) or tc.get("shared_expert_intermediate_size", 0))
+    if not shared and int(tc.get("n_shared_experts", 0) or 0):
+        shared = int(tc["n_shared_experts"]) * I
+    scoring = str(tc.get("scoring_func", "softmax")).lower()
+    norm = bool(tc.get("norm_topk_prob", False))
+    if scoring == "sigmoid":
+        if not norm:
+            raise NotImplementedError("sigmoid scoring without norm_topk_prob is not supported")
+        routing = "sigmoid_group"
+    elif scoring == "softmax":
+        routing = "topk_softmax" if norm else "softmax_topk"
+    else:
+        raise NotImplementedError(f"scoring_func {scoring!r} is not supported")
+    return MoeCheckpointSpec(
+        fmt=quant_format(config), hidden=int(tc["hidden_size"]), inter=I, num_experts=E,
+        top_k=int(tc.get("num_experts_per_tok", 1)), routing=routing, shared_inter=shared,
+        n_group=int(tc.get("n_group", 1) or 1), topk_group=int(tc.get("topk_group", 1) or 1),
+        routed_scaling=float(tc.get("routed_scaling_factor", 1.0) or 1.0),
+    )
+
+
+# ---------------------------------------------------------------- tensor names
+@dataclass(frozen=True)
+class NameTemplates:
+    """Tensor-name templates of one model family ({layer}, {expert}, {proj} placeholders;
+    {proj} is gate / up / down).  The defaults are the Hugging Face DeepSeek / Qwen MoE names."""
+
+    expert: str = "model.layers.{layer}.mlp.experts.{expert}.{proj}_proj"
+    router: str = "model.layers.{layer}.mlp.gate.weight"
+    bias: str = "model.layers.{layer}.mlp.gate.e_score_correction_bias"
+    shared: tuple[str, ...] = ("model.layers.{layer}.mlp.shared_experts.{proj}_proj",
+                               "model.layers.{layer}.mlp.shared_expert.{proj}_proj")
+    shared_gate: str = "model.layers.{layer}.mlp.shared_expert_gate.weight"
+
+
+def expert_pattern(template: str) -> re.Pattern[str]:
+    """Regex of an expert tensor-name template: ``{layer}`` and ``{expert}`` match digits,
+    ``{proj}`` a lower-case word; the template is anchored at the start only, so that the
+    ``.qweight`` / ``.weight`` / ``.weight_scale_inv`` suffix follows the match (the same
+    placeholder convention as ``ccut/experts/index.py:parse_expert_pattern``)."""
+    out, pos = [], 0
+    for m in re.finditer(r"\{(layer|expert|proj)\}", template):
+        out.append(re.escape(template[pos:m.start()]))
+        out.append({"layer": r"(?P<layer>\d+)", "expert": r"(?P<expert>\d+)", "proj": r"(?P<proj>[a-z]+)"}[m.group(1)])
+        pos = m.end()
+    out.append(re.escape(template[pos:]))
+    return re.compile("^" + "".join(out))
+
+
+_SUFFIXES = {"awq_int4_g128": ("qweight", "qzeros", "scales"), "fp8_b128": ("weight", "weight_scale_inv")}
+
+
+def _read_matrix(reader: CheckpointReader, prefix: str, fmt: str) -> dict:
+    main = _SUFFIXES[fmt][0]
+    if not reader.has(f"{prefix}.{main}"):
+        raise KeyError(f"no tensor {prefix}.{main!s} in the checkpoint")
+    out = {}
+    for suf in _SUFFIXES[fmt]:
+        name = f"{prefix}.{suf}"
+        if not reader.has(name):
+            raise ValueError(f"{prefix}: missing scale tensor {name!r}")
+        out[suf] = reader.tensor(name)
+    if fmt == "awq_int4_g128":
+        if reader.dtype(f"{prefix}.qweight") != "I32" or reader.dtype(f"{prefix}.scales") not in ("F16",):
+            raise ValueError(f"{prefix}: AWQ tensors must be I32 qweight/qzeros and F16 scales")
+    else:
+        if reader.dtype(f"{prefix}.weight") != "F8_E4M3" or reader.dtype(f"{prefix}.weight_scale_inv") != "F32":
+            raise ValueError(f"{prefix}: FP8 tensors must be F8_E4M3 weight and F32 weight_scale_inv")
+    return out
+
+
+def _float_tensor(reader: CheckpointReader, name: str) -> np.ndarray:
+    a, dt = reader.tensor(name), reader.dtype(name)
+    if dt == "BF16":
+        return (a.astype(np.uint32) << np.uint32(16)).view(np.float32)
+    if dt in ("F32", "F16", "F64"):
+        return a.astype(np.float32)
+    raise ValueError(f"{name}: expected a float tensor, got {dt}")
+
+
+def load_layer_weights(model_dir: str | Path, layer: int, names: NameTemplates | None = None):
+    """Host-side view of one MoE layer of a checkpoint: ``(spec, router fp32 [E, H],
+    experts [{gate, up, down}], shared [{gate, up, down}] or [], bias fp32 [E] or None)``.
+    Matrices are dicts of the checkpoint's tensors (read-only mmap views)."""
+    names = names or NameTemplates()
+    rd = CheckpointReader(model_dir)
+    spec = moe_spec_from_config(rd.config)
+    rx = expert_pattern(names.expert)
+    found: dict[int, set[str]] = {}
+    for name in rd.weight_map:
+        m = rx.match(name)
+        if m and int(m.group("layer")) == layer:
+            found.setdefault(int(m.group("expert")), set()).add(m.group("proj"))
+    missing = [e for e in range(spec.num_experts) if found.get(e, set()) < {"gate", "up", "down"}]
+    if missing:
+        raise ValueError(f"layer {layer}: experts {missing[:8]}{'...' if len(missing) > 8 else ''} are missing "
+                         f"gate/up/down tensors (template {names.expert!r})")
+    extra = sorted(e for e in found if e >= spec.num_experts)
+    if extra:
+        raise ValueError(f"layer {layer}: expert ids {extra[:8]} beyond num_experts={spec.num_experts}")
+    fmt = spec.fmt
+
+    def matrices(template: str, **kw) -> dict:
+        return {p: _read_matrix(rd, template.format(layer=layer, proj=p, **kw), fmt) for p in ("gate", "up", "down")}
+
+    experts = [matrices(names.expert, expert=e) for e in range(spec.num_experts)]
+    shared = []
+    if spec.shared_inter:
+        if rd.has(names.shared_gate.format(layer=layer)):
+            raise NotImplementedError("a per-token shared-expert gate (shared_expert_gate) is not supported")
+        for t in names.shared:
+            probe = f"{t.format(layer=layer, proj='gate')}.{_SUFFIXES[fmt][0]}"
+            if rd.has(probe):
+                shared = [matrices(t)]
+                break
+        else:
+            raise KeyError(f"layer {layer}: config has a shared expert but no tensors match {names.shared}")
+    router = _float_tensor(rd, names.router.format(layer=layer))
+    if router.shape != (spec.num_experts, spec.hidden):
+        raise ValueError(f"router {names.router.format(layer=layer)} has shape {router.shape}, "
+                         f"expected {(spec.num_experts, spec.hidden)}")
+    bname = names.bias.format(layer=layer)
+    bias = _float_tensor(rd, bname) if rd.has(bname) else None
+    return spec, router, experts, shared, bias
+
+
+def load_moe_layer(model_dir: str | Path, layer: int, device="cuda", kernel: str = "auto",
+                   names: NameTemplates | None = None):
+    """``MoeLayer`` of a checkpoint's MoE layer ``layer``, experts packed into HBM."""
+    from ccut_b200.layer import MoeLayer
+
+    spec, router, experts, shared, bias = load_layer_weights(model_dir, layer, names)
+    return MoeLayer(spec.fmt, spec.hidden, spec.inter, spec.num_experts, spec.top_k, spec.routing, router, experts,
+                    shared=shared or None, shared_inter=spec.shared_inter or None, n_group=spec.n_group,
+                    topk_group=spec.topk_group, routed_scaling=spec.routed_scaling, bias=bias, kernel=kernel,
+                    device=device)

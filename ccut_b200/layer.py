@@ -14,6 +14,7 @@ AWQ ``{"qweight": int32 [K, N/8], "qzeros": int32 [K/128, N/8], "scales": fp16 [
 from __future__ import annotations
 
 import ctypes as C
+import warnings
 from dataclasses import dataclass
 
 import numpy as np
@@ -37,7 +38,10 @@ def _dev(a, device, dtype=None) -> torch.Tensor:
     if isinstance(a, torch.Tensor):
         t = a
     else:
-        t = torch.from_numpy(np.ascontiguousarray(a))
+        a = np.ascontiguousarray(a)
+        with warnings.catch_warnings():  # read-only views (mmap'd checkpoints) are only read
+            warnings.simplefilter("ignore", UserWarning)
+            t = torch.from_numpy(a)
     if dtype is not None and t.dtype != dtype:
         t = t.view(dtype) if t.element_size() == torch.empty((), dtype=dtype).element_size() else t.to(dtype)
     return t.to(device, non_blocking=False).contiguous()

@@ -1,0 +1,106 @@
+"""Writes small safetensors checkpoints of the seeded synthetic layers (test fixtures).
+
+A checkpoint is a model directory with ``config.json`` (Hugging Face DeepSeek-style MoE
+keys and a ``quantization_config``), two shards and ``model.safetensors.index.json``,
+holding one MoE layer at index ``layer``: router, routed experts and the shared experts
+merged into one MLP along the intermediate axis (as DeepSeek stores ``shared_experts``).
+"""
+
+from __future__ import annotations
+
+import json
+import struct
+from pathlib import Path
+
+import numpy as np
+
+from oracle import inputs
+
+_DT = {np.dtype(np.float32): "F32", np.dtype(np.float16): "F16", np.dtype(np.int32): "I32",
+       np.dtype(np.uint8): "U8", np.dtype(np.uint16): "U16", np.dtype(np.int64): "I64"}
+
+
+def write_safetensors(path: Path, tensors: dict[str, tuple[str | None, np.ndarray]], metadata=None) -> None:
+    """tensors: name -> (safetensors dtype or None for the array's own, array)."""
+    header, blobs, off = {}, [], 0
+    for name, (dt, a) in tensors.items():
+        a = np.ascontiguousarray(a)
+        b = a.tobytes()
+        header[name] = {"dtype": dt or _DT[a.dtype], "shape": list(a.shape), "data_offsets": [off, off + len(b)]}
+        blobs.append(b)
+        off += len(b)
+    if metadata:
+        header["__metadata__"] = metadata
+    raw = json.dumps(header).encode()
+    raw += b" " * (-len(raw) % 8)
+    with open(path, "wb") as fh:
+        fh.write(struct.pack("<Q", len(raw)))
+        fh.write(raw)
+        for b in blobs:
+            fh.write(b)
+
+
+def _matrix_tensors(prefix: str, m) -> dict:
+    if isinstance(m, inputs.AwqMatrix):
+        return {f"{prefix}.qweight": (None, m.qweight), f"{prefix}.qzeros": (None, m.qzeros),
+                f"{prefix}.scales": (None, m.scales)}
+    return {f"{prefix}.weight": ("F8_E4M3", m.weight), f"{prefix}.weight_scale_inv": (None, m.scale)}
+
+
+def merged_shared(lw):
+    """The layer's shared experts as one MLP (intermediate axis concatenated)."""
+    if not lw.shared:
+        return None
+    out = {}
+    for proj in ("gate", "up", "down"):
+        mats = [getattr(s, proj) for s in lw.shared]
+        if isinstance(mats[0], inputs.AwqMatrix):  # [in, out]: gate/up cat along out, down along in
+            ax = 1 if proj != "down" else 0
+            out[proj] = inputs.AwqMatrix(*(np.concatenate([getattr(m, f) for m in mats], axis=ax)
+                                           for f in ("qweight", "qzeros", "scales")))
+        else:  # [out, in]
+            ax = 0 if proj != "down" else 1
+            out[proj] = inputs.Fp8Matrix(*(np.concatenate([getattr(m, f) for m in mats], axis=ax)
+                                           for f in ("weight", "scale")))
+    return out
+
+
+def write_checkpoint(root: Path, lw, layer: int = 3, router_bf16: bool = False, quant: dict | None = None,
+                     drop: tuple[str, ...] = (), extra_config: dict | None = None) -> Path:
+    c = lw.cfg
+    root.mkdir(parents=True, exist_ok=True)
+    q = quant or ({"quant_method": "awq", "bits": 4, "group_size": 128, "zero_point": True, "version": "gemm"}
+                  if c.fmt == "awq_int4_g128" else
+                  {"quant_method": "fp8", "fmt": "e4m3", "weight_block_size": [128, 128],
+                   "activation_scheme": "dynamic"})
+    cfg = {"architectures": ["DeepseekV2ForCausalLM"], "hidden_size": c.hidden, "moe_intermediate_size": c.inter,
+           "n_routed_experts": c.num_experts, "num_experts_per_tok": c.top_k,
+           "n_shared_experts": c.num_shared * c.shared_inter // c.inter if c.num_shared else 0,
+           "norm_topk_prob": c.routing == "topk_softmax", "scoring_func": "softmax",
+           "quantization_config": q}
+    cfg.update(extra_config or {})
+    (root / "config.json").write_text(json.dumps(cfg))
+    pre = f"model.layers.{layer}.mlp"
+    t1, t2 = {}, {}
+    r = lw.router.astype(np.float32)
+    if router_bf16:
+        t1[f"{pre}.gate.weight"] = ("BF16", inputs.synthetic.bf16_bits_from_f32(r))
+    else:
+        t1[f"{pre}.gate.weight"] = (None, r)
+    t1["model.embed_tokens.weight"] = (None, np.zeros((4, c.hidden), np.float32))  # an unrelated tensor
+    for e, ew in enumerate(lw.experts):
+        dst = t1 if e < c.num_experts // 2 else t2
+        for proj in ("gate", "up", "down"):
+            dst.update(_matrix_tensors(f"{pre}.experts.{e}.{proj}_proj", getattr(ew, proj)))
+    sh = merged_shared(lw)
+    if sh:
+        for proj in ("gate", "up", "down"):
+            t2.update(_matrix_tensors(f"{pre}.shared_experts.{proj}_proj", sh[proj]))
+    for name in drop:
+        t1.pop(name, None)
+        t2.pop(name, None)
+    write_safetensors(root / "model-00001-of-00002.safetensors", t1, {"format": "pt"})
+    write_safetensors(root / "model-00002-of-00002.safetensors", t2)
+    wm = {n: "model-00001-of-00002.safetensors" for n in t1} | {n: "model-00002-of-00002.safetensors" for n in t2}
+    (root / "model.safetensors.index.json").write_text(json.dumps({"metadata": {}, "weight_map": wm}))
+    return root
