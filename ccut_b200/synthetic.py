@@ -30,6 +30,7 @@ __all__ = [
     "ExpertWeights",
     "LayerWeights",
     "make_layer",
+    "make_layer_device",
     "scaled_config",
     "bf16_bits_from_f32",
     "GROUP",
@@ -177,6 +178,43 @@ def _gen_expert(rng, fmt: str, hidden: int, inter: int) -> ExpertWeights:
     up = _gen_matrix(rng, fmt, hidden, inter)
     down = _gen_matrix(rng, fmt, inter, hidden)
     return ExpertWeights(gate, up, down)
+
+
+def make_layer_device(cfg: str | MoeLayerConfig, seed: int = 0, device="cuda") -> LayerWeights:
+    """The same layer shapes and value distributions as ``make_layer``, drawn on the GPU from
+    a seeded torch generator (seconds instead of minutes for the 11 GB DeepSeek-V3 layer).
+    The values differ from ``make_layer``'s (another random stream): the benchmark uses it for
+    the layers too large to generate on the host in a bounded time; the parity tests use
+    ``make_layer``.  Matrices hold device tensors; ``make_x`` stays the host draw."""
+    import torch
+
+    cfg = CONFIGS[cfg] if isinstance(cfg, str) else cfg
+    if cfg.hidden % GROUP or cfg.inter % GROUP:
+        raise ValueError("hidden and inter must be multiples of 128")
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+
+    def mat(k: int, n: int):
+        if cfg.fmt == "awq_int4_g128":
+            q = torch.randint(-2**31, 2**31, (k, n // 8), generator=g, device=device, dtype=torch.int64).to(torch.int32)
+            z = torch.randint(-2**31, 2**31, (k // GROUP, n // 8), generator=g, device=device,
+                              dtype=torch.int64).to(torch.int32)
+            sc = (torch.randn((k // GROUP, n), generator=g, device=device) * 0.02).abs_().add_(1e-3).to(torch.float16)
+            return AwqMatrix(q, z, sc)
+        w = torch.randn((n, k), generator=g, device=device).clamp_(-448.0, 448.0).to(torch.float8_e4m3fn)
+        nb, kb = math.ceil(n / BLOCK), math.ceil(k / BLOCK)
+        lo, hi = math.log(1e-3), math.log(1e-1)
+        sc = torch.rand((nb, kb), generator=g, device=device).mul_(hi - lo).add_(lo).exp_()
+        return Fp8Matrix(w.view(torch.uint8), sc)
+
+    def expert(inter: int) -> ExpertWeights:
+        return ExpertWeights(mat(cfg.hidden, inter), mat(cfg.hidden, inter), mat(inter, cfg.hidden))
+
+    router = (torch.randn((cfg.num_experts, cfg.hidden), generator=g, device=device) * 0.02).cpu().numpy()
+    experts = [expert(cfg.inter) for _ in range(cfg.num_experts)]
+    shared = [expert(cfg.shared_inter) for _ in range(cfg.num_shared)]
+    rng = np.random.default_rng(seed)
+    return LayerWeights(cfg, router, experts, shared, rng_state=rng.bit_generator.state)
 
 
 def make_layer(cfg: str | MoeLayerConfig, seed: int = 0) -> LayerWeights:
