@@ -147,43 +147,14 @@ __device__ __forceinline__ float warp_sum(float v) {
 constexpr int kMaxPerLane = 8;  // E <= 256
 constexpr int kMaxTopK = 16;
 
-// One warp per token.  Logits come either from `part` (hsplit partial sums) or `logits_in`.
-__global__ void __launch_bounds__(256) route_topk_kernel(const float* __restrict__ part, int hsplit,
-                                                         const float* __restrict__ logits_in, int T, int E,
-                                                         ccut_route_params rp, int32_t* __restrict__ ids,
-                                                         float* __restrict__ weights, float* __restrict__ logits_out,
-                                                         int* __restrict__ counts) {
-  pdl_wait();
-  pdl_trigger();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 8 + warp;
-  if (t >= T) return;
+// Selection and weights of one token from its logits v (lane + 32 i holds expert lane + 32 i,
+// -inf beyond E), by one warp: the routing mode's selection score, top-k by repeated warp
+// arg-max (ties to the lower index), the routing weights, and the writes of ids / weights /
+// counts for token t.
+__device__ __forceinline__ void select_topk(const float (&v)[kMaxPerLane], int lane, int t, int E,
+                                            const ccut_route_params& rp, int32_t* __restrict__ ids,
+                                            float* __restrict__ weights, int* __restrict__ counts) {
   const int k = rp.top_k;
-  float v[kMaxPerLane];
-#pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) {
-    const int e = lane + 32 * i;
-    float val = -INFINITY;
-    if (e < E) {
-      if (logits_in) {
-        val = logits_in[(size_t)t * E + e];
-      } else {
-        // eight independent partial sums keep eight loads in flight per lane
-        const float* pp = part + (size_t)t * E + e;
-        const size_t ps = (size_t)T * E;
-        float a8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        int s = 0;
-        for (; s + 8 <= hsplit; s += 8) {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) a8[j] += pp[(size_t)(s + j) * ps];
-        }
-        for (; s < hsplit; ++s) a8[0] += pp[(size_t)s * ps];
-        val = ((a8[0] + a8[1]) + (a8[2] + a8[3])) + ((a8[4] + a8[5]) + (a8[6] + a8[7]));
-      }
-      if (logits_out) logits_out[(size_t)t * E + e] = val;
-    }
-    v[i] = val;
-  }
   // selection score
   float sel[kMaxPerLane], sg[kMaxPerLane];
   if (rp.mode == CCUT_ROUTE_SIGMOID_GROUP) {
@@ -303,7 +274,91 @@ __global__ void __launch_bounds__(256) route_topk_kernel(const float* __restrict
     ids[(size_t)t * k + lane] = my_id;
     weights[(size_t)t * k + lane] = w;
     if (counts) atomicAdd(&counts[my_id], 1);
+  }}
+
+// One warp per token.  Logits come either from `part` (hsplit partial sums) or `logits_in`.
+__global__ void __launch_bounds__(256) route_topk_kernel(const float* __restrict__ part, int hsplit,
+                                                         const float* __restrict__ logits_in, int T, int E,
+                                                         ccut_route_params rp, int32_t* __restrict__ ids,
+                                                         float* __restrict__ weights, float* __restrict__ logits_out,
+                                                         int* __restrict__ counts) {
+  pdl_wait();
+  pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + warp;
+  if (t >= T) return;
+  float v[kMaxPerLane];
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) {
+    const int e = lane + 32 * i;
+    float val = -INFINITY;
+    if (e < E) {
+      if (logits_in) {
+        val = logits_in[(size_t)t * E + e];
+      } else {
+        // eight independent partial sums keep eight loads in flight per lane
+        const float* pp = part + (size_t)t * E + e;
+        const size_t ps = (size_t)T * E;
+        float a8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        int s = 0;
+        for (; s + 8 <= hsplit; s += 8) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) a8[j] += pp[(size_t)(s + j) * ps];
+        }
+        for (; s < hsplit; ++s) a8[0] += pp[(size_t)s * ps];
+        val = ((a8[0] + a8[1]) + (a8[2] + a8[3])) + ((a8[4] + a8[5]) + (a8[6] + a8[7]));
+      }
+      if (logits_out) logits_out[(size_t)t * E + e] = val;
+    }
+    v[i] = val;
   }
+  select_topk(v, lane, t, E, rp, ids, weights, counts);
+}
+
+// Decode-sized calls (T <= kTopkWideMaxT) with partial sums: one CTA per token, so that the
+// H-split partial sums are read by 256 threads of T CTAs rather than one warp per token.
+// Thread (j, e) sums the splits s = j, j + 8, ... of expert e (split j = 0 also takes the
+// hsplit % 8 tail), and the eight sums are added in the same tree as route_topk_kernel, so
+// the logits (and hence the routing) are bit-identical to it.
+constexpr int kTopkWideMaxT = 256;
+
+__global__ void __launch_bounds__(256) route_topk_wide_kernel(const float* __restrict__ part, int hsplit, int T,
+                                                              int E, ccut_route_params rp, int32_t* __restrict__ ids,
+                                                              float* __restrict__ weights,
+                                                              float* __restrict__ logits_out,
+                                                              int* __restrict__ counts) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float a8s[8][kMaxPerLane * 32];
+  __shared__ float lg[kMaxPerLane * 32];
+  const int t = blockIdx.x, tid = threadIdx.x;
+  const size_t ps = (size_t)T * E;
+  const int main = hsplit / 8 * 8;
+  for (int idx = tid; idx < 8 * E; idx += blockDim.x) {
+    const int j = idx / E, e = idx - j * E;
+    const float* pp = part + (size_t)t * E + e;
+    float a = 0.f;
+    for (int s = j; s < main; s += 8) a += pp[(size_t)s * ps];
+    if (j == 0)
+      for (int s = main; s < hsplit; ++s) a += pp[(size_t)s * ps];
+    a8s[j][e] = a;
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += blockDim.x) {
+    const float val = ((a8s[0][e] + a8s[1][e]) + (a8s[2][e] + a8s[3][e])) +
+                      ((a8s[4][e] + a8s[5][e]) + (a8s[6][e] + a8s[7][e]));
+    lg[e] = val;
+    if (logits_out) logits_out[(size_t)t * E + e] = val;
+  }
+  __syncthreads();
+  if (tid >= 32) return;
+  float v[kMaxPerLane];
+#pragma unroll
+  for (int i = 0; i < kMaxPerLane; ++i) {
+    const int e = tid + 32 * i;
+    v[i] = e < E ? lg[e] : -INFINITY;
+  }
+  select_topk(v, tid, t, E, rp, ids, weights, counts);
 }
 
 // Stable counting sort of the T*k (token, slot) pairs by expert, one CTA per contiguous
@@ -413,6 +468,9 @@ int launch_route(const uint16_t* x, const float* router, int T, int H, int E, co
   dim3 g1((T + kRtTok - 1) / kRtTok, (E + kRtExp - 1) / kRtExp, hs);
   int rc = launch_k(route_logits_kernel, g1, dim3(256), 0, st, x, router, T, H, E, hs, part, counts, x16);
   if (rc) return rc;
+  if (T <= kTopkWideMaxT)
+    return launch_k(route_topk_wide_kernel, dim3(T), dim3(256), 0, st, (const float*)part, hs, T, E, rp, ids, weights,
+                    logits, counts);
   return launch_k(route_topk_kernel, dim3((T + 7) / 8), dim3(256), 0, st, (const float*)part, hs,
                   (const float*)nullptr, T, E, rp, ids, weights, logits, counts);
 }
