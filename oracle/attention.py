@@ -1,0 +1,69 @@
+"""CPU restatement (numpy, fp32) of the reference's attention and RMSNorm blocks.
+
+Test infrastructure only: the GPU tests check ``ccut_b200.blocks.attn_gqa`` and
+``ccut_b200.blocks.norm`` against these functions, and these functions are pinned to the
+reference's own outputs (``tests/golden/attn_norm.npz``, made by
+``tests/golden/make_golden_attn.py``).
+
+* ``gqa_attention`` follows ``gqa_attention_fast`` (``ccut/blocks/attn_gqa.py:127-153``), the
+  function the reference's attention layer calls (``ccut/models/generic.py:343``): fp32
+  scores ``q . k * scale`` (``scale = 1/sqrt(d)``), additive mask, row max subtracted,
+  ``exp``, entries whose shifted score is below -1e29 set to 0, normalised by
+  ``max(sum, 1e-30)``, then ``probs @ v``.  Query head ``h`` reads kv head ``h // (heads /
+  kv_heads)``.  The optional ``softcap`` (``tanh(s / c) * c`` before the mask) is the
+  parameter of the per-token variant ``gqa_attention`` (``:76-124``).
+* ``causal_mask`` follows ``build_causal_mask`` (``:65-73``): query ``i`` of a batch that
+  starts at absolute position ``start_pos`` sees kv positions ``<= start_pos + i``.
+* ``rms_norm`` follows ``ccut/blocks/norm.py:14-26``: ``x * (mean(x^2) + eps) ** -0.5 * w``
+  in fp32.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+__all__ = ["causal_mask", "gqa_attention", "rms_norm"]
+
+
+def causal_mask(seq_len: int, start_pos: int) -> np.ndarray:
+    """[seq_len, start_pos + seq_len] float32: 0 where visible, -1e30 where masked."""
+    q_idx = np.arange(start_pos, start_pos + seq_len)[:, None]
+    kv_idx = np.arange(start_pos + seq_len)[None, :]
+    m = np.zeros((seq_len, start_pos + seq_len), dtype=np.float32)
+    m[kv_idx > q_idx] = -1e30
+    return m
+
+
+def gqa_attention(q, k, v, mask=None, scale=None, softcap=None) -> np.ndarray:
+    """q [b, heads, s, d], k / v [b, kv_heads, kv_len, d] -> [b, heads, s, d] float32."""
+    q32 = np.asarray(q, dtype=np.float32)
+    k32 = np.asarray(k, dtype=np.float32)
+    v32 = np.asarray(v, dtype=np.float32)
+    b, heads, s, d = q32.shape
+    kvh = k32.shape[1]
+    if heads % kvh:
+        raise ValueError(f"heads ({heads}) must be a multiple of kv_heads ({kvh})")
+    g = heads // kvh
+    scale = scale or 1.0 / np.sqrt(d)
+    if g > 1:
+        k32 = np.repeat(k32, g, axis=1)
+        v32 = np.repeat(v32, g, axis=1)
+    scores = np.einsum("bhqd,bhkd->bhqk", q32, k32) * np.float32(scale)
+    if softcap is not None:
+        scores = (np.tanh(scores / np.float32(softcap)) * np.float32(softcap)).astype(np.float32)
+    if mask is not None:
+        scores = scores + np.asarray(mask, dtype=np.float32)
+    scores = scores - scores.max(axis=-1, keepdims=True)
+    ex = np.exp(scores)
+    ex[scores < -1e29] = 0.0
+    probs = ex / np.maximum(ex.sum(axis=-1, keepdims=True), 1e-30)
+    return np.einsum("bhqk,bhkd->bhqd", probs, v32).astype(np.float32)
+
+
+def rms_norm(x, weight=None, eps: float = 1e-6) -> np.ndarray:
+    x32 = np.asarray(x, dtype=np.float32)
+    var = np.mean(x32 * x32, axis=-1, keepdims=True)
+    y = x32 * (var + np.float32(eps)) ** np.float32(-0.5)
+    if weight is not None:
+        y = y * np.asarray(weight, dtype=np.float32)
+    return y.astype(np.float32)

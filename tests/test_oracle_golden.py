@@ -171,3 +171,33 @@ def test_layer_generator_is_deterministic_and_sized():
     assert inputs.CONFIGS["cfg1"].expert_bytes() == 8_652_864
     assert inputs.CONFIGS["cfg3"].expert_bytes() == 2_451_456
     assert inputs.CONFIGS["cfg4"].expert_bytes() == 44_050_944
+
+
+# ---------------------------------------------------------------- attention / RMSNorm
+def test_gqa_attention_oracle_matches_reference(golden_dir):
+    """oracle.attention.gqa_attention against the reference's gqa_attention_fast
+    (ccut/blocks/attn_gqa.py:127-153) on causal, unmasked and grouped cases."""
+    from oracle import attention
+
+    g = np.load(golden_dir / "attn_norm.npz")
+    i = 0
+    while f"gqa{i}_q" in g:
+        q, k, v = (formats.bf16_bits_to_f32(g[f"gqa{i}_{n}"]) for n in "qkv")
+        start = int(g[f"gqa{i}_start"])
+        s, kv = q.shape[2], k.shape[2]
+        mask = attention.causal_mask(s, start)[None, None] if start >= 0 else None
+        got = attention.gqa_attention(q, k, v, mask)
+        np.testing.assert_allclose(got, g[f"gqa{i}_out"], rtol=1e-5, atol=1e-5)
+        i += 1
+    assert i == 4
+
+
+def test_rms_norm_oracle_matches_reference(golden_dir):
+    from oracle import attention
+
+    g = np.load(golden_dir / "attn_norm.npz")
+    for i in range(2):
+        x = formats.bf16_bits_to_f32(g[f"rms{i}_x"])
+        w = g[f"rms{i}_w"]
+        y = attention.rms_norm(x, w if w.size else None, float(g[f"rms{i}_eps"]))
+        np.testing.assert_allclose(y, g[f"rms{i}_y"], rtol=1e-6, atol=1e-6)
