@@ -237,6 +237,29 @@ CCUT_API int ccut_quant_linear(int format, int layout, const void* packed, int K
                                const uint16_t* x, int M, float* y, void* workspace, size_t ws_bytes,
                                ccut_stream_t stream);
 
+/* ---- attention and normalisation blocks of the full model (ccut/blocks/attn_gqa.py,
+ * ccut/blocks/norm.py) ---------------------------------------------------------------- */
+/* GQA attention (ccut/blocks/attn_gqa.py:127-153, gqa_attention_fast, as called by
+ * ccut/models/generic.py:343).  q bf16 [batch, heads, seq, head_dim], k / v bf16
+ * [batch, kv_heads, kv_len, head_dim] (16-byte aligned rows), out [batch, heads, seq,
+ * head_dim] bf16 or fp32 (out_dtype).  Query head h reads kv head h / (heads / kv_heads).
+ * causal_start >= 0 masks as build_causal_mask(seq, causal_start) (:65-73): query i sees kv
+ * positions <= causal_start + i; -1: no mask.  scale <= 0 means 1/sqrt(head_dim); softcap
+ * > 0 applies tanh(s / softcap) * softcap to the scaled scores (the softcap of
+ * gqa_attention, :76-124).  head_dim 64 or 128.  `workspace` holds the per-split partial
+ * results (ccut_gqa_attention_workspace_bytes). */
+CCUT_API size_t ccut_gqa_attention_workspace_bytes(int batch, int heads, int kv_heads, int seq, int kv_len,
+                                                   int head_dim);
+CCUT_API int ccut_gqa_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, int batch, int heads,
+                                int kv_heads, int seq, int kv_len, int head_dim, int causal_start, float scale,
+                                float softcap, void* out, int out_dtype, void* workspace, size_t ws_bytes,
+                                ccut_stream_t stream);
+/* RMSNorm (ccut/blocks/norm.py:14-26): y = x * (mean(x^2) + eps)^-1/2 * weight per row, in
+ * fp32.  x [rows, dim] bf16 or fp32 (x_dtype, CCUT_OUT_BF16 / CCUT_OUT_F32), weight fp32
+ * [dim] or NULL (no affine), out [rows, dim] in out_dtype. */
+CCUT_API int ccut_rms_norm(const void* x, int x_dtype, const float* weight, int rows, int dim, float eps,
+                           void* out, int out_dtype, ccut_stream_t stream);
+
 /* ---- diagnostics ------------------------------------------------------------------- */
 /* Device-side status word kept at the start of every workspace: a kernel whose bounded
  * wait expired stores CCUT_ERR_TIMEOUT there instead of hanging.  Reads it (synchronises
