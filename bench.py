@@ -528,13 +528,82 @@ def run_ours(args, wl) -> None:
         del graph
 
 
+# Attention block of the full stacks (not the MoE layer): name -> (batch, heads, kv_heads,
+# seq, kv_len, head_dim).  cfg3: Qwen3-30B-A3B GQA (32 query heads, 4 kv heads, head dim
+# 128), batch-64 decode over a 4096-position bf16 kv cache.
+ATTN_WORKLOADS = {"cfg3_attn_decode": (64, 32, 4, 1, 4096, 128)}
+
+
+def run_attn(args, wl) -> None:
+    """One GQA attention call per step (ccut_gqa_attention) on device-resident q / k / v;
+    roofline: the K and V bytes read (the kv cache exceeds the L2)."""
+    import ctypes as C
+
+    import torch
+
+    from ccut_b200 import _lib, build
+    from ccut_b200.layer import _ptr, _stream
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    build.build()
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    b, h, kvh, s, L, d = ATTN_WORKLOADS[wl]
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    q = torch.randn((b, h, s, d), generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn((b, kvh, L, d), generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn((b, kvh, L, d), generator=g, device=dev).to(torch.bfloat16)
+    out = torch.empty((b, h, s, d), dtype=torch.bfloat16, device=dev)
+    lib = _lib.load()
+    ws = torch.zeros(max(lib.ccut_gqa_attention_workspace_bytes(b, h, kvh, s, L, d), 256), dtype=torch.uint8,
+                     device=dev)
+
+    def step():
+        _lib.call("ccut_gqa_attention", _ptr(q), _ptr(k), _ptr(v), b, h, kvh, s, L, d, L - s, 0.0, 0.0, _ptr(out),
+                  _lib.OUT_BF16, _ptr(ws), ws.numel(), _stream())
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(dev.index or 0)
+    K = args.steps
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(K):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    clk = clocks.stop()
+    pk, src = peaks()
+    kv_bytes = 2 * b * kvh * L * d * 2
+    byts = kv_bytes + 2 * b * h * s * d * 2
+    achieved = byts * K / (ms * 1e-3) / 1e9
+    peak = pk.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    print(json.dumps({
+        "metric": "GQA attention tokens/s", "value": b * s * K / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1,
+        "steps": K, "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 in, f32 accumulate", "data": "synthetic (seeded torch generator)",
+        "config": {"workload": wl, "batch": b, "heads": h, "kv_heads": kvh, "seq": s, "kv_len": L, "head_dim": d,
+                   "l2": f"kv cache {kv_bytes / 1e6:.0f} MB > 126 MB L2, no flush"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "kernel": "gqa_attn_kernel + gqa_combine_kernel",
+                     "algorithmic_bytes_per_launch": byts,
+                     "peak_source": f"{src} (MEASURED_PEAKS.json)" if src == "measured" else "fallback"},
+        "gpu_launches": 2 * K,
+        "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]},
+    }), flush=True)
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(ATTN_WORKLOADS), default=DEFAULT_WORKLOAD)
     ap.add_argument("--graph", choices=("auto", "on", "off"), default="auto")
     ap.add_argument("--soak", type=float, default=1.0, help="untimed seconds of load before timing")
     ap.add_argument("--cpu-sample", type=int, default=128, help="tokens in the CPU baseline sample")
@@ -543,7 +612,13 @@ def main(argv=None) -> int:
     args = ap.parse_args(argv)
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
-    if args.impl == "reference":
+    if args.workload in ATTN_WORKLOADS:
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference arm times the MoE layer; the "
+                              "attention workload has no reference timing"}), flush=True)
+        else:
+            run_attn(args, args.workload)
+    elif args.impl == "reference":
         run_reference(args, args.workload)
     else:
         run_ours(args, args.workload)
