@@ -8,14 +8,13 @@
 // attention layer calls at ccut/models/generic.py:343) with the mask of build_causal_mask
 // (:65-73) and the softcap of gqa_attention (:76-124).
 //
-// Work: a CTA takes 8 query rows of one (batch, kv head) -- the query heads that share the
-// kv head, row r = (s, g) with s = r / G, g = r % G -- and one split of the kv range.  K and
-// V tiles of 64 positions are staged in shared memory (K transposed, so that lane l reads
-// positions 2l, 2l+1 of one d without bank conflicts); each warp owns one query row and
-// keeps an online softmax (running max m, sum l, fp32 accumulator over its D/32 output
-// dims).  With one split the CTA writes o = acc / max(l, 1e-30); with several it writes
-// (m, l, acc) and gqa_combine_kernel merges the splits.  Bound: HBM (K and V read once per
-// (batch, kv head, split); query rows of a kv head share them).
+// Work: a CTA takes 16 query rows of one (batch, kv head) -- the query heads that share
+// the kv head, row r = (s, g) with s = r / G, g = r % G -- and one split of the kv range;
+// the 16 rows are the M of m16n8k16 bf16 tensor-core MMAs (S = Q K^T, then O += P V with P
+// split into bf16 hi + lo parts), see gqa_attn_kernel.  With one split the CTA writes
+// o = acc / max(l, 1e-30); with several it writes (m, l, acc) and gqa_combine_kernel merges
+// the splits.  Bound: HBM (K and V read once per (batch, kv head, split); the query rows of
+// a kv head share them).
 //
 // RMSNorm: y = x * (mean(x^2) + eps)^-1/2 * w per row in fp32 (ccut/blocks/norm.py:14-26).
 #include <math.h>
@@ -24,148 +23,258 @@
 
 namespace ccut {
 
-constexpr int kAttnRows = 8;   // query rows (warps) per CTA
 constexpr int kAttnTile = 64;  // kv positions per staged tile
 
 __device__ __forceinline__ float bf16_to_f32(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
 
+// ---- tensor-core tiles ------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  const uint32_t n = valid ? 16u : 0u;  // 0: the 16 bytes are zero-filled, nothing is read
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3,
+                                                  const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(smem_u32(p)));
+}
+// (bf16(a), bf16(b)) and the bf16 residuals (a - bf16(a), b - bf16(b)), packed low = a
+__device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  const __nv_bfloat162 r = __floats2bfloat162_rn(a - __low2float(h), b - __high2float(h));
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&r);
+}
+
+constexpr int kTcRows = 16;  // query rows per CTA (the MMA's M)
+constexpr int kTcWarps = 4;  // warps per CTA, each streaming its own kv tiles
+constexpr int kTcTile = 16;  // kv positions per warp tile
+
+template <int D>
+struct TcAttnSmem {
+  static constexpr int kRow = D + 8;  // padded row (elements): conflict-free ldmatrix
+  static constexpr int kTileElems = kTcTile * kRow;
+  static constexpr int kWarpElems = 2 * 2 * kTileElems;  // double-buffered K and V tiles
+  static constexpr int kQElems = kTcRows * kRow;
+  static constexpr size_t kLoopBytes = (size_t)(kQElems + kTcWarps * kWarpElems) * 2;
+  static constexpr size_t kMergeBytes = (size_t)kTcWarps * kTcRows * (D + 2) * 4;  // aliases the tiles
+  static constexpr size_t kBytes = kLoopBytes > kMergeBytes ? kLoopBytes : kMergeBytes;
+  static_assert((kRow * 2) % 16 == 0 && (kQElems * 2) % 16 == 0 && (kTileElems * 2) % 16 == 0, "16-byte rows");
+};
+
+// Tensor-core tiles on the m16n8k16 bf16 MMA (fp32 accumulate): the CTA's 16 query rows are
+// the A operand of S = Q K^T (K rows read with ldmatrix as B fragments); the probabilities
+// P, split into bf16 hi + lo parts so that P V keeps ~16 bits, are the A operand of O += P V
+// (V read with ldmatrix.trans).  Each warp streams its own tiles of 16 kv positions
+// (tile j of the CTA's range goes to warp j % 4) through a cp.async double buffer and keeps
+// its own online softmax (running max and sum of rows g and g + 8, fp32 O fragments); the
+// four warp states are merged through shared memory at the end.
 template <int D, bool OUT_BF16>
-__global__ void __launch_bounds__(256) gqa_attn_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k,
-                                                       const uint16_t* __restrict__ v, int Hq, int Hkv, int S, int L,
-                                                       int causal_start, float scale, float softcap, int splits,
-                                                       int tiles_per_split, void* __restrict__ out,
-                                                       float* __restrict__ part) {
+__global__ void __launch_bounds__(kTcWarps * 32) gqa_attn_kernel(
+    const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, const uint16_t* __restrict__ v, int Hq, int Hkv,
+    int S, int L, int causal_start, float scale, float softcap, int splits, int tiles_per_split,
+    void* __restrict__ out, float* __restrict__ part) {
   pdl_wait();
   pdl_trigger();
-  constexpr int DL = D / 32;  // output dims per lane
-  // K transposed, rows padded to 66 elements: the transposing stores then conflict 4-way
-  // instead of 16-way, and the per-lane score reads (one 32-bit word per lane) stay
-  // conflict-free
-  __shared__ __align__(16) uint16_t kT[D][kAttnTile + 2];
-  __shared__ __align__(16) uint16_t vt[kAttnTile][D];
-  __shared__ __align__(16) float qs[kAttnRows][D];
-  __shared__ float ps[kAttnRows][kAttnTile];
+  using SM = TcAttnSmem<D>;
+  constexpr int KS = D / 16;  // k steps of Q K^T; dim-tile pairs of P V
+  extern __shared__ __align__(128) uint8_t attn_smem[];
+  uint16_t* qs = reinterpret_cast<uint16_t*>(attn_smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int G = Hq / Hkv;
-  const int bh = blockIdx.y;  // b * Hkv + kvh
-  const int b = bh / Hkv, kvh = bh % Hkv;
-  const int r = blockIdx.x * kAttnRows + warp;  // query row within (b, kvh)
-  const bool row_ok = r < G * S;
-  const int s = row_ok ? r / G : 0, h = kvh * G + (row_ok ? r % G : 0);
+  const int g = lane >> 2, t = lane & 3;
+  const int G = Hq / Hkv, nrows = G * S;
+  const int bh = blockIdx.y, b = bh / Hkv, kvh = bh % Hkv;
+  const int r0 = blockIdx.x * kTcRows;
   const int split = blockIdx.z;
   const int k0 = split * tiles_per_split * kAttnTile;
   int k1 = min(L, k0 + tiles_per_split * kAttnTile);
-  // causal: the CTA's last row sees up to causal_start + s_last
-  if (causal_start >= 0) {
-    const int r_last = min(G * S, (int)(blockIdx.x + 1) * kAttnRows) - 1;
+  if (causal_start >= 0) {  // the CTA's last row sees up to causal_start + s_last
+    const int r_last = min(nrows, r0 + kTcRows) - 1;
     k1 = min(k1, causal_start + r_last / G + 1);
   }
-  const int lim = causal_start >= 0 ? causal_start + s : L - 1;  // last visible position of this row
-  const uint16_t* kb = k + (size_t)bh * L * D;
-  const uint16_t* vb = v + (size_t)bh * L * D;
-  if (row_ok) {
-    const uint16_t* qr = q + (((size_t)b * Hq + h) * S + s) * D;
-    for (int d = lane; d < D; d += 32) qs[warp][d] = bf16_to_f32(qr[d]);
+  // Q rows -> shared memory (zero rows past the end), then A fragments in registers
+  for (int c = threadIdx.x; c < kTcRows * (D / 8); c += blockDim.x) {
+    const int rr = c / (D / 8), dc = (c % (D / 8)) * 8, r = r0 + rr;
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (r < nrows) {
+      const int s = r / G, h = kvh * G + r % G;
+      val = *reinterpret_cast<const uint4*>(q + (((size_t)b * Hq + h) * S + s) * D + dc);
+    }
+    *reinterpret_cast<uint4*>(qs + rr * SM::kRow + dc) = val;
   }
-  float m = -INFINITY, l = 0.f, acc[DL];
+  __syncthreads();
+  uint32_t qa[KS][4];
 #pragma unroll
-  for (int j = 0; j < DL; ++j) acc[j] = 0.f;
+  for (int ks = 0; ks < KS; ++ks)
+    ldmatrix_x4(qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3],
+                qs + ((lane & 7) + ((lane >> 3) & 1) * 8) * SM::kRow + ks * 16 + (lane >> 4) * 8);
+  int lim[2];  // last visible kv position of rows g and g + 8
+#pragma unroll
+  for (int i = 0; i < 2; ++i) lim[i] = causal_start >= 0 ? causal_start + (r0 + g + 8 * i) / G : L - 1;
 
-  for (int t0 = k0; t0 < k1; t0 += kAttnTile) {
-    __syncthreads();  // previous tile consumed (and qs written, first time)
-    constexpr int kChunks = kAttnTile * D / 8;  // 16-byte chunks per tile
-    for (int c = threadIdx.x; c < kChunks; c += blockDim.x) {
-      const int p = c / (D / 8), dc = (c % (D / 8)) * 8;
-      uint4 kk = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-      if (t0 + p < k1) {
-        kk = *reinterpret_cast<const uint4*>(kb + (size_t)(t0 + p) * D + dc);
-        vv = *reinterpret_cast<const uint4*>(vb + (size_t)(t0 + p) * D + dc);
-      }
-      *reinterpret_cast<uint4*>(&vt[p][dc]) = vv;
-      const uint32_t w4[4] = {kk.x, kk.y, kk.z, kk.w};
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+  float o[2 * KS][4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        kT[dc + 2 * j][p] = (uint16_t)(w4[j] & 0xffffu);
-        kT[dc + 2 * j + 1][p] = (uint16_t)(w4[j] >> 16);
-      }
-    }
-    __syncthreads();
-    if (!row_ok) continue;
-    // scores of positions p0 = 2 lane, p0 + 1
-    float s0 = 0.f, s1 = 0.f;
-#pragma unroll 8
-    for (int d = 0; d < D; ++d) {
-      const float qd = qs[warp][d];
-      const uint32_t kk = *reinterpret_cast<const uint32_t*>(&kT[d][2 * lane]);
-      s0 = fmaf(qd, __uint_as_float(kk << 16), s0);
-      s1 = fmaf(qd, __uint_as_float(kk & 0xffff0000u), s1);
-    }
-    s0 *= scale;
-    s1 *= scale;
-    if (softcap > 0.f) {
-      s0 = tanhf(s0 / softcap) * softcap;
-      s1 = tanhf(s1 / softcap) * softcap;
-    }
-    const int pos0 = t0 + 2 * lane;
-    if (pos0 >= k1 || pos0 > lim) s0 = -INFINITY;
-    if (pos0 + 1 >= k1 || pos0 + 1 > lim) s1 = -INFINITY;
-    float mt = fmaxf(s0, s1);
+  for (int dn = 0; dn < 2 * KS; ++dn)
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
-    const float m_new = fmaxf(m, mt);
-    float p0 = 0.f, p1 = 0.f, alpha = 1.f;
-    if (m_new > -INFINITY) {
-      alpha = expf(m - m_new);  // 0 while nothing was visible (m = -inf)
-      p0 = expf(s0 - m_new);
-      p1 = expf(s1 - m_new);
+    for (int i = 0; i < 4; ++i) o[dn][i] = 0.f;
+  uint16_t* wb = qs + SM::kQElems + warp * SM::kWarpElems;  // [buf][K, V][16][kRow]
+  const uint16_t* kg = k + (size_t)bh * L * D;
+  const uint16_t* vg = v + (size_t)bh * L * D;
+  const int ntiles = k1 > k0 ? (k1 - k0 + kTcTile - 1) / kTcTile : 0;
+  auto issue = [&](int tile, int buf) {
+    const int p0 = k0 + tile * kTcTile;
+    uint16_t* kd = wb + buf * 2 * SM::kTileElems;
+    uint16_t* vd = kd + SM::kTileElems;
+    for (int c = lane; c < kTcTile * (D / 8); c += 32) {
+      const int pr = c / (D / 8), dc = (c % (D / 8)) * 8, pos = p0 + pr;
+      const bool ok = pos < k1;
+      const size_t off = (size_t)(ok ? pos : 0) * D + dc;
+      cp_async16(kd + pr * SM::kRow + dc, kg + off, ok);
+      cp_async16(vd + pr * SM::kRow + dc, vg + off, ok);
     }
-    float ts = p0 + p1;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ts += __shfl_xor_sync(0xffffffffu, ts, o);
-    l = l * alpha + ts;
-    m = m_new;
-    ps[warp][2 * lane] = p0;
-    ps[warp][2 * lane + 1] = p1;
-    __syncwarp();
-#pragma unroll
-    for (int j = 0; j < DL; ++j) acc[j] *= alpha;
-    const int npos = min(kAttnTile, k1 - t0);
-    for (int p = 0; p < npos; ++p) {
-      const float pp = ps[warp][p];
-      if constexpr (DL == 4) {
-        const uint2 vv = *reinterpret_cast<const uint2*>(&vt[p][lane * 4]);
-        acc[0] = fmaf(pp, __uint_as_float(vv.x << 16), acc[0]);
-        acc[1] = fmaf(pp, __uint_as_float(vv.x & 0xffff0000u), acc[1]);
-        acc[2] = fmaf(pp, __uint_as_float(vv.y << 16), acc[2]);
-        acc[3] = fmaf(pp, __uint_as_float(vv.y & 0xffff0000u), acc[3]);
-      } else {
-        const uint32_t vv = *reinterpret_cast<const uint32_t*>(&vt[p][lane * 2]);
-        acc[0] = fmaf(pp, __uint_as_float(vv << 16), acc[0]);
-        acc[1] = fmaf(pp, __uint_as_float(vv & 0xffff0000u), acc[1]);
-      }
+    cp_async_commit();
+  };
+  int buf = 0;
+  if (warp < ntiles) issue(warp, 0);
+  for (int jt = warp; jt < ntiles; jt += kTcWarps) {
+    if (jt + kTcWarps < ntiles) {
+      issue(jt + kTcWarps, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
     }
     __syncwarp();
+    const uint16_t* kd = wb + buf * 2 * SM::kTileElems;
+    const uint16_t* vd = kd + SM::kTileElems;
+    // S = Q K^T over 16 positions (two n8 tiles)
+    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      const int mi = lane >> 3;
+      uint32_t b0, b1, b2, b3;
+      ldmatrix_x4(b0, b1, b2, b3, kd + ((mi >> 1) * 8 + (lane & 7)) * SM::kRow + ks * 16 + (mi & 1) * 8);
+      mma_16816<true>(sc[0], qa[ks], b0, b1);
+      mma_16816<true>(sc[1], qa[ks], b2, b3);
+    }
+    // scale, cap, mask; element (n, i): row g + 8 (i >> 1), position p0 + 8 n + 2 t + (i & 1)
+    const int p0 = k0 + jt * kTcTile;
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float x = sc[n][i] * scale;
+        if (softcap > 0.f) x = tanhf(x / softcap) * softcap;
+        const int pos = p0 + 8 * n + 2 * t + (i & 1);
+        if (pos >= k1 || pos > lim[i >> 1]) x = -INFINITY;
+        sc[n][i] = x;
+        mx[i >> 1] = fmaxf(mx[i >> 1], x);
+      }
+    float mnew[2], alpha[2], rs[2] = {0.f, 0.f};
+#pragma unroll
+    for (int ri = 0; ri < 2; ++ri) {
+      mx[ri] = fmaxf(mx[ri], __shfl_xor_sync(0xffffffffu, mx[ri], 1));
+      mx[ri] = fmaxf(mx[ri], __shfl_xor_sync(0xffffffffu, mx[ri], 2));
+      mnew[ri] = fmaxf(m[ri], mx[ri]);
+      alpha[ri] = mnew[ri] == -INFINITY ? 1.f : expf(m[ri] - mnew[ri]);  // 0 after an all-masked start
+    }
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int ri = i >> 1;
+        const float p = mnew[ri] == -INFINITY ? 0.f : expf(sc[n][i] - mnew[ri]);
+        sc[n][i] = p;
+        rs[ri] += p;
+      }
+#pragma unroll
+    for (int ri = 0; ri < 2; ++ri) {
+      rs[ri] += __shfl_xor_sync(0xffffffffu, rs[ri], 1);
+      rs[ri] += __shfl_xor_sync(0xffffffffu, rs[ri], 2);
+      l[ri] = l[ri] * alpha[ri] + rs[ri];
+      m[ri] = mnew[ri];
+    }
+#pragma unroll
+    for (int dn = 0; dn < 2 * KS; ++dn) {
+      o[dn][0] *= alpha[0];
+      o[dn][1] *= alpha[0];
+      o[dn][2] *= alpha[1];
+      o[dn][3] *= alpha[1];
+    }
+    // P as the A operand (the two n8 score tiles form one k16 step), hi and lo parts
+    uint32_t ph[4], pl[4];
+    split_bf16x2(sc[0][0], sc[0][1], ph[0], pl[0]);
+    split_bf16x2(sc[0][2], sc[0][3], ph[1], pl[1]);
+    split_bf16x2(sc[1][0], sc[1][1], ph[2], pl[2]);
+    split_bf16x2(sc[1][2], sc[1][3], ph[3], pl[3]);
+#pragma unroll
+    for (int dp = 0; dp < KS; ++dp) {
+      const int mi = lane >> 3;
+      uint32_t b0, b1, b2, b3;
+      ldmatrix_x4_trans(b0, b1, b2, b3, vd + ((mi & 1) * 8 + (lane & 7)) * SM::kRow + dp * 16 + (mi >> 1) * 8);
+      mma_16816<true>(o[2 * dp], ph, b0, b1);
+      mma_16816<true>(o[2 * dp], pl, b0, b1);
+      mma_16816<true>(o[2 * dp + 1], ph, b2, b3);
+      mma_16816<true>(o[2 * dp + 1], pl, b2, b3);
+    }
+    __syncwarp();  // this buffer is refilled two tiles later
+    buf ^= 1;
   }
-  if (!row_ok) return;
-  const size_t orow = ((size_t)b * Hq + h) * S + s;
-  if (splits == 1) {
-    const float inv = 1.f / fmaxf(l, 1e-30f);
+  // merge the four warp states (the merge area aliases the tile buffers)
+  __syncthreads();
+  float* mg = reinterpret_cast<float*>(attn_smem);
+  {
+    float* wm = mg + (size_t)warp * kTcRows * (D + 2);
 #pragma unroll
-    for (int j = 0; j < DL; ++j) {
-      const float o = acc[j] * inv;
-      const size_t idx = orow * D + lane * DL + j;
-      if constexpr (OUT_BF16) static_cast<__nv_bfloat16*>(out)[idx] = __float2bfloat16_rn(o);
-      else static_cast<float*>(out)[idx] = o;
+    for (int dn = 0; dn < 2 * KS; ++dn) {
+      wm[g * (D + 2) + 2 + dn * 8 + 2 * t] = o[dn][0];
+      wm[g * (D + 2) + 3 + dn * 8 + 2 * t] = o[dn][1];
+      wm[(g + 8) * (D + 2) + 2 + dn * 8 + 2 * t] = o[dn][2];
+      wm[(g + 8) * (D + 2) + 3 + dn * 8 + 2 * t] = o[dn][3];
     }
-  } else {
-    const size_t rows_total = (size_t)gridDim.y / Hkv * Hq * S;  // B * Hq * S
-    float* p = part + ((size_t)split * rows_total + orow) * (D + 2);
-    if (lane == 0) {
-      p[0] = m;
-      p[1] = l;
+    if (t == 0) {
+      wm[g * (D + 2)] = m[0];
+      wm[g * (D + 2) + 1] = l[0];
+      wm[(g + 8) * (D + 2)] = m[1];
+      wm[(g + 8) * (D + 2) + 1] = l[1];
     }
+  }
+  __syncthreads();
+  const size_t rows_total = (size_t)(gridDim.y / Hkv) * Hq * S;  // B * Hq * S
+  for (int idx = threadIdx.x; idx < kTcRows * D; idx += blockDim.x) {
+    const int rr = idx / D, dd = idx % D, r = r0 + rr;
+    if (r >= nrows) continue;
+    float M = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < DL; ++j) p[2 + lane * DL + j] = acc[j];
+    for (int w = 0; w < kTcWarps; ++w) M = fmaxf(M, mg[(w * kTcRows + rr) * (D + 2)]);
+    float Ls = 0.f, ov = 0.f;
+    if (M > -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kTcWarps; ++w) {
+        const float* row = mg + (w * kTcRows + rr) * (D + 2);
+        const float e = expf(row[0] - M);  // 0 for a warp that saw nothing
+        Ls = fmaf(row[1], e, Ls);
+        ov = fmaf(row[2 + dd], e, ov);
+      }
+    }
+    const int s = r / G, h = kvh * G + r % G;
+    const size_t orow = ((size_t)b * Hq + h) * S + s;
+    if (splits == 1) {
+      const float val = ov / fmaxf(Ls, 1e-30f);
+      if constexpr (OUT_BF16) static_cast<__nv_bfloat16*>(out)[orow * D + dd] = __float2bfloat16_rn(val);
+      else static_cast<float*>(out)[orow * D + dd] = val;
+    } else {
+      float* p = part + ((size_t)split * rows_total + orow) * (D + 2);
+      if (dd == 0) {
+        p[0] = M;
+        p[1] = Ls;
+      }
+      p[2 + dd] = ov;
+    }
   }
 }
 
@@ -235,7 +344,7 @@ __global__ void __launch_bounds__(128) rms_norm_kernel(const void* __restrict__ 
 // kv splits: enough CTAs to cover the SMs twice, at least one 64-position tile per split.
 static int attn_splits(int B, int Hq, int Hkv, int S, int L) {
   const int G = Hq / Hkv;
-  const long base = (long)((G * S + kAttnRows - 1) / kAttnRows) * B * Hkv;
+  const long base = (long)((G * S + kTcRows - 1) / kTcRows) * B * Hkv;
   const int tiles = (L + kAttnTile - 1) / kAttnTile;
   long sp = (2L * 148 + base - 1) / base;
   if (sp > tiles) sp = tiles;
@@ -277,16 +386,25 @@ int ccut_gqa_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, 
   const int G = heads / kv_heads;
   const int tiles = (kv_len + kAttnTile - 1) / kAttnTile;
   const int tps = sp > 0 ? (tiles + sp - 1) / sp : 1;
-  const dim3 grid((G * seq + kAttnRows - 1) / kAttnRows, batch * kv_heads, sp);
+  const dim3 grid((G * seq + kTcRows - 1) / kTcRows, batch * kv_heads, sp);
   float* part = sp > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 256) : nullptr;
   const bool ob = out_dtype == CCUT_OUT_BF16;
   int rc;
-  if (head_dim == 128)
-    rc = launch_k(ob ? gqa_attn_kernel<128, true> : gqa_attn_kernel<128, false>, grid, dim3(256), 0, stream, q, k, v,
-                  heads, kv_heads, seq, kv_len, causal_start, scale, softcap, sp, tps, out, part);
-  else
-    rc = launch_k(ob ? gqa_attn_kernel<64, true> : gqa_attn_kernel<64, false>, grid, dim3(256), 0, stream, q, k, v,
-                  heads, kv_heads, seq, kv_len, causal_start, scale, softcap, sp, tps, out, part);
+  if (head_dim == 128) {
+    auto kern = ob ? gqa_attn_kernel<128, true> : gqa_attn_kernel<128, false>;
+    constexpr size_t smem = TcAttnSmem<128>::kBytes;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return CCUT_ERR_CUDA;
+    rc = launch_k(kern, grid, dim3(kTcWarps * 32), smem, stream, q, k, v, heads, kv_heads, seq, kv_len, causal_start,
+                  scale, softcap, sp, tps, out, part);
+  } else {
+    auto kern = ob ? gqa_attn_kernel<64, true> : gqa_attn_kernel<64, false>;
+    constexpr size_t smem = TcAttnSmem<64>::kBytes;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return CCUT_ERR_CUDA;
+    rc = launch_k(kern, grid, dim3(kTcWarps * 32), smem, stream, q, k, v, heads, kv_heads, seq, kv_len, causal_start,
+                  scale, softcap, sp, tps, out, part);
+  }
   if (rc || sp == 1) return rc;
   const int rows = batch * heads * seq;
   const dim3 g2((rows + 7) / 8);
