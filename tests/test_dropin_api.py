@@ -6,8 +6,10 @@ import inspect
 
 import pytest
 
+import numpy as np
+
 from ccut_b200 import quant
-from ccut_b200.blocks import moe
+from ccut_b200.blocks import attn_gqa, moe, norm
 
 # parameter names of the reference functions (ccut/blocks/moe.py, ccut/models/generic.py,
 # ccut/quant/method.py)
@@ -20,7 +22,35 @@ REFERENCE = {
     quant.QuantizeMethodBase.apply: ["self", "weight_bytes", "scales", "x"],
     quant.QuantizeMethodBase.create_weights: ["self", "spec"],
     quant.QuantizeMethodBase.process_weights_after_loading: ["self"],
+    # ccut/blocks/attn_gqa.py, ccut/blocks/norm.py (leading parameters; the GPU versions add
+    # keyword options after them)
+    attn_gqa.build_causal_mask: ["seq_len", "start_pos"],
+    attn_gqa.gqa_attention: ["q", "k", "v", "mask", "scale", "softcap"],
+    norm.rms_norm: ["x", "weight", "eps"],
 }
+PREFIX = {attn_gqa.gqa_attention_fast: ["q", "k", "v", "mask", "scale"]}
+
+
+@pytest.mark.parametrize("fn", list(PREFIX), ids=lambda f: f.__qualname__)
+def test_signature_prefix_matches_reference(fn):
+    names = list(inspect.signature(fn).parameters)
+    assert names[:len(PREFIX[fn])] == PREFIX[fn]
+
+
+def test_causal_mask_detection():
+    """The attention drop-in turns the reference's build_causal_mask masks (plain or
+    broadcast over batch and heads) into a causal offset and rejects other masks."""
+    m = attn_gqa.build_causal_mask(3, 5)
+    assert m.shape == (3, 8) and m[0, 5] == 0 and m[0, 6] < -1e29 and m[2, 7] == 0
+    assert attn_gqa._causal_start(None, 3, 8) == -1
+    assert attn_gqa._causal_start(m, 3, 8) == 5
+    assert attn_gqa._causal_start(np.broadcast_to(m[None, None], (2, 4, 3, 8)), 3, 8) == 5
+    with pytest.raises(NotImplementedError):
+        attn_gqa._causal_start(np.zeros((3, 8), np.float32) - 1.0, 3, 8)
+    with pytest.raises(NotImplementedError):  # the same masked count, other positions
+        attn_gqa._causal_start(m[:, ::-1].copy(), 3, 8)
+    with pytest.raises(ValueError):
+        attn_gqa._causal_start(m, 2, 8)
 
 
 @pytest.mark.parametrize("fn", list(REFERENCE), ids=lambda f: f.__qualname__)
