@@ -12,6 +12,11 @@ Public entry points
 ``ep.ExpertParallelMoeLayer`` the same layer with routed experts sharded over GPUs (NCCL)
 ``blocks.moe``               drop-ins for ``ccut.blocks.moe`` / ``ccut.models.generic.moe_forward``
 ``quant``                    ``QuantizeMethodBase``-compatible AWQ-int4-g128 / FP8-block-128 methods
+``checkpoint``               ``load_moe_layer``: a MoE layer of an AWQ / FP8-block safetensors
+                             checkpoint into HBM
+``dense.DenseFfn``           dense quantized SwiGLU FFN (the expert kernels with one expert)
+``blocks.attn_gqa``          drop-ins for ``ccut.blocks.attn_gqa`` (GQA attention on tensor cores)
+``blocks.norm``              drop-in for ``ccut.blocks.norm.rms_norm``
 """
 
 from ccut_b200.layer import MoeLayer, Permutation, Routing  # noqa: F401
