@@ -17,6 +17,7 @@
 // a kv head share them).
 //
 // RMSNorm: y = x * (mean(x^2) + eps)^-1/2 * w per row in fp32 (ccut/blocks/norm.py:14-26).
+// RoPE: half-rotation rotary embedding (ccut/blocks/rope.py:130-175).
 #include <math.h>
 
 #include "host.cuh"
@@ -57,7 +58,8 @@ template <int D>
 struct TcAttnSmem {
   static constexpr int kRow = D + 8;  // padded row (elements): conflict-free ldmatrix
   static constexpr int kTileElems = kTcTile * kRow;
-  static constexpr int kWarpElems = 2 * 2 * kTileElems;  // double-buffered K and V tiles
+  static constexpr int kStages = 3;                     // K/V tiles per warp: one in use, two in flight
+  static constexpr int kWarpElems = kStages * 2 * kTileElems;
   static constexpr int kQElems = kTcRows * kRow;
   static constexpr size_t kLoopBytes = (size_t)(kQElems + kTcWarps * kWarpElems) * 2;
   static constexpr size_t kMergeBytes = (size_t)kTcWarps * kTcRows * (D + 2) * 4;  // aliases the tiles
@@ -69,7 +71,7 @@ struct TcAttnSmem {
 // the A operand of S = Q K^T (K rows read with ldmatrix as B fragments); the probabilities
 // P, split into bf16 hi + lo parts so that P V keeps ~16 bits, are the A operand of O += P V
 // (V read with ldmatrix.trans).  Each warp streams its own tiles of 16 kv positions
-// (tile j of the CTA's range goes to warp j % 4) through a cp.async double buffer and keeps
+// (tile j of the CTA's range goes to warp j % 4) through a three-deep cp.async ring and keeps
 // its own online softmax (running max and sum of rows g and g + 8, fp32 O fragments); the
 // four warp states are merged through shared memory at the end.
 template <int D, bool OUT_BF16>
@@ -121,7 +123,7 @@ __global__ void __launch_bounds__(kTcWarps * 32) gqa_attn_kernel(
   for (int dn = 0; dn < 2 * KS; ++dn)
 #pragma unroll
     for (int i = 0; i < 4; ++i) o[dn][i] = 0.f;
-  uint16_t* wb = qs + SM::kQElems + warp * SM::kWarpElems;  // [buf][K, V][16][kRow]
+  uint16_t* wb = qs + SM::kQElems + warp * SM::kWarpElems;  // [stage][K, V][16][kRow]
   const uint16_t* kg = k + (size_t)bh * L * D;
   const uint16_t* vg = v + (size_t)bh * L * D;
   const int ntiles = k1 > k0 ? (k1 - k0 + kTcTile - 1) / kTcTile : 0;
@@ -136,17 +138,20 @@ __global__ void __launch_bounds__(kTcWarps * 32) gqa_attn_kernel(
       cp_async16(kd + pr * SM::kRow + dc, kg + off, ok);
       cp_async16(vd + pr * SM::kRow + dc, vg + off, ok);
     }
-    cp_async_commit();
   };
+  // one commit group per tile slot (empty past the end), so that wait_group<kStages - 1>
+  // always means "this iteration's tile has landed"
+#pragma unroll
+  for (int st = 0; st < SM::kStages - 1; ++st) {
+    if (warp + st * kTcWarps < ntiles) issue(warp + st * kTcWarps, st);
+    cp_async_commit();
+  }
   int buf = 0;
-  if (warp < ntiles) issue(warp, 0);
   for (int jt = warp; jt < ntiles; jt += kTcWarps) {
-    if (jt + kTcWarps < ntiles) {
-      issue(jt + kTcWarps, buf ^ 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
+    const int jn = jt + (SM::kStages - 1) * kTcWarps;
+    if (jn < ntiles) issue(jn, (buf + SM::kStages - 1) % SM::kStages);
+    cp_async_commit();
+    cp_async_wait<SM::kStages - 1>();
     __syncwarp();
     const uint16_t* kd = wb + buf * 2 * SM::kTileElems;
     const uint16_t* vd = kd + SM::kTileElems;
@@ -221,8 +226,8 @@ __global__ void __launch_bounds__(kTcWarps * 32) gqa_attn_kernel(
       mma_16816<true>(o[2 * dp + 1], ph, b2, b3);
       mma_16816<true>(o[2 * dp + 1], pl, b2, b3);
     }
-    __syncwarp();  // this buffer is refilled two tiles later
-    buf ^= 1;
+    __syncwarp();  // this stage is refilled by the next iteration's issue
+    buf = (buf + 1) % SM::kStages;
   }
   // merge the four warp states (the merge area aliases the tile buffers)
   __syncthreads();
@@ -341,6 +346,49 @@ __global__ void __launch_bounds__(128) rms_norm_kernel(const void* __restrict__ 
   }
 }
 
+// RoPE, half rotation (ccut/blocks/rope.py:130-175): for the pair (i, i + d/2) of a row
+// (b, head, s), f = positions[b, s] * inv_freq[i] (fp32), out_i = x_i cos f - x_{i+d/2} sin f,
+// out_{i+d/2} = x_{i+d/2} cos f + x_i sin f, with x first multiplied by `scale` (the
+// attention factor the reference applies to q).  Products are rounded before the sums, as
+// in the reference's numpy expression.
+template <bool IN_BF16, bool OUT_BF16>
+__global__ void __launch_bounds__(256) rope_kernel(const void* __restrict__ x, int heads, int S, int half,
+                                                   const float* __restrict__ inv_freq,
+                                                   const int32_t* __restrict__ positions, float scale,
+                                                   long long n_pairs, void* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < n_pairs;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int i = (int)(idx % half);
+    const long long row = idx / half;
+    const int s = (int)(row % S);
+    const long long b = row / S / heads;
+    const float f = __fmul_rn((float)positions[b * S + s], inv_freq[i]);
+    const float c = cosf(f), sn = sinf(f);
+    const size_t o1 = (size_t)row * (2 * half) + i, o2 = o1 + half;
+    float x1, x2;
+    if constexpr (IN_BF16) {
+      x1 = bf16_to_f32(static_cast<const uint16_t*>(x)[o1]);
+      x2 = bf16_to_f32(static_cast<const uint16_t*>(x)[o2]);
+    } else {
+      x1 = static_cast<const float*>(x)[o1];
+      x2 = static_cast<const float*>(x)[o2];
+    }
+    x1 = __fmul_rn(x1, scale);
+    x2 = __fmul_rn(x2, scale);
+    const float y1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, sn));
+    const float y2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, sn));
+    if constexpr (OUT_BF16) {
+      static_cast<__nv_bfloat16*>(out)[o1] = __float2bfloat16_rn(y1);
+      static_cast<__nv_bfloat16*>(out)[o2] = __float2bfloat16_rn(y2);
+    } else {
+      static_cast<float*>(out)[o1] = y1;
+      static_cast<float*>(out)[o2] = y2;
+    }
+  }
+}
+
 // kv splits: enough CTAs to cover the SMs twice, at least one 64-position tile per split.
 static int attn_splits(int B, int Hq, int Hkv, int S, int L) {
   const int G = Hq / Hkv;
@@ -413,6 +461,24 @@ int ccut_gqa_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, 
                     (const float*)part, rows, sp, out);
   return launch_k(ob ? gqa_combine_kernel<64, true> : gqa_combine_kernel<64, false>, g2, dim3(256), 0, stream,
                   (const float*)part, rows, sp, out);
+}
+
+int ccut_apply_rope(const void* x, int x_dtype, int batch, int heads, int seq, int head_dim, const float* inv_freq,
+                    const int32_t* positions, float scale, void* out, int out_dtype, ccut_stream_t stream) {
+  PdlScope pdl_scope((long)batch * seq);
+  if (batch < 0 || heads <= 0 || seq < 0 || head_dim <= 0 || head_dim % 2) return CCUT_ERR_INVALID;
+  if ((x_dtype != CCUT_OUT_BF16 && x_dtype != CCUT_OUT_F32) || (out_dtype != CCUT_OUT_BF16 && out_dtype != CCUT_OUT_F32))
+    return CCUT_ERR_INVALID;
+  const long long n_pairs = (long long)batch * heads * seq * (head_dim / 2);
+  if (n_pairs == 0) return CCUT_OK;
+  if (!x || !inv_freq || !positions || !out) return CCUT_ERR_INVALID;
+  long long blocks = (n_pairs + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  const bool ib = x_dtype == CCUT_OUT_BF16, ob = out_dtype == CCUT_OUT_BF16;
+  auto kern = ib ? (ob ? rope_kernel<true, true> : rope_kernel<true, false>)
+                 : (ob ? rope_kernel<false, true> : rope_kernel<false, false>);
+  return launch_k(kern, dim3((unsigned)blocks), dim3(256), 0, stream, x, heads, seq, head_dim / 2, inv_freq,
+                  positions, scale, n_pairs, out);
 }
 
 int ccut_rms_norm(const void* x, int x_dtype, const float* weight, int rows, int dim, float eps, void* out,

@@ -259,6 +259,14 @@ CCUT_API int ccut_gqa_attention(const uint16_t* q, const uint16_t* k, const uint
  * [dim] or NULL (no affine), out [rows, dim] in out_dtype. */
 CCUT_API int ccut_rms_norm(const void* x, int x_dtype, const float* weight, int rows, int dim, float eps,
                            void* out, int out_dtype, ccut_stream_t stream);
+/* Rotary position embedding, half rotation (ccut/blocks/rope.py:130-175, apply_rope), on
+ * one of q or k: x [batch, heads, seq, head_dim] (x_dtype), positions int32 [batch, seq],
+ * inv_freq fp32 [head_dim / 2] (as build_rope returns it); the pair (i, i + head_dim/2) is
+ * rotated by positions * inv_freq[i] after x is multiplied by `scale` (the attention factor
+ * the reference applies to q under yarn / linear scaling; 1 for k). */
+CCUT_API int ccut_apply_rope(const void* x, int x_dtype, int batch, int heads, int seq, int head_dim,
+                             const float* inv_freq, const int32_t* positions, float scale, void* out,
+                             int out_dtype, ccut_stream_t stream);
 
 /* ---- diagnostics ------------------------------------------------------------------- */
 /* Device-side status word kept at the start of every workspace: a kernel whose bounded

@@ -16,13 +16,18 @@ reference's own outputs (``tests/golden/attn_norm.npz``, made by
   starts at absolute position ``start_pos`` sees kv positions ``<= start_pos + i``.
 * ``rms_norm`` follows ``ccut/blocks/norm.py:14-26``: ``x * (mean(x^2) + eps) ** -0.5 * w``
   in fp32.
+* ``apply_rope`` follows ``ccut/blocks/rope.py:130-175``: half rotation with
+  ``freqs = positions * inv_freq`` (fp32), ``x1 * cos - x2 * sin`` and ``x2 * cos + x1 * sin``
+  over the two halves of the head dim, q first scaled by the attention factor for the
+  ``yarn`` / ``linear`` scalings; q ``[batch, heads, seq, d]``, k ``[batch, kv_heads, seq,
+  d]``, positions ``[batch, seq]``.
 """
 
 from __future__ import annotations
 
 import numpy as np
 
-__all__ = ["causal_mask", "gqa_attention", "rms_norm"]
+__all__ = ["apply_rope", "causal_mask", "gqa_attention", "rms_norm"]
 
 
 def causal_mask(seq_len: int, start_pos: int) -> np.ndarray:
@@ -67,3 +72,23 @@ def rms_norm(x, weight=None, eps: float = 1e-6) -> np.ndarray:
     if weight is not None:
         y = y * np.asarray(weight, dtype=np.float32)
     return y.astype(np.float32)
+
+
+def apply_rope(q, k, inv_freq, positions, attention_factor: float = 1.0, scaling_type: str = "none"):
+    q32 = np.asarray(q, dtype=np.float32)
+    k32 = np.asarray(k, dtype=np.float32)
+    freqs = np.asarray(positions).astype(np.float32)[..., None] * np.asarray(inv_freq, np.float32)[None, None, :]
+    if scaling_type in ("yarn", "linear") and attention_factor != 1.0:
+        q32 = q32 * np.float32(attention_factor)
+    cos = np.cos(freqs)[:, None, :, :]
+    sin = np.sin(freqs)[:, None, :, :]
+
+    def rot(x):
+        half = x.shape[-1] // 2
+        x1, x2 = x[..., :half], x[..., half:]
+        out = np.empty_like(x)
+        out[..., :half] = x1 * cos - x2 * sin
+        out[..., half:] = x2 * cos + x1 * sin
+        return out
+
+    return rot(q32), rot(k32)

@@ -10,6 +10,9 @@ Cases (inputs are bf16-representable, stored as bf16 bit patterns, outputs fp32)
               or no mask; grouped (8 query heads on 2 and on 1 kv heads) and plain heads,
               head dims 64 and 128, one and several query rows.
 ``rms{i}_*``  ``rms_norm`` (``ccut/blocks/norm.py:14-26``) with and without a weight.
+``rope{i}_*`` ``apply_rope`` (``ccut/blocks/rope.py:130-175``) with the inverse frequencies
+              and attention factor of ``build_rope``: no scaling (head dim 128, theta 1e6)
+              and yarn (head dim 64, factor 4: the attention factor scales q).
 """
 
 from __future__ import annotations
@@ -36,6 +39,9 @@ GQA_CASES = [
     (1, 16, 2, 7, 40, 128),
 ]
 RMS_CASES = [(7, 384, True, 1e-6), (3, 256, False, 1e-5)]
+# batch, heads, kv_heads, seq, head_dim, theta, rope_scaling, first positions per batch row
+ROPE_CASES = [(2, 4, 2, 3, 128, 1e6, None, (5, 100)),
+              (1, 2, 1, 5, 64, 1e4, {"type": "yarn", "factor": 4.0}, (4000,))]
 
 
 def bf16_round(x: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
@@ -52,6 +58,7 @@ def main(argv=None) -> int:
     sys.path.insert(0, args.reference)
     from ccut.blocks.attn_gqa import build_causal_mask, gqa_attention_fast
     from ccut.blocks.norm import rms_norm
+    from ccut.blocks.rope import apply_rope, build_rope
 
     rng = np.random.default_rng(2024)
     out = {}
@@ -72,6 +79,16 @@ def main(argv=None) -> int:
         y = rms_norm(x, w if with_w else None, eps)
         out.update({f"rms{i}_x": xb, f"rms{i}_w": w if with_w else np.zeros(0, np.float32),
                     f"rms{i}_eps": np.float32(eps), f"rms{i}_y": y.astype(np.float32)})
+    for i, (b, h, kvh, s, d, theta, scaling, starts) in enumerate(ROPE_CASES):
+        qb, q = bf16_round(rng.standard_normal((b, h, s, d)))
+        kb, k = bf16_round(rng.standard_normal((b, kvh, s, d)))
+        inv_freq, attn = build_rope(d, theta, 8192, scaling)
+        stype = (scaling or {}).get("type", "none")
+        pos = np.stack([np.arange(p, p + s) for p in starts]).astype(np.int64)
+        qo, ko = apply_rope(q, k, inv_freq, pos, attn, stype)
+        out.update({f"rope{i}_q": qb, f"rope{i}_k": kb, f"rope{i}_inv_freq": np.asarray(inv_freq, np.float32),
+                    f"rope{i}_attn": np.float32(attn), f"rope{i}_type": np.array(stype), f"rope{i}_pos": pos,
+                    f"rope{i}_q_out": qo.astype(np.float32), f"rope{i}_k_out": ko.astype(np.float32)})
     np.savez_compressed(HERE / "attn_norm.npz", **out)
     print("wrote", HERE / "attn_norm.npz")
     return 0

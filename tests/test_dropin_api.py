@@ -9,7 +9,7 @@ import pytest
 import numpy as np
 
 from ccut_b200 import quant
-from ccut_b200.blocks import attn_gqa, moe, norm
+from ccut_b200.blocks import attn_gqa, moe, norm, rope
 
 # parameter names of the reference functions (ccut/blocks/moe.py, ccut/models/generic.py,
 # ccut/quant/method.py)
@@ -27,6 +27,7 @@ REFERENCE = {
     attn_gqa.build_causal_mask: ["seq_len", "start_pos"],
     attn_gqa.gqa_attention: ["q", "k", "v", "mask", "scale", "softcap"],
     norm.rms_norm: ["x", "weight", "eps"],
+    rope.apply_rope: ["q", "k", "inv_freq", "positions", "attention_factor", "scaling_type", "seq_len"],
 }
 PREFIX = {attn_gqa.gqa_attention_fast: ["q", "k", "v", "mask", "scale"]}
 

@@ -130,3 +130,20 @@ def test_rms_norm_bf16_and_batched_shapes():
     np.testing.assert_allclose(got.float().cpu().numpy(), ref, rtol=1e-2, atol=1e-2)
     got32 = norm.rms_norm(torch.from_numpy(x).cuda(), w)
     np.testing.assert_allclose(got32.cpu().numpy(), ref, rtol=1e-5, atol=1e-5)
+
+
+def test_rope_matches_reference_golden(golden_dir):
+    """ccut_apply_rope against the reference's apply_rope (ccut/blocks/rope.py:130-175):
+    no scaling (head dim 128) and yarn (attention factor on q, positions ~4000)."""
+    from ccut_b200.blocks import rope
+
+    g = np.load(golden_dir / "attn_norm.npz")
+    for i in range(2):
+        q, k = (formats.bf16_bits_to_f32(g[f"rope{i}_{n}"]) for n in "qk")
+        args = (g[f"rope{i}_inv_freq"], g[f"rope{i}_pos"], float(g[f"rope{i}_attn"]), str(g[f"rope{i}_type"]))
+        qo, ko = rope.apply_rope(q, k, *args)  # numpy (fp32) in
+        np.testing.assert_allclose(qo, g[f"rope{i}_q_out"], rtol=1e-5, atol=1e-5)
+        np.testing.assert_allclose(ko, g[f"rope{i}_k_out"], rtol=1e-5, atol=1e-5)
+        qt, kt = rope.apply_rope(_dev(g[f"rope{i}_q"]), _dev(g[f"rope{i}_k"]), *args)  # bf16 tensors in
+        np.testing.assert_allclose(qt.cpu().numpy(), g[f"rope{i}_q_out"], rtol=1e-5, atol=1e-5)
+        np.testing.assert_allclose(kt.cpu().numpy(), g[f"rope{i}_k_out"], rtol=1e-5, atol=1e-5)

@@ -201,3 +201,16 @@ def test_rms_norm_oracle_matches_reference(golden_dir):
         w = g[f"rms{i}_w"]
         y = attention.rms_norm(x, w if w.size else None, float(g[f"rms{i}_eps"]))
         np.testing.assert_allclose(y, g[f"rms{i}_y"], rtol=1e-6, atol=1e-6)
+
+
+def test_rope_oracle_matches_reference(golden_dir):
+    """oracle.attention.apply_rope against the reference's apply_rope (ccut/blocks/rope.py:130-175)."""
+    from oracle import attention
+
+    g = np.load(golden_dir / "attn_norm.npz")
+    for i in range(2):
+        q, k = (formats.bf16_bits_to_f32(g[f"rope{i}_{n}"]) for n in "qk")
+        qo, ko = attention.apply_rope(q, k, g[f"rope{i}_inv_freq"], g[f"rope{i}_pos"], float(g[f"rope{i}_attn"]),
+                                      str(g[f"rope{i}_type"]))
+        np.testing.assert_allclose(qo, g[f"rope{i}_q_out"], rtol=1e-6, atol=1e-6)
+        np.testing.assert_allclose(ko, g[f"rope{i}_k_out"], rtol=1e-6, atol=1e-6)
