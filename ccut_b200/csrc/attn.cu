@@ -441,15 +441,17 @@ int ccut_gqa_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, 
   if (head_dim == 128) {
     auto kern = ob ? gqa_attn_kernel<128, true> : gqa_attn_kernel<128, false>;
     constexpr size_t smem = TcAttnSmem<128>::kBytes;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return CCUT_ERR_CUDA;
+    static std::atomic<uint64_t> smem_set[2];  // per output type: devices with the limit raised
+    rc = ensure_smem_limit(kern, smem, smem_set[ob]);
+    if (rc) return rc;
     rc = launch_k(kern, grid, dim3(kTcWarps * 32), smem, stream, q, k, v, heads, kv_heads, seq, kv_len, causal_start,
                   scale, softcap, sp, tps, out, part);
   } else {
     auto kern = ob ? gqa_attn_kernel<64, true> : gqa_attn_kernel<64, false>;
     constexpr size_t smem = TcAttnSmem<64>::kBytes;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return CCUT_ERR_CUDA;
+    static std::atomic<uint64_t> smem_set[2];
+    rc = ensure_smem_limit(kern, smem, smem_set[ob]);
+    if (rc) return rc;
     rc = launch_k(kern, grid, dim3(kTcWarps * 32), smem, stream, q, k, v, heads, kv_heads, seq, kv_len, causal_start,
                   scale, softcap, sp, tps, out, part);
   }

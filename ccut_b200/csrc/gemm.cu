@@ -414,12 +414,9 @@ template <int FMT, int MODE, int MT>
 static int launch_gemm_t(const GemmArgs& a, int num_sms, cudaStream_t st) {
   using C = GemmCfg<FMT, MODE, MT>;
   auto kern = moe_gemm_kernel<FMT, MODE, MT>;
-  static bool attr_done = false;  // per instantiation; benign race (idempotent)
-  if (!attr_done) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) != cudaSuccess)
-      return CCUT_ERR_CUDA;
-    attr_done = true;
-  }
+  static std::atomic<uint64_t> smem_set{0};  // devices with the shared-memory limit raised
+  const int rc = ensure_smem_limit(kern, C::kSmem, smem_set);
+  if (rc) return rc;
   return launch_k(kern, dim3(num_sms * C::kMinBlocks), dim3(C::kThreads), C::kSmem, st, a);
 }
 

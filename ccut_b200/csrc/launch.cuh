@@ -19,6 +19,8 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
+#include <cstdint>
 #include <utility>
 
 #include "../../include/ccut_moe.h"
@@ -40,6 +42,21 @@ struct PdlScope {
   PdlScope(const PdlScope&) = delete;
   PdlScope& operator=(const PdlScope&) = delete;
 };
+
+// Raises the dynamic shared-memory limit of `kern` to `bytes` on the current device, once
+// per device (the attribute belongs to the device's context, so a process that drives
+// several GPUs sets it on each).  `done` is the caller's per-kernel set of devices (bit d).
+template <typename K>
+int ensure_smem_limit(K kern, size_t bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CCUT_ERR_CUDA;
+  const uint64_t bit = dev >= 0 && dev < 64 ? (uint64_t)1 << dev : 0;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return CCUT_OK;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) != cudaSuccess)
+    return CCUT_ERR_CUDA;
+  done.fetch_or(bit, std::memory_order_release);
+  return CCUT_OK;
+}
 
 // kern<<<grid, block, smem, st>>>(args...), with programmatic stream serialization inside a
 // PdlScope for a small call.

@@ -480,14 +480,9 @@ template <int FMT, int MODE, int NT>
 static int launch_tc_t(const CUtensorMap& map, const TcArgs& a, int num_sms, cudaStream_t st) {
   using C = TcCfg<FMT, MODE, NT>;
   auto kern = tc_gemm_kernel<FMT, MODE, NT>;
-  static int attr_done = -1;  // device the attribute was set for
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (attr_done != dev) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) != cudaSuccess)
-      return CCUT_ERR_CUDA;
-    attr_done = dev;
-  }
+  static std::atomic<uint64_t> smem_set{0};  // devices with the shared-memory limit raised
+  const int rc = ensure_smem_limit(kern, C::kSmem, smem_set);
+  if (rc) return rc;
   return launch_k(kern, dim3(num_sms), dim3(C::kThreads), C::kSmem, st, map, a);
 }
 
