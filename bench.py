@@ -3,10 +3,13 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
 
 A step is one pass of the MoE layer (route -> permute -> gate/up GEMM -> down GEMM ->
-combine) over one batch of `tokens` seeded synthetic bf16 activations per GPU, with the
-seeded random-init layer resident in HBM.  Under torchrun each rank runs its own batch
-(weak scaling); timing is CUDA events on the launching stream between barrier +
-synchronize fences, max over ranks.
+combine) over one batch of the workload's seeded synthetic bf16 activations, with the
+seeded random-init layer resident in HBM.  Under torchrun (--gpus N > 1) the layer runs
+expert-parallel: the workload's tokens are split over the ranks (strong scaling: the same
+total tokens at every N), each rank keeps E/N routed experts, and tokens and partial
+outputs cross NCCL.  Timing is CUDA events on the launching stream between barrier +
+synchronize fences, max over ranks.  `--workload cfg3_attn_decode` times the GQA attention
+block instead (its own metric).
 
 `--impl reference` times the reference algorithm on the host cores instead (the numpy
 oracle port of CostCut-Infer's MoE path: per-call dequant of every touched expert, fp32

@@ -74,8 +74,11 @@ class DenseFfn:
         self._perm: dict[int, Permutation] = {}
 
     def _identity(self, T: int) -> Permutation:
+        """Identity permutation of T tokens (cached for the last few batch sizes)."""
         p = self._perm.get(T)
         if p is None:
+            if len(self._perm) >= 8:
+                self._perm.pop(next(iter(self._perm)))
             dev = self.device
             ar = torch.arange(max(T, 1), dtype=torch.int32, device=dev)
             p = Permutation(torch.tensor([0, T], dtype=torch.int32, device=dev), ar,
