@@ -21,13 +21,20 @@ reference's own outputs (``tests/golden/attn_norm.npz``, made by
   over the two halves of the head dim, q first scaled by the attention factor for the
   ``yarn`` / ``linear`` scalings; q ``[batch, heads, seq, d]``, k ``[batch, kv_heads, seq,
   d]``, positions ``[batch, seq]``.
+* ``mla_attention`` follows ``mla_prefill`` / ``mla_decode`` (``ccut/blocks/attn_mla.py:85-167``):
+  over a latent cache ``c [kv_len, rank]`` and ``k_pe [kv_len, d_rope]``, head h scores
+  ``(c @ k_up)[:, h] . q_nope[h] + k_pe . q_pe[h]`` times ``scale``, query row s of a batch that
+  starts at ``start_pos`` sees ``min(start_pos + s + 1, kv_len)`` positions, and the output is
+  ``softmax @ (c @ v_up)[:, h]``.  ``mla_attention_absorbed`` computes the same through the
+  latent space (``q_nope`` folded into ``k_up``, the output unfolded through ``v_up``), the
+  form a GPU kernel streams.
 """
 
 from __future__ import annotations
 
 import numpy as np
 
-__all__ = ["apply_rope", "causal_mask", "gqa_attention", "rms_norm"]
+__all__ = ["apply_rope", "causal_mask", "gqa_attention", "mla_attention", "mla_attention_absorbed", "rms_norm"]
 
 
 def causal_mask(seq_len: int, start_pos: int) -> np.ndarray:
@@ -92,3 +99,44 @@ def apply_rope(q, k, inv_freq, positions, attention_factor: float = 1.0, scaling
         return out
 
     return rot(q32), rot(k32)
+
+
+def _mla_probs(scores: np.ndarray, seq: int, kv_len: int, start_pos: int) -> np.ndarray:
+    """scores [seq, heads, kv_len] (already scaled) -> causal softmax probabilities."""
+    vis = np.minimum(start_pos + np.arange(seq) + 1, kv_len)
+    masked = np.arange(kv_len)[None, :] >= vis[:, None]  # [seq, kv_len]
+    scores = np.where(masked[:, None, :], np.float32(-1e30), scores).astype(np.float32)
+    scores = scores - scores.max(axis=-1, keepdims=True)
+    ex = np.exp(scores)
+    ex[scores < -1e29] = 0.0
+    return (ex / np.maximum(ex.sum(axis=-1, keepdims=True), 1e-30)).astype(np.float32)
+
+
+def mla_attention(c, k_pe, q_nope, q_pe, k_up, v_up, scale: float, start_pos: int) -> np.ndarray:
+    """c [kv_len, rank], k_pe [kv_len, d_rope], q_nope [seq, heads, d_nope], q_pe [seq, heads,
+    d_rope], k_up [rank, heads * d_nope], v_up [rank, heads * d_v] -> [seq, heads, d_v]."""
+    c, k_pe = np.asarray(c, np.float32), np.asarray(k_pe, np.float32)
+    q_nope, q_pe = np.asarray(q_nope, np.float32), np.asarray(q_pe, np.float32)
+    seq, heads, d_nope = q_nope.shape
+    kv_len = c.shape[0]
+    k = (c @ np.asarray(k_up, np.float32)).reshape(kv_len, heads, d_nope)
+    v = (c @ np.asarray(v_up, np.float32)).reshape(kv_len, heads, -1)
+    scores = (np.einsum("shd,khd->shk", q_nope, k) + np.einsum("shd,kd->shk", q_pe, k_pe)) * np.float32(scale)
+    probs = _mla_probs(scores, seq, kv_len, start_pos)
+    return np.einsum("shk,khd->shd", probs, v).astype(np.float32)
+
+
+def mla_attention_absorbed(c, k_pe, q_nope, q_pe, k_up, v_up, scale: float, start_pos: int) -> np.ndarray:
+    """``mla_attention`` through the latent space: q_lat[s, h] = k_up_h @ q_nope[s, h] (rank),
+    scores = q_lat . c + q_pe . k_pe, o_lat = probs @ c, out = o_lat @ v_up_h."""
+    c, k_pe = np.asarray(c, np.float32), np.asarray(k_pe, np.float32)
+    q_nope, q_pe = np.asarray(q_nope, np.float32), np.asarray(q_pe, np.float32)
+    seq, heads, d_nope = q_nope.shape
+    rank, kv_len = c.shape[1], c.shape[0]
+    ku = np.asarray(k_up, np.float32).reshape(rank, heads, d_nope)
+    vu = np.asarray(v_up, np.float32).reshape(rank, heads, -1)
+    q_lat = np.einsum("shd,rhd->shr", q_nope, ku)
+    scores = (np.einsum("shr,kr->shk", q_lat, c) + np.einsum("shd,kd->shk", q_pe, k_pe)) * np.float32(scale)
+    probs = _mla_probs(scores, seq, kv_len, start_pos)
+    o_lat = np.einsum("shk,kr->shr", probs, c)
+    return np.einsum("shr,rhd->shd", o_lat, vu).astype(np.float32)

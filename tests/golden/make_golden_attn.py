@@ -10,6 +10,9 @@ Cases (inputs are bf16-representable, stored as bf16 bit patterns, outputs fp32)
               or no mask; grouped (8 query heads on 2 and on 1 kv heads) and plain heads,
               head dims 64 and 128, one and several query rows.
 ``rms{i}_*``  ``rms_norm`` (``ccut/blocks/norm.py:14-26``) with and without a weight.
+``mla{i}_*``  ``mla_decode`` / ``mla_prefill`` (``ccut/blocks/attn_mla.py:85-167``) over an
+              ``MLAState`` latent cache: one decode token, and a causal prefill batch after a
+              prefix.
 ``rope{i}_*`` ``apply_rope`` (``ccut/blocks/rope.py:130-175``) with the inverse frequencies
               and attention factor of ``build_rope``: no scaling (head dim 128, theta 1e6)
               and yarn (head dim 64, factor 4: the attention factor scales q).
@@ -58,6 +61,7 @@ def main(argv=None) -> int:
     sys.path.insert(0, args.reference)
     from ccut.blocks.attn_gqa import build_causal_mask, gqa_attention_fast
     from ccut.blocks.norm import rms_norm
+    from ccut.blocks.attn_mla import MLAState, mla_decode, mla_prefill
     from ccut.blocks.rope import apply_rope, build_rope
 
     rng = np.random.default_rng(2024)
@@ -89,6 +93,26 @@ def main(argv=None) -> int:
         out.update({f"rope{i}_q": qb, f"rope{i}_k": kb, f"rope{i}_inv_freq": np.asarray(inv_freq, np.float32),
                     f"rope{i}_attn": np.float32(attn), f"rope{i}_type": np.array(stype), f"rope{i}_pos": pos,
                     f"rope{i}_q_out": qo.astype(np.float32), f"rope{i}_k_out": ko.astype(np.float32)})
+    # MLA: rank 64, rope dim 16, nope dim 32, v dim 32, 4 heads
+    rank, dr, dn, dv, heads = 64, 16, 32, 32, 4
+    for i, (prefix, seq) in enumerate(((19, 1), (11, 6))):
+        kv = prefix + seq
+        _, c = bf16_round(rng.standard_normal((kv, rank)))
+        _, kpe = bf16_round(rng.standard_normal((kv, dr)))
+        _, qn = bf16_round(rng.standard_normal((seq, heads, dn)))
+        _, qp = bf16_round(rng.standard_normal((seq, heads, dr)))
+        _, ku = bf16_round(rng.standard_normal((rank, heads * dn)) * 0.125)
+        _, vu = bf16_round(rng.standard_normal((rank, heads * dv)) * 0.125)
+        st = MLAState(rank, dr, max_tokens=64)
+        st.append(c, kpe)
+        scale = 1.0 / np.sqrt(dn + dr)
+        if seq == 1:
+            o = mla_decode(st, qn[0], qp[0], ku, vu, scale, prefix)[None]
+        else:
+            o = mla_prefill(st, qn, qp, ku, vu, scale, prefix)
+        out.update({f"mla{i}_c": c, f"mla{i}_kpe": kpe, f"mla{i}_qn": qn, f"mla{i}_qp": qp, f"mla{i}_ku": ku,
+                    f"mla{i}_vu": vu, f"mla{i}_scale": np.float32(scale), f"mla{i}_start": np.int64(prefix),
+                    f"mla{i}_out": np.asarray(o, np.float32)})
     np.savez_compressed(HERE / "attn_norm.npz", **out)
     print("wrote", HERE / "attn_norm.npz")
     return 0

@@ -214,3 +214,17 @@ def test_rope_oracle_matches_reference(golden_dir):
                                       str(g[f"rope{i}_type"]))
         np.testing.assert_allclose(qo, g[f"rope{i}_q_out"], rtol=1e-6, atol=1e-6)
         np.testing.assert_allclose(ko, g[f"rope{i}_k_out"], rtol=1e-6, atol=1e-6)
+
+
+def test_mla_oracle_matches_reference(golden_dir):
+    """oracle.attention.mla_attention (and its latent-space form) against the reference's
+    mla_decode / mla_prefill (ccut/blocks/attn_mla.py:85-167)."""
+    from oracle import attention
+
+    g = np.load(golden_dir / "attn_norm.npz")
+    for i in range(2):
+        args = [g[f"mla{i}_{n}"] for n in ("c", "kpe", "qn", "qp", "ku", "vu")]
+        scale, start = float(g[f"mla{i}_scale"]), int(g[f"mla{i}_start"])
+        ref = g[f"mla{i}_out"]
+        np.testing.assert_allclose(attention.mla_attention(*args, scale, start), ref, rtol=1e-5, atol=1e-5)
+        np.testing.assert_allclose(attention.mla_attention_absorbed(*args, scale, start), ref, rtol=1e-4, atol=1e-5)
