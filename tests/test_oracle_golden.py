@@ -228,3 +228,14 @@ def test_mla_oracle_matches_reference(golden_dir):
         ref = g[f"mla{i}_out"]
         np.testing.assert_allclose(attention.mla_attention(*args, scale, start), ref, rtol=1e-5, atol=1e-5)
         np.testing.assert_allclose(attention.mla_attention_absorbed(*args, scale, start), ref, rtol=1e-4, atol=1e-5)
+
+
+def test_topk_softmax_wide_routers_match_reference(golden_dir):
+    """The oracle's topk_softmax against the reference's at 128 experts top-8 (normalised)
+    and 256 experts top-16 (both modes), with exact ties: ids bit-exact, weights to fp32."""
+    g = np.load(golden_dir / "routing_wide.npz")
+    for i in range(3):
+        k, norm = int(g[f"c{i}_k"]), bool(g[f"c{i}_norm"])
+        w, ids = routing.topk_softmax(g[f"c{i}_logits"], k, norm_topk_prob=norm)
+        assert np.array_equal(ids, g[f"c{i}_ids"]), i
+        np.testing.assert_allclose(w, g[f"c{i}_w"], rtol=1e-6, atol=1e-7)
