@@ -17,6 +17,13 @@ Public entry points
 ``dense.DenseFfn``           dense quantized SwiGLU FFN (the expert kernels with one expert)
 ``blocks.attn_gqa``          drop-ins for ``ccut.blocks.attn_gqa`` (GQA attention on tensor cores)
 ``blocks.norm``              drop-in for ``ccut.blocks.norm.rms_norm``
+``blocks.rope``              drop-in for ``ccut.blocks.rope.apply_rope``
+``model``                    ``MoeDecoder``: embedding, ``full_attn`` decoder layers (attention,
+                             norms, RoPE, bf16 KV cache in HBM, MoE or dense FFN), final norm,
+                             ``lm_head`` -- the reference's generic layer forward on the GPU
+``backend.GenericBackend``   the ``generate_step`` backend the reference's ``Engine`` calls, over
+                             a ``MoeDecoder`` (prefix-reusing sequence caches, on-device sampling)
+``sampling``                 the reference's temperature / top-k / min-p / top-p transform in torch
 """
 
 from ccut_b200.layer import MoeLayer, Permutation, Routing  # noqa: F401

@@ -1,0 +1,244 @@
+"""Decoder stack on the GPU: the reference's generic layer forward run on this package's kernels.
+
+Follows ``model_forward_layer`` and ``full_attn_forward`` (``ccut/models/generic.py:304-345``,
+``:403-447``) for ``full_attn`` layers with a MoE or dense FFN, and the step layout of the same
+module (``ccut/models/generic.py:9-18``): embedding rows, the layers, the final RMSNorm and
+``lm_head``.  For ``seq`` new tokens of one sequence at absolute positions ``p .. p + seq - 1``
+each layer computes
+
+====================================  ==================================================
+``x = rms_norm(h, ln1)``              ``ccut_rms_norm`` on the fp32 residual, then bf16
+``q | k | v = x @ [Wq; Wk; Wv]^T``    one bf16 GEMM (torch, cuBLAS), bf16 out
+``q, k = q_norm(q), k_norm(k)``       ``ccut_rms_norm`` in bf16 (optional; the weight spans
+                                      the whole projection or one head)
+``q, k = rope(q, k, p ..)``           ``ccut_apply_rope``, then bf16
+``K[:, p:], V[:, p:] = k, v``         the sequence's bf16 cache ``[kv_heads, max_len, d]``
+``o = attention(q, K, V)``            ``ccut_gqa_attention`` over the cache buffer with
+                                      ``causal_start = p``: query ``i`` reads positions
+                                      ``<= p + i`` only, so the buffer needs no compaction
+``h += o @ Wo^T``                     bf16 GEMM, added to the fp32 residual
+``h += ffn(rms_norm(h, ln2))``        ``MoeLayer`` / ``DenseFfn`` (bf16 in, fp32 out)
+====================================  ==================================================
+
+and the step ends with ``logits = rms_norm(h, final_norm) @ lm_head^T`` in fp32 (``lm_head``
+is kept as an fp32 copy).  Every block gets its documented layout; the reference's layer
+passes q as ``[1, seq, heads, d]`` to blocks that take ``[batch, heads, seq, d]``, which is
+the same computation for one token and one kv head only.
+
+Nothing here runs on the host: the norms, RoPE and attention go through the C-ABI library
+(``_lib.call`` raises if it is missing), the FFN through ``MoeLayer`` / ``DenseFfn``.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from ccut_b200 import _lib
+from ccut_b200.blocks.norm import rms_norm
+from ccut_b200.blocks.rope import apply_rope
+from ccut_b200.layer import _ptr, _stream
+
+__all__ = ["DecoderLayer", "KvCache", "MoeDecoder", "rope_table"]
+
+
+def rope_table(head_dim: int, rope_theta: float, rope_scaling: dict | None = None) -> tuple[np.ndarray, float]:
+    """``(inv_freq [head_dim / 2] float32, attention_factor)`` of the reference's ``build_rope``
+    (``ccut/blocks/rope.py:88-127``) for no scaling and ``linear`` scaling, computed with the same
+    float32 operations.  Other scalings: pass the table ``build_rope`` returns to ``MoeDecoder``."""
+    rs = rope_scaling or {}
+    stype = (rs.get("type") or "none").casefold()
+    factor = float(rs.get("factor", 1.0))
+    inv = 1.0 / (rope_theta ** (np.arange(0, head_dim, 2, dtype=np.float32) / head_dim))
+    if stype == "none" or factor <= 1.0:
+        return inv.astype(np.float32), 1.0
+    if stype == "linear":
+        return (inv / factor).astype(np.float32), 1.0
+    raise NotImplementedError(f"rope scaling {stype!r}: pass inv_freq and attention_factor from build_rope")
+
+
+def _tensor(a, dev: torch.device, dtype: torch.dtype) -> torch.Tensor:
+    t = a if isinstance(a, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32))
+    return t.to(device=dev, dtype=dtype).contiguous()
+
+
+class KvCache:
+    """One sequence's bf16 k (rotated) / v cache, ``[layers, kv_heads, max_len, head_dim]`` each;
+    ``length`` positions are valid."""
+
+    def __init__(self, layers: int, kv_heads: int, max_len: int, head_dim: int, device="cuda"):
+        if max_len <= 0:
+            raise ValueError("max_len must be positive")
+        self.k = torch.zeros((layers, kv_heads, max_len, head_dim), dtype=torch.bfloat16, device=device)
+        self.v = torch.zeros_like(self.k)
+        self.max_len = int(max_len)
+        self.length = 0
+
+    def truncate(self, n: int) -> None:
+        """Keep the first ``n`` positions (later ones are overwritten by the next forward)."""
+        if not 0 <= n <= self.length:
+            raise ValueError(f"cannot truncate {self.length} cached positions to {n}")
+        self.length = int(n)
+
+
+def _attend(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, start_pos: int, softcap: float | None) -> torch.Tensor:
+    """q ``[1, heads, seq, d]`` bf16, k / v ``[kv_heads, max_len, d]`` bf16 cache buffers ->
+    ``[1, heads, seq, d]`` bf16 (``ccut_gqa_attention`` with ``causal_start = start_pos``)."""
+    if not (q.is_cuda and k.is_cuda and v.is_cuda):
+        raise ValueError("attention runs on CUDA tensors only")
+    _, H, S, d = q.shape
+    Hkv, L = k.shape[0], k.shape[1]
+    lib = _lib.load()
+    nbytes = lib.ccut_gqa_attention_workspace_bytes(1, H, Hkv, S, L, d)
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=q.device)
+    out = torch.empty((1, H, S, d), dtype=torch.bfloat16, device=q.device)
+    with torch.cuda.device(q.device):
+        _lib.call("ccut_gqa_attention", _ptr(q), _ptr(k), _ptr(v), 1, H, Hkv, S, L, d, int(start_pos), 0.0,
+                  float(softcap or 0.0), _ptr(out), _lib.OUT_BF16, _ptr(ws), ws.numel(), _stream())
+    return out
+
+
+class DecoderLayer:
+    """One ``full_attn`` decoder layer.
+
+    ``ln1`` / ``ln2`` [H]; ``wq`` [heads * d, H], ``wk`` / ``wv`` [kv_heads * d, H], ``wo``
+    [H, heads * d] (checkpoint ``[out, in]`` layout, converted to bf16); ``q_norm`` / ``k_norm``
+    None, ``[heads * d]`` / ``[kv_heads * d]`` (over the whole projection, the reference's
+    ``rms_norm(q.reshape(seq, -1), w)``) or ``[d]`` (per head); ``ffn`` any object with
+    ``forward(x_bf16 [T, H], out_dtype) -> [T, H]`` (``MoeLayer``, ``DenseFfn``)."""
+
+    def __init__(self, ln1, wq, wk, wv, wo, ln2, ffn, q_norm=None, k_norm=None, *, heads: int, kv_heads: int,
+                 head_dim: int, device="cuda"):
+        dev = torch.device(device)
+        if head_dim not in (64, 128):
+            raise NotImplementedError(f"head dim {head_dim} (have 64, 128)")
+        if heads <= 0 or kv_heads <= 0 or heads % kv_heads:
+            raise ValueError(f"heads ({heads}) must be a positive multiple of kv_heads ({kv_heads})")
+        self.heads, self.kv_heads, self.head_dim = int(heads), int(kv_heads), int(head_dim)
+        self.ln1, self.ln2 = _tensor(ln1, dev, torch.float32), _tensor(ln2, dev, torch.float32)
+        H = self.ln1.numel()
+        self.hidden = H
+        shapes = {"wq": (heads * head_dim, H), "wk": (kv_heads * head_dim, H), "wv": (kv_heads * head_dim, H),
+                  "wo": (H, heads * head_dim)}
+        mats = {}
+        for name, m in zip(shapes, (wq, wk, wv, wo)):
+            t = _tensor(m, dev, torch.bfloat16)
+            if tuple(t.shape) != shapes[name]:
+                raise ValueError(f"{name} must be {shapes[name]}, got {tuple(t.shape)}")
+            mats[name] = t
+        if self.ln2.numel() != H:
+            raise ValueError("ln1 and ln2 must have the same size")
+        self.wqkv = torch.cat([mats["wq"], mats["wk"], mats["wv"]], 0).contiguous()
+        self.wo = mats["wo"]
+        self.q_norm = self._norm_w(q_norm, heads, dev, "q_norm")
+        self.k_norm = self._norm_w(k_norm, kv_heads, dev, "k_norm")
+        self.ffn = ffn
+        self.device = dev
+
+    def _norm_w(self, w, n: int, dev, name: str):
+        if w is None:
+            return None
+        t = _tensor(w, dev, torch.float32)
+        if t.numel() not in (n * self.head_dim, self.head_dim):
+            raise ValueError(f"{name} must have {n * self.head_dim} or {self.head_dim} elements, got {t.numel()}")
+        return t
+
+    def _qk_norm(self, x: torch.Tensor, w, n: int, eps: float) -> torch.Tensor:
+        """x [seq, n * d] bf16 -> [seq, n, d] bf16."""
+        seq, d = x.shape[0], self.head_dim
+        if w is None:
+            return x.reshape(seq, n, d)
+        if w.numel() == n * d:
+            return rms_norm(x.contiguous(), w, eps).reshape(seq, n, d)
+        return rms_norm(x.reshape(seq, n, d).contiguous(), w, eps)
+
+    def forward(self, h: torch.Tensor, cache: KvCache, layer: int, start_pos: int, rope: "_Rope") -> torch.Tensor:
+        """h [seq, H] fp32 (the residual stream) -> [seq, H] fp32; writes the cache at
+        ``start_pos .. start_pos + seq - 1`` of ``layer``."""
+        seq = h.shape[0]
+        H, Hkv, d = self.heads, self.kv_heads, self.head_dim
+        x = rms_norm(h, self.ln1, rope.eps).to(torch.bfloat16)
+        qkv = F.linear(x, self.wqkv)
+        q = self._qk_norm(qkv[:, : H * d], self.q_norm, H, rope.eps)
+        k = self._qk_norm(qkv[:, H * d: (H + Hkv) * d], self.k_norm, Hkv, rope.eps)
+        v = qkv[:, (H + Hkv) * d:].reshape(seq, Hkv, d)
+        pos = torch.arange(start_pos, start_pos + seq, dtype=torch.int32, device=h.device).reshape(1, seq)
+        qr, kr = apply_rope(q.transpose(0, 1).unsqueeze(0), k.transpose(0, 1).unsqueeze(0), rope.inv_freq, pos,
+                            rope.attn_factor, rope.scaling_type)
+        qr = qr.to(torch.bfloat16)
+        cache.k[layer, :, start_pos: start_pos + seq] = kr[0]
+        cache.v[layer, :, start_pos: start_pos + seq] = v.transpose(0, 1)
+        o = _attend(qr, cache.k[layer], cache.v[layer], start_pos, rope.softcap)
+        h = h + F.linear(o[0].transpose(0, 1).reshape(seq, H * d), self.wo).float()
+        x2 = rms_norm(h, self.ln2, rope.eps).to(torch.bfloat16)
+        return h + self.ffn.forward(x2, out_dtype=torch.float32)
+
+
+class _Rope:
+    """The per-model constants every layer's attention reads."""
+
+    def __init__(self, inv_freq: torch.Tensor, attn_factor: float, scaling_type: str, eps: float, softcap):
+        self.inv_freq, self.attn_factor, self.scaling_type = inv_freq, float(attn_factor), scaling_type
+        self.eps, self.softcap = float(eps), softcap
+
+
+class MoeDecoder:
+    """Embedding, decoder layers, final norm and ``lm_head`` of one model.
+
+    ``embed`` / ``lm_head`` [vocab, H]; ``inv_freq`` / ``attention_factor`` / ``scaling_type``
+    as ``build_rope`` returns them (``rope_table`` for the plain cases); ``eps`` the epsilon of
+    every RMSNorm (the reference's layer calls ``rms_norm`` with its default, 1e-6); ``softcap``
+    the model's ``attn_logit_softcapping`` (or None)."""
+
+    def __init__(self, embed, layers: list, final_norm, lm_head, *, inv_freq, attention_factor: float = 1.0,
+                 scaling_type: str = "none", eps: float = 1e-6, softcap: float | None = None, device="cuda"):
+        dev = torch.device(device)
+        if not layers:
+            raise ValueError("a decoder needs at least one layer")
+        self.embed = _tensor(embed, dev, torch.bfloat16)
+        self.final_norm = _tensor(final_norm, dev, torch.float32)
+        self.lm_head = _tensor(lm_head, dev, torch.float32)
+        V, H = self.embed.shape
+        if tuple(self.lm_head.shape) != (V, H) or self.final_norm.numel() != H:
+            raise ValueError(f"lm_head must be {(V, H)} and final_norm [{H}]")
+        for i, lay in enumerate(layers):
+            if lay.hidden != H or (lay.kv_heads, lay.head_dim) != (layers[0].kv_heads, layers[0].head_dim):
+                raise ValueError(f"layer {i} does not match the model's hidden size / kv layout")
+        self.layers = list(layers)
+        self.vocab, self.hidden = V, H
+        ft = _tensor(inv_freq, dev, torch.float32)
+        if ft.numel() != layers[0].head_dim // 2:
+            raise ValueError(f"inv_freq has {ft.numel()} entries for head dim {layers[0].head_dim}")
+        self.rope = _Rope(ft, attention_factor, scaling_type, eps, softcap)
+        self.device = dev
+
+    def new_cache(self, max_len: int) -> KvCache:
+        l0 = self.layers[0]
+        return KvCache(len(self.layers), l0.kv_heads, max_len, l0.head_dim, self.device)
+
+    def forward(self, tokens, cache: KvCache, start_pos: int | None = None, all_logits: bool = False) -> torch.Tensor:
+        """Run ``tokens`` at positions ``start_pos ..`` (default: after the cached ones) and return
+        the fp32 logits of the last token ``[vocab]`` (``all_logits``: of every token
+        ``[seq, vocab]``).  Positions from ``start_pos`` on are replaced in ``cache``."""
+        if isinstance(tokens, torch.Tensor):
+            ids = tokens.to(device=self.device, dtype=torch.int64).reshape(-1)
+        else:
+            ids = torch.as_tensor(np.asarray(tokens, dtype=np.int64).reshape(-1)).to(self.device)
+        seq = ids.numel()
+        p = cache.length if start_pos is None else int(start_pos)
+        if seq == 0:
+            raise ValueError("no tokens to run")
+        if not 0 <= p <= cache.length:
+            raise ValueError(f"start position {p} is past the {cache.length} cached positions")
+        if p + seq > cache.max_len:
+            raise ValueError(f"{p} + {seq} positions do not fit the cache of {cache.max_len}")
+        if int(ids.min()) < 0 or int(ids.max()) >= self.vocab:
+            raise ValueError(f"token ids must be in [0, {self.vocab})")
+        h = self.embed.index_select(0, ids).float()
+        for i, lay in enumerate(self.layers):
+            h = lay.forward(h, cache, i, p, self.rope)
+        cache.length = p + seq
+        last = h if all_logits else h[-1:]
+        logits = F.linear(rms_norm(last, self.final_norm, self.rope.eps), self.lm_head)
+        return logits if all_logits else logits[0]

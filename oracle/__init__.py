@@ -16,6 +16,9 @@ Modules
 ``moe``      SwiGLU expert FFN, token grouping, weighted combine, shared experts,
              whole-layer forward.
 ``inputs``   seeded synthetic layer/activation generator for the benchmark configs.
+``attention`` GQA / MLA attention, RMSNorm and RoPE blocks.
+``model``    the generic decoder layer (attention block + MoE / dense FFN) and a whole
+             decoder step (embedding, layers, final norm, ``lm_head``).
 
 Pinning.  Each function cites the reference file:line it follows (paths relative to the
 reference's ``python/`` directory).  ``tests/golden/make_golden.py`` imports the

@@ -1,0 +1,303 @@
+"""Decoder stack and engine backend on the CPU: the oracle against the reference's own layer
+forward, the sampling transform against the reference's, and the host logic of
+``ccut_b200.model`` / ``ccut_b200.backend`` (weight layouts, cache positions, prefix reuse,
+errors).
+
+The host-logic tests run ``MoeDecoder`` on CPU tensors with its three device calls (RMSNorm,
+RoPE, attention) replaced by short torch functions written here and a torch MoE block; the
+product runs those calls through the CUDA library (``tests/test_zzz_gpu_engine.py``).
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from tests.model_helpers import make_tiny, rope_inv_freq
+from oracle import model as omodel
+
+
+# ---- oracle pins --------------------------------------------------------------------------
+def _golden_tiny(g, ci):
+    qk = str(g[f"m{ci}_qk_norm"])
+    return make_tiny(int(g[f"m{ci}_seed"]), norm_topk_prob=bool(g[f"m{ci}_norm"]), qk_norm=None if qk == "none" else qk)
+
+
+def test_oracle_decoder_matches_reference_layer(golden_dir):
+    """oracle.model against the reference's model_forward_layer (ccut/models/generic.py:403-447)
+    decoding token by token: hidden state after every layer and the logits of every step."""
+    g = np.load(golden_dir / "model_decode.npz")
+    for ci in range(2):
+        t = _golden_tiny(g, ci)
+        spec = t.spec(g[f"m{ci}_inv_freq"])
+        cache, ffns = omodel.KvCache(), t.dense_ffns()
+        for s, tok in enumerate(g[f"m{ci}_tokens"]):
+            lg, hs = omodel.model_forward([tok], t.embed, t.attn, ffns, t.final_norm, t.lm_head, spec, cache, s)
+            for i in range(t.layers):
+                np.testing.assert_allclose(hs[i][0], g[f"m{ci}_h"][s, i], rtol=1e-5, atol=1e-5)
+            np.testing.assert_allclose(lg[0], g[f"m{ci}_logits"][s], rtol=1e-5, atol=1e-5)
+
+
+def test_rope_tables_match_reference(golden_dir):
+    from ccut_b200.model import rope_table
+
+    g = np.load(golden_dir / "model_decode.npz")
+    inv, attn = rope_table(64, 10000.0)
+    assert np.array_equal(inv, g["m0_inv_freq"]) and attn == float(g["m0_attn_factor"])
+    np.testing.assert_allclose(rope_inv_freq(64, 10000.0), g["m0_inv_freq"], rtol=1e-6)
+    lin, _ = rope_table(64, 10000.0, {"type": "linear", "factor": 4.0})
+    np.testing.assert_allclose(lin, inv / 4.0, rtol=1e-7)
+    with pytest.raises(NotImplementedError):
+        rope_table(64, 10000.0, {"type": "yarn", "factor": 4.0})
+
+
+def test_sampling_transform_matches_reference(golden_dir):
+    """ccut_b200.sampling.temperature_topk against the reference's (ccut/blocks/heads.py:76-126):
+    the same kept tokens and the same probabilities, the top-p edge case included."""
+    from ccut_b200.sampling import temperature_topk
+
+    g = np.load(golden_dir / "model_decode.npz")
+    for j, (temp, top_k, top_p, min_p) in enumerate(g["samp_params"]):
+        ref = g[f"samp{j}_probs"]
+        got = temperature_topk(g["samp_logits"], temp, int(top_k), top_p, min_p)
+        assert np.array_equal(got > 0, ref > 0), j
+        np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-7)
+        tg = temperature_topk(torch.from_numpy(g["samp_logits"]), temp, int(top_k), top_p, min_p)
+        np.testing.assert_allclose(tg.numpy(), ref, rtol=1e-5, atol=1e-7)
+
+
+def test_sample_greedy_and_seeded():
+    from ccut_b200.sampling import sample
+
+    logits = torch.tensor([0.5, 3.0, 3.0, -1.0])
+    assert sample(logits, {"temperature": 0.0}) == 1  # ties to the lowest index
+    g1, g2 = torch.Generator().manual_seed(5), torch.Generator().manual_seed(5)
+    a = [sample(logits, {"temperature": 1.0, "top_k": 3}, g1) for _ in range(20)]
+    b = [sample(logits, {"temperature": 1.0, "top_k": 3}, g2) for _ in range(20)]
+    assert a == b and set(a) <= {0, 1, 2}
+    assert {sample(logits + torch.tensor([0, 0, -0.1, 0]), {"temperature": 0.7, "top_k": 1}, g1)
+            for _ in range(5)} == {1}
+    # values equal to the k-th largest stay in (the reference's threshold test is ``x < thr``)
+    assert {sample(logits, {"temperature": 0.7, "top_k": 1}, g1) for _ in range(40)} == {1, 2}
+
+
+# ---- host logic with torch stand-ins for the device calls ---------------------------------
+def _norm(x, weight=None, eps=1e-6):
+    x32 = x.float()
+    y = x32 * torch.rsqrt((x32 * x32).mean(-1, keepdim=True) + eps)
+    if weight is not None:
+        y = y * weight.float()
+    return y.to(torch.bfloat16) if x.dtype == torch.bfloat16 else y
+
+
+def _rope(q, k, inv_freq, positions, attention_factor=1.0, scaling_type="none", seq_len=0):
+    f = positions.float()[:, None, :, None] * inv_freq.float()[None, None, None, :]
+    c, s = torch.cos(f), torch.sin(f)
+
+    def rot(x, scale):
+        x = x.float() * scale
+        h = x.shape[-1] // 2
+        return torch.cat([x[..., :h] * c - x[..., h:] * s, x[..., h:] * c + x[..., :h] * s], -1)
+
+    qs = attention_factor if scaling_type in ("yarn", "linear") and attention_factor != 1.0 else 1.0
+    return rot(q, qs), rot(k, 1.0)
+
+
+def _attend(q, k, v, start_pos, softcap):
+    _, H, S, d = q.shape
+    g = H // k.shape[0]
+    L = start_pos + S
+    kk = k[:, :L].float().repeat_interleave(g, 0)
+    vv = v[:, :L].float().repeat_interleave(g, 0)
+    sc = torch.einsum("hsd,hld->hsl", q[0].float(), kk) / math.sqrt(d)
+    if softcap:
+        sc = torch.tanh(sc / softcap) * softcap
+    mask = torch.arange(L)[None, :] > (start_pos + torch.arange(S))[:, None]
+    p = torch.softmax(sc.masked_fill(mask, float("-inf")), -1)
+    return torch.einsum("hsl,hld->hsd", p, vv)[None].to(torch.bfloat16)
+
+
+class _TorchMoe:
+    """MoE block with the tiny model's dense experts (softmax routing as the reference)."""
+
+    def __init__(self, t, i):
+        self.router = torch.from_numpy(t.router[i])
+        self.experts = [tuple(torch.from_numpy(m) for m in e) for e in t.experts[i]]
+        self.shared = tuple(torch.from_numpy(m) for m in t.shared[i]) if t.shared[i] is not None else None
+        self.k, self.norm = t.top_k, t.norm_topk_prob
+        self.calls = []
+
+    def _mlp(self, x, wg, wu, wd):
+        gt = x @ wg
+        return (gt / (1 + torch.exp(-gt)) * (x @ wu)) @ wd
+
+    def forward(self, x, out_dtype=torch.bfloat16):
+        assert x.dtype == torch.bfloat16 and x.dim() == 2
+        self.calls.append(x.shape[0])
+        xf = x.float()
+        lg = xf @ self.router.T
+        if self.norm:
+            vals, ids = torch.topk(lg, self.k, dim=1)
+            w = torch.softmax(vals, 1)
+        else:
+            w, ids = torch.topk(torch.softmax(lg, 1), self.k, dim=1)
+        out = torch.zeros_like(xf)
+        for t in range(x.shape[0]):
+            for j in range(self.k):
+                out[t] += w[t, j] * self._mlp(xf[t:t + 1], *self.experts[int(ids[t, j])])[0]
+        if self.shared is not None:
+            out += self._mlp(xf, *self.shared)
+        return out.to(out_dtype)
+
+
+@pytest.fixture
+def torch_ops(monkeypatch):
+    import ccut_b200.model as m
+
+    monkeypatch.setattr(m, "rms_norm", _norm)
+    monkeypatch.setattr(m, "apply_rope", _rope)
+    monkeypatch.setattr(m, "_attend", _attend)
+    return m
+
+
+def _build(m, t, **kw):
+    layers = [m.DecoderLayer(w.ln1, w.wq, w.wk, w.wv, w.wo, w.ln2, _TorchMoe(t, i), w.q_norm, w.k_norm, heads=t.heads,
+                             kv_heads=t.kv_heads, head_dim=t.head_dim, device="cpu") for i, w in enumerate(t.attn)]
+    inv, attn = m.rope_table(t.head_dim, t.theta)
+    return m.MoeDecoder(t.embed, layers, t.final_norm, t.lm_head, inv_freq=inv, attention_factor=attn, eps=t.eps,
+                        device="cpu", **kw)
+
+
+def _rel(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-12))
+
+
+@pytest.mark.parametrize("kv_heads, qk_norm", [(1, "flat"), (2, "head"), (4, None)])
+def test_decoder_host_logic_matches_oracle(torch_ops, kv_heads, qk_norm):
+    """Prefill of 5 tokens, then 3 single-token steps and a 2-token chunk: logits of every
+    position against the oracle's decoder (bf16 at the same points)."""
+    m = torch_ops
+    t = make_tiny(21, kv_heads=kv_heads, qk_norm=qk_norm, norm_topk_prob=kv_heads == 2)
+    dec = _build(m, t)
+    cache = dec.new_cache(32)
+    spec, ocache, ffns = t.spec(), omodel.KvCache(), t.dense_ffns()
+    rng = np.random.default_rng(3)
+    pos = 0
+    for n in (5, 1, 1, 1, 2):
+        toks = rng.integers(0, t.vocab, n)
+        got = dec.forward(toks, cache, all_logits=True)
+        ref, _ = omodel.model_forward(toks, t.embed, t.attn, ffns, t.final_norm, t.lm_head, spec, ocache, pos,
+                                      bf16_acts=True)
+        assert got.shape == (n, t.vocab) and _rel(got.numpy(), ref) < 5e-3
+        pos += n
+        assert cache.length == pos
+        last = dec.forward(toks[-1:], cache, start_pos=pos - 1)  # recompute the last position
+        assert last.shape == (t.vocab,) and _rel(last.numpy(), ref[-1]) < 5e-3
+    # a wrong position (one past) changes the logits: the comparison above is position-sensitive
+    c2 = dec.new_cache(32)
+    dec.forward([3, 9], c2)
+    c3 = dec.new_cache(32)
+    dec.forward([3, 3, 9], c3)
+    assert _rel(dec.forward([5], c2).numpy(), dec.forward([5], c3).numpy()) > 1e-3
+
+
+def test_decoder_checks(torch_ops):
+    m = torch_ops
+    t = make_tiny(22)
+    dec = _build(m, t)
+    cache = dec.new_cache(4)
+    with pytest.raises(ValueError):
+        dec.forward([], cache)
+    with pytest.raises(ValueError):
+        dec.forward([1, 2, 3, 4, 5], cache)  # past max_len
+    with pytest.raises(ValueError):
+        dec.forward([t.vocab], cache)
+    with pytest.raises(ValueError):
+        dec.forward([1], cache, start_pos=1)  # past the cached positions
+    dec.forward([1, 2], cache)
+    cache.truncate(1)
+    with pytest.raises(ValueError):
+        cache.truncate(2)
+    w = t.attn[0]
+    kw = dict(heads=t.heads, kv_heads=t.kv_heads, head_dim=t.head_dim, device="cpu")
+    with pytest.raises(NotImplementedError):
+        m.DecoderLayer(w.ln1, w.wq, w.wk, w.wv, w.wo, w.ln2, None, **{**kw, "head_dim": 96})
+    with pytest.raises(ValueError):
+        m.DecoderLayer(w.ln1, w.wq, w.wk.T, w.wv, w.wo, w.ln2, None, **kw)  # [in, out] by mistake
+    with pytest.raises(ValueError):
+        m.DecoderLayer(w.ln1, w.wq, w.wk, w.wv, w.wo, w.ln2, None, q_norm=np.ones(3), **kw)
+    with pytest.raises(ValueError):
+        m.DecoderLayer(w.ln1, w.wq, w.wk, w.wv, w.wo, w.ln2, None, **{**kw, "kv_heads": 3})
+    with pytest.raises(ValueError):
+        m.MoeDecoder(t.embed, [], t.final_norm, t.lm_head, inv_freq=np.ones(32), device="cpu")
+    with pytest.raises(ValueError):
+        m.MoeDecoder(t.embed, dec.layers, t.final_norm, t.lm_head, inv_freq=np.ones(31), device="cpu")
+
+
+def test_backend_prefix_reuse(torch_ops):
+    """generate_step as Engine._backend_step calls it (ccut/engine.py:305-333): a request grown
+    one token per step runs one position per step; chunked prefill runs each chunk once; a
+    diverging request reuses the shared prefix; the least recently used cache is evicted."""
+    from ccut_b200.backend import GenericBackend, common_prefix
+
+    m = torch_ops
+    t = make_tiny(23)
+    be = GenericBackend(_build(m, t), max_seqs=2, max_len=64, prefill_chunk=4)
+    prompt = [5, 9, 13, 2, 8, 1, 4]
+    ref = be.model.forward(prompt, be.model.new_cache(64))
+    assert be.tokens_run == 0
+    np.testing.assert_allclose(be.logits_for(prompt).numpy(), ref.numpy(), rtol=1e-5, atol=1e-5)
+    assert be.tokens_run == 7
+    ids = list(prompt)
+    for step in range(3):
+        ids.append(be.generate_step(ids, {"temperature": 0.0}))
+        assert be.tokens_run == 8 + step
+    full = be.model.forward(ids, be.model.new_cache(64))
+    np.testing.assert_allclose(be.logits_for(ids).numpy(), full.numpy(), rtol=2e-2, atol=2e-2)
+    assert be.tokens_run == 11  # the last position again, for its logits
+    # a request sharing the first 4 prompt tokens with the cached one
+    other = prompt[:4] + [30, 31]
+    be.logits_for(other)
+    assert be.tokens_run == 11 + 2
+    # engine-style chunked prefill: the ids grow by chunks
+    before = be.tokens_run
+    long = list(range(40, 52))
+    for n in (4, 8, 12):
+        be.logits_for(long[:n])
+    assert be.tokens_run - before == 4 + 4 + 4
+    assert len(be._seqs) == 2
+    assert common_prefix([1, 2, 3], [1, 2, 4, 5]) == 2 and common_prefix([1], [1, 2]) == 1
+    assert common_prefix([], [3]) == 0
+    with pytest.raises(ValueError):
+        be.generate_step([], {})
+    with pytest.raises(ValueError):
+        be.generate_step(list(range(65)), {})
+
+
+def test_backend_l1_interface(torch_ops):
+    """forward_step / generate with the reference L1Backend's signatures
+    (ccut/models/backend_transformers.py:75-124): greedy by default, stops at eos."""
+    from ccut_b200.backend import GenericBackend
+
+    m = torch_ops
+    t = make_tiny(24)
+    be = GenericBackend(_build(m, t), max_len=32)
+    prompt = [3, 1, 4, 1, 5]
+    out = be.generate(prompt, 4)
+    ids = list(prompt)
+    for _ in range(4):
+        ids.append(be.generate_step(ids, {"temperature": 0.0}))
+    assert out == ids[len(prompt):]
+    seen = []
+    be.eos_token_id = out[1]
+    assert be.generate(prompt, 4, on_token=seen.append) == out[:2] and seen == out[:2]
+    calls = []
+    be.eos_token_id = None
+    be.generate(prompt, 2, sampling=lambda lg, pos: calls.append((tuple(lg.shape), pos)) or 0)
+    assert calls == [((1, t.vocab), 0), ((1, t.vocab), 1)]
+    logits, past = be.forward_step(prompt)
+    assert logits.shape == (1, t.vocab) and past.length == len(prompt)

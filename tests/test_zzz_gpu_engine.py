@@ -1,0 +1,177 @@
+"""The decoder stack and the engine backend on the GPU (``ccut_b200.model``,
+``ccut_b200.backend``) against the oracle's decoder (``oracle.model``, pinned to the
+reference's own layer forward, ``ccut/models/generic.py:304-447``).
+
+The oracle runs with bf16 at the points where the GPU path stores bf16 and with the
+dequantized experts of the same AWQ / FP8 layers.  Its MoE blocks take the expert ids and
+weights that the GPU chose for the same call (recorded by ``_Recorded``), after checking that
+they are the oracle's own choice except where the oracle's k-th and (k+1)-th router logits lie
+within ``NEAR_TIE`` (the two sides' inputs differ by bf16 roundings, so a near tie may break
+either way, and a different expert changes that token's output outright).  Tolerance: max over
+positions of ``max|logits - ref| / max|ref|`` <= ``LOGITS_TOL``; the MoE layers alone are held to
+1e-2 by the kernel tests.  The caches are much longer than the positions in use, so the
+attention kernel clips every kv split to the causal range.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from ccut_b200 import dense
+from ccut_b200.backend import GenericBackend
+from ccut_b200.model import DecoderLayer, MoeDecoder, rope_table
+from oracle import inputs, moe, routing
+from oracle import model as omodel
+from tests.gpu_helpers import gpu_layer
+from tests.model_helpers import make_tiny, quantized_layers
+
+pytestmark = pytest.mark.gpu
+
+LOGITS_TOL = 3e-2
+NEAR_TIE = 5e-3
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from ccut_b200 import build
+    build.build()
+
+
+def _rel_rows(a, b) -> float:
+    a, b = np.atleast_2d(np.asarray(a, np.float64)), np.atleast_2d(np.asarray(b, np.float64))
+    return float((np.abs(a - b).max(axis=1) / np.maximum(np.abs(b).max(axis=1), 1e-30)).max())
+
+
+class _Recorded:
+    """A ``MoeLayer`` that keeps the routing of every call (ids int64, weights fp32)."""
+
+    def __init__(self, layer):
+        self.layer = layer
+        self.routes: list = []
+
+    def forward(self, x, out_dtype=torch.bfloat16):
+        out, r = self.layer.forward(x, out_dtype, return_routing=True)
+        self.routes.append((r.ids.cpu().numpy().astype(np.int64), r.weights.cpu().numpy()))
+        return out
+
+    def workspace_status(self) -> int:
+        return self.layer.workspace_status()
+
+
+def _oracle_moe(ol, top_k: int, mode: str, rec: _Recorded):
+    """Oracle MoE block on the GPU's routing of the same call (oldest recorded first)."""
+
+    def f(x):
+        ids, w = rec.routes.pop(0)
+        assert ids.shape == (x.shape[0], top_k)
+        lg = x @ ol.router.T
+        _, own = routing.route(lg, top_k, mode)
+        s = np.sort(lg, axis=1)[:, ::-1]
+        for t in range(x.shape[0]):
+            if set(ids[t].tolist()) != set(own[t].tolist()):
+                assert s[t, top_k - 1] - s[t, top_k] < NEAR_TIE, f"token {t}: {ids[t]} vs {own[t]}"
+        return moe.moe_forward(x, ol.router, top_k, mode, ol.w_lookup, ol.shared_cat(), ids=ids, weights=w)[0]
+
+    return f
+
+
+def _decoder(t, ffns):
+    layers = [DecoderLayer(w.ln1, w.wq, w.wk, w.wv, w.wo, w.ln2, f, w.q_norm, w.k_norm, heads=t.heads,
+                           kv_heads=t.kv_heads, head_dim=t.head_dim) for w, f in zip(t.attn, ffns)]
+    inv, attn = rope_table(t.head_dim, t.theta)
+    return MoeDecoder(t.embed, layers, t.final_norm, t.lm_head, inv_freq=inv, attention_factor=attn, eps=t.eps)
+
+
+def _moe_model(t, fmt: str, seed: int):
+    qlayers = quantized_layers(t, fmt, seed=seed)
+    recs = [_Recorded(gpu_layer(ol.lw)) for ol in qlayers]
+    offs = [_oracle_moe(ol, t.top_k, t.mode, r) for ol, r in zip(qlayers, recs)]
+    return _decoder(t, recs), recs, offs
+
+
+# fmt, kv_heads, qk_norm, head_dim, model seed, token seed
+CASES = [("fp8_b128", 2, "head", 64, 31, 5), ("awq_int4_g128", 1, "flat", 128, 32, 6)]
+
+
+@pytest.mark.parametrize("fmt, kv_heads, qk_norm, head_dim, seed, tseed", CASES)
+def test_decoder_matches_oracle(fmt, kv_heads, qk_norm, head_dim, seed, tseed):
+    """A 37-token prefill, four single-token steps and a 20-token chunk through two layers
+    (GQA or MQA attention, q / k norm per head or over the projection, a MoE block with a
+    shared expert): the logits of every position."""
+    t = make_tiny(seed, kv_heads=kv_heads, qk_norm=qk_norm, head_dim=head_dim)
+    dec, recs, offs = _moe_model(t, fmt, seed)
+    cache = dec.new_cache(1024)
+    spec, ocache = t.spec(), omodel.KvCache()
+    rng = np.random.default_rng(tseed)
+    pos = 0
+    for n in (37, 1, 1, 1, 1, 20):
+        toks = rng.integers(0, t.vocab, n)
+        got = dec.forward(toks, cache, all_logits=True)
+        torch.cuda.synchronize()
+        assert got.shape == (n, t.vocab) and got.dtype == torch.float32 and cache.length == pos + n
+        ref, _ = omodel.model_forward(toks, t.embed, t.attn, offs, t.final_norm, t.lm_head, spec, ocache, pos,
+                                      bf16_acts=True)
+        err = _rel_rows(got.cpu().numpy(), ref)
+        assert err <= LOGITS_TOL, (n, pos, err)
+        pos += n
+    assert all(not r.routes for r in recs)
+    for r in recs:
+        assert r.workspace_status() == 0
+
+
+def test_decoder_with_dense_layer():
+    """A dense FFN layer (``DenseFfn``, the expert kernels with one expert) before a MoE layer,
+    as in models whose first layers are dense."""
+    t = make_tiny(33, kv_heads=2, qk_norm=None)
+    qlayers = quantized_layers(t, "fp8_b128", seed=33)
+    dl = inputs.make_layer(inputs.scaled_config("cfg1", hidden=t.hidden, inter=256, num_experts=1, top_k=1,
+                                                num_shared=0), seed=34)
+    de = dl.experts[0]
+    dff = dense.DenseFfn("fp8_b128", t.hidden, 256, de.gate, de.up, de.down)
+    wg, wu, wd = dl.w_lookup(0)
+    rec = _Recorded(gpu_layer(qlayers[1].lw))
+    offs = [lambda x: moe.expert_ffn(x, wg, wu, wd), _oracle_moe(qlayers[1], t.top_k, t.mode, rec)]
+    dec = _decoder(t, [dff, rec])
+    cache, ocache = dec.new_cache(256), omodel.KvCache()
+    rng = np.random.default_rng(9)
+    pos = 0
+    for n in (12, 1, 1):
+        toks = rng.integers(0, t.vocab, n)
+        got = dec.forward(toks, cache, all_logits=True)
+        ref, _ = omodel.model_forward(toks, t.embed, t.attn, offs, t.final_norm, t.lm_head, t.spec(), ocache, pos,
+                                      bf16_acts=True)
+        assert _rel_rows(got.cpu().numpy(), ref) <= LOGITS_TOL
+        pos += n
+    assert dff.workspace_status() == 0
+
+
+def test_backend_generate_step():
+    """``generate_step`` as the reference's Engine calls it (the whole id list every step,
+    ``ccut/engine.py:305-333``): a 40-token prompt run in 16-token prefill chunks, then six
+    greedy steps that each run one new position.  Every step's logits equal a fresh prefill of
+    the same ids, the greedy token is their arg-max, and the logits of the final ids at every
+    position match the oracle."""
+    t = make_tiny(35, kv_heads=2, qk_norm="head")
+    dec, recs, offs = _moe_model(t, "fp8_b128", 35)
+    be = GenericBackend(dec, max_seqs=2, max_len=512, prefill_chunk=16)
+    ids = [int(x) for x in np.random.default_rng(11).integers(0, t.vocab, 40)]
+    for step in range(6):
+        got = be.logits_for(ids).cpu().numpy()
+        fresh = dec.forward(ids, dec.new_cache(512)).cpu().numpy()
+        assert _rel_rows(got, fresh) <= LOGITS_TOL, step
+        tok = be.generate_step(ids, {"temperature": 0.0})
+        assert got[tok] >= got.max() - 1e-3 * np.abs(got).max(), step
+        ids.append(tok)
+    assert be.tokens_run == 40 + 6 * 2 - 1  # the prompt once, then per step the newest id and a recompute
+    top5 = set(np.argsort(-be.logits_for(ids).cpu().numpy())[:5].tolist())
+    assert {be.generate_step(ids, {"temperature": 1.0, "top_k": 5}) for _ in range(8)} <= top5
+    for r in recs:
+        r.routes.clear()
+    full = dec.forward(ids, dec.new_cache(512), all_logits=True).cpu().numpy()
+    ref, _ = omodel.model_forward(ids, t.embed, t.attn, offs, t.final_norm, t.lm_head, t.spec(), omodel.KvCache(), 0,
+                                  bf16_acts=True)
+    assert _rel_rows(full, ref) <= LOGITS_TOL
