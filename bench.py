@@ -540,8 +540,6 @@ ATTN_WORKLOADS = {"cfg3_attn_decode": (64, 32, 4, 1, 4096, 128)}
 def run_attn(args, wl) -> None:
     """One GQA attention call per step (ccut_gqa_attention) on device-resident q / k / v;
     roofline: the K and V bytes read (the kv cache exceeds the L2)."""
-    import ctypes as C
-
     import torch
 
     from ccut_b200 import _lib, build

@@ -19,8 +19,6 @@ reference.
 
 from __future__ import annotations
 
-import ctypes as C
-
 import numpy as np
 import torch
 

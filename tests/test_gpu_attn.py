@@ -75,8 +75,6 @@ def test_gqa_matches_oracle(b, h, kvh, s, L, d, causal, softcap):
 
 
 def test_gqa_bf16_output_and_edges():
-    import ctypes as C
-
     from ccut_b200 import _lib
     from ccut_b200.blocks import attn_gqa
     from ccut_b200.layer import _ptr, _stream

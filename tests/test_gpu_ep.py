@@ -11,7 +11,6 @@ import ctypes as C
 import datetime
 import socket
 
-import numpy as np
 import pytest
 import torch
 

@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 import torch
 
-from oracle import formats, inputs, moe, routing
+from oracle import formats, inputs, routing
 from tests.gpu_helpers import (TOL, gpu_layer, ids_match_except_near_ties, oracle_forward, oracle_scores,
                                rel_err_rows, small_cfg, x_device)
 
