@@ -16,6 +16,10 @@ one token id back (errors evict that request).  ``GenericBackend`` answers that 
   (``ccut_b200.sampling.sample``: greedy at ``temperature <= 0``, else the reference's
   temperature / top-k / min-p / top-p transform and one draw from a seeded generator).
 
+``generate_batch([(input_ids, sampling_params), ...])`` answers a whole engine step at once
+(the loop of ``_backend_step`` as one call): the requests' new ids run through one decoder
+pass per prefill chunk, so their MoE blocks see all the step's tokens together.
+
 ``generate`` and ``forward_step`` give the interface of the reference's fallback backend
 (``L1Backend``, ``ccut/models/backend_transformers.py:31-124``), which the engine uses when a
 backend has no ``generate_step``: ``forward_step(input_ids, past)`` returns the logits of the
@@ -70,9 +74,12 @@ class GenericBackend:
         self.tokens_run = 0  # positions the decoder computed (prefix reuse skips the rest)
 
     # ---- sequence caches ---------------------------------------------------------------
-    def _acquire(self, ids: list[int]) -> tuple[_Seq, int]:
+    def _acquire(self, ids: list[int], taken: list) -> tuple[_Seq, int]:
+        """The cache to run ``ids`` in (not one of ``taken``) and how many of its positions stay."""
         best, best_p = None, 0
         for s in self._seqs:
+            if any(s is t for t in taken):
+                continue
             p = common_prefix(s.ids, ids)
             if p > best_p:
                 best, best_p = s, p
@@ -82,36 +89,65 @@ class GenericBackend:
             if len(self._seqs) < self.max_seqs:
                 best = _Seq(self.model.new_cache(self.max_len))
             else:
-                best = self._seqs[0]  # least recently used
-        if best in self._seqs:
+                free = [s for s in self._seqs if not any(s is t for t in taken)]
+                if not free:
+                    raise ValueError(f"a batch of more than max_seqs={self.max_seqs} sequences")
+                best = free[0]  # least recently used
+        if any(best is s for s in self._seqs):
             self._seqs.remove(best)
         self._seqs.append(best)
         return best, reuse
 
-    def _run(self, seq: _Seq, ids: list[int], start: int) -> torch.Tensor:
-        seq.cache.truncate(min(start, seq.cache.length))
-        seq.ids = ids[: seq.cache.length]
-        logits = None
-        for c0 in range(start, len(ids), self.prefill_chunk):
-            c1 = min(len(ids), c0 + self.prefill_chunk)
-            logits = self.model.forward(ids[c0:c1], seq.cache, c0)
-            seq.ids = ids[:c1]
-            self.tokens_run += c1 - c0
-        return logits
-
-    def logits_for(self, input_ids) -> torch.Tensor:
-        """fp32 logits ``[vocab]`` of the last of ``input_ids`` (runs what no cache holds)."""
+    def _check(self, input_ids) -> list[int]:
         ids = [int(t) for t in input_ids]
         if not ids:
             raise ValueError("generate_step needs at least one input id")
         if len(ids) > self.max_len:
             raise ValueError(f"{len(ids)} ids exceed the backend's max_len of {self.max_len}")
-        seq, reuse = self._acquire(ids)
-        return self._run(seq, ids, reuse)
+        return ids
+
+    def logits_batch(self, id_lists) -> list:
+        """fp32 logits ``[vocab]`` of the last id of every list, the lists run together: each
+        call of the decoder takes the next ``prefill_chunk`` ids (at most) of every list that
+        has ids left, so decoding sequences share their MoE passes."""
+        lists = [self._check(ids) for ids in id_lists]
+        seqs: list[_Seq] = []
+        pos: list[int] = []
+        for ids in lists:
+            seq, reuse = self._acquire(ids, seqs)
+            seq.cache.truncate(min(reuse, seq.cache.length))
+            seq.ids = ids[: seq.cache.length]
+            seqs.append(seq)
+            pos.append(reuse)
+        out: list = [None] * len(lists)
+        while True:
+            todo = [j for j in range(len(lists)) if pos[j] < len(lists[j])]
+            if not todo:
+                return out
+            ends = [min(len(lists[j]), pos[j] + self.prefill_chunk) for j in todo]
+            logits = self.model.forward_batch(
+                [(lists[j][pos[j]: e], seqs[j].cache, pos[j]) for j, e in zip(todo, ends)])
+            for j, e, lg in zip(todo, ends, logits):
+                self.tokens_run += e - pos[j]
+                seqs[j].ids = lists[j][:e]
+                pos[j] = e
+                if e == len(lists[j]):
+                    out[j] = lg
+
+    def logits_for(self, input_ids) -> torch.Tensor:
+        """fp32 logits ``[vocab]`` of the last of ``input_ids`` (runs what no cache holds)."""
+        return self.logits_batch([input_ids])[0]
 
     # ---- Engine interface ----------------------------------------------------------------
     def generate_step(self, input_ids, sampling_params: dict | None = None) -> int:
         return sample(self.logits_for(input_ids), sampling_params, self._gen)
+
+    def generate_batch(self, requests) -> list[int]:
+        """``requests`` = ``[(input_ids, sampling_params), ...]``, one per scheduled request of an
+        engine step (at most ``max_seqs``): the next token of each, from one batched pass."""
+        requests = list(requests)
+        logits = self.logits_batch([r[0] for r in requests])
+        return [sample(lg, r[1], self._gen) for lg, r in zip(logits, requests)]
 
     # ---- L1Backend interface -------------------------------------------------------------
     def forward_step(self, input_ids, past: Any = None) -> tuple[torch.Tensor, KvCache]:

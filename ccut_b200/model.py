@@ -21,7 +21,10 @@ each layer computes
 ====================================  ==================================================
 
 and the step ends with ``logits = rms_norm(h, final_norm) @ lm_head^T`` in fp32 (``lm_head``
-is kept as an fp32 copy).  Every block gets its documented layout; the reference's layer
+is kept as an fp32 copy).  ``forward_batch`` runs several sequences in one pass: their tokens
+are stacked for the projections, norms, RoPE (each token at its own position) and the FFN, so
+a MoE block reads its experts once for the whole batch; attention runs per sequence over its
+own cache.  Every block gets its documented layout; the reference's layer
 passes q as ``[1, seq, heads, d]`` to blocks that take ``[batch, heads, seq, d]``, which is
 the same computation for one token and one kv head only.
 
@@ -153,26 +156,44 @@ class DecoderLayer:
             return rms_norm(x.contiguous(), w, eps).reshape(seq, n, d)
         return rms_norm(x.reshape(seq, n, d).contiguous(), w, eps)
 
-    def forward(self, h: torch.Tensor, cache: KvCache, layer: int, start_pos: int, rope: "_Rope") -> torch.Tensor:
-        """h [seq, H] fp32 (the residual stream) -> [seq, H] fp32; writes the cache at
-        ``start_pos .. start_pos + seq - 1`` of ``layer``."""
-        seq = h.shape[0]
+    def forward(self, h: torch.Tensor, spans: list, layer: int, rope: "_Rope") -> torch.Tensor:
+        """h [N, H] fp32 (the residual stream of every span's tokens, one after the other) ->
+        [N, H] fp32.  Each ``_Span`` writes its sequence's cache at ``start .. start + n - 1`` of
+        ``layer`` and attends over it; the projections, norms, RoPE and the FFN run once over
+        all N tokens."""
+        N = h.shape[0]
         H, Hkv, d = self.heads, self.kv_heads, self.head_dim
         x = rms_norm(h, self.ln1, rope.eps).to(torch.bfloat16)
         qkv = F.linear(x, self.wqkv)
         q = self._qk_norm(qkv[:, : H * d], self.q_norm, H, rope.eps)
         k = self._qk_norm(qkv[:, H * d: (H + Hkv) * d], self.k_norm, Hkv, rope.eps)
-        v = qkv[:, (H + Hkv) * d:].reshape(seq, Hkv, d)
-        pos = torch.arange(start_pos, start_pos + seq, dtype=torch.int32, device=h.device).reshape(1, seq)
-        qr, kr = apply_rope(q.transpose(0, 1).unsqueeze(0), k.transpose(0, 1).unsqueeze(0), rope.inv_freq, pos,
-                            rope.attn_factor, rope.scaling_type)
+        vt = qkv[:, (H + Hkv) * d:].reshape(N, Hkv, d).transpose(0, 1)
+        if len(spans) == 1:
+            s = spans[0]
+            pos = torch.arange(s.start, s.start + s.n, dtype=torch.int32, device=h.device)
+        else:
+            pos = torch.cat([torch.arange(s.start, s.start + s.n, dtype=torch.int32) for s in spans]).to(h.device)
+        qr, kr = apply_rope(q.transpose(0, 1).unsqueeze(0), k.transpose(0, 1).unsqueeze(0), rope.inv_freq,
+                            pos.reshape(1, N), rope.attn_factor, rope.scaling_type)
         qr = qr.to(torch.bfloat16)
-        cache.k[layer, :, start_pos: start_pos + seq] = kr[0]
-        cache.v[layer, :, start_pos: start_pos + seq] = v.transpose(0, 1)
-        o = _attend(qr, cache.k[layer], cache.v[layer], start_pos, rope.softcap)
-        h = h + F.linear(o[0].transpose(0, 1).reshape(seq, H * d), self.wo).float()
+        outs = []
+        for s in spans:
+            s.cache.k[layer, :, s.start: s.start + s.n] = kr[0, :, s.off: s.off + s.n]
+            s.cache.v[layer, :, s.start: s.start + s.n] = vt[:, s.off: s.off + s.n]
+            qs = qr[:, :, s.off: s.off + s.n].contiguous()
+            outs.append(_attend(qs, s.cache.k[layer], s.cache.v[layer], s.start, rope.softcap))
+        o = outs[0] if len(outs) == 1 else torch.cat(outs, dim=2)
+        h = h + F.linear(o[0].transpose(0, 1).reshape(N, H * d), self.wo).float()
         x2 = rms_norm(h, self.ln2, rope.eps).to(torch.bfloat16)
         return h + self.ffn.forward(x2, out_dtype=torch.float32)
+
+
+class _Span:
+    """One sequence's part of a batch: ``n`` tokens at rows ``off ..`` of the batch, positions
+    ``start ..`` of ``cache``."""
+
+    def __init__(self, cache: KvCache, start: int, off: int, n: int):
+        self.cache, self.start, self.off, self.n = cache, start, off, n
 
 
 class _Rope:
@@ -217,28 +238,52 @@ class MoeDecoder:
         l0 = self.layers[0]
         return KvCache(len(self.layers), l0.kv_heads, max_len, l0.head_dim, self.device)
 
+    def _ids(self, tokens) -> torch.Tensor:
+        if isinstance(tokens, torch.Tensor):
+            return tokens.to(device=self.device, dtype=torch.int64).reshape(-1)
+        return torch.as_tensor(np.asarray(tokens, dtype=np.int64).reshape(-1)).to(self.device)
+
     def forward(self, tokens, cache: KvCache, start_pos: int | None = None, all_logits: bool = False) -> torch.Tensor:
         """Run ``tokens`` at positions ``start_pos ..`` (default: after the cached ones) and return
         the fp32 logits of the last token ``[vocab]`` (``all_logits``: of every token
         ``[seq, vocab]``).  Positions from ``start_pos`` on are replaced in ``cache``."""
-        if isinstance(tokens, torch.Tensor):
-            ids = tokens.to(device=self.device, dtype=torch.int64).reshape(-1)
-        else:
-            ids = torch.as_tensor(np.asarray(tokens, dtype=np.int64).reshape(-1)).to(self.device)
-        seq = ids.numel()
-        p = cache.length if start_pos is None else int(start_pos)
-        if seq == 0:
-            raise ValueError("no tokens to run")
-        if not 0 <= p <= cache.length:
-            raise ValueError(f"start position {p} is past the {cache.length} cached positions")
-        if p + seq > cache.max_len:
-            raise ValueError(f"{p} + {seq} positions do not fit the cache of {cache.max_len}")
+        return self.forward_batch([(tokens, cache, start_pos)], all_logits)[0]
+
+    def forward_batch(self, items: list, all_logits: bool = False) -> list:
+        """Several sequences in one pass: ``items`` = ``[(tokens, cache, start_pos or None), ...]``
+        with a different cache each.  The projections and the FFN run once over all tokens (the
+        MoE block sees every sequence's tokens together); attention runs per sequence over its
+        own cache.  Returns per item the logits of its last token ``[vocab]`` (``all_logits``:
+        ``[n, vocab]``)."""
+        if not items:
+            return []
+        spans, ids_all, off = [], [], 0
+        for tokens, cache, start_pos in items:
+            ids = self._ids(tokens)
+            n = ids.numel()
+            p = cache.length if start_pos is None else int(start_pos)
+            if n == 0:
+                raise ValueError("no tokens to run")
+            if not 0 <= p <= cache.length:
+                raise ValueError(f"start position {p} is past the {cache.length} cached positions")
+            if p + n > cache.max_len:
+                raise ValueError(f"{p} + {n} positions do not fit the cache of {cache.max_len}")
+            if any(s.cache is cache for s in spans):
+                raise ValueError("each sequence of a batch needs its own cache")
+            spans.append(_Span(cache, p, off, n))
+            ids_all.append(ids)
+            off += n
+        ids = ids_all[0] if len(ids_all) == 1 else torch.cat(ids_all)
         if int(ids.min()) < 0 or int(ids.max()) >= self.vocab:
             raise ValueError(f"token ids must be in [0, {self.vocab})")
         h = self.embed.index_select(0, ids).float()
         for i, lay in enumerate(self.layers):
-            h = lay.forward(h, cache, i, p, self.rope)
-        cache.length = p + seq
-        last = h if all_logits else h[-1:]
-        logits = F.linear(rms_norm(last, self.final_norm, self.rope.eps), self.lm_head)
-        return logits if all_logits else logits[0]
+            h = lay.forward(h, spans, i, self.rope)
+        for s in spans:
+            s.cache.length = s.start + s.n
+        if all_logits:
+            logits = F.linear(rms_norm(h, self.final_norm, self.rope.eps), self.lm_head)
+            return [logits[s.off: s.off + s.n] for s in spans]
+        last = torch.tensor([s.off + s.n - 1 for s in spans], dtype=torch.int64).to(self.device)
+        logits = F.linear(rms_norm(h.index_select(0, last), self.final_norm, self.rope.eps), self.lm_head)
+        return [logits[j] for j in range(len(spans))]

@@ -301,3 +301,61 @@ def test_backend_l1_interface(torch_ops):
     assert calls == [((1, t.vocab), 0), ((1, t.vocab), 1)]
     logits, past = be.forward_step(prompt)
     assert logits.shape == (1, t.vocab) and past.length == len(prompt)
+
+
+def test_decoder_batch_matches_single_sequences(torch_ops):
+    """forward_batch (one pass over several sequences, attention per sequence) against the same
+    sequences run one at a time."""
+    m = torch_ops
+    t = make_tiny(25, kv_heads=2, qk_norm="head")
+    dec = _build(m, t)
+    rng = np.random.default_rng(8)
+    prompts = [rng.integers(0, t.vocab, n) for n in (6, 1, 9)]
+    singles, caches = [], []
+    for p in prompts:
+        c = dec.new_cache(32)
+        singles.append(dec.forward(p, c, all_logits=True))
+        caches.append(c)
+    bcaches = [dec.new_cache(32) for _ in prompts]
+    got = dec.forward_batch([(p, c, None) for p, c in zip(prompts, bcaches)], all_logits=True)
+    for g, s in zip(got, singles):
+        assert g.shape == s.shape and _rel(g.numpy(), s.numpy()) < 5e-3
+    # one more token each, from different positions; last-token logits only
+    nxt = [[int(x)] for x in rng.integers(0, t.vocab, 3)]
+    got = dec.forward_batch([(n, c, None) for n, c in zip(nxt, bcaches)])
+    for n, c, g in zip(nxt, caches, got):
+        assert g.shape == (t.vocab,) and _rel(g.numpy(), dec.forward(n, c).numpy()) < 5e-3
+    assert [c.length for c in bcaches] == [7, 2, 10]
+    with pytest.raises(ValueError):
+        dec.forward_batch([([1], bcaches[0], None), ([2], bcaches[0], None)])  # one cache twice
+    assert dec.forward_batch([]) == []
+
+
+def test_backend_generate_batch(torch_ops):
+    """generate_batch (one engine step for several requests in one pass) picks the tokens that
+    generate_step picks for each request alone, runs each prompt once and then one position
+    per request per step."""
+    from ccut_b200.backend import GenericBackend
+
+    m = torch_ops
+    t = make_tiny(26)
+    dec = _build(m, t)
+    prompts = [[4, 8, 15, 16, 23, 42], [7, 7, 7], [1, 2, 3, 4, 5, 6, 7, 8, 9, 10]]
+    solo = GenericBackend(dec, max_seqs=1, max_len=32)
+    want = []
+    for p in prompts:
+        ids = list(p)
+        for _ in range(3):
+            ids.append(solo.generate_step(ids, {"temperature": 0.0}))
+        want.append(ids)
+    be = GenericBackend(dec, max_seqs=3, max_len=32, prefill_chunk=4)
+    seqs = [list(p) for p in prompts]
+    for step in range(3):
+        before = be.tokens_run
+        toks = be.generate_batch([(s, {"temperature": 0.0}) for s in seqs])
+        for s, tok in zip(seqs, toks):
+            s.append(tok)
+        assert be.tokens_run - before == (sum(map(len, prompts)) if step == 0 else 3)
+    assert seqs == want
+    with pytest.raises(ValueError):
+        be.generate_batch([([1], {}), ([2], {}), ([3], {}), ([4], {})])  # more than max_seqs

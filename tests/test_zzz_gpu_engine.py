@@ -175,3 +175,34 @@ def test_backend_generate_step():
     ref, _ = omodel.model_forward(ids, t.embed, t.attn, offs, t.final_norm, t.lm_head, t.spec(), omodel.KvCache(), 0,
                                   bf16_acts=True)
     assert _rel_rows(full, ref) <= LOGITS_TOL
+
+
+def test_backend_generate_batch():
+    """``generate_batch`` (one engine step for several requests in one decoder pass, their MoE
+    blocks sharing it): every request's logits against its own fresh prefill on the GPU, the
+    prompts run once and then one position per request, and the final sequences' logits at
+    every position against the oracle."""
+    t = make_tiny(36, kv_heads=2, qk_norm="head")
+    dec, recs, offs = _moe_model(t, "awq_int4_g128", 36)
+    be = GenericBackend(dec, max_seqs=3, max_len=256, prefill_chunk=32)
+    rng = np.random.default_rng(12)
+    seqs = [[int(x) for x in rng.integers(0, t.vocab, n)] for n in (21, 5, 40)]
+    for step in range(4):
+        before = be.tokens_run
+        logits = be.logits_batch(seqs)
+        assert be.tokens_run - before == (66 if step == 0 else 3)
+        for s, lg in zip(seqs, logits):
+            fresh = dec.forward(s, dec.new_cache(256)).cpu().numpy()
+            assert _rel_rows(lg.cpu().numpy(), fresh) <= LOGITS_TOL, step
+        toks = be.generate_batch([(s, {"temperature": 0.0}) for s in seqs])
+        for s, lg, tok in zip(seqs, logits, toks):
+            g = lg.cpu().numpy()
+            assert g[tok] >= g.max() - 1e-3 * np.abs(g).max(), step
+            s.append(tok)
+    for s in seqs:
+        for r in recs:
+            r.routes.clear()
+        full = dec.forward(s, dec.new_cache(256), all_logits=True).cpu().numpy()
+        ref, _ = omodel.model_forward(s, t.embed, t.attn, offs, t.final_norm, t.lm_head, t.spec(), omodel.KvCache(),
+                                      0, bf16_acts=True)
+        assert _rel_rows(full, ref) <= LOGITS_TOL
