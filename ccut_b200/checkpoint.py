@@ -48,6 +48,11 @@ __all__ = [
     "moe_spec_from_config",
     "load_layer_weights",
     "load_moe_layer",
+    "DecoderNames",
+    "DecoderCheckpointSpec",
+    "decoder_spec_from_config",
+    "load_decoder_weights",
+    "load_decoder",
 ]
 
 # safetensors dtype -> numpy dtype of the stored bytes (BF16 and FP8 stay as raw bits)
@@ -312,8 +317,10 @@ def load_layer_weights(model_dir: str | Path, layer: int, names: NameTemplates |
     """Host-side view of one MoE layer of a checkpoint: ``(spec, router fp32 [E, H],
     experts [{gate, up, down}], shared [{gate, up, down}] or [], bias fp32 [E] or None)``.
     Matrices are dicts of the checkpoint's tensors (read-only mmap views)."""
-    names = names or NameTemplates()
-    rd = CheckpointReader(model_dir)
+    return _layer_weights(CheckpointReader(model_dir), layer, names or NameTemplates())
+
+
+def _layer_weights(rd: CheckpointReader, layer: int, names: NameTemplates):
     spec = moe_spec_from_config(rd.config)
     rx = expert_pattern(names.expert)
     found: dict[int, set[str]] = {}
@@ -364,3 +371,201 @@ def load_moe_layer(model_dir: str | Path, layer: int, device="cuda", kernel: str
                     shared=shared or None, shared_inter=spec.shared_inter or None, n_group=spec.n_group,
                     topk_group=spec.topk_group, routed_scaling=spec.routed_scaling, bias=bias, kernel=kernel,
                     device=device)
+
+
+# ---------------------------------------------------------------- whole decoder
+@dataclass(frozen=True)
+class DecoderNames:
+    """Tensor names of a decoder checkpoint (``{layer}``; ``{proj}`` is q / k / v / o for the
+    attention projections, gate / up / down for a dense MLP).  The defaults are the Hugging
+    Face Qwen / Llama / DeepSeek names."""
+
+    embed: str = "model.embed_tokens.weight"
+    final_norm: str = "model.norm.weight"
+    lm_head: str = "lm_head.weight"
+    input_norm: str = "model.layers.{layer}.input_layernorm.weight"
+    post_norm: str = "model.layers.{layer}.post_attention_layernorm.weight"
+    attn: str = "model.layers.{layer}.self_attn.{proj}_proj"
+    q_norm: str = "model.layers.{layer}.self_attn.q_norm.weight"
+    k_norm: str = "model.layers.{layer}.self_attn.k_norm.weight"
+    mlp: str = "model.layers.{layer}.mlp.{proj}_proj"
+    moe: NameTemplates = NameTemplates()
+
+
+@dataclass(frozen=True)
+class DecoderCheckpointSpec:
+    fmt: str
+    vocab: int
+    hidden: int
+    layers: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    inter: int  # dense MLP intermediate size (0: none)
+    eps: float
+    rope_theta: float
+    rope_scaling: dict | None
+    tie_word_embeddings: bool
+    softcap: float | None
+    moe_layers: tuple  # per layer: True for a MoE block, False for a dense MLP
+
+
+def _is_moe_layer(tc: dict, i: int) -> bool:
+    """Whether layer ``i`` has a MoE block: the model has experts, ``i`` is not in
+    ``mlp_only_layers``, ``i >= first_k_dense_replace``, ``(i + 1) % decoder_sparse_step == 0``
+    and ``i % moe_layer_freq == 0`` (the Qwen-MoE and DeepSeek config keys; a model without
+    them has a MoE block in every layer, as the reference's layer forward assumes,
+    ``ccut/models/generic.py:440-446``)."""
+    if not int(tc.get("num_experts") or tc.get("n_routed_experts") or 0):
+        return False
+    if i in [int(v) for v in (tc.get("mlp_only_layers") or [])]:
+        return False
+    if i < int(tc.get("first_k_dense_replace", 0) or 0):
+        return False
+    if (i + 1) % max(1, int(tc.get("decoder_sparse_step", 1) or 1)):
+        return False
+    return i % max(1, int(tc.get("moe_layer_freq", 1) or 1)) == 0
+
+
+def decoder_spec_from_config(config: dict) -> DecoderCheckpointSpec:
+    """Decoder shape of a ``config.json`` (the keys ``ccut/models/spec.py:parse_model_spec``
+    reads).  MLA attention (``kv_lora_rank``) and linear-attention layers raise
+    ``NotImplementedError``: the decoder runs ``full_attn`` GQA layers."""
+    tc = config.get("text_config", config)
+    if tc.get("kv_lora_rank") or tc.get("q_lora_rank"):
+        raise NotImplementedError("MLA attention layers (kv_lora_rank) are not supported by the decoder")
+    if tc.get("linear_num_key_heads") or int(tc.get("full_attention_interval", 0) or 0) > 1:
+        raise NotImplementedError("linear-attention layers are not supported by the decoder")
+    for key in ("hidden_size", "num_hidden_layers", "num_attention_heads", "vocab_size"):
+        if key not in tc:
+            raise KeyError(f"config.json has no {key!r}")
+    hidden, heads = int(tc["hidden_size"]), int(tc["num_attention_heads"])
+    L = int(tc["num_hidden_layers"])
+    cap = tc.get("attn_logit_softcapping")
+    return DecoderCheckpointSpec(
+        fmt=quant_format(config), vocab=int(tc["vocab_size"]), hidden=hidden, layers=L, heads=heads,
+        kv_heads=int(tc.get("num_key_value_heads", heads)), head_dim=int(tc.get("head_dim") or hidden // heads),
+        inter=int(tc.get("intermediate_size", 0) or 0), eps=float(tc.get("rms_norm_eps", 1e-6)),
+        rope_theta=float(tc.get("rope_theta", 10000.0)), rope_scaling=tc.get("rope_scaling"),
+        tie_word_embeddings=bool(tc.get("tie_word_embeddings", False)), softcap=float(cap) if cap else None,
+        moe_layers=tuple(_is_moe_layer(tc, i) for i in range(L)),
+    )
+
+
+def _dense_or_quant(rd: CheckpointReader, prefix: str, fmt: str, out_dim: int, in_dim: int):
+    """``("dense", fp32 [out, in])`` for a float ``<prefix>.weight``, else ``("quant", tensors)``
+    in the checkpoint's format."""
+    name = f"{prefix}.weight"
+    if rd.has(name) and rd.dtype(name) in ("BF16", "F16", "F32"):
+        a = _float_tensor(rd, name)
+        if a.shape != (out_dim, in_dim):
+            raise ValueError(f"{name} has shape {a.shape}, expected {(out_dim, in_dim)}")
+        return "dense", a
+    m = _read_matrix(rd, prefix, fmt)
+    shape = m["qweight"].shape if fmt == "awq_int4_g128" else m["weight"].shape
+    want = (in_dim, out_dim // 8) if fmt == "awq_int4_g128" else (out_dim, in_dim)
+    if shape != want:
+        raise ValueError(f"{prefix} has shape {shape}, expected {want}")
+    return "quant", m
+
+
+def _vector(rd: CheckpointReader, name: str, n: int) -> np.ndarray:
+    if not rd.has(name):
+        raise KeyError(f"no tensor {name!r} in the checkpoint")
+    a = _float_tensor(rd, name).reshape(-1)
+    if a.size != n:
+        raise ValueError(f"{name} has {a.size} elements, expected {n}")
+    return a
+
+
+def load_decoder_weights(model_dir: str | Path, names: DecoderNames | None = None) -> dict:
+    """Host-side view of a decoder checkpoint: ``{"spec", "embed", "lm_head", "final_norm",
+    "layers"}``; each layer a dict with ``ln1``, ``ln2``, ``q`` / ``k`` / ``v`` / ``o``
+    (``("dense", [out, in])`` or ``("quant", tensors)``), ``q_norm`` / ``k_norm`` (or None) and
+    ``ffn``: ``("moe", load_layer_weights(...))`` or ``("dense", {gate, up, down})``.  Float
+    tensors are fp32 copies, quantized ones read-only views."""
+    names = names or DecoderNames()
+    rd = CheckpointReader(model_dir)
+    spec = decoder_spec_from_config(rd.config)
+    H, d = spec.hidden, spec.head_dim
+    embed = _float_tensor(rd, names.embed)
+    if embed.shape != (spec.vocab, H):
+        raise ValueError(f"{names.embed} has shape {embed.shape}, expected {(spec.vocab, H)}")
+    if rd.has(names.lm_head):
+        lm_head = _float_tensor(rd, names.lm_head)
+        if lm_head.shape != (spec.vocab, H):
+            raise ValueError(f"{names.lm_head} has shape {lm_head.shape}, expected {(spec.vocab, H)}")
+    elif spec.tie_word_embeddings:
+        lm_head = embed
+    else:
+        raise KeyError(f"no tensor {names.lm_head!r} and tie_word_embeddings is false")
+    dims = {"q": (spec.heads * d, H), "k": (spec.kv_heads * d, H), "v": (spec.kv_heads * d, H),
+            "o": (H, spec.heads * d)}
+    layers = []
+    for i in range(spec.layers):
+        lay = {"ln1": _vector(rd, names.input_norm.format(layer=i), H),
+               "ln2": _vector(rd, names.post_norm.format(layer=i), H)}
+        for p, (o, n) in dims.items():
+            lay[p] = _dense_or_quant(rd, names.attn.format(layer=i, proj=p), spec.fmt, o, n)
+        for p, n in (("q_norm", spec.heads), ("k_norm", spec.kv_heads)):
+            name = getattr(names, p).format(layer=i)
+            w = _float_tensor(rd, name).reshape(-1) if rd.has(name) else None
+            if w is not None and w.size not in (d, n * d):
+                raise ValueError(f"{name} has {w.size} elements, expected {d} or {n * d}")
+            lay[p] = w
+        if spec.moe_layers[i]:
+            lay["ffn"] = ("moe", _layer_weights(rd, i, names.moe))
+        else:
+            if spec.inter < 1:
+                raise ValueError(f"layer {i} has a dense MLP but config.json has no intermediate_size")
+            lay["ffn"] = ("dense", {p: _read_matrix(rd, names.mlp.format(layer=i, proj=p), spec.fmt)
+                                    for p in ("gate", "up", "down")})
+        layers.append(lay)
+    final_norm = _vector(rd, names.final_norm, H)
+    return {"spec": spec, "embed": embed, "lm_head": lm_head, "final_norm": final_norm, "layers": layers}
+
+
+def load_decoder(model_dir: str | Path, device="cuda", kernel: str = "auto", names: DecoderNames | None = None):
+    """``MoeDecoder`` of a whole checkpoint: every layer's MoE experts packed into HBM
+    (``MoeLayer``) or its dense MLP (``DenseFfn``); quantized attention projections are
+    dequantized on the device (``quant.dequantize``) and kept as bf16 for the cuBLAS
+    projections; RoPE from ``rope_theta`` / ``rope_scaling`` (none or linear; other scalings
+    raise ``NotImplementedError``: build the ``MoeDecoder`` with ``build_rope``'s table)."""
+    import torch
+
+    from ccut_b200.dense import DenseFfn
+    from ccut_b200.layer import MoeLayer
+    from ccut_b200.model import DecoderLayer, MoeDecoder, rope_table
+    from ccut_b200.quant import dequantize
+
+    w = load_decoder_weights(model_dir, names)
+    spec = w["spec"]
+    inv_freq, attn_factor = rope_table(spec.head_dim, spec.rope_theta, spec.rope_scaling)
+
+    def dense(m, out_dim: int, in_dim: int) -> torch.Tensor:
+        kind, a = m
+        if kind == "dense":
+            return torch.from_numpy(np.ascontiguousarray(a)).to(device=device, dtype=torch.bfloat16)
+        main = _SUFFIXES[spec.fmt][0]
+        t = dequantize(spec.fmt, a[main], {k: v for k, v in a.items() if k != main}, in_dim, out_dim, device)
+        return t.to(torch.bfloat16).contiguous()
+
+    H, d = spec.hidden, spec.head_dim
+    dims = {"q": (spec.heads * d, H), "k": (spec.kv_heads * d, H), "v": (spec.kv_heads * d, H),
+            "o": (H, spec.heads * d)}
+    layers = []
+    for lay in w["layers"]:
+        kind, f = lay["ffn"]
+        if kind == "moe":
+            ms, router, experts, shared, bias = f
+            ffn = MoeLayer(ms.fmt, ms.hidden, ms.inter, ms.num_experts, ms.top_k, ms.routing, router, experts,
+                           shared=shared or None, shared_inter=ms.shared_inter or None, n_group=ms.n_group,
+                           topk_group=ms.topk_group, routed_scaling=ms.routed_scaling, bias=bias, kernel=kernel,
+                           device=device)
+        else:
+            ffn = DenseFfn(spec.fmt, H, spec.inter, f["gate"], f["up"], f["down"], kernel=kernel, device=device)
+        q, k, v, o = (dense(lay[p], *dims[p]) for p in "qkvo")
+        layers.append(DecoderLayer(lay["ln1"], q, k, v, o, lay["ln2"], ffn, lay["q_norm"], lay["k_norm"],
+                                   heads=spec.heads, kv_heads=spec.kv_heads, head_dim=d, device=device))
+    return MoeDecoder(w["embed"], layers, w["final_norm"], w["lm_head"], inv_freq=inv_freq,
+                      attention_factor=attn_factor, eps=spec.eps, softcap=spec.softcap, device=device)

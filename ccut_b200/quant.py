@@ -25,7 +25,7 @@ import torch
 from ccut_b200 import _lib
 from ccut_b200.layer import _dev, _ptr, _stream
 
-__all__ = ["QuantizeMethodBase", "AwqInt4G128Method", "Fp8Block128Method", "make_method"]
+__all__ = ["QuantizeMethodBase", "AwqInt4G128Method", "Fp8Block128Method", "make_method", "dequantize"]
 
 
 class QuantizeMethodBase:
@@ -148,3 +148,17 @@ def make_method(fmt: str, in_features: int, out_features: int, **kw) -> Quantize
     if fmt == "fp8_b128":
         return Fp8Block128Method(in_features, out_features, **kw)
     raise NotImplementedError(f"weight format {fmt!r} is not supported")
+
+
+def dequantize(fmt: str, weight_bytes, scales: dict, in_features: int, out_features: int,
+               device="cuda") -> torch.Tensor:
+    """fp32 ``[out, in]`` of one checkpoint matrix (the tensors ``apply`` takes), on the device:
+    packed with ``ccut_pack_matrix``, exported with ``ccut_dequant_matrix`` (``(q - z) * s`` /
+    ``e4m3 * scale``, bit-identical to the checkpoint dequant)."""
+    m = make_method(fmt, in_features, out_features, layout="rows", device=device)
+    packed = m._pack(weight_bytes, scales)
+    out = torch.empty((m.K, m.N), dtype=torch.float32, device=m.device)
+    with torch.cuda.device(m.device):
+        _lib.call("ccut_dequant_matrix", m.code, _lib.LAYOUTS["rows"], _ptr(packed), m.K, m.N, 1, 0, _ptr(out),
+                  _stream())
+    return out.t()

@@ -104,3 +104,63 @@ def write_checkpoint(root: Path, lw, layer: int = 3, router_bf16: bool = False, 
     wm = {n: "model-00001-of-00002.safetensors" for n in t1} | {n: "model-00002-of-00002.safetensors" for n in t2}
     (root / "model.safetensors.index.json").write_text(json.dumps({"metadata": {}, "weight_map": wm}))
     return root
+
+
+def write_decoder_checkpoint(root: Path, tiny, fmt: str, qlayers: list, attn_mats: list | None = None,
+                             dense: dict | None = None, dense_inter: int = 0, tie: bool = False,
+                             drop: tuple[str, ...] = (), extra_config: dict | None = None) -> Path:
+    """A Qwen-MoE style decoder checkpoint of a ``tests.model_helpers`` tiny model: BF16
+    embedding, norms and ``lm_head``; attention projections BF16 from ``tiny.attn`` or the
+    quantized ``attn_mats``; per layer the MoE block of ``qlayers[i]`` (F32 router, experts,
+    the shared expert under ``shared_experts``), or for the layers of ``dense`` (layer ->
+    ``ExpertWeights`` with intermediate size ``dense_inter``) a dense MLP listed in
+    ``mlp_only_layers``."""
+    root.mkdir(parents=True, exist_ok=True)
+    bf = inputs.synthetic.bf16_bits_from_f32
+    dense = dense or {}
+    c0 = qlayers[0].cfg
+    q = ({"quant_method": "awq", "bits": 4, "group_size": 128, "zero_point": True, "version": "gemm"}
+         if fmt == "awq_int4_g128" else
+         {"quant_method": "fp8", "fmt": "e4m3", "weight_block_size": [128, 128], "activation_scheme": "dynamic"})
+    cfg = {"architectures": ["Qwen3MoeForCausalLM"], "model_type": "qwen3_moe", "hidden_size": tiny.hidden,
+           "num_hidden_layers": tiny.layers, "num_attention_heads": tiny.heads,
+           "num_key_value_heads": tiny.kv_heads, "head_dim": tiny.head_dim, "vocab_size": tiny.vocab,
+           "rms_norm_eps": tiny.eps, "rope_theta": tiny.theta, "rope_scaling": None, "tie_word_embeddings": tie,
+           "num_experts": c0.num_experts, "num_experts_per_tok": c0.top_k, "moe_intermediate_size": c0.inter,
+           "norm_topk_prob": c0.routing == "topk_softmax", "n_shared_experts": c0.num_shared,
+           "decoder_sparse_step": 1, "mlp_only_layers": sorted(dense), "intermediate_size": dense_inter,
+           "quantization_config": q}
+    cfg.update(extra_config or {})
+    (root / "config.json").write_text(json.dumps(cfg))
+    t = {"model.embed_tokens.weight": ("BF16", bf(tiny.embed)), "model.norm.weight": ("BF16", bf(tiny.final_norm))}
+    if not tie:
+        t["lm_head.weight"] = ("BF16", bf(tiny.lm_head))
+    for i, w in enumerate(tiny.attn):
+        pre = f"model.layers.{i}"
+        t[f"{pre}.input_layernorm.weight"] = ("BF16", bf(w.ln1))
+        t[f"{pre}.post_attention_layernorm.weight"] = ("BF16", bf(w.ln2))
+        for p, m in zip("qkvo", (w.wq, w.wk, w.wv, w.wo)):
+            if attn_mats is None:
+                t[f"{pre}.self_attn.{p}_proj.weight"] = ("BF16", bf(m))
+            else:
+                t.update(_matrix_tensors(f"{pre}.self_attn.{p}_proj", attn_mats[i][p]))
+        if w.q_norm is not None:
+            t[f"{pre}.self_attn.q_norm.weight"] = ("BF16", bf(w.q_norm))
+            t[f"{pre}.self_attn.k_norm.weight"] = ("BF16", bf(w.k_norm))
+        if i in dense:
+            for proj in ("gate", "up", "down"):
+                t.update(_matrix_tensors(f"{pre}.mlp.{proj}_proj", getattr(dense[i], proj)))
+            continue
+        lw = qlayers[i]
+        t[f"{pre}.mlp.gate.weight"] = (None, lw.router.astype(np.float32))
+        for e, ew in enumerate(lw.experts):
+            for proj in ("gate", "up", "down"):
+                t.update(_matrix_tensors(f"{pre}.mlp.experts.{e}.{proj}_proj", getattr(ew, proj)))
+        sh = merged_shared(lw.lw if hasattr(lw, "lw") else lw)
+        if sh:
+            for proj in ("gate", "up", "down"):
+                t.update(_matrix_tensors(f"{pre}.mlp.shared_experts.{proj}_proj", sh[proj]))
+    for name in drop:
+        t.pop(name, None)
+    write_safetensors(root / "model.safetensors", t, {"format": "pt"})
+    return root

@@ -117,3 +117,22 @@ def quantized_layers(tiny: TinyModel, fmt: str, seed: int = 1) -> list:
 
 def quantized_ffns(tiny: TinyModel, layers: list) -> list:
     return [model.moe_ffn(ol.router, tiny.top_k, tiny.mode, ol.w_lookup, ol.shared_cat()) for ol in layers]
+
+
+def quantized_attention(tiny: TinyModel, fmt: str, seed: int = 2):
+    """Seeded AWQ / FP8 attention projections of the tiny model's shape: per layer the
+    checkpoint matrices ``{q, k, v, o}`` and the ``AttnWeights`` whose projections are their
+    dequantized values rounded to bf16 (what the decoder keeps after loading)."""
+    from ccut_b200 import synthetic
+
+    rng = np.random.default_rng(seed)
+    d, H = tiny.head_dim, tiny.hidden
+    shapes = {"q": (H, tiny.heads * d), "k": (H, tiny.kv_heads * d), "v": (H, tiny.kv_heads * d),
+              "o": (tiny.heads * d, H)}  # (in, out)
+    mats, attn = [], []
+    for w in tiny.attn:
+        m = {p: synthetic._gen_matrix(rng, fmt, k, n) for p, (k, n) in shapes.items()}
+        deq = {p: _bf16(inputs.dequant(m[p]).T) for p in m}  # [out, in]
+        mats.append(m)
+        attn.append(AttnWeights(w.ln1, deq["q"], deq["k"], deq["v"], deq["o"], w.ln2, w.q_norm, w.k_norm))
+    return mats, attn

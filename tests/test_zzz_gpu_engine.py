@@ -15,17 +15,21 @@ attention kernel clips every kv split to the causal range.
 
 from __future__ import annotations
 
+import dataclasses
+
 import numpy as np
 import pytest
 import torch
 
 from ccut_b200 import dense
 from ccut_b200.backend import GenericBackend
+from ccut_b200.checkpoint import load_decoder
 from ccut_b200.model import DecoderLayer, MoeDecoder, rope_table
 from oracle import inputs, moe, routing
 from oracle import model as omodel
+from tests.ckpt_helpers import write_decoder_checkpoint
 from tests.gpu_helpers import gpu_layer
-from tests.model_helpers import make_tiny, quantized_layers
+from tests.model_helpers import make_tiny, quantized_attention, quantized_layers
 
 pytestmark = pytest.mark.gpu
 
@@ -206,3 +210,34 @@ def test_backend_generate_batch():
         ref, _ = omodel.model_forward(s, t.embed, t.attn, offs, t.final_norm, t.lm_head, t.spec(), omodel.KvCache(),
                                       0, bf16_acts=True)
         assert _rel_rows(full, ref) <= LOGITS_TOL
+
+
+@pytest.mark.parametrize("fmt", ["fp8_b128", "awq_int4_g128"])
+def test_load_decoder_matches_oracle(tmp_path, fmt):
+    """``load_decoder`` of a written checkpoint (quantized attention projections dequantized
+    on the device to bf16, MoE layers 0 and 2, a dense MLP in layer 1) against the oracle's
+    decoder over the same tensors: a 25-token prefill and two single-token steps."""
+    t = make_tiny(44, kv_heads=2, qk_norm="head", layers=3)
+    q = quantized_layers(t, fmt, seed=44)
+    mats, attn = quantized_attention(t, fmt, seed=45)
+    dl = inputs.make_layer(inputs.scaled_config("cfg1" if fmt == "fp8_b128" else "cfg0", hidden=t.hidden, inter=256,
+                                                num_experts=1, top_k=1, num_shared=0), seed=46)
+    root = write_decoder_checkpoint(tmp_path / "m", t, fmt, q, mats, dense={1: dl.experts[0]}, dense_inter=256)
+    dec = load_decoder(root)
+    recs = {}
+    for i in (0, 2):
+        dec.layers[i].ffn = recs[i] = _Recorded(dec.layers[i].ffn)
+    wg, wu, wd = dl.w_lookup(0)
+    offs = [_oracle_moe(q[0], t.top_k, t.mode, recs[0]), lambda x: moe.expert_ffn(x, wg, wu, wd),
+            _oracle_moe(q[2], t.top_k, t.mode, recs[2])]
+    tq = dataclasses.replace(t, attn=attn)
+    cache, ocache = dec.new_cache(128), omodel.KvCache()
+    rng = np.random.default_rng(14)
+    pos = 0
+    for n in (25, 1, 1):
+        toks = rng.integers(0, t.vocab, n)
+        got = dec.forward(toks, cache, all_logits=True)
+        ref, _ = omodel.model_forward(toks, tq.embed, tq.attn, offs, tq.final_norm, tq.lm_head, tq.spec(), ocache,
+                                      pos, bf16_acts=True)
+        assert _rel_rows(got.cpu().numpy(), ref) <= LOGITS_TOL, (n, pos)
+        pos += n
