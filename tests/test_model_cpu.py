@@ -359,3 +359,15 @@ def test_backend_generate_batch(torch_ops):
     assert seqs == want
     with pytest.raises(ValueError):
         be.generate_batch([([1], {}), ([2], {}), ([3], {}), ([4], {})])  # more than max_seqs
+
+
+def test_temperature_topk_constraints_like_reference():
+    """The property the reference's own test checks (tests/test_blocks.py,
+    test_temperature_topk_constraints): with top_k=5, top_p=0.9 and min_p=0.05 at most five
+    tokens keep probability and every row sums to one."""
+    from ccut_b200.sampling import temperature_topk
+
+    lg = np.random.default_rng(6).standard_normal((3, 100)).astype(np.float32)
+    p = temperature_topk(lg, 1.0, top_k=5, top_p=0.9, min_p=0.05)
+    assert ((p > 0).sum(axis=1) <= 5).all()
+    np.testing.assert_allclose(p.sum(axis=1), 1.0, atol=1e-5)
