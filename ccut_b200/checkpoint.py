@@ -525,27 +525,32 @@ def load_decoder_weights(model_dir: str | Path, names: DecoderNames | None = Non
     return {"spec": spec, "embed": embed, "lm_head": lm_head, "final_norm": final_norm, "layers": layers}
 
 
-def load_decoder(model_dir: str | Path, device="cuda", kernel: str = "auto", names: DecoderNames | None = None):
+def load_decoder(model_dir: str | Path, device="cuda", kernel: str = "auto", names: DecoderNames | None = None,
+                 quantized_projections: bool = True):
     """``MoeDecoder`` of a whole checkpoint: every layer's MoE experts packed into HBM
-    (``MoeLayer``) or its dense MLP (``DenseFfn``); quantized attention projections are
-    dequantized on the device (``quant.dequantize``) and kept as bf16 for the cuBLAS
-    projections; RoPE from ``rope_theta`` / ``rope_scaling`` (none or linear; other scalings
-    raise ``NotImplementedError``: build the ``MoeDecoder`` with ``build_rope``'s table)."""
+    (``MoeLayer``) or its dense MLP (``DenseFfn``).  Quantized attention projections stay in
+    their format (``quant.QuantLinear``, run by ``ccut_quant_linear``), or with
+    ``quantized_projections=False`` are dequantized on the device (``quant.dequantize``) and
+    kept as bf16 for cuBLAS.  RoPE from ``rope_theta`` / ``rope_scaling`` (none or linear;
+    other scalings raise ``NotImplementedError``: build the ``MoeDecoder`` with
+    ``build_rope``'s table)."""
     import torch
 
     from ccut_b200.dense import DenseFfn
     from ccut_b200.layer import MoeLayer
     from ccut_b200.model import DecoderLayer, MoeDecoder, rope_table
-    from ccut_b200.quant import dequantize
+    from ccut_b200.quant import QuantLinear, dequantize
 
     w = load_decoder_weights(model_dir, names)
     spec = w["spec"]
     inv_freq, attn_factor = rope_table(spec.head_dim, spec.rope_theta, spec.rope_scaling)
 
-    def dense(m, out_dim: int, in_dim: int) -> torch.Tensor:
+    def dense(m, out_dim: int, in_dim: int):
         kind, a = m
         if kind == "dense":
             return torch.from_numpy(np.ascontiguousarray(a)).to(device=device, dtype=torch.bfloat16)
+        if quantized_projections:
+            return QuantLinear(spec.fmt, a, in_dim, out_dim, device)
         main = _SUFFIXES[spec.fmt][0]
         t = dequantize(spec.fmt, a[main], {k: v for k, v in a.items() if k != main}, in_dim, out_dim, device)
         return t.to(torch.bfloat16).contiguous()

@@ -42,6 +42,7 @@ from ccut_b200 import _lib
 from ccut_b200.blocks.norm import rms_norm
 from ccut_b200.blocks.rope import apply_rope
 from ccut_b200.layer import _ptr, _stream
+from ccut_b200.quant import QuantLinear
 
 __all__ = ["DecoderLayer", "KvCache", "MoeDecoder", "rope_table"]
 
@@ -64,6 +65,22 @@ def rope_table(head_dim: int, rope_theta: float, rope_scaling: dict | None = Non
 def _tensor(a, dev: torch.device, dtype: torch.dtype) -> torch.Tensor:
     t = a if isinstance(a, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32))
     return t.to(device=dev, dtype=dtype).contiguous()
+
+
+def _is_projection(w) -> bool:
+    """A projection object: ``in_features``, ``out_features`` and ``__call__(x bf16 [M, in])``
+    returning ``[M, out]`` (``quant.QuantLinear``)."""
+    return callable(w) and hasattr(w, "in_features") and hasattr(w, "out_features")
+
+
+def _project(w, x: torch.Tensor) -> torch.Tensor:
+    """x bf16 [M, in] through a bf16 weight [out, in] (cuBLAS, bf16 out), a projection object
+    (its own output type), or a list of either (outputs side by side, fp32)."""
+    if isinstance(w, torch.Tensor):
+        return F.linear(x, w)
+    if isinstance(w, list):
+        return torch.cat([_project(p, x).float() for p in w], dim=1)
+    return w(x)
 
 
 class KvCache:
@@ -106,7 +123,9 @@ class DecoderLayer:
     """One ``full_attn`` decoder layer.
 
     ``ln1`` / ``ln2`` [H]; ``wq`` [heads * d, H], ``wk`` / ``wv`` [kv_heads * d, H], ``wo``
-    [H, heads * d] (checkpoint ``[out, in]`` layout, converted to bf16); ``q_norm`` / ``k_norm``
+    [H, heads * d] (checkpoint ``[out, in]`` layout, converted to bf16), or projection objects
+    of those shapes (``quant.QuantLinear``: kept in their AWQ / FP8 format and run by
+    ``ccut_quant_linear``; three of them for q / k / v are fused into one); ``q_norm`` / ``k_norm``
     None, ``[heads * d]`` / ``[kv_heads * d]`` (over the whole projection, the reference's
     ``rms_norm(q.reshape(seq, -1), w)``) or ``[d]`` (per head); ``ffn`` any object with
     ``forward(x_bf16 [T, H], out_dtype) -> [T, H]`` (``MoeLayer``, ``DenseFfn``)."""
@@ -126,13 +145,25 @@ class DecoderLayer:
                   "wo": (H, heads * head_dim)}
         mats = {}
         for name, m in zip(shapes, (wq, wk, wv, wo)):
+            if _is_projection(m):
+                if (m.out_features, m.in_features) != shapes[name]:
+                    raise ValueError(f"{name} must map {shapes[name][1]} to {shapes[name][0]} features, got "
+                                     f"{m.in_features} -> {m.out_features}")
+                mats[name] = m
+                continue
             t = _tensor(m, dev, torch.bfloat16)
             if tuple(t.shape) != shapes[name]:
                 raise ValueError(f"{name} must be {shapes[name]}, got {tuple(t.shape)}")
             mats[name] = t
         if self.ln2.numel() != H:
             raise ValueError("ln1 and ln2 must have the same size")
-        self.wqkv = torch.cat([mats["wq"], mats["wk"], mats["wv"]], 0).contiguous()
+        qkv = [mats["wq"], mats["wk"], mats["wv"]]
+        if all(isinstance(p, torch.Tensor) for p in qkv):
+            self.wqkv = torch.cat(qkv, 0).contiguous()
+        elif all(isinstance(p, QuantLinear) for p in qkv):
+            self.wqkv = QuantLinear.cat(qkv)
+        else:
+            self.wqkv = qkv
         self.wo = mats["wo"]
         self.q_norm = self._norm_w(q_norm, heads, dev, "q_norm")
         self.k_norm = self._norm_w(k_norm, kv_heads, dev, "k_norm")
@@ -148,7 +179,7 @@ class DecoderLayer:
         return t
 
     def _qk_norm(self, x: torch.Tensor, w, n: int, eps: float) -> torch.Tensor:
-        """x [seq, n * d] bf16 -> [seq, n, d] bf16."""
+        """x [seq, n * d] -> [seq, n, d], the same type (bf16, or fp32 from a quantized projection)."""
         seq, d = x.shape[0], self.head_dim
         if w is None:
             return x.reshape(seq, n, d)
@@ -164,7 +195,7 @@ class DecoderLayer:
         N = h.shape[0]
         H, Hkv, d = self.heads, self.kv_heads, self.head_dim
         x = rms_norm(h, self.ln1, rope.eps).to(torch.bfloat16)
-        qkv = F.linear(x, self.wqkv)
+        qkv = _project(self.wqkv, x)
         q = self._qk_norm(qkv[:, : H * d], self.q_norm, H, rope.eps)
         k = self._qk_norm(qkv[:, H * d: (H + Hkv) * d], self.k_norm, Hkv, rope.eps)
         vt = qkv[:, (H + Hkv) * d:].reshape(N, Hkv, d).transpose(0, 1)
@@ -183,7 +214,7 @@ class DecoderLayer:
             qs = qr[:, :, s.off: s.off + s.n].contiguous()
             outs.append(_attend(qs, s.cache.k[layer], s.cache.v[layer], s.start, rope.softcap))
         o = outs[0] if len(outs) == 1 else torch.cat(outs, dim=2)
-        h = h + F.linear(o[0].transpose(0, 1).reshape(N, H * d), self.wo).float()
+        h = h + _project(self.wo, o[0].transpose(0, 1).reshape(N, H * d)).float()
         x2 = rms_norm(h, self.ln2, rope.eps).to(torch.bfloat16)
         return h + self.ffn.forward(x2, out_dtype=torch.float32)
 

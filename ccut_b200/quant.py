@@ -25,7 +25,8 @@ import torch
 from ccut_b200 import _lib
 from ccut_b200.layer import _dev, _ptr, _stream
 
-__all__ = ["QuantizeMethodBase", "AwqInt4G128Method", "Fp8Block128Method", "make_method", "dequantize"]
+__all__ = ["QuantizeMethodBase", "AwqInt4G128Method", "Fp8Block128Method", "make_method", "dequantize",
+           "QuantLinear", "cat_checkpoint_tensors"]
 
 
 class QuantizeMethodBase:
@@ -162,3 +163,60 @@ def dequantize(fmt: str, weight_bytes, scales: dict, in_features: int, out_featu
         _lib.call("ccut_dequant_matrix", m.code, _lib.LAYOUTS["rows"], _ptr(packed), m.K, m.N, 1, 0, _ptr(out),
                   _stream())
     return out.t()
+
+
+# checkpoint tensor names of one matrix per format: the weight, then its scale tensors, with the
+# axis along which the output channels run in each
+_TENSORS = {"awq_int4_g128": (("qweight", 1), ("qzeros", 1), ("scales", 1)),
+            "fp8_b128": (("weight", 0), ("weight_scale_inv", 0))}
+
+
+class QuantLinear:
+    """A linear projection ``y = x @ W^T`` kept in its checkpoint format (``W`` [out, in]) and
+    run by ``ccut_quant_linear`` (fp32 out) -- a quarter (AWQ) or half (FP8) of the bytes of
+    a bf16 copy.  ``tensors``: the checkpoint tensors of the matrix (AWQ ``qweight`` /
+    ``qzeros`` / ``scales``; FP8 ``weight`` / ``weight_scale_inv`` or ``scale``).  The
+    weight is packed into the kernel layout once, at construction."""
+
+    def __init__(self, fmt: str, tensors: dict, in_features: int, out_features: int, device="cuda",
+                 layout: str = "frags"):
+        if fmt not in _TENSORS:
+            raise NotImplementedError(f"weight format {fmt!r} is not supported")
+        t = dict(tensors)
+        if fmt == "fp8_b128" and "weight_scale_inv" not in t and "scale" in t:
+            t["weight_scale_inv"] = t.pop("scale")
+        missing = [n for n, _ in _TENSORS[fmt] if n not in t]
+        if missing:
+            raise ValueError(f"missing checkpoint tensors {missing}")
+        self.fmt, self.in_features, self.out_features = fmt, int(in_features), int(out_features)
+        self.tensors = {n: t[n] for n, _ in _TENSORS[fmt]}
+        self.method = make_method(fmt, self.in_features, self.out_features, layout=layout, device=device)
+        main = _TENSORS[fmt][0][0]
+        self._weight = self.tensors[main]
+        self._scales = {n: v for n, v in self.tensors.items() if n != main}
+        self.method._pack(self._weight, self._scales)
+        self.device = self.method.device
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        """x [M, in] (bf16, or converted to bf16) -> fp32 [M, out]."""
+        return self.method.apply(self._weight, self._scales, x)
+
+    @classmethod
+    def cat(cls, parts: list) -> "QuantLinear":
+        """One projection whose outputs are those of ``parts`` side by side (same format and
+        input size): the checkpoint tensors concatenated along the output channels."""
+        p0 = parts[0]
+        if any(p.fmt != p0.fmt or p.in_features != p0.in_features for p in parts):
+            raise ValueError("projections to concatenate need the same format and input size")
+        return cls(p0.fmt, cat_checkpoint_tensors(p0.fmt, [p.tensors for p in parts]), p0.in_features,
+                   sum(p.out_features for p in parts), p0.device, p0.method.layout)
+
+
+def cat_checkpoint_tensors(fmt: str, parts: list) -> dict:
+    """The checkpoint tensors of one matrix whose output channels are those of ``parts`` (each
+    a dict of one matrix's tensors) in order: AWQ ``qweight`` / ``qzeros`` / ``scales`` side by
+    side along their last axis, FP8 ``weight`` / ``weight_scale_inv`` stacked along the first.
+    Each part's output channels must be a multiple of 128 (one FP8 scale block)."""
+    if fmt not in _TENSORS:
+        raise NotImplementedError(f"weight format {fmt!r} is not supported")
+    return {n: np.concatenate([np.asarray(p[n]) for p in parts], axis=ax) for n, ax in _TENSORS[fmt]}

@@ -119,10 +119,11 @@ def quantized_ffns(tiny: TinyModel, layers: list) -> list:
     return [model.moe_ffn(ol.router, tiny.top_k, tiny.mode, ol.w_lookup, ol.shared_cat()) for ol in layers]
 
 
-def quantized_attention(tiny: TinyModel, fmt: str, seed: int = 2):
+def quantized_attention(tiny: TinyModel, fmt: str, seed: int = 2, bf16: bool = True):
     """Seeded AWQ / FP8 attention projections of the tiny model's shape: per layer the
     checkpoint matrices ``{q, k, v, o}`` and the ``AttnWeights`` whose projections are their
-    dequantized values rounded to bf16 (what the decoder keeps after loading)."""
+    dequantized values, rounded to bf16 (what the decoder keeps when it dequantizes them at
+    load) or exact (``bf16=False``: the quantized projections it runs as they are)."""
     from ccut_b200 import synthetic
 
     rng = np.random.default_rng(seed)
@@ -132,7 +133,9 @@ def quantized_attention(tiny: TinyModel, fmt: str, seed: int = 2):
     mats, attn = [], []
     for w in tiny.attn:
         m = {p: synthetic._gen_matrix(rng, fmt, k, n) for p, (k, n) in shapes.items()}
-        deq = {p: _bf16(inputs.dequant(m[p]).T) for p in m}  # [out, in]
+        deq = {p: inputs.dequant(m[p]).T.copy() for p in m}  # [out, in]
+        if bf16:
+            deq = {p: _bf16(v) for p, v in deq.items()}
         mats.append(m)
         attn.append(AttnWeights(w.ln1, deq["q"], deq["k"], deq["v"], deq["o"], w.ln2, w.q_norm, w.k_norm))
     return mats, attn

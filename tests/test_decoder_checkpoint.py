@@ -87,3 +87,26 @@ def test_load_decoder_weights(tmp_path, fmt, quant_attn):
     (root / "config.json").write_text(json.dumps(cfg | {"intermediate_size": 0}))
     with pytest.raises(ValueError):
         ck.load_decoder_weights(root)
+
+
+@pytest.mark.parametrize("fmt", ["awq_int4_g128", "fp8_b128"])
+def test_cat_checkpoint_tensors(fmt):
+    """Fusing the q / k / v projections: the concatenated checkpoint tensors dequantize to the
+    three matrices side by side (the oracle's dequant)."""
+    from ccut_b200.quant import cat_checkpoint_tensors
+    from ccut_b200.synthetic import _gen_matrix
+
+    rng = np.random.default_rng(3)
+    mats = [_gen_matrix(rng, fmt, 256, n) for n in (256, 128, 128)]  # [in, out] shapes 256 -> n
+    if fmt == "awq_int4_g128":
+        dicts = [{"qweight": m.qweight, "qzeros": m.qzeros, "scales": m.scales} for m in mats]
+        t = cat_checkpoint_tensors(fmt, dicts)
+        fused = inputs.AwqMatrix(t["qweight"], t["qzeros"], t["scales"])
+    else:
+        dicts = [{"weight": m.weight, "weight_scale_inv": m.scale} for m in mats]
+        t = cat_checkpoint_tensors(fmt, dicts)
+        fused = inputs.Fp8Matrix(t["weight"], t["weight_scale_inv"])
+    want = np.concatenate([inputs.dequant(m) for m in mats], axis=1)  # [in, sum(out)]
+    assert np.array_equal(inputs.dequant(fused), want)
+    with pytest.raises(NotImplementedError):
+        cat_checkpoint_tensors("int8", dicts)

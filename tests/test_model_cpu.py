@@ -371,3 +371,46 @@ def test_temperature_topk_constraints_like_reference():
     p = temperature_topk(lg, 1.0, top_k=5, top_p=0.9, min_p=0.05)
     assert ((p > 0).sum(axis=1) <= 5).all()
     np.testing.assert_allclose(p.sum(axis=1), 1.0, atol=1e-5)
+
+
+class _TorchProj:
+    """A projection object ([out, in] weight, fp32 out), as ``quant.QuantLinear`` is one."""
+
+    def __init__(self, w):
+        self.w = torch.from_numpy(np.ascontiguousarray(w, np.float32))
+        self.out_features, self.in_features = self.w.shape
+
+    def __call__(self, x):
+        return x.float() @ self.w.T
+
+
+@pytest.mark.parametrize("which", ["all", "kv_only"])
+def test_decoder_with_projection_objects(torch_ops, which):
+    """Projections given as objects (fp32 outputs, as the quantized ones give): all four, or
+    k / v only next to bf16 q / o weights (the mixed q / k / v path)."""
+    m = torch_ops
+    t = make_tiny(27, kv_heads=2, qk_norm="head")
+    layers = []
+    for i, w in enumerate(t.attn):
+        wq, wk, wv, wo = w.wq, _TorchProj(w.wk), _TorchProj(w.wv), w.wo
+        if which == "all":
+            wq, wo = _TorchProj(w.wq), _TorchProj(w.wo)
+        layers.append(m.DecoderLayer(w.ln1, wq, wk, wv, wo, w.ln2, _TorchMoe(t, i), w.q_norm, w.k_norm,
+                                     heads=t.heads, kv_heads=t.kv_heads, head_dim=t.head_dim, device="cpu"))
+    inv, attn = m.rope_table(t.head_dim, t.theta)
+    dec = m.MoeDecoder(t.embed, layers, t.final_norm, t.lm_head, inv_freq=inv, attention_factor=attn, eps=t.eps,
+                       device="cpu")
+    cache, ocache = dec.new_cache(16), omodel.KvCache()
+    rng = np.random.default_rng(4)
+    pos = 0
+    for n in (6, 1, 2):
+        toks = rng.integers(0, t.vocab, n)
+        got = dec.forward(toks, cache, all_logits=True)
+        ref, _ = omodel.model_forward(toks, t.embed, t.attn, t.dense_ffns(), t.final_norm, t.lm_head, t.spec(),
+                                      ocache, pos, bf16_acts=True)
+        assert _rel(got.numpy(), ref) < 1e-2
+        pos += n
+    with pytest.raises(ValueError):  # a projection object of the wrong shape
+        w = t.attn[0]
+        m.DecoderLayer(w.ln1, _TorchProj(w.wk), w.wk, w.wv, w.wo, w.ln2, None, heads=t.heads, kv_heads=t.kv_heads,
+                       head_dim=t.head_dim, device="cpu")

@@ -212,18 +212,20 @@ def test_backend_generate_batch():
         assert _rel_rows(full, ref) <= LOGITS_TOL
 
 
-@pytest.mark.parametrize("fmt", ["fp8_b128", "awq_int4_g128"])
-def test_load_decoder_matches_oracle(tmp_path, fmt):
+@pytest.mark.parametrize("fmt, keep_quantized", [("fp8_b128", False), ("awq_int4_g128", False),
+                                                 ("fp8_b128", True), ("awq_int4_g128", True)])
+def test_load_decoder_matches_oracle(tmp_path, fmt, keep_quantized):
     """``load_decoder`` of a written checkpoint (quantized attention projections dequantized
-    on the device to bf16, MoE layers 0 and 2, a dense MLP in layer 1) against the oracle's
-    decoder over the same tensors: a 25-token prefill and two single-token steps."""
+    on the device to bf16, or kept quantized and run by ``ccut_quant_linear``; MoE layers 0
+    and 2, a dense MLP in layer 1) against the oracle's decoder over the same tensors: a
+    25-token prefill and two single-token steps."""
     t = make_tiny(44, kv_heads=2, qk_norm="head", layers=3)
     q = quantized_layers(t, fmt, seed=44)
-    mats, attn = quantized_attention(t, fmt, seed=45)
+    mats, attn = quantized_attention(t, fmt, seed=45, bf16=not keep_quantized)
     dl = inputs.make_layer(inputs.scaled_config("cfg1" if fmt == "fp8_b128" else "cfg0", hidden=t.hidden, inter=256,
                                                 num_experts=1, top_k=1, num_shared=0), seed=46)
     root = write_decoder_checkpoint(tmp_path / "m", t, fmt, q, mats, dense={1: dl.experts[0]}, dense_inter=256)
-    dec = load_decoder(root)
+    dec = load_decoder(root, quantized_projections=keep_quantized)
     recs = {}
     for i in (0, 2):
         dec.layers[i].ffn = recs[i] = _Recorded(dec.layers[i].ffn)
