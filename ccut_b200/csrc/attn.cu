@@ -315,7 +315,236 @@ __global__ void __launch_bounds__(256) gqa_combine_kernel(const float* __restric
   }
 }
 
-// RMSNorm of one row per CTA (128 threads, dim % 8 == 0).
+// ---- MLA in the latent space (DeepSeek-V2 / V3, the absorbed form) -----------------------
+// q [B, S*H, 576] fp32, row r = s * H + h: q_nope of head h folded through k_up (512 latent
+// features), then the rotated q_pe (64).  kv [B, L, 576] bf16, one row per position: the
+// latent c (512), then the rotated k_pe (64).  out o_lat [B, S*H, 512] =
+// softmax(q . kv^T * scale, causal) @ kv[:, :512].  This is ccut/blocks/attn_mla.py:85-167
+// (mla_decode / mla_prefill) with the up-projections outside the kernel: the scores
+// (c k_up_h) . q_nope + k_pe . q_pe equal (q_nope k_up_h^T) . c + q_pe . k_pe, and the output
+// probs @ (c v_up_h) equals (probs @ c) v_up_h.
+//
+// Work: a CTA takes 16 query rows and one split of the kv range of one sequence; every row
+// of the CTA reads the same latent rows, so each position's 1152 bytes are read once per
+// (sequence, split).  Per 16-position tile, staged through a three-deep cp.async ring
+// shared by the CTA, the four warps split both products along the features: warp w computes
+// S over key features [144 w, 144 w + 144) (q split into bf16 hi + lo parts, so that q keeps
+// ~16 bits), the four partial S tiles are summed in warp order through shared memory (every
+// warp then holds the same S and runs the same online softmax), and warp w accumulates
+// O += P V for value features [128 w, 128 w + 128) (P split into hi + lo as in the GQA
+// kernel).  Splits are merged by gqa_combine_kernel<512>.
+constexpr int kMlaR = 512, kMlaP = 64, kMlaK = kMlaR + kMlaP;  // latent rank, rope features, key width
+constexpr int kMlaWarps = 4;
+constexpr int kMlaKS = kMlaK / kMlaWarps / 16;  // k16 steps of S per warp (9)
+constexpr int kMlaVW = kMlaR / kMlaWarps;       // value features per warp (128)
+constexpr int kMlaTile = 16;                    // kv positions per staged tile
+constexpr int kMlaStages = 3;
+constexpr int kMlaRow = kMlaK + 8;  // padded shared-memory row (elements): conflict-free ldmatrix
+
+struct MlaSmem {
+  static constexpr int kQElems = kTcRows * kMlaRow;     // one of the q hi / lo planes
+  static constexpr int kTileElems = kMlaTile * kMlaRow;  // one ring stage
+  static constexpr size_t kRedBytes = (size_t)kMlaWarps * 32 * 8 * sizeof(float);  // partial S fragments
+  static constexpr size_t kBytes = (size_t)(2 * kQElems + kMlaStages * kTileElems) * 2 + kRedBytes;
+  static_assert((kMlaRow * 2) % 16 == 0 && (kQElems * 2) % 16 == 0 && (kTileElems * 2) % 16 == 0, "16-byte rows");
+  static_assert(kMlaKS * 16 * kMlaWarps == kMlaK && kMlaVW % 16 == 0, "feature split");
+};
+
+template <bool OUT_BF16>
+__global__ void __launch_bounds__(kMlaWarps * 32) mla_attn_kernel(
+    const float* __restrict__ q, const uint16_t* __restrict__ kv, int H, int S, int L, int causal_start, float scale,
+    int splits, int tiles_per_split, void* __restrict__ out, float* __restrict__ part) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ __align__(128) uint8_t mla_smem[];
+  uint16_t* qhi = reinterpret_cast<uint16_t*>(mla_smem);
+  uint16_t* qlo = qhi + MlaSmem::kQElems;
+  uint16_t* ring = qlo + MlaSmem::kQElems;
+  float* red = reinterpret_cast<float*>(ring + kMlaStages * MlaSmem::kTileElems);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int nrows = S * H;
+  const int b = blockIdx.y, r0 = blockIdx.x * kTcRows, split = blockIdx.z;
+  const int k0 = split * tiles_per_split * kMlaTile;
+  int k1 = min(L, k0 + tiles_per_split * kMlaTile);
+  if (causal_start >= 0) {  // the CTA's last row sees up to causal_start + s_last
+    const int r_last = min(nrows, r0 + kTcRows) - 1;
+    k1 = min(k1, causal_start + r_last / H + 1);
+  }
+  const int ntiles = k1 > k0 ? (k1 - k0 + kMlaTile - 1) / kMlaTile : 0;
+  const uint16_t* kvg = kv + (size_t)b * L * kMlaK;
+  auto issue = [&](int tile) {  // tile -> ring stage tile % kMlaStages, zero-filled past k1
+    const int p0 = k0 + tile * kMlaTile;
+    uint16_t* dst = ring + (tile % kMlaStages) * MlaSmem::kTileElems;
+    for (int c = threadIdx.x; c < kMlaTile * (kMlaK / 8); c += blockDim.x) {
+      const int pr = c / (kMlaK / 8), dc = (c % (kMlaK / 8)) * 8, pos = p0 + pr;
+      const bool ok = pos < k1;
+      cp_async16(dst + pr * kMlaRow + dc, kvg + (size_t)(ok ? pos : 0) * kMlaK + dc, ok);
+    }
+  };
+#pragma unroll
+  for (int st = 0; st < kMlaStages - 1; ++st) {
+    if (st < ntiles) issue(st);
+    cp_async_commit();
+  }
+  // the CTA's 16 query rows -> bf16 hi / lo planes in shared memory (zero rows past the end)
+  for (int c = threadIdx.x; c < kTcRows * (kMlaK / 4); c += blockDim.x) {
+    const int rr = c / (kMlaK / 4), dc = (c % (kMlaK / 4)) * 4, r = r0 + rr;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (r < nrows) v = *reinterpret_cast<const float4*>(q + ((size_t)b * nrows + r) * kMlaK + dc);
+    uint32_t h0, l0, h1, l1;
+    split_bf16x2(v.x, v.y, h0, l0);
+    split_bf16x2(v.z, v.w, h1, l1);
+    *reinterpret_cast<uint2*>(qhi + rr * kMlaRow + dc) = make_uint2(h0, h1);
+    *reinterpret_cast<uint2*>(qlo + rr * kMlaRow + dc) = make_uint2(l0, l1);
+  }
+  __syncthreads();
+  uint32_t qah[kMlaKS][4], qal[kMlaKS][4];
+#pragma unroll
+  for (int kk = 0; kk < kMlaKS; ++kk) {
+    const int off = ((lane & 7) + ((lane >> 3) & 1) * 8) * kMlaRow + (warp * kMlaKS + kk) * 16 + (lane >> 4) * 8;
+    ldmatrix_x4(qah[kk][0], qah[kk][1], qah[kk][2], qah[kk][3], qhi + off);
+    ldmatrix_x4(qal[kk][0], qal[kk][1], qal[kk][2], qal[kk][3], qlo + off);
+  }
+  int lim[2];  // last visible kv position of rows g and g + 8
+#pragma unroll
+  for (int i = 0; i < 2; ++i) lim[i] = causal_start >= 0 ? causal_start + (r0 + g + 8 * i) / H : L - 1;
+
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+  float o[kMlaVW / 8][4];
+#pragma unroll
+  for (int dn = 0; dn < kMlaVW / 8; ++dn)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[dn][i] = 0.f;
+  for (int jt = 0; jt < ntiles; ++jt) {
+    cp_async_wait<kMlaStages - 2>();  // this thread's copies of tile jt have landed
+    __syncthreads();                  // everyone's have; every warp is done with tile jt - 1
+    if (jt + kMlaStages - 1 < ntiles) issue(jt + kMlaStages - 1);  // into the stage of tile jt - 1
+    cp_async_commit();
+    const uint16_t* kd = ring + (jt % kMlaStages) * MlaSmem::kTileElems;
+    // partial S = Q K^T over this warp's key features (two n8 tiles of positions)
+    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int kk = 0; kk < kMlaKS; ++kk) {
+      const int mi = lane >> 3;
+      uint32_t b0, b1, b2, b3;
+      ldmatrix_x4(b0, b1, b2, b3,
+                  kd + ((mi >> 1) * 8 + (lane & 7)) * kMlaRow + (warp * kMlaKS + kk) * 16 + (mi & 1) * 8);
+      mma_16816<true>(sc[0], qah[kk], b0, b1);
+      mma_16816<true>(sc[0], qal[kk], b0, b1);
+      mma_16816<true>(sc[1], qah[kk], b2, b3);
+      mma_16816<true>(sc[1], qal[kk], b2, b3);
+    }
+    // S = the four partial tiles, summed in warp order (the same fragment slots in every warp)
+    float* mine = red + (warp * 32 + lane) * 8;
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) mine[n * 4 + i] = sc[n][i];
+    __syncthreads();
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float s = 0.f;
+#pragma unroll
+        for (int w = 0; w < kMlaWarps; ++w) s += red[(w * 32 + lane) * 8 + n * 4 + i];
+        sc[n][i] = s;
+      }
+    // scale, mask; element (n, i): row g + 8 (i >> 1), position p0 + 8 n + 2 t + (i & 1)
+    const int p0 = k0 + jt * kMlaTile;
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float x = sc[n][i] * scale;
+        const int pos = p0 + 8 * n + 2 * t + (i & 1);
+        if (pos >= k1 || pos > lim[i >> 1]) x = -INFINITY;
+        sc[n][i] = x;
+        mx[i >> 1] = fmaxf(mx[i >> 1], x);
+      }
+    float mnew[2], alpha[2], rs[2] = {0.f, 0.f};
+#pragma unroll
+    for (int ri = 0; ri < 2; ++ri) {
+      mx[ri] = fmaxf(mx[ri], __shfl_xor_sync(0xffffffffu, mx[ri], 1));
+      mx[ri] = fmaxf(mx[ri], __shfl_xor_sync(0xffffffffu, mx[ri], 2));
+      mnew[ri] = fmaxf(m[ri], mx[ri]);
+      alpha[ri] = mnew[ri] == -INFINITY ? 1.f : expf(m[ri] - mnew[ri]);
+    }
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int ri = i >> 1;
+        const float p = mnew[ri] == -INFINITY ? 0.f : expf(sc[n][i] - mnew[ri]);
+        sc[n][i] = p;
+        rs[ri] += p;
+      }
+#pragma unroll
+    for (int ri = 0; ri < 2; ++ri) {
+      rs[ri] += __shfl_xor_sync(0xffffffffu, rs[ri], 1);
+      rs[ri] += __shfl_xor_sync(0xffffffffu, rs[ri], 2);
+      l[ri] = l[ri] * alpha[ri] + rs[ri];
+      m[ri] = mnew[ri];
+    }
+#pragma unroll
+    for (int dn = 0; dn < kMlaVW / 8; ++dn) {
+      o[dn][0] *= alpha[0];
+      o[dn][1] *= alpha[0];
+      o[dn][2] *= alpha[1];
+      o[dn][3] *= alpha[1];
+    }
+    uint32_t ph[4], pl[4];
+    split_bf16x2(sc[0][0], sc[0][1], ph[0], pl[0]);
+    split_bf16x2(sc[0][2], sc[0][3], ph[1], pl[1]);
+    split_bf16x2(sc[1][0], sc[1][1], ph[2], pl[2]);
+    split_bf16x2(sc[1][2], sc[1][3], ph[3], pl[3]);
+    // O += P V over this warp's value features (the latent part of the staged rows)
+#pragma unroll
+    for (int dp = 0; dp < kMlaVW / 16; ++dp) {
+      const int mi = lane >> 3;
+      uint32_t b0, b1, b2, b3;
+      ldmatrix_x4_trans(b0, b1, b2, b3,
+                        kd + ((mi & 1) * 8 + (lane & 7)) * kMlaRow + warp * kMlaVW + dp * 16 + (mi >> 1) * 8);
+      mma_16816<true>(o[2 * dp], ph, b0, b1);
+      mma_16816<true>(o[2 * dp], pl, b0, b1);
+      mma_16816<true>(o[2 * dp + 1], ph, b2, b3);
+      mma_16816<true>(o[2 * dp + 1], pl, b2, b3);
+    }
+  }
+  // every warp holds the same (m, l) and its own 128 output features of rows g and g + 8
+  const size_t rows_total = (size_t)gridDim.y * nrows;  // B * S * H
+#pragma unroll
+  for (int hi = 0; hi < 2; ++hi) {
+    const int r = r0 + g + 8 * hi;
+    if (r >= nrows) continue;
+    const size_t orow = (size_t)b * nrows + r;
+    const float inv = 1.f / fmaxf(l[hi], 1e-30f);
+    float* p = splits > 1 ? part + ((size_t)split * rows_total + orow) * (kMlaR + 2) : nullptr;
+    if (p && warp == 0 && t == 0) {
+      p[0] = m[hi];
+      p[1] = l[hi];
+    }
+#pragma unroll
+    for (int dn = 0; dn < kMlaVW / 8; ++dn) {
+      const int f = warp * kMlaVW + dn * 8 + 2 * t;
+      const float v0 = o[dn][2 * hi], v1 = o[dn][2 * hi + 1];
+      if (p) {
+        p[2 + f] = v0;
+        p[3 + f] = v1;
+      } else if constexpr (OUT_BF16) {
+        static_cast<__nv_bfloat16*>(out)[orow * kMlaR + f] = __float2bfloat16_rn(v0 * inv);
+        static_cast<__nv_bfloat16*>(out)[orow * kMlaR + f + 1] = __float2bfloat16_rn(v1 * inv);
+      } else {
+        static_cast<float*>(out)[orow * kMlaR + f] = v0 * inv;
+        static_cast<float*>(out)[orow * kMlaR + f + 1] = v1 * inv;
+      }
+    }
+  }
+}
+
+// RMSNorm of one row per CTA (128 threads, any dim).
 template <bool IN_BF16, bool OUT_BF16>
 __global__ void __launch_bounds__(128) rms_norm_kernel(const void* __restrict__ x, const float* __restrict__ w,
                                                        int dim, float eps, void* __restrict__ out) {
@@ -390,6 +619,17 @@ __global__ void __launch_bounds__(256) rope_kernel(const void* __restrict__ x, i
 }
 
 // kv splits: enough CTAs to cover the SMs twice, at least one 64-position tile per split.
+// kv splits of the MLA kernel: enough CTAs to cover the SMs twice, at least one 64-position
+// stretch per split.
+static int mla_splits(int B, int H, int S, int L) {
+  const long base = (long)(((long)S * H + kTcRows - 1) / kTcRows) * B;
+  const int tiles = (L + kAttnTile - 1) / kAttnTile;
+  long sp = base > 0 ? (2L * 148 + base - 1) / base : 1;
+  if (sp > tiles) sp = tiles;
+  if (sp > 64) sp = 64;
+  return sp < 1 ? 1 : (int)sp;
+}
+
 static int attn_splits(int B, int Hq, int Hkv, int S, int L) {
   const int G = Hq / Hkv;
   const long base = (long)((G * S + kTcRows - 1) / kTcRows) * B * Hkv;
@@ -463,6 +703,45 @@ int ccut_gqa_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, 
                     (const float*)part, rows, sp, out);
   return launch_k(ob ? gqa_combine_kernel<64, true> : gqa_combine_kernel<64, false>, g2, dim3(256), 0, stream,
                   (const float*)part, rows, sp, out);
+}
+
+size_t ccut_mla_attention_workspace_bytes(int batch, int heads, int seq, int kv_len) {
+  if (batch < 0 || heads <= 0 || seq < 0 || kv_len < 0) return 0;
+  const int sp = mla_splits(batch, heads, seq, kv_len);
+  if (sp <= 1) return 256;
+  return 256 + (size_t)sp * batch * heads * seq * (kMlaR + 2) * sizeof(float);
+}
+
+int ccut_mla_attention(const float* q, const uint16_t* kv, int batch, int heads, int seq, int kv_len, int rank,
+                       int rope_dim, int causal_start, float scale, void* out, int out_dtype, void* workspace,
+                       size_t ws_bytes, ccut_stream_t stream) {
+  PdlScope pdl_scope((long)batch * seq);
+  if (rank != kMlaR || rope_dim != kMlaP) return CCUT_ERR_UNSUPPORTED;
+  if (batch < 0 || heads <= 0 || seq < 0 || kv_len < 0 || !(scale > 0.f)) return CCUT_ERR_INVALID;
+  if (out_dtype != CCUT_OUT_BF16 && out_dtype != CCUT_OUT_F32) return CCUT_ERR_INVALID;
+  if (batch == 0 || seq == 0) return CCUT_OK;
+  if (!q || !out || (kv_len > 0 && !kv)) return CCUT_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(kv)) % 16) return CCUT_ERR_INVALID;
+  if (batch > 65535 || (long)seq * heads > 2147483647L - kTcRows) return CCUT_ERR_UNSUPPORTED;
+  const int sp = mla_splits(batch, heads, seq, kv_len);
+  if (sp > 1 && (!workspace || ws_bytes < ccut_mla_attention_workspace_bytes(batch, heads, seq, kv_len)))
+    return CCUT_ERR_WORKSPACE;
+  const int nrows = seq * heads;
+  const int tiles = (kv_len + kMlaTile - 1) / kMlaTile;
+  const int tps = (tiles + sp - 1) / sp;
+  const dim3 grid((nrows + kTcRows - 1) / kTcRows, batch, sp);
+  float* part = sp > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 256) : nullptr;
+  const bool ob = out_dtype == CCUT_OUT_BF16;
+  auto kern = ob ? mla_attn_kernel<true> : mla_attn_kernel<false>;
+  static std::atomic<uint64_t> smem_set[2];  // per output type: devices with the limit raised
+  int rc = ensure_smem_limit(kern, MlaSmem::kBytes, smem_set[ob]);
+  if (rc) return rc;
+  rc = launch_k(kern, grid, dim3(kMlaWarps * 32), MlaSmem::kBytes, stream, q, kv, heads, seq, kv_len, causal_start,
+                scale, sp, tps, out, part);
+  if (rc || sp == 1) return rc;
+  const int rows = batch * nrows;
+  return launch_k(ob ? gqa_combine_kernel<kMlaR, true> : gqa_combine_kernel<kMlaR, false>, dim3((rows + 7) / 8),
+                  dim3(256), 0, stream, (const float*)part, rows, sp, out);
 }
 
 int ccut_apply_rope(const void* x, int x_dtype, int batch, int heads, int seq, int head_dim, const float* inv_freq,

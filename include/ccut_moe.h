@@ -267,6 +267,19 @@ CCUT_API int ccut_rms_norm(const void* x, int x_dtype, const float* weight, int 
 CCUT_API int ccut_apply_rope(const void* x, int x_dtype, int batch, int heads, int seq, int head_dim,
                              const float* inv_freq, const int32_t* positions, float scale, void* out,
                              int out_dtype, ccut_stream_t stream);
+/* MLA attention in the latent space (ccut/blocks/attn_mla.py:85-167, mla_decode /
+ * mla_prefill, with the up-projections outside): q fp32 [batch, seq * heads, rank + rope_dim],
+ * row s * heads + h = (q_nope of head h times k_up_h^T, the rotated q_pe); kv bf16 [batch,
+ * kv_len, rank + rope_dim], per position (the latent c, the rotated k_pe); out [batch, seq *
+ * heads, rank] (out_dtype) = softmax(q . kv^T * scale) @ kv[:, :rank], the latent output the
+ * caller multiplies by v_up_h.  causal_start >= 0: query s sees positions <= causal_start +
+ * s (mla_prefill's rule with causal_start = start_pos); -1: every position (mla_decode).
+ * rank 512 and rope_dim 64 (DeepSeek-V2 / V3); scale > 0; q and kv 16-byte aligned.
+ * Workspace: 256 bytes, or ccut_mla_attention_workspace_bytes when the kv range is split. */
+CCUT_API size_t ccut_mla_attention_workspace_bytes(int batch, int heads, int seq, int kv_len);
+CCUT_API int ccut_mla_attention(const float* q, const uint16_t* kv, int batch, int heads, int seq, int kv_len,
+                                int rank, int rope_dim, int causal_start, float scale, void* out, int out_dtype,
+                                void* workspace, size_t ws_bytes, ccut_stream_t stream);
 
 /* ---- diagnostics ------------------------------------------------------------------- */
 /* Device-side status word kept at the start of every workspace: a kernel whose bounded

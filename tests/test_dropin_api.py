@@ -9,7 +9,7 @@ import pytest
 import numpy as np
 
 from ccut_b200 import quant
-from ccut_b200.blocks import attn_gqa, moe, norm, rope
+from ccut_b200.blocks import attn_gqa, attn_mla, moe, norm, rope
 
 # parameter names of the reference functions (ccut/blocks/moe.py, ccut/models/generic.py,
 # ccut/quant/method.py)
@@ -28,8 +28,13 @@ REFERENCE = {
     attn_gqa.gqa_attention: ["q", "k", "v", "mask", "scale", "softcap"],
     norm.rms_norm: ["x", "weight", "eps"],
     rope.apply_rope: ["q", "k", "inv_freq", "positions", "attention_factor", "scaling_type", "seq_len"],
+    # ccut/blocks/attn_mla.py
+    attn_mla.mla_update_state: ["state", "x", "kv_a_proj", "kv_a_scale", "q_pe"],
+    attn_mla.mla_decode: ["state", "q_nope", "q_pe_rot", "k_up_proj", "v_up_proj", "scale", "start_pos"],
+    attn_mla.mla_prefill: ["state", "q_nope", "q_pe_rot", "k_up_proj", "v_up_proj", "scale", "start_pos"],
 }
-PREFIX = {attn_gqa.gqa_attention_fast: ["q", "k", "v", "mask", "scale"]}
+PREFIX = {attn_gqa.gqa_attention_fast: ["q", "k", "v", "mask", "scale"],
+          attn_mla.MLAState.__init__: ["self", "kv_lora_rank", "qk_rope_head_dim", "max_tokens"]}
 
 
 @pytest.mark.parametrize("fn", list(PREFIX), ids=lambda f: f.__qualname__)
