@@ -8,8 +8,8 @@ seeded random-init layer resident in HBM.  Under torchrun (--gpus N > 1) the lay
 expert-parallel: the workload's tokens are split over the ranks (strong scaling: the same
 total tokens at every N), each rank keeps E/N routed experts, and tokens and partial
 outputs cross NCCL.  Timing is CUDA events on the launching stream between barrier +
-synchronize fences, max over ranks.  `--workload cfg3_attn_decode` times the GQA attention
-block instead (its own metric).
+synchronize fences, max over ranks.  `--workload cfg2_mla_decode` and `cfg3_attn_decode` time
+the MLA latent attention kernel and the GQA attention block instead (their own metrics).
 
 `--impl reference` times the reference algorithm on the host cores instead (the numpy
 oracle port of CostCut-Infer's MoE path: per-call dequant of every touched expert, fp32
@@ -535,6 +535,8 @@ def run_ours(args, wl) -> None:
 # seq, kv_len, head_dim).  cfg3: Qwen3-30B-A3B GQA (32 query heads, 4 kv heads, head dim
 # 128), batch-64 decode over a 4096-position bf16 kv cache.
 ATTN_WORKLOADS = {"cfg3_attn_decode": (64, 32, 4, 1, 4096, 128)}
+# DeepSeek-V2-Lite MLA decode (config 2's attention): batch, heads, seq, kv_len; latent 512 + rope 64
+MLA_WORKLOADS = {"cfg2_mla_decode": (64, 16, 1, 4096)}
 
 
 def run_attn(args, wl) -> None:
@@ -598,13 +600,76 @@ def run_attn(args, wl) -> None:
     }), flush=True)
 
 
+def run_mla(args, wl) -> None:
+    """One MLA latent attention call per step (ccut_mla_attention) on device-resident q and
+    latent cache; roofline: the cache bytes read (the cache exceeds the L2)."""
+    import torch
+
+    from ccut_b200 import _lib, build
+    from ccut_b200.layer import _ptr, _stream
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    build.build()
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    b, h, s, L = MLA_WORKLOADS[wl]
+    width = 512 + 64
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    q = torch.randn((b, s * h, width), generator=g, device=dev)
+    kv = torch.randn((b, L, width), generator=g, device=dev).to(torch.bfloat16)
+    out = torch.empty((b, s * h, 512), dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    ws = torch.zeros(max(lib.ccut_mla_attention_workspace_bytes(b, h, s, L), 256), dtype=torch.uint8, device=dev)
+    scale = 1.0 / (192 ** 0.5)
+
+    def step():
+        _lib.call("ccut_mla_attention", _ptr(q), _ptr(kv), b, h, s, L, 512, 64, L - s, scale, _ptr(out),
+                  _lib.OUT_F32, _ptr(ws), ws.numel(), _stream())
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(dev.index or 0)
+    K = args.steps
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(K):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    clk = clocks.stop()
+    pk, src = peaks()
+    kv_bytes = b * L * width * 2
+    byts = kv_bytes + b * s * h * (width + 512) * 4
+    achieved = byts * K / (ms * 1e-3) / 1e9
+    peak = pk.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    split = lib.ccut_mla_attention_workspace_bytes(b, h, s, L) > 256
+    print(json.dumps({
+        "metric": "MLA attention tokens/s", "value": b * s * K / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1,
+        "steps": K, "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 latent cache, f32 accumulate", "data": "synthetic (seeded torch generator)",
+        "config": {"workload": wl, "batch": b, "heads": h, "seq": s, "kv_len": L, "latent": 512, "rope": 64,
+                   "l2": f"latent cache {kv_bytes / 1e6:.0f} MB > 126 MB L2, no flush"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "kernel": "mla_attn_kernel" + (" + gqa_combine_kernel" if split else ""),
+                     "algorithmic_bytes_per_launch": byts,
+                     "peak_source": f"{src} (MEASURED_PEAKS.json)" if src == "measured" else "fallback"},
+        "gpu_launches": (2 if split else 1) * K,
+        "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]},
+    }), flush=True)
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(ATTN_WORKLOADS), default=DEFAULT_WORKLOAD)
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(ATTN_WORKLOADS) + sorted(MLA_WORKLOADS),
+                    default=DEFAULT_WORKLOAD)
     ap.add_argument("--graph", choices=("auto", "on", "off"), default="auto")
     ap.add_argument("--soak", type=float, default=1.0, help="untimed seconds of load before timing")
     ap.add_argument("--cpu-sample", type=int, default=128, help="tokens in the CPU baseline sample")
@@ -613,10 +678,12 @@ def main(argv=None) -> int:
     args = ap.parse_args(argv)
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
-    if args.workload in ATTN_WORKLOADS:
+    if args.workload in ATTN_WORKLOADS or args.workload in MLA_WORKLOADS:
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "the reference arm times the MoE layer; the "
                               "attention workload has no reference timing"}), flush=True)
+        elif args.workload in MLA_WORKLOADS:
+            run_mla(args, args.workload)
         else:
             run_attn(args, args.workload)
     elif args.impl == "reference":
