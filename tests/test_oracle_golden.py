@@ -230,6 +230,27 @@ def test_mla_oracle_matches_reference(golden_dir):
         np.testing.assert_allclose(attention.mla_attention_absorbed(*args, scale, start), ref, rtol=1e-4, atol=1e-5)
 
 
+def test_mla_latent_form_at_deepseek_sizes():
+    """The latent-space regrouping the MLA kernel computes equals the reference's expanded form
+    at the DeepSeek-V2-Lite sizes (rank 512, rope 64, nope 128, v 128, 16 heads): decode over a
+    long cache and a causal prefill after a prefix."""
+    from oracle import attention
+
+    rng = np.random.default_rng(9)
+    for prefix, seq in ((200, 1), (30, 12)):
+        kv = prefix + seq
+        c = rng.standard_normal((kv, 512)).astype(np.float32)
+        kpe = rng.standard_normal((kv, 64)).astype(np.float32)
+        qn = rng.standard_normal((seq, 16, 128)).astype(np.float32)
+        qp = rng.standard_normal((seq, 16, 64)).astype(np.float32)
+        ku = (rng.standard_normal((512, 16 * 128)) * 0.05).astype(np.float32)
+        vu = (rng.standard_normal((512, 16 * 128)) * 0.05).astype(np.float32)
+        scale = 1.0 / np.sqrt(192.0)
+        ref = attention.mla_attention(c, kpe, qn, qp, ku, vu, scale, prefix)
+        got = attention.mla_attention_absorbed(c, kpe, qn, qp, ku, vu, scale, prefix)
+        np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-5 * np.abs(ref).max())
+
+
 def test_topk_softmax_wide_routers_match_reference(golden_dir):
     """The oracle's topk_softmax against the reference's at 128 experts top-8 (normalised)
     and 256 experts top-16 (both modes), with exact ties: ids bit-exact, weights to fp32."""
