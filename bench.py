@@ -9,7 +9,8 @@ expert-parallel: the workload's tokens are split over the ranks (strong scaling:
 total tokens at every N), each rank keeps E/N routed experts, and tokens and partial
 outputs cross NCCL.  Timing is CUDA events on the launching stream between barrier +
 synchronize fences, max over ranks.  `--workload cfg2_mla_decode` and `cfg3_attn_decode` time
-the MLA latent attention kernel and the GQA attention block instead (their own metrics).
+the MLA latent attention kernel and the GQA attention block instead (their own metrics);
+`cfg3_engine_decode` times whole-model decode steps through the engine backend.
 
 `--impl reference` times the reference algorithm on the host cores instead (the numpy
 oracle port of CostCut-Infer's MoE path: per-call dequant of every touched expert, fp32
@@ -537,6 +538,11 @@ def run_ours(args, wl) -> None:
 ATTN_WORKLOADS = {"cfg3_attn_decode": (64, 32, 4, 1, 4096, 128)}
 # DeepSeek-V2-Lite MLA decode (config 2's attention): batch, heads, seq, kv_len; latent 512 + rope 64
 MLA_WORKLOADS = {"cfg2_mla_decode": (64, 16, 1, 4096)}
+# whole-model decode through the engine backend: a Qwen3-30B-A3B-shaped decoder (config 3's MoE
+# layer, GQA 32 / 4 heads of 128, 48 layers, vocab 151936), `batch` requests with `prompt`-token
+# prompts, one generate_batch call per step
+ENGINE_WORKLOADS = {"cfg3_engine_decode": {"moe": "cfg3", "layers": 48, "heads": 32, "kv_heads": 4, "head_dim": 128,
+                                           "vocab": 151936, "batch": 8, "prompt": 512}}
 
 
 def run_attn(args, wl) -> None:
@@ -662,14 +668,94 @@ def run_mla(args, wl) -> None:
     }), flush=True)
 
 
+def run_engine(args, wl) -> None:
+    """Decode steps of a whole synthetic model through ``GenericBackend.generate_batch`` (the
+    call an engine step makes): every step runs one new token per request through all layers
+    (bf16 projections on cuBLAS, RMSNorm / RoPE / GQA attention / the MoE layer on this
+    library's kernels) and samples greedily on the device."""
+    import torch
+
+    from ccut_b200 import build
+    from ccut_b200.backend import GenericBackend
+    from ccut_b200.layer import MoeLayer
+    from ccut_b200.model import DecoderLayer, MoeDecoder, rope_table
+    from ccut_b200.synthetic import CONFIGS, make_layer_device
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    build.build()
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    w = ENGINE_WORKLOADS[wl]
+    c = CONFIGS[w["moe"]]
+    H, nh, kvh, d = c.hidden, w["heads"], w["kv_heads"], w["head_dim"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+
+    def mat(o, i):
+        return (torch.randn((o, i), generator=g, device=dev) / i ** 0.5).to(torch.bfloat16)
+
+    def norm_w(n):
+        return torch.rand((n,), generator=g, device=dev) + 0.5
+
+    layers = []
+    for i in range(w["layers"]):
+        lw = make_layer_device(c, seed=i, device=dev)
+        moe = MoeLayer(c.fmt, c.hidden, c.inter, c.num_experts, c.top_k, c.routing, lw.router, lw.experts,
+                       shared=lw.shared or None, shared_inter=c.shared_inter or None, device=dev)
+        layers.append(DecoderLayer(norm_w(H), mat(nh * d, H), mat(kvh * d, H), mat(kvh * d, H), mat(H, nh * d),
+                                   norm_w(H), moe, norm_w(d), norm_w(d), heads=nh, kv_heads=kvh, head_dim=d,
+                                   device=dev))
+    inv, af = rope_table(d, 1e6)
+    dec = MoeDecoder(torch.randn((w["vocab"], H), generator=g, device=dev), layers, norm_w(H), mat(w["vocab"], H),
+                     inv_freq=inv, attention_factor=af, device=dev)
+    B, P = w["batch"], w["prompt"]
+    be = GenericBackend(dec, max_seqs=B, max_len=P + args.warmup + args.steps + 8, prefill_chunk=P)
+    rng = np.random.default_rng(0)
+    seqs = [[int(x) for x in rng.integers(0, w["vocab"], P)] for _ in range(B)]
+    greedy = {"temperature": 0.0}
+
+    def step():
+        for s, tok in zip(seqs, be.generate_batch([(s, greedy) for s in seqs])):
+            s.append(tok)
+
+    step()  # the prompts (prefill), untimed
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(dev.index or 0)
+    K = args.steps
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    start.record()
+    for _ in range(K):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    ms = start.elapsed_time(end)
+    clk = clocks.stop()
+    print(json.dumps({
+        "metric": "engine decode tokens/s", "value": B * K / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": K,
+        "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 activations, AWQ int4 experts, f32 accumulate", "data": "synthetic (seeded torch generator)",
+        "config": {"workload": wl, "layers": w["layers"], "batch": B, "prompt": P, "moe": w["moe"], "heads": nh,
+                   "kv_heads": kvh, "head_dim": d, "vocab": w["vocab"],
+                   "l2": "expert weights of every layer exceed the 126 MB L2, no flush"},
+        "e2e": {"value": B * K / wall, "unit": "tokens/s", "h2d_bytes_per_step": B * 8 * 2,
+                "d2h_bytes_per_step": B * 8},
+        "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]},
+    }), flush=True)
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(ATTN_WORKLOADS) + sorted(MLA_WORKLOADS),
-                    default=DEFAULT_WORKLOAD)
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(ATTN_WORKLOADS) + sorted(MLA_WORKLOADS)
+                    + sorted(ENGINE_WORKLOADS), default=DEFAULT_WORKLOAD)
     ap.add_argument("--graph", choices=("auto", "on", "off"), default="auto")
     ap.add_argument("--soak", type=float, default=1.0, help="untimed seconds of load before timing")
     ap.add_argument("--cpu-sample", type=int, default=128, help="tokens in the CPU baseline sample")
@@ -678,10 +764,12 @@ def main(argv=None) -> int:
     args = ap.parse_args(argv)
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
-    if args.workload in ATTN_WORKLOADS or args.workload in MLA_WORKLOADS:
+    if args.workload in ATTN_WORKLOADS or args.workload in MLA_WORKLOADS or args.workload in ENGINE_WORKLOADS:
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "the reference arm times the MoE layer; the "
-                              "attention workload has no reference timing"}), flush=True)
+                              "attention and engine workloads have no reference timing"}), flush=True)
+        elif args.workload in ENGINE_WORKLOADS:
+            run_engine(args, args.workload)
         elif args.workload in MLA_WORKLOADS:
             run_mla(args, args.workload)
         else:
