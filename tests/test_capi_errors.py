@@ -142,3 +142,14 @@ def test_error_strings_and_status(lib):
     with pytest.raises(TimeoutError):
         _lib.check(_lib.ERR_TIMEOUT)
     _lib.check(_lib.OK)
+
+
+def test_static_permute_checks(lib):
+    """The allocation-free permutation refuses more experts than its fixed scratch holds and
+    bad shapes before it looks up that scratch."""
+    out4 = [FAKE] * 4
+    assert lib.ccut_moe_permute_static(FAKE, FAKE, 4, 2, 257, 0, 1.0, *out4, NULL) == _lib.ERR_UNSUPPORTED
+    assert lib.ccut_moe_permute_static(FAKE, FAKE, 4, 0, 8, 0, 1.0, *out4, NULL) == _lib.ERR_INVALID
+    assert lib.ccut_moe_permute_static(FAKE, FAKE, -1, 2, 8, 0, 1.0, *out4, NULL) == _lib.ERR_INVALID
+    assert lib.ccut_moe_permute_static(NULL, NULL, 4, 2, 8, 0, 1.0, *out4, NULL) == _lib.ERR_INVALID
+    assert lib.ccut_moe_permute_static(FAKE, FAKE, 4, 2, 8, 0, 1.0, NULL, *out4[1:], NULL) == _lib.ERR_INVALID
