@@ -16,6 +16,9 @@ NULL = None
 
 @pytest.fixture(scope="module")
 def lib():
+    from ccut_b200 import build
+
+    build.build()  # nvcc cross-compiles here; no GPU is needed to load the library
     return _lib.load()
 
 

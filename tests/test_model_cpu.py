@@ -5,7 +5,7 @@ errors).
 
 The host-logic tests run ``MoeDecoder`` on CPU tensors with its three device calls (RMSNorm,
 RoPE, attention) replaced by short torch functions written here and a torch MoE block; the
-product runs those calls through the CUDA library (``tests/test_zzz_gpu_engine.py``).
+product runs those calls through the CUDA library (``tests/test_z_gpu_engine.py``).
 """
 
 from __future__ import annotations
