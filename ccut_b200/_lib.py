@@ -87,6 +87,8 @@ SIGNATURES: dict[str, tuple] = {
     "ccut_gqa_attention": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _f, _vp, _i, _vp, _sz, _vp]),
     "ccut_rms_norm": (_i, [_vp, _i, _vp, _i, _i, _f, _vp, _i, _vp]),
     "ccut_apply_rope": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _vp, _f, _vp, _i, _vp]),
+    "ccut_gqa_attention_pool": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, C.c_longlong, _i, _f, _f, _vp,
+                                     _i, _vp, _sz, _vp]),
     "ccut_mla_attention_workspace_bytes": (_sz, [_i, _i, _i, _i]),
     "ccut_mla_attention": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _i, _vp, _sz, _vp]),
     "ccut_moe_ep_forward": (_i, [_vp, C.POINTER(MoeLayerDesc), _i, _i, C.POINTER(RouteParams), _vp, _i, _vp, _i,

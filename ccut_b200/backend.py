@@ -62,10 +62,13 @@ class GenericBackend:
     tier = "L0"
 
     def __init__(self, model: MoeDecoder, max_seqs: int = 4, max_len: int = 4096, prefill_chunk: int = 4096,
-                 seed: int = 0, eos_token_id: int | None = None):
+                 seed: int = 0, eos_token_id: int | None = None, pool: bool = False):
+        """``pool``: keep the sequence caches in one ``KvPool``, so that a decode step of several
+        requests (``generate_batch``) runs one attention launch per layer."""
         if max_seqs < 1 or max_len < 1 or prefill_chunk < 1:
             raise ValueError("max_seqs, max_len and prefill_chunk must be positive")
         self.model = model
+        self._pool = model.new_pool(max_seqs, max_len) if pool else None
         self.max_seqs, self.max_len, self.prefill_chunk = int(max_seqs), int(max_len), int(prefill_chunk)
         self.eos_token_id = eos_token_id
         self._seqs: list[_Seq] = []  # least recently used first
@@ -87,7 +90,9 @@ class GenericBackend:
         if best is None or reuse == 0:
             reuse = 0
             if len(self._seqs) < self.max_seqs:
-                best = _Seq(self.model.new_cache(self.max_len))
+                cache = (self._pool.cache(len(self._seqs)) if self._pool is not None
+                         else self.model.new_cache(self.max_len))
+                best = _Seq(cache)
             else:
                 free = [s for s in self._seqs if not any(s is t for t in taken)]
                 if not free:

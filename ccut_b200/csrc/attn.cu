@@ -74,11 +74,19 @@ struct TcAttnSmem {
 // (tile j of the CTA's range goes to warp j % 4) through a three-deep cp.async ring and keeps
 // its own online softmax (running max and sum of rows g and g + 8, fp32 O fragments); the
 // four warp states are merged through shared memory at the end.
-template <int D, bool OUT_BF16>
-__global__ void __launch_bounds__(kTcWarps * 32) gqa_attn_kernel(
+//
+// The body serves two kernels.  gqa_attn_kernel: batch row b reads k / v at b's slice of
+// [B, Hkv, L, D] with one causal offset for all rows.  gqa_attn_pool_kernel (POOL): batch row
+// b reads slot slots[b] of a cache pool (slots slot_stride elements apart, kv head h at
+// h * L * D inside a slot) with causal offset starts[b], so one launch serves sequences of
+// different lengths; a slot outside [0, num_slots) or a negative offset reads nothing and its
+// rows come out zero.
+template <int D, bool OUT_BF16, bool POOL>
+__device__ __forceinline__ void gqa_attn_body(
     const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, const uint16_t* __restrict__ v, int Hq, int Hkv,
     int S, int L, int causal_start, float scale, float softcap, int splits, int tiles_per_split,
-    void* __restrict__ out, float* __restrict__ part) {
+    void* __restrict__ out, float* __restrict__ part, const int* __restrict__ slots, const int* __restrict__ starts,
+    long long slot_stride, int num_slots) {
   pdl_wait();
   pdl_trigger();
   using SM = TcAttnSmem<D>;
@@ -93,6 +101,17 @@ __global__ void __launch_bounds__(kTcWarps * 32) gqa_attn_kernel(
   const int split = blockIdx.z;
   const int k0 = split * tiles_per_split * kAttnTile;
   int k1 = min(L, k0 + tiles_per_split * kAttnTile);
+  size_t kv_off = (size_t)bh * L * D;
+  if constexpr (POOL) {
+    const int slot = slots[b];
+    causal_start = starts[b];
+    const bool valid = slot >= 0 && slot < num_slots && causal_start >= 0;
+    if (!valid) {
+      k1 = 0;  // nothing to read: the rows come out zero
+      causal_start = 0;
+    }
+    kv_off = (valid ? (size_t)slot * (size_t)slot_stride : (size_t)0) + (size_t)kvh * L * D;
+  }
   if (causal_start >= 0) {  // the CTA's last row sees up to causal_start + s_last
     const int r_last = min(nrows, r0 + kTcRows) - 1;
     k1 = min(k1, causal_start + r_last / G + 1);
@@ -124,8 +143,8 @@ __global__ void __launch_bounds__(kTcWarps * 32) gqa_attn_kernel(
 #pragma unroll
     for (int i = 0; i < 4; ++i) o[dn][i] = 0.f;
   uint16_t* wb = qs + SM::kQElems + warp * SM::kWarpElems;  // [stage][K, V][16][kRow]
-  const uint16_t* kg = k + (size_t)bh * L * D;
-  const uint16_t* vg = v + (size_t)bh * L * D;
+  const uint16_t* kg = k + kv_off;
+  const uint16_t* vg = v + kv_off;
   const int ntiles = k1 > k0 ? (k1 - k0 + kTcTile - 1) / kTcTile : 0;
   auto issue = [&](int tile, int buf) {
     const int p0 = k0 + tile * kTcTile;
@@ -281,6 +300,25 @@ __global__ void __launch_bounds__(kTcWarps * 32) gqa_attn_kernel(
       p[2 + dd] = ov;
     }
   }
+}
+
+template <int D, bool OUT_BF16>
+__global__ void __launch_bounds__(kTcWarps * 32) gqa_attn_kernel(
+    const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, const uint16_t* __restrict__ v, int Hq, int Hkv,
+    int S, int L, int causal_start, float scale, float softcap, int splits, int tiles_per_split,
+    void* __restrict__ out, float* __restrict__ part) {
+  gqa_attn_body<D, OUT_BF16, false>(q, k, v, Hq, Hkv, S, L, causal_start, scale, softcap, splits, tiles_per_split,
+                                    out, part, nullptr, nullptr, 0, 0);
+}
+
+template <int D, bool OUT_BF16>
+__global__ void __launch_bounds__(kTcWarps * 32) gqa_attn_pool_kernel(
+    const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, const uint16_t* __restrict__ v, int Hq, int Hkv,
+    int S, int L, float scale, float softcap, int splits, int tiles_per_split, void* __restrict__ out,
+    float* __restrict__ part, const int* __restrict__ slots, const int* __restrict__ starts, long long slot_stride,
+    int num_slots) {
+  gqa_attn_body<D, OUT_BF16, true>(q, k, v, Hq, Hkv, S, L, 0, scale, softcap, splits, tiles_per_split, out, part,
+                                   slots, starts, slot_stride, num_slots);
 }
 
 // Merge of the kv splits: one warp per output row.
@@ -694,6 +732,59 @@ int ccut_gqa_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, 
     if (rc) return rc;
     rc = launch_k(kern, grid, dim3(kTcWarps * 32), smem, stream, q, k, v, heads, kv_heads, seq, kv_len, causal_start,
                   scale, softcap, sp, tps, out, part);
+  }
+  if (rc || sp == 1) return rc;
+  const int rows = batch * heads * seq;
+  const dim3 g2((rows + 7) / 8);
+  if (head_dim == 128)
+    return launch_k(ob ? gqa_combine_kernel<128, true> : gqa_combine_kernel<128, false>, g2, dim3(256), 0, stream,
+                    (const float*)part, rows, sp, out);
+  return launch_k(ob ? gqa_combine_kernel<64, true> : gqa_combine_kernel<64, false>, g2, dim3(256), 0, stream,
+                  (const float*)part, rows, sp, out);
+}
+
+int ccut_gqa_attention_pool(const uint16_t* q, const uint16_t* k_pool, const uint16_t* v_pool, const int32_t* slots,
+                            const int32_t* starts, int batch, int heads, int kv_heads, int seq, int max_len,
+                            int head_dim, long long slot_stride, int num_slots, float scale, float softcap, void* out,
+                            int out_dtype, void* workspace, size_t ws_bytes, ccut_stream_t stream) {
+  PdlScope pdl_scope((long)batch * seq);
+  if (head_dim != 64 && head_dim != 128) return CCUT_ERR_UNSUPPORTED;
+  if (!attn_shape_ok(batch, heads, kv_heads, seq, max_len, head_dim) || num_slots < 0) return CCUT_ERR_INVALID;
+  if (out_dtype != CCUT_OUT_BF16 && out_dtype != CCUT_OUT_F32) return CCUT_ERR_INVALID;
+  if (slot_stride < (long long)kv_heads * max_len * head_dim || slot_stride % 8) return CCUT_ERR_INVALID;
+  if (batch == 0 || seq == 0) return CCUT_OK;
+  if (!q || !out || !slots || !starts || (max_len > 0 && num_slots > 0 && (!k_pool || !v_pool)))
+    return CCUT_ERR_INVALID;
+  if ((size_t)batch * kv_heads > 65535) return CCUT_ERR_UNSUPPORTED;
+  const size_t need = ccut_gqa_attention_workspace_bytes(batch, heads, kv_heads, seq, max_len, head_dim);
+  const int sp = attn_splits(batch, heads, kv_heads, seq, max_len);
+  if (sp > 1 && (!workspace || ws_bytes < need)) return CCUT_ERR_WORKSPACE;
+  if (!(scale > 0.f)) scale = 1.f / sqrtf((float)head_dim);
+  const int G = heads / kv_heads;
+  const int tiles = (max_len + kAttnTile - 1) / kAttnTile;
+  const int tps = sp > 0 ? (tiles + sp - 1) / sp : 1;
+  const dim3 grid((G * seq + kTcRows - 1) / kTcRows, batch * kv_heads, sp);
+  float* part = sp > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 256) : nullptr;
+  const bool ob = out_dtype == CCUT_OUT_BF16;
+  const int* sl = reinterpret_cast<const int*>(slots);
+  const int* st = reinterpret_cast<const int*>(starts);
+  int rc;
+  if (head_dim == 128) {
+    auto kern = ob ? gqa_attn_pool_kernel<128, true> : gqa_attn_pool_kernel<128, false>;
+    constexpr size_t smem = TcAttnSmem<128>::kBytes;
+    static std::atomic<uint64_t> smem_set[2];  // per output type: devices with the limit raised
+    rc = ensure_smem_limit(kern, smem, smem_set[ob]);
+    if (rc) return rc;
+    rc = launch_k(kern, grid, dim3(kTcWarps * 32), smem, stream, q, k_pool, v_pool, heads, kv_heads, seq, max_len,
+                  scale, softcap, sp, tps, out, part, sl, st, slot_stride, num_slots);
+  } else {
+    auto kern = ob ? gqa_attn_pool_kernel<64, true> : gqa_attn_pool_kernel<64, false>;
+    constexpr size_t smem = TcAttnSmem<64>::kBytes;
+    static std::atomic<uint64_t> smem_set[2];
+    rc = ensure_smem_limit(kern, smem, smem_set[ob]);
+    if (rc) return rc;
+    rc = launch_k(kern, grid, dim3(kTcWarps * 32), smem, stream, q, k_pool, v_pool, heads, kv_heads, seq, max_len,
+                  scale, softcap, sp, tps, out, part, sl, st, slot_stride, num_slots);
   }
   if (rc || sp == 1) return rc;
   const int rows = batch * heads * seq;

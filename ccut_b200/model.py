@@ -44,7 +44,7 @@ from ccut_b200.blocks.rope import apply_rope
 from ccut_b200.layer import _ptr, _stream
 from ccut_b200.quant import QuantLinear
 
-__all__ = ["DecoderLayer", "KvCache", "MoeDecoder", "rope_table"]
+__all__ = ["DecoderLayer", "KvCache", "KvPool", "MoeDecoder", "rope_table"]
 
 
 def rope_table(head_dim: int, rope_theta: float, rope_scaling: dict | None = None) -> tuple[np.ndarray, float]:
@@ -94,12 +94,58 @@ class KvCache:
         self.v = torch.zeros_like(self.k)
         self.max_len = int(max_len)
         self.length = 0
+        self.pool, self.slot = None, -1
+
+    @classmethod
+    def in_pool(cls, pool: "KvPool", slot: int) -> "KvCache":
+        """The cache of slot ``slot`` of ``pool`` (views of the pool's tensors), empty."""
+        if not 0 <= slot < pool.slots:
+            raise ValueError(f"slot {slot} outside the pool's {pool.slots}")
+        c = cls.__new__(cls)
+        c.k, c.v = pool.k[slot], pool.v[slot]
+        c.max_len, c.length, c.pool, c.slot = pool.max_len, 0, pool, int(slot)
+        return c
 
     def truncate(self, n: int) -> None:
         """Keep the first ``n`` positions (later ones are overwritten by the next forward)."""
         if not 0 <= n <= self.length:
             raise ValueError(f"cannot truncate {self.length} cached positions to {n}")
         self.length = int(n)
+
+
+class KvPool:
+    """The caches of up to ``slots`` sequences in one allocation, ``[slots, layers, kv_heads,
+    max_len, head_dim]`` bf16 for k and for v: a decode step over several of them is one
+    attention launch per layer (``ccut_gqa_attention_pool``)."""
+
+    def __init__(self, slots: int, layers: int, kv_heads: int, max_len: int, head_dim: int, device="cuda"):
+        if slots <= 0 or max_len <= 0:
+            raise ValueError("slots and max_len must be positive")
+        self.k = torch.zeros((slots, layers, kv_heads, max_len, head_dim), dtype=torch.bfloat16, device=device)
+        self.v = torch.zeros_like(self.k)
+        self.slots, self.max_len = int(slots), int(max_len)
+
+    def cache(self, slot: int) -> KvCache:
+        return KvCache.in_pool(self, slot)
+
+
+def _attend_pool(q: torch.Tensor, pool: KvPool, layer: int, slots: torch.Tensor, starts: torch.Tensor,
+                 softcap: float | None) -> torch.Tensor:
+    """q ``[B, heads, S, d]`` bf16; batch row b attends over slot ``slots[b]`` of ``pool`` at
+    ``layer`` with causal offset ``starts[b]`` -> ``[B, heads, S, d]`` bf16."""
+    if not q.is_cuda:
+        raise ValueError("attention runs on CUDA tensors only")
+    B, H, S, d = q.shape
+    Hkv, L = pool.k.shape[2], pool.k.shape[3]
+    lib = _lib.load()
+    nbytes = lib.ccut_gqa_attention_workspace_bytes(B, H, Hkv, S, L, d)
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=q.device)
+    out = torch.empty((B, H, S, d), dtype=torch.bfloat16, device=q.device)
+    with torch.cuda.device(q.device):
+        _lib.call("ccut_gqa_attention_pool", _ptr(q), _ptr(pool.k[0, layer]), _ptr(pool.v[0, layer]), _ptr(slots),
+                  _ptr(starts), B, H, Hkv, S, L, d, int(pool.k.stride(0)), pool.slots, 0.0, float(softcap or 0.0),
+                  _ptr(out), _lib.OUT_BF16, _ptr(ws), ws.numel(), _stream())
+    return out
 
 
 def _attend(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, start_pos: int, softcap: float | None) -> torch.Tensor:
@@ -187,11 +233,12 @@ class DecoderLayer:
             return rms_norm(x.contiguous(), w, eps).reshape(seq, n, d)
         return rms_norm(x.reshape(seq, n, d).contiguous(), w, eps)
 
-    def forward(self, h: torch.Tensor, spans: list, layer: int, rope: "_Rope") -> torch.Tensor:
+    def forward(self, h: torch.Tensor, spans: list, layer: int, rope: "_Rope", pooled=None) -> torch.Tensor:
         """h [N, H] fp32 (the residual stream of every span's tokens, one after the other) ->
         [N, H] fp32.  Each ``_Span`` writes its sequence's cache at ``start .. start + n - 1`` of
         ``layer`` and attends over it; the projections, norms, RoPE and the FFN run once over
-        all N tokens."""
+        all N tokens.  ``pooled`` = ``(pool, slots, starts)`` when every span is one token of a
+        cache in the same ``KvPool``: attention is then one launch for all of them."""
         N = h.shape[0]
         H, Hkv, d = self.heads, self.kv_heads, self.head_dim
         x = rms_norm(h, self.ln1, rope.eps).to(torch.bfloat16)
@@ -207,14 +254,20 @@ class DecoderLayer:
         qr, kr = apply_rope(q.transpose(0, 1).unsqueeze(0), k.transpose(0, 1).unsqueeze(0), rope.inv_freq,
                             pos.reshape(1, N), rope.attn_factor, rope.scaling_type)
         qr = qr.to(torch.bfloat16)
-        outs = []
         for s in spans:
             s.cache.k[layer, :, s.start: s.start + s.n] = kr[0, :, s.off: s.off + s.n]
             s.cache.v[layer, :, s.start: s.start + s.n] = vt[:, s.off: s.off + s.n]
-            qs = qr[:, :, s.off: s.off + s.n].contiguous()
-            outs.append(_attend(qs, s.cache.k[layer], s.cache.v[layer], s.start, rope.softcap))
-        o = outs[0] if len(outs) == 1 else torch.cat(outs, dim=2)
-        h = h + _project(self.wo, o[0].transpose(0, 1).reshape(N, H * d)).float()
+        if pooled is not None:  # N sequences of one token each: q [N, heads, 1, d]
+            pool, slots, starts = pooled
+            o = _attend_pool(qr[0].transpose(0, 1).unsqueeze(2).contiguous(), pool, layer, slots, starts,
+                             rope.softcap)
+            o2 = o[:, :, 0, :].reshape(N, H * d)
+        else:
+            outs = [_attend(qr[:, :, s.off: s.off + s.n].contiguous(), s.cache.k[layer], s.cache.v[layer], s.start,
+                            rope.softcap) for s in spans]
+            o = outs[0] if len(outs) == 1 else torch.cat(outs, dim=2)
+            o2 = o[0].transpose(0, 1).reshape(N, H * d)
+        h = h + _project(self.wo, o2).float()
         x2 = rms_norm(h, self.ln2, rope.eps).to(torch.bfloat16)
         return h + self.ffn.forward(x2, out_dtype=torch.float32)
 
@@ -269,6 +322,10 @@ class MoeDecoder:
         l0 = self.layers[0]
         return KvCache(len(self.layers), l0.kv_heads, max_len, l0.head_dim, self.device)
 
+    def new_pool(self, slots: int, max_len: int) -> KvPool:
+        l0 = self.layers[0]
+        return KvPool(slots, len(self.layers), l0.kv_heads, max_len, l0.head_dim, self.device)
+
     def _ids(self, tokens) -> torch.Tensor:
         if isinstance(tokens, torch.Tensor):
             return tokens.to(device=self.device, dtype=torch.int64).reshape(-1)
@@ -299,7 +356,8 @@ class MoeDecoder:
                 raise ValueError(f"start position {p} is past the {cache.length} cached positions")
             if p + n > cache.max_len:
                 raise ValueError(f"{p} + {n} positions do not fit the cache of {cache.max_len}")
-            if any(s.cache is cache for s in spans):
+            if any(s.cache is cache or (cache.pool is not None and s.cache.pool is cache.pool
+                                        and s.cache.slot == cache.slot) for s in spans):
                 raise ValueError("each sequence of a batch needs its own cache")
             spans.append(_Span(cache, p, off, n))
             ids_all.append(ids)
@@ -307,9 +365,15 @@ class MoeDecoder:
         ids = ids_all[0] if len(ids_all) == 1 else torch.cat(ids_all)
         if int(ids.min()) < 0 or int(ids.max()) >= self.vocab:
             raise ValueError(f"token ids must be in [0, {self.vocab})")
+        pool = spans[0].cache.pool
+        pooled = None
+        if len(spans) > 1 and pool is not None and all(s.n == 1 and s.cache.pool is pool for s in spans):
+            slots = torch.tensor([s.cache.slot for s in spans], dtype=torch.int32).to(self.device)
+            starts = torch.tensor([s.start for s in spans], dtype=torch.int32).to(self.device)
+            pooled = (pool, slots, starts)
         h = self.embed.index_select(0, ids).float()
         for i, lay in enumerate(self.layers):
-            h = lay.forward(h, spans, i, self.rope)
+            h = lay.forward(h, spans, i, self.rope, pooled)
         for s in spans:
             s.cache.length = s.start + s.n
         if all_logits:

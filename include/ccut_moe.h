@@ -267,6 +267,19 @@ CCUT_API int ccut_rms_norm(const void* x, int x_dtype, const float* weight, int 
 CCUT_API int ccut_apply_rope(const void* x, int x_dtype, int batch, int heads, int seq, int head_dim,
                              const float* inv_freq, const int32_t* positions, float scale, void* out,
                              int out_dtype, ccut_stream_t stream);
+/* ccut_gqa_attention for a batch of sequences whose caches live in one pool (the decode step of
+ * several requests in one launch; the reference attends per request,
+ * ccut/models/generic.py:304-345): the k / v of batch row b are slot slots[b] (int32, device)
+ * of k_pool / v_pool, slots slot_stride elements apart (a multiple of 8, at least kv_heads *
+ * max_len * head_dim), kv head h at h * max_len * head_dim inside a slot; row b's query i sees
+ * positions <= starts[b] + i (int32, device).  A slot outside [0, num_slots) or a negative
+ * start reads nothing and gives zero rows.  The workspace is that of ccut_gqa_attention with
+ * kv_len = max_len. */
+CCUT_API int ccut_gqa_attention_pool(const uint16_t* q, const uint16_t* k_pool, const uint16_t* v_pool,
+                                     const int32_t* slots, const int32_t* starts, int batch, int heads, int kv_heads,
+                                     int seq, int max_len, int head_dim, long long slot_stride, int num_slots,
+                                     float scale, float softcap, void* out, int out_dtype, void* workspace,
+                                     size_t ws_bytes, ccut_stream_t stream);
 /* MLA attention in the latent space (ccut/blocks/attn_mla.py:85-167, mla_decode /
  * mla_prefill, with the up-projections outside): q fp32 [batch, seq * heads, rank + rope_dim],
  * row s * heads + h = (q_nope of head h times k_up_h^T, the rotated q_pe); kv bf16 [batch,

@@ -156,3 +156,27 @@ def test_static_permute_checks(lib):
     assert lib.ccut_moe_permute_static(FAKE, FAKE, -1, 2, 8, 0, 1.0, *out4, NULL) == _lib.ERR_INVALID
     assert lib.ccut_moe_permute_static(NULL, NULL, 4, 2, 8, 0, 1.0, *out4, NULL) == _lib.ERR_INVALID
     assert lib.ccut_moe_permute_static(FAKE, FAKE, 4, 2, 8, 0, 1.0, NULL, *out4[1:], NULL) == _lib.ERR_INVALID
+
+
+def test_pool_attention_checks(lib):
+    bf = _lib.OUT_BF16
+    pool = lib.ccut_gqa_attention_pool
+    stride = 2 * 300 * 64
+
+    def call(*, q=FAKE, slots=FAKE, batch=3, heads=8, kvh=2, seq=1, L=300, d=64, stride=stride, n=4, out_dtype=bf,
+             ws=1 << 20):
+        return pool(q, FAKE, FAKE, slots, FAKE, batch, heads, kvh, seq, L, d, stride, n, 0.0, 0.0, FAKE, out_dtype,
+                    FAKE, ws, NULL)
+
+    assert call(d=96) == _lib.ERR_UNSUPPORTED
+    assert call(heads=3) == _lib.ERR_INVALID
+    assert call(stride=stride - 8) == _lib.ERR_INVALID  # slots would overlap
+    assert call(stride=stride + 4) == _lib.ERR_INVALID  # slots not 16-byte aligned
+    assert call(n=-1) == _lib.ERR_INVALID
+    assert call(out_dtype=9) == _lib.ERR_INVALID
+    assert call(batch=0) == _lib.OK
+    assert call(slots=NULL) == _lib.ERR_INVALID
+    assert call(q=NULL) == _lib.ERR_INVALID
+    need = lib.ccut_gqa_attention_workspace_bytes(3, 8, 2, 1, 300, 64)
+    if need > 256:
+        assert call(ws=need - 1) == _lib.ERR_WORKSPACE

@@ -414,3 +414,49 @@ def test_decoder_with_projection_objects(torch_ops, which):
         w = t.attn[0]
         m.DecoderLayer(w.ln1, _TorchProj(w.wk), w.wk, w.wv, w.wo, w.ln2, None, heads=t.heads, kv_heads=t.kv_heads,
                        head_dim=t.head_dim, device="cpu")
+
+
+def _attend_pool(q, pool, layer, slots, starts, softcap):
+    """Torch stand-in of the pooled attention: row b over its slot's positions <= starts[b] + i."""
+    outs = []
+    for b in range(q.shape[0]):
+        slot, st = int(slots[b]), int(starts[b])
+        outs.append(_attend(q[b:b + 1], pool.k[slot, layer], pool.v[slot, layer], st, softcap)[0])
+    return torch.stack(outs)
+
+
+def test_backend_pooled_caches_match(torch_ops, monkeypatch):
+    """Caches in one KvPool (a decode step of several requests is one attention call per layer):
+    the same tokens as separate caches, the decode steps through the pooled call with every
+    request at once, slots reused after eviction, and two views of one slot refused."""
+    from ccut_b200.backend import GenericBackend
+
+    m = torch_ops
+    calls = []
+
+    def pooled(*a):
+        calls.append(a[0].shape[0])
+        return _attend_pool(*a)
+
+    monkeypatch.setattr(m, "_attend_pool", pooled)
+    t = make_tiny(28, kv_heads=2, qk_norm="head")
+    dec = _build(m, t)
+    prompts = [[4, 8, 15, 16], [23, 42], [7, 1, 7, 1, 7, 1]]
+    ref = GenericBackend(dec, max_seqs=3, max_len=32)
+    be = GenericBackend(dec, max_seqs=3, max_len=32, pool=True)
+    a, b = [list(p) for p in prompts], [list(p) for p in prompts]
+    for _ in range(3):
+        for s, tok in zip(a, ref.generate_batch([(s, {"temperature": 0.0}) for s in a])):
+            s.append(tok)
+        for s, tok in zip(b, be.generate_batch([(s, {"temperature": 0.0}) for s in b])):
+            s.append(tok)
+    assert a == b
+    assert calls and set(calls) == {3}
+    assert sorted(s.cache.slot for s in be._seqs) == [0, 1, 2]
+    np.testing.assert_allclose(be.logits_for(b[0]).numpy(), ref.logits_for(a[0]).numpy(), rtol=5e-3, atol=5e-3)
+    be.logits_for([9, 9, 9])  # a new request takes the least recently used slot
+    assert sorted(s.cache.slot for s in be._seqs) == [0, 1, 2]
+    with pytest.raises(ValueError):
+        dec.forward_batch([([1], be._pool.cache(1), None), ([2], be._pool.cache(1), None)])
+    with pytest.raises(ValueError):
+        be._pool.cache(3)
