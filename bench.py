@@ -542,7 +542,9 @@ MLA_WORKLOADS = {"cfg2_mla_decode": (64, 16, 1, 4096)}
 # layer, GQA 32 / 4 heads of 128, 48 layers, vocab 151936), `batch` requests with `prompt`-token
 # prompts, one generate_batch call per step
 ENGINE_WORKLOADS = {"cfg3_engine_decode": {"moe": "cfg3", "layers": 48, "heads": 32, "kv_heads": 4, "head_dim": 128,
-                                           "vocab": 151936, "batch": 8, "prompt": 512}}
+                                           "vocab": 151936, "batch": 8, "prompt": 512, "pool": False}}
+# the same with the requests' caches in one pool: one attention launch per layer and step
+ENGINE_WORKLOADS["cfg3_engine_decode_pool"] = dict(ENGINE_WORKLOADS["cfg3_engine_decode"], pool=True)
 
 
 def run_attn(args, wl) -> None:
@@ -710,7 +712,7 @@ def run_engine(args, wl) -> None:
     dec = MoeDecoder(torch.randn((w["vocab"], H), generator=g, device=dev), layers, norm_w(H), mat(w["vocab"], H),
                      inv_freq=inv, attention_factor=af, device=dev)
     B, P = w["batch"], w["prompt"]
-    be = GenericBackend(dec, max_seqs=B, max_len=P + args.warmup + args.steps + 8, prefill_chunk=P)
+    be = GenericBackend(dec, max_seqs=B, max_len=P + args.warmup + args.steps + 8, prefill_chunk=P, pool=w["pool"])
     rng = np.random.default_rng(0)
     seqs = [[int(x) for x in rng.integers(0, w["vocab"], P)] for _ in range(B)]
     greedy = {"temperature": 0.0}
@@ -739,7 +741,8 @@ def run_engine(args, wl) -> None:
         "metric": "engine decode tokens/s", "value": B * K / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": K,
         "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16 activations, AWQ int4 experts, f32 accumulate", "data": "synthetic (seeded torch generator)",
-        "config": {"workload": wl, "layers": w["layers"], "batch": B, "prompt": P, "moe": w["moe"], "heads": nh,
+        "config": {"workload": wl, "layers": w["layers"], "batch": B, "prompt": P, "moe": w["moe"], "pool": w["pool"],
+                   "heads": nh,
                    "kv_heads": kvh, "head_dim": d, "vocab": w["vocab"],
                    "l2": "expert weights of every layer exceed the 126 MB L2, no flush"},
         "e2e": {"value": B * K / wall, "unit": "tokens/s", "h2d_bytes_per_step": B * 8 * 2,
