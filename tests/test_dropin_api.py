@@ -72,3 +72,47 @@ def test_unknown_format_is_not_implemented():
 def test_tile_multiples_required():
     with pytest.raises(ValueError):
         quant.AwqInt4G128Method(100, 128)
+
+
+def test_expert_pipeline_host_side():
+    """ccut_b200.experts keeps the reference pipeline's names (ccut/experts/pipeline.py): the
+    step signature, the metrics dict, the routing history's prediction rule, and the argument
+    checks, which run before any GPU work."""
+    import types
+
+    from ccut_b200 import experts
+
+    assert list(inspect.signature(experts.ExpertPipeline.step).parameters) == [
+        "self", "layer", "x", "gate_w", "top_k", "norm_topk_prob", "shared_projs", "shared_gate"]
+    assert list(inspect.signature(experts.ExpertPipeline.__init__).parameters) == [
+        "self", "reader", "num_workers", "speculative_window", "prefetch_steps_ahead", "metrics_enabled"]
+    m = experts.PipelineMetrics()
+    assert set(m.to_dict()) == {"compute_ns", "prefetch_ns", "overlap_ns", "overlap_ratio", "steps",
+                                "spec_accept_rate", "ring_hits", "ring_misses"}
+    assert m.overlap_ratio() == 0.0 and m.speculative_accept_rate() == 0.0
+    h = experts.RouteHistory(window=3)
+    assert h.predict(2) == []
+    for s in ([1, 2, 3], [2, 3, 4], [3, 5]):
+        h.record(s)
+    assert h.predict(2) == [3, 2]
+    h.record([9])  # the window drops [1, 2, 3]
+    assert h.predict(1) == [3] and 1 not in h.predict(10)
+    t = experts.RouteHistory(window=2)
+    t.record([7])
+    t.record([8])
+    assert t.predict(2) == [7, 8]  # a tie keeps the order of first counting
+    layer = types.SimpleNamespace(top_k=2, routing="softmax_topk", num_slices=0, router=np.zeros((8, 128), np.float32),
+                                  hidden=128, device="cuda")
+    pipe = experts.ExpertPipeline({0: layer})
+    x, gw = np.zeros((2, 128), np.float32), np.zeros((8, 128), np.float32)
+    with pytest.raises(ValueError):
+        pipe.step(0, x, gw, top_k=3, norm_topk_prob=False)
+    with pytest.raises(ValueError):
+        pipe.step(0, x, gw, top_k=2, norm_topk_prob=True)
+    with pytest.raises(ValueError):
+        pipe.step(0, x, gw, top_k=2, norm_topk_prob=False, shared_projs={"gate_proj": None})
+    with pytest.raises(ValueError):
+        pipe.step(0, x, np.zeros((4, 128), np.float32), top_k=2, norm_topk_prob=False)
+    with pytest.raises(KeyError):
+        pipe.step(1, x, gw, top_k=2, norm_topk_prob=False)
+    pipe.close()
