@@ -12,6 +12,7 @@ Public entry points
 ``ep.ExpertParallelMoeLayer`` the same layer with routed experts sharded over GPUs (NCCL)
 ``blocks.moe``               drop-ins for ``ccut.blocks.moe`` / ``ccut.models.generic.moe_forward``
 ``experts``                  drop-in for ``ccut.experts.pipeline.ExpertPipeline`` over resident layers
+``config``                   the reference's ``[experts]`` / ``[quant]`` settings read for this path
 ``quant``                    ``QuantizeMethodBase``-compatible AWQ-int4-g128 / FP8-block-128 methods
 ``checkpoint``               ``load_moe_layer``: a MoE layer of an AWQ / FP8-block safetensors
                              checkpoint into HBM

@@ -526,14 +526,15 @@ def load_decoder_weights(model_dir: str | Path, names: DecoderNames | None = Non
 
 
 def load_decoder(model_dir: str | Path, device="cuda", kernel: str = "auto", names: DecoderNames | None = None,
-                 quantized_projections: bool = True):
+                 quantized_projections: bool = True, app_config=None):
     """``MoeDecoder`` of a whole checkpoint: every layer's MoE experts packed into HBM
     (``MoeLayer``) or its dense MLP (``DenseFfn``).  Quantized attention projections stay in
     their format (``quant.QuantLinear``, run by ``ccut_quant_linear``), or with
     ``quantized_projections=False`` are dequantized on the device (``quant.dequantize``) and
     kept as bf16 for cuBLAS.  RoPE from ``rope_theta`` / ``rope_scaling`` (none or linear;
     other scalings raise ``NotImplementedError``: build the ``MoeDecoder`` with
-    ``build_rope``'s table)."""
+    ``build_rope``'s table).  ``app_config``: the engine's config (``[experts]`` / ``[quant]``,
+    ``ccut_b200.config``), checked against the checkpoint before anything is uploaded."""
     import torch
 
     from ccut_b200.dense import DenseFfn
@@ -541,6 +542,10 @@ def load_decoder(model_dir: str | Path, device="cuda", kernel: str = "auto", nam
     from ccut_b200.model import DecoderLayer, MoeDecoder, rope_table
     from ccut_b200.quant import QuantLinear, dequantize
 
+    if app_config is not None:  # the engine's [experts] / [quant] settings, checked before any upload
+        from ccut_b200.config import resolve
+
+        resolve(app_config, CheckpointReader(model_dir).config)
     w = load_decoder_weights(model_dir, names)
     spec = w["spec"]
     inv_freq, attn_factor = rope_table(spec.head_dim, spec.rope_theta, spec.rope_scaling)

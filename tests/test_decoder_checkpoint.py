@@ -110,3 +110,14 @@ def test_cat_checkpoint_tensors(fmt):
     assert np.array_equal(inputs.dequant(fused), want)
     with pytest.raises(NotImplementedError):
         cat_checkpoint_tensors("int8", dicts)
+
+
+def test_load_decoder_checks_engine_config_first(tmp_path):
+    """The engine's [quant] / [experts] settings are checked before any weight is uploaded."""
+    t = make_tiny(45, kv_heads=2, qk_norm=None, layers=1)
+    q = quantized_layers(t, "fp8_b128", seed=45)
+    root = write_decoder_checkpoint(tmp_path / "m", t, "fp8_b128", q)
+    with pytest.raises(NotImplementedError):
+        ck.load_decoder(root, app_config={"quant": {"quantization": "mxfp8"}})
+    with pytest.raises(ValueError):
+        ck.load_decoder(root, app_config={"experts": {"expert_ring_slots": 0}})
