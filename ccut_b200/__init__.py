@@ -10,6 +10,7 @@ Public entry points
                              ``permute``, ``expert_ffn``, ``gate_up``, ``down``, ``combine``,
                              ``dequant``
 ``ep.ExpertParallelMoeLayer`` the same layer with routed experts sharded over GPUs (NCCL)
+``ep_a2a.AllToAllMoeLayer``  expert parallelism exchanging only the routed rows (all-to-all)
 ``blocks.moe``               drop-ins for ``ccut.blocks.moe`` / ``ccut.models.generic.moe_forward``
 ``experts``                  drop-in for ``ccut.experts.pipeline.ExpertPipeline`` over resident layers
 ``config``                   the reference's ``[experts]`` / ``[quant]`` settings read for this path
