@@ -20,7 +20,14 @@ each layer computes
 ``h += ffn(rms_norm(h, ln2))``        ``MoeLayer`` / ``DenseFfn`` (bf16 in, fp32 out)
 ====================================  ==================================================
 
-and the step ends with ``logits = rms_norm(h, final_norm) @ lm_head^T`` in fp32 (``lm_head``
+``MlaDecoderLayer`` is the same layer with multi-head latent attention (DeepSeek-V2 / V3,
+the reference's MLA blocks ``ccut/blocks/attn_mla.py`` assembled into a layer): one GEMM
+gives ``q`` (or ``q_a``) and ``kv_a = [c, k_pe]``, ``c`` goes through ``kv_a_layernorm``,
+RoPE turns ``q_pe`` / ``k_pe`` only, the cache keeps one bf16 row ``[c, k_pe_rot]`` (576
+elements) per position, and ``ccut_mla_attention`` runs in the latent space between two
+batched GEMMs (``q_nope`` folded through ``k_up``, the output unfolded through ``v_up``).
+
+The step ends with ``logits = rms_norm(h, final_norm) @ lm_head^T`` in fp32 (``lm_head``
 is kept as an fp32 copy).  ``forward_batch`` runs several sequences in one pass: their tokens
 are stacked for the projections, norms, RoPE (each token at its own position) and the FFN, so
 a MoE block reads its experts once for the whole batch; attention runs per sequence over its
@@ -39,12 +46,13 @@ import torch
 import torch.nn.functional as F
 
 from ccut_b200 import _lib
+from ccut_b200.blocks.attn_mla import _latent_attention as _mla_attend
 from ccut_b200.blocks.norm import rms_norm
 from ccut_b200.blocks.rope import apply_rope
 from ccut_b200.layer import _ptr, _stream
 from ccut_b200.quant import QuantLinear
 
-__all__ = ["DecoderLayer", "KvCache", "KvPool", "MoeDecoder", "rope_table"]
+__all__ = ["DecoderLayer", "KvCache", "KvPool", "MlaDecoderLayer", "MoeDecoder", "rope_table"]
 
 
 def rope_table(head_dim: int, rope_theta: float, rope_scaling: dict | None = None) -> tuple[np.ndarray, float]:
@@ -85,13 +93,14 @@ def _project(w, x: torch.Tensor) -> torch.Tensor:
 
 class KvCache:
     """One sequence's bf16 k (rotated) / v cache, ``[layers, kv_heads, max_len, head_dim]`` each;
-    ``length`` positions are valid."""
+    ``length`` positions are valid.  ``values=False`` keeps k only (``v`` None): the latent cache
+    of MLA layers, ``[layers, 1, max_len, kv_lora_rank + qk_rope_head_dim]``."""
 
-    def __init__(self, layers: int, kv_heads: int, max_len: int, head_dim: int, device="cuda"):
+    def __init__(self, layers: int, kv_heads: int, max_len: int, head_dim: int, device="cuda", values: bool = True):
         if max_len <= 0:
             raise ValueError("max_len must be positive")
         self.k = torch.zeros((layers, kv_heads, max_len, head_dim), dtype=torch.bfloat16, device=device)
-        self.v = torch.zeros_like(self.k)
+        self.v = torch.zeros_like(self.k) if values else None
         self.max_len = int(max_len)
         self.length = 0
         self.pool, self.slot = None, -1
@@ -216,6 +225,15 @@ class DecoderLayer:
         self.ffn = ffn
         self.device = dev
 
+    @property
+    def cache_layout(self) -> tuple:
+        """What this layer keeps per position: ``(kind, kv_heads, width)``."""
+        return ("gqa", self.kv_heads, self.head_dim)
+
+    @property
+    def rope_dim(self) -> int:
+        return self.head_dim
+
     def _norm_w(self, w, n: int, dev, name: str):
         if w is None:
             return None
@@ -272,6 +290,143 @@ class DecoderLayer:
         return h + self.ffn.forward(x2, out_dtype=torch.float32)
 
 
+def _fuse_inputs(parts: list):
+    """Projections of the same input run as one: bf16 weights concatenated (one cuBLAS GEMM),
+    ``QuantLinear`` ones fused into one, else the list (``_project`` runs each)."""
+    if all(isinstance(p, torch.Tensor) for p in parts):
+        return torch.cat(parts, 0).contiguous()
+    if all(isinstance(p, QuantLinear) for p in parts):
+        return QuantLinear.cat(parts)
+    return list(parts)
+
+
+def _weight(m, shape: tuple, dev, name: str, projection_ok: bool = True):
+    """A bf16 ``[out, in]`` weight of ``shape`` or a projection object mapping ``in`` to ``out``."""
+    if _is_projection(m):
+        if not projection_ok:
+            raise ValueError(f"{name} must be a dense matrix")
+        if (m.out_features, m.in_features) != shape:
+            raise ValueError(f"{name} must map {shape[1]} to {shape[0]} features, got {m.in_features} -> "
+                             f"{m.out_features}")
+        return m
+    t = _tensor(m, dev, torch.bfloat16)
+    if tuple(t.shape) != shape:
+        raise ValueError(f"{name} must be {shape}, got {tuple(t.shape)}")
+    return t
+
+
+class MlaDecoderLayer:
+    """One multi-head latent attention decoder layer (DeepSeek-V2 / V3).
+
+    Checkpoint ``[out, in]`` matrices (converted to bf16) or projection objects
+    (``quant.QuantLinear``): ``wq`` = ``q_proj`` [heads * (d_nope + d_rope), H], or with
+    ``q_a`` / ``q_a_norm`` (``q_a_proj`` [q_rank, H] and its RMSNorm) the ``q_b_proj``
+    [heads * (d_nope + d_rope), q_rank]; ``wkv_a`` = ``kv_a_proj_with_mqa`` [rank + d_rope, H];
+    ``wkv_b`` = ``kv_b_proj`` [heads * (d_nope + d_v), rank], per head ``d_nope`` rows of k then
+    ``d_v`` rows of v (a dense matrix: its blocks are kept as fp32 ``k_up`` [heads, d_nope, rank]
+    and ``v_up`` [heads, rank, d_v] for the batched GEMMs around the kernel); ``wo`` =
+    ``o_proj`` [H, heads * d_v]; ``kv_norm`` = ``kv_a_layernorm`` [rank] or None.
+    ``softmax_scale`` None is ``(d_nope + d_rope) ** -0.5``.  ``ccut_mla_attention`` takes
+    ``kv_lora_rank`` 512 and ``qk_rope_head_dim`` 64; other sizes raise ``NotImplementedError``."""
+
+    def __init__(self, ln1, wq, wkv_a, wkv_b, wo, ln2, ffn, kv_norm=None, *, heads: int, qk_nope_head_dim: int,
+                 qk_rope_head_dim: int, v_head_dim: int, kv_lora_rank: int = 512, q_a=None, q_a_norm=None,
+                 softmax_scale: float | None = None, device="cuda"):
+        dev = torch.device(device)
+        if (kv_lora_rank, qk_rope_head_dim) != (512, 64):
+            raise NotImplementedError(f"MLA with kv_lora_rank {kv_lora_rank} / qk_rope_head_dim {qk_rope_head_dim} "
+                                      "(have 512 / 64)")
+        H_, dn, dr, dv, R = int(heads), int(qk_nope_head_dim), int(qk_rope_head_dim), int(v_head_dim), 512
+        if H_ <= 0 or dn <= 0 or dv <= 0:
+            raise ValueError("heads, qk_nope_head_dim and v_head_dim must be positive")
+        self.heads, self.d_nope, self.d_rope, self.d_v, self.rank = H_, dn, dr, dv, R
+        self.ln1, self.ln2 = _tensor(ln1, dev, torch.float32), _tensor(ln2, dev, torch.float32)
+        H = self.ln1.numel()
+        if self.ln2.numel() != H:
+            raise ValueError("ln1 and ln2 must have the same size")
+        self.hidden = H
+        if (q_a is None) != (q_a_norm is None):
+            raise ValueError("q_a and q_a_norm go together")
+        self.q_rank = 0
+        if q_a is not None:
+            self.q_rank = int(q_a.out_features if _is_projection(q_a) else np.shape(q_a)[0])
+            q_a = _weight(q_a, (self.q_rank, H), dev, "q_a")
+            self.q_a_norm = _tensor(q_a_norm, dev, torch.float32)
+            if self.q_a_norm.numel() != self.q_rank:
+                raise ValueError(f"q_a_norm must have {self.q_rank} elements")
+        wq = _weight(wq, (H_ * (dn + dr), self.q_rank or H), dev, "wq")
+        wkv_a = _weight(wkv_a, (R + dr, H), dev, "wkv_a")
+        self.w_in = _fuse_inputs([q_a if q_a is not None else wq, wkv_a])
+        self.wq_b = wq if q_a is not None else None
+        b = _tensor(wkv_b, dev, torch.float32) if not _is_projection(wkv_b) else None
+        if b is None or tuple(b.shape) != (H_ * (dn + dv), R):
+            raise ValueError(f"wkv_b must be a dense [{H_ * (dn + dv)}, {R}] matrix")
+        b = b.view(H_, dn + dv, R)
+        self.k_up = b[:, :dn].contiguous()  # [heads, d_nope, rank]
+        self.v_up = b[:, dn:].transpose(1, 2).contiguous()  # [heads, rank, d_v]
+        self.wo = _weight(wo, (H, H_ * dv), dev, "wo")
+        self.kv_norm = None
+        if kv_norm is not None:
+            self.kv_norm = _tensor(kv_norm, dev, torch.float32)
+            if self.kv_norm.numel() != R:
+                raise ValueError(f"kv_norm must have {R} elements")
+        self.scale = float(softmax_scale) if softmax_scale is not None else float((dn + dr) ** -0.5)
+        if not self.scale > 0:
+            raise ValueError("softmax_scale must be positive")
+        self.ffn = ffn
+        self.device = dev
+
+    @property
+    def cache_layout(self) -> tuple:
+        return ("mla", 1, self.rank + self.d_rope)
+
+    @property
+    def rope_dim(self) -> int:
+        return self.d_rope
+
+    def forward(self, h: torch.Tensor, spans: list, layer: int, rope: "_Rope", pooled=None) -> torch.Tensor:
+        """h [N, H] fp32 -> [N, H] fp32, as ``DecoderLayer.forward``; each span writes its
+        latent rows at ``start .. start + n - 1`` of ``layer`` and attends over rows ``0 ..
+        start + n - 1`` with ``causal_start = start``."""
+        if pooled is not None:
+            raise NotImplementedError("MLA layers keep one cache per sequence (no pooled attention)")
+        N = h.shape[0]
+        H, dn, dr, dv, R = self.heads, self.d_nope, self.d_rope, self.d_v, self.rank
+        x = rms_norm(h, self.ln1, rope.eps).to(torch.bfloat16)
+        proj = _project(self.w_in, x)
+        if self.wq_b is not None:
+            qa = rms_norm(proj[:, : self.q_rank].contiguous(), self.q_a_norm, rope.eps)
+            q = _project(self.wq_b, qa.to(torch.bfloat16))
+        else:
+            q = proj[:, : H * (dn + dr)]
+        q = q.reshape(N, H, dn + dr)
+        kv_a = proj[:, -(R + dr):]
+        c = kv_a[:, :R].contiguous()
+        if self.kv_norm is not None:
+            c = rms_norm(c, self.kv_norm, rope.eps)
+        if len(spans) == 1:
+            s = spans[0]
+            pos = torch.arange(s.start, s.start + s.n, dtype=torch.int32, device=h.device)
+        else:
+            pos = torch.cat([torch.arange(s.start, s.start + s.n, dtype=torch.int32) for s in spans]).to(h.device)
+        q_pe, k_pe = apply_rope(q[:, :, dn:].transpose(0, 1).unsqueeze(0).contiguous(),
+                                kv_a[:, R:].reshape(1, 1, N, dr).contiguous(), rope.inv_freq, pos.reshape(1, N),
+                                rope.attn_factor, rope.scaling_type)
+        for s in spans:
+            rows = s.cache.k[layer, 0, s.start: s.start + s.n]
+            rows[:, :R] = c[s.off: s.off + s.n]
+            rows[:, R:] = k_pe[0, 0, s.off: s.off + s.n]
+        q_lat = torch.bmm(q[:, :, :dn].float().transpose(0, 1), self.k_up)  # [heads, N, rank]
+        qq = torch.cat([q_lat.transpose(0, 1), q_pe[0].transpose(0, 1).float()], dim=-1).contiguous()  # [N, H, 576]
+        o_lat = torch.cat([_mla_attend(qq[s.off: s.off + s.n], s.cache.k[layer, 0, : s.start + s.n], s.start,
+                                       self.scale).view(s.n, H, R) for s in spans])
+        o = torch.bmm(o_lat.transpose(0, 1), self.v_up)  # [heads, N, d_v]
+        o2 = o.transpose(0, 1).reshape(N, H * dv).to(torch.bfloat16)
+        h = h + _project(self.wo, o2).float()
+        x2 = rms_norm(h, self.ln2, rope.eps).to(torch.bfloat16)
+        return h + self.ffn.forward(x2, out_dtype=torch.float32)
+
+
 class _Span:
     """One sequence's part of a batch: ``n`` tokens at rows ``off ..`` of the batch, positions
     ``start ..`` of ``cache``."""
@@ -291,7 +446,8 @@ class _Rope:
 class MoeDecoder:
     """Embedding, decoder layers, final norm and ``lm_head`` of one model.
 
-    ``embed`` / ``lm_head`` [vocab, H]; ``inv_freq`` / ``attention_factor`` / ``scaling_type``
+    ``layers``: ``DecoderLayer`` or ``MlaDecoderLayer`` objects, all of one kind (the cache
+    layout is the model's).  ``embed`` / ``lm_head`` [vocab, H]; ``inv_freq`` / ``attention_factor`` / ``scaling_type``
     as ``build_rope`` returns them (``rope_table`` for the plain cases); ``eps`` the epsilon of
     every RMSNorm (the reference's layer calls ``rms_norm`` with its default, 1e-6); ``softcap``
     the model's ``attn_logit_softcapping`` (or None)."""
@@ -308,23 +464,28 @@ class MoeDecoder:
         if tuple(self.lm_head.shape) != (V, H) or self.final_norm.numel() != H:
             raise ValueError(f"lm_head must be {(V, H)} and final_norm [{H}]")
         for i, lay in enumerate(layers):
-            if lay.hidden != H or (lay.kv_heads, lay.head_dim) != (layers[0].kv_heads, layers[0].head_dim):
+            if lay.hidden != H or lay.cache_layout != layers[0].cache_layout or lay.rope_dim != layers[0].rope_dim:
                 raise ValueError(f"layer {i} does not match the model's hidden size / kv layout")
         self.layers = list(layers)
         self.vocab, self.hidden = V, H
+        self.layout = layers[0].cache_layout
         ft = _tensor(inv_freq, dev, torch.float32)
-        if ft.numel() != layers[0].head_dim // 2:
-            raise ValueError(f"inv_freq has {ft.numel()} entries for head dim {layers[0].head_dim}")
+        if ft.numel() != layers[0].rope_dim // 2:
+            raise ValueError(f"inv_freq has {ft.numel()} entries for rope dim {layers[0].rope_dim}")
+        if self.layout[0] == "mla" and softcap:
+            raise NotImplementedError("attention logit soft-capping in MLA layers")
         self.rope = _Rope(ft, attention_factor, scaling_type, eps, softcap)
         self.device = dev
 
     def new_cache(self, max_len: int) -> KvCache:
-        l0 = self.layers[0]
-        return KvCache(len(self.layers), l0.kv_heads, max_len, l0.head_dim, self.device)
+        kind, kvh, width = self.layout
+        return KvCache(len(self.layers), kvh, max_len, width, self.device, values=kind == "gqa")
 
     def new_pool(self, slots: int, max_len: int) -> KvPool:
-        l0 = self.layers[0]
-        return KvPool(slots, len(self.layers), l0.kv_heads, max_len, l0.head_dim, self.device)
+        kind, kvh, width = self.layout
+        if kind != "gqa":
+            raise NotImplementedError("pooled caches for MLA layers")
+        return KvPool(slots, len(self.layers), kvh, max_len, width, self.device)
 
     def _ids(self, tokens) -> torch.Tensor:
         if isinstance(tokens, torch.Tensor):

@@ -1,7 +1,8 @@
 """Seeded tiny decoder models for the engine-wiring tests (test fixtures).
 
 ``make_tiny(seed, ...)`` draws from ``numpy.random.default_rng(seed)``, in this order: the
-embedding; per layer the attention weights (``oracle.model.AttnWeights``), a router and the
+embedding; per layer the attention weights (``oracle.model.AttnWeights``, or with ``mla`` the
+latent-attention weights ``oracle.model.MlaWeights``), a router and the
 dense experts of a MoE block (``[in, out]`` like ``expert_ffn`` takes them) plus one shared
 expert; then the final norm and ``lm_head``.  Every matrix is bf16-representable (fp32
 draws rounded to bf16), the router stays fp32.  The GPU kernels take quantized experts, so
@@ -16,7 +17,7 @@ from dataclasses import dataclass, field
 import numpy as np
 
 from oracle import inputs, model
-from oracle.model import AttnWeights, DecoderSpec
+from oracle.model import AttnWeights, DecoderSpec, MlaWeights
 
 
 def _bf16(a: np.ndarray) -> np.ndarray:
@@ -48,6 +49,7 @@ class TinyModel:
     router: list = field(repr=False)
     experts: list = field(repr=False)  # [layer][expert] = (wg [H, I], wu [H, I], wd [I, H])
     shared: list = field(repr=False)  # [layer] = (sg, su, sd) or None
+    mla: dict | None = None  # the MLA sizes, when the layers are MLA layers
 
     @property
     def layers(self) -> int:
@@ -57,8 +59,12 @@ class TinyModel:
     def mode(self) -> str:
         return "topk_softmax" if self.norm_topk_prob else "softmax_topk"
 
+    @property
+    def rope_dim(self) -> int:
+        return self.mla["d_rope"] if self.mla else self.head_dim
+
     def spec(self, inv_freq: np.ndarray | None = None) -> DecoderSpec:
-        f = rope_inv_freq(self.head_dim, self.theta) if inv_freq is None else np.asarray(inv_freq, np.float32)
+        f = rope_inv_freq(self.rope_dim, self.theta) if inv_freq is None else np.asarray(inv_freq, np.float32)
         return DecoderSpec(self.hidden, self.heads, self.kv_heads, self.head_dim, f, eps=self.eps)
 
     def dense_ffns(self) -> list:
@@ -69,8 +75,10 @@ class TinyModel:
 def make_tiny(seed: int = 0, vocab: int = 512, hidden: int = 256, heads: int = 4, kv_heads: int = 1,
               head_dim: int = 64, layers: int = 2, num_experts: int = 8, top_k: int = 2, inter: int = 128,
               shared_inter: int = 128, norm_topk_prob: bool = False, qk_norm: str | None = "flat",
-              theta: float = 10000.0, eps: float = 1e-6) -> TinyModel:
-    """qk_norm: None, ``"flat"`` (weights over the whole q / k projection) or ``"head"``."""
+              theta: float = 10000.0, eps: float = 1e-6, mla: dict | None = None) -> TinyModel:
+    """qk_norm: None, ``"flat"`` (weights over the whole q / k projection) or ``"head"``.
+    ``mla``: MLA layers instead, ``{"rank", "d_nope", "d_rope", "d_v"}`` and optionally
+    ``"q_rank"`` (a q_a / q_b pair) and ``"kv_norm"`` (False: no ``kv_a_layernorm``)."""
     rng = np.random.default_rng(seed)
     H, d = hidden, head_dim
 
@@ -84,15 +92,29 @@ def make_tiny(seed: int = 0, vocab: int = 512, hidden: int = 256, heads: int = 4
     attn, router, experts, shared = [], [], [], []
     for _ in range(layers):
         ln1 = norm_w(H)
-        wq, wk, wv = mat(heads * d, H), mat(kv_heads * d, H), mat(kv_heads * d, H)
-        wo = mat(H, heads * d)
-        ln2 = norm_w(H)
-        qn = kn = None
-        if qk_norm == "flat":
-            qn, kn = norm_w(heads * d), norm_w(kv_heads * d)
-        elif qk_norm == "head":
-            qn, kn = norm_w(d), norm_w(d)
-        attn.append(AttnWeights(ln1, wq, wk, wv, wo, ln2, qn, kn))
+        if mla:
+            R, dn, dr, dv = mla["rank"], mla["d_nope"], mla["d_rope"], mla["d_v"]
+            qr = mla.get("q_rank")
+            wq_a = mat(qr, H) if qr else None
+            q_a_norm = norm_w(qr) if qr else None
+            wq = mat(heads * (dn + dr), qr or H)
+            wkv_a = mat(R + dr, H)
+            kv_norm = norm_w(R) if mla.get("kv_norm", True) else None
+            wkv_b = mat(heads * (dn + dv), R)
+            wo = mat(H, heads * dv)
+            ln2 = norm_w(H)
+            attn.append(MlaWeights(ln1, wq, wkv_a, wkv_b, wo, ln2, heads, dn, dr, dv, kv_norm, wq_a, q_a_norm,
+                                   mla.get("scale")))
+        else:
+            wq, wk, wv = mat(heads * d, H), mat(kv_heads * d, H), mat(kv_heads * d, H)
+            wo = mat(H, heads * d)
+            ln2 = norm_w(H)
+            qn = kn = None
+            if qk_norm == "flat":
+                qn, kn = norm_w(heads * d), norm_w(kv_heads * d)
+            elif qk_norm == "head":
+                qn, kn = norm_w(d), norm_w(d)
+            attn.append(AttnWeights(ln1, wq, wk, wv, wo, ln2, qn, kn))
         router.append((rng.standard_normal((num_experts, H), dtype=np.float32) * np.float32(0.1)).astype(np.float32))
         # [in, out]: gate / up [H, I], down [I, H]
         experts.append([(mat(inter, H).T.copy(), mat(inter, H).T.copy(), mat(H, inter).T.copy())
@@ -102,7 +124,11 @@ def make_tiny(seed: int = 0, vocab: int = 512, hidden: int = 256, heads: int = 4
     final_norm = norm_w(H)
     lm_head = mat(vocab, H)
     return TinyModel(vocab, hidden, heads, kv_heads, head_dim, num_experts, top_k, inter, shared_inter,
-                     norm_topk_prob, theta, eps, embed, lm_head, final_norm, attn, router, experts, shared)
+                     norm_topk_prob, theta, eps, embed, lm_head, final_norm, attn, router, experts, shared,
+                     dict(mla) if mla else None)
+
+
+MLA_TINY = {"rank": 512, "d_nope": 32, "d_rope": 64, "d_v": 48}
 
 
 def quantized_layers(tiny: TinyModel, fmt: str, seed: int = 1) -> list:

@@ -16,7 +16,9 @@ import numpy as np
 import pytest
 import torch
 
-from tests.model_helpers import make_tiny, rope_inv_freq
+import json
+
+from tests.model_helpers import MLA_TINY, make_tiny, rope_inv_freq
 from oracle import model as omodel
 
 
@@ -39,6 +41,30 @@ def test_oracle_decoder_matches_reference_layer(golden_dir):
             for i in range(t.layers):
                 np.testing.assert_allclose(hs[i][0], g[f"m{ci}_h"][s, i], rtol=1e-5, atol=1e-5)
             np.testing.assert_allclose(lg[0], g[f"m{ci}_logits"][s], rtol=1e-5, atol=1e-5)
+
+
+def _golden_mla(g, ci):
+    return make_tiny(int(g[f"c{ci}_seed"]), norm_topk_prob=bool(g[f"c{ci}_norm"]), mla=json.loads(str(g[f"c{ci}_mla"])))
+
+
+def test_oracle_mla_decoder_matches_reference_blocks(golden_dir):
+    """oracle.model's MLA layer against the reference's MLA blocks assembled into a layer
+    (tests/golden/make_golden_mla_model.py): a prefill chunk, single-token steps and a second
+    chunk, with and without kv_a_layernorm, with a q_a / q_b pair and an explicit scale."""
+    g = np.load(golden_dir / "mla_decoder.npz")
+    for ci in range(2):
+        t = _golden_mla(g, ci)
+        spec = t.spec(g[f"c{ci}_inv_freq"])
+        cache, ffns = omodel.KvCache(), t.dense_ffns()
+        tokens, pos = g[f"c{ci}_tokens"], 0
+        for n in g["chunks"]:
+            lg, hs = omodel.model_forward(tokens[pos: pos + n], t.embed, t.attn, ffns, t.final_norm, t.lm_head, spec,
+                                          cache, pos)
+            for i in range(t.layers):
+                np.testing.assert_allclose(hs[i], g[f"c{ci}_h"][pos: pos + n, i], rtol=2e-5, atol=2e-5)
+            np.testing.assert_allclose(lg, g[f"c{ci}_logits"][pos: pos + n], rtol=2e-5, atol=2e-5)
+            pos += int(n)
+        assert cache.k[0].shape == (1, pos, MLA_TINY["rank"]) and cache.v[0].shape == (1, pos, MLA_TINY["d_rope"])
 
 
 def test_rope_tables_match_reference(golden_dir):
@@ -120,6 +146,19 @@ def _attend(q, k, v, start_pos, softcap):
     return torch.einsum("hsl,hld->hsd", p, vv)[None].to(torch.bfloat16)
 
 
+def _mla(q, kv, causal_start, scale):
+    """``ccut_mla_attention`` for one sequence: q fp32 [S, H, 576], kv bf16 [n, 576] -> the
+    latent output [S * H, 512]."""
+    S, H, _ = q.shape
+    n = kv.shape[0]
+    kvf = kv.float()
+    sc = torch.einsum("shk,nk->shn", q.float(), kvf) * scale
+    vis = torch.full((S,), n) if causal_start < 0 else torch.clamp(causal_start + torch.arange(S) + 1, max=n)
+    mask = torch.arange(n)[None, :] >= vis[:, None]
+    p = torch.softmax(sc.masked_fill(mask[:, None, :], float("-inf")), -1)
+    return torch.einsum("shn,nr->shr", p, kvf[:, :512]).reshape(S * H, 512)
+
+
 class _TorchMoe:
     """MoE block with the tiny model's dense experts (softmax routing as the reference)."""
 
@@ -160,6 +199,7 @@ def torch_ops(monkeypatch):
     monkeypatch.setattr(m, "rms_norm", _norm)
     monkeypatch.setattr(m, "apply_rope", _rope)
     monkeypatch.setattr(m, "_attend", _attend)
+    monkeypatch.setattr(m, "_mla_attend", _mla)
     return m
 
 
@@ -169,6 +209,19 @@ def _build(m, t, **kw):
     inv, attn = m.rope_table(t.head_dim, t.theta)
     return m.MoeDecoder(t.embed, layers, t.final_norm, t.lm_head, inv_freq=inv, attention_factor=attn, eps=t.eps,
                         device="cpu", **kw)
+
+
+def _mla_layers(m, t, ffns=None):
+    return [m.MlaDecoderLayer(w.ln1, w.wq, w.wkv_a, w.wkv_b, w.wo, w.ln2, ffns[i] if ffns else _TorchMoe(t, i),
+                              w.kv_norm, heads=w.heads, qk_nope_head_dim=w.d_nope, qk_rope_head_dim=w.d_rope,
+                              v_head_dim=w.d_v, q_a=w.wq_a, q_a_norm=w.q_a_norm, softmax_scale=w.scale, device="cpu")
+            for i, w in enumerate(t.attn)]
+
+
+def _build_mla(m, t, **kw):
+    inv, attn = m.rope_table(t.rope_dim, t.theta)
+    return m.MoeDecoder(t.embed, _mla_layers(m, t), t.final_norm, t.lm_head, inv_freq=inv, attention_factor=attn,
+                        eps=t.eps, device="cpu", **kw)
 
 
 def _rel(a, b):
@@ -460,3 +513,96 @@ def test_backend_pooled_caches_match(torch_ops, monkeypatch):
         dec.forward_batch([([1], be._pool.cache(1), None), ([2], be._pool.cache(1), None)])
     with pytest.raises(ValueError):
         be._pool.cache(3)
+
+
+MLA_VARIANTS = [{}, {"kv_norm": False}, {"q_rank": 128, "scale": 0.09}]
+
+
+@pytest.mark.parametrize("extra", MLA_VARIANTS)
+def test_mla_decoder_host_logic_matches_oracle(torch_ops, extra):
+    """MLA layers (DeepSeek-V2 / V3 latent attention) in MoeDecoder: a 5-token prefill, single
+    steps, a 2-token chunk and a recomputed last position against the oracle's MLA decoder
+    (bf16 at the same points); the cache holds one [c, k_pe] row per position, no values."""
+    m = torch_ops
+    t = make_tiny(41, mla={**MLA_TINY, **extra}, norm_topk_prob=bool(extra))
+    dec = _build_mla(m, t)
+    cache = dec.new_cache(32)
+    assert cache.v is None and tuple(cache.k.shape) == (t.layers, 1, 32, 576)
+    spec, ocache, ffns = t.spec(), omodel.KvCache(), t.dense_ffns()
+    rng = np.random.default_rng(4)
+    pos = 0
+    for n in (5, 1, 1, 2):
+        toks = rng.integers(0, t.vocab, n)
+        got = dec.forward(toks, cache, all_logits=True)
+        ref, _ = omodel.model_forward(toks, t.embed, t.attn, ffns, t.final_norm, t.lm_head, spec, ocache, pos,
+                                      bf16_acts=True)
+        assert got.shape == (n, t.vocab) and _rel(got.numpy(), ref) < 5e-3
+        pos += n
+        assert cache.length == pos
+        # the cached latent rows are the oracle's c and rotated k_pe, in bf16
+        np.testing.assert_allclose(cache.k[0, 0, :pos, :512].float().numpy(), ocache.k[0][0], rtol=1e-2, atol=1e-2)
+        np.testing.assert_allclose(cache.k[0, 0, :pos, 512:].float().numpy(), ocache.v[0][0], rtol=1e-2, atol=1e-2)
+        last = dec.forward(toks[-1:], cache, start_pos=pos - 1)
+        assert _rel(last.numpy(), ref[-1]) < 5e-3
+
+
+def test_mla_decoder_batch_and_backend(torch_ops):
+    """forward_batch over MLA caches equals the sequences run alone; the backend's prefix reuse
+    runs on MLA caches; pooled caches are refused for MLA layers."""
+    from ccut_b200.backend import GenericBackend
+
+    m = torch_ops
+    t = make_tiny(42, mla=MLA_TINY)
+    dec = _build_mla(m, t)
+    rng = np.random.default_rng(9)
+    prompts = [rng.integers(0, t.vocab, n) for n in (4, 1, 7)]
+    singles = [dec.forward(p, dec.new_cache(16), all_logits=True) for p in prompts]
+    got = dec.forward_batch([(p, dec.new_cache(16), None) for p in prompts], all_logits=True)
+    for g, s in zip(got, singles):
+        assert _rel(g.numpy(), s.numpy()) < 5e-3
+    be = GenericBackend(dec, max_seqs=2, max_len=32)
+    prompt = [7, 3, 11, 5]
+    ids = list(prompt)
+    for _ in range(3):
+        ids.append(be.generate_step(ids, {"temperature": 0.0}))
+    assert be.tokens_run == 4 + 2
+    full = dec.forward(ids, dec.new_cache(32))
+    assert _rel(be.logits_for(ids).numpy(), full.numpy()) < 2e-2
+    with pytest.raises(NotImplementedError):
+        GenericBackend(dec, max_seqs=2, max_len=32, pool=True)
+
+
+def test_mla_decoder_checks(torch_ops):
+    m = torch_ops
+    t = make_tiny(43, mla=MLA_TINY)
+    w = t.attn[0]
+    kw = dict(heads=w.heads, qk_nope_head_dim=w.d_nope, qk_rope_head_dim=w.d_rope, v_head_dim=w.d_v, device="cpu")
+    args = (w.ln1, w.wq, w.wkv_a, w.wkv_b, w.wo, w.ln2, None, w.kv_norm)
+    with pytest.raises(NotImplementedError):
+        m.MlaDecoderLayer(*args, **{**kw, "kv_lora_rank": 256})
+    with pytest.raises(NotImplementedError):
+        m.MlaDecoderLayer(*args, **{**kw, "qk_rope_head_dim": 32})
+    with pytest.raises(ValueError):
+        m.MlaDecoderLayer(w.ln1, w.wq, w.wkv_a, w.wkv_b.T, w.wo, w.ln2, None, **kw)  # kv_b_proj transposed
+    with pytest.raises(ValueError):
+        m.MlaDecoderLayer(w.ln1, w.wq, w.wkv_a.T, w.wkv_b, w.wo, w.ln2, None, **kw)
+    with pytest.raises(ValueError):
+        m.MlaDecoderLayer(*args, **{**kw, "v_head_dim": w.d_v + 1})
+    with pytest.raises(ValueError):
+        m.MlaDecoderLayer(w.ln1, w.wq, w.wkv_a, w.wkv_b, w.wo, w.ln2, None, np.ones(3), **kw)
+    with pytest.raises(ValueError):
+        m.MlaDecoderLayer(*args, q_a=np.ones((128, t.hidden)), **kw)  # q_a without its norm
+    with pytest.raises(ValueError):
+        m.MlaDecoderLayer(*args, softmax_scale=0.0, **kw)
+    dec = _build_mla(m, t)
+    with pytest.raises(NotImplementedError):
+        dec.new_pool(2, 16)
+    inv, _ = m.rope_table(64, t.theta)
+    with pytest.raises(NotImplementedError):
+        m.MoeDecoder(t.embed, dec.layers, t.final_norm, t.lm_head, inv_freq=inv, softcap=30.0, device="cpu")
+    with pytest.raises(ValueError):
+        m.MoeDecoder(t.embed, dec.layers, t.final_norm, t.lm_head, inv_freq=np.ones(64), device="cpu")
+    g = make_tiny(44, head_dim=64)
+    gqa = _build(m, g).layers[0]
+    with pytest.raises(ValueError):  # one cache layout per model
+        m.MoeDecoder(t.embed, [dec.layers[0], gqa], t.final_norm, t.lm_head, inv_freq=inv, device="cpu")

@@ -24,12 +24,12 @@ import torch
 from ccut_b200 import dense
 from ccut_b200.backend import GenericBackend
 from ccut_b200.checkpoint import load_decoder
-from ccut_b200.model import DecoderLayer, MoeDecoder, rope_table
+from ccut_b200.model import DecoderLayer, MlaDecoderLayer, MoeDecoder, rope_table
 from oracle import inputs, moe, routing
 from oracle import model as omodel
 from tests.ckpt_helpers import write_decoder_checkpoint
 from tests.gpu_helpers import gpu_layer
-from tests.model_helpers import make_tiny, quantized_attention, quantized_layers
+from tests.model_helpers import MLA_TINY, make_tiny, quantized_attention, quantized_layers
 
 pytestmark = pytest.mark.gpu
 
@@ -125,6 +125,48 @@ def test_decoder_matches_oracle(fmt, kv_heads, qk_norm, head_dim, seed, tseed):
     assert all(not r.routes for r in recs)
     for r in recs:
         assert r.workspace_status() == 0
+
+
+@pytest.mark.parametrize("fmt, extra, seed", [("awq_int4_g128", {}, 35),
+                                              ("fp8_b128", {"q_rank": 128, "kv_norm": False}, 36)])
+def test_mla_decoder_matches_oracle(fmt, extra, seed):
+    """MLA layers (``MlaDecoderLayer``: latent cache rows, ``ccut_mla_attention`` between the
+    ``k_up`` / ``v_up`` GEMMs) with quantized MoE blocks: a 37-token prefill, four single-token
+    steps and a 20-token chunk, the logits of every position against the oracle's MLA decoder
+    (pinned to the reference's MLA blocks)."""
+    t = make_tiny(seed, mla={**MLA_TINY, **extra})
+    qlayers = quantized_layers(t, fmt, seed=seed)
+    recs = [_Recorded(gpu_layer(ol.lw)) for ol in qlayers]
+    offs = [_oracle_moe(ol, t.top_k, t.mode, r) for ol, r in zip(qlayers, recs)]
+    layers = [MlaDecoderLayer(w.ln1, w.wq, w.wkv_a, w.wkv_b, w.wo, w.ln2, r, w.kv_norm, heads=w.heads,
+                              qk_nope_head_dim=w.d_nope, qk_rope_head_dim=w.d_rope, v_head_dim=w.d_v, q_a=w.wq_a,
+                              q_a_norm=w.q_a_norm, softmax_scale=w.scale) for w, r in zip(t.attn, recs)]
+    inv, attn = rope_table(t.rope_dim, t.theta)
+    dec = MoeDecoder(t.embed, layers, t.final_norm, t.lm_head, inv_freq=inv, attention_factor=attn, eps=t.eps)
+    cache = dec.new_cache(512)
+    spec, ocache = t.spec(), omodel.KvCache()
+    rng = np.random.default_rng(seed + 100)
+    pos = 0
+    for n in (37, 1, 1, 1, 1, 20):
+        toks = rng.integers(0, t.vocab, n)
+        got = dec.forward(toks, cache, all_logits=True)
+        torch.cuda.synchronize()
+        assert got.shape == (n, t.vocab) and cache.length == pos + n
+        ref, _ = omodel.model_forward(toks, t.embed, t.attn, offs, t.final_norm, t.lm_head, spec, ocache, pos,
+                                      bf16_acts=True)
+        err = _rel_rows(got.cpu().numpy(), ref)
+        assert err <= LOGITS_TOL, (n, pos, err)
+        pos += n
+    assert all(not r.routes for r in recs)
+    # a batch of two sequences (their MoE tokens together) equals each run alone
+    be = GenericBackend(dec, max_seqs=2, max_len=128)
+    a, b = [int(x) for x in rng.integers(0, t.vocab, 9)], [int(x) for x in rng.integers(0, t.vocab, 3)]
+    for r in recs:
+        r.routes.clear()
+    got = be.logits_batch([a, b])
+    for ids, g in zip((a, b), got):
+        alone = dec.forward(ids, dec.new_cache(128))
+        assert _rel_rows(g.cpu().numpy(), alone.cpu().numpy()) <= LOGITS_TOL
 
 
 def test_decoder_with_dense_layer():
