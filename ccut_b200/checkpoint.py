@@ -390,6 +390,10 @@ class DecoderNames:
     k_norm: str = "model.layers.{layer}.self_attn.k_norm.weight"
     mlp: str = "model.layers.{layer}.mlp.{proj}_proj"
     moe: NameTemplates = NameTemplates()
+    # MLA layers (DeepSeek-V2 / V3): q / q_a / q_b / kv_b / o through ``attn``, and
+    kv_a: str = "model.layers.{layer}.self_attn.kv_a_proj_with_mqa"
+    kv_a_norm: str = "model.layers.{layer}.self_attn.kv_a_layernorm.weight"
+    q_a_norm: str = "model.layers.{layer}.self_attn.q_a_layernorm.weight"
 
 
 @dataclass(frozen=True)
@@ -408,6 +412,7 @@ class DecoderCheckpointSpec:
     tie_word_embeddings: bool
     softcap: float | None
     moe_layers: tuple  # per layer: True for a MoE block, False for a dense MLP
+    mla: dict | None = None  # MLA sizes (``_mla_spec``) when the attention is multi-head latent attention
 
 
 def _is_moe_layer(tc: dict, i: int) -> bool:
@@ -427,13 +432,49 @@ def _is_moe_layer(tc: dict, i: int) -> bool:
     return i % max(1, int(tc.get("moe_layer_freq", 1) or 1)) == 0
 
 
+def _rope_scaling(tc: dict) -> dict | None:
+    """``rope_scaling`` (or the newer ``rope_parameters``) with its kind under ``"type"``; None
+    for plain RoPE."""
+    rs = tc.get("rope_scaling") or tc.get("rope_parameters")
+    if not rs:
+        return None
+    rs = dict(rs)
+    kind = rs.get("type") or rs.get("rope_type")
+    if kind in (None, "default"):
+        return None
+    rs["type"] = kind
+    if kind == "yarn" and rs.get("factor") is None:  # the ratio of the context lengths (DeepSeek-V3 configs)
+        rs["factor"] = float(tc["max_position_embeddings"]) / float(rs["original_max_position_embeddings"])
+    return rs
+
+
+def _mla_spec(tc: dict, rope_scaling: dict | None) -> dict:
+    """The MLA sizes of a DeepSeek-V2 / V3 ``config.json`` and its softmax scale:
+    ``(qk_nope_head_dim + qk_rope_head_dim) ** -0.5``, times ``yarn_mscale(factor,
+    mscale_all_dim) ** 2`` under YaRN scaling with ``mscale_all_dim`` (the models' own attention
+    code).  ``rope_interleave`` (default true): the checkpoint's rope features are stored as
+    interleaved pairs."""
+    from ccut_b200.rope_tables import yarn_mscale
+
+    for key in ("qk_nope_head_dim", "qk_rope_head_dim", "v_head_dim"):
+        if key not in tc:
+            raise KeyError(f"config.json has no {key!r}")
+    dn, dr, dv = int(tc["qk_nope_head_dim"]), int(tc["qk_rope_head_dim"]), int(tc["v_head_dim"])
+    scale = (dn + dr) ** -0.5
+    if rope_scaling and rope_scaling["type"] == "yarn" and rope_scaling.get("mscale_all_dim"):
+        scale *= yarn_mscale(float(rope_scaling["factor"]), float(rope_scaling["mscale_all_dim"])) ** 2
+    return {"kv_lora_rank": int(tc["kv_lora_rank"]), "q_lora_rank": int(tc.get("q_lora_rank") or 0),
+            "qk_nope_head_dim": dn, "qk_rope_head_dim": dr, "v_head_dim": dv, "softmax_scale": float(scale),
+            "rope_interleave": bool(tc.get("rope_interleave", True))}
+
+
 def decoder_spec_from_config(config: dict) -> DecoderCheckpointSpec:
     """Decoder shape of a ``config.json`` (the keys ``ccut/models/spec.py:parse_model_spec``
-    reads).  MLA attention (``kv_lora_rank``) and linear-attention layers raise
-    ``NotImplementedError``: the decoder runs ``full_attn`` GQA layers."""
+    reads, plus the MLA keys of DeepSeek-V2 / V3: ``kv_lora_rank``, ``q_lora_rank``,
+    ``qk_nope_head_dim``, ``qk_rope_head_dim``, ``v_head_dim``).  For MLA models ``head_dim`` is
+    the rope dimension (the size of the RoPE table).  Linear-attention layers raise
+    ``NotImplementedError``."""
     tc = config.get("text_config", config)
-    if tc.get("kv_lora_rank") or tc.get("q_lora_rank"):
-        raise NotImplementedError("MLA attention layers (kv_lora_rank) are not supported by the decoder")
     if tc.get("linear_num_key_heads") or int(tc.get("full_attention_interval", 0) or 0) > 1:
         raise NotImplementedError("linear-attention layers are not supported by the decoder")
     for key in ("hidden_size", "num_hidden_layers", "num_attention_heads", "vocab_size"):
@@ -442,14 +483,68 @@ def decoder_spec_from_config(config: dict) -> DecoderCheckpointSpec:
     hidden, heads = int(tc["hidden_size"]), int(tc["num_attention_heads"])
     L = int(tc["num_hidden_layers"])
     cap = tc.get("attn_logit_softcapping")
+    rs = _rope_scaling(tc)
+    mla = _mla_spec(tc, rs) if tc.get("kv_lora_rank") else None
+    theta = tc.get("rope_theta") or (tc.get("rope_parameters") or {}).get("rope_theta") or 10000.0
     return DecoderCheckpointSpec(
         fmt=quant_format(config), vocab=int(tc["vocab_size"]), hidden=hidden, layers=L, heads=heads,
-        kv_heads=int(tc.get("num_key_value_heads", heads)), head_dim=int(tc.get("head_dim") or hidden // heads),
+        kv_heads=1 if mla else int(tc.get("num_key_value_heads", heads)),
+        head_dim=mla["qk_rope_head_dim"] if mla else int(tc.get("head_dim") or hidden // heads),
         inter=int(tc.get("intermediate_size", 0) or 0), eps=float(tc.get("rms_norm_eps", 1e-6)),
-        rope_theta=float(tc.get("rope_theta", 10000.0)), rope_scaling=tc.get("rope_scaling"),
+        rope_theta=float(theta), rope_scaling=rs,
         tie_word_embeddings=bool(tc.get("tie_word_embeddings", False)), softcap=float(cap) if cap else None,
-        moe_layers=tuple(_is_moe_layer(tc, i) for i in range(L)),
+        moe_layers=tuple(_is_moe_layer(tc, i) for i in range(L)), mla=mla,
     )
+
+
+def _rope_perm(width: int, offsets, d_rope: int) -> np.ndarray:
+    """Output-channel order that turns interleaved rope pairs ``(2i, 2i + 1)`` into the half
+    layout ``(i, i + d_rope / 2)`` that RoPE here rotates, for the ``d_rope`` channels starting
+    at each of ``offsets`` (the other channels stay).  Scores are unchanged: q and k are permuted
+    alike."""
+    perm = np.arange(width, dtype=np.int64)
+    half = np.concatenate([np.arange(0, d_rope, 2), np.arange(1, d_rope, 2)])
+    for off in offsets:
+        perm[off: off + d_rope] = off + half
+    return perm
+
+
+def _permute_rows(m, fmt: str, perm: np.ndarray):
+    """A ``_dense_or_quant`` matrix with its output channels in ``perm`` order."""
+    from ccut_b200.quant import permute_out_channels
+
+    kind, a = m
+    if kind == "dense":
+        return "dense", np.ascontiguousarray(a[perm])
+    return "quant", permute_out_channels(fmt, a, perm)
+
+
+def _mla_attention(rd: CheckpointReader, spec: DecoderCheckpointSpec, names: DecoderNames, i: int) -> dict:
+    """One MLA layer's attention tensors: ``q`` (or ``q_a`` / ``q_a_norm`` / ``q_b``),
+    ``kv_a``, ``kv_a_norm`` (or None), ``kv_b``, ``o``; with ``rope_interleave`` the rope
+    channels of q and of ``kv_a`` are reordered into the half layout."""
+    m, H, nh = spec.mla, spec.hidden, spec.heads
+    dn, dr, dv, R, qr = (m["qk_nope_head_dim"], m["qk_rope_head_dim"], m["v_head_dim"], m["kv_lora_rank"],
+                         m["q_lora_rank"])
+    attn = names.attn.format
+    out = {}
+    q_out = nh * (dn + dr)
+    if qr:
+        out["q_a"] = _dense_or_quant(rd, attn(layer=i, proj="q_a"), spec.fmt, qr, H)
+        out["q_a_norm"] = _vector(rd, names.q_a_norm.format(layer=i), qr)
+        q = _dense_or_quant(rd, attn(layer=i, proj="q_b"), spec.fmt, q_out, qr)
+    else:
+        q = _dense_or_quant(rd, attn(layer=i, proj="q"), spec.fmt, q_out, H)
+    kv_a = _dense_or_quant(rd, names.kv_a.format(layer=i), spec.fmt, R + dr, H)
+    if m["rope_interleave"]:
+        q = _permute_rows(q, spec.fmt, _rope_perm(q_out, [h * (dn + dr) + dn for h in range(nh)], dr))
+        kv_a = _permute_rows(kv_a, spec.fmt, _rope_perm(R + dr, [R], dr))
+    out["q"], out["kv_a"] = q, kv_a
+    name = names.kv_a_norm.format(layer=i)
+    out["kv_a_norm"] = _vector(rd, name, R) if rd.has(name) else None
+    out["kv_b"] = _dense_or_quant(rd, attn(layer=i, proj="kv_b"), spec.fmt, nh * (dn + dv), R)
+    out["o"] = _dense_or_quant(rd, attn(layer=i, proj="o"), spec.fmt, H, nh * dv)
+    return out
 
 
 def _dense_or_quant(rd: CheckpointReader, prefix: str, fmt: str, out_dim: int, in_dim: int):
@@ -482,8 +577,10 @@ def load_decoder_weights(model_dir: str | Path, names: DecoderNames | None = Non
     """Host-side view of a decoder checkpoint: ``{"spec", "embed", "lm_head", "final_norm",
     "layers"}``; each layer a dict with ``ln1``, ``ln2``, ``q`` / ``k`` / ``v`` / ``o``
     (``("dense", [out, in])`` or ``("quant", tensors)``), ``q_norm`` / ``k_norm`` (or None) and
-    ``ffn``: ``("moe", load_layer_weights(...))`` or ``("dense", {gate, up, down})``.  Float
-    tensors are fp32 copies, quantized ones read-only views."""
+    ``ffn``: ``("moe", load_layer_weights(...))`` or ``("dense", {gate, up, down})``.  An MLA
+    layer has ``q`` (or ``q_a`` / ``q_a_norm`` / ``q_b`` in ``q``), ``kv_a``, ``kv_a_norm``,
+    ``kv_b`` and ``o`` instead (``_mla_attention``).  Float tensors are fp32 copies, quantized
+    ones read-only views (copies where rope channels were reordered)."""
     names = names or DecoderNames()
     rd = CheckpointReader(model_dir)
     spec = decoder_spec_from_config(rd.config)
@@ -505,14 +602,17 @@ def load_decoder_weights(model_dir: str | Path, names: DecoderNames | None = Non
     for i in range(spec.layers):
         lay = {"ln1": _vector(rd, names.input_norm.format(layer=i), H),
                "ln2": _vector(rd, names.post_norm.format(layer=i), H)}
-        for p, (o, n) in dims.items():
-            lay[p] = _dense_or_quant(rd, names.attn.format(layer=i, proj=p), spec.fmt, o, n)
-        for p, n in (("q_norm", spec.heads), ("k_norm", spec.kv_heads)):
-            name = getattr(names, p).format(layer=i)
-            w = _float_tensor(rd, name).reshape(-1) if rd.has(name) else None
-            if w is not None and w.size not in (d, n * d):
-                raise ValueError(f"{name} has {w.size} elements, expected {d} or {n * d}")
-            lay[p] = w
+        if spec.mla:
+            lay.update(_mla_attention(rd, spec, names, i))
+        else:
+            for p, (o, n) in dims.items():
+                lay[p] = _dense_or_quant(rd, names.attn.format(layer=i, proj=p), spec.fmt, o, n)
+            for p, n in (("q_norm", spec.heads), ("k_norm", spec.kv_heads)):
+                name = getattr(names, p).format(layer=i)
+                w = _float_tensor(rd, name).reshape(-1) if rd.has(name) else None
+                if w is not None and w.size not in (d, n * d):
+                    raise ValueError(f"{name} has {w.size} elements, expected {d} or {n * d}")
+                lay[p] = w
         if spec.moe_layers[i]:
             lay["ffn"] = ("moe", _layer_weights(rd, i, names.moe))
         else:
@@ -534,13 +634,20 @@ def load_decoder(model_dir: str | Path, device="cuda", kernel: str = "auto", nam
     kept as bf16 for cuBLAS.  RoPE from ``rope_theta`` / ``rope_scaling`` (none or linear;
     other scalings raise ``NotImplementedError``: build the ``MoeDecoder`` with
     ``build_rope``'s table).  ``app_config``: the engine's config (``[experts]`` / ``[quant]``,
-    ``ccut_b200.config``), checked against the checkpoint before anything is uploaded."""
+    ``ccut_b200.config``), checked against the checkpoint before anything is uploaded.
+
+    MLA checkpoints (DeepSeek-V2 / V3) give ``MlaDecoderLayer`` layers: ``kv_a_proj_with_mqa``
+    (576 outputs, not a multiple of the 128 the quantized-projection kernel tiles by) and
+    ``kv_b_proj`` (whose per-head blocks the layer keeps) are dequantized on the device, the
+    first padded with zero channels to a multiple of 128 for the export; RoPE from YaRN
+    (``yarn_rope_table``) with its factor applied to ``q_pe`` squared (the models scale both
+    ``cos`` and ``sin``, so the scores carry the factor twice)."""
     import torch
 
     from ccut_b200.dense import DenseFfn
     from ccut_b200.layer import MoeLayer
-    from ccut_b200.model import DecoderLayer, MoeDecoder, rope_table
-    from ccut_b200.quant import QuantLinear, dequantize
+    from ccut_b200.model import DecoderLayer, MlaDecoderLayer, MoeDecoder, rope_table, yarn_rope_table
+    from ccut_b200.quant import QuantLinear, dequantize, pad_out_channels
 
     if app_config is not None:  # the engine's [experts] / [quant] settings, checked before any upload
         from ccut_b200.config import resolve
@@ -548,17 +655,26 @@ def load_decoder(model_dir: str | Path, device="cuda", kernel: str = "auto", nam
         resolve(app_config, CheckpointReader(model_dir).config)
     w = load_decoder_weights(model_dir, names)
     spec = w["spec"]
-    inv_freq, attn_factor = rope_table(spec.head_dim, spec.rope_theta, spec.rope_scaling)
+    scaling_type = "none"
+    if spec.mla and spec.rope_scaling and spec.rope_scaling["type"] == "yarn":
+        inv_freq, f = yarn_rope_table(spec.head_dim, spec.rope_theta, spec.rope_scaling)
+        attn_factor, scaling_type = f * f, "yarn"
+    else:
+        inv_freq, attn_factor = rope_table(spec.head_dim, spec.rope_theta, spec.rope_scaling)
 
-    def dense(m, out_dim: int, in_dim: int):
+    def dense(m, out_dim: int, in_dim: int, keep_quant: bool | None = None, dtype=torch.bfloat16):
         kind, a = m
         if kind == "dense":
-            return torch.from_numpy(np.ascontiguousarray(a)).to(device=device, dtype=torch.bfloat16)
-        if quantized_projections:
+            return torch.from_numpy(np.ascontiguousarray(a)).to(device=device, dtype=dtype)
+        keep = quantized_projections if keep_quant is None else keep_quant
+        if keep and out_dim % 128 == 0 and in_dim % 128 == 0:
             return QuantLinear(spec.fmt, a, in_dim, out_dim, device)
+        padded = -(-out_dim // 128) * 128
+        if padded != out_dim:
+            a = pad_out_channels(spec.fmt, a, padded)
         main = _SUFFIXES[spec.fmt][0]
-        t = dequantize(spec.fmt, a[main], {k: v for k, v in a.items() if k != main}, in_dim, out_dim, device)
-        return t.to(torch.bfloat16).contiguous()
+        t = dequantize(spec.fmt, a[main], {k: v for k, v in a.items() if k != main}, in_dim, padded, device)
+        return t[:out_dim].to(dtype).contiguous()
 
     H, d = spec.hidden, spec.head_dim
     dims = {"q": (spec.heads * d, H), "k": (spec.kv_heads * d, H), "v": (spec.kv_heads * d, H),
@@ -574,8 +690,23 @@ def load_decoder(model_dir: str | Path, device="cuda", kernel: str = "auto", nam
                            device=device)
         else:
             ffn = DenseFfn(spec.fmt, H, spec.inter, f["gate"], f["up"], f["down"], kernel=kernel, device=device)
+        if spec.mla:
+            m, nh = spec.mla, spec.heads
+            dn, dr, dv, R, qr = (m["qk_nope_head_dim"], m["qk_rope_head_dim"], m["v_head_dim"], m["kv_lora_rank"],
+                                 m["q_lora_rank"])
+            q = dense(lay["q"], nh * (dn + dr), qr or H)
+            q_a = dense(lay["q_a"], qr, H) if qr else None
+            kv_a = dense(lay["kv_a"], R + dr, H, keep_quant=False)
+            kv_b = dense(lay["kv_b"], nh * (dn + dv), R, keep_quant=False, dtype=torch.float32)
+            o = dense(lay["o"], H, nh * dv)
+            layers.append(MlaDecoderLayer(lay["ln1"], q, kv_a, kv_b, o, lay["ln2"], ffn, lay["kv_a_norm"], heads=nh,
+                                          qk_nope_head_dim=dn, qk_rope_head_dim=dr, v_head_dim=dv, kv_lora_rank=R,
+                                          q_a=q_a, q_a_norm=lay.get("q_a_norm"), softmax_scale=m["softmax_scale"],
+                                          device=device))
+            continue
         q, k, v, o = (dense(lay[p], *dims[p]) for p in "qkvo")
         layers.append(DecoderLayer(lay["ln1"], q, k, v, o, lay["ln2"], ffn, lay["q_norm"], lay["k_norm"],
                                    heads=spec.heads, kv_heads=spec.kv_heads, head_dim=d, device=device))
     return MoeDecoder(w["embed"], layers, w["final_norm"], w["lm_head"], inv_freq=inv_freq,
-                      attention_factor=attn_factor, eps=spec.eps, softcap=spec.softcap, device=device)
+                      attention_factor=attn_factor, scaling_type=scaling_type, eps=spec.eps, softcap=spec.softcap,
+                      device=device)

@@ -51,23 +51,10 @@ from ccut_b200.blocks.norm import rms_norm
 from ccut_b200.blocks.rope import apply_rope
 from ccut_b200.layer import _ptr, _stream
 from ccut_b200.quant import QuantLinear
+from ccut_b200.rope_tables import rope_table, yarn_mscale, yarn_rope_table
 
-__all__ = ["DecoderLayer", "KvCache", "KvPool", "MlaDecoderLayer", "MoeDecoder", "rope_table"]
-
-
-def rope_table(head_dim: int, rope_theta: float, rope_scaling: dict | None = None) -> tuple[np.ndarray, float]:
-    """``(inv_freq [head_dim / 2] float32, attention_factor)`` of the reference's ``build_rope``
-    (``ccut/blocks/rope.py:88-127``) for no scaling and ``linear`` scaling, computed with the same
-    float32 operations.  Other scalings: pass the table ``build_rope`` returns to ``MoeDecoder``."""
-    rs = rope_scaling or {}
-    stype = (rs.get("type") or "none").casefold()
-    factor = float(rs.get("factor", 1.0))
-    inv = 1.0 / (rope_theta ** (np.arange(0, head_dim, 2, dtype=np.float32) / head_dim))
-    if stype == "none" or factor <= 1.0:
-        return inv.astype(np.float32), 1.0
-    if stype == "linear":
-        return (inv / factor).astype(np.float32), 1.0
-    raise NotImplementedError(f"rope scaling {stype!r}: pass inv_freq and attention_factor from build_rope")
+__all__ = ["DecoderLayer", "KvCache", "KvPool", "MlaDecoderLayer", "MoeDecoder", "rope_table", "yarn_mscale",
+           "yarn_rope_table"]
 
 
 def _tensor(a, dev: torch.device, dtype: torch.dtype) -> torch.Tensor:

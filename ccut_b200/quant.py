@@ -26,7 +26,7 @@ from ccut_b200 import _lib
 from ccut_b200.layer import _dev, _ptr, _stream
 
 __all__ = ["QuantizeMethodBase", "AwqInt4G128Method", "Fp8Block128Method", "make_method", "dequantize",
-           "QuantLinear", "cat_checkpoint_tensors"]
+           "QuantLinear", "cat_checkpoint_tensors", "permute_out_channels", "pad_out_channels"]
 
 
 class QuantizeMethodBase:
@@ -220,3 +220,80 @@ def cat_checkpoint_tensors(fmt: str, parts: list) -> dict:
     if fmt not in _TENSORS:
         raise NotImplementedError(f"weight format {fmt!r} is not supported")
     return {n: np.concatenate([np.asarray(p[n]) for p in parts], axis=ax) for n, ax in _TENSORS[fmt]}
+
+
+# nibble slot i (bits 4i .. 4i + 3) of an AWQ qweight / qzeros word holds column _AWQ_COL_OF_SLOT[i]
+# of its group of 8 output channels (the AutoAWQ checkpoint layout)
+_AWQ_COL_OF_SLOT = (0, 2, 4, 6, 1, 3, 5, 7)
+
+
+def _awq_columns(words: np.ndarray) -> np.ndarray:
+    """int32 ``[rows, N / 8]`` AWQ words -> uint8 ``[rows, N]`` nibbles in column order."""
+    w = np.ascontiguousarray(words).view(np.uint32)
+    out = np.empty(w.shape + (8,), np.uint8)
+    for slot, col in enumerate(_AWQ_COL_OF_SLOT):
+        out[..., col] = (w >> np.uint32(4 * slot)) & np.uint32(15)
+    return out.reshape(w.shape[0], -1)
+
+
+def _awq_words(cols: np.ndarray) -> np.ndarray:
+    """The inverse of ``_awq_columns``."""
+    c = cols.reshape(cols.shape[0], -1, 8).astype(np.uint32)
+    w = np.zeros(c.shape[:2], np.uint32)
+    for slot, col in enumerate(_AWQ_COL_OF_SLOT):
+        w |= c[..., col] << np.uint32(4 * slot)
+    return w.view(np.int32)
+
+
+def permute_out_channels(fmt: str, tensors: dict, perm) -> dict:
+    """The checkpoint tensors of ``W[perm]`` (output channel ``j`` of the result is channel
+    ``perm[j]`` of ``W``), in the same format: AWQ nibbles and scales moved along the output
+    axis; FP8 weight rows moved, which needs every row to stay in its 128-row scale block
+    (``ValueError`` otherwise).  Byte moves only: the values dequantize to the permuted rows
+    exactly."""
+    perm = np.asarray(perm, np.int64)
+    if fmt == "awq_int4_g128":
+        n = tensors["scales"].shape[1]
+        if perm.shape != (n,):
+            raise ValueError(f"perm must have {n} entries")
+        return {"qweight": _awq_words(_awq_columns(tensors["qweight"])[:, perm]),
+                "qzeros": _awq_words(_awq_columns(tensors["qzeros"])[:, perm]),
+                "scales": np.ascontiguousarray(np.asarray(tensors["scales"])[:, perm])}
+    if fmt == "fp8_b128":
+        w = np.asarray(tensors["weight"])
+        if perm.shape != (w.shape[0],):
+            raise ValueError(f"perm must have {w.shape[0]} entries")
+        if np.any(perm // 128 != np.arange(perm.size) // 128):
+            raise ValueError("an FP8 row permutation must keep every row in its 128-row scale block")
+        out = dict(tensors)
+        out["weight"] = np.ascontiguousarray(w[perm])
+        return out
+    raise NotImplementedError(f"weight format {fmt!r} is not supported")
+
+
+def pad_out_channels(fmt: str, tensors: dict, out_features: int) -> dict:
+    """The checkpoint tensors with zero output channels appended up to ``out_features`` (so
+    that a matrix whose output size is not a multiple of 128 can be packed and dequantized;
+    the padded channels dequantize to 0)."""
+    if fmt == "awq_int4_g128":
+        s = np.asarray(tensors["scales"])
+        extra = out_features - s.shape[1]
+        if extra < 0 or extra % 8 or s.shape[1] % 8:
+            raise ValueError(f"cannot pad {s.shape[1]} AWQ output channels to {out_features}")
+
+        def pad(a, n):
+            a = np.asarray(a)
+            return np.concatenate([a, np.zeros((a.shape[0], n), a.dtype)], axis=1)
+
+        return {"qweight": pad(tensors["qweight"], extra // 8), "qzeros": pad(tensors["qzeros"], extra // 8),
+                "scales": pad(s, extra)}
+    if fmt == "fp8_b128":
+        w = np.asarray(tensors["weight"])
+        extra = out_features - w.shape[0]
+        if extra < 0:
+            raise ValueError(f"cannot pad {w.shape[0]} FP8 output channels to {out_features}")
+        sc = np.asarray(tensors.get("weight_scale_inv", tensors.get("scale")))
+        blocks = -(-out_features // 128)
+        sc = np.concatenate([sc, np.ones((blocks - sc.shape[0], sc.shape[1]), sc.dtype)]) if blocks > sc.shape[0] else sc
+        return {"weight": np.concatenate([w, np.zeros((extra, w.shape[1]), w.dtype)]), "weight_scale_inv": sc}
+    raise NotImplementedError(f"weight format {fmt!r} is not supported")

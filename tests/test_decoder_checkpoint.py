@@ -36,8 +36,10 @@ def test_moe_layer_selection_and_spec():
     assert (s.kv_heads, s.head_dim, s.eps, s.softcap, s.tie_word_embeddings, s.fmt) == (2, 128, 1e-5, 30.0, True,
                                                                                          "fp8_b128")
     assert ck.decoder_spec_from_config(_cfg()).head_dim == 64
-    with pytest.raises(NotImplementedError):
-        ck.decoder_spec_from_config(_cfg(kv_lora_rank=512))  # MLA
+    with pytest.raises(KeyError):
+        ck.decoder_spec_from_config(_cfg(kv_lora_rank=512))  # MLA without its head sizes
+    m = ck.decoder_spec_from_config(_cfg(kv_lora_rank=512, qk_nope_head_dim=128, qk_rope_head_dim=64, v_head_dim=128))
+    assert m.mla["kv_lora_rank"] == 512 and m.head_dim == 64 and m.mla["softmax_scale"] == pytest.approx(192 ** -0.5)
     with pytest.raises(NotImplementedError):
         ck.decoder_spec_from_config(_cfg(linear_num_key_heads=16))
     with pytest.raises(KeyError):

@@ -23,11 +23,12 @@ import torch
 
 from ccut_b200 import dense
 from ccut_b200.backend import GenericBackend
-from ccut_b200.checkpoint import load_decoder
+from ccut_b200.checkpoint import load_decoder, load_decoder_weights
 from ccut_b200.model import DecoderLayer, MlaDecoderLayer, MoeDecoder, rope_table
 from oracle import inputs, moe, routing
 from oracle import model as omodel
 from tests.ckpt_helpers import write_decoder_checkpoint
+from tests.deepseek_helpers import DS_CASES, oracle_decoder, write_deepseek_checkpoint
 from tests.gpu_helpers import gpu_layer
 from tests.model_helpers import MLA_TINY, make_tiny, quantized_attention, quantized_layers
 
@@ -285,3 +286,51 @@ def test_load_decoder_matches_oracle(tmp_path, fmt, keep_quantized):
                                       pos, bf16_acts=True)
         assert _rel_rows(got.cpu().numpy(), ref) <= LOGITS_TOL, (n, pos)
         pos += n
+
+
+def _forced_moe(rec: _Recorded, inner):
+    """The oracle MoE callable ``inner`` (``omodel.moe_ffn``) on the routing the GPU chose,
+    after checking that the GPU's experts are a near-optimal choice under the oracle's own
+    selection scores (their sum within ``NEAR_TIE`` of the oracle's)."""
+    router, top_k, mode, lookup, shared, kw = inner.args
+
+    def f(x):
+        ids, w = rec.routes.pop(0)
+        lg = x @ router.T
+        _, own = routing.route(lg, top_k, mode, **kw)
+        c = 1.0 / (1.0 + np.exp(-lg)) + (kw["bias"] if kw.get("bias") is not None else 0.0)
+        for t in range(x.shape[0]):
+            if set(ids[t].tolist()) != set(own[t].tolist()):
+                assert c[t, own[t]].sum() - c[t, ids[t]].sum() < NEAR_TIE, f"token {t}: {ids[t]} vs {own[t]}"
+        return moe.moe_forward(x, router, top_k, mode, lookup, shared, ids=ids, weights=w)[0]
+
+    return f
+
+
+@pytest.mark.parametrize("case", sorted(DS_CASES))
+@pytest.mark.parametrize("keep_quantized", [False, True])
+def test_load_deepseek_decoder_matches_oracle(tmp_path, case, keep_quantized):
+    """``load_decoder`` of a DeepSeek-V3-style checkpoint (MLA with YaRN and interleaved rope
+    channels, a dense first layer, grouped sigmoid routing): a 9-token prefill and three
+    single-token steps against the oracle's decoder over the same tensors, which matches
+    transformers' DeepseekV3ForCausalLM on the CPU."""
+    root = write_deepseek_checkpoint(tmp_path / case, case)
+    dec = load_decoder(root, quantized_projections=keep_quantized)
+    assert type(dec.layers[0]).__name__ == "MlaDecoderLayer" and dec.layout == ("mla", 1, 576)
+    rec = _Recorded(dec.layers[1].ffn)
+    dec.layers[1].ffn = rec
+    w = load_decoder_weights(root)
+    layers, ffns, spec = oracle_decoder(w, "quantized" if keep_quantized else "bf16")
+    ffns[1] = _forced_moe(rec, ffns[1])
+    cache, ocache = dec.new_cache(256), omodel.KvCache()
+    toks = np.random.default_rng(7).integers(0, w["spec"].vocab, 12)
+    pos = 0
+    for n in (9, 1, 1, 1):
+        got = dec.forward(toks[pos: pos + n], cache, all_logits=True)
+        torch.cuda.synchronize()
+        ref, _ = omodel.model_forward(toks[pos: pos + n], w["embed"], layers, ffns, w["final_norm"], w["lm_head"],
+                                      spec, ocache, pos, bf16_acts=True)
+        err = _rel_rows(got.cpu().numpy(), ref)
+        assert err <= LOGITS_TOL, (case, pos, err)
+        pos += n
+    assert not rec.routes
