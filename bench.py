@@ -545,6 +545,13 @@ ENGINE_WORKLOADS = {"cfg3_engine_decode": {"moe": "cfg3", "layers": 48, "heads":
                                            "vocab": 151936, "batch": 8, "prompt": 512, "pool": False}}
 # the same with the requests' caches in one pool: one attention launch per layer and step
 ENGINE_WORKLOADS["cfg3_engine_decode_pool"] = dict(ENGINE_WORKLOADS["cfg3_engine_decode"], pool=True)
+# config 2: the DeepSeek-V2-Lite-shaped stack -- 27 layers, layer 0 a dense FFN of intermediate
+# 10944, the others config 0's AWQ MoE layer; MLA attention (16 heads, kv rank 512, nope 128,
+# rope 64, v 128); vocab 102400; 2048-token prompts, then decode at batch 32 and batch 1
+ENGINE_WORKLOADS["cfg2_engine_decode"] = {"moe": "cfg0", "layers": 27, "attn": "mla", "heads": 16, "d_nope": 128,
+                                          "d_rope": 64, "d_v": 128, "dense_layers": 1, "dense_inter": 10944,
+                                          "vocab": 102400, "batch": 32, "prompt": 2048, "pool": False}
+ENGINE_WORKLOADS["cfg2_engine_decode_b1"] = dict(ENGINE_WORKLOADS["cfg2_engine_decode"], batch=1)
 
 
 def run_attn(args, wl) -> None:
@@ -673,15 +680,16 @@ def run_mla(args, wl) -> None:
 def run_engine(args, wl) -> None:
     """Decode steps of a whole synthetic model through ``GenericBackend.generate_batch`` (the
     call an engine step makes): every step runs one new token per request through all layers
-    (bf16 projections on cuBLAS, RMSNorm / RoPE / GQA attention / the MoE layer on this
-    library's kernels) and samples greedily on the device."""
+    (bf16 projections on cuBLAS, RMSNorm / RoPE / GQA or MLA attention / the MoE layer and the
+    dense FFN on this library's kernels) and samples greedily on the device."""
     import torch
 
     from ccut_b200 import build
     from ccut_b200.backend import GenericBackend
     from ccut_b200.layer import MoeLayer
-    from ccut_b200.model import DecoderLayer, MoeDecoder, rope_table
-    from ccut_b200.synthetic import CONFIGS, make_layer_device
+    from ccut_b200.dense import DenseFfn
+    from ccut_b200.model import DecoderLayer, MlaDecoderLayer, MoeDecoder, rope_table
+    from ccut_b200.synthetic import CONFIGS, _gen_matrix, make_layer_device
 
     if int(os.environ.get("RANK", "0")) != 0:
         return
@@ -690,7 +698,9 @@ def run_engine(args, wl) -> None:
     torch.cuda.set_device(dev)
     w = ENGINE_WORKLOADS[wl]
     c = CONFIGS[w["moe"]]
-    H, nh, kvh, d = c.hidden, w["heads"], w["kv_heads"], w["head_dim"]
+    mla = w.get("attn") == "mla"
+    H, nh = c.hidden, w["heads"]
+    kvh, d = (1, w["d_rope"]) if mla else (w["kv_heads"], w["head_dim"])
     g = torch.Generator(device=dev)
     g.manual_seed(0)
 
@@ -700,15 +710,31 @@ def run_engine(args, wl) -> None:
     def norm_w(n):
         return torch.rand((n,), generator=g, device=dev) + 0.5
 
+    def dense_ffn(i):  # seeded AWQ / FP8 SwiGLU; the down projection drawn over the padded intermediate
+        rng = np.random.default_rng(1000 + i)
+        inter = w["dense_inter"]
+        ip = -(-inter // 128) * 128
+        return DenseFfn(c.fmt, H, inter, _gen_matrix(rng, c.fmt, H, inter), _gen_matrix(rng, c.fmt, H, inter),
+                        _gen_matrix(rng, c.fmt, ip, H), device=dev)
+
     layers = []
     for i in range(w["layers"]):
-        lw = make_layer_device(c, seed=i, device=dev)
-        moe = MoeLayer(c.fmt, c.hidden, c.inter, c.num_experts, c.top_k, c.routing, lw.router, lw.experts,
-                       shared=lw.shared or None, shared_inter=c.shared_inter or None, device=dev)
-        layers.append(DecoderLayer(norm_w(H), mat(nh * d, H), mat(kvh * d, H), mat(kvh * d, H), mat(H, nh * d),
-                                   norm_w(H), moe, norm_w(d), norm_w(d), heads=nh, kv_heads=kvh, head_dim=d,
-                                   device=dev))
-    inv, af = rope_table(d, 1e6)
+        if i < w.get("dense_layers", 0):
+            ffn = dense_ffn(i)
+        else:
+            lw = make_layer_device(c, seed=i, device=dev)
+            ffn = MoeLayer(c.fmt, c.hidden, c.inter, c.num_experts, c.top_k, c.routing, lw.router, lw.experts,
+                           shared=lw.shared or None, shared_inter=c.shared_inter or None, device=dev)
+        if mla:
+            dn, dr, dv = w["d_nope"], w["d_rope"], w["d_v"]
+            layers.append(MlaDecoderLayer(norm_w(H), mat(nh * (dn + dr), H), mat(512 + dr, H), mat(nh * (dn + dv), 512),
+                                          mat(H, nh * dv), norm_w(H), ffn, norm_w(512), heads=nh, qk_nope_head_dim=dn,
+                                          qk_rope_head_dim=dr, v_head_dim=dv, device=dev))
+        else:
+            layers.append(DecoderLayer(norm_w(H), mat(nh * d, H), mat(kvh * d, H), mat(kvh * d, H), mat(H, nh * d),
+                                       norm_w(H), ffn, norm_w(d), norm_w(d), heads=nh, kv_heads=kvh, head_dim=d,
+                                       device=dev))
+    inv, af = rope_table(d, 1e4 if mla else 1e6)
     dec = MoeDecoder(torch.randn((w["vocab"], H), generator=g, device=dev), layers, norm_w(H), mat(w["vocab"], H),
                      inv_freq=inv, attention_factor=af, device=dev)
     B, P = w["batch"], w["prompt"]
@@ -742,8 +768,9 @@ def run_engine(args, wl) -> None:
         "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16 activations, AWQ int4 experts, f32 accumulate", "data": "synthetic (seeded torch generator)",
         "config": {"workload": wl, "layers": w["layers"], "batch": B, "prompt": P, "moe": w["moe"], "pool": w["pool"],
-                   "heads": nh,
-                   "kv_heads": kvh, "head_dim": d, "vocab": w["vocab"],
+                   "attention": "mla (rank 512, nope / rope / v = %d / %d / %d)" % (w["d_nope"], d, w["d_v"]) if mla
+                   else "gqa", "heads": nh, "kv_heads": kvh, "head_dim": d, "vocab": w["vocab"],
+                   "dense_layers": w.get("dense_layers", 0),
                    "l2": "expert weights of every layer exceed the 126 MB L2, no flush"},
         "e2e": {"value": B * K / wall, "unit": "tokens/s", "h2d_bytes_per_step": B * 8 * 2,
                 "d2h_bytes_per_step": B * 8},

@@ -16,14 +16,18 @@ Public entry points
 ``config``                   the reference's ``[experts]`` / ``[quant]`` settings read for this path
 ``quant``                    ``QuantizeMethodBase``-compatible AWQ-int4-g128 / FP8-block-128 methods
 ``checkpoint``               ``load_moe_layer``: a MoE layer of an AWQ / FP8-block safetensors
-                             checkpoint into HBM
+                             checkpoint into HBM; ``load_decoder``: a whole Qwen-MoE or
+                             DeepSeek-V2 / V3 decoder
 ``dense.DenseFfn``           dense quantized SwiGLU FFN (the expert kernels with one expert)
 ``blocks.attn_gqa``          drop-ins for ``ccut.blocks.attn_gqa`` (GQA attention on tensor cores)
 ``blocks.norm``              drop-in for ``ccut.blocks.norm.rms_norm``
 ``blocks.rope``              drop-in for ``ccut.blocks.rope.apply_rope``
-``model``                    ``MoeDecoder``: embedding, ``full_attn`` decoder layers (attention,
-                             norms, RoPE, bf16 KV cache in HBM, MoE or dense FFN), final norm,
-                             ``lm_head`` -- the reference's generic layer forward on the GPU
+``blocks.attn_mla``          drop-ins for ``ccut.blocks.attn_mla`` (MLA latent attention)
+``model``                    ``MoeDecoder``: embedding, decoder layers (``DecoderLayer``: GQA
+                             attention, ``MlaDecoderLayer``: multi-head latent attention; norms,
+                             RoPE, bf16 caches in HBM, MoE or dense FFN), final norm, ``lm_head``
+                             -- the reference's generic layer forward on the GPU
+``rope_tables``              RoPE tables: the reference's ``build_rope`` cases, YaRN
 ``backend.GenericBackend``   the ``generate_step`` backend the reference's ``Engine`` calls, over
                              a ``MoeDecoder`` (prefix-reusing sequence caches, on-device sampling)
 ``sampling``                 the reference's temperature / top-k / min-p / top-p transform in torch
