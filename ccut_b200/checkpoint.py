@@ -186,8 +186,34 @@ class CheckpointReader:
 
 
 # ---------------------------------------------------------------- config
+def _compressed_tensors_format(q: dict) -> str:
+    """The format of this path that a compressed-tensors ``quantization_config`` stores (the
+    scheme kinds of ``ccut/quant/compressed_tensors.py:44-71``): one config group of int4
+    weights, group strategy with group size 128, no activation quantization and no
+    activation reordering (``pack-quantized``, repacked into AWQ's layout at load), or of FP8
+    weights with the ``block`` strategy and 128 x 128 blocks (``float-quantized``; its
+    activations run in 16 bits here, whatever ``input_activations`` says)."""
+    groups = q.get("config_groups") or {}
+    if len(groups) != 1:
+        raise NotImplementedError(f"compressed-tensors with {len(groups)} config groups (have one)")
+    g = next(iter(groups.values()))
+    w = g.get("weights") or {}
+    kind, bits, strategy = str(w.get("type", "")).lower(), int(w.get("num_bits") or 0), str(w.get("strategy", "")).lower()
+    if kind == "int" and bits == 4 and strategy == "group" and int(w.get("group_size") or 0) == 128:
+        if g.get("input_activations") or w.get("actorder") not in (None, False, "none"):
+            raise NotImplementedError("compressed-tensors int4 with activation quantization or activation reordering")
+        return "awq_int4_g128"
+    if kind == "float" and bits == 8 and strategy == "block" and [int(v) for v in (w.get("block_structure") or [])] \
+            == [128, 128]:
+        return "fp8_b128"
+    raise NotImplementedError(f"compressed-tensors weights type={kind!r} num_bits={bits} strategy={strategy!r} are not "
+                              "supported (int4 group 128, or FP8 128 x 128 blocks)")
+
+
 def quant_format(config: dict) -> str:
-    """Weight format of this path for a checkpoint's ``quantization_config``."""
+    """Weight format of this path for a checkpoint's ``quantization_config``: AWQ
+    (``quant_method = "awq"``), FP8 blocks (``"fp8"``), or the compressed-tensors schemes that
+    store the same values (``_compressed_tensors_format``)."""
     tc = config.get("text_config", config)
     q = tc.get("quantization_config") or config.get("quantization_config")
     if not q:
@@ -207,7 +233,9 @@ def quant_format(config: dict) -> str:
             raise NotImplementedError(f"FP8 variant fmt={fmt!r} weight_block_size={block} is not supported"
                                       " (e4m3, 128 x 128 blocks)")
         return "fp8_b128"
-    raise NotImplementedError(f"quant_method {method!r} is not supported (have 'awq', 'fp8')")
+    if method == "compressed-tensors":
+        return _compressed_tensors_format(q)
+    raise NotImplementedError(f"quant_method {method!r} is not supported (have 'awq', 'fp8', 'compressed-tensors')")
 
 
 @dataclass(frozen=True)
@@ -285,7 +313,42 @@ def expert_pattern(template: str) -> re.Pattern[str]:
 _SUFFIXES = {"awq_int4_g128": ("qweight", "qzeros", "scales"), "fp8_b128": ("weight", "weight_scale_inv")}
 
 
+def _read_compressed_tensors(reader: CheckpointReader, prefix: str, fmt: str) -> dict | None:
+    """A compressed-tensors matrix in this path's tensors, or None when ``prefix`` has none:
+    int4 ``weight_packed`` / ``weight_scale`` / ``weight_zero_point`` repacked into AWQ's
+    (``quant.ct_int4_to_awq``); FP8 ``weight`` with its block scales under ``weight_scale``."""
+    from ccut_b200.quant import ct_int4_to_awq
+
+    if fmt == "awq_int4_g128" and reader.has(f"{prefix}.weight_packed"):
+        if reader.has(f"{prefix}.weight_g_idx"):
+            raise NotImplementedError(f"{prefix}: activation reordering (weight_g_idx) is not supported")
+        if reader.dtype(f"{prefix}.weight_packed") != "I32":
+            raise ValueError(f"{prefix}: weight_packed must be I32")
+        if not reader.has(f"{prefix}.weight_scale"):
+            raise ValueError(f"{prefix}: missing scale tensor {prefix + '.weight_scale'!r}")
+        zp = reader.tensor(f"{prefix}.weight_zero_point") if reader.has(f"{prefix}.weight_zero_point") else None
+        shape = reader.tensor(f"{prefix}.weight_shape") if reader.has(f"{prefix}.weight_shape") else None
+        return ct_int4_to_awq(reader.tensor(f"{prefix}.weight_packed"), _float_tensor(reader, f"{prefix}.weight_scale"),
+                              zp, shape)
+    if (fmt == "fp8_b128" and reader.has(f"{prefix}.weight") and reader.has(f"{prefix}.weight_scale")
+            and not reader.has(f"{prefix}.weight_scale_inv")):
+        if reader.dtype(f"{prefix}.weight") != "F8_E4M3":
+            raise ValueError(f"{prefix}: FP8 tensors must be an F8_E4M3 weight")
+        return {"weight": reader.tensor(f"{prefix}.weight"),
+                "weight_scale_inv": _float_tensor(reader, f"{prefix}.weight_scale")}
+    return None
+
+
+def _has_matrix(reader: CheckpointReader, prefix: str, fmt: str) -> bool:
+    """Whether ``prefix`` names a matrix in ``fmt`` (its own tensors or compressed-tensors')."""
+    return reader.has(f"{prefix}.{_SUFFIXES[fmt][0]}") or (fmt == "awq_int4_g128"
+                                                           and reader.has(f"{prefix}.weight_packed"))
+
+
 def _read_matrix(reader: CheckpointReader, prefix: str, fmt: str) -> dict:
+    ct = _read_compressed_tensors(reader, prefix, fmt)
+    if ct is not None:
+        return ct
     main = _SUFFIXES[fmt][0]
     if not reader.has(f"{prefix}.{main}"):
         raise KeyError(f"no tensor {prefix}.{main!s} in the checkpoint")
@@ -346,8 +409,7 @@ def _layer_weights(rd: CheckpointReader, layer: int, names: NameTemplates):
         if rd.has(names.shared_gate.format(layer=layer)):
             raise NotImplementedError("a per-token shared-expert gate (shared_expert_gate) is not supported")
         for t in names.shared:
-            probe = f"{t.format(layer=layer, proj='gate')}.{_SUFFIXES[fmt][0]}"
-            if rd.has(probe):
+            if _has_matrix(rd, t.format(layer=layer, proj="gate"), fmt):
                 shared = [matrices(t)]
                 break
         else:

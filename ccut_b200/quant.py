@@ -26,7 +26,7 @@ from ccut_b200 import _lib
 from ccut_b200.layer import _dev, _ptr, _stream
 
 __all__ = ["QuantizeMethodBase", "AwqInt4G128Method", "Fp8Block128Method", "make_method", "dequantize",
-           "QuantLinear", "cat_checkpoint_tensors", "permute_out_channels", "pad_out_channels"]
+           "QuantLinear", "cat_checkpoint_tensors", "permute_out_channels", "pad_out_channels", "ct_int4_to_awq"]
 
 
 class QuantizeMethodBase:
@@ -297,3 +297,46 @@ def pad_out_channels(fmt: str, tensors: dict, out_features: int) -> dict:
         sc = np.concatenate([sc, np.ones((blocks - sc.shape[0], sc.shape[1]), sc.dtype)]) if blocks > sc.shape[0] else sc
         return {"weight": np.concatenate([w, np.zeros((extra, w.shape[1]), w.dtype)]), "weight_scale_inv": sc}
     raise NotImplementedError(f"weight format {fmt!r} is not supported")
+
+
+def _nibbles_sequential(words: np.ndarray) -> np.ndarray:
+    """int32 ``[rows, C]`` words holding 8 nibbles each, nibble i in bits 4i .. 4i + 3 ->
+    uint8 ``[rows, 8 C]`` in that order."""
+    w = np.ascontiguousarray(words).view(np.uint32)
+    return np.stack([(w >> np.uint32(4 * i)) & np.uint32(15) for i in range(8)], axis=-1).astype(
+        np.uint8).reshape(w.shape[0], -1)
+
+
+def ct_int4_to_awq(weight_packed, weight_scale, weight_zero_point=None, weight_shape=None,
+                   group_size: int = 128) -> dict:
+    """A compressed-tensors ``pack-quantized`` int4 matrix (W4A16, group strategy) as the AWQ
+    tensors this path runs, with the same values: ``weight_packed`` int32 [N, K/8] holds
+    ``v + 8`` for the signed int4 ``v`` of element (n, k) in nibble ``k % 8`` of word
+    ``k / 8``; ``weight_scale`` [N, K/group] (float); ``weight_zero_point`` int32
+    [N/8, K/group] holds ``zp + 8`` packed the same way along N, or None (symmetric: zero point
+    0).  ``(v - zp) * s`` equals AWQ's ``(q - z) * s`` with ``q = v + 8`` and ``z = zp + 8``, so
+    the repack moves nibbles only: ``qweight`` [K, N/8] and ``qzeros`` [K/group, N/8] in AWQ's
+    nibble order, ``scales`` fp16 [K/group, N] (``ValueError`` when a scale is not exactly an
+    fp16 value, or the sizes do not fit group-128 AWQ)."""
+    wp = np.asarray(weight_packed)
+    if wp.dtype != np.int32 or wp.ndim != 2:
+        raise ValueError("weight_packed must be a 2-D int32 array")
+    N, K = (int(v) for v in weight_shape) if weight_shape is not None else (wp.shape[0], wp.shape[1] * 8)
+    if group_size != 128 or K % 128 or N % 8 or wp.shape != (N, -(-K // 8)):
+        raise ValueError(f"a [{N}, {K}] int4 matrix packed as {wp.shape} does not fit AWQ int4 group 128")
+    s = np.asarray(weight_scale, np.float32)
+    if s.shape != (N, K // 128):
+        raise ValueError(f"weight_scale must be [{N}, {K // 128}], got {s.shape}")
+    s16 = s.astype(np.float16)
+    if not np.array_equal(s16.astype(np.float32), s):
+        raise ValueError("weight_scale holds values that fp16 does not represent exactly")
+    q = _nibbles_sequential(wp)[:, :K]  # [N, K] = v + 8
+    if weight_zero_point is None:
+        z = np.full((K // 128, N), 8, np.uint8)
+    else:
+        zp = np.asarray(weight_zero_point)
+        if zp.dtype != np.int32 or zp.shape != (N // 8, K // 128):
+            raise ValueError(f"weight_zero_point must be int32 [{N // 8}, {K // 128}], got {zp.dtype} {zp.shape}")
+        z = _nibbles_sequential(np.ascontiguousarray(zp.T))[:, :N]  # [K / 128, N] = zp + 8
+    return {"qweight": _awq_words(np.ascontiguousarray(q.T)), "qzeros": _awq_words(z),
+            "scales": np.ascontiguousarray(s16.T)}

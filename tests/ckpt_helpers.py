@@ -14,7 +14,7 @@ from pathlib import Path
 
 import numpy as np
 
-from oracle import inputs
+from oracle import formats, inputs
 
 _DT = {np.dtype(np.float32): "F32", np.dtype(np.float16): "F16", np.dtype(np.int32): "I32",
        np.dtype(np.uint8): "U8", np.dtype(np.uint16): "U16", np.dtype(np.int64): "I64"}
@@ -47,6 +47,46 @@ def _matrix_tensors(prefix: str, m) -> dict:
     return {f"{prefix}.weight": ("F8_E4M3", m.weight), f"{prefix}.weight_scale_inv": (None, m.scale)}
 
 
+def _pack_sequential(cols: np.ndarray) -> np.ndarray:
+    """uint8 nibbles [R, 8 C] -> int32 [R, C], nibble i of a word in bits 4i .. 4i + 3."""
+    c = cols.reshape(cols.shape[0], -1, 8).astype(np.uint32)
+    w = np.zeros(c.shape[:2], np.uint32)
+    for i in range(8):
+        w |= c[..., i] << np.uint32(4 * i)
+    return w.view(np.int32)
+
+
+def ct_quant_config(fmt: str) -> dict:
+    """A compressed-tensors ``quantization_config`` for ``fmt``: int4 group 128 weights
+    (``pack-quantized``, asymmetric) or FP8 128 x 128 block weights with dynamic activations."""
+    if fmt == "awq_int4_g128":
+        w = {"num_bits": 4, "type": "int", "symmetric": False, "strategy": "group", "group_size": 128,
+             "actorder": None}
+        return {"quant_method": "compressed-tensors", "format": "pack-quantized",
+                "config_groups": {"group_0": {"targets": ["Linear"], "weights": w, "input_activations": None}},
+                "ignore": ["lm_head", "re:.*mlp.gate$"]}
+    w = {"num_bits": 8, "type": "float", "symmetric": True, "strategy": "block", "block_structure": [128, 128]}
+    a = {"num_bits": 8, "type": "float", "symmetric": True, "strategy": "group", "group_size": 128, "dynamic": True}
+    return {"quant_method": "compressed-tensors", "format": "float-quantized",
+            "config_groups": {"group_0": {"targets": ["Linear"], "weights": w, "input_activations": a}},
+            "ignore": ["lm_head", "re:.*mlp.gate$"]}
+
+
+def _ct_matrix_tensors(prefix: str, m) -> dict:
+    """One matrix in compressed-tensors form with the same values: AWQ ``(q - z) * s`` as
+    ``weight_packed`` (q along K, 8 per word), ``weight_zero_point`` (z along N),
+    ``weight_scale`` fp16 [N, K / 128], ``weight_shape``; FP8 as ``weight`` + ``weight_scale``."""
+    if isinstance(m, inputs.AwqMatrix):
+        q = formats.awq_unpack(m.qweight)  # [K, N]
+        z = formats.awq_unpack(m.qzeros)  # [K / 128, N]
+        K, N = q.shape
+        return {f"{prefix}.weight_packed": (None, _pack_sequential(np.ascontiguousarray(q.T))),
+                f"{prefix}.weight_zero_point": (None, np.ascontiguousarray(_pack_sequential(z).T)),
+                f"{prefix}.weight_scale": (None, np.ascontiguousarray(m.scales.T)),
+                f"{prefix}.weight_shape": (None, np.array([N, K], np.int64))}
+    return {f"{prefix}.weight": ("F8_E4M3", m.weight), f"{prefix}.weight_scale": (None, m.scale)}
+
+
 def merged_shared(lw):
     """The layer's shared experts as one MLP (intermediate axis concatenated)."""
     if not lw.shared:
@@ -66,9 +106,13 @@ def merged_shared(lw):
 
 
 def write_checkpoint(root: Path, lw, layer: int = 3, router_bf16: bool = False, quant: dict | None = None,
-                     drop: tuple[str, ...] = (), extra_config: dict | None = None) -> Path:
+                     drop: tuple[str, ...] = (), extra_config: dict | None = None, ct: bool = False) -> Path:
+    """One MoE layer of ``lw`` as a two-shard checkpoint; ``ct``: in compressed-tensors form."""
     c = lw.cfg
     root.mkdir(parents=True, exist_ok=True)
+    mt = _ct_matrix_tensors if ct else _matrix_tensors
+    if ct and quant is None:
+        quant = ct_quant_config(c.fmt)
     q = quant or ({"quant_method": "awq", "bits": 4, "group_size": 128, "zero_point": True, "version": "gemm"}
                   if c.fmt == "awq_int4_g128" else
                   {"quant_method": "fp8", "fmt": "e4m3", "weight_block_size": [128, 128],
@@ -91,11 +135,11 @@ def write_checkpoint(root: Path, lw, layer: int = 3, router_bf16: bool = False, 
     for e, ew in enumerate(lw.experts):
         dst = t1 if e < c.num_experts // 2 else t2
         for proj in ("gate", "up", "down"):
-            dst.update(_matrix_tensors(f"{pre}.experts.{e}.{proj}_proj", getattr(ew, proj)))
+            dst.update(mt(f"{pre}.experts.{e}.{proj}_proj", getattr(ew, proj)))
     sh = merged_shared(lw)
     if sh:
         for proj in ("gate", "up", "down"):
-            t2.update(_matrix_tensors(f"{pre}.shared_experts.{proj}_proj", sh[proj]))
+            t2.update(mt(f"{pre}.shared_experts.{proj}_proj", sh[proj]))
     for name in drop:
         t1.pop(name, None)
         t2.pop(name, None)

@@ -92,10 +92,13 @@ def test_config_resolution():
         ck.moe_spec_from_config({"hidden_size": 8, "quantization_config": base["quantization_config"]})
 
 
+@pytest.mark.parametrize("ct", [False, True])
 @pytest.mark.parametrize("fmt", ["awq_int4_g128", "fp8_b128"])
-def test_load_layer_weights_matches_the_written_layer(tmp_path, fmt):
+def test_load_layer_weights_matches_the_written_layer(tmp_path, fmt, ct):
+    """The layer read back equals the written one; ``ct``: written in compressed-tensors form
+    (int4 repacked into AWQ's layout, FP8 block scales under ``weight_scale``)."""
     lw = _layer(fmt)
-    root = write_checkpoint(tmp_path / "m", lw, layer=3, router_bf16=True)
+    root = write_checkpoint(tmp_path / "m", lw, layer=3, router_bf16=True, ct=ct)
     spec, router, experts, shared, bias = ck.load_layer_weights(root, 3)
     c = lw.cfg
     assert (spec.fmt, spec.hidden, spec.inter, spec.num_experts, spec.top_k, spec.shared_inter) == \
