@@ -91,6 +91,8 @@ SIGNATURES: dict[str, tuple] = {
                                      _i, _vp, _sz, _vp]),
     "ccut_mla_attention_workspace_bytes": (_sz, [_i, _i, _i, _i]),
     "ccut_mla_attention": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _i, _vp, _sz, _vp]),
+    "ccut_mla_attention_pool": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, C.c_longlong, _i, _f, _vp, _i, _vp,
+                                     _sz, _vp]),
     "ccut_moe_ep_forward": (_i, [_vp, C.POINTER(MoeLayerDesc), _i, _i, C.POINTER(RouteParams), _vp, _i, _vp, _i,
                                  _vp, _sz, _vp]),
     "ccut_workspace_status": (_i, [_vp, _vp]),

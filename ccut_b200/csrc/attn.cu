@@ -370,7 +370,11 @@ __global__ void __launch_bounds__(256) gqa_combine_kernel(const float* __restric
 // ~16 bits), the four partial S tiles are summed in warp order through shared memory (every
 // warp then holds the same S and runs the same online softmax), and warp w accumulates
 // O += P V for value features [128 w, 128 w + 128) (P split into hi + lo as in the GQA
-// kernel).  Splits are merged by gqa_combine_kernel<512>.
+// kernel).  Splits are merged by gqa_combine_kernel<512>.  mla_attn_pool_kernel (POOL): batch
+// row b reads slot slots[b] of a latent-cache pool (slots slot_stride elements apart, L rows
+// of 576 in each) with causal offset starts[b], so one launch serves sequences of different
+// lengths; a slot outside [0, num_slots) or a negative offset reads nothing and its rows come
+// out zero.
 constexpr int kMlaR = 512, kMlaP = 64, kMlaK = kMlaR + kMlaP;  // latent rank, rope features, key width
 constexpr int kMlaWarps = 4;
 constexpr int kMlaKS = kMlaK / kMlaWarps / 16;  // k16 steps of S per warp (9)
@@ -388,10 +392,11 @@ struct MlaSmem {
   static_assert(kMlaKS * 16 * kMlaWarps == kMlaK && kMlaVW % 16 == 0, "feature split");
 };
 
-template <bool OUT_BF16>
-__global__ void __launch_bounds__(kMlaWarps * 32) mla_attn_kernel(
+template <bool OUT_BF16, bool POOL>
+__device__ __forceinline__ void mla_attn_body(
     const float* __restrict__ q, const uint16_t* __restrict__ kv, int H, int S, int L, int causal_start, float scale,
-    int splits, int tiles_per_split, void* __restrict__ out, float* __restrict__ part) {
+    int splits, int tiles_per_split, void* __restrict__ out, float* __restrict__ part, const int* __restrict__ slots,
+    const int* __restrict__ starts, long long slot_stride, int num_slots) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ __align__(128) uint8_t mla_smem[];
@@ -405,12 +410,23 @@ __global__ void __launch_bounds__(kMlaWarps * 32) mla_attn_kernel(
   const int b = blockIdx.y, r0 = blockIdx.x * kTcRows, split = blockIdx.z;
   const int k0 = split * tiles_per_split * kMlaTile;
   int k1 = min(L, k0 + tiles_per_split * kMlaTile);
+  size_t kv_off = (size_t)b * L * kMlaK;
+  if constexpr (POOL) {
+    const int slot = slots[b];
+    causal_start = starts[b];
+    const bool valid = slot >= 0 && slot < num_slots && causal_start >= 0;
+    if (!valid) {
+      k1 = 0;  // nothing to read: the rows come out zero
+      causal_start = 0;
+    }
+    kv_off = valid ? (size_t)slot * (size_t)slot_stride : (size_t)0;
+  }
   if (causal_start >= 0) {  // the CTA's last row sees up to causal_start + s_last
     const int r_last = min(nrows, r0 + kTcRows) - 1;
     k1 = min(k1, causal_start + r_last / H + 1);
   }
   const int ntiles = k1 > k0 ? (k1 - k0 + kMlaTile - 1) / kMlaTile : 0;
-  const uint16_t* kvg = kv + (size_t)b * L * kMlaK;
+  const uint16_t* kvg = kv + kv_off;
   auto issue = [&](int tile) {  // tile -> ring stage tile % kMlaStages, zero-filled past k1
     const int p0 = k0 + tile * kMlaTile;
     uint16_t* dst = ring + (tile % kMlaStages) * MlaSmem::kTileElems;
@@ -580,6 +596,23 @@ __global__ void __launch_bounds__(kMlaWarps * 32) mla_attn_kernel(
       }
     }
   }
+}
+
+template <bool OUT_BF16>
+__global__ void __launch_bounds__(kMlaWarps * 32) mla_attn_kernel(
+    const float* __restrict__ q, const uint16_t* __restrict__ kv, int H, int S, int L, int causal_start, float scale,
+    int splits, int tiles_per_split, void* __restrict__ out, float* __restrict__ part) {
+  mla_attn_body<OUT_BF16, false>(q, kv, H, S, L, causal_start, scale, splits, tiles_per_split, out, part, nullptr,
+                                 nullptr, 0, 0);
+}
+
+template <bool OUT_BF16>
+__global__ void __launch_bounds__(kMlaWarps * 32) mla_attn_pool_kernel(
+    const float* __restrict__ q, const uint16_t* __restrict__ kv, int H, int S, int L, float scale, int splits,
+    int tiles_per_split, void* __restrict__ out, float* __restrict__ part, const int* __restrict__ slots,
+    const int* __restrict__ starts, long long slot_stride, int num_slots) {
+  mla_attn_body<OUT_BF16, true>(q, kv, H, S, L, 0, scale, splits, tiles_per_split, out, part, slots, starts,
+                                slot_stride, num_slots);
 }
 
 // RMSNorm of one row per CTA (128 threads, any dim).
@@ -829,6 +862,41 @@ int ccut_mla_attention(const float* q, const uint16_t* kv, int batch, int heads,
   if (rc) return rc;
   rc = launch_k(kern, grid, dim3(kMlaWarps * 32), MlaSmem::kBytes, stream, q, kv, heads, seq, kv_len, causal_start,
                 scale, sp, tps, out, part);
+  if (rc || sp == 1) return rc;
+  const int rows = batch * nrows;
+  return launch_k(ob ? gqa_combine_kernel<kMlaR, true> : gqa_combine_kernel<kMlaR, false>, dim3((rows + 7) / 8),
+                  dim3(256), 0, stream, (const float*)part, rows, sp, out);
+}
+
+int ccut_mla_attention_pool(const float* q, const uint16_t* kv_pool, const int32_t* slots, const int32_t* starts,
+                            int batch, int heads, int seq, int max_len, int rank, int rope_dim, long long slot_stride,
+                            int num_slots, float scale, void* out, int out_dtype, void* workspace, size_t ws_bytes,
+                            ccut_stream_t stream) {
+  PdlScope pdl_scope((long)batch * seq);
+  if (rank != kMlaR || rope_dim != kMlaP) return CCUT_ERR_UNSUPPORTED;
+  if (batch < 0 || heads <= 0 || seq < 0 || max_len < 0 || num_slots < 0 || !(scale > 0.f)) return CCUT_ERR_INVALID;
+  if (out_dtype != CCUT_OUT_BF16 && out_dtype != CCUT_OUT_F32) return CCUT_ERR_INVALID;
+  if (slot_stride < (long long)max_len * kMlaK || slot_stride % 8) return CCUT_ERR_INVALID;
+  if (batch == 0 || seq == 0) return CCUT_OK;
+  if (!q || !out || !slots || !starts || (max_len > 0 && num_slots > 0 && !kv_pool)) return CCUT_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(kv_pool)) % 16) return CCUT_ERR_INVALID;
+  if (batch > 65535 || (long)seq * heads > 2147483647L - kTcRows) return CCUT_ERR_UNSUPPORTED;
+  const int sp = mla_splits(batch, heads, seq, max_len);
+  if (sp > 1 && (!workspace || ws_bytes < ccut_mla_attention_workspace_bytes(batch, heads, seq, max_len)))
+    return CCUT_ERR_WORKSPACE;
+  const int nrows = seq * heads;
+  const int tiles = (max_len + kMlaTile - 1) / kMlaTile;
+  const int tps = (tiles + sp - 1) / sp;
+  const dim3 grid((nrows + kTcRows - 1) / kTcRows, batch, sp);
+  float* part = sp > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 256) : nullptr;
+  const bool ob = out_dtype == CCUT_OUT_BF16;
+  auto kern = ob ? mla_attn_pool_kernel<true> : mla_attn_pool_kernel<false>;
+  static std::atomic<uint64_t> smem_set[2];  // per output type: devices with the limit raised
+  int rc = ensure_smem_limit(kern, MlaSmem::kBytes, smem_set[ob]);
+  if (rc) return rc;
+  rc = launch_k(kern, grid, dim3(kMlaWarps * 32), MlaSmem::kBytes, stream, q, kv_pool, heads, seq, max_len, scale, sp,
+                tps, out, part, reinterpret_cast<const int*>(slots), reinterpret_cast<const int*>(starts), slot_stride,
+                num_slots);
   if (rc || sp == 1) return rc;
   const int rows = batch * nrows;
   return launch_k(ob ? gqa_combine_kernel<kMlaR, true> : gqa_combine_kernel<kMlaR, false>, dim3((rows + 7) / 8),

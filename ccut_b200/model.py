@@ -98,7 +98,7 @@ class KvCache:
         if not 0 <= slot < pool.slots:
             raise ValueError(f"slot {slot} outside the pool's {pool.slots}")
         c = cls.__new__(cls)
-        c.k, c.v = pool.k[slot], pool.v[slot]
+        c.k, c.v = pool.k[slot], (pool.v[slot] if pool.v is not None else None)
         c.max_len, c.length, c.pool, c.slot = pool.max_len, 0, pool, int(slot)
         return c
 
@@ -112,13 +112,16 @@ class KvCache:
 class KvPool:
     """The caches of up to ``slots`` sequences in one allocation, ``[slots, layers, kv_heads,
     max_len, head_dim]`` bf16 for k and for v: a decode step over several of them is one
-    attention launch per layer (``ccut_gqa_attention_pool``)."""
+    attention launch per layer (``ccut_gqa_attention_pool``).  ``values=False`` keeps k only:
+    the latent caches of MLA layers, ``[slots, layers, 1, max_len, 576]``
+    (``ccut_mla_attention_pool``)."""
 
-    def __init__(self, slots: int, layers: int, kv_heads: int, max_len: int, head_dim: int, device="cuda"):
+    def __init__(self, slots: int, layers: int, kv_heads: int, max_len: int, head_dim: int, device="cuda",
+                 values: bool = True):
         if slots <= 0 or max_len <= 0:
             raise ValueError("slots and max_len must be positive")
         self.k = torch.zeros((slots, layers, kv_heads, max_len, head_dim), dtype=torch.bfloat16, device=device)
-        self.v = torch.zeros_like(self.k)
+        self.v = torch.zeros_like(self.k) if values else None
         self.slots, self.max_len = int(slots), int(max_len)
 
     def cache(self, slot: int) -> KvCache:
@@ -141,6 +144,26 @@ def _attend_pool(q: torch.Tensor, pool: KvPool, layer: int, slots: torch.Tensor,
         _lib.call("ccut_gqa_attention_pool", _ptr(q), _ptr(pool.k[0, layer]), _ptr(pool.v[0, layer]), _ptr(slots),
                   _ptr(starts), B, H, Hkv, S, L, d, int(pool.k.stride(0)), pool.slots, 0.0, float(softcap or 0.0),
                   _ptr(out), _lib.OUT_BF16, _ptr(ws), ws.numel(), _stream())
+    return out
+
+
+def _mla_attend_pool(q: torch.Tensor, pool: KvPool, layer: int, slots: torch.Tensor, starts: torch.Tensor,
+                     scale: float) -> torch.Tensor:
+    """q fp32 ``[B, heads, 576]``, one query row per sequence; row b attends over slot
+    ``slots[b]`` of the latent pool at ``layer``, positions ``<= starts[b]`` -> the latent output
+    ``[B * heads, 512]`` fp32 (``ccut_mla_attention_pool``)."""
+    if not q.is_cuda:
+        raise ValueError("attention runs on CUDA tensors only")
+    B, H, _ = q.shape
+    L = pool.k.shape[3]
+    lib = _lib.load()
+    nbytes = lib.ccut_mla_attention_workspace_bytes(B, H, 1, L)
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=q.device)
+    out = torch.empty((B * H, 512), dtype=torch.float32, device=q.device)
+    with torch.cuda.device(q.device):
+        _lib.call("ccut_mla_attention_pool", _ptr(q), _ptr(pool.k[0, layer]), _ptr(slots), _ptr(starts), B, H, 1, L,
+                  512, 64, int(pool.k.stride(0)), pool.slots, float(scale), _ptr(out), _lib.OUT_F32, _ptr(ws),
+                  ws.numel(), _stream())
     return out
 
 
@@ -374,9 +397,8 @@ class MlaDecoderLayer:
     def forward(self, h: torch.Tensor, spans: list, layer: int, rope: "_Rope", pooled=None) -> torch.Tensor:
         """h [N, H] fp32 -> [N, H] fp32, as ``DecoderLayer.forward``; each span writes its
         latent rows at ``start .. start + n - 1`` of ``layer`` and attends over rows ``0 ..
-        start + n - 1`` with ``causal_start = start``."""
-        if pooled is not None:
-            raise NotImplementedError("MLA layers keep one cache per sequence (no pooled attention)")
+        start + n - 1`` with ``causal_start = start``; with ``pooled`` (one token per span, all
+        caches in one ``KvPool``) in one launch for all of them."""
         N = h.shape[0]
         H, dn, dr, dv, R = self.heads, self.d_nope, self.d_rope, self.d_v, self.rank
         x = rms_norm(h, self.ln1, rope.eps).to(torch.bfloat16)
@@ -405,8 +427,12 @@ class MlaDecoderLayer:
             rows[:, R:] = k_pe[0, 0, s.off: s.off + s.n]
         q_lat = torch.bmm(q[:, :, :dn].float().transpose(0, 1), self.k_up)  # [heads, N, rank]
         qq = torch.cat([q_lat.transpose(0, 1), q_pe[0].transpose(0, 1).float()], dim=-1).contiguous()  # [N, H, 576]
-        o_lat = torch.cat([_mla_attend(qq[s.off: s.off + s.n], s.cache.k[layer, 0, : s.start + s.n], s.start,
-                                       self.scale).view(s.n, H, R) for s in spans])
+        if pooled is not None:  # N sequences of one token each
+            pool, slots, starts = pooled
+            o_lat = _mla_attend_pool(qq, pool, layer, slots, starts, self.scale).view(N, H, R)
+        else:
+            o_lat = torch.cat([_mla_attend(qq[s.off: s.off + s.n], s.cache.k[layer, 0, : s.start + s.n], s.start,
+                                           self.scale).view(s.n, H, R) for s in spans])
         o = torch.bmm(o_lat.transpose(0, 1), self.v_up)  # [heads, N, d_v]
         o2 = o.transpose(0, 1).reshape(N, H * dv).to(torch.bfloat16)
         h = h + _project(self.wo, o2).float()
@@ -470,9 +496,7 @@ class MoeDecoder:
 
     def new_pool(self, slots: int, max_len: int) -> KvPool:
         kind, kvh, width = self.layout
-        if kind != "gqa":
-            raise NotImplementedError("pooled caches for MLA layers")
-        return KvPool(slots, len(self.layers), kvh, max_len, width, self.device)
+        return KvPool(slots, len(self.layers), kvh, max_len, width, self.device, values=kind == "gqa")
 
     def _ids(self, tokens) -> torch.Tensor:
         if isinstance(tokens, torch.Tensor):

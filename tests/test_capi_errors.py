@@ -180,3 +180,30 @@ def test_pool_attention_checks(lib):
     need = lib.ccut_gqa_attention_workspace_bytes(3, 8, 2, 1, 300, 64)
     if need > 256:
         assert call(ws=need - 1) == _lib.ERR_WORKSPACE
+
+
+def test_mla_pool_attention_checks(lib):
+    f32 = _lib.OUT_F32
+    pool = lib.ccut_mla_attention_pool
+    stride = 300 * 576
+
+    def call(*, q=FAKE, kv=FAKE, slots=FAKE, batch=3, heads=16, seq=1, L=300, rank=512, rope=64, stride=stride, n=4,
+             scale=0.1, out_dtype=f32, ws=1 << 24):
+        return pool(q, kv, slots, FAKE, batch, heads, seq, L, rank, rope, stride, n, scale, FAKE, out_dtype, FAKE, ws,
+                    NULL)
+
+    assert call(rank=256) == _lib.ERR_UNSUPPORTED
+    assert call(rope=32) == _lib.ERR_UNSUPPORTED
+    assert call(heads=0) == _lib.ERR_INVALID
+    assert call(scale=0.0) == _lib.ERR_INVALID
+    assert call(stride=stride - 8) == _lib.ERR_INVALID  # slots would overlap
+    assert call(stride=stride + 4) == _lib.ERR_INVALID  # slots not 16-byte aligned
+    assert call(n=-1) == _lib.ERR_INVALID
+    assert call(out_dtype=9) == _lib.ERR_INVALID
+    assert call(batch=0) == _lib.OK
+    assert call(slots=NULL) == _lib.ERR_INVALID
+    assert call(kv=NULL) == _lib.ERR_INVALID
+    assert call(q=C.c_void_p(4104)) == _lib.ERR_INVALID  # q not 16-byte aligned
+    need = lib.ccut_mla_attention_workspace_bytes(3, 16, 1, 300)
+    assert need > 256
+    assert call(ws=need - 1) == _lib.ERR_WORKSPACE

@@ -159,6 +159,19 @@ def _mla(q, kv, causal_start, scale):
     return torch.einsum("shn,nr->shr", p, kvf[:, :512]).reshape(S * H, 512)
 
 
+def _mla_pool(q, pool, layer, slots, starts, scale):
+    """``ccut_mla_attention_pool``: row b over its slot's latent rows ``<= starts[b]`` (zero
+    rows for a slot outside the pool or a negative start)."""
+    outs = []
+    for b in range(q.shape[0]):
+        slot, st = int(slots[b]), int(starts[b])
+        if not (0 <= slot < pool.slots and st >= 0):
+            outs.append(torch.zeros((q.shape[1], 512)))
+            continue
+        outs.append(_mla(q[b:b + 1], pool.k[slot, layer, 0, : st + 1], st, scale))
+    return torch.cat(outs)
+
+
 class _TorchMoe:
     """MoE block with the tiny model's dense experts (softmax routing as the reference)."""
 
@@ -200,6 +213,7 @@ def torch_ops(monkeypatch):
     monkeypatch.setattr(m, "apply_rope", _rope)
     monkeypatch.setattr(m, "_attend", _attend)
     monkeypatch.setattr(m, "_mla_attend", _mla)
+    monkeypatch.setattr(m, "_mla_attend_pool", _mla_pool)
     return m
 
 
@@ -546,12 +560,20 @@ def test_mla_decoder_host_logic_matches_oracle(torch_ops, extra):
         assert _rel(last.numpy(), ref[-1]) < 5e-3
 
 
-def test_mla_decoder_batch_and_backend(torch_ops):
+def test_mla_decoder_batch_and_backend(torch_ops, monkeypatch):
     """forward_batch over MLA caches equals the sequences run alone; the backend's prefix reuse
-    runs on MLA caches; pooled caches are refused for MLA layers."""
+    runs on MLA caches; with pooled latent caches a decode step of several requests is one
+    pooled attention call per layer and generates the same tokens."""
     from ccut_b200.backend import GenericBackend
 
     m = torch_ops
+    calls = []
+
+    def pooled(*a):
+        calls.append(a[0].shape[0])
+        return _mla_pool(*a)
+
+    monkeypatch.setattr(m, "_mla_attend_pool", pooled)
     t = make_tiny(42, mla=MLA_TINY)
     dec = _build_mla(m, t)
     rng = np.random.default_rng(9)
@@ -568,8 +590,18 @@ def test_mla_decoder_batch_and_backend(torch_ops):
     assert be.tokens_run == 4 + 2
     full = dec.forward(ids, dec.new_cache(32))
     assert _rel(be.logits_for(ids).numpy(), full.numpy()) < 2e-2
-    with pytest.raises(NotImplementedError):
-        GenericBackend(dec, max_seqs=2, max_len=32, pool=True)
+    ref = GenericBackend(dec, max_seqs=3, max_len=32)
+    bp = GenericBackend(dec, max_seqs=3, max_len=32, pool=True)
+    assert bp._pool.v is None and tuple(bp._pool.k.shape) == (3, t.layers, 1, 32, 576)
+    a = [[int(x) for x in p] for p in prompts]
+    b = [list(s) for s in a]
+    for _ in range(3):
+        for s, tok in zip(a, ref.generate_batch([(s, {"temperature": 0.0}) for s in a])):
+            s.append(tok)
+        for s, tok in zip(b, bp.generate_batch([(s, {"temperature": 0.0}) for s in b])):
+            s.append(tok)
+    assert a == b
+    assert calls and set(calls) == {3} and len(calls) == 2 * t.layers  # two decode steps after the prefill
 
 
 def test_mla_decoder_checks(torch_ops):
@@ -595,8 +627,8 @@ def test_mla_decoder_checks(torch_ops):
     with pytest.raises(ValueError):
         m.MlaDecoderLayer(*args, softmax_scale=0.0, **kw)
     dec = _build_mla(m, t)
-    with pytest.raises(NotImplementedError):
-        dec.new_pool(2, 16)
+    pool = dec.new_pool(2, 16)
+    assert pool.v is None and pool.cache(1).v is None and tuple(pool.cache(1).k.shape) == (t.layers, 1, 16, 576)
     inv, _ = m.rope_table(64, t.theta)
     with pytest.raises(NotImplementedError):
         m.MoeDecoder(t.embed, dec.layers, t.final_norm, t.lm_head, inv_freq=inv, softcap=30.0, device="cpu")
