@@ -552,6 +552,8 @@ ENGINE_WORKLOADS["cfg2_engine_decode"] = {"moe": "cfg0", "layers": 27, "attn": "
                                           "d_rope": 64, "d_v": 128, "dense_layers": 1, "dense_inter": 10944,
                                           "vocab": 102400, "batch": 32, "prompt": 2048, "pool": False}
 ENGINE_WORKLOADS["cfg2_engine_decode_b1"] = dict(ENGINE_WORKLOADS["cfg2_engine_decode"], batch=1)
+# batch 32 with the latent caches in one pool: one MLA launch per layer and step
+ENGINE_WORKLOADS["cfg2_engine_decode_pool"] = dict(ENGINE_WORKLOADS["cfg2_engine_decode"], pool=True)
 
 
 def run_attn(args, wl) -> None:
