@@ -679,26 +679,17 @@ def run_mla(args, wl) -> None:
     }), flush=True)
 
 
-def run_engine(args, wl) -> None:
-    """Decode steps of a whole synthetic model through ``GenericBackend.generate_batch`` (the
-    call an engine step makes): every step runs one new token per request through all layers
-    (bf16 projections on cuBLAS, RMSNorm / RoPE / GQA or MLA attention / the MoE layer and the
-    dense FFN on this library's kernels) and samples greedily on the device."""
+def engine_model(w: dict, dev):
+    """The seeded synthetic ``MoeDecoder`` of engine workload ``w`` on ``dev``: config
+    ``w["moe"]``'s MoE layer (a ``DenseFfn`` in the first ``dense_layers`` layers), GQA or MLA
+    attention with bf16 projections, a random embedding and ``lm_head``."""
     import torch
 
-    from ccut_b200 import build
-    from ccut_b200.backend import GenericBackend
-    from ccut_b200.layer import MoeLayer
     from ccut_b200.dense import DenseFfn
+    from ccut_b200.layer import MoeLayer
     from ccut_b200.model import DecoderLayer, MlaDecoderLayer, MoeDecoder, rope_table
     from ccut_b200.synthetic import CONFIGS, _gen_matrix, make_layer_device
 
-    if int(os.environ.get("RANK", "0")) != 0:
-        return
-    build.build()
-    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
-    torch.cuda.set_device(dev)
-    w = ENGINE_WORKLOADS[wl]
     c = CONFIGS[w["moe"]]
     mla = w.get("attn") == "mla"
     H, nh = c.hidden, w["heads"]
@@ -737,8 +728,31 @@ def run_engine(args, wl) -> None:
                                        norm_w(H), ffn, norm_w(d), norm_w(d), heads=nh, kv_heads=kvh, head_dim=d,
                                        device=dev))
     inv, af = rope_table(d, 1e4 if mla else 1e6)
-    dec = MoeDecoder(torch.randn((w["vocab"], H), generator=g, device=dev), layers, norm_w(H), mat(w["vocab"], H),
-                     inv_freq=inv, attention_factor=af, device=dev)
+    return MoeDecoder(torch.randn((w["vocab"], H), generator=g, device=dev), layers, norm_w(H), mat(w["vocab"], H),
+                      inv_freq=inv, attention_factor=af, device=dev)
+
+
+def run_engine(args, wl) -> None:
+    """Decode steps of a whole synthetic model (``engine_model``) through
+    ``GenericBackend.generate_batch`` (the call an engine step makes): every step runs one new
+    token per request through all layers (bf16 projections on cuBLAS, RMSNorm / RoPE / GQA or
+    MLA attention / the MoE layer and the dense FFN on this library's kernels) and samples
+    greedily on the device."""
+    import torch
+
+    from ccut_b200 import build
+    from ccut_b200.backend import GenericBackend
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    build.build()
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    w = ENGINE_WORKLOADS[wl]
+    mla = w.get("attn") == "mla"
+    nh = w["heads"]
+    kvh, d = (1, w["d_rope"]) if mla else (w["kv_heads"], w["head_dim"])
+    dec = engine_model(w, dev)
     B, P = w["batch"], w["prompt"]
     be = GenericBackend(dec, max_seqs=B, max_len=P + args.warmup + args.steps + 8, prefill_chunk=P, pool=w["pool"])
     rng = np.random.default_rng(0)
