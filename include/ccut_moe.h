@@ -293,7 +293,8 @@ CCUT_API size_t ccut_mla_attention_workspace_bytes(int batch, int heads, int seq
 CCUT_API int ccut_mla_attention(const float* q, const uint16_t* kv, int batch, int heads, int seq, int kv_len,
                                 int rank, int rope_dim, int causal_start, float scale, void* out, int out_dtype,
                                 void* workspace, size_t ws_bytes, ccut_stream_t stream);
-/* ccut_mla_attention over a pool of latent caches: batch row b attends over slot slots[b]
+/* ccut_mla_attention over a pool of latent caches (mla_decode, ccut/blocks/attn_mla.py:83-124,
+ * for the requests of one engine step at once): batch row b attends over slot slots[b]
  * (int32, device) of kv_pool, whose slots are slot_stride elements apart (>= max_len *
  * (rank + rope_dim), a multiple of 8) and hold max_len rows each, with causal offset
  * starts[b] (int32, device): query s sees positions <= starts[b] + s.  A slot outside
