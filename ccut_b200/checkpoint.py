@@ -202,6 +202,9 @@ def _compressed_tensors_format(q: dict) -> str:
     if kind == "int" and bits == 4 and strategy == "group" and int(w.get("group_size") or 0) == 128:
         if g.get("input_activations") or w.get("actorder") not in (None, False, "none"):
             raise NotImplementedError("compressed-tensors int4 with activation quantization or activation reordering")
+        stored = str(g.get("format") or q.get("format") or "pack-quantized").lower()
+        if stored != "pack-quantized":
+            raise NotImplementedError(f"compressed-tensors int4 stored as {stored!r} (have pack-quantized)")
         return "awq_int4_g128"
     if kind == "float" and bits == 8 and strategy == "block" and [int(v) for v in (w.get("block_structure") or [])] \
             == [128, 128]:

@@ -69,6 +69,10 @@ def test_compressed_tensors_config_resolution():
     with pytest.raises(NotImplementedError):  # W4A8: activations would be quantized
         ck.quant_format({**base, "quantization_config": q})
     q = ct_quant_config("awq_int4_g128")
+    q["format"] = "naive-quantized"  # int4 values stored unpacked, one per int8
+    with pytest.raises(NotImplementedError):
+        ck.quant_format({**base, "quantization_config": q})
+    q = ct_quant_config("awq_int4_g128")
     q["config_groups"]["group_1"] = q["config_groups"]["group_0"]
     with pytest.raises(NotImplementedError):
         ck.quant_format({**base, "quantization_config": q})
