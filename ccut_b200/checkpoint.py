@@ -696,9 +696,9 @@ def load_decoder(model_dir: str | Path, device="cuda", kernel: str = "auto", nam
     (``MoeLayer``) or its dense MLP (``DenseFfn``).  Quantized attention projections stay in
     their format (``quant.QuantLinear``, run by ``ccut_quant_linear``), or with
     ``quantized_projections=False`` are dequantized on the device (``quant.dequantize``) and
-    kept as bf16 for cuBLAS.  RoPE from ``rope_theta`` / ``rope_scaling`` (none or linear;
-    other scalings raise ``NotImplementedError``: build the ``MoeDecoder`` with
-    ``build_rope``'s table).  ``app_config``: the engine's config (``[experts]`` / ``[quant]``,
+    kept as bf16 for cuBLAS.  RoPE from ``rope_theta`` / ``rope_scaling``: the reference's
+    ``build_rope`` table (``rope_table``: none, linear, dynamic, its own yarn), whose attention
+    factor the reference's layer does not apply, and neither does this decoder.  ``app_config``: the engine's config (``[experts]`` / ``[quant]``,
     ``ccut_b200.config``), checked against the checkpoint before anything is uploaded.
 
     MLA checkpoints (DeepSeek-V2 / V3) give ``MlaDecoderLayer`` layers: ``kv_a_proj_with_mqa``

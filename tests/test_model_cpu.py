@@ -76,8 +76,14 @@ def test_rope_tables_match_reference(golden_dir):
     np.testing.assert_allclose(rope_inv_freq(64, 10000.0), g["m0_inv_freq"], rtol=1e-6)
     lin, _ = rope_table(64, 10000.0, {"type": "linear", "factor": 4.0})
     np.testing.assert_allclose(lin, inv / 4.0, rtol=1e-7)
-    with pytest.raises(NotImplementedError):
-        rope_table(64, 10000.0, {"type": "yarn", "factor": 4.0})
+    # the reference's build_rope for yarn (its own formula), dynamic and linear, bit for bit
+    # (tests/golden/rope_tables.npz, made by tests/golden/make_golden_rope.py)
+    r = np.load(golden_dir / "rope_tables.npz")
+    for i in range(int(r["n"])):
+        got, af = rope_table(int(r[f"r{i}_head_dim"]), float(r[f"r{i}_theta"]), json.loads(str(r[f"r{i}_scaling"])))
+        assert np.array_equal(got, r[f"r{i}_inv_freq"]) and af == float(r[f"r{i}_attn_factor"]), i
+    with pytest.raises(ValueError):
+        rope_table(64, 10000.0, {"type": "longrope", "factor": 4.0})
 
 
 def test_sampling_transform_matches_reference(golden_dir):
