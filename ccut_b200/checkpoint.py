@@ -275,6 +275,12 @@ def moe_spec_from_config(config: dict) -> MoeCheckpointSpec:
         routing = "sigmoid_group"
     elif scoring == "softmax":
         routing = "topk_softmax" if norm else "softmax_topk"
+        # DeepSeek-V2's group-limited greedy top-k and its routed scaling of softmax weights are
+        # other routings (the softmax modes here take the top-k over all experts, weights as is)
+        if str(tc.get("topk_method", "greedy")).lower() == "group_limited_greedy" and int(tc.get("n_group") or 1) > 1:
+            raise NotImplementedError("group-limited greedy softmax routing (topk_method = group_limited_greedy)")
+        if float(tc.get("routed_scaling_factor", 1.0) or 1.0) != 1.0:
+            raise NotImplementedError("softmax routing with routed_scaling_factor != 1")
     else:
         raise NotImplementedError(f"scoring_func {scoring!r} is not supported")
     return MoeCheckpointSpec(

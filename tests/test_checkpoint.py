@@ -81,6 +81,13 @@ def test_config_resolution():
     s = ck.moe_spec_from_config(v3)
     assert (s.fmt, s.routing, s.n_group, s.topk_group, s.routed_scaling, s.shared_inter) == \
         ("fp8_b128", "sigmoid_group", 8, 4, 2.5, 2048)
+    # DeepSeek-V2 (not Lite): group-limited greedy softmax routing, routed scaling 16
+    for extra in ({"topk_method": "group_limited_greedy", "n_group": 8, "topk_group": 3},
+                  {"routed_scaling_factor": 16.0}):
+        with pytest.raises(NotImplementedError):
+            ck.moe_spec_from_config({**base, **extra})
+    lite = ck.moe_spec_from_config({**base, "topk_method": "greedy", "n_group": 1, "routed_scaling_factor": 1.0})
+    assert lite.routing == "softmax_topk"
     for bad in ({"quant_method": "gptq", "bits": 4}, {"quant_method": "awq", "bits": 8, "group_size": 128},
                 {"quant_method": "awq", "bits": 4, "group_size": 64},
                 {"quant_method": "fp8", "weight_block_size": [1, 128]}, {"quant_method": "fp8"}):
