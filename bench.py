@@ -206,8 +206,7 @@ def workload_config(wl: str, n: int, parallelism: str) -> dict:
     }
 
 
-# DRAM bytes (read + write) of one gate/up launch from an ncu capture of the same workload
-# (profiles/tc_gemm_kernel_cfg1_prefill.md, profiles/moe_gemm_kernel_cfg0_decode.md);
+# DRAM bytes (read + write) of one gate/up launch from an ncu capture of the same workload;
 # workloads without a capture report null.
 NCU_TRAFFIC = {"cfg1_prefill": 480.6e6, "cfg0_decode": 202.2e6}
 

@@ -144,8 +144,9 @@ FwdScratch carve_fwd(Carver& c, const ccut_moe_layer* L, int T, int k) {
 }
 
 
-// gate/up: h rows [R, I] (f16) from x.  `x16` is the mma.sync path's f16 copy of x;
-// `xp` the tcgen05 path's gather buffer.
+// gate/up: h rows [R, I] from x: bf16 from the tcgen05 kernel, f16 from the mma.sync kernel
+// (run_down reads them with the same kernel).  `x16` is the mma.sync path's f16 copy of x;
+// `xp` the tcgen05 path's bf16 gather buffer.
 int run_gate_up(const ccut_moe_layer* L, long per_expert, const uint16_t* x, const uint16_t* x16, uint16_t* xp,
                 int T, int k, const int32_t* offsets, const int32_t* row_token, uint16_t* hbuf, int* sched, int* status,
                 cudaStream_t st) {
@@ -153,16 +154,15 @@ int run_gate_up(const ccut_moe_layer* L, long per_expert, const uint16_t* x, con
   const int ne = L->num_experts + L->num_shared_slices;
   if (use_tc(L, per_expert)) {
     const int R = static_cast<int>(rows_of(L, T, k));
-    int rc = launch_gather_f16(x, row_token, R, offsets + ne, L->hidden, xp, st);
+    int rc = launch_gather_rows(x, row_token, R, offsets + ne, L->hidden, xp, st);
     if (rc) return rc;
-    const int nt = tc_token_tile(static_cast<int>(per_expert));
     CUtensorMap map;
-    rc = encode_rows_map(&map, xp, R, L->hidden, nt);
+    rc = encode_rows_map(&map, xp, R, L->hidden, kTcBoxRows);
     if (rc) return rc;
     // fused gate/up rows: 2I packed rows, intermediate rows of I channels out
     TcArgs a{static_cast<const uint8_t*>(L->w13), ccut_w13_bytes(fmt, L->hidden, L->inter), L->hidden,
              2 * L->inter, offsets, ne, hbuf, L->inter, nullptr, status};
-    return launch_tc_gemm(fmt, kFfn1, nt, map, a, num_sms(), st);
+    return launch_tc_gemm(fmt, kFfn1, map, a, num_sms(), st);
   }
   if (!x16) return CCUT_ERR_INVALID;
   GemmArgs a{static_cast<const uint8_t*>(L->w13_frags),
@@ -188,13 +188,12 @@ int run_down(const ccut_moe_layer* L, long per_expert, const uint16_t* hbuf, int
   const int ne = L->num_experts + L->num_shared_slices;
   if (use_tc(L, per_expert)) {
     const int R = static_cast<int>(rows_of(L, T, k));
-    const int nt = tc_token_tile(static_cast<int>(per_expert));
     CUtensorMap map;
-    int rc = encode_rows_map(&map, hbuf, R, L->inter, nt);
+    int rc = encode_rows_map(&map, hbuf, R, L->inter, kTcBoxRows);
     if (rc) return rc;
     TcArgs a{static_cast<const uint8_t*>(L->w2), ccut_w2_bytes(fmt, L->hidden, L->inter), L->inter, L->hidden,
              offsets, ne, y_rows, L->hidden, row_weight, status};
-    return launch_tc_gemm(fmt, kFfn2, nt, map, a, num_sms(), st);
+    return launch_tc_gemm(fmt, kFfn2, map, a, num_sms(), st);
   }
   GemmArgs a{static_cast<const uint8_t*>(L->w2_frags),
              ccut_w2_bytes(fmt, L->hidden, L->inter),
@@ -517,15 +516,12 @@ int ccut_quant_linear(int format, int layout, const void* packed, int K, int N, 
   uint16_t* x16 = c.take<uint16_t>((size_t)M * K);
   int rc = launch_fill_offsets(off, M, stream);
   if (rc) return rc;
-  if (layout == CCUT_LAYOUT_ROWS) {
-    rc = launch_gather_f16(x, nullptr, M, nullptr, K, x16, stream);
-    if (rc) return rc;
-    const int nt = tc_token_tile(M);
+  if (layout == CCUT_LAYOUT_ROWS) {  // x is already [M, K] bf16 rows: the TMA reads it in place
     CUtensorMap map;
-    rc = encode_rows_map(&map, x16, M, K, nt);
+    rc = encode_rows_map(&map, x, M, K, kTcBoxRows);
     if (rc) return rc;
     TcArgs a{static_cast<const uint8_t*>(packed), 0, K, N, off, 1, y, N, nullptr, status};
-    return launch_tc_gemm(format, kFfn2, nt, map, a, num_sms(), stream);
+    return launch_tc_gemm(format, kFfn2, map, a, num_sms(), stream);
   }
   rc = launch_bf16_to_f16(x, x16, (size_t)M * K, stream);
   if (rc) return rc;

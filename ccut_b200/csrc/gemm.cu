@@ -23,16 +23,6 @@
 
 namespace ccut {
 
-// Debug-only per-CTA cycle counters of the role waits (built only with -DCCUT_GEMM_PROFILE).
-#ifdef CCUT_GEMM_PROFILE
-__device__ unsigned long long g_gemm_prof[1024][8];
-#define GM_PROF_START(v) const long long v = clock64()
-#define GM_PROF_ADD(slot, v) atomicAdd(&g_gemm_prof[blockIdx.x & 1023][slot], (unsigned long long)(clock64() - (v)))
-#else
-#define GM_PROF_START(v)
-#define GM_PROF_ADD(slot, v)
-#endif
-
 template <int FMT, int MODE, int MT>
 struct GemmCfg {
   using B = Blk<FMT>;
@@ -100,10 +90,7 @@ __device__ __forceinline__ bool consume_item(const GemmArgs& a, uint8_t* stages,
   for (int kt = 0; kt < nstages; ++kt, ++use) {
     const int s = use % S;
     const int nq = C::kKG > 1 ? min(C::kKG, ktiles - kt * C::kKG) : Q;  // slots staged
-    GM_PROF_START(c0);
     if (!mbar_wait(&full[s], (use / S) & 1, a.status)) return false;
-    if (threadIdx.x == 0) GM_PROF_ADD(1, c0);
-    GM_PROF_START(c1);
     const uint8_t* st = stages + s * C::kStageBytes;
     const uint8_t* xs = st + C::kWBytes;
     float part[Q][MT / 8][4];
@@ -192,7 +179,6 @@ __device__ __forceinline__ bool consume_item(const GemmArgs& a, uint8_t* stages,
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
-    if (threadIdx.x == 0) GM_PROF_ADD(2, c1);
     // promote: acc += scale * partial (fp32); k-group slots share one accumulator
 #pragma unroll
     for (int m = 0; m < Q; ++m)
@@ -227,7 +213,6 @@ __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT,
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntiles = a.N / kTileN, ktiles = a.K / kTileK;
-  GM_PROF_START(t_kernel);
 
   if (warp == 0) {  // item prefix over experts: tiles(e) = ceil(M_e / MT) * ntiles
     int carry = 0;
@@ -288,12 +273,10 @@ __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT,
         const uint32_t wbytes = nq * C::kNMat * B::kBytes, xbytes = nq * kTileK * 2;
         const int s = use % S;
         const uint32_t ph = (use / S) & 1;
-        GM_PROF_START(p0);
         if (!mbar_wait(&empty[s], ph ^ 1, a.status)) {
           ok = false;
           break;
         }
-        if (lane == 0) GM_PROF_ADD(0, p0);
         uint8_t* st = stages + s * C::kStageBytes;
         if (lane == 0) {
           if (kt == 0) slot_item[s] = item;
@@ -370,7 +353,6 @@ __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT,
     if (!alive) return;
 
     // ---------------- epilogue ----------------
-    GM_PROF_START(c2);
     const int row0 = a.offsets[e] + m0;
     const int n_lo = nt * kTileN + ch_lo, n_hi = n_lo + 8;
 #pragma unroll
@@ -394,21 +376,9 @@ __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT,
         }
       }
     }
-    if (threadIdx.x == 0) GM_PROF_ADD(3, c2);
   }
-  if (threadIdx.x == 0) GM_PROF_ADD(4, t_kernel);
 }
 
-#ifdef CCUT_GEMM_PROFILE
-extern "C" __attribute__((visibility("default"))) int ccut_debug_gemm_prof(unsigned long long* host, int clear) {
-  if (cudaMemcpyFromSymbol(host, g_gemm_prof, sizeof(g_gemm_prof)) != cudaSuccess) return CCUT_ERR_CUDA;
-  if (clear) {
-    static unsigned long long zeros[1024][8];
-    if (cudaMemcpyToSymbol(g_gemm_prof, zeros, sizeof(zeros)) != cudaSuccess) return CCUT_ERR_CUDA;
-  }
-  return CCUT_OK;
-}
-#endif
 
 template <int FMT, int MODE, int MT>
 static int launch_gemm_t(const GemmArgs& a, int num_sms, cudaStream_t st) {

@@ -23,9 +23,9 @@ struct Carver {
   }
 };
 
-// Expert-FFN scratch.  Row layout (tcgen05): xp = f16 activations gathered in expert
+// Expert-FFN scratch.  Row layout (tcgen05): xp = bf16 activations gathered in expert
 // order [R, H].  Fragment layout (mma.sync): x16 = f16 copy of x [T, H].
-// Both: intermediate rows [R, I] (f16).
+// Both: intermediate rows [R, I] (bf16 from tcgen05, f16 from mma.sync).
 struct FfnScratch {
   uint16_t* x16;
   uint16_t* xp;

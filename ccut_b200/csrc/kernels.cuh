@@ -40,16 +40,17 @@ struct TcArgs {
   int* status;
 };
 
-// tc_gemm.cu
-int tc_token_tile(int rows_per_expert);
-int launch_tc_gemm(int fmt, int mode, int nt_tokens, const CUtensorMap& map, const TcArgs& a, int num_sms,
-                   cudaStream_t st);
-// tmap.cu: 2-D f16 tensor map over a row-major [rows, cols] buffer, boxes of 64 x box_rows,
+// tc_gemm.cu: the activation operand `map` covers bf16 rows [R, K] in expert order (boxes
+// of 64 x 128, encode_rows_map)
+int launch_tc_gemm(int fmt, int mode, const CUtensorMap& map, const TcArgs& a, int num_sms, cudaStream_t st);
+// tmap.cu: 2-D bf16 tensor map over a row-major [rows, cols] buffer, boxes of 64 x box_rows,
 // 128-byte swizzle (host side)
 int encode_rows_map(CUtensorMap* map, const void* base, int rows, int cols, int box_rows);
-// nrows: device row count bound (rows >= *nrows are left alone), or null
-int launch_gather_f16(const uint16_t* x_bf16, const int32_t* row_token, int R, const int* nrows, int H,
-                      uint16_t* xp, cudaStream_t st);
+constexpr int kTcBoxRows = 128;  // token rows per CTA and stage of the tcgen05 GEMM
+// xp[r] = x[row_token[r]] (bf16 rows in expert order); nrows: device row count bound (rows
+// >= *nrows are left alone), or null
+int launch_gather_rows(const uint16_t* x_bf16, const int32_t* row_token, int R, const int* nrows, int H,
+                       uint16_t* xp, cudaStream_t st);
 
 // pack.cu
 int launch_pack(int fmt, int layout, const void* q, const void* z, const void* s, int K, int N, int nibble_order,

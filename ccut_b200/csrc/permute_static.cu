@@ -10,13 +10,16 @@
 //
 // Scratch: kStaticCounters int32 counters (one per routed expert), zeroed on the stream by
 // every call before the counting kernel runs.  Nothing the caller passes must start at
-// zero; pair_row is filled with -1 by the call itself, as in ccut_moe_permute.
+// zero: the permutation kernel writes every pair_row entry itself (-1 for a pair without an
+// expert), exactly as in ccut_moe_permute.  Like ccut_moe_permute, a call of at most 256
+// tokens launches its kernels with programmatic dependent launch.
 //
 // Setup: the first call on each device (with that device current) resolves the device
 // address of the array once with cudaGetSymbolAddress and caches it.  Make that first call
 // before any stream capture begins.  The array is shared by every call on a device, so
 // calls that overlap in time on one device (two streams, two host threads) race on it;
 // serialise them.
+#include <atomic>
 #include <mutex>
 
 #include "kernels.cuh"
@@ -32,19 +35,24 @@ constexpr int kMaxTopKStatic = 16;
 static __device__ __align__(256) int g_permute_counts[kStaticCounters];
 
 std::mutex g_setup_mutex;
-int* g_counts_ptr[kMaxDevices] = {nullptr};
+std::atomic<int*> g_counts_ptr[kMaxDevices];
 
-// Device address of g_permute_counts on the current device (nullptr on failure).
+// Device address of g_permute_counts on the current device (nullptr on failure).  After the
+// first call on a device this is one atomic load; the lock only guards the lookup itself.
 int* static_counts() {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  int* cached = g_counts_ptr[dev].load(std::memory_order_acquire);
+  if (cached) return cached;
   std::lock_guard<std::mutex> lock(g_setup_mutex);
-  if (!g_counts_ptr[dev]) {
+  cached = g_counts_ptr[dev].load(std::memory_order_relaxed);
+  if (!cached) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_permute_counts) != cudaSuccess || !p) return nullptr;
-    g_counts_ptr[dev] = static_cast<int*>(p);
+    cached = static_cast<int*>(p);
+    g_counts_ptr[dev].store(cached, std::memory_order_release);
   }
-  return g_counts_ptr[dev];
+  return cached;
 }
 
 }  // namespace
@@ -63,8 +71,7 @@ extern "C" int ccut_moe_permute_static(const int32_t* ids, const float* weights,
   if (!offsets || !row_token || !row_weight || !pair_row || (T > 0 && (!ids || !weights))) return CCUT_ERR_INVALID;
   int* counts = static_counts();
   if (!counts) return CCUT_ERR_CUDA;
-  if (T > 0 && cudaMemsetAsync(pair_row, 0xFF, sizeof(int32_t) * (size_t)T * k, stream) != cudaSuccess)
-    return CCUT_ERR_CUDA;
+  PdlScope pdl_scope(T);  // PDL for decode-sized calls, as in ccut_moe_permute
   int rc = launch_count(ids, T * k, E, counts, stream);  // zeroes counts[0, E) first
   if (rc) return rc;
   return launch_permute(ids, weights, T, k, E, num_shared_slices, shared_gate, counts, offsets, row_token,

@@ -121,5 +121,119 @@ CCUT_DEVICE void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// ---- CTA pairs (cta_group::2): one MMA of M = 256 spans the tensor cores of two SMs -------
+// A cluster of two CTAs: rank 0 (the "leader") issues the MMAs; each CTA holds its 128 rows
+// of A and its half of the N columns of B in its own shared memory at the same offsets, and
+// its 128 rows of D in its own tensor memory.
+
+CCUT_DEVICE uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+CCUT_DEVICE void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// shared::cluster address of the object at the same offset as `local` in CTA `rank` of the cluster.
+CCUT_DEVICE uint32_t mapa(const void* local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
+  return r;
+}
+
+CCUT_DEVICE void tmem_alloc2(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+CCUT_DEVICE void tmem_relinquish2() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::); }
+CCUT_DEVICE void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Instruction descriptor, kind::f16 with A = B = bf16, D = f32, both K-major, M = 256.
+CCUT_DEVICE uint32_t idesc_bf16_m256(uint32_t n) {
+  return (1u << 4)            // D format f32
+         | (1u << 7)          // A bf16
+         | (1u << 10)         // B bf16
+         | ((n >> 3) << 17)   // N / 8
+         | ((256u >> 4) << 24);  // M / 16
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc] over the CTA pair; issued by one thread of rank 0.
+CCUT_DEVICE void mma_ss2(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive once on the mbarrier at the same offset as `bar` in every CTA of `mask`, when all
+// MMAs this thread issued before it have completed.
+CCUT_DEVICE void commit2_mc(uint64_t* bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(mask)
+      : "memory");
+}
+
+// Arrive on an mbarrier given by its shared::cluster address (this CTA's or the peer's).
+CCUT_DEVICE void mbar_arrive_cl(uint32_t cl_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cl_addr) : "memory");
+}
+CCUT_DEVICE void mbar_arrive_expect_tx_cl(uint32_t cl_addr, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(cl_addr), "r"(bytes)
+               : "memory");
+}
+// Wait on a barrier of this CTA that arrivals from the peer CTA complete (cluster-scope
+// acquire), bounded like mbar_spin.
+CCUT_DEVICE bool mbar_try_wait_cl(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+CCUT_DEVICE bool mbar_wait_cl(uint64_t* bar, uint32_t parity, int* status) {
+  if (mbar_try_wait_cl(bar, parity)) return true;
+  long long t0 = clock64();
+  while (!mbar_try_wait_cl(bar, parity)) {
+    if (clock64() - t0 > kWaitBudgetCycles) {
+      record_error(status, CCUT_ERR_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
+// TMA tiled load into this CTA's shared memory whose completion is counted on the mbarrier
+// at shared::cluster address `bar_cl` (the pair leader's), no multicast.
+CCUT_DEVICE void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y, uint32_t bar_cl) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cl)
+      : "memory");
+}
+
+// Shared-memory writes of this thread become visible to the tensor cores' async proxy.
+CCUT_DEVICE void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+template <uint32_t N>
+CCUT_DEVICE void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+CCUT_DEVICE void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 }  // namespace tc
 }  // namespace ccut

@@ -1,8 +1,8 @@
 // tmap.cu -- TMA tensor maps for the activation operand, and the row gather that feeds it.
 //
 // The activation rows of the grouped GEMM must be contiguous per expert for tiled TMA
-// loads, so the gate/up input is first gathered into expert-sorted order (and converted
-// to f16, the MMA operand type): xp[r] = f16(x[row_token[r]]).
+// loads, so the gate/up input is first gathered into expert-sorted order: xp[r] =
+// x[row_token[r]], bf16 as given (the MMA operand type).
 #include <cudaTypedefs.h>
 
 #include "kernels.cuh"
@@ -29,14 +29,14 @@ int encode_rows_map(CUtensorMap* map, const void* base, int rows, int cols, int 
   cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
   cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? CCUT_OK : CCUT_ERR_CUDA;
 }
 
-__global__ void gather_f16_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ row_token, int R,
-                                  const int* __restrict__ nrows, int H, uint16_t* __restrict__ xp) {
+__global__ void gather_rows_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ row_token, int R,
+                                   const int* __restrict__ nrows, int H, uint16_t* __restrict__ xp) {
   pdl_wait();
   pdl_trigger();
   const int per_row = H / 8;
@@ -45,25 +45,17 @@ __global__ void gather_f16_kernel(const uint16_t* __restrict__ x, const int32_t*
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const int r = static_cast<int>(i / per_row), c = static_cast<int>(i % per_row);
     const int t = row_token ? row_token[r] : r;
-    const uint4 v = *reinterpret_cast<const uint4*>(x + (size_t)t * H + 8 * c);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-    uint32_t o[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const __half2 h = __floats2half2_rn(__uint_as_float(w[j] << 16), __uint_as_float(w[j] & 0xffff0000u));
-      o[j] = *reinterpret_cast<const uint32_t*>(&h);
-    }
-    *reinterpret_cast<uint4*>(xp + (size_t)r * H + 8 * c) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4*>(xp + (size_t)r * H + 8 * c) = *reinterpret_cast<const uint4*>(x + (size_t)t * H + 8 * c);
   }
 }
 
-int launch_gather_f16(const uint16_t* x_bf16, const int32_t* row_token, int R, const int* nrows, int H, uint16_t* xp,
-                      cudaStream_t st) {
+int launch_gather_rows(const uint16_t* x_bf16, const int32_t* row_token, int R, const int* nrows, int H,
+                       uint16_t* xp, cudaStream_t st) {
   size_t total = (size_t)R * (H / 8);
   size_t blocks = (total + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
   if (blocks < 1) blocks = 1;
-  return launch_k(gather_f16_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st, x_bf16, row_token, R,
+  return launch_k(gather_rows_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st, x_bf16, row_token, R,
                   nrows, H, xp);
 }
 

@@ -32,7 +32,7 @@ from ccut_b200 import _lib
 from ccut_b200.ep import expert_range
 from ccut_b200.layer import MoeLayer, Routing, _dev, _ptr, _stream
 
-__all__ = ["AllToAllMoeLayer", "exchange_plan"]
+__all__ = ["AllToAllMoeLayer", "exchange_plan", "compact_local_ids"]
 
 
 def exchange_plan(ids: torch.Tensor, world: int, bounds: list[tuple[int, int]]):
@@ -56,6 +56,22 @@ def exchange_plan(ids: torch.Tensor, world: int, bounds: list[tuple[int, int]]):
     lo_d, hi_d = los[dest][:, None], his[dest][:, None]
     local_ids = torch.where((sid >= lo_d) & (sid < hi_d), sid - lo_d, torch.full_like(sid, -1))
     return order, counts, local_ids.to(torch.int32)
+
+
+def compact_local_ids(local_ids: torch.Tensor, weights: torch.Tensor, num_local: int):
+    """Narrow received rows ``local_ids [R, k]`` / ``weights [R, k]`` to ``min(k, num_local)``
+    columns: a row's ids are distinct experts, so at most ``num_local`` of them are this rank's
+    (>= 0); those move to the front in their original order (a stable sort), so the combine
+    still sums them in slot order.  The expert FFN refuses a width above the rank's expert count
+    (``ccut_moe_expert_ffn`` checks ``k <= num_experts``), which a split with fewer local
+    experts than ``top_k`` (e.g. 64 experts, top-6, 16 ranks) would otherwise hit."""
+    R, k = local_ids.shape
+    kk = min(k, int(num_local))
+    if kk >= k:
+        return local_ids, weights
+    foreign = (local_ids < 0).to(torch.int8)
+    order = torch.argsort(foreign, dim=1, stable=True)[:, :kk]
+    return torch.gather(local_ids, 1, order).contiguous(), torch.gather(weights, 1, order).contiguous()
 
 
 class _GpuExperts:
@@ -94,9 +110,11 @@ class _GpuExperts:
         return ids, wts
 
     def routed(self, rows: torch.Tensor, local_ids: torch.Tensor, weights: torch.Tensor) -> torch.Tensor:
-        R, k = local_ids.shape
+        R = local_ids.shape[0]
         if R == 0:
             return torch.zeros((0, self.hidden), dtype=torch.float32, device=self.device)
+        local_ids, weights = compact_local_ids(local_ids, weights, self.local.num_experts)
+        k = local_ids.shape[1]
         perm = self.local.permute(Routing(local_ids, weights))
         y = self.local.expert_ffn(rows, perm, k)
         return self.local.combine(y, perm, R, k, out_dtype=torch.float32)

@@ -288,7 +288,8 @@ class MoeLayer:
         return y[:R]
 
     def gate_up(self, x: torch.Tensor, perm: Permutation, k: int | None = None) -> torch.Tensor:
-        """Intermediate rows h [R, I] (16-bit bit patterns: bf16 for AWQ, f16 for FP8)."""
+        """Intermediate rows h [R, I] as 16-bit bit patterns: bf16 when the call runs the tcgen05
+        kernel, f16 when it runs the mma.sync kernel; ``down`` reads them back with the same kernel."""
         x = self._check_x(x)
         T = x.shape[0]
         k = k or self.top_k

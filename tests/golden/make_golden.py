@@ -65,8 +65,11 @@ def small_cfg(fmt: str, routing: str, top_k: int, shared: int) -> inputs.MoeLaye
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("CCUT_REFERENCE", "/root/reference/python"))
+    ap.add_argument("--reference", default=os.environ.get("CCUT_REFERENCE"),
+                    help="the reference's python/ directory (or set CCUT_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("--reference (or CCUT_REFERENCE) must name the reference\'s python/ directory")
     rmoe, rgen, rk, rwo, MoeSpec, LayerQuantSpec, ScaleDesc, get_quant_key = _import_reference(Path(args.reference))
     rng = np.random.default_rng(20240601)
 

@@ -54,8 +54,11 @@ CHUNKS = (4, 1, 1, 1, 2)
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference/python")
+    ap.add_argument("--reference", default=os.environ.get("CCUT_REFERENCE"),
+                    help="the reference's python/ directory (or set CCUT_REFERENCE)")
     args = ap.parse_args(argv)
+    if not args.reference:
+        ap.error("--reference (or CCUT_REFERENCE) must name the reference\'s python/ directory")
     os.environ.setdefault("NUMBA_CACHE_DIR", tempfile.mkdtemp(prefix="ccut-numba-"))
     sys.dont_write_bytecode = True
     sys.path.insert(0, args.reference)

@@ -27,6 +27,69 @@ def test_exchange_plan():
     assert lids.tolist() == [[0, 1], [2, -1], [1, 2], [-1, 1], [0, -1]]
 
 
+class _FakeLocal:
+    """The rank's MoeLayer on the CPU, with the C ABI's argument rules: the permutation takes ids
+    in [-1, E) only, and the expert FFN refuses a width k above the rank's expert count
+    (``ccut_moe_expert_ffn`` returns CCUT_ERR_INVALID, raised as ValueError).  Expert e maps a
+    row to (e + 1) * row."""
+
+    def __init__(self, num_experts):
+        self.num_experts = num_experts
+
+    def permute(self, routing):
+        ids = routing.ids
+        assert int(ids.min()) >= -1 and int(ids.max()) < self.num_experts
+        return routing
+
+    def expert_ffn(self, rows, perm, k):
+        if k > self.num_experts:
+            raise ValueError("invalid argument or shape")
+        ids, w = perm.ids.long(), perm.weights
+        f = (ids + 1).clamp(min=0).float()[:, :, None] * rows[:, None, :]
+        return torch.where(ids[:, :, None] >= 0, w[:, :, None] * f, torch.zeros_like(f))
+
+    def combine(self, y, perm, R, k, out_dtype=torch.float32):
+        out = torch.zeros((R, y.shape[2]), dtype=torch.float32)
+        for j in range(k):  # slot order, as combine_kernel sums
+            out += y[:, j]
+        return out.to(out_dtype)
+
+
+@pytest.mark.parametrize("num_local,k", [(1, 2), (2, 6), (3, 8), (6, 6)])
+def test_routed_rows_narrowed_to_local_experts(num_local, k):
+    """A rank that owns fewer experts than top_k (e.g. 64 experts, top-6 over 16 ranks gives 4)
+    still runs its received rows: each row's local ids are narrowed to min(k, E_local) columns
+    before the permutation, keeping their slot order, and the partial outputs are unchanged."""
+    from types import SimpleNamespace
+
+    from ccut_b200.ep_a2a import _GpuExperts, compact_local_ids
+
+    g = torch.Generator().manual_seed(num_local * 31 + k)
+    R, H = 9, 5
+    lids = torch.full((R, k), -1, dtype=torch.int32)
+    for r in range(R):  # distinct local experts at random slots, like a received row
+        n = int(torch.randint(0, min(k, num_local) + 1, (1,), generator=g))
+        slots = torch.randperm(k, generator=g)[:n]
+        lids[r, slots] = torch.randperm(num_local, generator=g)[:n].int()
+    w = torch.rand((R, k), generator=g)
+    rows = torch.randn((R, H), generator=g)
+    expect = torch.zeros((R, H))
+    for r in range(R):
+        for j in range(k):
+            if lids[r, j] >= 0:
+                expect[r] += w[r, j] * (int(lids[r, j]) + 1) * rows[r]
+    nl, nw = compact_local_ids(lids, w, num_local)
+    assert nl.shape == (R, min(k, num_local))
+    for r in range(R):  # same valid ids in the same order
+        assert [int(v) for v in lids[r] if v >= 0] == [int(v) for v in nl[r] if v >= 0]
+    impl = SimpleNamespace(local=_FakeLocal(num_local), hidden=H, device="cpu")
+    got = _GpuExperts.routed(impl, rows, lids, w)
+    torch.testing.assert_close(got, expect, rtol=1e-6, atol=1e-6)
+    if k > num_local:  # without the narrowing the FFN call is refused
+        with pytest.raises(ValueError):
+            _FakeLocal(num_local).expert_ffn(rows, SimpleNamespace(ids=lids, weights=w), k)
+
+
 class _OracleExperts:
     """The oracle in place of the GPU side of one rank."""
 

@@ -81,6 +81,33 @@ def test_static_scratch_matches_workspace_entry_point(T, k, E, slices):
             assert torch.equal(a, b), f"{name} differs (seed {seed})"
 
 
+@pytest.mark.parametrize("case", ["unrouted", "empty"])
+def test_static_scratch_unrouted_pairs_and_empty_batch(case):
+    """Pairs without an expert (-1, or an id of E or more) get pair_row -1 from the kernel
+    itself (the outputs start at -7, so a missing write would show), and T = 0 writes the
+    offsets only; bit-exact against the workspace entry point, two calls in a row."""
+    T, k, E, slices = (50, 4, 16, 1) if case == "unrouted" else (0, 4, 16, 2)
+    for seed in (21, 22):
+        if T:
+            ids, w = _routing(T, k, E, seed)
+            rng = np.random.default_rng(seed)
+            bad = torch.from_numpy(rng.choice(np.array([-1, E, E + 3], np.int32), size=(T, k))).cuda()
+            drop = torch.from_numpy(rng.random((T, k)) < 0.3).cuda()
+            ids = torch.where(drop, bad, ids).contiguous()
+        else:
+            ids = torch.zeros((0, k), dtype=torch.int32, device="cuda")
+            w = torch.zeros((0, k), dtype=torch.float32, device="cuda")
+        ref = _permute_workspace(ids, w, T, k, E, slices, 0.5)
+        got = _permute_static(ids, w, T, k, E, slices, 0.5)
+        torch.cuda.synchronize()
+        for name, a, b in zip(("offsets", "row_token", "row_weight", "pair_row"), got, ref):
+            assert torch.equal(a, b), f"{name} differs (seed {seed})"
+        if T:
+            assert torch.equal(got[3].view(T, k) == -1, drop), "pair_row -1 exactly where unrouted"
+        else:
+            assert got[0].tolist() == [0] * (E + 1) + [0] * slices
+
+
 def test_static_scratch_rejects_too_many_experts():
     ids, w = _routing(8, 2, 8, 0)
     with pytest.raises(NotImplementedError):
