@@ -54,7 +54,9 @@ struct TcCfg {
   static constexpr bool kAwq = FMT == CCUT_FMT_AWQ_INT4_G128;
   static constexpr int kMaxN = 256;                   // tokens per tile (both ranks)
   static constexpr int kHalfW = kAwq ? 4096 : 8192;   // packed weights of one 64-k half block
-  static constexpr int kMeta = kAwq ? 64 : 0;         // AWQ zero points of the block's 128 rows
+  // Metadata copied with each stage: AWQ scales + zero points (the dequant reads the zero
+  // points), the FP8 scale slot; this also brings the scales the epilogue reads into L2.
+  static constexpr int kMeta = kAwq ? 320 : 16;
   static constexpr int kWBytes = kHalfW + kMeta;      // one weight stage (multiple of 16)
   static constexpr int kAB = 32768;                   // A tile 16 KB + B tile 16 KB
   static constexpr int kSA = 5;                       // A/B stages
@@ -105,13 +107,22 @@ __device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
   asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
   return r;
 }
-// Two e4m3 bytes (low byte = element 0) -> bf16x2, exact for every code (NaN stays NaN).
-__device__ __forceinline__ uint32_t e4m3x2_to_bf16x2(uint16_t v) {
-  const uint32_t h = e4m3x2_to_f16x2(v);
-  const float lo = __half2float(__ushort_as_half(static_cast<uint16_t>(h & 0xffffu)));
-  const float hi = __half2float(__ushort_as_half(static_cast<uint16_t>(h >> 16)));
-  const __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<const uint32_t*>(&b);
+// Bytes `sel` of a word of e4m3 codes -> bf16x2 with integer / bf16 FMA-pipe operations only
+// (the conversion pipe is left to the epilogue's exp / reciprocal).  The code's 7 magnitude
+// bits placed at bf16 bits [10:4] read as e4m3 * 2^-120 (exponent field E, mantissa M; for
+// E = 0 a bf16 subnormal 0.M * 2^-126, again e4m3 * 2^-120), so one bf16 multiply by +-2^120,
+// carrying the sign, gives the e4m3 value exactly, subnormals and zeros included.  The two
+// NaN codes (0x7F, 0xFF) come out as +-480: valid FP8 checkpoints do not hold them (the debug
+// export and the mma.sync kernel keep them NaN).
+template <uint32_t kSel>  // prmt selector placing the two codes at bits [15:8] and [31:24]
+__device__ __forceinline__ uint32_t e4m3x2_to_bf16x2(uint32_t w) {
+  uint32_t x, mag, sgn, r;
+  asm("prmt.b32 %0, %1, 0, %2;" : "=r"(x) : "r"(w), "n"(kSel));
+  asm("shr.b32 %0, %1, 4;" : "=r"(mag) : "r"(x));
+  asm("and.b32 %0, %1, 0x07F007F0;" : "=r"(mag) : "r"(mag));
+  asm("lop3.b32 %0, %1, 0x80008000, 0x7B807B80, 0xEA;" : "=r"(sgn) : "r"(x));  // (x & 0x80008000) | 2^120
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(mag), "r"(sgn));
+  return r;
 }
 
 // Row r of a staged 64-k half block -> 64 bf16 weights (unscaled) as row r of the A tile,
@@ -126,7 +137,10 @@ __device__ __forceinline__ void dequant_row(const uint8_t* half, const uint8_t* 
       const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
       uint32_t o[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = e4m3x2_to_bf16x2(static_cast<uint16_t>(w4[i >> 1] >> (16 * (i & 1))));
+      for (int i = 0; i < 4; ++i) {
+        o[2 * i] = e4m3x2_to_bf16x2<0x1404>(w4[i]);      // bytes 0, 1
+        o[2 * i + 1] = e4m3x2_to_bf16x2<0x3424>(w4[i]);  // bytes 2, 3
+      }
       *reinterpret_cast<uint4*>(arow + (((2 * c) ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
       *reinterpret_cast<uint4*>(arow + (((2 * c + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
     }
@@ -257,7 +271,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
         const uint8_t* wb = a.w + (size_t)e * a.expert_stride + (size_t)(valid ? blk : 0) * ktiles * BK::kBytes;
         for (int st = 0; st < nstages; ++st, ++use) {
           const int s = use % SW;
-          if (!mbar_spin(&wempty[s], ((use / SW) & 1) ^ 1, a.status)) {
+          // a suspending wait: a spinning warp would take issue slots from the dequant warp
+          // that shares its SM sub-partition
+          if (!mbar_wait(&wempty[s], ((use / SW) & 1) ^ 1, a.status)) {
             ok = false;
             break;
           }
@@ -266,7 +282,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
             const uint8_t* blkp = wb + (size_t)(st >> 1) * BK::kBytes;
             mbar_arrive_expect_tx(&wfull[s], C::kWBytes);
             bulk_g2s(sb, blkp + (st & 1) * C::kHalfW, C::kHalfW, &wfull[s]);
-            if constexpr (C::kAwq) bulk_g2s(sb + C::kHalfW, blkp + BK::kZeroOff, C::kMeta, &wfull[s]);
+            bulk_g2s(sb + C::kHalfW, blkp + BK::kScaleOff, C::kMeta, &wfull[s]);
           } else {
             mbar_arrive(&wfull[s]);
           }
@@ -305,14 +321,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
         const uint32_t idesc = tc::idesc_bf16_m256((uint32_t)n);
         for (int kb = 0; kb < nkb && ok; ++kb, ++j) {
           const int slot = j & 1;
-          if (!tc::mbar_wait_cl(&pempty[slot], ((j >> 1) & 1) ^ 1, a.status)) {
+          if (!tc::mbar_spin_cl(&pempty[slot], ((j >> 1) & 1) ^ 1, a.status)) {
             ok = false;
             break;
           }
           tc::fence_after_sync();
           for (int h = 0; h < 2; ++h, ++use) {
             const int sa = use % SA;
-            if (!tc::mbar_wait_cl(&abfull[sa], (use / SA) & 1, a.status)) {
+            if (!tc::mbar_spin_cl(&abfull[sa], (use / SA) & 1, a.status)) {
               ok = false;
               break;
             }
@@ -349,7 +365,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
         }
         if (valid) {
           const uint8_t* half = wtiles + s * C::kWBytes;
-          dequant_row<FMT>(half, half + C::kHalfW, r, ab + sa * C::kAB);
+          dequant_row<FMT>(half, half + C::kHalfW + (C::kAwq ? 256 : 0), r, ab + sa * C::kAB);
         }
         tc::fence_proxy_async_smem();
         __syncwarp();
@@ -380,9 +396,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
       float tot[128];
 #pragma unroll
       for (int i = 0; i < 128; ++i) tot[i] = 0.f;
+      // scales of k-blocks kb and kb + 1 in flight while kb is promoted (their loads are
+      // issued two blocks ahead, so the global-load latency stays off the promotion path)
+      float s_cur = valid ? block_scale<FMT, MODE>(wb, r) : 0.f;
+      float s_nxt = (valid && nkb > 1) ? block_scale<FMT, MODE>(wb + BK::kBytes, r) : 0.f;
       for (int kb = 0; kb < nkb; ++kb, ++j) {
         const int slot = j & 1;
-        const float s = valid ? block_scale<FMT, MODE>(wb + (size_t)kb * BK::kBytes, r) : 0.f;
+        const float s = s_cur;
+        s_cur = s_nxt;
+        s_nxt = (valid && kb + 2 < nkb) ? block_scale<FMT, MODE>(wb + (size_t)(kb + 2) * BK::kBytes, r) : 0.f;
         if (!tc::mbar_wait_cl(&pfull[slot], (j >> 1) & 1, a.status)) {
           ok = false;
           break;
@@ -416,14 +438,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
             }
             named_bar(1 + ewg, 128);
             if (q < 2) {
-              uint16_t* orow = static_cast<uint16_t*>(a.out) + (size_t)(row0 + ewg * 128 + c) * a.out_ld + ch;
+              // all 32 values first (no branch between them, so their exp / reciprocal
+              // latencies overlap), then the stores, guarded only on a partial chunk
+              uint16_t hv[32];
 #pragma unroll
               for (int i = 0; i < 32; ++i) {
-                if (ewg * 128 + c + i < rows) {
-                  const float g = tot[c + i];
-                  const float hv = __fdividef(g, 1.0f + __expf(-g)) * xb[r * C::kXRow + i];
-                  orow[(size_t)i * a.out_ld] = __bfloat16_as_ushort(__float2bfloat16_rn(hv));
-                }
+                const float g = tot[c + i];
+                hv[i] = __bfloat16_as_ushort(__float2bfloat16_rn(__fdividef(g, 1.0f + __expf(-g)) * xb[r * C::kXRow + i]));
+              }
+              uint16_t* orow = static_cast<uint16_t*>(a.out) + (size_t)(row0 + ewg * 128 + c) * a.out_ld + ch;
+              const int left = rows - (ewg * 128 + c);
+              if (left >= 32) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) orow[(size_t)i * a.out_ld] = hv[i];
+              } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                  if (i < left) orow[(size_t)i * a.out_ld] = hv[i];
               }
             }
             named_bar(1 + ewg, 128);
@@ -435,13 +466,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
         for (int c = 0; c < 128; c += 32) {
           if (c < ncols) {
             const int t0 = ewg * 128 + c;
+            const int left = rows - t0;
             float* orow = static_cast<float*>(a.out) + (size_t)(row0 + t0) * a.out_ld + ch;
+            float v[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              if (t0 + i < rows) {
-                const float wr = a.row_weight ? __ldg(a.row_weight + row0 + t0 + i) : 1.f;
-                orow[(size_t)i * a.out_ld] = tot[c + i] * wr;
-              }
+            for (int i = 0; i < 32; ++i) {  // routing weights of the chunk's rows (clamped index)
+              const float wr = a.row_weight ? __ldg(a.row_weight + row0 + t0 + min(i, left - 1)) : 1.f;
+              v[i] = tot[c + i] * wr;
+            }
+            if (left >= 32) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) orow[(size_t)i * a.out_ld] = v[i];
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (i < left) orow[(size_t)i * a.out_ld] = v[i];
             }
           }
         }
