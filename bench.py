@@ -12,9 +12,14 @@ synchronize fences, max over ranks.  `--workload cfg2_mla_decode` and `cfg3_attn
 the MLA latent attention kernel and the GQA attention block instead (their own metrics);
 `cfg3_engine_decode` times whole-model decode steps through the engine backend.
 
+`value` times K calls of the fused public entry point (ccut_moe_forward), inputs resident in
+HBM; `e2e` times the same call with pinned host input and output copies every step; the
+roofline kernel (the gate/up GEMM) is timed in a separate pass of K staged steps.
+
 `--impl reference` times the reference algorithm on the host cores instead (the numpy
 oracle port of CostCut-Infer's MoE path: per-call dequant of every touched expert, fp32
-BLAS matmuls, the reference's combine loop) on a bounded token sample; rank 0 only.
+BLAS matmuls, the reference's combine loop) on the workload's whole batch per call, K calls;
+rank 0 only.
 """
 
 from __future__ import annotations
@@ -134,7 +139,9 @@ def layer_flops(cfg, T: int) -> float:
 
 # ------------------------------------------------------------------ CPU (oracle) leg
 def cpu_sample_run(cfg_name: str, T: int, sample: int, steps: int, budget_s: float) -> dict:
-    """Time the oracle port of the reference path on `sample` tokens of the workload."""
+    """Time the oracle port of the reference path on `sample` tokens of the workload (the
+    whole batch by default: the reference dequantizes every touched expert once per call, so
+    a smaller sample would spread that cost over fewer tokens than the workload has)."""
     from oracle import formats, inputs, moe  # the checker; only this leg runs it
 
     cores = os.cpu_count() or 1
@@ -159,9 +166,11 @@ def cpu_sample_run(cfg_name: str, T: int, sample: int, steps: int, budget_s: flo
         if time.perf_counter() - t_start > budget_s:
             break
     med = statistics.median(times)
+    what = f"the whole {T}-token batch" if sample == T else f"{sample} of the {T} tokens"
     return {
         "value": sample / med, "unit": "tokens/s", "cores": cores, "kind": "port", "steps_run": len(times),
-        "sample": (f"{sample} of the {T} tokens of {cfg_name}; numpy oracle port of the reference path "
+        "ms_per_call": med * 1e3,
+        "sample": (f"{what} of {cfg_name} per call; numpy oracle port of the reference path "
                    f"(per-call dequant of every touched expert as the reference does, fp32 BLAS on {cores} "
                    f"threads); median of {len(times)} call(s)"),
     }
@@ -177,10 +186,10 @@ def run_reference(args, wl) -> None:
                           "(11 GB of FP8 weights, 45 GB dequantized) in host memory; the reference arm runs on the "
                           "other workloads"}), flush=True)
         return
-    sample = min(T, args.cpu_sample)
+    sample = T if args.cpu_sample <= 0 else min(T, args.cpu_sample)
     for _ in range(max(0, min(args.warmup, 1))):
         cpu_sample_run(cfg_name, T, min(sample, 8), 1, 60)
-    r = cpu_sample_run(cfg_name, T, sample, args.steps, args.cpu_budget)
+    r = cpu_sample_run(cfg_name, T, sample, args.steps, float("inf"))  # exactly K calls
     line = {
         "impl": "reference", "metric": METRIC, "value": r["value"], "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": r["steps_run"], "warmup": args.warmup, "ms_per_step": sample / r["value"] * 1000.0,
@@ -206,9 +215,35 @@ def workload_config(wl: str, n: int, parallelism: str) -> dict:
     }
 
 
-# DRAM bytes (read + write) of one gate/up launch from an ncu capture of the same workload;
-# workloads without a capture report null.
-NCU_TRAFFIC = {"cfg1_prefill": 480.6e6, "cfg0_decode": 202.2e6}
+# DRAM bytes (read + write) of one gate/up launch from an ncu capture of the current kernel on
+# the same workload; workloads without such a capture report null.
+NCU_TRAFFIC: dict = {}
+
+# Dense FP8 (e4m3 x e4m3) peak of this GPU, measured in the run: torch._scaled_mm 8192^3,
+# bf16 out, best of 10 (cuBLAS).  MEASURED_PEAKS.json has no FP8 figure.
+def fp8_peak_tflops(dev) -> float:
+    import torch
+
+    n = 8192
+    a = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn)
+    b = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn).t()
+    one = torch.tensor(1.0, device=dev)
+
+    def mm():
+        return torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+
+    for _ in range(3):
+        mm()
+    best = float("inf")
+    for _ in range(10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        mm()
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    del a, b
+    return 2.0 * n ** 3 / (best * 1e-3) / 1e12
 
 # ------------------------------------------------------------------ end-to-end leg
 def e2e_pipelined(forward, x_pin, out_shape, dev, K: int) -> float:
@@ -252,9 +287,6 @@ def e2e_pipelined(forward, x_pin, out_shape, dev, K: int) -> float:
 # ------------------------------------------------------------------ GPU leg
 # Kernels of this library per staged single-GPU step: route (logits, top-k), permute
 # (count, permute), gate/up (gather or f16 convert, GEMM), down (GEMM), combine.
-LAUNCHES_SINGLE = 8
-
-
 def ep_launches(cfg) -> int:
     """Kernels of this library per expert-parallel step (NCCL's own kernels not counted):
     route 2, localize + count 1, permute 1, routed FFN 3, combine 1, add/cast 1, and for
@@ -419,11 +451,14 @@ def run_ours(args, wl) -> None:
     del lw
     use_graph = args.graph == "on" or (args.graph == "auto" and T <= 256)
     # the gate/up launch timed between ev0 and ev1: tcgen05 kernel (plus its activation
-    # gather) at >= CCUT_TC_MIN_ROWS mean rows per expert, else mma.sync (plus f16 convert)
+    # gather) at >= CCUT_TC_MIN_ROWS mean rows per expert, else mma.sync
     tc_path = T * c.top_k / c.num_experts >= 64
-    kname = "tc_gemm_kernel<gate/up>" if tc_path else "moe_gemm_kernel<gate/up>"
+    kname = ("tc_gemm_kernel<gate/up> (with its row gather)" if tc_path else "moe_gemm_kernel<gate/up>")
 
-    def step(ev0=None, ev1=None):
+    def fused():  # the public layer call: one ccut_moe_forward
+        return L.forward(x)
+
+    def staged(ev0=None, ev1=None):  # the same layer through its stage entry points
         r = L.route(x)
         p = L.permute(r)
         if ev0 is not None:
@@ -436,49 +471,62 @@ def run_ours(args, wl) -> None:
 
     # warm-up (also sizes every workspace before any capture)
     for _ in range(max(args.warmup, 3)):
-        step()
+        fused()
+        staged()
     torch.cuda.synchronize()
-    _, perm = step()
+    _, perm = staged()
     offsets = perm.offsets.cpu().numpy()
     K = args.steps
     mk = lambda: torch.cuda.Event(enable_timing=True, external=use_graph)  # noqa: E731
     ev0 = [mk() for _ in range(K)]
     ev1 = [mk() for _ in range(K)]
-    graph = None
+    g_fused = g_staged = None
     if use_graph:
-        g = torch.cuda.CUDAGraph()
         s = torch.cuda.Stream(device=dev)
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
-            step()  # warm the side stream
+            fused()
+            staged()  # warm the side stream
             torch.cuda.synchronize()
-            with torch.cuda.graph(g, stream=s):
+            g_fused, g_staged = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_fused, stream=s):
+                for _ in range(K):
+                    fused()
+            with torch.cuda.graph(g_staged, stream=s):
                 for i in range(K):
-                    step(ev0[i], ev1[i])
+                    staged(ev0[i], ev1[i])
         torch.cuda.current_stream().wait_stream(s)
-        graph = g
-        graph.replay()
+        g_fused.replay()
+        g_staged.replay()
         torch.cuda.synchronize()
 
     clocks = ClockSampler(local)
     t_soak = time.perf_counter()
     while time.perf_counter() - t_soak < args.soak:  # steady clocks before the timed region
-        if graph is not None:
-            graph.replay()
+        if g_fused is not None:
+            g_fused.replay()
         else:
-            step()
+            fused()
         torch.cuda.synchronize()
+    # value: K fused layer calls, inputs resident in HBM
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     start.record()
-    if graph is not None:
-        graph.replay()
+    if g_fused is not None:
+        g_fused.replay()
     else:
-        for i in range(K):
-            step(ev0[i], ev1[i])
+        for _ in range(K):
+            fused()
     end.record()
     torch.cuda.synchronize()
     ms = start.elapsed_time(end)
+    # roofline kernel: its own pass of K staged steps, events around the gate/up call
+    if g_staged is not None:
+        g_staged.replay()
+    else:
+        for i in range(K):
+            staged(ev0[i], ev1[i])
+    torch.cuda.synchronize()
     kern_ms = [a.elapsed_time(b) for a, b in zip(ev0, ev1)]
 
     # end to end: host bf16 in (pinned) -> public forward -> host bf16 out, every step
@@ -505,18 +553,28 @@ def run_ours(args, wl) -> None:
             peak = pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
             roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                     "frac": achieved / peak, "traffic": NCU_TRAFFIC.get(wl), "kernel": kname,
-                    "algorithmic_flops_per_launch": flops}
+                    "algorithmic_flops_per_launch": flops,
+                    "mma": "tcgen05 kind::f16, bf16 operands (the exact weight codes), fp32 scale per 128-k block"}
+            if c.fmt == "fp8_b128":
+                p8 = fp8_peak_tflops(dev)
+                roof["peak_fp8"] = p8
+                roof["frac_fp8"] = achieved / p8
+                roof["peak_fp8_source"] = "measured in this run: torch._scaled_mm e4m3 8192^3, best of 10"
         roof["peak_source"] = f"{src} (MEASURED_PEAKS.json)" if src == "measured" else "fallback"
         roof["kernel_ms"] = kmean
+        launches = 7 if tc_path else 6  # route logits, top-k, permute, [row gather], gate/up, down, combine
         line = {
             "metric": METRIC, "value": T * K / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": K,
             "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16" if c.fmt == "awq_int4_g128" else "f16", "data": "synthetic",
-            "config": workload_config(wl, 1, "single"),
+            "vs_baseline": None, "dtype": "bf16" if tc_path else "f16", "data": "synthetic",
+            "config": dict(workload_config(wl, 1, "single"),
+                           weights={"fp8_b128": "fp8 e4m3, 128x128 fp32 block scales",
+                                    "awq_int4_g128": "awq int4, group 128, fp16 scales, packed zero points"}[c.fmt],
+                           path="ccut_moe_forward (fused C entry point)"),
             "roofline": roof,
             "e2e": {"value": T * K / (e2e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": T * c.hidden * 2, "d2h_bytes_per_step": T * c.hidden * 2},
-            "gpu_launches": LAUNCHES_SINGLE * K,
+            "gpu_launches": launches * K,
             "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]},
             "layer_tflops": layer_flops(c, T) * K / (ms * 1e-3) / 1e12,
             "cuda_graph": use_graph,
@@ -524,11 +582,11 @@ def run_ours(args, wl) -> None:
         if cfg_name in DEVICE_GENERATED:
             line["data"] = "synthetic (generated on the GPU from a seeded torch generator)"
         if not args.no_cpu_baseline and cfg_name not in DEVICE_GENERATED:
-            r = cpu_sample_run(cfg_name, T, min(T, args.cpu_sample), 1, args.cpu_budget)
+            sample = T if args.cpu_sample <= 0 else min(T, args.cpu_sample)
+            r = cpu_sample_run(cfg_name, T, sample, 1, args.cpu_budget)
             line["cpu_baseline"] = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
         print(json.dumps(line), flush=True)
-    if graph is not None:
-        del graph
+    del g_fused, g_staged
 
 
 # Attention block of the full stacks (not the MoE layer): name -> (batch, heads, kv_heads,
@@ -803,8 +861,9 @@ def main(argv=None) -> int:
                     + sorted(ENGINE_WORKLOADS), default=DEFAULT_WORKLOAD)
     ap.add_argument("--graph", choices=("auto", "on", "off"), default="auto")
     ap.add_argument("--soak", type=float, default=1.0, help="untimed seconds of load before timing")
-    ap.add_argument("--cpu-sample", type=int, default=128, help="tokens in the CPU baseline sample")
-    ap.add_argument("--cpu-budget", type=float, default=60.0, help="seconds cap of the CPU timing")
+    ap.add_argument("--cpu-sample", type=int, default=0,
+                    help="tokens per CPU-baseline call (0: the whole batch of the workload)")
+    ap.add_argument("--cpu-budget", type=float, default=120.0, help="seconds cap of the cpu_baseline leg")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)
     if args.warmup < 3 and args.impl == "ours":

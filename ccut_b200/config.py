@@ -9,8 +9,12 @@
   caches are bf16); ``fp8`` is refused.  ``quant_ignore`` applies to online quantization only.
 - ``[experts]``: the reference streams experts from disk (``expert_residency = "zero"`` or
   ``"page_cache_only"``, a ring of ``expert_ring_slots``); here every expert is packed into HBM
-  once, so these settings are checked against the reference's allowed values and have no
-  further effect.
+  once.  ``expert_residency`` takes this path's own value ``"hbm"`` (the default) besides the
+  reference's two, which are checked and then run resident as well.  ``expert_parallel_size``
+  (new, default 1) splits each layer's routed experts over that many GPUs, one process per
+  GPU (``ccut_b200.ep``); it must equal the ``torch.distributed`` world size.
+- ``cross_validate`` keeps the reference's rule that ``tensor_parallel_size`` and
+  ``pipeline_parallel_size`` are 1 (``ccut/config.py:466-470``) and admits expert parallelism.
 
 Unsupported values raise ``NotImplementedError`` and out-of-range ones ``ValueError``, as the
 reference's config validation and quant registry do.
@@ -20,7 +24,9 @@ from __future__ import annotations
 
 from ccut_b200.checkpoint import quant_format
 
-__all__ = ["quant_settings", "expert_settings", "resolve"]
+__all__ = ["quant_settings", "expert_settings", "cross_validate", "resolve"]
+
+_RESIDENCY = ("hbm", "zero", "page_cache_only")
 
 _ONLINE = ("fp8_per_token", "int8_per_channel_weight_only", "mxfp8", "nvfp4_per_token", "int8_per_token", "bf16")
 
@@ -57,18 +63,43 @@ def quant_settings(app_config, checkpoint_config: dict) -> dict:
 
 
 def expert_settings(app_config) -> dict:
-    """The ``[experts]`` section checked against the reference's allowed values; the experts
-    are resident in HBM whatever it says."""
+    """The ``[experts]`` section checked against the allowed values; the experts are resident
+    in HBM whatever it says."""
     e = _section(app_config, "experts")
-    residency = str(e.get("expert_residency", "zero"))
-    if residency not in ("zero", "page_cache_only"):
-        raise ValueError(f"[experts] expert_residency = {residency!r} is not one of zero, page_cache_only")
+    residency = str(e.get("expert_residency", "hbm"))
+    if residency not in _RESIDENCY:
+        raise ValueError(f"[experts] expert_residency = {residency!r} is not one of {', '.join(_RESIDENCY)}")
     slots = int(e.get("expert_ring_slots", 2))
     if not 1 <= slots <= 8:
         raise ValueError(f"[experts] expert_ring_slots = {slots} is outside [1, 8]")
-    return {"residency": "hbm", "expert_residency": residency, "expert_ring_slots": slots}
+    ep = e.get("expert_parallel_size", 1)
+    if isinstance(ep, bool) or not isinstance(ep, int) or ep < 1:
+        raise ValueError(f"[experts] expert_parallel_size = {ep!r} must be an integer >= 1")
+    return {"residency": "hbm", "expert_residency": residency, "expert_ring_slots": slots,
+            "expert_parallel_size": ep}
+
+
+def cross_validate(app_config, world_size: int | None = None, num_experts: int | None = None) -> dict:
+    """Cross-field checks (``ccut/config.py:466-484`` for the reference's own): tensor and
+    pipeline parallelism stay 1 as in the reference; expert parallelism may be above 1, equal to
+    the process group's ``world_size`` when one is given, and at most ``num_experts`` (every rank
+    owns at least one routed expert).  Raises ``ValueError``; returns the ``[experts]`` settings."""
+    eng = _section(app_config, "engine")
+    for key in ("tensor_parallel_size", "pipeline_parallel_size"):
+        v = eng.get(key, 1)
+        if v != 1:
+            raise ValueError(f"[engine] {key} = {v!r}: only expert parallelism splits a layer over GPUs here "
+                             "(tensor and pipeline parallel sizes must be 1, as in the reference)")
+    ex = expert_settings(app_config)
+    ep = ex["expert_parallel_size"]
+    if world_size is not None and ep != world_size:
+        raise ValueError(f"[experts] expert_parallel_size = {ep} but the process group has {world_size} ranks")
+    if num_experts is not None and ep > num_experts:
+        raise ValueError(f"[experts] expert_parallel_size = {ep} exceeds the layer's {num_experts} routed experts")
+    return ex
 
 
 def resolve(app_config, checkpoint_config: dict) -> dict:
-    """Both sections, merged."""
+    """Both sections, merged, after the cross-field checks."""
+    cross_validate(app_config)
     return {**expert_settings(app_config), **quant_settings(app_config, checkpoint_config)}

@@ -32,6 +32,10 @@ def test_defaults_and_checkpoint_format():
     ("quant", "kv_cache_dtype", "fp8", NotImplementedError),
     ("quant", "kv_cache_dtype", "fp16", ValueError),
     ("experts", "expert_residency", "always", ValueError),
+    ("experts", "expert_parallel_size", 0, ValueError),
+    ("experts", "expert_parallel_size", "2", ValueError),
+    ("engine", "tensor_parallel_size", 2, ValueError),
+    ("engine", "pipeline_parallel_size", 2, ValueError),
     ("experts", "expert_ring_slots", 9, ValueError),
 ])
 def test_refused_settings(section, key, value, exc):
@@ -42,3 +46,20 @@ def test_refused_settings(section, key, value, exc):
 def test_unquantized_checkpoint_is_refused():
     with pytest.raises(NotImplementedError):
         config.resolve({}, {"hidden_size": 128})
+
+
+def test_expert_residency_hbm_and_expert_parallel_size():
+    assert config.expert_settings(None)["expert_residency"] == "hbm"
+    r = config.resolve({"experts": {"expert_residency": "hbm", "expert_parallel_size": 8}}, FP8)
+    assert r["residency"] == "hbm" and r["expert_parallel_size"] == 8
+
+
+def test_cross_validate_admits_expert_parallelism_only():
+    app = {"engine": {"tensor_parallel_size": 1, "pipeline_parallel_size": 1}, "experts": {"expert_parallel_size": 4}}
+    assert config.cross_validate(app, world_size=4, num_experts=64)["expert_parallel_size"] == 4
+    with pytest.raises(ValueError):
+        config.cross_validate(app, world_size=2)  # the size must be the process group's
+    with pytest.raises(ValueError):
+        config.cross_validate({"experts": {"expert_parallel_size": 16}}, num_experts=8)
+    with pytest.raises(ValueError):
+        config.cross_validate({"engine": {"tensor_parallel_size": 2}, "experts": {"expert_parallel_size": 2}})
