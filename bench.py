@@ -55,7 +55,10 @@ WORKLOADS = {
 # another random stream) because the host generator needs minutes for them; their CPU
 # baseline is not run (the oracle would need the same 11 GB of weights in fp32 on the host).
 DEVICE_GENERATED = {"cfg4"}
-DEFAULT_WORKLOAD = "cfg1_prefill"
+# The default: BASELINE config 3 (Qwen3-30B-A3B-shaped MoE layer, AWQ int4, 128 experts,
+# top-8), 4096-token prefill -- the config that names expert parallelism over 2 / 4 / 8 GPUs
+# and the token count of the scaling target; the same total tokens at every N.
+DEFAULT_WORKLOAD = "cfg3_prefill"
 METRIC = "MoE-layer tokens/s"
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
@@ -289,14 +292,17 @@ def e2e_pipelined(forward, x_pin, out_shape, dev, K: int) -> float:
 # (count, permute), gate/up (gather or f16 convert, GEMM), down (GEMM), combine.
 def ep_launches(cfg) -> int:
     """Kernels of this library per expert-parallel step (NCCL's own kernels not counted):
-    route 2, localize + count 1, permute 1, routed FFN 3, combine 1, add/cast 1, and for
+    route 2, plan 1, count 1, permute 1, routed FFN 3, per-row combine 1, final sum 1, and for
     shared experts permute 1, FFN 3, combine 1."""
-    return 9 + (5 if cfg.num_shared else 0)
+    return 10 + (5 if cfg.num_shared else 0)
 
 
 def run_ep(args, wl, world: int, rank: int, local: int) -> None:
     """Expert-parallel layer over `world` GPUs: the workload's tokens split evenly over the
-    ranks (strong scaling), routed experts sharded, NCCL all-gather / reduce-scatter."""
+    ranks (strong scaling), routed experts sharded, routed rows exchanged over NCCL (counts
+    first, then each token row to each rank that owns one of its experts, partial rows back).
+    The count exchange is read on the host inside every step, so the steps are not captured
+    in a CUDA graph."""
     import datetime
 
     import torch
@@ -330,32 +336,10 @@ def run_ep(args, wl, world: int, rank: int, local: int) -> None:
         ep.forward(x)
     torch.cuda.synchronize()
     K = args.steps
-    # The K timed steps replay as one CUDA graph, NCCL calls included: a step enqueues ~25
-    # operations, which the host issues no faster than 4-8 GPUs finish them.  The graph is
-    # reset before the communicator is destroyed.
-    graph = None
-    if args.graph in ("auto", "on"):
-        graph = torch.cuda.CUDAGraph()
-        cap = torch.cuda.Stream(device=dev)
-        cap.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(cap):
-            ep.forward(x)
-            torch.cuda.synchronize()
-            with torch.cuda.graph(graph, stream=cap):
-                for _ in range(K):
-                    ep.forward(x)
-        torch.cuda.current_stream().wait_stream(cap)
-        torch.cuda.synchronize()
-        dist.barrier()
-        graph.replay()
-        torch.cuda.synchronize()
-
+    graph = None  # the step waits on the host for the exchanged counts: no graph capture
     def timed_steps():
-        if graph is not None:
-            graph.replay()
-        else:
-            for _ in range(K):
-                ep.forward(x)
+        for _ in range(K):
+            ep.forward(x)
 
     clocks = ClockSampler(local)
     t_soak = time.perf_counter()
@@ -404,8 +388,8 @@ def run_ep(args, wl, world: int, rank: int, local: int) -> None:
         line = {
             "metric": METRIC, "value": T * K / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16" if c.fmt == "awq_int4_g128" else "f16", "data": "synthetic",
-            "config": cfgd, "roofline": roof,
+            "vs_baseline": None, "dtype": "bf16" if T * c.top_k / c.num_experts >= 64 else "f16",
+            "data": "synthetic", "config": cfgd, "roofline": roof,
             "e2e": {"value": T * K / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": T * c.hidden * 2,
                     "d2h_bytes_per_step": T * c.hidden * 2},
             "gpu_launches": ep_launches(c) * K,
@@ -414,9 +398,6 @@ def run_ep(args, wl, world: int, rank: int, local: int) -> None:
             "cuda_graph": graph is not None,
         }
         print(json.dumps(line), flush=True)
-    if graph is not None:
-        graph.reset()  # drop the captured NCCL work before the communicator goes
-        graph = None
     torch.cuda.synchronize()
     dist.barrier()
     ep.close()

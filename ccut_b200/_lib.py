@@ -80,8 +80,10 @@ SIGNATURES: dict[str, tuple] = {
     "ccut_ep_unique_id": (_i, [_vp]),
     "ccut_ep_init": (_i, [_vp, _i, _i, C.c_double, C.POINTER(_vp)]),
     "ccut_ep_destroy": (_i, [_vp]),
-    "ccut_moe_ep_dispatch": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp]),
-    "ccut_moe_ep_combine": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
+    "ccut_moe_ep_exchange_workspace_bytes": (_sz, [_i, _i, _i, _i]),
+    "ccut_moe_ep_dispatch": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _i, C.POINTER(_i), _vp, _sz,
+                                  _vp]),
+    "ccut_moe_ep_combine": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _sz, _vp]),
     "ccut_moe_ep_forward_workspace_bytes": (_sz, [C.POINTER(MoeLayerDesc), _i, _i, _i, _i]),
     "ccut_gqa_attention_workspace_bytes": (_sz, [_i, _i, _i, _i, _i, _i]),
     "ccut_gqa_attention": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _f, _vp, _i, _vp, _sz, _vp]),
@@ -93,9 +95,10 @@ SIGNATURES: dict[str, tuple] = {
     "ccut_mla_attention": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _i, _vp, _sz, _vp]),
     "ccut_mla_attention_pool": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, C.c_longlong, _i, _f, _vp, _i, _vp,
                                      _sz, _vp]),
-    "ccut_moe_ep_forward": (_i, [_vp, C.POINTER(MoeLayerDesc), _i, _i, C.POINTER(RouteParams), _vp, _i, _vp, _i,
-                                 _vp, _sz, _vp]),
+    "ccut_moe_ep_forward": (_i, [_vp, C.POINTER(MoeLayerDesc), _i, _i, C.POINTER(RouteParams), _vp, _i, _i, _vp,
+                                 _i, _vp, _sz, _vp]),
     "ccut_workspace_status": (_i, [_vp, _vp]),
+    "ccut_debug_wait_expiry": (_i, [_vp, C.c_longlong, _vp]),
 }
 
 _lib = None

@@ -220,11 +220,40 @@ int run_ffn(const ccut_moe_layer* L, long per_expert, const uint16_t* x, const F
   return run_down(L, per_expert, s.hbuf, T, k, offsets, row_weight, y_rows, s.sched, status, st);
 }
 
+// The bounded waits of the kernels, exercised on barriers with a known outcome: barrier 0
+// completes (one arrival), barrier 1 never does (nothing arrives on it).  Both wait forms
+// run out on barrier 1 after `budget` cycles and record CCUT_ERR_TIMEOUT in the status word;
+// the kernel then returns.
+__global__ void wait_expiry_kernel(int* status, long long budget, int* outcome) {
+  __shared__ uint64_t bars[2];
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_arrive(&bars[0]);
+    const bool done = mbar_wait(&bars[0], 0, status, budget);            // completes
+    const bool late = mbar_wait(&bars[1], 0, status, budget);            // runs out
+    const bool late_spin = mbar_spin(&bars[1], 0, status, budget);       // runs out
+    outcome[0] = (done ? 1 : 0) | (late ? 2 : 0) | (late_spin ? 4 : 0);
+  }
+}
+
 }  // namespace ccut
 
 using namespace ccut;
 
 extern "C" {
+
+int ccut_debug_wait_expiry(void* workspace, long long budget_cycles, ccut_stream_t stream) {
+  if (!workspace || budget_cycles < 0 || budget_cycles > kWaitBudgetCycles) return CCUT_ERR_INVALID;
+  int* ws = static_cast<int*>(workspace);
+  // outcome flags at ws[1]: bit 0 = the completed barrier's wait succeeded, bits 1-2 = the
+  // waits on the barrier nothing arrives on succeeded (both stay 0)
+  return launch_k(wait_expiry_kernel, dim3(1), dim3(32), 0, stream, ws, budget_cycles, ws + 1);
+}
 
 const char* ccut_strerror(int code) {
   switch (code) {

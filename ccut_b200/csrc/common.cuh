@@ -63,12 +63,12 @@ CCUT_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with `parity` to complete.  Returns false on timeout (the
-// status word then holds CCUT_ERR_TIMEOUT).
-CCUT_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
+// status word then holds CCUT_ERR_TIMEOUT).  `budget` in SM clock cycles.
+CCUT_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, long long budget = kWaitBudgetCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > kWaitBudgetCycles) {
+    if (clock64() - t0 > budget) {
       record_error(status, CCUT_ERR_TIMEOUT);
       return false;
     }
@@ -90,11 +90,11 @@ CCUT_DEVICE bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
 
 // Bounded busy wait (non-suspending test_wait) for single-thread roles whose wake-up
 // latency is on the critical path (MMA issue, TMA producer).
-CCUT_DEVICE bool mbar_spin(uint64_t* bar, uint32_t parity, int* status) {
+CCUT_DEVICE bool mbar_spin(uint64_t* bar, uint32_t parity, int* status, long long budget = kWaitBudgetCycles) {
   if (mbar_test_wait(bar, parity)) return true;
   long long t0 = clock64();
   while (!mbar_test_wait(bar, parity)) {
-    if (clock64() - t0 > kWaitBudgetCycles) {
+    if (clock64() - t0 > budget) {
       record_error(status, CCUT_ERR_TIMEOUT);
       return false;
     }

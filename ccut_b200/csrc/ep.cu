@@ -1,19 +1,28 @@
-// ep.cu -- expert-parallel MoE forward, one process per GPU, over NCCL.
+// ep.cu -- expert-parallel MoE forward, one process per GPU, over NCCL: only routed rows
+// cross the links.
 //
-// Rank r of P holds the routed experts [expert_lo, expert_lo + E_r) plus every shared
-// expert, and its own T_r tokens.  One forward:
+// Rank r of P holds the routed experts [lo_r, hi_r) (contiguous blocks whose sizes differ by
+// at most one, ep_range) plus every shared expert, and its own T_r tokens (T_r may differ
+// between ranks; every rank sized its workspace for the same T_cap >= T_r).  One forward:
 //   1. route the local tokens against the global router (ids are global expert indices);
-//   2. dispatch: one grouped NCCL all-gather of the tokens, ids and routing weights, so that
-//      every rank sees all T = sum T_r tokens;
-//   3. keep the (token, slot) pairs whose expert is local (others get id -1 and take no
-//      row), permute them by local expert and run the grouped expert FFN on them only;
-//   4. combine the local rows per token (fp32 [T, H], zero for tokens with no local
-//      expert) and reduce-scatter it: rank r receives the sum over ranks of its T_r rows;
-//   5. shared experts run data-parallel on the local tokens and are added in; they only need
-//      the local tokens, so they run on a second stream while the dispatch is in flight.
-// The reference runs the experts of one layer in a single process
-// (ccut/models/generic.py:364-385, ccut/experts/pipeline.py:123-190); the partitioning is
-// new.  One blocking NCCL communicator per layer handle carries the collectives.
+//   2. plan (ep_plan_kernel, one CTA per destination d): the local tokens with at least one
+//      expert on d, in token order; each is packed ONCE into d's segment of the send buffer
+//      (bf16 row, its k ids made local to d with -1 for other ranks' experts, its k routing
+//      weights), and send_pos[t, d] keeps the row's place for the way back;
+//   3. count exchange: one int per (source, destination) pair, grouped ncclSend / ncclRecv,
+//      copied to the host (a bounded wait): the sizes of the row exchange;
+//   4. dispatch: grouped ncclSend / ncclRecv of each segment; the rows from source s are
+//      packed at receive offset sum_{s' < s} recv_cnt[s'];
+//   5. the received rows through this rank's experts: permute by local expert (a -1 id takes
+//      no row), grouped FFN, per-row weighted sum over the row's k slots in slot order (fp32);
+//   6. return: each source's partial rows sent back to it, received in its send order;
+//   7. out[t] = sum over destinations d = 0..P-1 of the partial row of (t, d), in that fixed
+//      order, plus the shared experts, which run data-parallel on the local tokens on a second
+//      stream meanwhile.
+// The volume per rank is the routed rows only: a token crosses to each rank that owns one of
+// its experts once, whatever P is.  The reference runs the experts of one layer in a single
+// process (ccut/models/generic.py:364-385, ccut/experts/pipeline.py:123-190); the partitioning
+// is new.  One blocking NCCL communicator per handle carries the exchanges.
 #include <nccl.h>
 
 #include <chrono>
@@ -28,12 +37,16 @@ struct ccut_ep {
   int rank;
   int world;
   double timeout_s;
-  cudaStream_t side;  // shared experts run here, beside the dispatch collective
-  cudaEvent_t fork, join;
+  cudaStream_t side;  // shared experts run here, beside the exchange
+  cudaEvent_t fork, join, counted;
+  int* h_counts;  // pinned host: [world] rows sent to, [world] rows received from each rank (last dispatch)
 };
 
 namespace ccut {
 namespace {
+
+constexpr int kPlanThreads = 1024;
+constexpr int kMaxWorld = 64;
 
 // Wait (bounded) for a call on a non-blocking communicator to leave ncclInProgress.
 int nccl_settle(ncclComm_t comm, ncclResult_t r, double budget_s) {
@@ -47,60 +60,122 @@ int nccl_settle(ncclComm_t comm, ncclResult_t r, double budget_s) {
   return r == ncclSuccess ? CCUT_OK : CCUT_ERR_NCCL;
 }
 
-// ids_loc[i] = ids[i] - lo when expert ids[i] is local, else -1; weights copied; counts[e]
-// of the local experts accumulated (shared-memory histogram, then one atomic per expert
-// and CTA).  counts must start at zero.
-__global__ void __launch_bounds__(256) localize_count_kernel(const int32_t* __restrict__ ids,
-                                                             const float* __restrict__ w, int n, int lo, int e_local,
-                                                             int32_t* __restrict__ ids_loc,
-                                                             float* __restrict__ w_loc, int* __restrict__ counts) {
-  pdl_wait();
-  pdl_trigger();
-  __shared__ int hist[kMaxExperts];
-  for (int e = threadIdx.x; e < e_local; e += blockDim.x) hist[e] = 0;
-  __syncthreads();
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const int e = ids[i] - lo;
-    const bool mine = e >= 0 && e < e_local;
-    ids_loc[i] = mine ? e : -1;
-    w_loc[i] = w[i];
-    if (mine) atomicAdd(&hist[e], 1);
-  }
-  __syncthreads();
-  for (int e = threadIdx.x; e < e_local; e += blockDim.x)
-    if (hist[e]) atomicAdd(&counts[e], hist[e]);
+// First routed expert of rank d (contiguous blocks, sizes differing by at most one; the same
+// split as ccut_b200.ep.expert_range).
+__host__ __device__ inline int ep_lo(int E, int world, int d) {
+  const int base = E / world, extra = E % world;
+  return d * base + (d < extra ? d : extra);
 }
 
-// out = a (+ b), fp32 -> bf16 or fp32.
-__global__ void add_cast_kernel(const float4* __restrict__ a, const float4* __restrict__ b, size_t n4, void* out,
-                                int out_dtype) {
+// One CTA per destination rank d: the local tokens with an expert on d, in token order
+// (block-wide scan of the flags, 1024 tokens per round), packed into d's segment of the send
+// buffers; send_pos[t * world + d] = the row's index in the send buffers, or -1.
+__global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(const uint16_t* __restrict__ x,
+                                                               const int32_t* __restrict__ ids,
+                                                               const float* __restrict__ w, int T, int k, int H,
+                                                               int E, int world, int seg, int* __restrict__ send_cnt,
+                                                               int32_t* __restrict__ send_pos,
+                                                               uint16_t* __restrict__ x_send,
+                                                               int32_t* __restrict__ ids_send,
+                                                               float* __restrict__ w_send) {
   pdl_wait();
   pdl_trigger();
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
-    float4 v = a[i];
-    if (b) {
-      const float4 u = b[i];
-      v.x += u.x;
-      v.y += u.y;
-      v.z += u.z;
-      v.w += u.w;
+  __shared__ int wsum[kPlanThreads / 32];
+  __shared__ int tok[kPlanThreads];
+  __shared__ int s_total;
+  const int d = blockIdx.x, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int lo = ep_lo(E, world, d), hi = ep_lo(E, world, d + 1);
+  int carry = 0;
+  for (int base = 0; base < T; base += kPlanThreads) {
+    const int t = base + tid;
+    bool flag = false;
+    if (t < T)
+      for (int j = 0; j < k; ++j) {
+        const int e = ids[(size_t)t * k + j];
+        flag |= e >= lo && e < hi;
+      }
+    const unsigned bal = __ballot_sync(0xffffffffu, flag);
+    if (lane == 0) wsum[wid] = __popc(bal);
+    __syncthreads();
+    if (wid == 0) {  // exclusive scan of the 32 warp counts
+      const int c = wsum[lane];
+      int inc = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += u;
+      }
+      wsum[lane] = inc - c;
+      if (lane == 31) s_total = inc;
     }
-    if (out_dtype == CCUT_OUT_BF16) {
-      __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
-      uint2 pk;
-      pk.x = *reinterpret_cast<uint32_t*>(&lo);
-      pk.y = *reinterpret_cast<uint32_t*>(&hi);
-      static_cast<uint2*>(out)[i] = pk;
-    } else {
-      static_cast<float4*>(out)[i] = v;
+    __syncthreads();
+    const int pos = wsum[wid] + __popc(bal & ((1u << lane) - 1u));
+    if (flag) {
+      const int row = d * seg + carry + pos;
+      tok[pos] = t;
+      send_pos[(size_t)t * world + d] = row;
+      for (int j = 0; j < k; ++j) {
+        const int e = ids[(size_t)t * k + j];
+        ids_send[(size_t)row * k + j] = (e >= lo && e < hi) ? e - lo : -1;
+        w_send[(size_t)row * k + j] = w[(size_t)t * k + j];
+      }
+    } else if (t < T) {
+      send_pos[(size_t)t * world + d] = -1;
     }
+    __syncthreads();
+    const int n = s_total;
+    // rows of this round: one warp per row, 16-byte lanes
+    const int per_row = H / 8;
+    for (int i = wid; i < n; i += kPlanThreads / 32) {
+      const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)tok[i] * H);
+      uint4* dst = reinterpret_cast<uint4*>(x_send + (size_t)(d * seg + carry + i) * H);
+      for (int c = lane; c < per_row; c += 32) dst[c] = src[c];
+    }
+    carry += n;
+    __syncthreads();
   }
+  if (tid == 0) send_cnt[d] = carry;
 }
 
-int grid_for(size_t n, int per_block) {
-  size_t b = (n + per_block - 1) / per_block;
-  if (b > 148 * 8) b = 148 * 8;
-  return b < 1 ? 1 : static_cast<int>(b);
+// out[t] = sum_{d = 0..world-1} back[send_pos[t, d]] (rows that were sent) + shared[t], in that
+// order, fp32 -> bf16 or fp32.  One CTA per (token, 1024-column chunk).
+__global__ void __launch_bounds__(256) ep_sum_kernel(const float* __restrict__ back, const int32_t* __restrict__ send_pos,
+                                                     const float* __restrict__ shared, int world, int H, void* out,
+                                                     int out_dtype) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ int rows[kMaxWorld];
+  const int t = blockIdx.x;
+  if (threadIdx.x < world) rows[threadIdx.x] = send_pos[(size_t)t * world + threadIdx.x];
+  __syncthreads();
+  const int h4n = H / 4, h4 = blockIdx.y * 256 + threadIdx.x;
+  if (h4 >= h4n) return;
+  const float4* b4 = reinterpret_cast<const float4*>(back);
+  float4 s = shared ? reinterpret_cast<const float4*>(shared)[(size_t)t * h4n + h4] : make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int d = 0; d < world; ++d) {
+    const int r = rows[d];
+    if (r >= 0) {
+      const float4 v = b4[(size_t)r * h4n + h4];
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+  }
+  acc.x += s.x;
+  acc.y += s.y;
+  acc.z += s.z;
+  acc.w += s.w;
+  if (out_dtype == CCUT_OUT_BF16) {
+    __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+    uint2 pk;
+    pk.x = *reinterpret_cast<uint32_t*>(&lo);
+    pk.y = *reinterpret_cast<uint32_t*>(&hi);
+    reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + (size_t)t * H)[h4] = pk;
+  } else {
+    reinterpret_cast<float4*>(static_cast<float*>(out) + (size_t)t * H)[h4] = acc;
+  }
 }
 
 // Layer views: the routed experts alone, and the shared slices behind one empty routed
@@ -132,19 +207,41 @@ ccut_moe_layer with_policy(ccut_moe_layer v, long per_expert) {
   return v;
 }
 
-struct EpScratch {
+// The exchange's own scratch (the plan of the last dispatch, kept for its combine).
+struct ExScratch {
   int* status;
+  int* cnt;          // [2 * world]: rows sent to each destination, rows received from each source
+  int32_t* send_pos;  // [T_cap, world]
+  uint16_t* x_send;   // [world * T_cap, H]
+  int32_t* ids_send;  // [world * T_cap, k]
+  float* w_send;      // [world * T_cap, k]
+  float* back;        // [world * T_cap, H] partial outputs returned to this rank
+};
+
+ExScratch carve_ex(Carver& c, int world, int T_cap, int H, int k) {
+  ExScratch s{};
+  const size_t rows = (size_t)world * T_cap;
+  s.status = c.take<int>(64);
+  s.cnt = c.take<int>(2 * (size_t)world);
+  s.send_pos = c.take<int32_t>((size_t)T_cap * world);
+  s.x_send = c.take<uint16_t>(rows * H);
+  s.ids_send = c.take<int32_t>(rows * k);
+  s.w_send = c.take<float>(rows * k);
+  s.back = c.take<float>(rows * H);
+  return s;
+}
+
+struct EpScratch {
+  ExScratch ex;
   int* sched;     // GEMM work counters of the routed FFN
   int* sh_sched;  // and of the shared-expert FFN (runs concurrently on the side stream)
   float* part;
   int* counts_g;
   int32_t* ids_l;
   float* w_l;
-  uint16_t* x_all;
-  int32_t* ids_all;
-  float* w_all;
-  int32_t* ids_loc;
-  float* w_loc;
+  uint16_t* x_recv;
+  int32_t* ids_recv;
+  float* w_recv;
   int* counts;
   int32_t* offsets;
   int32_t* row_token;
@@ -152,8 +249,7 @@ struct EpScratch {
   int32_t* pair_row;
   FfnScratch ffn;
   float* ybuf;
-  float* y_part;
-  float* y_loc;
+  float* y_recv;
   // shared experts
   int32_t* sh_ids;
   float* sh_w;
@@ -167,68 +263,149 @@ struct EpScratch {
   float* y_sh;
 };
 
-EpScratch carve_ep(Carver& c, const ccut_moe_layer* L, int E_global, int world, int T_l, int k) {
+EpScratch carve_ep(Carver& c, const ccut_moe_layer* L, int E_global, int world, int T_cap, int k) {
   const int H = L->hidden, S = L->num_shared_slices;
-  const int T = world * T_l;
+  const int R = world * T_cap;  // received rows: every token of every rank at most once
   const ccut_moe_layer rv = routed_view(L);
   EpScratch s{};
-  s.status = c.take<int>(64);
+  s.ex = carve_ex(c, world, T_cap, H, k);
   s.sched = take_sched(c);
   s.sh_sched = take_sched(c);
-  s.part = c.take<float>((size_t)route_hsplit(T_l, E_global, H) * T_l * E_global);
+  s.part = c.take<float>((size_t)route_hsplit(T_cap, E_global, H) * T_cap * E_global);
   s.counts_g = c.take<int>(E_global);
-  s.ids_l = c.take<int32_t>((size_t)T_l * k);
-  s.w_l = c.take<float>((size_t)T_l * k);
-  s.x_all = c.take<uint16_t>((size_t)T * H);
-  s.ids_all = c.take<int32_t>((size_t)T * k);
-  s.w_all = c.take<float>((size_t)T * k);
-  s.ids_loc = c.take<int32_t>((size_t)T * k);
-  s.w_loc = c.take<float>((size_t)T * k);
+  s.ids_l = c.take<int32_t>((size_t)T_cap * k);
+  s.w_l = c.take<float>((size_t)T_cap * k);
+  s.x_recv = c.take<uint16_t>((size_t)R * H);
+  s.ids_recv = c.take<int32_t>((size_t)R * k);
+  s.w_recv = c.take<float>((size_t)R * k);
   s.counts = c.take<int>(L->num_experts);
   s.offsets = c.take<int32_t>(L->num_experts + 1);
-  s.row_token = c.take<int32_t>((size_t)T * k);
-  s.row_weight = c.take<float>((size_t)T * k);
-  s.pair_row = c.take<int32_t>((size_t)T * k);
-  s.ffn = carve_ffn(c, &rv, T, k, true, s.sched);
-  s.ybuf = c.take<float>((size_t)T * k * H);
-  s.y_part = c.take<float>((size_t)T * H);
-  s.y_loc = c.take<float>((size_t)T_l * H);
+  s.row_token = c.take<int32_t>((size_t)R * k);
+  s.row_weight = c.take<float>((size_t)R * k);
+  s.pair_row = c.take<int32_t>((size_t)R * k);
+  s.ffn = carve_ffn(c, &rv, R, k, true, s.sched);
+  s.ybuf = c.take<float>((size_t)R * k * H);
+  s.y_recv = c.take<float>((size_t)R * H);
   if (S > 0) {
     const ccut_moe_layer sv = shared_view(L);
-    const size_t R = (size_t)(S + 1) * T_l;
-    s.sh_ids = c.take<int32_t>(T_l);
-    s.sh_w = c.take<float>(T_l);
+    const size_t Rs = (size_t)(S + 1) * T_cap;
+    s.sh_ids = c.take<int32_t>(T_cap);
+    s.sh_w = c.take<float>(T_cap);
     s.sh_counts = c.take<int>(1);
     s.sh_offsets = c.take<int32_t>(S + 2);
-    s.sh_row_token = c.take<int32_t>(R);
-    s.sh_row_weight = c.take<float>(R);
-    s.sh_pair_row = c.take<int32_t>(T_l);
-    s.sh_ffn = carve_ffn(c, &sv, T_l, 1, true, s.sh_sched);
-    s.sh_ybuf = c.take<float>(R * H);
-    s.y_sh = c.take<float>((size_t)T_l * H);
+    s.sh_row_token = c.take<int32_t>(Rs);
+    s.sh_row_weight = c.take<float>(Rs);
+    s.sh_pair_row = c.take<int32_t>(T_cap);
+    s.sh_ffn = carve_ffn(c, &sv, T_cap, 1, true, s.sh_sched);
+    s.sh_ybuf = c.take<float>(Rs * H);
+    s.y_sh = c.take<float>((size_t)T_cap * H);
   }
   return s;
 }
 
 int check_ep(const ccut_ep* ep) {
-  if (!ep || !ep->comm || ep->world < 1 || ep->rank < 0 || ep->rank >= ep->world) return CCUT_ERR_INVALID;
+  if (!ep || ep->world < 1 || ep->world > kMaxWorld || ep->rank < 0 || ep->rank >= ep->world) return CCUT_ERR_INVALID;
+  if (!ep->comm) return CCUT_ERR_NCCL;  // aborted after an expired wait
   return CCUT_OK;
 }
 
-int ep_allgather(ccut_ep* ep, const uint16_t* x, const int32_t* ids, const float* w, int T_l, int H, int k,
-                 uint16_t* x_all, int32_t* ids_all, float* w_all, cudaStream_t st) {
-  ncclResult_t r = ncclGroupStart();
-  if (r != ncclSuccess) return CCUT_ERR_NCCL;
-  ncclAllGather(x, x_all, (size_t)T_l * H * 2, ncclUint8, ep->comm, st);
-  ncclAllGather(ids, ids_all, (size_t)T_l * k, ncclInt32, ep->comm, st);
-  ncclAllGather(w, w_all, (size_t)T_l * k, ncclFloat32, ep->comm, st);
+// The communicator is aborted after an expired host wait: its streams may hold operations that
+// wait for a peer that never came, and only an abort releases them.
+int ep_fail(ccut_ep* ep, int rc) {
+  if (rc == CCUT_ERR_TIMEOUT && ep->comm) {
+    ncclCommAbort(ep->comm);
+    ep->comm = nullptr;
+  }
+  return rc;
+}
+
+// Steps 2-4: plan, count exchange (host-visible), row exchange.  Returns the received row
+// count in *recv_rows.  ids are global expert ids [T_l, k].
+int ep_dispatch(ccut_ep* ep, const uint16_t* x, const int32_t* ids, const float* w, int T_l, int T_cap, int H, int k,
+                int E, const ExScratch& s, uint16_t* x_recv, int32_t* ids_recv, float* w_recv, int recv_capacity,
+                int* recv_rows, cudaStream_t st) {
+  const int P = ep->world;
+  int* send_cnt = s.cnt;
+  int* recv_cnt = s.cnt + P;
+  if (T_l > 0) {
+    int rc = launch_k(ep_plan_kernel, dim3(P), dim3(kPlanThreads), 0, st, x, ids, w, T_l, k, H, E, P, T_cap, send_cnt,
+                      s.send_pos, s.x_send, s.ids_send, s.w_send);
+    if (rc) return rc;
+  } else if (cudaMemsetAsync(send_cnt, 0, sizeof(int) * P, st) != cudaSuccess) {
+    return CCUT_ERR_CUDA;
+  }
+  // count exchange
+  if (ncclGroupStart() != ncclSuccess) return CCUT_ERR_NCCL;
+  for (int d = 0; d < P; ++d) {
+    ncclSend(send_cnt + d, 1, ncclInt32, d, ep->comm, st);
+    ncclRecv(recv_cnt + d, 1, ncclInt32, d, ep->comm, st);
+  }
+  int rc = nccl_settle(ep->comm, ncclGroupEnd(), ep->timeout_s);
+  if (rc) return rc;
+  if (cudaMemcpyAsync(ep->h_counts, s.cnt, sizeof(int) * 2 * P, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaEventRecord(ep->counted, st) != cudaSuccess)
+    return CCUT_ERR_CUDA;
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {  // bounded host wait: a missing peer ends here with a timeout, not a hang
+    const cudaError_t q = cudaEventQuery(ep->counted);
+    if (q == cudaSuccess) break;
+    if (q != cudaErrorNotReady) return CCUT_ERR_CUDA;
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > ep->timeout_s)
+      return ep_fail(ep, CCUT_ERR_TIMEOUT);
+    std::this_thread::yield();
+  }
+  const int* hs = ep->h_counts;
+  const int* hr = ep->h_counts + P;
+  long total = 0;
+  for (int p = 0; p < P; ++p) {
+    if (hs[p] < 0 || hs[p] > T_l || hr[p] < 0) return CCUT_ERR_INVALID;
+    total += hr[p];
+  }
+  if (total > recv_capacity) return CCUT_ERR_WORKSPACE;
+  // row exchange
+  if (ncclGroupStart() != ncclSuccess) return CCUT_ERR_NCCL;
+  long roff = 0;
+  for (int p = 0; p < P; ++p) {
+    if (hs[p] > 0) {
+      const size_t r0 = (size_t)p * T_cap;
+      ncclSend(s.x_send + r0 * H, (size_t)hs[p] * H * 2, ncclUint8, p, ep->comm, st);
+      ncclSend(s.ids_send + r0 * k, (size_t)hs[p] * k, ncclInt32, p, ep->comm, st);
+      ncclSend(s.w_send + r0 * k, (size_t)hs[p] * k, ncclFloat32, p, ep->comm, st);
+    }
+    if (hr[p] > 0) {
+      ncclRecv(x_recv + (size_t)roff * H, (size_t)hr[p] * H * 2, ncclUint8, p, ep->comm, st);
+      ncclRecv(ids_recv + (size_t)roff * k, (size_t)hr[p] * k, ncclInt32, p, ep->comm, st);
+      ncclRecv(w_recv + (size_t)roff * k, (size_t)hr[p] * k, ncclFloat32, p, ep->comm, st);
+    }
+    roff += hr[p];
+  }
+  rc = nccl_settle(ep->comm, ncclGroupEnd(), ep->timeout_s);
+  if (rc) return rc;
+  *recv_rows = static_cast<int>(total);
+  return CCUT_OK;
+}
+
+// Step 6: the partial rows y_recv [recv_rows, H] (fp32) back to their sources, into s.back.
+int ep_return(ccut_ep* ep, const float* y_recv, int T_cap, int H, const ExScratch& s, cudaStream_t st) {
+  const int P = ep->world;
+  const int* hs = ep->h_counts;
+  const int* hr = ep->h_counts + P;
+  if (ncclGroupStart() != ncclSuccess) return CCUT_ERR_NCCL;
+  long roff = 0;
+  for (int p = 0; p < P; ++p) {
+    if (hr[p] > 0) ncclSend(y_recv + (size_t)roff * H, (size_t)hr[p] * H, ncclFloat32, p, ep->comm, st);
+    if (hs[p] > 0) ncclRecv(s.back + (size_t)p * T_cap * H, (size_t)hs[p] * H, ncclFloat32, p, ep->comm, st);
+    roff += hr[p];
+  }
   return nccl_settle(ep->comm, ncclGroupEnd(), ep->timeout_s);
 }
 
-int ep_reduce_scatter(ccut_ep* ep, const float* y_part, int T_l, int H, float* y_loc, cudaStream_t st) {
-  return nccl_settle(ep->comm,
-                     ncclReduceScatter(y_part, y_loc, (size_t)T_l * H, ncclFloat32, ncclSum, ep->comm, st),
-                     ep->timeout_s);
+int launch_ep_sum(const ExScratch& s, const float* shared, int T_l, int world, int H, void* out, int out_dtype,
+                  cudaStream_t st) {
+  if (T_l == 0) return CCUT_OK;
+  const dim3 grid(T_l, (H / 4 + 255) / 256);
+  return launch_k(ep_sum_kernel, grid, dim3(256), 0, st, (const float*)s.back, (const int32_t*)s.send_pos, shared,
+                  world, H, out, out_dtype);
 }
 
 }  // namespace
@@ -249,29 +426,34 @@ int ccut_ep_unique_id(void* id_out) {
 }
 
 int ccut_ep_init(const void* unique_id, int rank, int world, double timeout_s, ccut_ep** out) {
-  if (!unique_id || !out || world < 1 || rank < 0 || rank >= world || !(timeout_s > 0)) return CCUT_ERR_INVALID;
+  if (!unique_id || !out || world < 1 || world > kMaxWorld || rank < 0 || rank >= world || !(timeout_s > 0))
+    return CCUT_ERR_INVALID;
   *out = nullptr;
   ncclUniqueId id;
   std::memcpy(&id, unique_id, sizeof(id));
   // A blocking communicator: init returns once every rank has joined (the caller bounds
   // that wait: the unique id reaches the ranks through a collective with a timeout, and the
-  // process has its own limit); collectives are enqueued without host polling.
+  // process has its own limit); exchanges are enqueued without host polling.
   ncclComm_t comm = nullptr;
   if (ncclCommInitRank(&comm, world, id, rank) != ncclSuccess) {
     if (comm) ncclCommAbort(comm);
     return CCUT_ERR_NCCL;
   }
-  ccut_ep* ep = new (std::nothrow) ccut_ep{comm, rank, world, timeout_s, nullptr, nullptr, nullptr};
+  ccut_ep* ep = new (std::nothrow) ccut_ep{comm, rank, world, timeout_s, nullptr, nullptr, nullptr, nullptr, nullptr};
   if (!ep) {
     ncclCommAbort(comm);
     return CCUT_ERR_INVALID;
   }
   if (cudaStreamCreateWithFlags(&ep->side, cudaStreamNonBlocking) != cudaSuccess ||
       cudaEventCreateWithFlags(&ep->fork, cudaEventDisableTiming) != cudaSuccess ||
-      cudaEventCreateWithFlags(&ep->join, cudaEventDisableTiming) != cudaSuccess) {
+      cudaEventCreateWithFlags(&ep->join, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&ep->counted, cudaEventDisableTiming) != cudaSuccess ||
+      cudaHostAlloc(reinterpret_cast<void**>(&ep->h_counts), sizeof(int) * 2 * world, cudaHostAllocDefault) !=
+          cudaSuccess) {
     ccut_ep_destroy(ep);
     return CCUT_ERR_CUDA;
   }
+  std::memset(ep->h_counts, 0, sizeof(int) * 2 * world);
   *out = ep;
   return CCUT_OK;
 }
@@ -290,66 +472,96 @@ int ccut_ep_destroy(ccut_ep* ep) {
   if (ep->side) cudaStreamDestroy(ep->side);
   if (ep->fork) cudaEventDestroy(ep->fork);
   if (ep->join) cudaEventDestroy(ep->join);
+  if (ep->counted) cudaEventDestroy(ep->counted);
+  if (ep->h_counts) cudaFreeHost(ep->h_counts);
   delete ep;
   return rc;
 }
 
-int ccut_moe_ep_dispatch(ccut_ep* ep, const uint16_t* x, const int32_t* ids, const float* weights, int T_local,
-                         int H, int k, uint16_t* x_all, int32_t* ids_all, float* w_all, ccut_stream_t stream) {
-  int rc = check_ep(ep);
-  if (rc) return rc;
-  if (T_local < 0 || H <= 0 || k < 1 || k > kMaxTopK) return CCUT_ERR_INVALID;
-  if (T_local == 0) return CCUT_OK;
-  if (!x || !ids || !weights || !x_all || !ids_all || !w_all) return CCUT_ERR_INVALID;
-  return ep_allgather(ep, x, ids, weights, T_local, H, k, x_all, ids_all, w_all, stream);
-}
-
-int ccut_moe_ep_combine(ccut_ep* ep, const float* y_part, int T_local, int H, float* y_local, ccut_stream_t stream) {
-  int rc = check_ep(ep);
-  if (rc) return rc;
-  if (T_local < 0 || H <= 0) return CCUT_ERR_INVALID;
-  if (T_local == 0) return CCUT_OK;
-  if (!y_part || !y_local) return CCUT_ERR_INVALID;
-  return ep_reduce_scatter(ep, y_part, T_local, H, y_local, stream);
-}
-
-size_t ccut_moe_ep_forward_workspace_bytes(const ccut_moe_layer* L, int num_experts_global, int world,
-                                           int T_local, int top_k) {
-  if (check_layer(L) || world < 1 || T_local < 0 || top_k < 1 || num_experts_global < L->num_experts) return 0;
+size_t ccut_moe_ep_exchange_workspace_bytes(int world, int T_cap, int H, int k) {
+  if (world < 1 || world > kMaxWorld || T_cap < 0 || H <= 0 || H % 8 || k < 1 || k > kMaxTopK) return 0;
   Carver c(nullptr);
-  carve_ep(c, L, num_experts_global, world, T_local, top_k);
+  carve_ex(c, world, T_cap, H, k);
+  return c.off;
+}
+
+int ccut_moe_ep_dispatch(ccut_ep* ep, const uint16_t* x, const int32_t* ids, const float* weights, int T_local,
+                         int T_cap, int H, int k, int num_experts_global, uint16_t* x_recv, int32_t* ids_recv,
+                         float* w_recv, int recv_capacity, int* recv_rows, void* workspace, size_t ws_bytes,
+                         ccut_stream_t stream) {
+  int rc = check_ep(ep);
+  if (rc) return rc;
+  PdlScope pdl_scope((long)T_local * ep->world);
+  if (T_local < 0 || T_local > T_cap || H <= 0 || H % 8 || k < 1 || k > kMaxTopK || !recv_rows ||
+      num_experts_global < ep->world || num_experts_global > kMaxRoutedExperts || recv_capacity < 0)
+    return CCUT_ERR_INVALID;
+  if ((T_local > 0 && (!x || !ids || !weights)) || (recv_capacity > 0 && (!x_recv || !ids_recv || !w_recv)) ||
+      !workspace)
+    return CCUT_ERR_INVALID;
+  if (ws_bytes < ccut_moe_ep_exchange_workspace_bytes(ep->world, T_cap, H, k)) return CCUT_ERR_WORKSPACE;
+  Carver c(workspace);
+  const ExScratch s = carve_ex(c, ep->world, T_cap, H, k);
+  return ep_dispatch(ep, x, ids, weights, T_local, T_cap, H, k, num_experts_global, s, x_recv, ids_recv, w_recv,
+                     recv_capacity, recv_rows, stream);
+}
+
+int ccut_moe_ep_combine(ccut_ep* ep, const float* y_recv, int T_local, int T_cap, int H, int k, float* y_local,
+                        void* workspace, size_t ws_bytes, ccut_stream_t stream) {
+  int rc = check_ep(ep);
+  if (rc) return rc;
+  PdlScope pdl_scope((long)T_local * ep->world);
+  if (T_local < 0 || T_local > T_cap || H <= 0 || H % 8 || k < 1 || k > kMaxTopK) return CCUT_ERR_INVALID;
+  if ((T_local > 0 && !y_local) || !workspace) return CCUT_ERR_INVALID;
+  long recv = 0;
+  for (int p = 0; p < ep->world; ++p) recv += ep->h_counts[ep->world + p];
+  if (recv > 0 && !y_recv) return CCUT_ERR_INVALID;
+  if (ws_bytes < ccut_moe_ep_exchange_workspace_bytes(ep->world, T_cap, H, k)) return CCUT_ERR_WORKSPACE;
+  Carver c(workspace);
+  const ExScratch s = carve_ex(c, ep->world, T_cap, H, k);
+  rc = ep_return(ep, y_recv, T_cap, H, s, stream);
+  if (rc) return rc;
+  return launch_ep_sum(s, nullptr, T_local, ep->world, H, y_local, CCUT_OUT_F32, stream);
+}
+
+size_t ccut_moe_ep_forward_workspace_bytes(const ccut_moe_layer* L, int num_experts_global, int world, int T_cap,
+                                           int top_k) {
+  if (check_layer(L) || world < 1 || world > kMaxWorld || T_cap < 0 || top_k < 1 || top_k > kMaxTopK ||
+      num_experts_global < L->num_experts)
+    return 0;
+  Carver c(nullptr);
+  carve_ep(c, L, num_experts_global, world, T_cap, top_k);
   return c.off;
 }
 
 int ccut_moe_ep_forward(ccut_ep* ep, const ccut_moe_layer* L, int expert_lo, int num_experts_global,
-                        const ccut_route_params* rp, const uint16_t* x, int T_local, void* out, int out_dtype,
-                        void* workspace, size_t ws_bytes, ccut_stream_t stream) {
+                        const ccut_route_params* rp, const uint16_t* x, int T_local, int T_cap, void* out,
+                        int out_dtype, void* workspace, size_t ws_bytes, ccut_stream_t stream) {
   int rc = check_ep(ep);
   if (rc) return rc;
-  PdlScope pdl_scope((long)T_local * ep->world);  // PDL for decode-sized calls (all ranks' tokens)
+  PdlScope pdl_scope((long)T_local * ep->world);  // PDL for decode-sized calls
   rc = check_layer(L);
   if (rc) return rc;
   if (!L->router) return CCUT_ERR_INVALID;
-  if (num_experts_global < 1 || num_experts_global > kMaxRoutedExperts || expert_lo < 0 ||
-      expert_lo + L->num_experts > num_experts_global)
-    return CCUT_ERR_INVALID;
+  if (num_experts_global < ep->world || num_experts_global > kMaxRoutedExperts ||
+      expert_lo != ep_lo(num_experts_global, ep->world, ep->rank) ||
+      expert_lo + L->num_experts != ep_lo(num_experts_global, ep->world, ep->rank + 1))
+    return CCUT_ERR_INVALID;  // the layer must hold exactly this rank's block of experts
   rc = check_route(rp, num_experts_global);
   if (rc) return rc;
   if (out_dtype != CCUT_OUT_BF16 && out_dtype != CCUT_OUT_F32) return CCUT_ERR_INVALID;
-  if (T_local < 0) return CCUT_ERR_INVALID;
-  // every rank must take part in the collectives, so an empty local batch still runs them
+  if (T_local < 0 || T_local > T_cap) return CCUT_ERR_INVALID;
+  // every rank must take part in the exchanges, so an empty local batch still runs them
   const int k = rp->top_k, H = L->hidden, E_l = L->num_experts, S = L->num_shared_slices;
-  const int T = ep->world * T_local;
   if (T_local > 0 && (!x || !out)) return CCUT_ERR_INVALID;
   if (!workspace) return CCUT_ERR_INVALID;
-  if (ws_bytes < ccut_moe_ep_forward_workspace_bytes(L, num_experts_global, ep->world, T_local, k))
+  if (ws_bytes < ccut_moe_ep_forward_workspace_bytes(L, num_experts_global, ep->world, T_cap, k))
     return CCUT_ERR_WORKSPACE;
-  if (T == 0) return CCUT_OK;
   cudaStream_t st = stream;
   Carver c(workspace);
-  EpScratch s = carve_ep(c, L, num_experts_global, ep->world, T_local, k);
+  EpScratch s = carve_ep(c, L, num_experts_global, ep->world, T_cap, k);
+  int* status = s.ex.status;
 
-  // 5 (forked). shared experts on the local tokens, on the side stream: no routed pair is
+  // 7 (forked). shared experts on the local tokens, on the side stream: no routed pair is
   //    valid there, so every row belongs to a shared slice (rows s * T_local + t)
   const bool shared = S > 0 && T_local > 0;
   if (shared) {
@@ -357,7 +569,6 @@ int ccut_moe_ep_forward(ccut_ep* ep, const ccut_moe_layer* L, int expert_lo, int
     if (cudaEventRecord(ep->fork, st) != cudaSuccess || cudaStreamWaitEvent(ss, ep->fork, 0) != cudaSuccess)
       return CCUT_ERR_CUDA;
     if (cudaMemsetAsync(s.sh_ids, 0xFF, sizeof(int32_t) * T_local, ss) != cudaSuccess) return CCUT_ERR_CUDA;
-    if (cudaMemsetAsync(s.sh_pair_row, 0xFF, sizeof(int32_t) * T_local, ss) != cudaSuccess) return CCUT_ERR_CUDA;
     if (cudaMemsetAsync(s.sh_counts, 0, sizeof(int), ss) != cudaSuccess) return CCUT_ERR_CUDA;
     rc = launch_permute(s.sh_ids, s.sh_w, T_local, 1, 1, S, L->shared_gate, s.sh_counts, s.sh_offsets,
                         s.sh_row_token, s.sh_row_weight, s.sh_pair_row, ss);
@@ -368,7 +579,7 @@ int ccut_moe_ep_forward(ccut_ep* ep, const ccut_moe_layer* L, int expert_lo, int
       if (rc) return rc;
     }
     rc = run_ffn(&sv, T_local, x, s.sh_ffn, T_local, 1, s.sh_offsets, s.sh_row_token, s.sh_row_weight, s.sh_ybuf,
-                 s.status, ss);
+                 status, ss);
     if (rc) return rc;
     rc = launch_combine(s.sh_ybuf, s.sh_pair_row, T_local, 1, H, S, 0, s.y_sh, CCUT_OUT_F32, ss);
     if (rc) return rc;
@@ -380,35 +591,37 @@ int ccut_moe_ep_forward(ccut_ep* ep, const ccut_moe_layer* L, int expert_lo, int
                       s.counts_g, nullptr, st);
     if (rc) return rc;
   }
-  // 2. dispatch
-  rc = ep_allgather(ep, x, s.ids_l, s.w_l, T_local, H, k, s.x_all, s.ids_all, s.w_all, st);
+  // 2-4. plan, counts, routed rows
+  int R = 0;
+  rc = ep_dispatch(ep, x, s.ids_l, s.w_l, T_local, T_cap, H, k, num_experts_global, s.ex, s.x_recv, s.ids_recv,
+                   s.w_recv, ep->world * T_cap, &R, st);
   if (rc) return rc;
-  // 3. local pairs -> permutation -> grouped FFN over the local experts
-  if (cudaMemsetAsync(s.counts, 0, sizeof(int) * E_l, st) != cudaSuccess) return CCUT_ERR_CUDA;
-  rc = launch_k(localize_count_kernel, dim3(grid_for((size_t)T * k, 256 * 4)), dim3(256), 0, st,
-                (const int32_t*)s.ids_all, (const float*)s.w_all, T * k, expert_lo, E_l, s.ids_loc, s.w_loc, s.counts);
-  if (rc) return rc;
-  rc = launch_permute(s.ids_loc, s.w_loc, T, k, E_l, 0, 0.f, s.counts, s.offsets, s.row_token, s.row_weight,
-                      s.pair_row, st);
-  if (rc) return rc;
-  const long per_expert = (long)T * k / num_experts_global;  // rows of a local expert, on average
-  const ccut_moe_layer rv = with_policy(routed_view(L), per_expert);
-  if (rv.kernel == CCUT_KERNEL_MMA) {
-    rc = launch_bf16_to_f16(s.x_all, s.ffn.x16, (size_t)T * H, st);
+  // 5. received rows -> permutation -> grouped FFN over the local experts -> per-row sums
+  if (R > 0) {
+    rc = launch_count(s.ids_recv, R * k, E_l, s.counts, st);
+    if (rc) return rc;
+    rc = launch_permute(s.ids_recv, s.w_recv, R, k, E_l, 0, 0.f, s.counts, s.offsets, s.row_token, s.row_weight,
+                        s.pair_row, st);
+    if (rc) return rc;
+    // rows of a local expert, on average, when the ranks carry T_cap tokens each
+    const long per_expert = (long)T_cap * ep->world * k / num_experts_global;
+    const ccut_moe_layer rv = with_policy(routed_view(L), per_expert);
+    if (rv.kernel == CCUT_KERNEL_MMA) {
+      rc = launch_bf16_to_f16(s.x_recv, s.ffn.x16, (size_t)R * H, st);
+      if (rc) return rc;
+    }
+    rc = run_ffn(&rv, per_expert, s.x_recv, s.ffn, R, k, s.offsets, s.row_token, s.row_weight, s.ybuf, status, st);
+    if (rc) return rc;
+    rc = launch_combine(s.ybuf, s.pair_row, R, k, H, 0, -1, s.y_recv, CCUT_OUT_F32, st);
     if (rc) return rc;
   }
-  rc = run_ffn(&rv, per_expert, s.x_all, s.ffn, T, k, s.offsets, s.row_token, s.row_weight, s.ybuf, s.status, st);
-  if (rc) return rc;
-  // 4. per-token sum of the local rows, then reduce-scatter back to the token owners
-  rc = launch_combine(s.ybuf, s.pair_row, T, k, H, 0, -1, s.y_part, CCUT_OUT_F32, st);
-  if (rc) return rc;
-  rc = ep_reduce_scatter(ep, s.y_part, T_local, H, s.y_loc, st);
+  // 6. partial rows back to their owners
+  rc = ep_return(ep, s.y_recv, T_cap, H, s.ex, st);
   if (rc) return rc;
   if (T_local == 0) return CCUT_OK;
   if (shared && cudaStreamWaitEvent(st, ep->join, 0) != cudaSuccess) return CCUT_ERR_CUDA;
-  const size_t n4 = (size_t)T_local * H / 4;
-  return launch_k(add_cast_kernel, dim3(grid_for(n4, 256)), dim3(256), 0, st, reinterpret_cast<const float4*>(s.y_loc),
-                  shared ? reinterpret_cast<const float4*>(s.y_sh) : nullptr, n4, out, out_dtype);
+  // 7. out[t] = partials in destination order + shared experts
+  return launch_ep_sum(s.ex, shared ? s.y_sh : nullptr, T_local, ep->world, H, out, out_dtype, st);
 }
 
 }  // extern "C"

@@ -24,17 +24,18 @@
 // Work item = (expert, token tile of up to 256 rows, pair p of 128-row weight blocks); each
 // cluster of two CTAs walks the items with a stride of the cluster count.  A 64-k stage is
 // one A tile (128 rows x 64 k bf16, 16 KB) and one B tile (128 tokens x 64 k, 16 KB) per CTA.
-// Warp roles (16 warps per CTA):
+// Warp roles (20 warps per CTA):
 //   warp 0        weight producer: per stage one bulk copy of the packed 64-k half block (and
-//                 the AWQ zero points) into the weight ring
+//                 its scale / zero-point metadata) into the weight ring
 //   warp 1        activation producer: one TMA tile per stage, counted on rank 0's barrier
 //   warp 2        rank 0: the MMA issuer (one thread); both ranks: tensor-memory allocation
-//   warps 4..7    dequant: one weight row per thread, 64 k per stage, into the A tile (128-byte
-//                 swizzled K-major), then a proxy fence and an arrival on rank 0's barrier
-//   warps 8..15   two epilogue warpgroups (128 token columns each): promotion of every 128-k
-//                 partial, then silu(gate) * up as bf16 rows (gate rows pair with up rows through
-//                 shared memory) or row_weight * total as fp32 rows (down)
-// Registers: warpgroups 0 and 1 give theirs up (setmaxnreg) so that each epilogue thread can
+//   warps 4..11   two dequant warpgroups: one weight row and 32 k of each stage per thread,
+//                 into the A tile (128-byte swizzled K-major), then a proxy fence and an
+//                 arrival on rank 0's barrier
+//   warps 12..19  two epilogue warpgroups (128 token columns each): promotion of every 128-k
+//                 partial (packed fp32x2 FMAs), then silu(gate) * up as bf16 rows (gate rows
+//                 pair with up rows through shared memory) or row_weight * total as fp32 rows
+// Registers: warpgroups 0 to 2 give theirs up (setmaxnreg) so that each epilogue thread can
 // hold its 128 fp32 totals.  Every wait is bounded; an expired wait records CCUT_ERR_TIMEOUT
 // and the kernel unwinds.
 //
@@ -63,7 +64,8 @@ struct TcCfg {
   static constexpr int kSW = kAwq ? 6 : 4;            // weight stages
   static constexpr int kXRow = 33;                    // floats per row of the SwiGLU exchange
   static constexpr int kXchg = 2 * 64 * kXRow * 4;
-  static constexpr int kThreads = 512;
+  static constexpr int kThreads = 640;
+  static constexpr int kDeqWarps = 8;
   static constexpr int kEpiWarps = 8;
   static constexpr int kNBar = 2 * kSW + 2 * kSA + 2 + 2 + 1;
   static constexpr int kHeader = kNBar * 8 + 16 + 4 * (kMaxExperts + 1);
@@ -75,9 +77,10 @@ struct TcCfg {
   static_assert(kWBytes % 16 == 0, "bulk copies move multiples of 16 bytes");
 };
 
-// Register shares after setmaxnreg (multiples of 8): the launch gives 512 threads x 128.
-constexpr uint32_t kRegProducers = 40, kRegDequant = 88, kRegEpilogue = 192;
-static_assert(128 * kRegProducers + 128 * kRegDequant + 256 * kRegEpilogue <= 512 * 128, "register pool");
+// Register shares after setmaxnreg (multiples of 8): the launch gives 640 threads x 96 (the
+// largest multiple of 8 within 65536 / 640).
+constexpr uint32_t kRegProducers = 32, kRegDequant = 48, kRegEpilogue = 176;
+static_assert(128 * kRegProducers + 256 * kRegDequant + 256 * kRegEpilogue <= 640 * 96, "register pool");
 
 // Item -> (expert e, weight block pair p, first tile row m0, rows, tile width N).  An expert's
 // M_e rows are cut into ceil(M_e / 256) tiles of equal width (a multiple of 32).
@@ -125,14 +128,17 @@ __device__ __forceinline__ uint32_t e4m3x2_to_bf16x2(uint32_t w) {
   return r;
 }
 
-// Row r of a staged 64-k half block -> 64 bf16 weights (unscaled) as row r of the A tile,
-// 128-byte swizzled K-major: 16-byte chunk c (k 8c .. 8c + 7) at r * 128 + ((c ^ (r & 7)) << 4).
+// k [32 h, 32 h + 32) of row r of a staged 64-k half block -> 32 bf16 weights (unscaled) in
+// row r of the A tile, 128-byte swizzled K-major: 16-byte chunk c (k 8c .. 8c + 7) at
+// r * 128 + ((c ^ (r & 7)) << 4).
 template <int FMT>
-__device__ __forceinline__ void dequant_row(const uint8_t* half, const uint8_t* meta, int r, uint8_t* atile) {
+__device__ __forceinline__ void dequant_half_row(const uint8_t* half, const uint8_t* zeros, int r, int h,
+                                                 uint8_t* atile) {
   uint8_t* arow = atile + r * 128;
   if constexpr (FMT == CCUT_FMT_FP8_E4M3_B128) {
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {  // 16 e4m3 values: k 16c .. 16c + 15
+    for (int cc = 0; cc < 2; ++cc) {  // 16 e4m3 values: k 16c .. 16c + 15
+      const int c = 2 * h + cc;
       const uint4 q = *reinterpret_cast<const uint4*>(half + r * 64 + 16 * (c ^ ((r >> 1) & 3)));
       const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
       uint32_t o[8];
@@ -145,23 +151,20 @@ __device__ __forceinline__ void dequant_row(const uint8_t* half, const uint8_t* 
       *reinterpret_cast<uint4*>(arow + (((2 * c + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
     }
   } else {
-    const uint32_t z = (meta[r >> 1] >> (4 * (r & 1))) & 0xFu;
+    const uint32_t z = (zeros[r >> 1] >> (4 * (r & 1))) & 0xFu;
     const uint32_t zz = (0x4300u | z) * 0x10001u;  // bf16x2 (128 + z, 128 + z)
+    const uint4 q = *reinterpret_cast<const uint4*>(half + r * 32 + 16 * (h ^ ((r >> 2) & 1)));  // k 32h .. +31
+    const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {  // 32 nibbles: k 32c .. 32c + 31
-      const uint4 q = *reinterpret_cast<const uint4*>(half + r * 32 + 16 * (c ^ ((r >> 2) & 1)));
-      const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+    for (int j = 0; j < 4; ++j) {  // word j: k 32h + 8j .. +7 -> A chunk 4h + j
+      uint32_t o[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {  // word j: k 32c + 8j .. +7 -> A chunk 4c + j
-        uint32_t o[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          uint32_t v;  // bf16x2 (128 + q_lo, 128 + q_hi); minus (128 + z) is q - z, exact
-          asm("lop3.b32 %0, %1, 0x000F000F, 0x43004300, 0xEA;" : "=r"(v) : "r"(w4[j] >> (4 * i)));
-          o[i] = bf16x2_sub(v, zz);
-        }
-        *reinterpret_cast<uint4*>(arow + (((4 * c + j) ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+      for (int i = 0; i < 4; ++i) {
+        uint32_t v;  // bf16x2 (128 + q_lo, 128 + q_hi); minus (128 + z) is q - z, exact
+        asm("lop3.b32 %0, %1, 0x000F000F, 0x43004300, 0xEA;" : "=r"(v) : "r"(w4[j] >> (4 * i)));
+        o[i] = bf16x2_sub(v, zz);
       }
+      *reinterpret_cast<uint4*>(arow + (((4 * h + j) ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
     }
   }
 }
@@ -180,8 +183,21 @@ __device__ __forceinline__ void named_bar(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// total[i] += s * partial[i] for 16 columns, as 8 packed fp32x2 FMAs.
+__device__ __forceinline__ void promote16(float* tot, const uint32_t (&v)[16], float s) {
+  const uint64_t ss = (static_cast<uint64_t>(__float_as_uint(s)) << 32) | __float_as_uint(s);
+#pragma unroll
+  for (int i = 0; i < 16; i += 2) {
+    uint64_t acc = (static_cast<uint64_t>(__float_as_uint(tot[i + 1])) << 32) | __float_as_uint(tot[i]);
+    const uint64_t pv = (static_cast<uint64_t>(v[i + 1]) << 32) | v[i];
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(ss), "l"(pv));
+    tot[i] = __uint_as_float(static_cast<uint32_t>(acc));
+    tot[i + 1] = __uint_as_float(static_cast<uint32_t>(acc >> 32));
+  }
+}
+
 template <int FMT, int MODE>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap bmap, TcArgs a) {
   pdl_wait();
   pdl_trigger();
@@ -219,10 +235,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < SW; ++s) {
       mbar_init(&wfull[s], 1);
-      mbar_init(&wempty[s], 4);
+      mbar_init(&wempty[s], C::kDeqWarps);
     }
     for (int s = 0; s < SA; ++s) {
-      mbar_init(&abfull[s], 2 * 4 + 2);  // dequant warps of both CTAs + both TMA threads
+      mbar_init(&abfull[s], 2 * C::kDeqWarps + 2);  // dequant warps of both CTAs + both TMA threads
       mbar_init(&abempty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -346,10 +362,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
       tc::commit2_mc(drain, 1);  // all MMAs issued above have completed once this lands
       mbar_wait(drain, 0, a.status);
     }
-  } else if (warp < 8) {
-    // ------------------------------------------------------------ dequant warpgroup
+  } else if (warp < 12) {
+    // ------------------------------------------------------------ dequant warpgroups
     tc::setmaxnreg_dec<kRegDequant>();
-    const int r = (warp - 4) * 32 + lane;  // weight row of this thread
+    const int dq = (warp - 4) * 32 + lane;
+    const int r = dq & 127, hk = dq >> 7;  // weight row and 32-k half of the stage of this thread
     int use = 0;
     bool ok = true;
     for (int item = cluster; item < total && ok; item += nclusters) {
@@ -365,7 +382,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
         }
         if (valid) {
           const uint8_t* half = wtiles + s * C::kWBytes;
-          dequant_row<FMT>(half, half + C::kHalfW + (C::kAwq ? 256 : 0), r, ab + sa * C::kAB);
+          dequant_half_row<FMT>(half, half + C::kHalfW + (C::kAwq ? 256 : 0), r, hk, ab + sa * C::kAB);
         }
         tc::fence_proxy_async_smem();
         __syncwarp();
@@ -378,7 +395,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
   } else {
     // ------------------------------------------------------------ epilogue warpgroups
     tc::setmaxnreg_inc<kRegEpilogue>();
-    const int ewg = (warp - 8) >> 2;  // token columns [128 ewg, 128 ewg + 128)
+    const int ewg = (warp - 12) >> 2;  // token columns [128 ewg, 128 ewg + 128)
     const int q = warp & 3;           // tensor-memory lane quarter
     const int r = q * 32 + lane;      // weight row of this thread
     const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ewg * 128);
@@ -413,11 +430,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
 #pragma unroll
         for (int c = 0; c < 128; c += 32) {
           if (c < ncols) {  // uniform over the warpgroup
-            uint32_t v[32];
-            tc::ld_32x32b_x32(tl + (uint32_t)(slot * 256 + c), v);
-            tc::wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) tot[c + i] = fmaf(s, __uint_as_float(v[i]), tot[c + i]);
+            for (int c2 = 0; c2 < 32; c2 += 16) {  // 16 columns per load: registers for the totals
+              uint32_t v[16];
+              tc::ld_32x32b_x16(tl + (uint32_t)(slot * 256 + c + c2), v);
+              tc::wait_ld();
+              promote16(tot + c + c2, v, s);
+            }
           }
         }
         tc::fence_before_sync();
@@ -438,23 +457,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
             }
             named_bar(1 + ewg, 128);
             if (q < 2) {
-              // all 32 values first (no branch between them, so their exp / reciprocal
-              // latencies overlap), then the stores, guarded only on a partial chunk
-              uint16_t hv[32];
 #pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                const float g = tot[c + i];
-                hv[i] = __bfloat16_as_ushort(__float2bfloat16_rn(__fdividef(g, 1.0f + __expf(-g)) * xb[r * C::kXRow + i]));
-              }
-              uint16_t* orow = static_cast<uint16_t*>(a.out) + (size_t)(row0 + ewg * 128 + c) * a.out_ld + ch;
-              const int left = rows - (ewg * 128 + c);
-              if (left >= 32) {
+              for (int c2 = 0; c2 < 32; c2 += 16) {
+                // all 16 values first (no branch between them, so their exp / reciprocal
+                // latencies overlap), then the stores, guarded only on a partial chunk
+                uint16_t hv[16];
 #pragma unroll
-                for (int i = 0; i < 32; ++i) orow[(size_t)i * a.out_ld] = hv[i];
-              } else {
+                for (int i = 0; i < 16; ++i) {
+                  const float g = tot[c + c2 + i];
+                  hv[i] = __bfloat16_as_ushort(
+                      __float2bfloat16_rn(__fdividef(g, 1.0f + __expf(-g)) * xb[r * C::kXRow + c2 + i]));
+                }
+                uint16_t* orow = static_cast<uint16_t*>(a.out) + (size_t)(row0 + ewg * 128 + c + c2) * a.out_ld + ch;
+                const int left = rows - (ewg * 128 + c + c2);
+                if (left >= 16) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                  if (i < left) orow[(size_t)i * a.out_ld] = hv[i];
+                  for (int i = 0; i < 16; ++i) orow[(size_t)i * a.out_ld] = hv[i];
+                } else {
+#pragma unroll
+                  for (int i = 0; i < 16; ++i)
+                    if (i < left) orow[(size_t)i * a.out_ld] = hv[i];
+                }
               }
             }
             named_bar(1 + ewg, 128);
@@ -465,22 +488,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
 #pragma unroll
         for (int c = 0; c < 128; c += 32) {
           if (c < ncols) {
-            const int t0 = ewg * 128 + c;
-            const int left = rows - t0;
-            float* orow = static_cast<float*>(a.out) + (size_t)(row0 + t0) * a.out_ld + ch;
-            float v[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {  // routing weights of the chunk's rows (clamped index)
-              const float wr = a.row_weight ? __ldg(a.row_weight + row0 + t0 + min(i, left - 1)) : 1.f;
-              v[i] = tot[c + i] * wr;
-            }
-            if (left >= 32) {
+            for (int c2 = 0; c2 < 32; c2 += 16) {
+              const int t0 = ewg * 128 + c + c2;
+              const int left = rows - t0;
+              float* orow = static_cast<float*>(a.out) + (size_t)(row0 + t0) * a.out_ld + ch;
+              float v[16];
 #pragma unroll
-              for (int i = 0; i < 32; ++i) orow[(size_t)i * a.out_ld] = v[i];
-            } else {
+              for (int i = 0; i < 16; ++i) {  // routing weights of the chunk's rows (clamped index)
+                const float wr = a.row_weight ? __ldg(a.row_weight + row0 + t0 + min(i, max(left - 1, 0))) : 1.f;
+                v[i] = tot[c + c2 + i] * wr;
+              }
+              if (left >= 16) {
 #pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if (i < left) orow[(size_t)i * a.out_ld] = v[i];
+                for (int i = 0; i < 16; ++i) orow[(size_t)i * a.out_ld] = v[i];
+              } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                  if (i < left) orow[(size_t)i * a.out_ld] = v[i];
+              }
             }
           }
         }

@@ -2,11 +2,12 @@
 
 Rank ``r`` of ``world`` keeps routed experts ``expert_range(E, world, r)`` and every shared
 expert resident in its HBM.  ``forward`` takes this rank's tokens and runs
-``ccut_moe_ep_forward``: route locally, all-gather tokens and routing over NCCL, run the
-grouped FFN on the (token, slot) pairs routed to local experts, reduce-scatter the partial
-outputs back to the token owners, add the shared experts (data-parallel on the local
-tokens).  The NCCL communicator belongs to the C library; ``torch.distributed`` (any
-backend) only carries its unique id from rank 0 to the others.
+``ccut_moe_ep_forward``: route locally, exchange per-destination row counts, send each token
+row once to every rank that owns one of its experts (NCCL send / receive of the routed rows
+only), run the received rows through the local grouped FFN, send one partial row per
+(token, rank) back to the token's owner, which sums them in rank order and adds the shared
+experts (data-parallel on the local tokens).  The NCCL communicator belongs to the C library;
+``torch.distributed`` (any backend) only carries its unique id from rank 0 to the others.
 
 The reference has no expert parallelism (one process runs a layer's experts,
 ``ccut/models/generic.py:364-385``); the partitioning follows the layout of its experts
@@ -66,13 +67,15 @@ class ExpertParallelMoeLayer:
 
     Arguments are those of ``MoeLayer`` for the whole layer (all ``num_experts`` routed
     experts); only this rank's block of experts is packed and kept.  ``rank`` / ``world``
-    default to ``torch.distributed``'s.  Every rank calls ``forward`` with the same number
-    of tokens (its own)."""
+    default to ``torch.distributed``'s.  Every rank calls ``forward`` (collective) with its own
+    tokens; the counts may differ between ranks up to ``max_tokens``, which every rank must
+    pass alike (default: each call's own count, for ranks that always carry equal batches)."""
 
     def __init__(self, fmt, hidden, inter, num_experts, top_k, routing, router, experts, shared=None,
                  shared_inter=None, shared_gate=1.0, n_group=1, topk_group=1, routed_scaling=1.0, bias=None,
                  nibble_order="awq", kernel="auto", device="cuda", rank=None, world=None, group=None,
-                 timeout_s: float = 60.0):
+                 timeout_s: float = 60.0, max_tokens: int | None = None):
+        self.max_tokens = int(max_tokens) if max_tokens is not None else None
         if rank is None or world is None:
             import torch.distributed as dist
 
@@ -118,15 +121,19 @@ class ExpertParallelMoeLayer:
         if out_dtype not in (torch.bfloat16, torch.float32):
             raise ValueError("out_dtype must be bf16 or fp32")
         out = torch.empty((T, self.hidden), dtype=out_dtype, device=self.device)
-        nbytes = self.lib.ccut_moe_ep_forward_workspace_bytes(C.byref(self.desc), self.num_experts, self.world, T,
-                                                              self.top_k)
+        T_cap = T if self.max_tokens is None else self.max_tokens
+        if T > T_cap:
+            raise ValueError(f"{T} tokens exceed max_tokens = {T_cap}")
+        nbytes = self.lib.ccut_moe_ep_forward_workspace_bytes(C.byref(self.desc), self.num_experts, self.world,
+                                                              T_cap, self.top_k)
         if nbytes == 0:
             raise ValueError("invalid expert-parallel layer or shape")
         if self._ws is None or self._ws.numel() < nbytes:
             self._ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
         od = _lib.OUT_BF16 if out_dtype == torch.bfloat16 else _lib.OUT_F32
         _lib.call("ccut_moe_ep_forward", self._ep, C.byref(self.desc), self.lo, self.num_experts,
-                  C.byref(self.route_params), _ptr(x), T, _ptr(out), od, _ptr(self._ws), self._ws.numel(), _stream())
+                  C.byref(self.route_params), _ptr(x), T, T_cap, _ptr(out), od, _ptr(self._ws), self._ws.numel(),
+                  _stream())
         return out
 
     __call__ = forward

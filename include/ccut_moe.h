@@ -311,41 +311,69 @@ CCUT_API int ccut_mla_attention_pool(const float* q, const uint16_t* kv_pool, co
  * wait expired stores CCUT_ERR_TIMEOUT there instead of hanging.  Reads it (synchronises
  * `stream`) and clears it. */
 CCUT_API int ccut_workspace_status(void* workspace, ccut_stream_t stream);
+/* No reference counterpart (the reference's only timeout is the host-side one of
+ * ccut/experts/reader.py:320-331).  Test of the kernels' bounded device waits: one small
+ * launch waits, with the same wait routines the kernels use and a limit of budget_cycles SM
+ * clocks (at most the kernels' own ~1 s), on one mbarrier that completes and on one that
+ * nothing ever arrives on.  The second wait runs out, stores CCUT_ERR_TIMEOUT in the status
+ * word of `workspace` (at least 256 bytes, zero-filled) and the kernel returns; int 1 of the
+ * workspace receives the outcome bits (1: the completed wait succeeded; 2 and 4: the waits on
+ * the idle barrier succeeded, which they must not).  Read the status with
+ * ccut_workspace_status. */
+CCUT_API int ccut_debug_wait_expiry(void* workspace, long long budget_cycles, ccut_stream_t stream);
 
 /* ---- expert parallelism over NCCL (no reference counterpart: the reference runs a
  * layer's experts in one process, ccut/models/generic.py:364-385,
  * ccut/experts/pipeline.py:123-190) -------------------------------------------------- */
-/* One process per GPU.  Rank r holds routed experts [expert_lo, expert_lo + E_r) and every
- * shared expert; all ranks pass the same T_local.  ccut_ep_init is collective and returns
- * once every rank has joined: distribute the unique id through a channel with a timeout
- * (e.g. a torch.distributed broadcast) so that a missing rank fails there.  `timeout_s`
- * bounds the host waits of ccut_ep_destroy. */
+/* One process per GPU.  Rank r holds the routed experts [lo_r, hi_r) -- contiguous blocks of
+ * E_global experts whose sizes differ by at most one, lo_r = r * (E/P) + min(r, E % P) -- and
+ * every shared expert.  Ranks may carry different token counts T_local, all at most the
+ * T_cap every rank sized its workspace for.  Only routed rows cross the links: a token row
+ * goes once to each rank that owns one of its experts, and one fp32 partial row per
+ * (token, rank) comes back.  ccut_ep_init is collective and returns once every rank has
+ * joined: distribute the unique id through a channel with a timeout (e.g. a
+ * torch.distributed broadcast) so that a missing rank fails there.  `timeout_s` bounds every
+ * host wait of the handle; a wait that expires returns CCUT_ERR_TIMEOUT and aborts the
+ * communicator (later calls return CCUT_ERR_NCCL: destroy the handle). */
 typedef struct ccut_ep ccut_ep;
 /* Size of the NCCL unique id (host bytes) that rank 0 creates and every rank passes to
  * ccut_ep_init. */
 CCUT_API size_t ccut_ep_unique_id_bytes(void);
 CCUT_API int ccut_ep_unique_id(void* id_out);
-/* Collective over `world` ranks; uses the current CUDA device. */
+/* Collective over `world` ranks (at most 64); uses the current CUDA device. */
 CCUT_API int ccut_ep_init(const void* unique_id, int rank, int world, double timeout_s, ccut_ep** out);
 CCUT_API int ccut_ep_destroy(ccut_ep* ep);
-/* Dispatch: all-gather of the local tokens x bf16 [T_local, H], ids int32 [T_local, k] and
- * routing weights fp32 [T_local, k] into [world * T_local, ...] (rank-major). */
-CCUT_API int ccut_moe_ep_dispatch(ccut_ep* ep, const uint16_t* x, const int32_t* ids,
-                                  const float* weights, int T_local, int H, int k, uint16_t* x_all,
-                                  int32_t* ids_all, float* w_all, ccut_stream_t stream);
-/* Combine: y_local fp32 [T_local, H] = sum over ranks of their partial outputs for this
- * rank's tokens, from y_part fp32 [world * T_local, H] (reduce-scatter). */
-CCUT_API int ccut_moe_ep_combine(ccut_ep* ep, const float* y_part, int T_local, int H,
-                                 float* y_local, ccut_stream_t stream);
-/* Whole expert-parallel layer: route (against L->router, fp32 [E_global, H]), dispatch,
- * local grouped FFN, combine, shared experts; out [T_local, H] bf16 or fp32.  L describes
- * this rank's experts: num_experts = E_r routed experts (global ids expert_lo..), then the
- * shared slices.  Every rank must call it, also with T_local = 0. */
+/* Workspace of ccut_moe_ep_dispatch / ccut_moe_ep_combine (the plan of a dispatch, which its
+ * combine reads back). */
+CCUT_API size_t ccut_moe_ep_exchange_workspace_bytes(int world, int T_cap, int H, int k);
+/* Dispatch: the local tokens x bf16 [T_local, H] with their routing ids int32 [T_local, k]
+ * (global expert ids) and weights fp32 [T_local, k] go to the ranks that own their experts.
+ * Counts are exchanged first (grouped ncclSend / ncclRecv of one int per pair of ranks, read
+ * back on the host: this call waits for them), then the rows.  Received rows are packed by
+ * source rank (rank 0's first), each with its k ids made local to this rank (-1 for experts
+ * elsewhere) and its k weights: x_recv bf16 [*recv_rows, H], ids_recv int32 [*recv_rows, k],
+ * w_recv fp32 [*recv_rows, k]; *recv_rows (host int) <= recv_capacity, else
+ * CCUT_ERR_WORKSPACE.  Collective: every rank calls it, also with T_local = 0. */
+CCUT_API int ccut_moe_ep_dispatch(ccut_ep* ep, const uint16_t* x, const int32_t* ids, const float* weights,
+                                  int T_local, int T_cap, int H, int k, int num_experts_global, uint16_t* x_recv,
+                                  int32_t* ids_recv, float* w_recv, int recv_capacity, int* recv_rows,
+                                  void* workspace, size_t ws_bytes, ccut_stream_t stream);
+/* Combine: y_recv fp32 [recv_rows, H], one partial output per row the last dispatch on this
+ * handle received (in its order), goes back to the row's source; y_local fp32 [T_local, H] =
+ * for each local token the sum of its partial rows in rank order (0 for a token routed to no
+ * expert).  Same workspace as that dispatch.  Collective. */
+CCUT_API int ccut_moe_ep_combine(ccut_ep* ep, const float* y_recv, int T_local, int T_cap, int H, int k,
+                                 float* y_local, void* workspace, size_t ws_bytes, ccut_stream_t stream);
+/* Whole expert-parallel layer: route (against L->router, fp32 [E_global, H]), dispatch, the
+ * received rows through the local grouped FFN, combine, shared experts (on a second stream,
+ * overlapping the exchange); out [T_local, H] bf16 or fp32.  L describes this rank's experts:
+ * num_experts = hi_r - lo_r routed experts (global ids expert_lo = lo_r ..), then the shared
+ * slices.  Every rank must call it, also with T_local = 0. */
 CCUT_API size_t ccut_moe_ep_forward_workspace_bytes(const ccut_moe_layer* L, int num_experts_global,
-                                                    int world, int T_local, int top_k);
+                                                    int world, int T_cap, int top_k);
 CCUT_API int ccut_moe_ep_forward(ccut_ep* ep, const ccut_moe_layer* L, int expert_lo,
                                  int num_experts_global, const ccut_route_params* rp,
-                                 const uint16_t* x, int T_local, void* out, int out_dtype,
+                                 const uint16_t* x, int T_local, int T_cap, void* out, int out_dtype,
                                  void* workspace, size_t ws_bytes, ccut_stream_t stream);
 
 #ifdef __cplusplus

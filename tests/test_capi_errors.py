@@ -207,3 +207,30 @@ def test_mla_pool_attention_checks(lib):
     need = lib.ccut_mla_attention_workspace_bytes(3, 16, 1, 300)
     assert need > 256
     assert call(ws=need - 1) == _lib.ERR_WORKSPACE
+
+
+def test_expert_parallel_checks(lib):
+    """The routed-rows exchange's size queries and argument checks, before any NCCL call."""
+    nb = lib.ccut_moe_ep_exchange_workspace_bytes(2, 64, 256, 6)
+    assert nb > 2 * 64 * 256 * 2  # at least the send rows
+    assert lib.ccut_moe_ep_exchange_workspace_bytes(0, 64, 256, 6) == 0
+    assert lib.ccut_moe_ep_exchange_workspace_bytes(65, 64, 256, 6) == 0  # at most 64 ranks
+    assert lib.ccut_moe_ep_exchange_workspace_bytes(2, 64, 100, 6) == 0  # rows of 16-byte lanes
+    assert lib.ccut_moe_ep_exchange_workspace_bytes(2, 64, 256, 17) == 0
+    n = C.c_int(0)
+    # no handle
+    assert lib.ccut_moe_ep_dispatch(NULL, FAKE, FAKE, FAKE, 4, 4, 256, 2, 8, FAKE, FAKE, FAKE, 8, C.byref(n), FAKE,
+                                    nb, NULL) == _lib.ERR_INVALID
+    assert lib.ccut_moe_ep_combine(NULL, FAKE, 4, 4, 256, 2, FAKE, FAKE, nb, NULL) == _lib.ERR_INVALID
+    layer = _lib.MoeLayerDesc(_lib.FMT_FP8_E4M3_B128, 0, 256, 128, 4, 0, 1.0, FAKE.value, FAKE.value, None, None,
+                              FAKE.value)
+    assert lib.ccut_moe_ep_forward_workspace_bytes(C.byref(layer), 8, 2, 64, 2) > 0
+    assert lib.ccut_moe_ep_forward_workspace_bytes(C.byref(layer), 2, 2, 64, 2) == 0  # fewer global than local
+    assert lib.ccut_moe_ep_forward(NULL, C.byref(layer), 0, 8, C.byref(_rp()), FAKE, 4, 4, FAKE, 0, FAKE, 1 << 30,
+                                   NULL) == _lib.ERR_INVALID
+
+
+def test_wait_expiry_checks(lib):
+    assert lib.ccut_debug_wait_expiry(NULL, 1000, NULL) == _lib.ERR_INVALID
+    assert lib.ccut_debug_wait_expiry(FAKE, -1, NULL) == _lib.ERR_INVALID
+    assert lib.ccut_debug_wait_expiry(FAKE, 1 << 40, NULL) == _lib.ERR_INVALID  # above the kernels' own budget

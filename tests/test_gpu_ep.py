@@ -71,6 +71,9 @@ def test_ep_world1_matches_oracle(fmt, mode, E, k, shared, T, kernel):
 
 
 def test_ep_dispatch_and_combine_world1():
+    """The routed-rows exchange on one rank: a token goes to the rank once if any of its ids is
+    a global expert in [0, E) and never if none is; its ids arrive made local (-1 elsewhere);
+    combine returns each token's partial row (0 for a token that went nowhere)."""
     from ccut_b200 import _lib
     from ccut_b200.ep import _broadcast_unique_id
 
@@ -80,21 +83,36 @@ def test_ep_dispatch_and_combine_world1():
     h = C.c_void_p()
     _lib.call("ccut_ep_init", C.cast(buf, C.c_void_p), 0, 1, C.c_double(30.0), C.byref(h))
     try:
-        T, H, k = 7, 256, 3
+        T, H, k, E = 9, 256, 3, 8
         x = torch.randn(T, H, device="cuda").to(torch.bfloat16)
-        ids = torch.randint(0, 8, (T, k), device="cuda", dtype=torch.int32)
+        ids = torch.randint(0, E, (T, k), device="cuda", dtype=torch.int32)
+        ids[2] = -1  # token 2 routed nowhere
         w = torch.rand(T, k, device="cuda")
-        xa, ia, wa = torch.empty_like(x), torch.empty_like(ids), torch.empty_like(w)
+        xr = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+        ir = torch.empty(T, k, dtype=torch.int32, device="cuda")
+        wr = torch.empty(T, k, device="cuda")
+        nb = lib.ccut_moe_ep_exchange_workspace_bytes(1, T, H, k)
+        ws = torch.zeros(nb, dtype=torch.uint8, device="cuda")
         s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
         p = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
-        _lib.call("ccut_moe_ep_dispatch", h, p(x), p(ids), p(w), T, H, k, p(xa), p(ia), p(wa), s)
-        y = torch.randn(T, H, device="cuda")
-        yl = torch.empty_like(y)
-        _lib.call("ccut_moe_ep_combine", h, p(y), T, H, p(yl), s)
+        nrecv = C.c_int(-1)
+        _lib.call("ccut_moe_ep_dispatch", h, p(x), p(ids), p(w), T, T, H, k, E, p(xr), p(ir), p(wr), T,
+                  C.byref(nrecv), p(ws), nb, s)
         torch.cuda.synchronize()
-        assert torch.equal(xa, x) and torch.equal(ia, ids) and torch.equal(wa, w) and torch.equal(yl, y)
+        sent = [t for t in range(T) if t != 2]
+        assert nrecv.value == len(sent)
+        assert torch.equal(xr[:len(sent)], x[sent]) and torch.equal(ir[:len(sent)], ids[sent])
+        assert torch.equal(wr[:len(sent)], w[sent])
+        y = torch.randn(len(sent), H, device="cuda")
+        yl = torch.full((T, H), 7.0, device="cuda")
+        _lib.call("ccut_moe_ep_combine", h, p(y), T, T, H, k, p(yl), p(ws), nb, s)
+        torch.cuda.synchronize()
+        assert torch.equal(yl[sent], y) and torch.equal(yl[2], torch.zeros(H, device="cuda"))
         with pytest.raises(ValueError):
-            _lib.call("ccut_moe_ep_combine", h, p(y), -1, H, p(yl), s)
+            _lib.call("ccut_moe_ep_combine", h, p(y), -1, T, H, k, p(yl), p(ws), nb, s)
+        with pytest.raises(ValueError):  # more tokens than the workspace was planned for
+            _lib.call("ccut_moe_ep_dispatch", h, p(x), p(ids), p(w), T, T - 1, H, k, E, p(xr), p(ir), p(wr), T,
+                      C.byref(nrecv), p(ws), nb, s)
     finally:
         _lib.call("ccut_ep_destroy", h)
 
