@@ -62,8 +62,8 @@ struct TcCfg {
   static constexpr int kAB = 32768;                   // A tile 16 KB + B tile 16 KB
   static constexpr int kSA = 5;                       // A/B stages
   static constexpr int kSW = kAwq ? 6 : 4;            // weight stages
-  static constexpr int kXRow = 33;                    // floats per row of the SwiGLU exchange
-  static constexpr int kXchg = 2 * 64 * kXRow * 4;
+  static constexpr int kXRow = 17;                    // floats per row of the output staging (16 + pad)
+  static constexpr int kXchg = 2 * 128 * kXRow * 4;   // per epilogue warpgroup: 128 rows x 16 tokens
   static constexpr int kThreads = 640;
   static constexpr int kDeqWarps = 8;
   static constexpr int kEpiWarps = 8;
@@ -399,7 +399,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
     const int q = warp & 3;           // tensor-memory lane quarter
     const int r = q * 32 + lane;      // weight row of this thread
     const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ewg * 128);
-    float* xb = xchg + ewg * 64 * C::kXRow;
+    float* xb = xchg + ewg * 128 * C::kXRow;
     const uint32_t pe0 = tc::mapa(&pempty[0], 0), pe1 = tc::mapa(&pempty[1], 0);
     int j = 0;
     bool ok = true;
@@ -444,71 +444,46 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
         if (lane == 0) tc::mbar_arrive_cl(slot ? pe1 : pe0);
       }
       if (!ok || !valid) continue;
+      // Output: the totals go through shared memory 16 tokens at a time (thread r writes row r),
+      // then each thread of the warpgroup produces 8 (FFN1) or 16 (FFN2) consecutive output
+      // channels of one token and stores them as 16-byte vectors.
       const int row0 = a.offsets[e] + m0;
-      if constexpr (MODE == kFfn1) {
-        // rows 0..63: gate, rows 64..127: up of the same 64 channels
-        const int ch = blk * 64 + r;
+      const int tt = threadIdx.x & 15;          // token of the chunk this thread writes out
+      const int grp = (threadIdx.x >> 4) & 7;   // channel group of this thread
 #pragma unroll
-        for (int c = 0; c < 128; c += 32) {
-          if (c < ncols) {
-            if (q >= 2) {
+      for (int c = 0; c < 128; c += 16) {
+        if (c < ncols) {  // uniform over the warpgroup
 #pragma unroll
-              for (int i = 0; i < 32; ++i) xb[(r - 64) * C::kXRow + i] = tot[c + i];
-            }
-            named_bar(1 + ewg, 128);
-            if (q < 2) {
+          for (int i = 0; i < 16; ++i) xb[r * C::kXRow + i] = tot[c + i];
+          named_bar(1 + ewg, 128);
+          const int tok = ewg * 128 + c + tt;  // token index inside the tile
+          if (tok < rows) {
+            if constexpr (MODE == kFfn1) {
+              // rows 0..63: gate, rows 64..127: up of the same 64 channels; channels grp*8 .. +7
+              uint32_t pk[4];
 #pragma unroll
-              for (int c2 = 0; c2 < 32; c2 += 16) {
-                // all 16 values first (no branch between them, so their exp / reciprocal
-                // latencies overlap), then the stores, guarded only on a partial chunk
-                uint16_t hv[16];
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                  const float g = tot[c + c2 + i];
-                  hv[i] = __bfloat16_as_ushort(
-                      __float2bfloat16_rn(__fdividef(g, 1.0f + __expf(-g)) * xb[r * C::kXRow + c2 + i]));
-                }
-                uint16_t* orow = static_cast<uint16_t*>(a.out) + (size_t)(row0 + ewg * 128 + c + c2) * a.out_ld + ch;
-                const int left = rows - (ewg * 128 + c + c2);
-                if (left >= 16) {
-#pragma unroll
-                  for (int i = 0; i < 16; ++i) orow[(size_t)i * a.out_ld] = hv[i];
-                } else {
-#pragma unroll
-                  for (int i = 0; i < 16; ++i)
-                    if (i < left) orow[(size_t)i * a.out_ld] = hv[i];
-                }
+              for (int j = 0; j < 8; j += 2) {
+                const float g0 = xb[(grp * 8 + j) * C::kXRow + tt], g1 = xb[(grp * 8 + j + 1) * C::kXRow + tt];
+                const float u0 = xb[(64 + grp * 8 + j) * C::kXRow + tt];
+                const float u1 = xb[(64 + grp * 8 + j + 1) * C::kXRow + tt];
+                const __nv_bfloat162 h2 = __floats2bfloat162_rn(__fdividef(g0, 1.0f + __expf(-g0)) * u0,
+                                                                __fdividef(g1, 1.0f + __expf(-g1)) * u1);
+                pk[j >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
               }
-            }
-            named_bar(1 + ewg, 128);
-          }
-        }
-      } else {
-        const int ch = blk * kTileN + r;
+              uint16_t* orow = static_cast<uint16_t*>(a.out) + (size_t)(row0 + tok) * a.out_ld + blk * 64 + grp * 8;
+              *reinterpret_cast<uint4*>(orow) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            } else {
+              // channels grp*16 .. +15 of the block's 128, times the row's routing weight
+              const float wr = a.row_weight ? __ldg(a.row_weight + row0 + tok) : 1.f;
+              float* orow = static_cast<float*>(a.out) + (size_t)(row0 + tok) * a.out_ld + blk * kTileN + grp * 16;
 #pragma unroll
-        for (int c = 0; c < 128; c += 32) {
-          if (c < ncols) {
-#pragma unroll
-            for (int c2 = 0; c2 < 32; c2 += 16) {
-              const int t0 = ewg * 128 + c + c2;
-              const int left = rows - t0;
-              float* orow = static_cast<float*>(a.out) + (size_t)(row0 + t0) * a.out_ld + ch;
-              float v[16];
-#pragma unroll
-              for (int i = 0; i < 16; ++i) {  // routing weights of the chunk's rows (clamped index)
-                const float wr = a.row_weight ? __ldg(a.row_weight + row0 + t0 + min(i, max(left - 1, 0))) : 1.f;
-                v[i] = tot[c + c2 + i] * wr;
-              }
-              if (left >= 16) {
-#pragma unroll
-                for (int i = 0; i < 16; ++i) orow[(size_t)i * a.out_ld] = v[i];
-              } else {
-#pragma unroll
-                for (int i = 0; i < 16; ++i)
-                  if (i < left) orow[(size_t)i * a.out_ld] = v[i];
-              }
+              for (int j = 0; j < 16; j += 4)
+                *reinterpret_cast<float4*>(orow + j) = make_float4(
+                    xb[(grp * 16 + j) * C::kXRow + tt] * wr, xb[(grp * 16 + j + 1) * C::kXRow + tt] * wr,
+                    xb[(grp * 16 + j + 2) * C::kXRow + tt] * wr, xb[(grp * 16 + j + 3) * C::kXRow + tt] * wr);
             }
           }
+          named_bar(1 + ewg, 128);
         }
       }
     }
