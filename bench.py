@@ -299,10 +299,10 @@ def ep_launches(cfg) -> int:
 
 def run_ep(args, wl, world: int, rank: int, local: int) -> None:
     """Expert-parallel layer over `world` GPUs: the workload's tokens split evenly over the
-    ranks (strong scaling), routed experts sharded, routed rows exchanged over NCCL (counts
-    first, then each token row to each rank that owns one of its experts, partial rows back).
-    The count exchange is read on the host inside every step, so the steps are not captured
-    in a CUDA graph."""
+    ranks (strong scaling), routed experts sharded, routed rows exchanged over NCCL (each token
+    row to each rank that owns one of its experts in fixed segments, partial rows back).  No
+    step waits on the host, so the K timed steps replay as one CUDA graph, NCCL calls included;
+    the graph is released before the communicator is destroyed."""
     import datetime
 
     import torch
@@ -336,10 +336,28 @@ def run_ep(args, wl, world: int, rank: int, local: int) -> None:
         ep.forward(x)
     torch.cuda.synchronize()
     K = args.steps
-    graph = None  # the step waits on the host for the exchanged counts: no graph capture
-    def timed_steps():
-        for _ in range(K):
+    graph = None
+    if args.graph in ("auto", "on"):
+        graph = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream(device=dev)
+        cap.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(cap):
             ep.forward(x)
+            torch.cuda.synchronize()
+            with torch.cuda.graph(graph, stream=cap):
+                for _ in range(K):
+                    ep.forward(x)
+        torch.cuda.current_stream().wait_stream(cap)
+        torch.cuda.synchronize()
+        dist.barrier()
+        graph.replay()
+        torch.cuda.synchronize()
+    def timed_steps():
+        if graph is not None:
+            graph.replay()
+        else:
+            for _ in range(K):
+                ep.forward(x)
 
     clocks = ClockSampler(local)
     t_soak = time.perf_counter()
@@ -398,6 +416,9 @@ def run_ep(args, wl, world: int, rank: int, local: int) -> None:
             "cuda_graph": graph is not None,
         }
         print(json.dumps(line), flush=True)
+    if graph is not None:
+        graph.reset()  # drop the captured NCCL work before the communicator goes
+        graph = None
     torch.cuda.synchronize()
     dist.barrier()
     ep.close()

@@ -6,16 +6,18 @@
 // between ranks; every rank sized its workspace for the same T_cap >= T_r).  One forward:
 //   1. route the local tokens against the global router (ids are global expert indices);
 //   2. plan (ep_plan_kernel, one CTA per destination d): the local tokens with at least one
-//      expert on d, in token order; each is packed ONCE into d's segment of the send buffer
-//      (bf16 row, its k ids made local to d with -1 for other ranks' experts, its k routing
-//      weights), and send_pos[t, d] keeps the row's place for the way back;
-//   3. count exchange: one int per (source, destination) pair, grouped ncclSend / ncclRecv,
-//      copied to the host (a bounded wait): the sizes of the row exchange;
-//   4. dispatch: grouped ncclSend / ncclRecv of each segment; the rows from source s are
-//      packed at receive offset sum_{s' < s} recv_cnt[s'];
+//      expert on d, in token order; each gets ONE row in d's segment of the send buffers (its
+//      k ids made local to d with -1 for other ranks' experts, its k routing weights, its
+//      token), and send_pos[t, d] keeps the row's place for the way back; then
+//      ep_gather_kernel (a full grid) copies the bf16 token rows into those places;
+//   3. dispatch: grouped ncclSend / ncclRecv of each destination's segment, T_cap rows (the rows
+//      past the segment's count carry ids -1 and take no expert), received at s * T_cap for
+//      source s.  The segments have a size the host knows, so no count travels to the host and
+//      the step never waits on it (the unused tail of a segment crosses the link as well: at
+//      small rank counts nearly every token goes to every rank, at 8 ranks about 2/3 of them);
 //   5. the received rows through this rank's experts: permute by local expert (a -1 id takes
 //      no row), grouped FFN, per-row weighted sum over the row's k slots in slot order (fp32);
-//   6. return: each source's partial rows sent back to it, received in its send order;
+//   6. return: each source's segment of partial rows sent back to it, in its send order;
 //   7. out[t] = sum over destinations d = 0..P-1 of the partial row of (t, d), in that fixed
 //      order, plus the shared experts, which run data-parallel on the local tokens on a second
 //      stream meanwhile.
@@ -38,8 +40,7 @@ struct ccut_ep {
   int world;
   double timeout_s;
   cudaStream_t side;  // shared experts run here, beside the exchange
-  cudaEvent_t fork, join, counted;
-  int* h_counts;  // pinned host: [world] rows sent to, [world] rows received from each rank (last dispatch)
+  cudaEvent_t fork, join;
 };
 
 namespace ccut {
@@ -68,20 +69,19 @@ __host__ __device__ inline int ep_lo(int E, int world, int d) {
 }
 
 // One CTA per destination rank d: the local tokens with an expert on d, in token order
-// (block-wide scan of the flags, 1024 tokens per round), packed into d's segment of the send
-// buffers; send_pos[t * world + d] = the row's index in the send buffers, or -1.
-__global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(const uint16_t* __restrict__ x,
-                                                               const int32_t* __restrict__ ids,
-                                                               const float* __restrict__ w, int T, int k, int H,
-                                                               int E, int world, int seg, int* __restrict__ send_cnt,
+// (block-wide scan of the flags, 1024 tokens per round), each given a row of d's segment of
+// the send buffers; send_pos[t * world + d] = the row's index in the send buffers, or -1, and
+// send_tok[row] = t.
+__global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(const int32_t* __restrict__ ids,
+                                                               const float* __restrict__ w, int T, int k, int E,
+                                                               int world, int seg, int* __restrict__ send_cnt,
                                                                int32_t* __restrict__ send_pos,
-                                                               uint16_t* __restrict__ x_send,
+                                                               int32_t* __restrict__ send_tok,
                                                                int32_t* __restrict__ ids_send,
                                                                float* __restrict__ w_send) {
   pdl_wait();
   pdl_trigger();
   __shared__ int wsum[kPlanThreads / 32];
-  __shared__ int tok[kPlanThreads];
   __shared__ int s_total;
   const int d = blockIdx.x, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int lo = ep_lo(E, world, d), hi = ep_lo(E, world, d + 1);
@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(const uint16_t* _
     const int pos = wsum[wid] + __popc(bal & ((1u << lane) - 1u));
     if (flag) {
       const int row = d * seg + carry + pos;
-      tok[pos] = t;
+      send_tok[row] = t;
       send_pos[(size_t)t * world + d] = row;
       for (int j = 0; j < k; ++j) {
         const int e = ids[(size_t)t * k + j];
@@ -122,19 +122,34 @@ __global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(const uint16_t* _
     } else if (t < T) {
       send_pos[(size_t)t * world + d] = -1;
     }
-    __syncthreads();
-    const int n = s_total;
-    // rows of this round: one warp per row, 16-byte lanes
-    const int per_row = H / 8;
-    for (int i = wid; i < n; i += kPlanThreads / 32) {
-      const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)tok[i] * H);
-      uint4* dst = reinterpret_cast<uint4*>(x_send + (size_t)(d * seg + carry + i) * H);
-      for (int c = lane; c < per_row; c += 32) dst[c] = src[c];
-    }
-    carry += n;
+    carry += s_total;
     __syncthreads();
   }
+  // the segment's rows past its count take no expert on the receiving rank
+  for (int row = carry + tid; row < seg; row += kPlanThreads)
+    for (int j = 0; j < k; ++j) {
+      ids_send[((size_t)d * seg + row) * k + j] = -1;
+      w_send[((size_t)d * seg + row) * k + j] = 0.f;
+    }
   if (tid == 0) send_cnt[d] = carry;
+}
+
+// x_send[row] = x[send_tok[row]] for the first send_cnt[d] rows of every destination's segment
+// (seg rows each), 16 bytes per thread, grid-stride.
+__global__ void __launch_bounds__(256) ep_gather_kernel(const uint16_t* __restrict__ x,
+                                                        const int32_t* __restrict__ send_tok,
+                                                        const int* __restrict__ send_cnt, int world, int seg, int H,
+                                                        uint16_t* __restrict__ x_send) {
+  pdl_wait();
+  pdl_trigger();
+  const int per_row = H / 8;
+  const size_t total = (size_t)world * seg * per_row;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int row = static_cast<int>(i / per_row), c = static_cast<int>(i % per_row);
+    if (row % seg >= send_cnt[row / seg]) continue;
+    reinterpret_cast<uint4*>(x_send + (size_t)row * H)[c] =
+        reinterpret_cast<const uint4*>(x + (size_t)send_tok[row] * H)[c];
+  }
 }
 
 // out[t] = sum_{d = 0..world-1} back[send_pos[t, d]] (rows that were sent) + shared[t], in that
@@ -210,8 +225,9 @@ ccut_moe_layer with_policy(ccut_moe_layer v, long per_expert) {
 // The exchange's own scratch (the plan of the last dispatch, kept for its combine).
 struct ExScratch {
   int* status;
-  int* cnt;          // [2 * world]: rows sent to each destination, rows received from each source
+  int* cnt;          // [world]: rows sent to each destination
   int32_t* send_pos;  // [T_cap, world]
+  int32_t* send_tok;  // [world * T_cap] local token of each send row
   uint16_t* x_send;   // [world * T_cap, H]
   int32_t* ids_send;  // [world * T_cap, k]
   float* w_send;      // [world * T_cap, k]
@@ -222,8 +238,9 @@ ExScratch carve_ex(Carver& c, int world, int T_cap, int H, int k) {
   ExScratch s{};
   const size_t rows = (size_t)world * T_cap;
   s.status = c.take<int>(64);
-  s.cnt = c.take<int>(2 * (size_t)world);
+  s.cnt = c.take<int>((size_t)world);
   s.send_pos = c.take<int32_t>((size_t)T_cap * world);
+  s.send_tok = c.take<int32_t>(rows);
   s.x_send = c.take<uint16_t>(rows * H);
   s.ids_send = c.take<int32_t>(rows * k);
   s.w_send = c.take<float>(rows * k);
@@ -305,97 +322,49 @@ EpScratch carve_ep(Carver& c, const ccut_moe_layer* L, int E_global, int world, 
 
 int check_ep(const ccut_ep* ep) {
   if (!ep || ep->world < 1 || ep->world > kMaxWorld || ep->rank < 0 || ep->rank >= ep->world) return CCUT_ERR_INVALID;
-  if (!ep->comm) return CCUT_ERR_NCCL;  // aborted after an expired wait
+  if (!ep->comm) return CCUT_ERR_NCCL;
   return CCUT_OK;
 }
 
-// The communicator is aborted after an expired host wait: its streams may hold operations that
-// wait for a peer that never came, and only an abort releases them.
-int ep_fail(ccut_ep* ep, int rc) {
-  if (rc == CCUT_ERR_TIMEOUT && ep->comm) {
-    ncclCommAbort(ep->comm);
-    ep->comm = nullptr;
-  }
-  return rc;
-}
-
-// Steps 2-4: plan, count exchange (host-visible), row exchange.  Returns the received row
-// count in *recv_rows.  ids are global expert ids [T_l, k].
+// Steps 2-3: plan and row exchange.  The received rows land in segments of T_cap rows per
+// source rank (x_recv, ids_recv, w_recv: world * T_cap rows).  ids are global expert ids
+// [T_l, k].
 int ep_dispatch(ccut_ep* ep, const uint16_t* x, const int32_t* ids, const float* w, int T_l, int T_cap, int H, int k,
-                int E, const ExScratch& s, uint16_t* x_recv, int32_t* ids_recv, float* w_recv, int recv_capacity,
-                int* recv_rows, cudaStream_t st) {
+                int E, const ExScratch& s, uint16_t* x_recv, int32_t* ids_recv, float* w_recv, cudaStream_t st) {
   const int P = ep->world;
-  int* send_cnt = s.cnt;
-  int* recv_cnt = s.cnt + P;
+  int rc = launch_k(ep_plan_kernel, dim3(P), dim3(kPlanThreads), 0, st, ids, w, T_l, k, E, P, T_cap, s.cnt,
+                    s.send_pos, s.send_tok, s.ids_send, s.w_send);
+  if (rc) return rc;
   if (T_l > 0) {
-    int rc = launch_k(ep_plan_kernel, dim3(P), dim3(kPlanThreads), 0, st, x, ids, w, T_l, k, H, E, P, T_cap, send_cnt,
-                      s.send_pos, s.x_send, s.ids_send, s.w_send);
+    size_t blocks = ((size_t)P * T_cap * (H / 8) + 255) / 256;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    rc = launch_k(ep_gather_kernel, dim3(static_cast<unsigned>(blocks < 1 ? 1 : blocks)), dim3(256), 0, st, x,
+                  (const int32_t*)s.send_tok, (const int*)s.cnt, P, T_cap, H, s.x_send);
     if (rc) return rc;
-  } else if (cudaMemsetAsync(send_cnt, 0, sizeof(int) * P, st) != cudaSuccess) {
-    return CCUT_ERR_CUDA;
   }
-  // count exchange
+  if (T_cap == 0) return CCUT_OK;
   if (ncclGroupStart() != ncclSuccess) return CCUT_ERR_NCCL;
-  for (int d = 0; d < P; ++d) {
-    ncclSend(send_cnt + d, 1, ncclInt32, d, ep->comm, st);
-    ncclRecv(recv_cnt + d, 1, ncclInt32, d, ep->comm, st);
-  }
-  int rc = nccl_settle(ep->comm, ncclGroupEnd(), ep->timeout_s);
-  if (rc) return rc;
-  if (cudaMemcpyAsync(ep->h_counts, s.cnt, sizeof(int) * 2 * P, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
-      cudaEventRecord(ep->counted, st) != cudaSuccess)
-    return CCUT_ERR_CUDA;
-  const auto t0 = std::chrono::steady_clock::now();
-  for (;;) {  // bounded host wait: a missing peer ends here with a timeout, not a hang
-    const cudaError_t q = cudaEventQuery(ep->counted);
-    if (q == cudaSuccess) break;
-    if (q != cudaErrorNotReady) return CCUT_ERR_CUDA;
-    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > ep->timeout_s)
-      return ep_fail(ep, CCUT_ERR_TIMEOUT);
-    std::this_thread::yield();
-  }
-  const int* hs = ep->h_counts;
-  const int* hr = ep->h_counts + P;
-  long total = 0;
   for (int p = 0; p < P; ++p) {
-    if (hs[p] < 0 || hs[p] > T_l || hr[p] < 0) return CCUT_ERR_INVALID;
-    total += hr[p];
+    const size_t r0 = (size_t)p * T_cap;
+    ncclSend(s.x_send + r0 * H, (size_t)T_cap * H * 2, ncclUint8, p, ep->comm, st);
+    ncclSend(s.ids_send + r0 * k, (size_t)T_cap * k, ncclInt32, p, ep->comm, st);
+    ncclSend(s.w_send + r0 * k, (size_t)T_cap * k, ncclFloat32, p, ep->comm, st);
+    ncclRecv(x_recv + r0 * H, (size_t)T_cap * H * 2, ncclUint8, p, ep->comm, st);
+    ncclRecv(ids_recv + r0 * k, (size_t)T_cap * k, ncclInt32, p, ep->comm, st);
+    ncclRecv(w_recv + r0 * k, (size_t)T_cap * k, ncclFloat32, p, ep->comm, st);
   }
-  if (total > recv_capacity) return CCUT_ERR_WORKSPACE;
-  // row exchange
-  if (ncclGroupStart() != ncclSuccess) return CCUT_ERR_NCCL;
-  long roff = 0;
-  for (int p = 0; p < P; ++p) {
-    if (hs[p] > 0) {
-      const size_t r0 = (size_t)p * T_cap;
-      ncclSend(s.x_send + r0 * H, (size_t)hs[p] * H * 2, ncclUint8, p, ep->comm, st);
-      ncclSend(s.ids_send + r0 * k, (size_t)hs[p] * k, ncclInt32, p, ep->comm, st);
-      ncclSend(s.w_send + r0 * k, (size_t)hs[p] * k, ncclFloat32, p, ep->comm, st);
-    }
-    if (hr[p] > 0) {
-      ncclRecv(x_recv + (size_t)roff * H, (size_t)hr[p] * H * 2, ncclUint8, p, ep->comm, st);
-      ncclRecv(ids_recv + (size_t)roff * k, (size_t)hr[p] * k, ncclInt32, p, ep->comm, st);
-      ncclRecv(w_recv + (size_t)roff * k, (size_t)hr[p] * k, ncclFloat32, p, ep->comm, st);
-    }
-    roff += hr[p];
-  }
-  rc = nccl_settle(ep->comm, ncclGroupEnd(), ep->timeout_s);
-  if (rc) return rc;
-  *recv_rows = static_cast<int>(total);
-  return CCUT_OK;
+  return nccl_settle(ep->comm, ncclGroupEnd(), ep->timeout_s);
 }
 
-// Step 6: the partial rows y_recv [recv_rows, H] (fp32) back to their sources, into s.back.
+// Step 6: the partial rows y_recv [world * T_cap, H] (fp32) back to their sources, into s.back.
 int ep_return(ccut_ep* ep, const float* y_recv, int T_cap, int H, const ExScratch& s, cudaStream_t st) {
   const int P = ep->world;
-  const int* hs = ep->h_counts;
-  const int* hr = ep->h_counts + P;
+  if (T_cap == 0) return CCUT_OK;
   if (ncclGroupStart() != ncclSuccess) return CCUT_ERR_NCCL;
-  long roff = 0;
   for (int p = 0; p < P; ++p) {
-    if (hr[p] > 0) ncclSend(y_recv + (size_t)roff * H, (size_t)hr[p] * H, ncclFloat32, p, ep->comm, st);
-    if (hs[p] > 0) ncclRecv(s.back + (size_t)p * T_cap * H, (size_t)hs[p] * H, ncclFloat32, p, ep->comm, st);
-    roff += hr[p];
+    const size_t r0 = (size_t)p * T_cap;
+    ncclSend(y_recv + r0 * H, (size_t)T_cap * H, ncclFloat32, p, ep->comm, st);
+    ncclRecv(s.back + r0 * H, (size_t)T_cap * H, ncclFloat32, p, ep->comm, st);
   }
   return nccl_settle(ep->comm, ncclGroupEnd(), ep->timeout_s);
 }
@@ -439,21 +408,17 @@ int ccut_ep_init(const void* unique_id, int rank, int world, double timeout_s, c
     if (comm) ncclCommAbort(comm);
     return CCUT_ERR_NCCL;
   }
-  ccut_ep* ep = new (std::nothrow) ccut_ep{comm, rank, world, timeout_s, nullptr, nullptr, nullptr, nullptr, nullptr};
+  ccut_ep* ep = new (std::nothrow) ccut_ep{comm, rank, world, timeout_s, nullptr, nullptr, nullptr};
   if (!ep) {
     ncclCommAbort(comm);
     return CCUT_ERR_INVALID;
   }
   if (cudaStreamCreateWithFlags(&ep->side, cudaStreamNonBlocking) != cudaSuccess ||
       cudaEventCreateWithFlags(&ep->fork, cudaEventDisableTiming) != cudaSuccess ||
-      cudaEventCreateWithFlags(&ep->join, cudaEventDisableTiming) != cudaSuccess ||
-      cudaEventCreateWithFlags(&ep->counted, cudaEventDisableTiming) != cudaSuccess ||
-      cudaHostAlloc(reinterpret_cast<void**>(&ep->h_counts), sizeof(int) * 2 * world, cudaHostAllocDefault) !=
-          cudaSuccess) {
+      cudaEventCreateWithFlags(&ep->join, cudaEventDisableTiming) != cudaSuccess) {
     ccut_ep_destroy(ep);
     return CCUT_ERR_CUDA;
   }
-  std::memset(ep->h_counts, 0, sizeof(int) * 2 * world);
   *out = ep;
   return CCUT_OK;
 }
@@ -472,8 +437,6 @@ int ccut_ep_destroy(ccut_ep* ep) {
   if (ep->side) cudaStreamDestroy(ep->side);
   if (ep->fork) cudaEventDestroy(ep->fork);
   if (ep->join) cudaEventDestroy(ep->join);
-  if (ep->counted) cudaEventDestroy(ep->counted);
-  if (ep->h_counts) cudaFreeHost(ep->h_counts);
   delete ep;
   return rc;
 }
@@ -495,14 +458,17 @@ int ccut_moe_ep_dispatch(ccut_ep* ep, const uint16_t* x, const int32_t* ids, con
   if (T_local < 0 || T_local > T_cap || H <= 0 || H % 8 || k < 1 || k > kMaxTopK || !recv_rows ||
       num_experts_global < ep->world || num_experts_global > kMaxRoutedExperts || recv_capacity < 0)
     return CCUT_ERR_INVALID;
-  if ((T_local > 0 && (!x || !ids || !weights)) || (recv_capacity > 0 && (!x_recv || !ids_recv || !w_recv)) ||
+  if ((T_local > 0 && (!x || !ids || !weights)) || (T_cap > 0 && (!x_recv || !ids_recv || !w_recv)) ||
       !workspace)
     return CCUT_ERR_INVALID;
+  if ((long)recv_capacity < (long)ep->world * T_cap) return CCUT_ERR_WORKSPACE;
   if (ws_bytes < ccut_moe_ep_exchange_workspace_bytes(ep->world, T_cap, H, k)) return CCUT_ERR_WORKSPACE;
   Carver c(workspace);
   const ExScratch s = carve_ex(c, ep->world, T_cap, H, k);
-  return ep_dispatch(ep, x, ids, weights, T_local, T_cap, H, k, num_experts_global, s, x_recv, ids_recv, w_recv,
-                     recv_capacity, recv_rows, stream);
+  rc = ep_dispatch(ep, x, ids, weights, T_local, T_cap, H, k, num_experts_global, s, x_recv, ids_recv, w_recv,
+                   stream);
+  if (rc == CCUT_OK) *recv_rows = ep->world * T_cap;
+  return rc;
 }
 
 int ccut_moe_ep_combine(ccut_ep* ep, const float* y_recv, int T_local, int T_cap, int H, int k, float* y_local,
@@ -511,10 +477,7 @@ int ccut_moe_ep_combine(ccut_ep* ep, const float* y_recv, int T_local, int T_cap
   if (rc) return rc;
   PdlScope pdl_scope((long)T_local * ep->world);
   if (T_local < 0 || T_local > T_cap || H <= 0 || H % 8 || k < 1 || k > kMaxTopK) return CCUT_ERR_INVALID;
-  if ((T_local > 0 && !y_local) || !workspace) return CCUT_ERR_INVALID;
-  long recv = 0;
-  for (int p = 0; p < ep->world; ++p) recv += ep->h_counts[ep->world + p];
-  if (recv > 0 && !y_recv) return CCUT_ERR_INVALID;
+  if ((T_local > 0 && !y_local) || (T_cap > 0 && !y_recv) || !workspace) return CCUT_ERR_INVALID;
   if (ws_bytes < ccut_moe_ep_exchange_workspace_bytes(ep->world, T_cap, H, k)) return CCUT_ERR_WORKSPACE;
   Carver c(workspace);
   const ExScratch s = carve_ex(c, ep->world, T_cap, H, k);
@@ -591,10 +554,10 @@ int ccut_moe_ep_forward(ccut_ep* ep, const ccut_moe_layer* L, int expert_lo, int
                       s.counts_g, nullptr, st);
     if (rc) return rc;
   }
-  // 2-4. plan, counts, routed rows
-  int R = 0;
+  // 2-3. plan, routed rows
+  const int R = ep->world * T_cap;
   rc = ep_dispatch(ep, x, s.ids_l, s.w_l, T_local, T_cap, H, k, num_experts_global, s.ex, s.x_recv, s.ids_recv,
-                   s.w_recv, ep->world * T_cap, &R, st);
+                   s.w_recv, st);
   if (rc) return rc;
   // 5. received rows -> permutation -> grouped FFN over the local experts -> per-row sums
   if (R > 0) {

@@ -328,13 +328,13 @@ CCUT_API int ccut_debug_wait_expiry(void* workspace, long long budget_cycles, cc
 /* One process per GPU.  Rank r holds the routed experts [lo_r, hi_r) -- contiguous blocks of
  * E_global experts whose sizes differ by at most one, lo_r = r * (E/P) + min(r, E % P) -- and
  * every shared expert.  Ranks may carry different token counts T_local, all at most the
- * T_cap every rank sized its workspace for.  Only routed rows cross the links: a token row
- * goes once to each rank that owns one of its experts, and one fp32 partial row per
- * (token, rank) comes back.  ccut_ep_init is collective and returns once every rank has
- * joined: distribute the unique id through a channel with a timeout (e.g. a
- * torch.distributed broadcast) so that a missing rank fails there.  `timeout_s` bounds every
- * host wait of the handle; a wait that expires returns CCUT_ERR_TIMEOUT and aborts the
- * communicator (later calls return CCUT_ERR_NCCL: destroy the handle). */
+ * T_cap every rank sized its workspace for.  A token row goes once to each rank that owns one
+ * of its experts, and one fp32 partial row per (token, rank) comes back; the exchange moves
+ * fixed segments of T_cap rows per pair of ranks (rows past a segment's count carry ids -1),
+ * so that no count has to reach the host and a step never waits on it.  ccut_ep_init is
+ * collective and returns once every rank has joined: distribute the unique id through a
+ * channel with a timeout (e.g. a torch.distributed broadcast) so that a missing rank fails
+ * there.  `timeout_s` bounds the host waits of ccut_ep_destroy. */
 typedef struct ccut_ep ccut_ep;
 /* Size of the NCCL unique id (host bytes) that rank 0 creates and every rank passes to
  * ccut_ep_init. */
@@ -348,20 +348,21 @@ CCUT_API int ccut_ep_destroy(ccut_ep* ep);
 CCUT_API size_t ccut_moe_ep_exchange_workspace_bytes(int world, int T_cap, int H, int k);
 /* Dispatch: the local tokens x bf16 [T_local, H] with their routing ids int32 [T_local, k]
  * (global expert ids) and weights fp32 [T_local, k] go to the ranks that own their experts.
- * Counts are exchanged first (grouped ncclSend / ncclRecv of one int per pair of ranks, read
- * back on the host: this call waits for them), then the rows.  Received rows are packed by
- * source rank (rank 0's first), each with its k ids made local to this rank (-1 for experts
- * elsewhere) and its k weights: x_recv bf16 [*recv_rows, H], ids_recv int32 [*recv_rows, k],
- * w_recv fp32 [*recv_rows, k]; *recv_rows (host int) <= recv_capacity, else
- * CCUT_ERR_WORKSPACE.  Collective: every rank calls it, also with T_local = 0. */
+ * Received rows land in one segment of T_cap rows per source rank (rank s at s * T_cap), in
+ * the source's token order, each with its k ids made local to this rank (-1 for experts
+ * elsewhere) and its k weights; rows past what a source sent carry ids -1:
+ * x_recv bf16 [world * T_cap, H], ids_recv int32 [world * T_cap, k], w_recv fp32
+ * [world * T_cap, k]; *recv_rows (host int) = world * T_cap, which recv_capacity must reach
+ * (else CCUT_ERR_WORKSPACE).  Collective: every rank calls it, also with T_local = 0. */
 CCUT_API int ccut_moe_ep_dispatch(ccut_ep* ep, const uint16_t* x, const int32_t* ids, const float* weights,
                                   int T_local, int T_cap, int H, int k, int num_experts_global, uint16_t* x_recv,
                                   int32_t* ids_recv, float* w_recv, int recv_capacity, int* recv_rows,
                                   void* workspace, size_t ws_bytes, ccut_stream_t stream);
-/* Combine: y_recv fp32 [recv_rows, H], one partial output per row the last dispatch on this
- * handle received (in its order), goes back to the row's source; y_local fp32 [T_local, H] =
- * for each local token the sum of its partial rows in rank order (0 for a token routed to no
- * expert).  Same workspace as that dispatch.  Collective. */
+/* Combine: y_recv fp32 [world * T_cap, H], one partial output per row the last dispatch on
+ * this workspace received (in its order; rows with no local expert are ignored by their
+ * source), goes back to the row's source; y_local fp32 [T_local, H] = for each local token the
+ * sum of its partial rows in rank order (0 for a token routed to no expert).  Same workspace
+ * as that dispatch.  Collective. */
 CCUT_API int ccut_moe_ep_combine(ccut_ep* ep, const float* y_recv, int T_local, int T_cap, int H, int k,
                                  float* y_local, void* workspace, size_t ws_bytes, ccut_stream_t stream);
 /* Whole expert-parallel layer: route (against L->router, fp32 [E_global, H]), dispatch, the

@@ -100,14 +100,15 @@ def test_ep_dispatch_and_combine_world1():
                   C.byref(nrecv), p(ws), nb, s)
         torch.cuda.synchronize()
         sent = [t for t in range(T) if t != 2]
-        assert nrecv.value == len(sent)
+        assert nrecv.value == T  # one segment of T_cap rows from the one rank
         assert torch.equal(xr[:len(sent)], x[sent]) and torch.equal(ir[:len(sent)], ids[sent])
         assert torch.equal(wr[:len(sent)], w[sent])
-        y = torch.randn(len(sent), H, device="cuda")
+        assert (ir[len(sent):] == -1).all()  # the segment's unused row takes no expert
+        y = torch.randn(T, H, device="cuda")
         yl = torch.full((T, H), 7.0, device="cuda")
         _lib.call("ccut_moe_ep_combine", h, p(y), T, T, H, k, p(yl), p(ws), nb, s)
         torch.cuda.synchronize()
-        assert torch.equal(yl[sent], y) and torch.equal(yl[2], torch.zeros(H, device="cuda"))
+        assert torch.equal(yl[sent], y[:len(sent)]) and torch.equal(yl[2], torch.zeros(H, device="cuda"))
         with pytest.raises(ValueError):
             _lib.call("ccut_moe_ep_combine", h, p(y), -1, T, H, k, p(yl), p(ws), nb, s)
         with pytest.raises(ValueError):  # more tokens than the workspace was planned for
@@ -133,13 +134,15 @@ def _rank_main(rank, world, port, case, out):
         fmt, mode, E, k, shared, T, kernel = case
         cfg = small_cfg(fmt, mode, hidden=256, inter=128, experts=E, top_k=k, shared=shared)
         lw = inputs.make_layer(cfg, seed=33)
-        Tl = T // world
-        xb = lw.make_x(T)[rank * Tl:(rank + 1) * Tl]
-        ep = _ep_layer(lw, rank, world, kernel=kernel, device=f"cuda:{rank}", timeout_s=60.0)
+        counts = T if isinstance(T, tuple) else (T // world,) * world  # tokens per rank (may differ)
+        start = sum(counts[:rank])
+        xb = lw.make_x(sum(counts))[start:start + counts[rank]]
+        ep = _ep_layer(lw, rank, world, kernel=kernel, device=f"cuda:{rank}", timeout_s=60.0,
+                       max_tokens=max(counts))
         y = ep.forward(x_device(xb, f"cuda:{rank}"))
         torch.cuda.synchronize()
         status = ep.workspace_status()
-        err = _check_rank(lw, xb, y, kernel)
+        err = _check_rank(lw, xb, y, kernel) if counts[rank] else 0.0
         ep.close()
         out[rank] = (err, status)
     finally:
@@ -147,7 +150,11 @@ def _rank_main(rank, world, port, case, out):
 
 
 @pytest.mark.parametrize("case", [("fp8_b128", "softmax_topk", 8, 2, 2, 64, "tc"),
-                                  ("awq_int4_g128", "topk_softmax", 16, 4, 0, 32, "mma")])
+                                  ("awq_int4_g128", "topk_softmax", 16, 4, 0, 32, "mma"),
+                                  # ragged token counts; top-6 over 4 experts per rank
+                                  ("fp8_b128", "softmax_topk", 8, 6, 1, (40, 24), "tc"),
+                                  # a rank with no tokens still takes part in the exchange
+                                  ("awq_int4_g128", "topk_softmax", 16, 4, 1, (33, 0), "mma")])
 def test_ep_two_gpus(case):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
