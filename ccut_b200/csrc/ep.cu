@@ -17,7 +17,8 @@
 //      small rank counts nearly every token goes to every rank, at 8 ranks about 2/3 of them);
 //   5. the received rows through this rank's experts: permute by local expert (a -1 id takes
 //      no row), grouped FFN, per-row weighted sum over the row's k slots in slot order (fp32);
-//   6. return: each source's segment of partial rows sent back to it, in its send order;
+//   6. return: each source's segment of partial rows sent back to it as bf16 (one rounding of
+//      each partial sum, as the layer's bf16 output has), in its send order;
 //   7. out[t] = sum over destinations d = 0..P-1 of the partial row of (t, d), in that fixed
 //      order, plus the shared experts, which run data-parallel on the local tokens on a second
 //      stream meanwhile.
@@ -152,9 +153,9 @@ __global__ void __launch_bounds__(256) ep_gather_kernel(const uint16_t* __restri
   }
 }
 
-// out[t] = sum_{d = 0..world-1} back[send_pos[t, d]] (rows that were sent) + shared[t], in that
-// order, fp32 -> bf16 or fp32.  One CTA per (token, 1024-column chunk).
-__global__ void __launch_bounds__(256) ep_sum_kernel(const float* __restrict__ back, const int32_t* __restrict__ send_pos,
+// out[t] = sum_{d = 0..world-1} back[send_pos[t, d]] (bf16 rows that were sent) + shared[t],
+// in that order in fp32 -> bf16 or fp32.  One CTA per (token, 1024-column chunk).
+__global__ void __launch_bounds__(256) ep_sum_kernel(const uint16_t* __restrict__ back, const int32_t* __restrict__ send_pos,
                                                      const float* __restrict__ shared, int world, int H, void* out,
                                                      int out_dtype) {
   pdl_wait();
@@ -165,17 +166,17 @@ __global__ void __launch_bounds__(256) ep_sum_kernel(const float* __restrict__ b
   __syncthreads();
   const int h4n = H / 4, h4 = blockIdx.y * 256 + threadIdx.x;
   if (h4 >= h4n) return;
-  const float4* b4 = reinterpret_cast<const float4*>(back);
+  const uint2* b4 = reinterpret_cast<const uint2*>(back);
   float4 s = shared ? reinterpret_cast<const float4*>(shared)[(size_t)t * h4n + h4] : make_float4(0.f, 0.f, 0.f, 0.f);
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int d = 0; d < world; ++d) {
     const int r = rows[d];
     if (r >= 0) {
-      const float4 v = b4[(size_t)r * h4n + h4];
-      acc.x += v.x;
-      acc.y += v.y;
-      acc.z += v.z;
-      acc.w += v.w;
+      const uint2 v = b4[(size_t)r * h4n + h4];
+      acc.x += __uint_as_float(v.x << 16);
+      acc.y += __uint_as_float(v.x & 0xffff0000u);
+      acc.z += __uint_as_float(v.y << 16);
+      acc.w += __uint_as_float(v.y & 0xffff0000u);
     }
   }
   acc.x += s.x;
@@ -231,7 +232,7 @@ struct ExScratch {
   uint16_t* x_send;   // [world * T_cap, H]
   int32_t* ids_send;  // [world * T_cap, k]
   float* w_send;      // [world * T_cap, k]
-  float* back;        // [world * T_cap, H] partial outputs returned to this rank
+  uint16_t* back;     // [world * T_cap, H] bf16 partial outputs returned to this rank
 };
 
 ExScratch carve_ex(Carver& c, int world, int T_cap, int H, int k) {
@@ -244,7 +245,7 @@ ExScratch carve_ex(Carver& c, int world, int T_cap, int H, int k) {
   s.x_send = c.take<uint16_t>(rows * H);
   s.ids_send = c.take<int32_t>(rows * k);
   s.w_send = c.take<float>(rows * k);
-  s.back = c.take<float>(rows * H);
+  s.back = c.take<uint16_t>(rows * H);
   return s;
 }
 
@@ -266,7 +267,7 @@ struct EpScratch {
   int32_t* pair_row;
   FfnScratch ffn;
   float* ybuf;
-  float* y_recv;
+  uint16_t* y_recv;  // bf16 partial output per received row
   // shared experts
   int32_t* sh_ids;
   float* sh_w;
@@ -302,7 +303,7 @@ EpScratch carve_ep(Carver& c, const ccut_moe_layer* L, int E_global, int world, 
   s.pair_row = c.take<int32_t>((size_t)R * k);
   s.ffn = carve_ffn(c, &rv, R, k, true, s.sched);
   s.ybuf = c.take<float>((size_t)R * k * H);
-  s.y_recv = c.take<float>((size_t)R * H);
+  s.y_recv = c.take<uint16_t>((size_t)R * H);
   if (S > 0) {
     const ccut_moe_layer sv = shared_view(L);
     const size_t Rs = (size_t)(S + 1) * T_cap;
@@ -356,15 +357,15 @@ int ep_dispatch(ccut_ep* ep, const uint16_t* x, const int32_t* ids, const float*
   return nccl_settle(ep->comm, ncclGroupEnd(), ep->timeout_s);
 }
 
-// Step 6: the partial rows y_recv [world * T_cap, H] (fp32) back to their sources, into s.back.
-int ep_return(ccut_ep* ep, const float* y_recv, int T_cap, int H, const ExScratch& s, cudaStream_t st) {
+// Step 6: the partial rows y_recv [world * T_cap, H] (bf16) back to their sources, into s.back.
+int ep_return(ccut_ep* ep, const uint16_t* y_recv, int T_cap, int H, const ExScratch& s, cudaStream_t st) {
   const int P = ep->world;
   if (T_cap == 0) return CCUT_OK;
   if (ncclGroupStart() != ncclSuccess) return CCUT_ERR_NCCL;
   for (int p = 0; p < P; ++p) {
     const size_t r0 = (size_t)p * T_cap;
-    ncclSend(y_recv + r0 * H, (size_t)T_cap * H, ncclFloat32, p, ep->comm, st);
-    ncclRecv(s.back + r0 * H, (size_t)T_cap * H, ncclFloat32, p, ep->comm, st);
+    ncclSend(y_recv + r0 * H, (size_t)T_cap * H, ncclBfloat16, p, ep->comm, st);
+    ncclRecv(s.back + r0 * H, (size_t)T_cap * H, ncclBfloat16, p, ep->comm, st);
   }
   return nccl_settle(ep->comm, ncclGroupEnd(), ep->timeout_s);
 }
@@ -373,7 +374,7 @@ int launch_ep_sum(const ExScratch& s, const float* shared, int T_l, int world, i
                   cudaStream_t st) {
   if (T_l == 0) return CCUT_OK;
   const dim3 grid(T_l, (H / 4 + 255) / 256);
-  return launch_k(ep_sum_kernel, grid, dim3(256), 0, st, (const float*)s.back, (const int32_t*)s.send_pos, shared,
+  return launch_k(ep_sum_kernel, grid, dim3(256), 0, st, (const uint16_t*)s.back, (const int32_t*)s.send_pos, shared,
                   world, H, out, out_dtype);
 }
 
@@ -471,7 +472,7 @@ int ccut_moe_ep_dispatch(ccut_ep* ep, const uint16_t* x, const int32_t* ids, con
   return rc;
 }
 
-int ccut_moe_ep_combine(ccut_ep* ep, const float* y_recv, int T_local, int T_cap, int H, int k, float* y_local,
+int ccut_moe_ep_combine(ccut_ep* ep, const uint16_t* y_recv, int T_local, int T_cap, int H, int k, float* y_local,
                         void* workspace, size_t ws_bytes, ccut_stream_t stream) {
   int rc = check_ep(ep);
   if (rc) return rc;
@@ -575,7 +576,7 @@ int ccut_moe_ep_forward(ccut_ep* ep, const ccut_moe_layer* L, int expert_lo, int
     }
     rc = run_ffn(&rv, per_expert, s.x_recv, s.ffn, R, k, s.offsets, s.row_token, s.row_weight, s.ybuf, status, st);
     if (rc) return rc;
-    rc = launch_combine(s.ybuf, s.pair_row, R, k, H, 0, -1, s.y_recv, CCUT_OUT_F32, st);
+    rc = launch_combine(s.ybuf, s.pair_row, R, k, H, 0, -1, s.y_recv, CCUT_OUT_BF16, st);
     if (rc) return rc;
   }
   // 6. partial rows back to their owners

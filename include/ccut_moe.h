@@ -330,7 +330,8 @@ CCUT_API int ccut_debug_wait_expiry(void* workspace, long long budget_cycles, cc
  * every shared expert.  Ranks may carry different token counts T_local, all at most the
  * T_cap every rank sized its workspace for.  A token row goes once to each rank that owns one
  * of its experts, and one fp32 partial row per (token, rank) comes back; the exchange moves
- * fixed segments of T_cap rows per pair of ranks (rows past a segment's count carry ids -1),
+ * fixed segments of T_cap rows per pair of ranks (rows past a segment's count carry ids -1;
+ * partial rows travel as bf16, one rounding of each, as the layer's bf16 output has),
  * so that no count has to reach the host and a step never waits on it.  ccut_ep_init is
  * collective and returns once every rank has joined: distribute the unique id through a
  * channel with a timeout (e.g. a torch.distributed broadcast) so that a missing rank fails
@@ -358,12 +359,12 @@ CCUT_API int ccut_moe_ep_dispatch(ccut_ep* ep, const uint16_t* x, const int32_t*
                                   int T_local, int T_cap, int H, int k, int num_experts_global, uint16_t* x_recv,
                                   int32_t* ids_recv, float* w_recv, int recv_capacity, int* recv_rows,
                                   void* workspace, size_t ws_bytes, ccut_stream_t stream);
-/* Combine: y_recv fp32 [world * T_cap, H], one partial output per row the last dispatch on
+/* Combine: y_recv bf16 [world * T_cap, H], one partial output per row the last dispatch on
  * this workspace received (in its order; rows with no local expert are ignored by their
  * source), goes back to the row's source; y_local fp32 [T_local, H] = for each local token the
- * sum of its partial rows in rank order (0 for a token routed to no expert).  Same workspace
- * as that dispatch.  Collective. */
-CCUT_API int ccut_moe_ep_combine(ccut_ep* ep, const float* y_recv, int T_local, int T_cap, int H, int k,
+ * fp32 sum of its partial rows in rank order (0 for a token routed to no expert).  Same
+ * workspace as that dispatch.  Collective. */
+CCUT_API int ccut_moe_ep_combine(ccut_ep* ep, const uint16_t* y_recv, int T_local, int T_cap, int H, int k,
                                  float* y_local, void* workspace, size_t ws_bytes, ccut_stream_t stream);
 /* Whole expert-parallel layer: route (against L->router, fp32 [E_global, H]), dispatch, the
  * received rows through the local grouped FFN, combine, shared experts (on a second stream,

@@ -104,11 +104,11 @@ def test_ep_dispatch_and_combine_world1():
         assert torch.equal(xr[:len(sent)], x[sent]) and torch.equal(ir[:len(sent)], ids[sent])
         assert torch.equal(wr[:len(sent)], w[sent])
         assert (ir[len(sent):] == -1).all()  # the segment's unused row takes no expert
-        y = torch.randn(T, H, device="cuda")
+        y = torch.randn(T, H, device="cuda").to(torch.bfloat16)
         yl = torch.full((T, H), 7.0, device="cuda")
         _lib.call("ccut_moe_ep_combine", h, p(y), T, T, H, k, p(yl), p(ws), nb, s)
         torch.cuda.synchronize()
-        assert torch.equal(yl[sent], y[:len(sent)]) and torch.equal(yl[2], torch.zeros(H, device="cuda"))
+        assert torch.equal(yl[sent], y[:len(sent)].float()) and torch.equal(yl[2], torch.zeros(H, device="cuda"))
         with pytest.raises(ValueError):
             _lib.call("ccut_moe_ep_combine", h, p(y), -1, T, H, k, p(yl), p(ws), nb, s)
         with pytest.raises(ValueError):  # more tokens than the workspace was planned for
