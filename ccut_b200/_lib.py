@@ -17,13 +17,14 @@ _PKG = Path(__file__).resolve().parent
 LIB_PATH = Path(os.environ.get("CCUT_B200_LIB", _PKG / "_build" / "libccut_moe.so"))
 
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE, ERR_TIMEOUT, ERR_NCCL = range(7)
-FMT_AWQ_INT4_G128, FMT_FP8_E4M3_B128 = 1, 2
+FMT_AWQ_INT4_G128, FMT_FP8_E4M3_B128, FMT_FP8_E4M3_CH, FMT_INT4_SYM_G128 = 1, 2, 3, 4
 NIBBLES_AWQ, NIBBLES_SEQUENTIAL = 0, 1
 LAYOUT_ROWS, LAYOUT_FRAGS = 0, 1
 ROUTE_SOFTMAX_TOPK, ROUTE_TOPK_SOFTMAX, ROUTE_SIGMOID_GROUP = 0, 1, 2
 OUT_BF16, OUT_F32 = 0, 1
 
-FORMATS = {"awq_int4_g128": FMT_AWQ_INT4_G128, "fp8_b128": FMT_FP8_E4M3_B128}
+FORMATS = {"awq_int4_g128": FMT_AWQ_INT4_G128, "fp8_b128": FMT_FP8_E4M3_B128, "fp8_channel": FMT_FP8_E4M3_CH,
+           "int4_sym_g128": FMT_INT4_SYM_G128}
 LAYOUTS = {"rows": LAYOUT_ROWS, "frags": LAYOUT_FRAGS}
 KERNEL_AUTO, KERNEL_TC, KERNEL_MMA = 0, 1, 2
 KERNELS = {"auto": KERNEL_AUTO, "tc": KERNEL_TC, "mma": KERNEL_MMA}
@@ -66,6 +67,7 @@ SIGNATURES: dict[str, tuple] = {
     "ccut_moe_expert_ffn": (_i, [C.POINTER(MoeLayerDesc), _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "ccut_moe_expert_ffn_w4a16": (_i, [C.POINTER(MoeLayerDesc), _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "ccut_moe_expert_ffn_fp8b128": (_i, [C.POINTER(MoeLayerDesc), _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "ccut_moe_expert_ffn_w8a16": (_i, [C.POINTER(MoeLayerDesc), _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "ccut_gate_up_workspace_bytes": (_sz, [C.POINTER(MoeLayerDesc), _i]),
     "ccut_down_workspace_bytes": (_sz, [C.POINTER(MoeLayerDesc)]),
     "ccut_moe_gate_up": (_i, [C.POINTER(MoeLayerDesc), _vp, _i, _i, _vp, _vp, _vp, _vp, _sz, _vp]),

@@ -31,7 +31,10 @@ bool pdl_enabled() {
   return on;
 }
 
-bool valid_fmt(int f) { return f == CCUT_FMT_AWQ_INT4_G128 || f == CCUT_FMT_FP8_E4M3_B128; }
+bool valid_fmt(int f) {
+  return f == CCUT_FMT_AWQ_INT4_G128 || f == CCUT_FMT_FP8_E4M3_B128 || f == CCUT_FMT_FP8_E4M3_CH ||
+         f == CCUT_FMT_INT4_SYM_G128;
+}
 
 int check_layer(const ccut_moe_layer* L) {
   if (!L) return CCUT_ERR_INVALID;
@@ -285,10 +288,10 @@ int ccut_pack_matrix(int format, int layout, const void* q, const void* z, const
   if (layout != CCUT_LAYOUT_ROWS && layout != CCUT_LAYOUT_FRAGS) return CCUT_ERR_UNSUPPORTED;
   if (!q || !s || !dst || K <= 0 || N <= 0 || K % 128 || N % 128) return CCUT_ERR_INVALID;
   if (nmat < 1 || nmat > 2 || slot < 0 || slot >= nmat) return CCUT_ERR_INVALID;
-  if (format == CCUT_FMT_AWQ_INT4_G128) {
-    if (!z) return CCUT_ERR_INVALID;
-    if (nibble_order != CCUT_NIBBLES_AWQ && nibble_order != CCUT_NIBBLES_SEQUENTIAL) return CCUT_ERR_INVALID;
-  }
+  if (format == CCUT_FMT_AWQ_INT4_G128 && !z) return CCUT_ERR_INVALID;
+  if ((format == CCUT_FMT_AWQ_INT4_G128 || format == CCUT_FMT_INT4_SYM_G128) &&
+      nibble_order != CCUT_NIBBLES_AWQ && nibble_order != CCUT_NIBBLES_SEQUENTIAL)
+    return CCUT_ERR_INVALID;
   return launch_pack(format, layout, q, z, s, K, N, nibble_order, dst, nmat, slot, stream);
 }
 
@@ -395,7 +398,7 @@ int ccut_moe_expert_ffn(const ccut_moe_layer* L, const uint16_t* x, int T, int k
 int ccut_moe_expert_ffn_w4a16(const ccut_moe_layer* L, const uint16_t* x, int T, int k, const int32_t* offsets,
                               const int32_t* row_token, const float* row_weight, float* y_rows, void* workspace,
                               size_t ws_bytes, ccut_stream_t stream) {
-  if (!L || L->format != CCUT_FMT_AWQ_INT4_G128) return CCUT_ERR_UNSUPPORTED;
+  if (!L || (L->format != CCUT_FMT_AWQ_INT4_G128 && L->format != CCUT_FMT_INT4_SYM_G128)) return CCUT_ERR_UNSUPPORTED;
   return ccut_moe_expert_ffn(L, x, T, k, offsets, row_token, row_weight, y_rows, workspace, ws_bytes, stream);
 }
 
@@ -403,6 +406,13 @@ int ccut_moe_expert_ffn_fp8b128(const ccut_moe_layer* L, const uint16_t* x, int 
                                 const int32_t* row_token, const float* row_weight, float* y_rows, void* workspace,
                                 size_t ws_bytes, ccut_stream_t stream) {
   if (!L || L->format != CCUT_FMT_FP8_E4M3_B128) return CCUT_ERR_UNSUPPORTED;
+  return ccut_moe_expert_ffn(L, x, T, k, offsets, row_token, row_weight, y_rows, workspace, ws_bytes, stream);
+}
+
+int ccut_moe_expert_ffn_w8a16(const ccut_moe_layer* L, const uint16_t* x, int T, int k, const int32_t* offsets,
+                              const int32_t* row_token, const float* row_weight, float* y_rows, void* workspace,
+                              size_t ws_bytes, ccut_stream_t stream) {
+  if (!L || L->format != CCUT_FMT_FP8_E4M3_CH) return CCUT_ERR_UNSUPPORTED;
   return ccut_moe_expert_ffn(L, x, T, k, offsets, row_token, row_weight, y_rows, workspace, ws_bytes, stream);
 }
 

@@ -31,7 +31,7 @@ struct GemmCfg {
   static constexpr int kNMat = MODE == kFfn1 ? 2 : 1;
   // AWQ down blocks are half the size of the other stages: stage two 128-k groups at once so
   // that the per-stage work (barriers, scales, partial promotion) covers as many bytes
-  static constexpr int kKG = (FMT == CCUT_FMT_AWQ_INT4_G128 && MODE == kFfn2) ? 2 : 1;
+  static constexpr int kKG = (B::kInt4 && MODE == kFfn2) ? 2 : 1;
   static constexpr int kNBlk = kNMat * kKG;  // packed blocks per stage (slots)
   static constexpr int kStageK = kTileK * kKG;
   static constexpr int kWBytes = kNBlk * B::kBytes;
@@ -108,14 +108,24 @@ __device__ __forceinline__ bool consume_item(const GemmArgs& a, uint8_t* stages,
 #pragma unroll
     for (int m = 0; m < Q; ++m) {
       const uint8_t* blk = st + (m < nq ? m : 0) * B::kBytes;
-      if constexpr (FMT == CCUT_FMT_AWQ_INT4_G128) {
+      if constexpr (B::kScale == kScaleF16Row) {
         const uint16_t* sc = reinterpret_cast<const uint16_t*>(blk + B::kScaleOff);
         sc_lo[m] = __half2float(__ushort_as_half(sc[ch_lo]));
         sc_hi[m] = __half2float(__ushort_as_half(sc[ch_hi]));
-        zp_lo[m] = zero_pair_f16_1024(blk[B::kZeroOff + (ch_lo >> 1)] >> (4 * (ch_lo & 1)));
-        zp_hi[m] = zero_pair_f16_neg64(blk[B::kZeroOff + (ch_hi >> 1)] >> (4 * (ch_hi & 1)));
+      } else if constexpr (B::kScale == kScaleF32Row) {
+        const float* sc = reinterpret_cast<const float*>(blk + B::kScaleOff);
+        sc_lo[m] = sc[ch_lo];
+        sc_hi[m] = sc[ch_hi];
       } else {
         sc_lo[m] = sc_hi[m] = reinterpret_cast<const float*>(blk + B::kScaleOff)[0];
+      }
+      if constexpr (B::kZeros) {
+        zp_lo[m] = zero_pair_f16_1024(blk[B::kZeroOff + (ch_lo >> 1)] >> (4 * (ch_lo & 1)));
+        zp_hi[m] = zero_pair_f16_neg64(blk[B::kZeroOff + (ch_hi >> 1)] >> (4 * (ch_hi & 1)));
+      } else if constexpr (B::kInt4) {  // zero point 8
+        zp_lo[m] = zero_pair_f16_1024(8);
+        zp_hi[m] = zero_pair_f16_neg64(8);
+      } else {
         zp_lo[m] = zp_hi[m] = 0;
       }
     }
@@ -132,7 +142,7 @@ __device__ __forceinline__ bool consume_item(const GemmArgs& a, uint8_t* stages,
         uint32_t af[Q][4];
 #pragma unroll
         for (int m = 0; m < Q; ++m) {
-          if constexpr (FMT == CCUT_FMT_AWQ_INT4_G128) {
+          if constexpr (B::kInt4) {
             const uint32_t wd = j == 0 ? raw[m].x : j == 1 ? raw[m].y : j == 2 ? raw[m].z : raw[m].w;
             // a0/a2: channel ch_lo (nibbles 0,4 / 2,6); a1/a3: ch_hi (nibbles 1,5 / 3,7)
             af[m][0] = nib_lo_to_f16x2_minus(wd, zp_lo[m]);
@@ -400,11 +410,20 @@ static int launch_gemm_mt(int mt, const GemmArgs& a, int num_sms, cudaStream_t s
 // Token-tile height: 16 (two CTAs per SM) and 32 cover decode batches in one tile; 64
 // halves weight re-reads for larger batches.
 int launch_gemm(int fmt, int mode, int mt, const GemmArgs& a, int num_sms, cudaStream_t st) {
-  if (fmt == CCUT_FMT_AWQ_INT4_G128)
-    return mode == kFfn1 ? launch_gemm_mt<CCUT_FMT_AWQ_INT4_G128, kFfn1>(mt, a, num_sms, st)
-                         : launch_gemm_mt<CCUT_FMT_AWQ_INT4_G128, kFfn2>(mt, a, num_sms, st);
-  return mode == kFfn1 ? launch_gemm_mt<CCUT_FMT_FP8_E4M3_B128, kFfn1>(mt, a, num_sms, st)
-                       : launch_gemm_mt<CCUT_FMT_FP8_E4M3_B128, kFfn2>(mt, a, num_sms, st);
+  switch (fmt) {
+    case CCUT_FMT_AWQ_INT4_G128:
+      return mode == kFfn1 ? launch_gemm_mt<CCUT_FMT_AWQ_INT4_G128, kFfn1>(mt, a, num_sms, st)
+                           : launch_gemm_mt<CCUT_FMT_AWQ_INT4_G128, kFfn2>(mt, a, num_sms, st);
+    case CCUT_FMT_INT4_SYM_G128:
+      return mode == kFfn1 ? launch_gemm_mt<CCUT_FMT_INT4_SYM_G128, kFfn1>(mt, a, num_sms, st)
+                           : launch_gemm_mt<CCUT_FMT_INT4_SYM_G128, kFfn2>(mt, a, num_sms, st);
+    case CCUT_FMT_FP8_E4M3_CH:
+      return mode == kFfn1 ? launch_gemm_mt<CCUT_FMT_FP8_E4M3_CH, kFfn1>(mt, a, num_sms, st)
+                           : launch_gemm_mt<CCUT_FMT_FP8_E4M3_CH, kFfn2>(mt, a, num_sms, st);
+    default:
+      return mode == kFfn1 ? launch_gemm_mt<CCUT_FMT_FP8_E4M3_B128, kFfn1>(mt, a, num_sms, st)
+                           : launch_gemm_mt<CCUT_FMT_FP8_E4M3_B128, kFfn2>(mt, a, num_sms, st);
+  }
 }
 
 }  // namespace ccut

@@ -22,6 +22,10 @@
 //                             [16384, 16388) fp32 block scale, 12 bytes padding
 //     bytes [8j, 8j+8) of a lane cover k-step j; byte b is A-tile element
 //     (row g + 8*((b>>1)&1), col 2t + 8*(b>>2) + (b&1)), i.e. byte pair r is A register r.
+//   FP8 e4m3 channel-scaled block (16896 B): the FP8 codes as above, then at 16384 the fp32
+//     scale of each of the 128 channels (for this 128-k group).
+//   Signed int4 block (8704 B): the AWQ nibbles as above holding q = v + 8 (zero point 8 for
+//     every channel), then at 8192 the fp32 scale of each of the 128 channels.
 //
 // Row layout (used by the tcgen05 kernel): the same block sizes, but each block holds one
 // output channel per row (one tensor-memory lane of the A operand) and is split into two
@@ -34,6 +38,8 @@
 //   FP8:      half h at [8192 h, 8192 h + 8192): 128 rows x 64 B; chunk c (0..3) of row r at
 //             r*64 + 16*(c ^ ((r >> 1) & 3)); byte b of a chunk is k = 64h + 16c + b.  Scale at
 //             16384 (a fused gate/up block: gate scale at 16384, up scale at 16388).
+//   The channel-scaled formats keep the codes of their base format and one fp32 scale per
+//   row at the scale offset (row r of a fused gate/up block: the scale of its channel).
 // The XOR swizzle makes the eight rows read by each quarter-warp hit eight distinct bank
 // groups.  A lone matrix (down projection) uses blocks of 128 channels; the gate and up
 // matrices are fused: block t holds gate channels [64t, 64t+64) in rows 0..63 and the same
@@ -72,36 +78,72 @@ inline __host__ __device__ int rows_channel(int nt, int r, int nmat, int slot) {
 // Row-layout blocks along the channel axis of a matrix with N channels.
 inline __host__ __device__ int rows_nblocks(int N, int nmat) { return nmat == 1 ? N / 128 : N / 64; }
 
-template <int FMT>
-struct Blk;
+// Scale kinds: fp16 per channel (AWQ), one fp32 per block (FP8 b128), fp32 per channel.
+enum { kScaleF16Row = 0, kScaleF32Block = 1, kScaleF32Row = 2 };
 
-template <>
-struct Blk<CCUT_FMT_AWQ_INT4_G128> {
+struct BlkInt4 {                            // nibble codes (AWQ and signed int4)
+  static constexpr bool kInt4 = true;
   static constexpr int kChunks = 2;         // k chunks of 64 per channel block
   static constexpr int kChunkK = 64;
   static constexpr int kStepsPerChunk = 4;  // 16-k MMA steps per chunk
   static constexpr int kAtomBytes = 8192;
   static constexpr int kScaleOff = 8192;
-  static constexpr int kZeroOff = 8448;
-  static constexpr int kBytes = 8512;
   static constexpr bool kBf16 = false;  // f16 operands ((q - z) is exact in f16)
 };
 
-template <>
-struct Blk<CCUT_FMT_FP8_E4M3_B128> {
+struct BlkE4m3 {  // e4m3 codes
+  static constexpr bool kInt4 = false;
   static constexpr int kChunks = 4;  // k chunks of 32
   static constexpr int kChunkK = 32;
   static constexpr int kStepsPerChunk = 2;
   static constexpr int kAtomBytes = 16384;
   static constexpr int kScaleOff = 16384;
   static constexpr int kZeroOff = 0;
-  static constexpr int kBytes = 16400;
+  static constexpr bool kZeros = false;
   static constexpr bool kBf16 = false;  // f16 operands (e4m3 -> f16 is exact)
 };
 
+template <int FMT>
+struct Blk;
+
+template <>
+struct Blk<CCUT_FMT_AWQ_INT4_G128> : BlkInt4 {
+  static constexpr int kZeroOff = 8448;
+  static constexpr bool kZeros = true;  // 4-bit zero point per channel
+  static constexpr int kScale = kScaleF16Row;
+  static constexpr int kBytes = 8512;
+};
+
+template <>
+struct Blk<CCUT_FMT_INT4_SYM_G128> : BlkInt4 {
+  static constexpr int kZeroOff = 0;
+  static constexpr bool kZeros = false;  // zero point 8
+  static constexpr int kScale = kScaleF32Row;
+  static constexpr int kBytes = 8704;
+};
+
+template <>
+struct Blk<CCUT_FMT_FP8_E4M3_B128> : BlkE4m3 {
+  static constexpr int kScale = kScaleF32Block;
+  static constexpr int kBytes = 16400;
+};
+
+template <>
+struct Blk<CCUT_FMT_FP8_E4M3_CH> : BlkE4m3 {
+  static constexpr int kScale = kScaleF32Row;
+  static constexpr int kBytes = 16896;
+};
+
 inline __host__ __device__ size_t block_bytes(int fmt) {
-  return fmt == CCUT_FMT_AWQ_INT4_G128 ? Blk<CCUT_FMT_AWQ_INT4_G128>::kBytes
-                                       : Blk<CCUT_FMT_FP8_E4M3_B128>::kBytes;
+  switch (fmt) {
+    case CCUT_FMT_AWQ_INT4_G128: return Blk<CCUT_FMT_AWQ_INT4_G128>::kBytes;
+    case CCUT_FMT_INT4_SYM_G128: return Blk<CCUT_FMT_INT4_SYM_G128>::kBytes;
+    case CCUT_FMT_FP8_E4M3_CH: return Blk<CCUT_FMT_FP8_E4M3_CH>::kBytes;
+    default: return Blk<CCUT_FMT_FP8_E4M3_B128>::kBytes;
+  }
+}
+inline __host__ __device__ bool fmt_int4(int fmt) {
+  return fmt == CCUT_FMT_AWQ_INT4_G128 || fmt == CCUT_FMT_INT4_SYM_G128;
 }
 
 // Byte offset of block (nt, kt, slot) in a packed buffer with `ktiles` k tiles and `nmat`

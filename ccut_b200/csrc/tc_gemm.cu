@@ -52,18 +52,21 @@ namespace ccut {
 template <int FMT>
 struct TcCfg {
   using B = Blk<FMT>;
-  static constexpr bool kAwq = FMT == CCUT_FMT_AWQ_INT4_G128;
+  static constexpr bool kInt4 = B::kInt4;
   static constexpr int kMaxN = 256;                   // tokens per tile (both ranks)
-  static constexpr int kHalfW = kAwq ? 4096 : 8192;   // packed weights of one 64-k half block
+  static constexpr int kHalfW = kInt4 ? 4096 : 8192;  // packed weights of one 64-k half block
   // Metadata copied with each stage: AWQ scales + zero points (the dequant reads the zero
-  // points), the FP8 scale slot; this also brings the scales the epilogue reads into L2.
-  static constexpr int kMeta = kAwq ? 320 : 16;
+  // points), the per-channel fp32 scales, the FP8 block scale slot; this also brings the
+  // scales the epilogue reads into L2.
+  static constexpr int kMeta = B::kScale == kScaleF32Row ? 512 : B::kZeros ? 320 : 16;
   static constexpr int kWBytes = kHalfW + kMeta;      // one weight stage (multiple of 16)
   static constexpr int kAB = 32768;                   // A tile 16 KB + B tile 16 KB
   static constexpr int kSA = 5;                       // A/B stages
-  static constexpr int kSW = kAwq ? 6 : 4;            // weight stages
-  static constexpr int kXRow = 17;                    // floats per row of the output staging (16 + pad)
+  static constexpr int kSW = kInt4 ? 6 : 4;           // weight stages
+  static constexpr int kXRow = 17;                    // FFN1 staging: floats per weight row (16 + pad)
+  static constexpr int kTokPitch = 132;               // FFN2 staging: floats per token (128 + pad, 16-B rows)
   static constexpr int kXchg = 2 * 128 * kXRow * 4;   // per epilogue warpgroup: 128 rows x 16 tokens
+  static_assert(16 * kTokPitch <= 128 * kXRow && (kTokPitch * 4) % 16 == 0, "FFN2 staging fits the exchange");
   static constexpr int kThreads = 640;
   static constexpr int kDeqWarps = 8;
   static constexpr int kEpiWarps = 8;
@@ -135,7 +138,7 @@ template <int FMT>
 __device__ __forceinline__ void dequant_half_row(const uint8_t* half, const uint8_t* zeros, int r, int h,
                                                  uint8_t* atile) {
   uint8_t* arow = atile + r * 128;
-  if constexpr (FMT == CCUT_FMT_FP8_E4M3_B128) {
+  if constexpr (!Blk<FMT>::kInt4) {
 #pragma unroll
     for (int cc = 0; cc < 2; ++cc) {  // 16 e4m3 values: k 16c .. 16c + 15
       const int c = 2 * h + cc;
@@ -151,7 +154,7 @@ __device__ __forceinline__ void dequant_half_row(const uint8_t* half, const uint
       *reinterpret_cast<uint4*>(arow + (((2 * c + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
     }
   } else {
-    const uint32_t z = (zeros[r >> 1] >> (4 * (r & 1))) & 0xFu;
+    const uint32_t z = Blk<FMT>::kZeros ? (zeros[r >> 1] >> (4 * (r & 1))) & 0xFu : 8u;
     const uint32_t zz = (0x4300u | z) * 0x10001u;  // bf16x2 (128 + z, 128 + z)
     const uint4 q = *reinterpret_cast<const uint4*>(half + r * 32 + 16 * (h ^ ((r >> 2) & 1)));  // k 32h .. +31
     const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
@@ -172,10 +175,13 @@ __device__ __forceinline__ void dequant_half_row(const uint8_t* half, const uint
 // fp32 scale of weight row r of the block at `blk` (one 128-k block).
 template <int FMT, int MODE>
 __device__ __forceinline__ float block_scale(const uint8_t* blk, int r) {
-  if constexpr (FMT == CCUT_FMT_AWQ_INT4_G128) {
-    return __half2float(__ushort_as_half(__ldg(reinterpret_cast<const unsigned short*>(blk + 8192) + r)));
+  using B = Blk<FMT>;
+  if constexpr (B::kScale == kScaleF16Row) {
+    return __half2float(__ushort_as_half(__ldg(reinterpret_cast<const unsigned short*>(blk + B::kScaleOff) + r)));
+  } else if constexpr (B::kScale == kScaleF32Row) {
+    return __ldg(reinterpret_cast<const float*>(blk + B::kScaleOff) + r);
   } else {
-    return __ldg(reinterpret_cast<const float*>(blk + 16384) + (MODE == kFfn1 ? (r >> 6) : 0));
+    return __ldg(reinterpret_cast<const float*>(blk + B::kScaleOff) + (MODE == kFfn1 ? (r >> 6) : 0));
   }
 }
 
@@ -382,7 +388,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
         }
         if (valid) {
           const uint8_t* half = wtiles + s * C::kWBytes;
-          dequant_half_row<FMT>(half, half + C::kHalfW + (C::kAwq ? 256 : 0), r, hk, ab + sa * C::kAB);
+          dequant_half_row<FMT>(half, half + C::kHalfW + (BK::kZeros ? 256 : 0), r, hk, ab + sa * C::kAB);
         }
         tc::fence_proxy_async_smem();
         __syncwarp();
@@ -444,21 +450,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
         if (lane == 0) tc::mbar_arrive_cl(slot ? pe1 : pe0);
       }
       if (!ok || !valid) continue;
-      // Output: the totals go through shared memory 16 tokens at a time (thread r writes row r),
-      // then each thread of the warpgroup produces 8 (FFN1) or 16 (FFN2) consecutive output
-      // channels of one token and stores them as 16-byte vectors.
+      // Output: the totals go through shared memory 16 tokens at a time (thread r writes row
+      // r).  FFN1: each thread of the warpgroup then produces 8 consecutive SwiGLU channels of
+      // one token and stores them as one 16-byte vector.  FFN2: the chunk is staged token-major
+      // and each warp writes whole token rows, lane l channels 4l .. 4l + 3, so that one store
+      // instruction covers 512 contiguous bytes of one output row.
       const int row0 = a.offsets[e] + m0;
-      const int tt = threadIdx.x & 15;          // token of the chunk this thread writes out
-      const int grp = (threadIdx.x >> 4) & 7;   // channel group of this thread
+      const int tt = threadIdx.x & 15;          // FFN1: token of the chunk this thread writes out
+      const int grp = (threadIdx.x >> 4) & 7;   // FFN1: channel group of this thread
 #pragma unroll
       for (int c = 0; c < 128; c += 16) {
         if (c < ncols) {  // uniform over the warpgroup
+          if constexpr (MODE == kFfn2) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) xb[r * C::kXRow + i] = tot[c + i];
-          named_bar(1 + ewg, 128);
-          const int tok = ewg * 128 + c + tt;  // token index inside the tile
-          if (tok < rows) {
-            if constexpr (MODE == kFfn1) {
+            for (int i = 0; i < 16; ++i) xb[i * C::kTokPitch + r] = tot[c + i];
+            named_bar(1 + ewg, 128);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int tl = q * 4 + j;            // token of the chunk (uniform over the warp)
+              const int tok = ewg * 128 + c + tl;  // token index inside the tile
+              if (tok < rows) {
+                const float wr = a.row_weight ? __ldg(a.row_weight + row0 + tok) : 1.f;
+                const float4 v = *reinterpret_cast<const float4*>(xb + tl * C::kTokPitch + 4 * lane);
+                float* orow = static_cast<float*>(a.out) + (size_t)(row0 + tok) * a.out_ld + blk * kTileN + 4 * lane;
+                *reinterpret_cast<float4*>(orow) = make_float4(v.x * wr, v.y * wr, v.z * wr, v.w * wr);
+              }
+            }
+            named_bar(1 + ewg, 128);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) xb[r * C::kXRow + i] = tot[c + i];
+            named_bar(1 + ewg, 128);
+            const int tok = ewg * 128 + c + tt;  // token index inside the tile
+            if (tok < rows) {
               // rows 0..63: gate, rows 64..127: up of the same 64 channels; channels grp*8 .. +7
               uint32_t pk[4];
 #pragma unroll
@@ -472,18 +496,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
               }
               uint16_t* orow = static_cast<uint16_t*>(a.out) + (size_t)(row0 + tok) * a.out_ld + blk * 64 + grp * 8;
               *reinterpret_cast<uint4*>(orow) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-            } else {
-              // channels grp*16 .. +15 of the block's 128, times the row's routing weight
-              const float wr = a.row_weight ? __ldg(a.row_weight + row0 + tok) : 1.f;
-              float* orow = static_cast<float*>(a.out) + (size_t)(row0 + tok) * a.out_ld + blk * kTileN + grp * 16;
-#pragma unroll
-              for (int j = 0; j < 16; j += 4)
-                *reinterpret_cast<float4*>(orow + j) = make_float4(
-                    xb[(grp * 16 + j) * C::kXRow + tt] * wr, xb[(grp * 16 + j + 1) * C::kXRow + tt] * wr,
-                    xb[(grp * 16 + j + 2) * C::kXRow + tt] * wr, xb[(grp * 16 + j + 3) * C::kXRow + tt] * wr);
             }
+            named_bar(1 + ewg, 128);
           }
-          named_bar(1 + ewg, 128);
         }
       }
     }
@@ -532,11 +547,20 @@ static int launch_tc_t(const CUtensorMap& map, const TcArgs& a, int num_sms, cud
 }
 
 int launch_tc_gemm(int fmt, int mode, const CUtensorMap& map, const TcArgs& a, int num_sms, cudaStream_t st) {
-  if (fmt == CCUT_FMT_AWQ_INT4_G128)
-    return mode == kFfn1 ? launch_tc_t<CCUT_FMT_AWQ_INT4_G128, kFfn1>(map, a, num_sms, st)
-                         : launch_tc_t<CCUT_FMT_AWQ_INT4_G128, kFfn2>(map, a, num_sms, st);
-  return mode == kFfn1 ? launch_tc_t<CCUT_FMT_FP8_E4M3_B128, kFfn1>(map, a, num_sms, st)
-                       : launch_tc_t<CCUT_FMT_FP8_E4M3_B128, kFfn2>(map, a, num_sms, st);
+  switch (fmt) {
+    case CCUT_FMT_AWQ_INT4_G128:
+      return mode == kFfn1 ? launch_tc_t<CCUT_FMT_AWQ_INT4_G128, kFfn1>(map, a, num_sms, st)
+                           : launch_tc_t<CCUT_FMT_AWQ_INT4_G128, kFfn2>(map, a, num_sms, st);
+    case CCUT_FMT_INT4_SYM_G128:
+      return mode == kFfn1 ? launch_tc_t<CCUT_FMT_INT4_SYM_G128, kFfn1>(map, a, num_sms, st)
+                           : launch_tc_t<CCUT_FMT_INT4_SYM_G128, kFfn2>(map, a, num_sms, st);
+    case CCUT_FMT_FP8_E4M3_CH:
+      return mode == kFfn1 ? launch_tc_t<CCUT_FMT_FP8_E4M3_CH, kFfn1>(map, a, num_sms, st)
+                           : launch_tc_t<CCUT_FMT_FP8_E4M3_CH, kFfn2>(map, a, num_sms, st);
+    default:
+      return mode == kFfn1 ? launch_tc_t<CCUT_FMT_FP8_E4M3_B128, kFfn1>(map, a, num_sms, st)
+                           : launch_tc_t<CCUT_FMT_FP8_E4M3_B128, kFfn2>(map, a, num_sms, st);
+  }
 }
 
 }  // namespace ccut

@@ -9,7 +9,7 @@ into the gate/up epilogue, and the bf16 (or fp32) output written by the combine 
 
 An intermediate size that is not a multiple of 128 (10944) is padded with zero channels
 on the host before packing: the padded gate/up channels have zero weights (FP8 code 0,
-AWQ scale 0), so ``silu(0) * 0 = 0`` and the padded down-projection inputs contribute
+AWQ scale 0, signed int4 value 0), so ``silu(0) * 0 = 0`` and the padded down-projection inputs contribute
 nothing.  AWQ group-128 matrices need their input size to be a multiple of 128, so an AWQ
 down projection must come with ``in_features`` already a multiple of 128.
 """
@@ -19,25 +19,30 @@ from __future__ import annotations
 import numpy as np
 import torch
 
+from ccut_b200 import formats
 from ccut_b200.layer import MoeLayer, Permutation, _get, _ptr, _stream
 
 __all__ = ["DenseFfn"]
 
 
-def _pad_to(a: np.ndarray, axis: int, size: int) -> np.ndarray:
-    a = np.asarray(a)
+def _pad_to(a: np.ndarray, axis: int, size: int, value=0) -> np.ndarray:
+    a = a.detach().cpu().numpy() if isinstance(a, torch.Tensor) else np.asarray(a)
     if a.shape[axis] == size:
         return a
     if a.shape[axis] > size:
         raise ValueError(f"cannot pad axis {axis} of {a.shape} down to {size}")
     pad = [(0, 0)] * a.ndim
     pad[axis] = (0, size - a.shape[axis])
-    return np.pad(a, pad)
+    return np.pad(a, pad, constant_values=value)
+
+
+_V0 = np.int32(-0x77777778)  # 0x88888888: eight nibbles v + 8 = 8, i.e. signed int4 zeros
 
 
 class DenseFfn:
-    """``fmt``: ``"awq_int4_g128"`` (matrices ``qweight``/``qzeros``/``scales``, ``[in, out]``)
-    or ``"fp8_b128"`` (``weight`` ``[out, in]`` + ``weight_scale_inv``/``scale``).
+    """``fmt``: ``"awq_int4_g128"`` (matrices ``qweight``/``qzeros``/``scales``, ``[in, out]``),
+    ``"fp8_b128"`` (``weight`` ``[out, in]`` + ``weight_scale_inv``/``scale``), or the
+    ``"fp8_channel"`` / ``"int4_sym_g128"`` forms of ``ccut_b200.formats``.
     ``inter`` is the model's intermediate size; it is padded to a multiple of 128."""
 
     def __init__(self, fmt: str, hidden: int, inter: int, gate, up, down, kernel: str = "auto", device="cuda"):
@@ -66,6 +71,22 @@ class DenseFfn:
                 mats[role] = {"weight": _pad_to(w, 0, ip), "scale": _pad_to(s, 0, ip // 128)}
             w, s = _get(down, "weight"), _get(down, "weight_scale_inv", "scale")  # [H, I]: pad columns
             mats["down"] = {"weight": _pad_to(w, 1, ip), "scale": _pad_to(s, 1, ip // 128)}
+        elif fmt == "fp8_channel":
+            mats = {}
+            for role, m in (("gate", gate), ("up", up)):  # [I, H]: pad rows (zero codes)
+                t = formats.canonical(fmt, m)
+                mats[role] = {"weight": _pad_to(t["weight"], 0, ip), "scales": _pad_to(t["scales"], 1, ip)}
+            t = formats.canonical(fmt, down)  # [H, I]: pad columns
+            if t["weight"].shape[1] % 128:
+                raise ValueError("down: per-channel FP8 input size must be a multiple of 128")
+            mats["down"] = {"weight": _pad_to(t["weight"], 1, ip), "scales": _pad_to(t["scales"], 0, ip // 128)}
+        elif fmt == "int4_sym_g128":
+            mats = {}
+            for role, m in (("gate", gate), ("up", up)):  # [H, I]: pad the output channels with v = 0
+                t = formats.canonical(fmt, m)
+                mats[role] = {"qweight": _pad_to(t["qweight"], 1, ip // 8, _V0), "scales": _pad_to(t["scales"], 1, ip)}
+            t = formats.canonical(fmt, down)
+            mats["down"] = {"qweight": _pad_to(t["qweight"], 0, ip, _V0), "scales": _pad_to(t["scales"], 0, ip // 128)}
         else:
             raise NotImplementedError(f"weight format {fmt!r} is not supported")
         self.layer = MoeLayer(fmt, self.hidden, ip, 1, 1, "softmax_topk", np.zeros((1, self.hidden), np.float32),

@@ -5,10 +5,12 @@ buffer + ``ccut/models/generic.py:389-400`` per-call segment dequant): every exp
 checkpoint tensors are uploaded once, packed on the device into the kernel tile layout
 and stay resident.  ``forward`` is the whole MoE layer of ``ccut/models/generic.py:348-386``.
 
-Checkpoint tensors are accepted per matrix as a mapping (or object with attributes):
-AWQ ``{"qweight": int32 [K, N/8], "qzeros": int32 [K/128, N/8], "scales": fp16 [K/128, N]}``
-(``[in, out]``); FP8 ``{"weight": e4m3/uint8 [N, K], "scale": fp32 [N/128, K/128]}``
-(``[out, in]``, the ``weight_scale_inv`` tensor of DeepSeek checkpoints).
+Checkpoint tensors are accepted per matrix as a mapping (or object with attributes), in
+the forms ``ccut_b200.formats`` lists: AWQ ``{"qweight": int32 [K, N/8], "qzeros": int32
+[K/128, N/8], "scales": fp16 [K/128, N]}`` (``[in, out]``); block FP8 ``{"weight": e4m3/uint8
+[N, K], "scale": fp32 [N/128, K/128]}`` (``[out, in]``, the ``weight_scale_inv`` tensor of
+DeepSeek checkpoints); per-channel FP8 ``{"weight": [N, K], "scale": fp32 [N]}``; signed int4
+``{"weight": uint8 [N, K/2], "scale": fp32 [K]}``.
 """
 
 from __future__ import annotations
@@ -20,7 +22,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
-from ccut_b200 import _lib
+from ccut_b200 import _lib, formats
 
 __all__ = ["MoeLayer", "Routing", "Permutation"]
 
@@ -73,7 +75,8 @@ class Permutation:
 class MoeLayer:
     """One MoE layer with experts resident in HBM.
 
-    ``fmt``: ``"awq_int4_g128"`` or ``"fp8_b128"``; ``routing``: ``"softmax_topk"``
+    ``fmt``: ``"awq_int4_g128"``, ``"fp8_b128"``, ``"fp8_channel"`` or ``"int4_sym_g128"``;
+    ``routing``: ``"softmax_topk"``
     (``norm_topk_prob=False``), ``"topk_softmax"`` (``norm_topk_prob=True``) or
     ``"sigmoid_group"``.  ``kernel``: ``"auto"`` keeps both packed layouts resident and runs
     the mma.sync kernel for decode-sized batches and the tcgen05 kernel otherwise; ``"tc"``
@@ -160,29 +163,16 @@ class MoeLayer:
 
     # ---- packing ------------------------------------------------------------------
     def _slice(self, mat, role: str, lo: int, width: int):
-        """Checkpoint tensors of intermediate channels [lo, lo+width) of one matrix."""
-        if self.fmt == "awq_int4_g128":
-            q, z, s = _get(mat, "qweight"), _get(mat, "qzeros"), _get(mat, "scales")
-            if role in ("gate", "up"):  # [K=H, N=I]: slice N
-                return q[:, lo // 8:(lo + width) // 8], z[:, lo // 8:(lo + width) // 8], s[:, lo:lo + width]
-            return q[lo:lo + width], z[lo // 128:(lo + width) // 128], s[lo // 128:(lo + width) // 128]
-        w, sc = _get(mat, "weight"), _get(mat, "scale", "weight_scale_inv")
-        if role in ("gate", "up"):  # [N=I, K=H]: slice N
-            return w[lo:lo + width], None, sc[lo // 128:(lo + width) // 128]
-        return w[:, lo:lo + width], None, sc[:, lo // 128:(lo + width) // 128]
+        """Canonical checkpoint tensors of intermediate channels [lo, lo+width) of one matrix:
+        the output channels of gate / up, the input channels of down."""
+        t = formats.canonical(self.fmt, mat)
+        return formats.slice_out(self.fmt, t, lo, width) if role in ("gate", "up") else formats.slice_in(
+            self.fmt, t, lo, width)
 
     def _pack_one(self, layout_code, mat, role, lo, width, K, N, dst: torch.Tensor, nmat: int, slot: int):
-        q, z, s = self._slice(mat, role, lo, width)
-        if self.fmt == "awq_int4_g128":
-            qd, zd, sd = _dev(q, self.device, torch.int32), _dev(z, self.device, torch.int32), _dev(s, self.device,
-                                                                                                   torch.float16)
-            if tuple(qd.shape) != (K, N // 8) or tuple(sd.shape) != (K // 128, N):
-                raise ValueError(f"{role}: AWQ tensors have shapes q{tuple(qd.shape)} s{tuple(sd.shape)} for K={K} N={N}")
-        else:
-            qd, zd, sd = _dev(q, self.device, torch.uint8), None, _dev(s, self.device, torch.float32)
-            if tuple(qd.shape) != (N, K) or tuple(sd.shape) != (N // 128, K // 128):
-                raise ValueError(f"{role}: FP8 tensors have shapes w{tuple(qd.shape)} s{tuple(sd.shape)} for K={K} N={N}")
-        _lib.call("ccut_pack_matrix", self.fmt_code, layout_code, _ptr(qd), _ptr(zd), _ptr(sd), K, N, self.nibbles,
+        qd, zd, sd = formats.pack_args(self.fmt, self._slice(mat, role, lo, width), K, N, self.device, role)
+        nibbles = _lib.NIBBLES_AWQ if formats.repacked(self.fmt, mat) else self.nibbles
+        _lib.call("ccut_pack_matrix", self.fmt_code, layout_code, _ptr(qd), _ptr(zd), _ptr(sd), K, N, nibbles,
                   _ptr(dst), nmat, slot, _stream())
 
     def _pack_expert(self, code, w13_all, w2_all, e: int, ew, lo: int, width: int):

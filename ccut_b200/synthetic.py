@@ -11,7 +11,12 @@ then activations.  Within one matrix: AWQ ``qweight``, ``qzeros``, ``scales``; F
 * AWQ nibbles and zero-points uniform in ``[0, 15]`` (uniform 32-bit words), scales
   fp16 ``|N(0, 0.02)| + 1e-3``;
 * FP8 values ``N(0, 1)`` clipped to +-448 and rounded to e4m3 (nearest-even), block
-  scales fp32 log-uniform in ``[1e-3, 1e-1]``.
+  scales fp32 log-uniform in ``[1e-3, 1e-1]``;
+* per-channel FP8 (``fp8_channel``, the reference's own FP8): the same codes, one fp32
+  scale per output channel, log-uniform in ``[1e-3, 1e-1]``;
+* signed int4 (``int4_sym_g128``, the reference's ``int4_w4a16_sym``): values uniform in
+  ``[-8, 7]``, one fp32 scale per input column, ``|N(0, 0.02)| + 1e-3`` drawn per 128-k
+  group (the scale is constant within each group, as the kernels require).
 """
 
 from __future__ import annotations
@@ -27,6 +32,8 @@ __all__ = [
     "CONFIGS",
     "AwqMatrix",
     "Fp8Matrix",
+    "Fp8ChannelMatrix",
+    "Int4SymMatrix",
     "ExpertWeights",
     "LayerWeights",
     "make_layer",
@@ -58,7 +65,7 @@ class MoeLayerConfig:
     top_k: int
     num_shared: int
     shared_inter: int
-    fmt: str  # "awq_int4_g128" | "fp8_b128"
+    fmt: str  # "awq_int4_g128" | "fp8_b128" | "fp8_channel" | "int4_sym_g128"
     routing: str  # "softmax_topk" | "topk_softmax" | "sigmoid_group"
     n_group: int = 1
     topk_group: int = 1
@@ -83,9 +90,14 @@ class MoeLayerConfig:
 
 
 def _matrix_bytes(fmt: str, k: int, n: int) -> int:
+    """Checkpoint bytes of one matrix (weights + scales + zero-points)."""
     if fmt == "awq_int4_g128":
         groups = k // GROUP
         return k * n // 2 + groups * n * 2 + groups * n // 2
+    if fmt == "fp8_channel":
+        return k * n + n * 4
+    if fmt == "int4_sym_g128":
+        return k * n // 2 + k * 4
     nb, kb = math.ceil(n / BLOCK), math.ceil(k / BLOCK)
     return k * n + nb * kb * 4
 
@@ -126,6 +138,23 @@ class Fp8Matrix:
 
     weight: np.ndarray  # uint8 [N, K]
     scale: np.ndarray  # fp32 [N/128, K/128]
+
+
+@dataclass
+class Fp8ChannelMatrix:
+    """FP8 e4m3 with one fp32 scale per output channel, [out, in] = [N, K] (the reference's
+    ``fp8_dequant_mat`` layout)."""
+
+    weight: np.ndarray  # uint8 [N, K]
+    scale: np.ndarray  # fp32 [N]
+
+
+@dataclass
+class Int4SymMatrix:
+    """Signed int4 weight-only, [out, in] (the reference's ``WeightOnlyMethod`` layout)."""
+
+    weight: np.ndarray  # uint8 [N, K/2], low nibble = even input column
+    scale: np.ndarray  # fp32 [K], one per input column
 
 
 @dataclass
@@ -170,6 +199,14 @@ def _gen_matrix(rng: np.random.Generator, fmt: str, k: int, n: int):
         nb, kb = math.ceil(n / BLOCK), math.ceil(k / BLOCK)
         scale = np.exp(rng.uniform(math.log(1e-3), math.log(1e-1), size=(nb, kb))).astype(np.float32)
         return Fp8Matrix(_encode_e4m3(w), scale)
+    if fmt == "fp8_channel":
+        w = np.clip(rng.standard_normal((n, k), dtype=np.float32), -448.0, 448.0)
+        scale = np.exp(rng.uniform(math.log(1e-3), math.log(1e-1), size=n)).astype(np.float32)
+        return Fp8ChannelMatrix(_encode_e4m3(w), scale)
+    if fmt == "int4_sym_g128":
+        packed = rng.integers(0, 256, size=(n, k // 2), dtype=np.uint8)
+        sg = (np.abs(rng.normal(0.0, 0.02, size=k // GROUP)) + 1e-3).astype(np.float32)
+        return Int4SymMatrix(packed, np.repeat(sg, GROUP))
     raise ValueError(f"unknown format {fmt!r}")
 
 
@@ -195,6 +232,15 @@ def make_layer_device(cfg: str | MoeLayerConfig, seed: int = 0, device="cuda") -
     g.manual_seed(seed)
 
     def mat(k: int, n: int):
+        lo, hi = math.log(1e-3), math.log(1e-1)
+        if cfg.fmt == "int4_sym_g128":
+            packed = torch.randint(0, 256, (n, k // 2), generator=g, device=device, dtype=torch.int32).to(torch.uint8)
+            sg = (torch.randn((k // GROUP,), generator=g, device=device) * 0.02).abs_().add_(1e-3)
+            return Int4SymMatrix(packed, sg.repeat_interleave(GROUP))
+        if cfg.fmt == "fp8_channel":
+            w = torch.randn((n, k), generator=g, device=device).clamp_(-448.0, 448.0).to(torch.float8_e4m3fn)
+            sc = torch.rand((n,), generator=g, device=device).mul_(hi - lo).add_(lo).exp_()
+            return Fp8ChannelMatrix(w.view(torch.uint8), sc)
         if cfg.fmt == "awq_int4_g128":
             q = torch.randint(-2**31, 2**31, (k, n // 8), generator=g, device=device, dtype=torch.int64).to(torch.int32)
             z = torch.randint(-2**31, 2**31, (k // GROUP, n // 8), generator=g, device=device,
@@ -203,7 +249,6 @@ def make_layer_device(cfg: str | MoeLayerConfig, seed: int = 0, device="cuda") -
             return AwqMatrix(q, z, sc)
         w = torch.randn((n, k), generator=g, device=device).clamp_(-448.0, 448.0).to(torch.float8_e4m3fn)
         nb, kb = math.ceil(n / BLOCK), math.ceil(k / BLOCK)
-        lo, hi = math.log(1e-3), math.log(1e-1)
         sc = torch.rand((nb, kb), generator=g, device=device).mul_(hi - lo).add_(lo).exp_()
         return Fp8Matrix(w.view(torch.uint8), sc)
 

@@ -53,10 +53,18 @@ enum {
 };
 
 /* Weight formats (the reference registers formats as QuantKey names,
- * ccut/quant/spec.py:72-149; these two are new keys). */
+ * ccut/quant/spec.py:72-149).  AWQ_INT4_G128 and FP8_E4M3_B128 are new keys.  FP8_E4M3_CH is
+ * the reference's own FP8 (fp8_static_channel_sym / fp8_dynamic_token_sym /
+ * fp8_static_tensor_sym: e4m3 with an fp32 scale per output channel, ccut/quant/kernels.py:
+ * 150-171) and INT4_SYM_G128 its signed int4 (int4_w4a16_sym, ccut/quant/kernels.py:277-295);
+ * both take one fp32 scale per output channel per 128-k group, so a per-channel (or
+ * per-tensor) scale is that scale repeated along K, and a per-input scale must be constant
+ * within each 128-k group. */
 enum {
   CCUT_FMT_AWQ_INT4_G128 = 1, /* AWQ: qweight int32 [K,N/8], qzeros int32 [K/128,N/8], scales fp16 [K/128,N] */
-  CCUT_FMT_FP8_E4M3_B128 = 2  /* DeepSeek fp8: weight e4m3 [N,K], scale fp32 [N/128,K/128] */
+  CCUT_FMT_FP8_E4M3_B128 = 2, /* DeepSeek fp8: weight e4m3 [N,K], scale fp32 [N/128,K/128] */
+  CCUT_FMT_FP8_E4M3_CH = 3,   /* weight e4m3 [N,K], scale fp32 [K/128,N] */
+  CCUT_FMT_INT4_SYM_G128 = 4  /* signed int4 v as q = v + 8 in qweight int32 [K,N/8], scale fp32 [K/128,N] */
 };
 
 /* Packed tile layouts (same byte size).  ROWS feeds the tcgen05 kernel (one output channel
@@ -128,13 +136,17 @@ CCUT_API size_t ccut_w2_bytes(int format, int hidden, int inter);
  * 2 * ccut_packed_matrix_bytes() (FRAGS: interleaved blocks; ROWS: fused 128-row blocks of
  * 64 gate + 64 up channels); `nmat` = 1 packs a lone matrix.
  * AWQ: q = qweight [K, N/8], z = qzeros [K/128, N/8], s = scales fp16 [K/128, N].
- * FP8: q = weight e4m3 [N, K], z unused (NULL), s = scale fp32 [N/128, K/128].
+ * FP8 (B128): q = weight e4m3 [N, K], z unused (NULL), s = scale fp32 [N/128, K/128].
+ * FP8 (CH): q = weight e4m3 [N, K], z unused (NULL), s = scale fp32 [K/128, N].
+ * INT4 (SYM): q = qweight [K, N/8] of v + 8 (nibble order as for AWQ), z unused (NULL),
+ * s = scale fp32 [K/128, N].
  * Replaces the load-time layout handling of ccut/quant/method.py:35-43 (create_weights). */
 CCUT_API int ccut_pack_matrix(int format, int layout, const void* q, const void* z, const void* s, int K,
                               int N, int nibble_order, void* dst, int nmat, int slot, ccut_stream_t stream);
 
 /* Debug export: packed matrix -> fp32 [K, N] (in, out), bit-identical to the checkpoint
- * dequant ((q - z) * s for AWQ; e4m3 * scale for FP8, NaN codes -> NaN).
+ * dequant ((q - z) * s for AWQ, (q - 8) * s for INT4 (SYM); e4m3 * scale for FP8, NaN codes
+ * -> NaN).
  * Replaces ccut/quant/kernels.py:150-171 (fp8_dequant_mat) / :276-295 (int4_dequant_row). */
 CCUT_API int ccut_dequant_matrix(int format, int layout, const void* packed, int K, int N, int nmat,
                                  int slot, float* out, ccut_stream_t stream);
@@ -190,7 +202,10 @@ CCUT_API int ccut_moe_expert_ffn(const ccut_moe_layer* L, const uint16_t* x, int
                         const int32_t* offsets, const int32_t* row_token,
                         const float* row_weight, float* y_rows, void* workspace,
                         size_t ws_bytes, ccut_stream_t stream);
-/* Same call restricted to one format (fails with CCUT_ERR_UNSUPPORTED otherwise). */
+/* Same call restricted to formats (fails with CCUT_ERR_UNSUPPORTED otherwise): _w4a16 takes
+ * the int4 formats (AWQ_INT4_G128, INT4_SYM_G128; the reference's "w4a16" compute path),
+ * _fp8b128 FP8_E4M3_B128, _w8a16 FP8_E4M3_CH (the reference's "w8a16" path of per-channel FP8,
+ * ccut/quant/method.py:109-111). */
 CCUT_API int ccut_moe_expert_ffn_w4a16(const ccut_moe_layer* L, const uint16_t* x, int T, int k,
                               const int32_t* offsets, const int32_t* row_token,
                               const float* row_weight, float* y_rows, void* workspace,
@@ -199,6 +214,10 @@ CCUT_API int ccut_moe_expert_ffn_fp8b128(const ccut_moe_layer* L, const uint16_t
                                 const int32_t* offsets, const int32_t* row_token,
                                 const float* row_weight, float* y_rows, void* workspace,
                                 size_t ws_bytes, ccut_stream_t stream);
+CCUT_API int ccut_moe_expert_ffn_w8a16(const ccut_moe_layer* L, const uint16_t* x, int T, int k,
+                              const int32_t* offsets, const int32_t* row_token,
+                              const float* row_weight, float* y_rows, void* workspace,
+                              size_t ws_bytes, ccut_stream_t stream);
 
 /* The two halves of ccut_moe_expert_ffn, for callers that schedule them separately.
  * gate/up: h_rows [R, I] = silu(x_r @ Wg) * (x_r @ Wu), f16 (both formats)

@@ -24,6 +24,17 @@ FP8 e4m3, 128x128 blocks
     ``m/8 * 2^-6``, 0x7F / 0xFF = NaN, no infinities.  The reference only implements the
     per-row scaled variant (``ccut/quant/kernels.py:150-171``); the block variant is a
     restatement (the reference's ``Fp8Config`` raises, ``ccut/quant/fp8.py:37-51``).
+
+FP8 e4m3, one scale per output channel (the reference's own FP8)
+    ``weight`` uint8 [N, K], ``scale`` fp32 [N]:
+    ``w[n, k] = e4m3(b[n, k]) * scale[n]``, ``fp8_dequant_mat`` (``ccut/quant/kernels.py:
+    150-171``; ``fp8_static_channel_sym``, ``ccut/quant/spec.py:139``).
+
+Signed int4 weight-only (the reference's ``int4_w4a16_sym``)
+    ``weight`` uint8 [N, K/2] (two signed nibbles per byte, low nibble = even column),
+    ``scale`` fp32 [K] (one per input column): ``w[n, k] = v[n, k] * scale[k]``,
+    ``int4_dequant_row`` (``ccut/quant/kernels.py:277-295``) as ``WeightOnlyMethod.apply``
+    calls it (``ccut/quant/weight_only.py:37-54``).
 """
 
 from __future__ import annotations
@@ -41,6 +52,9 @@ __all__ = [
     "fp8_e4m3_decode",
     "fp8_e4m3_encode",
     "fp8_block_dequant",
+    "fp8_channel_dequant",
+    "int4_sym_unpack",
+    "int4_sym_dequant",
     "bf16_bits_from_f32",
     "bf16_bits_to_f32",
 ]
@@ -167,6 +181,39 @@ def fp8_block_dequant(w: np.ndarray, scale: np.ndarray, block: int = BLOCK) -> n
         raise ValueError(f"scale shape {scale.shape} != {(nb, kb)}")
     sfull = np.repeat(np.repeat(scale, block, axis=0), block, axis=1)[:N, :K]
     return (fp8_e4m3_decode(w) * sfull).astype(np.float32)
+
+
+def fp8_channel_dequant(w: np.ndarray, scale: np.ndarray) -> np.ndarray:
+    """Per-output-channel FP8 -> fp32 [N, K] (``[out, in]``), following ``fp8_dequant_mat``
+    (``ccut/quant/kernels.py:150-171``): ``out[n, k] = e4m3(w[n, k]) * scale[n]``.  The exact
+    product of an e4m3 value and an fp32 scale has at most 28 significant bits, so the
+    reference's float64 product rounded once to fp32 equals this fp32 multiply."""
+    w = np.asarray(w, dtype=np.uint8)
+    scale = np.asarray(scale, dtype=np.float32).reshape(-1)
+    if scale.shape != (w.shape[0],):
+        raise ValueError(f"scale shape {scale.shape} != ({w.shape[0]},)")
+    return (fp8_e4m3_decode(w) * scale[:, None]).astype(np.float32)
+
+
+def int4_sym_unpack(packed: np.ndarray) -> np.ndarray:
+    """uint8 [N, K/2] of two signed nibbles (low nibble = even column) -> int8 [N, K] in
+    [-8, 7], as ``int4_dequant_row`` reads them (``ccut/quant/kernels.py:283-293``)."""
+    p = np.asarray(packed, dtype=np.uint8)
+    v = np.empty((p.shape[0], p.shape[1] * 2), dtype=np.int8)
+    lo, hi = (p & 0x0F).astype(np.int8), (p >> 4).astype(np.int8)
+    v[:, 0::2] = np.where(lo >= 8, lo - 16, lo)
+    v[:, 1::2] = np.where(hi >= 8, hi - 16, hi)
+    return v
+
+
+def int4_sym_dequant(packed: np.ndarray, scale: np.ndarray) -> np.ndarray:
+    """Signed int4 weight-only -> fp32 [N, K] (``[out, in]``), following ``int4_dequant_row``
+    (``ccut/quant/kernels.py:277-295``): ``out[n, k] = v[n, k] * scale[k]``."""
+    v = int4_sym_unpack(packed)
+    scale = np.asarray(scale, dtype=np.float32).reshape(-1)
+    if scale.shape != (v.shape[1],):
+        raise ValueError(f"scale shape {scale.shape} != ({v.shape[1]},)")
+    return (v.astype(np.float32) * scale[None, :]).astype(np.float32)
 
 
 def bf16_bits_from_f32(x: np.ndarray) -> np.ndarray:

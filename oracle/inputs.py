@@ -14,7 +14,9 @@ from ccut_b200.synthetic import (  # noqa: F401  (re-exported)
     CONFIGS,
     AwqMatrix,
     ExpertWeights,
+    Fp8ChannelMatrix,
     Fp8Matrix,
+    Int4SymMatrix,
     LayerWeights,
     MoeLayerConfig,
     scaled_config,
@@ -22,8 +24,8 @@ from ccut_b200.synthetic import (  # noqa: F401  (re-exported)
 from ccut_b200 import synthetic
 from oracle import formats
 
-__all__ = ["CONFIGS", "MoeLayerConfig", "AwqMatrix", "Fp8Matrix", "ExpertWeights", "OracleLayer", "make_layer",
-           "scaled_config", "dequant"]
+__all__ = ["CONFIGS", "MoeLayerConfig", "AwqMatrix", "Fp8Matrix", "Fp8ChannelMatrix", "Int4SymMatrix",
+           "ExpertWeights", "OracleLayer", "make_layer", "scaled_config", "dequant"]
 
 
 def dequant(mat) -> np.ndarray:
@@ -32,6 +34,10 @@ def dequant(mat) -> np.ndarray:
         return formats.awq_dequant(mat.qweight, mat.qzeros, mat.scales)
     if isinstance(mat, Fp8Matrix):
         return np.ascontiguousarray(formats.fp8_block_dequant(mat.weight, mat.scale).T)
+    if isinstance(mat, Fp8ChannelMatrix):
+        return np.ascontiguousarray(formats.fp8_channel_dequant(mat.weight, mat.scale).T)
+    if isinstance(mat, Int4SymMatrix):
+        return np.ascontiguousarray(formats.int4_sym_dequant(mat.weight, mat.scale).T)
     raise TypeError(f"unknown matrix type {type(mat).__name__}")
 
 
