@@ -98,10 +98,18 @@ def _x_bf16(x, hidden: int, device) -> tuple[torch.Tensor, bool]:
 def moe_combine(x, expert_ids, weights, expert_outputs=None, expert_fn=None, w_lookup=None):
     """``y[t] = sum_j weights[t, j] * expert_{ids[t, j]}(x[t])`` in fp32 with the given
     routing; ``w_lookup`` is the resident layer.  Shared experts are not added (the
-    reference adds them outside ``moe_combine``)."""
-    if expert_outputs is not None or expert_fn is not None:
-        raise NotImplementedError("precomputed expert outputs / custom expert functions: the experts run on the GPU")
+    reference adds them outside ``moe_combine``).
+
+    ``expert_fn=None`` runs the layer's fused expert kernels.  A caller's ``expert_fn`` is
+    called as in the reference, ``expert_fn(x_rows, w_gate, w_up, w_down)`` per expert on
+    host arrays (fp32, ``[in, out]``), with the weights the layer's packed tiles export
+    (bit-identical to the checkpoint dequant); its rows are weighted and summed per token by
+    the combine kernel in slot order.  ``expert_outputs`` is accepted and not read: the
+    reference's ``moe_combine`` does not read it either (``ccut/blocks/moe.py:144-174``)."""
+    del expert_outputs
     L = _resolve_layer(w_lookup)
+    if expert_fn is not None:
+        return _combine_with_fn(L, x, expert_ids, weights, expert_fn)
     xt, was_np = _x_bf16(x, L.hidden, L.device)
     ids = expert_ids if isinstance(expert_ids, torch.Tensor) else torch.from_numpy(np.asarray(expert_ids))
     wts = weights if isinstance(weights, torch.Tensor) else torch.from_numpy(np.asarray(weights, dtype=np.float32))
@@ -120,6 +128,36 @@ def moe_combine(x, expert_ids, weights, expert_outputs=None, expert_fn=None, w_l
     else:
         perm = L.permute(r)
         out = L.combine(L.expert_ffn(xt, perm, k), perm, T, k, out_dtype=torch.float32)
+    return out.cpu().numpy() if was_np else out
+
+
+def _combine_with_fn(L: MoeLayer, x, expert_ids, weights, expert_fn):
+    was_np = not isinstance(x, torch.Tensor)
+    xf = np.asarray(x, dtype=np.float32) if was_np else x.detach().float().cpu().numpy()
+    if xf.ndim != 2 or xf.shape[1] != L.hidden:
+        raise ValueError(f"activations must be [seq, {L.hidden}], got {xf.shape}")
+    ids = expert_ids if isinstance(expert_ids, torch.Tensor) else torch.from_numpy(np.asarray(expert_ids))
+    wts = weights if isinstance(weights, torch.Tensor) else torch.from_numpy(np.asarray(weights, dtype=np.float32))
+    if ids.shape != wts.shape or ids.dim() != 2 or ids.shape[0] != xf.shape[0]:
+        raise ValueError("expert_ids and weights must both be [seq, k] for the seq rows of x")
+    ids = ids.to(L.device, torch.int32)
+    if ids.numel() and (int(ids.min()) < 0 or int(ids.max()) >= L.num_experts):
+        raise ValueError(f"expert ids must lie in [0, {L.num_experts})")
+    T, k = ids.shape
+    perm = L.permute(Routing(ids, wts.to(L.device, torch.float32)))
+    offs = perm.offsets.cpu().numpy()
+    row_token = perm.row_token.cpu().numpy()
+    y = torch.zeros((perm.row_token.numel(), L.hidden), dtype=torch.float32, device=L.device)
+    for e in range(L.num_experts):
+        lo, hi = int(offs[e]), int(offs[e + 1])
+        if hi == lo:
+            continue
+        mats = [L.dequant(e, w).cpu().numpy() for w in ("gate", "up", "down")]
+        ye = np.asarray(expert_fn(xf[row_token[lo:hi]], *mats), dtype=np.float32)
+        if ye.shape != (hi - lo, L.hidden):
+            raise ValueError(f"expert_fn returned {ye.shape} for {hi - lo} rows of expert {e}")
+        y[lo:hi] = torch.from_numpy(ye).to(L.device) * perm.row_weight[lo:hi, None]
+    out = L.combine(y, perm, T, k, out_dtype=torch.float32)
     return out.cpu().numpy() if was_np else out
 
 

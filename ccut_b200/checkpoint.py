@@ -205,12 +205,19 @@ def _compressed_tensors_format(q: dict) -> str:
         stored = str(g.get("format") or q.get("format") or "pack-quantized").lower()
         if stored != "pack-quantized":
             raise NotImplementedError(f"compressed-tensors int4 stored as {stored!r} (have pack-quantized)")
-        return "awq_int4_g128"
+        # symmetric: signed int4 with its fp32 group scales as they are; asymmetric: AWQ's
+        # unsigned codes and zero points (fp16 scales)
+        return "int4_sym_g128" if w.get("symmetric", True) else "awq_int4_g128"
     if kind == "float" and bits == 8 and strategy == "block" and [int(v) for v in (w.get("block_structure") or [])] \
             == [128, 128]:
         return "fp8_b128"
+    if kind == "float" and bits == 8 and strategy in ("channel", "tensor"):
+        # the reference's own FP8 (its checkpoints' weights are per-channel static,
+        # ccut/quant/compressed_tensors.py:3-10); per-token dynamic activations run in 16 bits
+        # here, as the reference computes them (dequantized weights, ccut/quant/method.py:131-139)
+        return "fp8_channel"
     raise NotImplementedError(f"compressed-tensors weights type={kind!r} num_bits={bits} strategy={strategy!r} are not "
-                              "supported (int4 group 128, or FP8 128 x 128 blocks)")
+                              "supported (int4 group 128, FP8 per channel / per tensor / 128 x 128 blocks)")
 
 
 def quant_format(config: dict) -> str:
@@ -319,15 +326,35 @@ def expert_pattern(template: str) -> re.Pattern[str]:
     return re.compile("^" + "".join(out))
 
 
-_SUFFIXES = {"awq_int4_g128": ("qweight", "qzeros", "scales"), "fp8_b128": ("weight", "weight_scale_inv")}
+_SUFFIXES = {"awq_int4_g128": ("qweight", "qzeros", "scales"), "fp8_b128": ("weight", "weight_scale_inv"),
+             "fp8_channel": ("weight", "weight_scale"), "int4_sym_g128": ("weight_packed", "weight_scale")}
 
 
 def _read_compressed_tensors(reader: CheckpointReader, prefix: str, fmt: str) -> dict | None:
     """A compressed-tensors matrix in this path's tensors, or None when ``prefix`` has none:
     int4 ``weight_packed`` / ``weight_scale`` / ``weight_zero_point`` repacked into AWQ's
     (``quant.ct_int4_to_awq``); FP8 ``weight`` with its block scales under ``weight_scale``."""
-    from ccut_b200.quant import ct_int4_to_awq
+    from ccut_b200.quant import ct_int4_to_awq, ct_int4_to_sym
 
+    if fmt == "int4_sym_g128":
+        if not reader.has(f"{prefix}.weight_packed"):
+            return None
+        if reader.has(f"{prefix}.weight_g_idx"):
+            raise NotImplementedError(f"{prefix}: activation reordering (weight_g_idx) is not supported")
+        if reader.has(f"{prefix}.weight_zero_point"):
+            raise ValueError(f"{prefix}: a symmetric int4 matrix has no zero points")
+        if reader.dtype(f"{prefix}.weight_packed") != "I32" or not reader.has(f"{prefix}.weight_scale"):
+            raise ValueError(f"{prefix}: int4 tensors must be an I32 weight_packed with a weight_scale")
+        shape = reader.tensor(f"{prefix}.weight_shape") if reader.has(f"{prefix}.weight_shape") else None
+        return ct_int4_to_sym(reader.tensor(f"{prefix}.weight_packed"), _float_tensor(reader, f"{prefix}.weight_scale"),
+                              shape)
+    if fmt == "fp8_channel":
+        if not reader.has(f"{prefix}.weight"):
+            return None
+        if reader.dtype(f"{prefix}.weight") != "F8_E4M3" or not reader.has(f"{prefix}.weight_scale"):
+            raise ValueError(f"{prefix}: FP8 tensors must be an F8_E4M3 weight with a weight_scale")
+        return {"weight": reader.tensor(f"{prefix}.weight"),
+                "weight_scale": _float_tensor(reader, f"{prefix}.weight_scale").reshape(-1)}
     if fmt == "awq_int4_g128" and reader.has(f"{prefix}.weight_packed"):
         if reader.has(f"{prefix}.weight_g_idx"):
             raise NotImplementedError(f"{prefix}: activation reordering (weight_g_idx) is not supported")
@@ -359,6 +386,8 @@ def _read_matrix(reader: CheckpointReader, prefix: str, fmt: str) -> dict:
     if ct is not None:
         return ct
     main = _SUFFIXES[fmt][0]
+    if fmt in ("fp8_channel", "int4_sym_g128"):  # only compressed-tensors checkpoints store these
+        raise KeyError(f"no tensor {prefix}.{main!s} in the checkpoint")
     if not reader.has(f"{prefix}.{main}"):
         raise KeyError(f"no tensor {prefix}.{main!s} in the checkpoint")
     out = {}
@@ -628,8 +657,8 @@ def _dense_or_quant(rd: CheckpointReader, prefix: str, fmt: str, out_dim: int, i
             raise ValueError(f"{name} has shape {a.shape}, expected {(out_dim, in_dim)}")
         return "dense", a
     m = _read_matrix(rd, prefix, fmt)
-    shape = m["qweight"].shape if fmt == "awq_int4_g128" else m["weight"].shape
-    want = (in_dim, out_dim // 8) if fmt == "awq_int4_g128" else (out_dim, in_dim)
+    shape = m["qweight"].shape if "qweight" in m else m["weight"].shape
+    want = (in_dim, out_dim // 8) if "qweight" in m else (out_dim, in_dim)
     if shape != want:
         raise ValueError(f"{prefix} has shape {shape}, expected {want}")
     return "quant", m
@@ -743,7 +772,7 @@ def load_decoder(model_dir: str | Path, device="cuda", kernel: str = "auto", nam
         padded = -(-out_dim // 128) * 128
         if padded != out_dim:
             a = pad_out_channels(spec.fmt, a, padded)
-        main = _SUFFIXES[spec.fmt][0]
+        main = "qweight" if "qweight" in a else _SUFFIXES[spec.fmt][0]
         t = dequantize(spec.fmt, a[main], {k: v for k, v in a.items() if k != main}, in_dim, padded, device)
         return t[:out_dim].to(dtype).contiguous()
 

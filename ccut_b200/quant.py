@@ -187,7 +187,10 @@ class Fp8ChannelMethod(_PackedLinear):
     scale_names = (("weight_scale", "scale"),)
 
     def _matrix(self, weight_bytes, scales):
-        return {"weight": _as_array(weight_bytes, np.uint8).reshape(self.N, self.K),
+        w = _as_array(weight_bytes, np.uint8).reshape(self.N, self.K)
+        if "scales" in scales and self.scale_name not in scales:  # one scale per channel per 128-k group
+            return {"weight": w, "scales": np.asarray(scales["scales"], np.float32).reshape(self.K // 128, self.N)}
+        return {"weight": w,
                 "scale": np.asarray(self._scale(scales, ("weight_scale", "scale")), dtype=np.float32).reshape(-1)}
 
 
@@ -201,6 +204,9 @@ class Int4SymMethod(_PackedLinear):
     bits = 4
 
     def _matrix(self, weight_bytes, scales):
+        if "scales" in scales and self.scale_name not in scales:  # qweight int32 [K, N/8] of v + 8
+            return {"qweight": _as_array(weight_bytes, np.int32).reshape(self.K, self.N // 8),
+                    "scales": np.asarray(scales["scales"], np.float32).reshape(self.K // 128, self.N)}
         return {"weight": _as_array(weight_bytes, np.uint8).reshape(self.N, self.K // 2),
                 "scale": np.asarray(self._scale(scales, ("weight_scale", "scale")), dtype=np.float32).reshape(-1)}
 
@@ -311,6 +317,15 @@ _TENSORS = {"awq_int4_g128": (("qweight", 1), ("qzeros", 1), ("scales", 1)),
             "int4_sym_g128": (("weight", 0), ("weight_scale", None))}
 _ALIASES = {"fp8_b128": {"scale": "weight_scale_inv"}, "fp8_channel": {"scale": "weight_scale"},
             "int4_sym_g128": {"scale": "weight_scale"}}
+# the grouped forms of the per-channel formats (``ccut_b200.formats``): fp32 scales [in/128, out]
+_GROUPED = {"fp8_channel": (("weight", 0), ("scales", 1)), "int4_sym_g128": (("qweight", 1), ("scales", 1))}
+
+
+def _names(fmt: str, t: dict) -> tuple:
+    """Tensor names (and output-channel axes) of one matrix's checkpoint tensors ``t``."""
+    if fmt in _GROUPED and "scales" in t:
+        return _GROUPED[fmt]
+    return _TENSORS[fmt]
 
 
 class QuantLinear:
@@ -329,13 +344,14 @@ class QuantLinear:
         for alias, name in _ALIASES.get(fmt, {}).items():
             if name not in t and alias in t:
                 t[name] = t.pop(alias)
-        missing = [n for n, _ in _TENSORS[fmt] if n not in t]
+        names = _names(fmt, t)
+        missing = [n for n, _ in names if n not in t]
         if missing:
             raise ValueError(f"missing checkpoint tensors {missing}")
         self.fmt, self.in_features, self.out_features = fmt, int(in_features), int(out_features)
-        self.tensors = {n: t[n] for n, _ in _TENSORS[fmt]}
+        self.tensors = {n: t[n] for n, _ in names}
         self.method = make_method(fmt, self.in_features, self.out_features, layout=layout, device=device)
-        main = _TENSORS[fmt][0][0]
+        main = names[0][0]
         self._weight = self.tensors[main]
         self._scales = {n: v for n, v in self.tensors.items() if n != main}
         self.method._pack(self._weight, self._scales)
@@ -365,7 +381,7 @@ def cat_checkpoint_tensors(fmt: str, parts: list) -> dict:
     if fmt not in _TENSORS:
         raise NotImplementedError(f"weight format {fmt!r} is not supported")
     out = {}
-    for n, ax in _TENSORS[fmt]:
+    for n, ax in _names(fmt, parts[0]):
         arrs = [np.asarray(p[n]) for p in parts]
         if ax is None:
             if any(not np.array_equal(a, arrs[0]) for a in arrs[1:]):
@@ -383,12 +399,20 @@ def permute_out_channels(fmt: str, tensors: dict, perm) -> dict:
     in its 128-row scale block (``ValueError`` otherwise); signed int4 weight rows moved.  Byte
     moves only: the values dequantize to the permuted rows exactly."""
     perm = np.asarray(perm, np.int64)
-    if fmt == "awq_int4_g128":
+    if fmt == "awq_int4_g128" or (fmt == "int4_sym_g128" and "qweight" in tensors):
         n = tensors["scales"].shape[1]
         if perm.shape != (n,):
             raise ValueError(f"perm must have {n} entries")
-        return {"qweight": _awq_words(_awq_columns(tensors["qweight"])[:, perm]),
-                "qzeros": _awq_words(_awq_columns(tensors["qzeros"])[:, perm]),
+        out = {"qweight": _awq_words(_awq_columns(tensors["qweight"])[:, perm]),
+               "scales": np.ascontiguousarray(np.asarray(tensors["scales"])[:, perm])}
+        if "qzeros" in tensors:
+            out["qzeros"] = _awq_words(_awq_columns(tensors["qzeros"])[:, perm])
+        return out
+    if fmt == "fp8_channel" and "scales" in tensors:
+        w = np.asarray(tensors["weight"])
+        if perm.shape != (w.shape[0],):
+            raise ValueError(f"perm must have {w.shape[0]} entries")
+        return {"weight": np.ascontiguousarray(w[perm]),
                 "scales": np.ascontiguousarray(np.asarray(tensors["scales"])[:, perm])}
     if fmt in ("fp8_b128", "fp8_channel", "int4_sym_g128"):
         w = np.asarray(tensors["weight"])
@@ -410,6 +434,19 @@ def pad_out_channels(fmt: str, tensors: dict, out_features: int) -> dict:
     """The checkpoint tensors with zero output channels appended up to ``out_features`` (so
     that a matrix whose output size is not a multiple of 128 can be packed and dequantized;
     the padded channels dequantize to 0)."""
+    if fmt in ("int4_sym_g128", "fp8_channel") and "scales" in tensors:  # grouped forms: zero scales
+        s = np.asarray(tensors["scales"])
+        extra = out_features - s.shape[1]
+        if extra < 0 or (fmt == "int4_sym_g128" and (extra % 8 or s.shape[1] % 8)):
+            raise ValueError(f"cannot pad {s.shape[1]} output channels to {out_features}")
+        out = {"scales": np.concatenate([s, np.zeros((s.shape[0], extra), s.dtype)], axis=1)}
+        if fmt == "int4_sym_g128":
+            q = np.asarray(tensors["qweight"])
+            out["qweight"] = np.concatenate([q, np.full((q.shape[0], extra // 8), -0x77777778, np.int32)], axis=1)
+        else:
+            w = np.asarray(tensors["weight"])
+            out["weight"] = np.concatenate([w, np.zeros((extra, w.shape[1]), w.dtype)])
+        return out
     if fmt == "awq_int4_g128":
         s = np.asarray(tensors["scales"])
         extra = out_features - s.shape[1]

@@ -58,7 +58,21 @@ def _pack_sequential(cols: np.ndarray) -> np.ndarray:
 
 def ct_quant_config(fmt: str) -> dict:
     """A compressed-tensors ``quantization_config`` for ``fmt``: int4 group 128 weights
-    (``pack-quantized``, asymmetric) or FP8 128 x 128 block weights with dynamic activations."""
+    (``pack-quantized``, asymmetric for AWQ, symmetric for ``int4_sym_g128``), FP8 128 x 128
+    block weights with dynamic activations, or per-channel FP8 weights with per-token dynamic
+    activations (the reference's own checkpoints, ``ccut/quant/compressed_tensors.py:3-10``)."""
+    if fmt == "int4_sym_g128":
+        w = {"num_bits": 4, "type": "int", "symmetric": True, "strategy": "group", "group_size": 128,
+             "actorder": None}
+        return {"quant_method": "compressed-tensors", "format": "pack-quantized",
+                "config_groups": {"group_0": {"targets": ["Linear"], "weights": w, "input_activations": None}},
+                "ignore": ["lm_head", "re:.*mlp.gate$"]}
+    if fmt == "fp8_channel":
+        w = {"num_bits": 8, "type": "float", "symmetric": True, "strategy": "channel", "dynamic": False}
+        a = {"num_bits": 8, "type": "float", "symmetric": True, "strategy": "token", "dynamic": True}
+        return {"quant_method": "compressed-tensors", "format": "float-quantized",
+                "config_groups": {"group_0": {"targets": ["Linear"], "weights": w, "input_activations": a}},
+                "ignore": ["lm_head", "re:.*mlp.gate$"]}
     if fmt == "awq_int4_g128":
         w = {"num_bits": 4, "type": "int", "symmetric": False, "strategy": "group", "group_size": 128,
              "actorder": None}
@@ -84,6 +98,14 @@ def _ct_matrix_tensors(prefix: str, m) -> dict:
                 f"{prefix}.weight_zero_point": (None, np.ascontiguousarray(_pack_sequential(z).T)),
                 f"{prefix}.weight_scale": (None, np.ascontiguousarray(m.scales.T)),
                 f"{prefix}.weight_shape": (None, np.array([N, K], np.int64))}
+    if isinstance(m, inputs.Fp8ChannelMatrix):
+        return {f"{prefix}.weight": ("F8_E4M3", m.weight), f"{prefix}.weight_scale": (None, m.scale.reshape(-1, 1))}
+    if isinstance(m, inputs.Int4SymMatrix):  # signed v as v + 8, 8 per word along K; group scales [N, K/128]
+        v8 = formats.int4_sym_unpack(m.weight).astype(np.int16) + 8  # [N, K]
+        N, K = v8.shape
+        return {f"{prefix}.weight_packed": (None, _pack_sequential(v8.astype(np.uint8))),
+                f"{prefix}.weight_scale": (None, np.ascontiguousarray(np.repeat(m.scale[None, ::128], N, axis=0))),
+                f"{prefix}.weight_shape": (None, np.array([N, K], np.int64))}
     return {f"{prefix}.weight": ("F8_E4M3", m.weight), f"{prefix}.weight_scale": (None, m.scale)}
 
 
@@ -94,7 +116,11 @@ def merged_shared(lw):
     out = {}
     for proj in ("gate", "up", "down"):
         mats = [getattr(s, proj) for s in lw.shared]
-        if isinstance(mats[0], inputs.AwqMatrix):  # [in, out]: gate/up cat along out, down along in
+        if isinstance(mats[0], (inputs.Fp8ChannelMatrix, inputs.Int4SymMatrix)):
+            if len(mats) != 1:  # per-channel / per-column scales do not survive a merge along K
+                raise NotImplementedError("one shared expert for the per-channel formats")
+            out[proj] = mats[0]
+        elif isinstance(mats[0], inputs.AwqMatrix):  # [in, out]: gate/up cat along out, down along in
             ax = 1 if proj != "down" else 0
             out[proj] = inputs.AwqMatrix(*(np.concatenate([getattr(m, f) for m in mats], axis=ax)
                                            for f in ("qweight", "qzeros", "scales")))

@@ -126,6 +126,33 @@ def test_load_layer_weights_matches_the_written_layer(tmp_path, fmt, ct):
             assert np.array_equal(shared[0][proj][f], getattr(ms[proj], src.get(f, f)))
 
 
+@pytest.mark.parametrize("fmt", ["fp8_channel", "int4_sym_g128"])
+def test_load_compressed_tensors_channel_formats(tmp_path, fmt):
+    """compressed-tensors per-channel FP8 (the reference's own checkpoints) and symmetric int4
+    with fp32 group scales read back as tensors that dequantize to the written matrices."""
+    from ccut_b200 import formats as F
+    from oracle import formats
+
+    lw = _layer(fmt, shared=1)
+    root = write_checkpoint(tmp_path / "m", lw, layer=3, ct=True)
+    spec, router, experts, shared, bias = ck.load_layer_weights(root, 3)
+    assert spec.fmt == fmt and len(experts) == lw.cfg.num_experts and len(shared) == 1
+
+    def deq(t):  # fp32 [N, K] of a loaded matrix, through the canonical form
+        c = F.canonical(fmt, t)
+        if fmt == "fp8_channel":
+            return formats.fp8_e4m3_decode(c["weight"]) * np.repeat(c["scales"], 128, axis=0).T
+        q = formats.awq_unpack(c["qweight"]).astype(np.float32) - 8.0
+        return (q * np.repeat(c["scales"], 128, axis=0)).T
+
+    for e in (0, 5, 7):
+        for proj in ("gate", "up", "down"):
+            ref = inputs.dequant(getattr(lw.experts[e], proj)).T
+            assert np.array_equal(deq(experts[e][proj]).astype(np.float32), ref)
+    for proj in ("gate", "up", "down"):
+        assert np.array_equal(deq(shared[0][proj]).astype(np.float32), inputs.dequant(getattr(lw.shared[0], proj)).T)
+
+
 def test_load_errors(tmp_path):
     lw = _layer("fp8_b128")
     # a missing block scale

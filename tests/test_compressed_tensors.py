@@ -59,9 +59,13 @@ def test_compressed_tensors_config_resolution():
         grp["weights"] = {**grp["weights"], **w}
         return {**base, "quantization_config": q}
 
+    assert ck.quant_format({**base, "quantization_config": ct_quant_config("fp8_channel")}) == "fp8_channel"
+    assert ck.quant_format({**base, "quantization_config": ct_quant_config("int4_sym_g128")}) == "int4_sym_g128"
+    assert ck.quant_format(variant("fp8_b128", strategy="tensor")) == "fp8_channel"  # one scale for all channels
+    assert ck.quant_format(variant("fp8_b128", strategy="channel")) == "fp8_channel"
     for cfg in (variant("awq_int4_g128", group_size=64), variant("awq_int4_g128", strategy="channel"),
                 variant("awq_int4_g128", num_bits=8), variant("awq_int4_g128", actorder="group"),
-                variant("fp8_b128", strategy="channel"), variant("fp8_b128", block_structure=[64, 64])):
+                variant("fp8_b128", strategy="group"), variant("fp8_b128", block_structure=[64, 64])):
         with pytest.raises(NotImplementedError):
             ck.quant_format(cfg)
     q = ct_quant_config("awq_int4_g128")

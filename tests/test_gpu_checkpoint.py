@@ -25,11 +25,13 @@ def _cuda():
 
 @pytest.mark.parametrize("kernel", ["tc", "mma"])
 @pytest.mark.parametrize("fmt,mode,shared", [("awq_int4_g128", "softmax_topk", 2), ("fp8_b128", "topk_softmax", 1),
-                                             ("awq_int4_g128", "topk_softmax", 0)])
+                                             ("awq_int4_g128", "topk_softmax", 0), ("fp8_channel", "topk_softmax", 1),
+                                             ("int4_sym_g128", "softmax_topk", 1)])
 def test_checkpoint_layer_matches_in_memory_layer(tmp_path, fmt, mode, shared, kernel):
     cfg = small_cfg(fmt, mode, hidden=384, inter=256, experts=8, top_k=2, shared=shared)
     lw = inputs.make_layer(cfg, seed=31)
-    root = write_checkpoint(tmp_path / "m", lw, layer=7)
+    # the per-channel formats come in compressed-tensors checkpoints only
+    root = write_checkpoint(tmp_path / "m", lw, layer=7, ct=fmt in ("fp8_channel", "int4_sym_g128"))
     L = ck.load_moe_layer(root, 7, kernel=kernel)
     ref_layer = gpu_layer(lw, kernel=kernel)
     for T in (1, 9, 70):

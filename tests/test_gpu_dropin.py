@@ -81,6 +81,20 @@ def test_moe_combine_dropin_given_routing():
     out = moe_combine(x, ids, w, w_lookup=L)
     ref = moe.moe_combine(x, ids, w, lw.w_lookup)  # routed experts only, as in the reference
     assert rel_err_rows(out, ref) <= TOL
+    # a caller's expert function gets the exported (bit-exact) weights and the token rows;
+    # expert_outputs is accepted and not read, as in the reference
+    calls = []
+
+    def fn(rows, wg, wu, wd):
+        calls.append(rows.shape[0])
+        return moe.expert_ffn(rows, wg, wu, wd)
+
+    out_fn = moe_combine(x, ids, w, expert_outputs={0: None}, expert_fn=fn, w_lookup=L)
+    assert sum(calls) == ids.size and len(calls) == len(np.unique(ids))
+    assert rel_err_rows(out_fn, ref) <= 1e-5  # the same fp32 matrices: summation order only
+    out_t = moe_combine(torch.from_numpy(x).cuda(), torch.from_numpy(ids), torch.from_numpy(w), expert_fn=fn,
+                        w_lookup=L)
+    assert isinstance(out_t, torch.Tensor) and rel_err_rows(out_t.cpu().numpy(), ref) <= 1e-5
 
 
 @pytest.mark.parametrize("layout", ["frags", "rows"])
