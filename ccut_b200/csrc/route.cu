@@ -14,10 +14,10 @@
 
 namespace ccut {
 
-constexpr int kRtTok = 64;  // tokens per logits CTA
-constexpr int kRtExp = 64;  // experts per logits CTA
-constexpr int kRtH = 32;    // h per shared-memory chunk
-constexpr int kRtPad = 68;  // padded row (floats): 16-byte aligned float4 reads
+constexpr int kRtTok = 64;   // tokens per logits CTA
+constexpr int kRtExp = 64;   // experts per logits CTA
+constexpr int kRtH = 64;     // h per shared-memory chunk
+constexpr int kRtPitch = 72; // bf16 per staged row (64 + 8): conflict-free ldmatrix rows
 
 // Number of H splits: enough CTAs to cover the SMs at small T, one split at large T.
 int route_hsplit(int T, int E, int H) {
@@ -30,89 +30,110 @@ int route_hsplit(int T, int E, int H) {
   return hs;
 }
 
-// part[hs][t][e] = sum over this split's h of x[t, h] * router[e, h] (fp32).  Also zeroes
-// counts[E] and writes x16 (f16 copy of x) when requested.
+// fp32 -> (hi, mid, lo) bf16 with hi + mid + lo == w exactly: each part keeps the next 8
+// significant bits of the remainder (bf16 has fp32's exponent range).
+__device__ __forceinline__ void split3_bf16(float w, uint16_t& hi, uint16_t& mid, uint16_t& lo) {
+  const __nv_bfloat16 h = __float2bfloat16_rn(w);
+  const float r1 = w - __bfloat162float(h);
+  const __nv_bfloat16 m = __float2bfloat16_rn(r1);
+  const __nv_bfloat16 l = __float2bfloat16_rn(r1 - __bfloat162float(m));
+  hi = __bfloat16_as_ushort(h);
+  mid = __bfloat16_as_ushort(m);
+  lo = __bfloat16_as_ushort(l);
+}
+
+// part[hs][t][e] = sum over this split's h of x[t, h] * router[e, h] (fp32) on the tensor
+// cores: the bf16 activations are exact operands and each fp32 router weight is the exact sum
+// of three bf16 parts, so every product is exact and only the fp32 accumulation rounds, as in
+// an fp32 GEMM.  CTA tile 64 tokens x 64 experts; warp w owns tokens 16 (w & 3) .. + 15 and
+// experts 32 (w >> 2) .. + 31 (four m16n8k16 column tiles, three MMAs each per 16-h step).
+// Also zeroes counts[E] and writes x16 (f16 copy of x) when requested.
 __global__ void __launch_bounds__(256) route_logits_kernel(const uint16_t* __restrict__ x,
                                                            const float* __restrict__ router, int T, int H, int E,
                                                            int hsplit, float* __restrict__ part,
                                                            int* __restrict__ counts, uint16_t* __restrict__ x16) {
   pdl_wait();
   pdl_trigger();
-  __shared__ __align__(16) float xs[kRtH][kRtPad];  // [h][token]
-  __shared__ __align__(16) float ws[kRtH][kRtPad];  // [h][expert]
+  __shared__ __align__(16) uint16_t xs[kRtTok * kRtPitch];     // [token][h]
+  __shared__ __align__(16) uint16_t ws[3][kRtExp * kRtPitch];  // [part][expert][h]
   const int t0 = blockIdx.x * kRtTok, e0 = blockIdx.y * kRtExp, hs = blockIdx.z;
   const int hlen = H / hsplit, hbeg = hs * hlen;
-  const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (counts && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
     for (int e = tid; e < E; e += blockDim.x) counts[e] = 0;
+  const int tg = warp & 3, eh = warp >> 2;
   float acc[4][4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int j = 0; j < 4; ++j)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
-  const int lr = tid >> 2, lseg = tid & 3;  // loader: row (token / expert), 8-wide h segment
+    for (int i = 0; i < 4; ++i) acc[j][i] = 0.f;
   for (int h0 = hbeg; h0 < hbeg + hlen; h0 += kRtH) {
-    {
-      const int t = t0 + lr;
-      float v[8];
-      if (t < T) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(x + (size_t)t * H + h0 + lseg * 8);
-        const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+    // activations: 64 rows x 8 chunks of 8 bf16, two chunks per thread
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          v[2 * j] = __uint_as_float(w4[j] << 16);
-          v[2 * j + 1] = __uint_as_float(w4[j] & 0xffff0000u);
-        }
+    for (int i = 0; i < 2; ++i) {
+      const int c = tid + 256 * i, row = c >> 3, seg = c & 7;
+      const int t = t0 + row;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (t < T) {
+        v = *reinterpret_cast<const uint4*>(x + (size_t)t * H + h0 + seg * 8);
         if (x16 && blockIdx.y == 0) {
+          const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
           uint32_t o[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const __half2 hh = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+            const __half2 hh = __floats2half2_rn(__uint_as_float(w4[j] << 16), __uint_as_float(w4[j] & 0xffff0000u));
             o[j] = *reinterpret_cast<const uint32_t*>(&hh);
           }
-          *reinterpret_cast<uint4*>(x16 + (size_t)t * H + h0 + lseg * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+          *reinterpret_cast<uint4*>(x16 + (size_t)t * H + h0 + seg * 8) = make_uint4(o[0], o[1], o[2], o[3]);
         }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = 0.f;
       }
+      *reinterpret_cast<uint4*>(xs + row * kRtPitch + seg * 8) = v;
+    }
+    // router: 64 rows x 16 float4, four per thread, each split into three bf16 parts
 #pragma unroll
-      for (int j = 0; j < 8; ++j) xs[lseg * 8 + j][lr] = v[j];
-      const int e = e0 + lr;
-      float w[8];
-      if (e < E) {
-        const float4 a = *reinterpret_cast<const float4*>(router + (size_t)e * H + h0 + lseg * 8);
-        const float4 b = *reinterpret_cast<const float4*>(router + (size_t)e * H + h0 + lseg * 8 + 4);
-        w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w; w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
-      } else {
+    for (int i = 0; i < 4; ++i) {
+      const int c = tid + 256 * i, row = c >> 4, seg = c & 15;
+      const int e = e0 + row;
+      float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (e < E) w = __ldg(reinterpret_cast<const float4*>(router + (size_t)e * H + h0 + seg * 4));
+      const float wa[4] = {w.x, w.y, w.z, w.w};
+      uint16_t p[3][4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) w[j] = 0.f;
-      }
+      for (int j = 0; j < 4; ++j) split3_bf16(wa[j], p[0][j], p[1][j], p[2][j]);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) ws[lseg * 8 + j][lr] = w[j];
+      for (int s = 0; s < 3; ++s)
+        *reinterpret_cast<uint2*>(ws[s] + row * kRtPitch + seg * 4) =
+            make_uint2(p[s][0] | (uint32_t)p[s][1] << 16, p[s][2] | (uint32_t)p[s][3] << 16);
     }
     __syncthreads();
-#pragma unroll 8
-    for (int h = 0; h < kRtH; ++h) {
-      const float4 xv = *reinterpret_cast<const float4*>(&xs[h][ty * 4]);
-      const float4 wv = *reinterpret_cast<const float4*>(&ws[h][tx * 4]);
-      const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
-      const float wa[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+    for (int ks = 0; ks < kRtH / 16; ++ks) {
+      uint32_t a[4];
+      ldmatrix_x4(a[0], a[1], a[2], a[3],
+                  xs + (tg * 16 + ((lane >> 3) & 1) * 8 + (lane & 7)) * kRtPitch + ks * 16 + (lane >> 4) * 8);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xa[i], wa[j], acc[i][j]);
+      for (int s = 0; s < 3; ++s) {
+#pragma unroll
+        for (int j = 0; j < 4; j += 2) {  // column tiles j, j + 1
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4(b0, b1, b2, b3,
+                      ws[s] + (eh * 32 + (j + (lane >> 4)) * 8 + (lane & 7)) * kRtPitch + ks * 16 +
+                          ((lane >> 3) & 1) * 8);
+          mma_16816<true>(acc[j], a, b0, b1);
+          mma_16816<true>(acc[j + 1], a, b2, b3);
+        }
+      }
     }
     __syncthreads();
   }
+  const int g = lane >> 2, c2 = 2 * (lane & 3);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int t = t0 + ty * 4 + i;
-    if (t >= T) continue;
+  for (int j = 0; j < 4; ++j) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int e = e0 + tx * 4 + j;
-      if (e < E) part[((size_t)hs * T + t) * E + e] = acc[i][j];
+    for (int i = 0; i < 4; ++i) {
+      const int t = t0 + tg * 16 + g + 8 * (i >> 1);
+      const int e = e0 + eh * 32 + j * 8 + c2 + (i & 1);
+      if (t < T && e < E) part[((size_t)hs * T + t) * E + e] = acc[j][i];
     }
   }
 }
