@@ -185,8 +185,9 @@ int run_gate_up(const ccut_moe_layer* L, long per_expert, const uint16_t* x, con
   return launch_gemm(fmt, kFfn1, pick_mt(per_expert), a, num_sms(), st);
 }
 
+// down: weighted rows y [R, H], fp32 or (y_bf16) bf16.
 int run_down(const ccut_moe_layer* L, long per_expert, const uint16_t* hbuf, int T, int k, const int32_t* offsets,
-             const float* row_weight, float* y_rows, int* sched, int* status, cudaStream_t st) {
+             const float* row_weight, void* y_rows, int y_bf16, int* sched, int* status, cudaStream_t st) {
   const int fmt = L->format;
   const int ne = L->num_experts + L->num_shared_slices;
   if (use_tc(L, per_expert)) {
@@ -195,7 +196,7 @@ int run_down(const ccut_moe_layer* L, long per_expert, const uint16_t* hbuf, int
     int rc = encode_rows_map(&map, hbuf, R, L->inter, kTcBoxRows);
     if (rc) return rc;
     TcArgs a{static_cast<const uint8_t*>(L->w2), ccut_w2_bytes(fmt, L->hidden, L->inter), L->inter, L->hidden,
-             offsets, ne, y_rows, L->hidden, row_weight, status};
+             offsets, ne, y_rows, L->hidden, row_weight, status, y_bf16};
     return launch_tc_gemm(fmt, kFfn2, map, a, num_sms(), st);
   }
   GemmArgs a{static_cast<const uint8_t*>(L->w2_frags),
@@ -211,16 +212,17 @@ int run_down(const ccut_moe_layer* L, long per_expert, const uint16_t* hbuf, int
              L->hidden,
              row_weight,
              status};
+  a.out_bf16 = y_bf16;
   set_sched(a, sched);
   return launch_gemm(fmt, kFfn2, pick_mt(per_expert), a, num_sms(), st);
 }
 
 int run_ffn(const ccut_moe_layer* L, long per_expert, const uint16_t* x, const FfnScratch& s, int T, int k,
-            const int32_t* offsets,
-            const int32_t* row_token, const float* row_weight, float* y_rows, int* status, cudaStream_t st) {
+            const int32_t* offsets, const int32_t* row_token, const float* row_weight, void* y_rows, int y_bf16,
+            int* status, cudaStream_t st) {
   int rc = run_gate_up(L, per_expert, x, s.x16, s.xp, T, k, offsets, row_token, s.hbuf, s.sched, status, st);
   if (rc) return rc;
-  return run_down(L, per_expert, s.hbuf, T, k, offsets, row_weight, y_rows, s.sched, status, st);
+  return run_down(L, per_expert, s.hbuf, T, k, offsets, row_weight, y_rows, y_bf16, s.sched, status, st);
 }
 
 // The bounded waits of the kernels, exercised on barriers with a known outcome: barrier 0
@@ -392,7 +394,7 @@ int ccut_moe_expert_ffn(const ccut_moe_layer* L, const uint16_t* x, int T, int k
     rc = launch_bf16_to_f16(x, s.x16, (size_t)T * L->hidden, stream);
     if (rc) return rc;
   }
-  return run_ffn(L, mean_rows(L, T, k), x, s, T, k, offsets, row_token, row_weight, y_rows, status, stream);
+  return run_ffn(L, mean_rows(L, T, k), x, s, T, k, offsets, row_token, row_weight, y_rows, 0, status, stream);
 }
 
 int ccut_moe_expert_ffn_w4a16(const ccut_moe_layer* L, const uint16_t* x, int T, int k, const int32_t* offsets,
@@ -472,7 +474,7 @@ int ccut_moe_down(const ccut_moe_layer* L, const uint16_t* h_rows, int T, int k,
     c.take<int>(64);
     sched = take_sched(c);
   }
-  return run_down(L, mean_rows(L, T, k), h_rows, T, k, offsets, row_weight, y_rows, sched,
+  return run_down(L, mean_rows(L, T, k), h_rows, T, k, offsets, row_weight, y_rows, 0, sched,
                   static_cast<int*>(workspace), stream);
 }
 
@@ -484,7 +486,7 @@ int ccut_moe_combine(const float* y_rows, const int32_t* pair_row, int T, int k,
   if (out_dtype != CCUT_OUT_BF16 && out_dtype != CCUT_OUT_F32) return CCUT_ERR_INVALID;
   if (T == 0) return CCUT_OK;
   if (!y_rows || !pair_row || !out) return CCUT_ERR_INVALID;
-  return launch_combine(y_rows, pair_row, T, k, H, num_shared_slices, -1, out, out_dtype, stream);
+  return launch_combine(y_rows, 0, pair_row, T, k, H, num_shared_slices, -1, out, out_dtype, stream);
 }
 
 size_t ccut_moe_forward_workspace_bytes(const ccut_moe_layer* L, int T, int top_k) {
@@ -519,9 +521,13 @@ int ccut_moe_forward(const ccut_moe_layer* L, const ccut_route_params* rp, const
   rc = launch_permute(s.ids, s.wts, T, k, E, L->num_shared_slices, L->shared_gate, s.counts, s.offsets, s.row_token,
                       s.row_weight, s.pair_row, st);
   if (rc) return rc;
-  rc = run_ffn(L, mean_rows(L, T, k), x, s.ffn, T, k, s.offsets, s.row_token, s.row_weight, s.ybuf, s.status, st);
+  // bf16 output: the weighted rows go through bf16 (one rounding each, half the bytes of
+  // the down GEMM's writes and the combine's reads); fp32 output keeps fp32 rows
+  const int y_bf16 = out_dtype == CCUT_OUT_BF16;
+  rc = run_ffn(L, mean_rows(L, T, k), x, s.ffn, T, k, s.offsets, s.row_token, s.row_weight, s.ybuf, y_bf16, s.status,
+               st);
   if (rc) return rc;
-  rc = launch_combine(s.ybuf, s.pair_row, T, k, H, L->num_shared_slices, -1, out, out_dtype, st);
+  rc = launch_combine(s.ybuf, y_bf16, s.pair_row, T, k, H, L->num_shared_slices, -1, out, out_dtype, st);
   if (rc) return rc;
   if (ids && cudaMemcpyAsync(ids, s.ids, sizeof(int32_t) * (size_t)T * k, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
     return CCUT_ERR_CUDA;

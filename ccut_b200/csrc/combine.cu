@@ -1,7 +1,9 @@
 // combine.cu -- weighted un-permute: out[t] = sum_j y[pair_row[t, j]] + sum_s y[shared row].
 //
 // The rows already carry their routing weight (applied in the down-projection epilogue),
-// so this is a fixed-order fp32 sum per token: deterministic, no atomics.  Follows the
+// so this is a fixed-order fp32 sum per token: deterministic, no atomics.  The rows are
+// fp32, or bf16 when the fused forward produces a bf16 output (one rounding of each
+// weighted row, half the bytes written by the down GEMM and read here).  Follows the
 // scatter-add of ccut/models/generic.py:377-378 and the shared-expert add of
 // ccut/models/generic.py:380-385.
 #include "launch.cuh"
@@ -15,8 +17,8 @@ constexpr int kCombMaxRows = 16 + CCUT_MAX_SHARED_SLICES;  // top-k + shared sli
 // One CTA per (token, 1024-column chunk).  The token's source rows are staged in shared
 // memory first, so every lane's row loads are independent of one another; the sum runs in
 // the fixed order j = 0..k-1, then the shared slices.
-template <bool kBf16Out>
-__global__ void __launch_bounds__(kCombThreads) combine_kernel(const float* __restrict__ y,
+template <bool kBf16In, bool kBf16Out>
+__global__ void __launch_bounds__(kCombThreads) combine_kernel(const void* __restrict__ y,
                                                                const int32_t* __restrict__ pair_row, int T, int k,
                                                                int H, int slices, int shared_base,
                                                                void* __restrict__ out) {
@@ -36,13 +38,19 @@ __global__ void __launch_bounds__(kCombThreads) combine_kernel(const float* __re
   const int h4n = H / 4;
   const int h4 = blockIdx.y * kCombThreads + threadIdx.x;
   if (h4 >= h4n) return;
-  const float4* y4 = reinterpret_cast<const float4*>(y);
   float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4
   for (int j = 0; j < n; ++j) {
     const int p = rows[j];
     if (p >= 0) {
-      const float4 v = y4[(size_t)p * h4n + h4];
+      float4 v;
+      if constexpr (kBf16In) {  // 4 bf16 -> fp32 (exact)
+        const uint2 u = reinterpret_cast<const uint2*>(y)[(size_t)p * h4n + h4];
+        v = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
+                        __uint_as_float(u.y & 0xffff0000u));
+      } else {
+        v = reinterpret_cast<const float4*>(y)[(size_t)p * h4n + h4];
+      }
       s.x += v.x;
       s.y += v.y;
       s.z += v.z;
@@ -61,14 +69,17 @@ __global__ void __launch_bounds__(kCombThreads) combine_kernel(const float* __re
   }
 }
 
-int launch_combine(const float* y, const int32_t* pair_row, int T, int k, int H, int slices, int shared_base,
+// y: the weighted rows, fp32 or (y_bf16) bf16.
+int launch_combine(const void* y, int y_bf16, const int32_t* pair_row, int T, int k, int H, int slices, int shared_base,
                    void* out, int out_dtype, cudaStream_t st) {
   if (k < 1 || slices < 0 || k + slices > kCombMaxRows || H % 4) return CCUT_ERR_UNSUPPORTED;
   if (T == 0) return CCUT_OK;
   if (shared_base < 0) shared_base = T * k;
   const dim3 grid(T, (H / 4 + kCombThreads - 1) / kCombThreads);
-  return launch_k(out_dtype == CCUT_OUT_BF16 ? combine_kernel<true> : combine_kernel<false>, grid, dim3(kCombThreads),
-                  0, st, y, pair_row, T, k, H, slices, shared_base, out);
+  const bool bo = out_dtype == CCUT_OUT_BF16;
+  auto kern = y_bf16 ? (bo ? combine_kernel<true, true> : combine_kernel<true, false>)
+                     : (bo ? combine_kernel<false, true> : combine_kernel<false, false>);
+  return launch_k(kern, grid, dim3(kCombThreads), 0, st, y, pair_row, T, k, H, slices, shared_base, out);
 }
 
 // bf16 -> f16 copy (FP8 path operands are f16).

@@ -543,9 +543,9 @@ int ccut_moe_ep_forward(ccut_ep* ep, const ccut_moe_layer* L, int expert_lo, int
       if (rc) return rc;
     }
     rc = run_ffn(&sv, T_local, x, s.sh_ffn, T_local, 1, s.sh_offsets, s.sh_row_token, s.sh_row_weight, s.sh_ybuf,
-                 status, ss);
+                 0, status, ss);
     if (rc) return rc;
-    rc = launch_combine(s.sh_ybuf, s.sh_pair_row, T_local, 1, H, S, 0, s.y_sh, CCUT_OUT_F32, ss);
+    rc = launch_combine(s.sh_ybuf, 0, s.sh_pair_row, T_local, 1, H, S, 0, s.y_sh, CCUT_OUT_F32, ss);
     if (rc) return rc;
     if (cudaEventRecord(ep->join, ss) != cudaSuccess) return CCUT_ERR_CUDA;
   }
@@ -574,9 +574,10 @@ int ccut_moe_ep_forward(ccut_ep* ep, const ccut_moe_layer* L, int expert_lo, int
       rc = launch_bf16_to_f16(s.x_recv, s.ffn.x16, (size_t)R * H, st);
       if (rc) return rc;
     }
-    rc = run_ffn(&rv, per_expert, s.x_recv, s.ffn, R, k, s.offsets, s.row_token, s.row_weight, s.ybuf, status, st);
+    // the partial rows return in bf16, so the weighted rows are bf16 too
+    rc = run_ffn(&rv, per_expert, s.x_recv, s.ffn, R, k, s.offsets, s.row_token, s.row_weight, s.ybuf, 1, status, st);
     if (rc) return rc;
-    rc = launch_combine(s.ybuf, s.pair_row, R, k, H, 0, -1, s.y_recv, CCUT_OUT_BF16, st);
+    rc = launch_combine(s.ybuf, 1, s.pair_row, R, k, H, 0, -1, s.y_recv, CCUT_OUT_BF16, st);
     if (rc) return rc;
   }
   // 6. partial rows back to their owners

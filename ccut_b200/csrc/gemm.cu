@@ -381,7 +381,10 @@ __global__ void __launch_bounds__(GemmCfg<FMT, MODE, MT>::kThreads, GemmCfg<FMT,
             static_cast<uint16_t*>(a.out)[o] = hv;
           } else {
             const float wr = a.row_weight ? a.row_weight[row0 + tok] : 1.f;
-            static_cast<float*>(a.out)[o] = acc[0][b][i] * wr;
+            if (a.out_bf16)
+              static_cast<uint16_t*>(a.out)[o] = __bfloat16_as_ushort(__float2bfloat16_rn(acc[0][b][i] * wr));
+            else
+              static_cast<float*>(a.out)[o] = acc[0][b][i] * wr;
           }
         }
       }

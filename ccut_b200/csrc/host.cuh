@@ -53,9 +53,9 @@ size_t rows_of(const ccut_moe_layer* L, int T, int k);
 // sched: this FFN's GEMM work counters (take_sched), or null for the static schedule.
 FfnScratch carve_ffn(Carver& c, const ccut_moe_layer* L, int T, int k, bool with_input, int* sched);
 // gate/up then down over the rows of a permutation; x16 must already hold x in f16 when
-// the mma.sync kernel runs.
+// the mma.sync kernel runs.  y_rows: the weighted rows, fp32 or (y_bf16) bf16.
 int run_ffn(const ccut_moe_layer* L, long per_expert, const uint16_t* x, const FfnScratch& s, int T, int k,
-            const int32_t* offsets, const int32_t* row_token, const float* row_weight, float* y_rows, int* status,
-            cudaStream_t st);
+            const int32_t* offsets, const int32_t* row_token, const float* row_weight, void* y_rows, int y_bf16,
+            int* status, cudaStream_t st);
 
 }  // namespace ccut

@@ -24,6 +24,7 @@ struct GemmArgs {
   // Dynamic scheduling (gemm.cu): sched[0] hands out work items, sched[1] counts the CTAs
   // done; both zero on entry, left zero on exit.  Null: static item striding.
   int* sched;
+  int out_bf16 = 0;  // FFN2: weighted rows as bf16 (one rounding) instead of fp32
 };
 
 // Arguments of the tcgen05 grouped GEMM (tc_gemm.cu); the activation operand arrives
@@ -38,6 +39,7 @@ struct TcArgs {
   int out_ld;
   const float* row_weight;
   int* status;
+  int out_bf16 = 0;  // FFN2: weighted rows as bf16 (one rounding) instead of fp32
 };
 
 // tc_gemm.cu: the activation operand `map` covers bf16 rows [R, K] in expert order (boxes
@@ -72,7 +74,7 @@ int launch_count(const int32_t* ids, int n, int E, int* counts, cudaStream_t st)
 int launch_gemm(int fmt, int mode, int mt, const GemmArgs& a, int num_sms, cudaStream_t st);
 // combine.cu
 // shared rows of slice s sit at shared_base + s * T (shared_base < 0: T * k)
-int launch_combine(const float* y, const int32_t* pair_row, int T, int k, int H, int slices, int shared_base,
+int launch_combine(const void* y, int y_bf16, const int32_t* pair_row, int T, int k, int H, int slices, int shared_base,
                    void* out, int out_dtype, cudaStream_t st);
 int launch_bf16_to_f16(const uint16_t* in, uint16_t* out, size_t n, cudaStream_t st);
 int launch_fill_offsets(int32_t* off, int m, cudaStream_t st);

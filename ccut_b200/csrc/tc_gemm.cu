@@ -73,7 +73,8 @@ struct TcCfg {
   static constexpr int kNBar = 2 * kSW + 2 * kSA + 2 + 2 + 1;
   static constexpr int kHeader = kNBar * 8 + 16 + 4 * (kMaxExperts + 1);
   static constexpr int kXchgOff = (kHeader + 1023) / 1024 * 1024;
-  static constexpr int kABOff = kXchgOff + (kXchg + 1023) / 1024 * 1024;  // 1024-aligned tiles
+  static constexpr int kRowWOff = kXchgOff + kXchg;   // FFN2: routing weights of the item's 256 tokens
+  static constexpr int kABOff = kXchgOff + (kXchg + 256 * 4 + 1023) / 1024 * 1024;  // 1024-aligned tiles
   static constexpr int kWOff = kABOff + kSA * kAB;
   static constexpr int kSmem = kWOff + kSW * kWBytes + 1024;  // +1024: runtime alignment slack
   static_assert(kSmem <= 227 * 1024, "shared memory budget");
@@ -406,6 +407,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
     const int r = q * 32 + lane;      // weight row of this thread
     const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ewg * 128);
     float* xb = xchg + ewg * 128 * C::kXRow;
+    float* wsm = reinterpret_cast<float*>(smem + C::kRowWOff) + ewg * 128;  // FFN2: weights of the WG's tokens
     const uint32_t pe0 = tc::mapa(&pempty[0], 0), pe1 = tc::mapa(&pempty[1], 0);
     int j = 0;
     bool ok = true;
@@ -416,6 +418,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
       const bool valid = blk < ntiles;
       const int ncols = max(0, min(128, n - ewg * 128));
       const uint8_t* wb = a.w + (size_t)e * a.expert_stride + (size_t)(valid ? blk : 0) * ktiles * BK::kBytes;
+      const int row0 = a.offsets[e] + m0;
+      // FFN2: this thread's token's routing weight, loaded now so that its latency passes
+      // under the item's k loop (staged through shared memory for the output phase)
+      float my_wr = 1.f;
+      if constexpr (MODE == kFfn2)
+        if (valid && a.row_weight && ewg * 128 + r < rows) my_wr = __ldg(a.row_weight + row0 + ewg * 128 + r);
       float tot[128];
 #pragma unroll
       for (int i = 0; i < 128; ++i) tot[i] = 0.f;
@@ -455,28 +463,47 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
       // one token and stores them as one 16-byte vector.  FFN2: the chunk is staged token-major
       // and each warp writes whole token rows, lane l channels 4l .. 4l + 3, so that one store
       // instruction covers 512 contiguous bytes of one output row.
-      const int row0 = a.offsets[e] + m0;
+      if constexpr (MODE == kFfn2) wsm[r] = my_wr;  // read after the first chunk's barrier
       const int tt = threadIdx.x & 15;          // FFN1: token of the chunk this thread writes out
       const int grp = (threadIdx.x >> 4) & 7;   // FFN1: channel group of this thread
 #pragma unroll
       for (int c = 0; c < 128; c += 16) {
         if (c < ncols) {  // uniform over the warpgroup
           if constexpr (MODE == kFfn2) {
+            if (a.out_bf16) {  // uniform: staged token-major, each warp writes 4 tokens' 256-byte rows
 #pragma unroll
-            for (int i = 0; i < 16; ++i) xb[i * C::kTokPitch + r] = tot[c + i];
-            named_bar(1 + ewg, 128);
+              for (int i = 0; i < 16; ++i) xb[i * C::kTokPitch + r] = tot[c + i];
+              named_bar(1 + ewg, 128);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int tl = q * 4 + j;            // token of the chunk (uniform over the warp)
-              const int tok = ewg * 128 + c + tl;  // token index inside the tile
-              if (tok < rows) {
-                const float wr = a.row_weight ? __ldg(a.row_weight + row0 + tok) : 1.f;
-                const float4 v = *reinterpret_cast<const float4*>(xb + tl * C::kTokPitch + 4 * lane);
-                float* orow = static_cast<float*>(a.out) + (size_t)(row0 + tok) * a.out_ld + blk * kTileN + 4 * lane;
-                *reinterpret_cast<float4*>(orow) = make_float4(v.x * wr, v.y * wr, v.z * wr, v.w * wr);
+              for (int j = 0; j < 4; ++j) {
+                const int tl = q * 4 + j;  // token of the chunk (uniform over the warp)
+                if (ewg * 128 + c + tl < rows) {
+                  const float wr = wsm[c + tl];
+                  const float4 v = *reinterpret_cast<const float4*>(xb + tl * C::kTokPitch + 4 * lane);
+                  const __nv_bfloat162 h0 = __floats2bfloat162_rn(v.x * wr, v.y * wr);
+                  const __nv_bfloat162 h1 = __floats2bfloat162_rn(v.z * wr, v.w * wr);
+                  uint16_t* orow = static_cast<uint16_t*>(a.out) + (size_t)(row0 + ewg * 128 + c + tl) * a.out_ld +
+                                   blk * kTileN + 4 * lane;
+                  *reinterpret_cast<uint2*>(orow) =
+                      make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
+                }
               }
+              named_bar(1 + ewg, 128);
+              continue;
             }
-            named_bar(1 + ewg, 128);
+            // fp32 straight from the registers: for each token the warp's 32 lanes hold 32
+            // consecutive channels, so one 4-byte store per lane writes a whole 128-byte line
+            if (c == 0) named_bar(1 + ewg, 128);  // the item's routing weights are staged
+            float* orow = static_cast<float*>(a.out) + (size_t)(row0 + ewg * 128 + c) * a.out_ld + blk * kTileN + r;
+#pragma unroll
+            for (int i = 0; i < 16; i += 4) {
+              const float4 wr = *reinterpret_cast<const float4*>(wsm + c + i);
+              const float w4[4] = {wr.x, wr.y, wr.z, wr.w};
+#pragma unroll
+              for (int u = 0; u < 4; ++u)
+                if (ewg * 128 + c + i + u < rows) orow[(size_t)(i + u) * a.out_ld] = tot[c + i + u] * w4[u];
+            }
+            if (c + 16 >= ncols) named_bar(1 + ewg, 128);  // weights read before the next item's
           } else {
 #pragma unroll
             for (int i = 0; i < 16; ++i) xb[r * C::kXRow + i] = tot[c + i];

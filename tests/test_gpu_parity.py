@@ -202,7 +202,7 @@ def test_forward_matches_oracle(fmt, mode, E, k, S, H, I, Ts, kernel):
         ref_same, _, _ = oracle_forward(lw, xb, ids=ids, weights=w)
         err = rel_err_rows(out.cpu().numpy(), ref_same)
         assert err <= TOL, f"T={T}: max row rel err {err:.3e}"
-        # bf16 output is the rounded fp32 one
+        # bf16 output (the weighted rows pass through bf16 once before the fp32 sum)
         outb = L.forward(x_device(xb)).float().cpu().numpy()
         assert rel_err_rows(outb, ref_same) <= TOL
     assert L.workspace_status() == 0
