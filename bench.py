@@ -193,15 +193,28 @@ def run_reference(args, wl) -> None:
     for _ in range(max(0, min(args.warmup, 1))):
         cpu_sample_run(cfg_name, T, min(sample, 8), 1, 60)
     r = cpu_sample_run(cfg_name, T, sample, args.steps, float("inf"))  # exactly K calls
+    # the same config as our arm's line at this N (the same total batch; run here on rank 0's
+    # host cores)
+    n = max(1, args.gpus)
+    cfgd = workload_config(wl, 1, "single" if n == 1 else f"ep{n}")
+    if n > 1:
+        cfgd["tokens_per_gpu"] = T // n
+        cfgd["experts_per_gpu"] = _layer_config(cfg_name).num_experts // n
     line = {
         "impl": "reference", "metric": METRIC, "value": r["value"], "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": r["steps_run"], "warmup": args.warmup, "ms_per_step": sample / r["value"] * 1000.0,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": workload_config(wl, args.gpus, parallelism="host cores"),
+        "higher_is_better": True, "scaling": "weak" if n == 1 else "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": cfgd, "reference_run": "the whole batch on the host cores of rank 0",
         "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": r["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def _layer_config(name: str):
+    from ccut_b200.synthetic import CONFIGS
+
+    return CONFIGS[name]
 
 
 def workload_config(wl: str, n: int, parallelism: str) -> dict:

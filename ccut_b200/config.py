@@ -2,11 +2,14 @@
 ``engine.toml:26-42``) read for this path.
 
 - ``[quant]``: ``quantization = "auto"`` takes the format from the checkpoint's
-  ``quantization_config`` (AWQ int4 g128 or FP8 e4m3 128 x 128 blocks); the online
-  quantization shorthands (``fp8_per_token``, ``mxfp8``, ...) are formats this path does not
-  run.  ``fp8_compute_mode = "w8a16"`` is what the kernels do (weights dequantized, activations
-  in 16 bits); ``w8a8`` is refused.  ``kv_cache_dtype``: ``auto`` / ``bf16`` (the decoder's
-  caches are bf16); ``fp8`` is refused.  ``quant_ignore`` applies to online quantization only.
+  ``quantization_config`` (AWQ int4 g128, FP8 e4m3 128 x 128 blocks or per channel, signed
+  int4); the online quantization shorthands (``fp8_per_token``, ``mxfp8``, ...) are formats
+  this path does not run.  ``fp8_compute_mode``: ``w8a16`` is what the kernels do (exact
+  weight codes, activations in 16 bits); ``w8a8`` is accepted and computed the same way, as
+  the reference computes it (its ``_w8a8`` dequantizes the weights and multiplies the
+  unquantized activations, ``ccut/quant/method.py:131-139``).  ``kv_cache_dtype``: ``auto`` /
+  ``bf16`` (the decoder's caches are bf16); ``fp8`` is refused.  ``quant_ignore`` applies to
+  online quantization only.
 - ``[experts]``: the reference streams experts from disk (``expert_residency = "zero"`` or
   ``"page_cache_only"``, a ring of ``expert_ring_slots``); here every expert is packed into HBM
   once.  ``expert_residency`` takes this path's own value ``"hbm"`` (the default) besides the
@@ -49,17 +52,14 @@ def quant_settings(app_config, checkpoint_config: dict) -> dict:
     if quantization != "auto":
         raise ValueError(f"[quant] quantization = {quantization!r} is not one of auto, {', '.join(_ONLINE)}")
     mode = str(q.get("fp8_compute_mode", "w8a16"))
-    if mode == "w8a8":
-        raise NotImplementedError("fp8_compute_mode = \"w8a8\": the kernels dequantize the weights and keep 16-bit "
-                                  "activations (w8a16)")
-    if mode != "w8a16":
+    if mode not in ("w8a16", "w8a8"):
         raise ValueError(f"[quant] fp8_compute_mode = {mode!r} is not one of w8a16, w8a8")
     kv = str(q.get("kv_cache_dtype", "auto"))
     if kv == "fp8":
         raise NotImplementedError("kv_cache_dtype = \"fp8\": the decoder's kv caches are bf16")
     if kv not in ("auto", "bf16"):
         raise ValueError(f"[quant] kv_cache_dtype = {kv!r} is not one of auto, bf16, fp8")
-    return {"format": quant_format(checkpoint_config), "fp8_compute_mode": "w8a16", "kv_cache_dtype": "bf16"}
+    return {"format": quant_format(checkpoint_config), "fp8_compute_mode": mode, "kv_cache_dtype": "bf16"}
 
 
 def expert_settings(app_config) -> dict:

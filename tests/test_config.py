@@ -20,6 +20,8 @@ def test_defaults_and_checkpoint_format():
     assert r["format"] == "awq_int4_g128" and r["kv_cache_dtype"] == "bf16" and r["residency"] == "hbm"
     assert config.resolve(None, FP8)["format"] == "fp8_b128"
     assert config.quant_settings({"quant": {"kv_cache_dtype": "bf16"}}, FP8)["format"] == "fp8_b128"
+    # the reference computes its w8a8 label as w8a16 (dequantized weights, 16-bit activations)
+    assert config.quant_settings({"quant": {"fp8_compute_mode": "w8a8"}}, FP8)["fp8_compute_mode"] == "w8a8"
     assert config.expert_settings({"experts": {"expert_residency": "page_cache_only", "expert_ring_slots": 8}})[
         "expert_ring_slots"] == 8
 
@@ -27,7 +29,6 @@ def test_defaults_and_checkpoint_format():
 @pytest.mark.parametrize("section, key, value, exc", [
     ("quant", "quantization", "nvfp4_per_token", NotImplementedError),
     ("quant", "quantization", "int4", ValueError),
-    ("quant", "fp8_compute_mode", "w8a8", NotImplementedError),
     ("quant", "fp8_compute_mode", "w4a4", ValueError),
     ("quant", "kv_cache_dtype", "fp8", NotImplementedError),
     ("quant", "kv_cache_dtype", "fp16", ValueError),
