@@ -780,8 +780,9 @@ def engine_model(w: dict, dev):
         inter = w["dense_inter"]
         ip = -(-inter // 128) * 128
         return DenseFfn(c.fmt, H, inter, _gen_matrix(rng, c.fmt, H, inter), _gen_matrix(rng, c.fmt, H, inter),
-                        _gen_matrix(rng, c.fmt, ip, H), device=dev)
+                        _gen_matrix(rng, c.fmt, ip, H), device=dev, workspaces=ws)
 
+    ws: dict = {}  # one set of FFN workspaces for all layers (they run one after another)
     layers = []
     for i in range(w["layers"]):
         if i < w.get("dense_layers", 0):
@@ -789,7 +790,7 @@ def engine_model(w: dict, dev):
         else:
             lw = make_layer_device(c, seed=i, device=dev)
             ffn = MoeLayer(c.fmt, c.hidden, c.inter, c.num_experts, c.top_k, c.routing, lw.router, lw.experts,
-                           shared=lw.shared or None, shared_inter=c.shared_inter or None, device=dev)
+                           shared=lw.shared or None, shared_inter=c.shared_inter or None, device=dev, workspaces=ws)
         if mla:
             dn, dr, dv = w["d_nope"], w["d_rope"], w["d_v"]
             layers.append(MlaDecoderLayer(norm_w(H), mat(nh * (dn + dr), H), mat(512 + dr, H), mat(nh * (dn + dv), 512),

@@ -780,6 +780,7 @@ def load_decoder(model_dir: str | Path, device="cuda", kernel: str = "auto", nam
     dims = {"q": (spec.heads * d, H), "k": (spec.kv_heads * d, H), "v": (spec.kv_heads * d, H),
             "o": (H, spec.heads * d)}
     layers = []
+    ws: dict = {}  # the layers run one after another: one set of FFN workspaces for all of them
     for lay in w["layers"]:
         kind, f = lay["ffn"]
         if kind == "moe":
@@ -787,9 +788,10 @@ def load_decoder(model_dir: str | Path, device="cuda", kernel: str = "auto", nam
             ffn = MoeLayer(ms.fmt, ms.hidden, ms.inter, ms.num_experts, ms.top_k, ms.routing, router, experts,
                            shared=shared or None, shared_inter=ms.shared_inter or None, n_group=ms.n_group,
                            topk_group=ms.topk_group, routed_scaling=ms.routed_scaling, bias=bias, kernel=kernel,
-                           device=device)
+                           device=device, workspaces=ws)
         else:
-            ffn = DenseFfn(spec.fmt, H, spec.inter, f["gate"], f["up"], f["down"], kernel=kernel, device=device)
+            ffn = DenseFfn(spec.fmt, H, spec.inter, f["gate"], f["up"], f["down"], kernel=kernel, device=device,
+                           workspaces=ws)
         if spec.mla:
             m, nh = spec.mla, spec.heads
             dn, dr, dv, R, qr = (m["qk_nope_head_dim"], m["qk_rope_head_dim"], m["v_head_dim"], m["kv_lora_rank"],

@@ -37,13 +37,15 @@
 //             nibbles at 8448, per row, as above.
 //   FP8:      half h at [8192 h, 8192 h + 8192): 128 rows x 64 B; chunk c (0..3) of row r at
 //             r*64 + 16*(c ^ ((r >> 1) & 3)); byte b of a chunk is k = 64h + 16c + b.  Scale at
-//             16384 (a fused gate/up block: gate scale at 16384, up scale at 16388).
+//             16384 (a fused gate/up block: gate scale at 16384, up scale at 16388; the scale
+//             of row r is at 16384 + 4 (r & 1)).
 //   The channel-scaled formats keep the codes of their base format and one fp32 scale per
 //   row at the scale offset (row r of a fused gate/up block: the scale of its channel).
 // The XOR swizzle makes the eight rows read by each quarter-warp hit eight distinct bank
 // groups.  A lone matrix (down projection) uses blocks of 128 channels; the gate and up
-// matrices are fused: block t holds gate channels [64t, 64t+64) in rows 0..63 and the same
-// up channels in rows 64..127, so that one 128-row MMA tile yields both halves of SwiGLU.
+// matrices are fused: block t holds gate channel 64t + i in row 2i and the up channel of the
+// same index in row 2i + 1, so that one 128-row MMA tile yields both halves of SwiGLU and the
+// two sums of a channel sit in adjacent tensor-memory lanes (one warp's lanes 2i, 2i + 1).
 #pragma once
 
 #include "common.cuh"
@@ -70,10 +72,11 @@ inline __host__ __device__ int rows_fp8_byte(int r, int k) {
   return h * 8192 + r * 64 + 16 * (c ^ ((r >> 1) & 3)) + (k & 15);
 }
 // Source channel of row r of row-layout block `nt` for matrix `slot` (-1: the row belongs to
-// the other matrix of a fused gate/up block).
+// the other matrix of a fused gate/up block, whose rows interleave: row 2i is gate channel
+// 64 nt + i, row 2i + 1 the up channel of the same index).
 inline __host__ __device__ int rows_channel(int nt, int r, int nmat, int slot) {
   if (nmat == 1) return nt * 128 + r;
-  return (r >> 6) == slot ? nt * 64 + (r & 63) : -1;
+  return (r & 1) == slot ? nt * 64 + (r >> 1) : -1;
 }
 // Row-layout blocks along the channel axis of a matrix with N channels.
 inline __host__ __device__ int rows_nblocks(int N, int nmat) { return nmat == 1 ? N / 128 : N / 64; }

@@ -71,6 +71,25 @@ __device__ __forceinline__ void put_row_meta(uint8_t* b, int r, int n, int kt, i
   }
 }
 
+// Scale and zero point of row r alone (channel n): the other nibble of the row's zero-point
+// byte belongs to the other matrix of a fused block, packed by a separate (earlier or later)
+// launch, so the byte is read, modified and written.
+template <int FMT>
+__device__ __forceinline__ void put_one_row_meta(uint8_t* b, int r, int n, int kt, int N, const void* scales,
+                                                 const int32_t* qzeros, const NibbleOrder& ord) {
+  using B = Blk<FMT>;
+  if constexpr (B::kScale == kScaleF16Row) {
+    reinterpret_cast<uint16_t*>(b + B::kScaleOff)[r] = static_cast<const uint16_t*>(scales)[(size_t)kt * N + n];
+  } else {
+    reinterpret_cast<float*>(b + B::kScaleOff)[r] = static_cast<const float*>(scales)[(size_t)kt * N + n];
+  }
+  if constexpr (B::kZeros) {
+    const uint32_t z = awq_get(qzeros, N / 8, kt, n, ord.slot_of_col);
+    uint8_t& zb = b[B::kZeroOff + (r >> 1)];
+    zb = static_cast<uint8_t>((zb & (0xF0u >> (4 * (r & 1)))) | (z << (4 * (r & 1))));
+  }
+}
+
 template <int FMT>  // per-channel metadata of the fragment layout (AWQ and signed int4)
 __global__ void pack_int4_meta_kernel(const int32_t* __restrict__ qzeros, const void* __restrict__ scales, int K,
                                       int N, NibbleOrder ord, uint8_t* __restrict__ dst, int nmat, int slot) {
@@ -239,7 +258,9 @@ __global__ void pack_int4_rows_kernel(const int32_t* __restrict__ qweight, const
         word |= awq_get(qweight, N / 8, k, n, ord.slot_of_col) << (4 * rows_awq_slot(kk));
       }
       *reinterpret_cast<uint32_t*>(b + rows_awq_word(r, 8 * j)) = word;
-    } else if ((r & 1) == 0) {  // metadata of rows r, r+1 (same matrix: halves are 64 rows)
+    } else if (nmat == 2) {  // fused: row r alone is this matrix's (rows alternate gate / up)
+      put_one_row_meta<FMT>(b, r, n, kt, N, scales, qzeros, ord);
+    } else if ((r & 1) == 0) {  // metadata of rows r, r + 1 (zero points share a byte)
       put_row_meta<FMT>(b, r, n, kt, N, scales, qzeros, ord);
     }
   }
@@ -265,7 +286,7 @@ __global__ void pack_fp8_rows_kernel(const uint8_t* __restrict__ w, const float*
     *reinterpret_cast<uint4*>(b + rows_fp8_byte(r, 16 * c)) = v;
     if constexpr (B::kScale == kScaleF32Row) {  // scale [K/128, N]: the row's channel
       if (c == 0) reinterpret_cast<float*>(b + B::kScaleOff)[r] = scale[(size_t)kt * N + n];
-    } else if (c == 0 && (r & 63) == 0 && (nmat == 2 || r == 0)) {
+    } else if (c == 0 && (nmat == 2 ? r == slot : r == 0)) {
       // block scale(s): a fused gate/up block keeps the gate scale at [0], the up scale at [1]
       float* s = reinterpret_cast<float*>(b + B::kScaleOff);
       s[nmat == 2 ? slot : 0] = scale[(size_t)(n / 128) * ktiles + kt];

@@ -65,8 +65,13 @@ struct TcCfg {
   static constexpr int kSW = kInt4 ? 6 : 4;           // weight stages
   static constexpr int kXRow = 17;                    // FFN1 staging: floats per weight row (16 + pad)
   static constexpr int kTokPitch = 132;               // FFN2 staging: floats per token (128 + pad, 16-B rows)
+  // FFN1 staging (bf16 elements): 16 token rows of 64 channels for the even lanes' tokens, then
+  // (after 64 bytes of padding, so that the odd lanes' stores hit other banks) the odd lanes'
+  static constexpr int kFfn1Odd = 16 * 64 + 32;
+  static constexpr int kFfn1Buf = kFfn1Odd + 16 * 64;
   static constexpr int kXchg = 2 * 128 * kXRow * 4;   // per epilogue warpgroup: 128 rows x 16 tokens
   static_assert(16 * kTokPitch <= 128 * kXRow && (kTokPitch * 4) % 16 == 0, "FFN2 staging fits the exchange");
+  static_assert(2 * kFfn1Buf * 2 <= 128 * kXRow * 4 && (kFfn1Buf * 2) % 16 == 0, "FFN1 staging fits the exchange");
   static constexpr int kThreads = 640;
   static constexpr int kDeqWarps = 8;
   static constexpr int kEpiWarps = 8;
@@ -182,7 +187,7 @@ __device__ __forceinline__ float block_scale(const uint8_t* blk, int r) {
   } else if constexpr (B::kScale == kScaleF32Row) {
     return __ldg(reinterpret_cast<const float*>(blk + B::kScaleOff) + r);
   } else {
-    return __ldg(reinterpret_cast<const float*>(blk + B::kScaleOff) + (MODE == kFfn1 ? (r >> 6) : 0));
+    return __ldg(reinterpret_cast<const float*>(blk + B::kScaleOff) + (MODE == kFfn1 ? (r & 1) : 0));
   }
 }
 
@@ -408,6 +413,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
     const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ewg * 128);
     float* xb = xchg + ewg * 128 * C::kXRow;
     float* wsm = reinterpret_cast<float*>(smem + C::kRowWOff) + ewg * 128;  // FFN2: weights of the WG's tokens
+    int ffn1_use = 0;  // FFN1: output chunks staged so far (buffer = ffn1_use & 1)
     const uint32_t pe0 = tc::mapa(&pempty[0], 0), pe1 = tc::mapa(&pempty[1], 0);
     int j = 0;
     bool ok = true;
@@ -458,18 +464,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
         if (lane == 0) tc::mbar_arrive_cl(slot ? pe1 : pe0);
       }
       if (!ok || !valid) continue;
-      // Output: the totals go through shared memory 16 tokens at a time (thread r writes row
-      // r).  FFN1: each thread of the warpgroup then produces 8 consecutive SwiGLU channels of
-      // one token and stores them as one 16-byte vector.  FFN2: the chunk is staged token-major
-      // and each warp writes whole token rows, lane l channels 4l .. 4l + 3, so that one store
-      // instruction covers 512 contiguous bytes of one output row.
-      if constexpr (MODE == kFfn2) wsm[r] = my_wr;  // read after the first chunk's barrier
-      const int tt = threadIdx.x & 15;          // FFN1: token of the chunk this thread writes out
-      const int grp = (threadIdx.x >> 4) & 7;   // FFN1: channel group of this thread
+      // Output, 16 tokens at a time.  FFN2: bf16 rows are staged token-major in shared memory
+      // and each warp writes whole token rows, lane l channels 4l .. 4l + 3; fp32 rows go
+      // straight from the registers.  FFN1: see below.
+      if constexpr (MODE == kFfn2) {
+        wsm[r] = my_wr;  // read after the first chunk's barrier
 #pragma unroll
       for (int c = 0; c < 128; c += 16) {
         if (c < ncols) {  // uniform over the warpgroup
-          if constexpr (MODE == kFfn2) {
+          {
             if (a.out_bf16) {  // uniform: staged token-major, each warp writes 4 tokens' 256-byte rows
 #pragma unroll
               for (int i = 0; i < 16; ++i) xb[i * C::kTokPitch + r] = tot[c + i];
@@ -504,29 +507,47 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
                 if (ewg * 128 + c + i + u < rows) orow[(size_t)(i + u) * a.out_ld] = tot[c + i + u] * w4[u];
             }
             if (c + 16 >= ncols) named_bar(1 + ewg, 128);  // weights read before the next item's
-          } else {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) xb[r * C::kXRow + i] = tot[c + i];
-            named_bar(1 + ewg, 128);
-            const int tok = ewg * 128 + c + tt;  // token index inside the tile
-            if (tok < rows) {
-              // rows 0..63: gate, rows 64..127: up of the same 64 channels; channels grp*8 .. +7
-              uint32_t pk[4];
-#pragma unroll
-              for (int j = 0; j < 8; j += 2) {
-                const float g0 = xb[(grp * 8 + j) * C::kXRow + tt], g1 = xb[(grp * 8 + j + 1) * C::kXRow + tt];
-                const float u0 = xb[(64 + grp * 8 + j) * C::kXRow + tt];
-                const float u1 = xb[(64 + grp * 8 + j + 1) * C::kXRow + tt];
-                const __nv_bfloat162 h2 = __floats2bfloat162_rn(__fdividef(g0, 1.0f + __expf(-g0)) * u0,
-                                                                __fdividef(g1, 1.0f + __expf(-g1)) * u1);
-                pk[j >> 1] = *reinterpret_cast<const uint32_t*>(&h2);
-              }
-              uint16_t* orow = static_cast<uint16_t*>(a.out) + (size_t)(row0 + tok) * a.out_ld + blk * 64 + grp * 8;
-              *reinterpret_cast<uint4*>(orow) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-            }
-            named_bar(1 + ewg, 128);
           }
         }
+      }
+      } else {
+#pragma unroll
+      for (int c = 0; c < 64; c += 16) {
+        if (c < ncols) {  // uniform over the warpgroup
+          {
+            // rows 2i / 2i + 1 hold the gate / up sums of channel i (i = r >> 1) in adjacent
+            // lanes: a shuffle gives the even lane the up sums of tokens c .. c + 15 and the odd
+            // lane the gate sums of tokens 64 + c .. 64 + c + 15, so the even lane writes
+            // SwiGLU for the first and the odd lane for the second 16 tokens of the chunk,
+            // staged as bf16 token rows (two buffers, one barrier per chunk) and stored as
+            // 16-byte vectors, four whole 128-byte rows per warp instruction.
+            const bool up_row = r & 1;
+            uint16_t* buf = reinterpret_cast<uint16_t*>(xb) + (ffn1_use & 1) * C::kFfn1Buf;
+            uint16_t* mine = buf + (up_row ? C::kFfn1Odd : 0) + (r >> 1);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float other = __shfl_xor_sync(0xffffffffu, up_row ? tot[c + i] : tot[64 + c + i], 1);
+              const float g = up_row ? other : tot[c + i];
+              const float u = up_row ? tot[64 + c + i] : other;
+              mine[i * 64] = __bfloat16_as_ushort(__float2bfloat16_rn(__fdividef(g, 1.0f + __expf(-g)) * u));
+            }
+            named_bar(1 + ewg, 128);
+            const int wt = r >> 3, part = r & 7;  // 16 tokens of each half: 8 x 16-byte parts per token row
+#pragma unroll
+            for (int pass = 0; pass < 2; ++pass) {
+              const int tl = wt + 16 * pass;  // 0..15: tokens c + tl; 16..31: tokens 64 + c + tl - 16
+              const int tok = ewg * 128 + (pass == 0 ? c + tl : 64 + c + tl - 16);
+              if (tok < rows) {
+                const uint4 v =
+                    *reinterpret_cast<const uint4*>(buf + (pass ? C::kFfn1Odd + (tl - 16) * 64 : tl * 64) + part * 8);
+                *reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + (size_t)(row0 + tok) * a.out_ld + blk * 64 +
+                                          part * 8) = v;
+              }
+            }
+            ++ffn1_use;
+          }
+        }
+      }
       }
     }
   }

@@ -45,7 +45,8 @@ class DenseFfn:
     ``"fp8_channel"`` / ``"int4_sym_g128"`` forms of ``ccut_b200.formats``.
     ``inter`` is the model's intermediate size; it is padded to a multiple of 128."""
 
-    def __init__(self, fmt: str, hidden: int, inter: int, gate, up, down, kernel: str = "auto", device="cuda"):
+    def __init__(self, fmt: str, hidden: int, inter: int, gate, up, down, kernel: str = "auto", device="cuda",
+                 workspaces: dict | None = None):
         if hidden % 128:
             raise ValueError("hidden must be a multiple of 128")
         self.hidden, self.inter = int(hidden), int(inter)
@@ -90,7 +91,7 @@ class DenseFfn:
         else:
             raise NotImplementedError(f"weight format {fmt!r} is not supported")
         self.layer = MoeLayer(fmt, self.hidden, ip, 1, 1, "softmax_topk", np.zeros((1, self.hidden), np.float32),
-                              [mats], kernel=kernel, device=device)
+                              [mats], kernel=kernel, device=device, workspaces=workspaces)
         self.device = self.layer.device
         self._perm: dict[int, Permutation] = {}
 

@@ -80,7 +80,9 @@ class MoeLayer:
     (``norm_topk_prob=False``), ``"topk_softmax"`` (``norm_topk_prob=True``) or
     ``"sigmoid_group"``.  ``kernel``: ``"auto"`` keeps both packed layouts resident and runs
     the mma.sync kernel for decode-sized batches and the tcgen05 kernel otherwise; ``"tc"``
-    keeps only the tcgen05 layout; ``"mma"`` forces the mma.sync kernel."""
+    keeps only the tcgen05 layout; ``"mma"`` forces the mma.sync kernel.  ``workspaces``: a
+    dict shared by layers that never run concurrently (the layers of one decoder), so that
+    they reuse one set of device workspaces instead of one set each."""
 
     def __init__(
         self,
@@ -102,6 +104,7 @@ class MoeLayer:
         nibble_order: str = "awq",
         kernel: str = "auto",
         device: str | torch.device = "cuda",
+        workspaces: dict | None = None,
     ):
         if fmt not in _lib.FORMATS:
             raise NotImplementedError(f"weight format {fmt!r} is not supported (have {sorted(_lib.FORMATS)})")
@@ -159,7 +162,9 @@ class MoeLayer:
             self.fmt_code, _lib.KERNELS[kernel], hidden, inter, num_experts, self.num_slices, self.shared_gate,
             _ptr(self.w13), _ptr(self.w2), _ptr(w13f), _ptr(w2f), _ptr(self.router),
         )
-        self._ws: dict[str, torch.Tensor] = {}
+        # workspaces by entry point; layers that run one after another on one stream (the
+        # layers of a decoder) may share one dict, so that a long prefill sizes one set
+        self._ws: dict[str, torch.Tensor] = workspaces if workspaces is not None else {}
 
     # ---- packing ------------------------------------------------------------------
     def _slice(self, mat, role: str, lo: int, width: int):
