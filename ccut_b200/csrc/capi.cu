@@ -133,7 +133,7 @@ FwdScratch carve_fwd(Carver& c, const ccut_moe_layer* L, int T, int k) {
   FwdScratch s;
   s.status = c.take<int>(64);
   s.sched = take_sched(c);
-  s.part = c.take<float>((size_t)route_hsplit(T, E, H) * T * E);
+  s.part = c.take<float>((size_t)route_scratch_floats(T, E, H));
   s.counts = c.take<int>(E);
   s.offsets = c.take<int32_t>(E + S + 1);
   s.ids = c.take<int32_t>((size_t)T * k);
@@ -310,7 +310,7 @@ size_t ccut_route_workspace_bytes(int T, int E, int H) {
   if (T <= 0 || E <= 0 || H <= 0 || H % 64) return 256;
   Carver c(nullptr);
   c.take<int>(64);
-  c.take<float>((size_t)route_hsplit(T, E, H) * T * E);
+  c.take<float>((size_t)route_scratch_floats(T, E, H));
   return c.off;
 }
 
@@ -326,7 +326,7 @@ int ccut_moe_route(const uint16_t* x, const float* router, int T, int H, int E, 
   if (ws_bytes < ccut_route_workspace_bytes(T, E, H)) return CCUT_ERR_WORKSPACE;
   Carver c(workspace);
   c.take<int>(64);
-  float* part = c.take<float>((size_t)route_hsplit(T, E, H) * T * E);
+  float* part = c.take<float>((size_t)route_scratch_floats(T, E, H));
   return launch_route(x, router, T, H, E, *rp, ids, weights, logits, part, nullptr, nullptr, stream);
 }
 

@@ -289,7 +289,7 @@ EpScratch carve_ep(Carver& c, const ccut_moe_layer* L, int E_global, int world, 
   s.ex = carve_ex(c, world, T_cap, H, k);
   s.sched = take_sched(c);
   s.sh_sched = take_sched(c);
-  s.part = c.take<float>((size_t)route_hsplit(T_cap, E_global, H) * T_cap * E_global);
+  s.part = c.take<float>((size_t)route_scratch_floats_upto(T_cap, E_global, H));
   s.counts_g = c.take<int>(E_global);
   s.ids_l = c.take<int32_t>((size_t)T_cap * k);
   s.w_l = c.take<float>((size_t)T_cap * k);

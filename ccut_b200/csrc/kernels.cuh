@@ -61,6 +61,8 @@ int launch_dequant(int fmt, int layout, const void* packed, int K, int N, int nm
                    cudaStream_t st);
 // route.cu
 int route_hsplit(int T, int E, int H);
+size_t route_scratch_floats(int T, int E, int H);  // the `part` scratch launch_route needs
+size_t route_scratch_floats_upto(int T_cap, int E, int H);  // enough for every T <= T_cap
 int launch_route(const uint16_t* x, const float* router, int T, int H, int E, const ccut_route_params& rp,
                  int32_t* ids, float* weights, float* logits, float* part, int* counts, uint16_t* x16,
                  cudaStream_t st);

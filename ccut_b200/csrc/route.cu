@@ -9,6 +9,8 @@
 // deterministic run to run.
 #include <math.h>
 
+#include <algorithm>
+
 #include "launch.cuh"
 #include "layout.cuh"
 
@@ -18,6 +20,7 @@ constexpr int kRtTok = 64;   // tokens per logits CTA
 constexpr int kRtExp = 64;   // experts per logits CTA
 constexpr int kRtH = 64;     // h per shared-memory chunk
 constexpr int kRtPitch = 72; // bf16 per staged row (64 + 8): conflict-free ldmatrix rows
+constexpr int kRtTiledMinT = 256;  // from this batch size on: split once, then the pipelined GEMM
 
 // Number of H splits: enough CTAs to cover the SMs at small T, one split at large T.
 int route_hsplit(int T, int E, int H) {
@@ -28,6 +31,23 @@ int route_hsplit(int T, int E, int H) {
   if (hs < 1) hs = 1;
   while (chunks % hs) --hs;
   return hs;
+}
+
+// fp32 scratch of launch_route: the H-split partial logits, then (T >= kRtTiledMinT) the router's
+// three bf16 split planes, 16-byte aligned.
+size_t route_scratch_floats(int T, int E, int H) {
+  size_t n = (size_t)route_hsplit(T, E, H) * T * E;
+  if (T >= kRtTiledMinT) n = (n + 3) / 4 * 4 + ((size_t)3 * E * H + 1) / 2;
+  return n;
+}
+
+// An amount of that scratch that serves every batch of at most T_cap tokens: the split count
+// hs <= 296 / ctas + 1 with ctas >= T / 64 tiles gives hs * T <= 296 * 64 + T, and hs <= H / 64.
+size_t route_scratch_floats_upto(int T_cap, int E, int H) {
+  const size_t ht = std::min((size_t)(H / kRtH) * T_cap, (size_t)296 * kRtTok + T_cap);
+  size_t n = ht * E;
+  if (T_cap >= kRtTiledMinT) n = (n + 3) / 4 * 4 + ((size_t)3 * E * H + 1) / 2;
+  return n;
 }
 
 // fp32 -> (hi, mid, lo) bf16 with hi + mid + lo == w exactly: each part keeps the next 8
@@ -126,6 +146,137 @@ __global__ void __launch_bounds__(256) route_logits_kernel(const uint16_t* __res
     }
     __syncthreads();
   }
+  const int g = lane >> 2, c2 = 2 * (lane & 3);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int t = t0 + tg * 16 + g + 8 * (i >> 1);
+      const int e = e0 + eh * 32 + j * 8 + c2 + (i & 1);
+      if (t < T && e < E) part[((size_t)hs * T + t) * E + e] = acc[j][i];
+    }
+  }
+}
+
+// ---- prefill-sized batches: split once, then a pipelined tensor-core GEMM ---------------
+// At T >= kRtTiledMinT every token tile would re-split the whole router, so the split runs
+// once per call into scratch (w3 = hi, mid, lo planes of bf16 [E, H]) and the logits GEMM
+// streams x and w3 through a 4-stage cp.async ring of 32-h chunks.  Each thread accumulates
+// the same exact products in the same fp32 order as in route_logits_kernel (16-h blocks in h
+// order; hi, mid, lo within a block), so both kernels give identical logits.
+constexpr int kRtH2 = 32;                                            // h per stage
+constexpr int kRtPitch2 = 40;                                        // bf16 per staged row (32 + 8)
+constexpr int kRtStages = 4;
+constexpr int kRtStageBytes = (kRtTok + 3 * kRtExp) * kRtPitch2 * 2;  // x tile + three weight planes
+constexpr int kRtSmem = kRtStages * kRtStageBytes;
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// w3[s][e][h] (s = 0, 1, 2): the exact three-way bf16 split of router[e][h].
+__global__ void route_split_kernel(const float* __restrict__ router, size_t n4, size_t plane,
+                                   uint16_t* __restrict__ w3) {
+  pdl_wait();
+  pdl_trigger();
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+    const float4 w = __ldg(reinterpret_cast<const float4*>(router) + i);
+    const float wa[4] = {w.x, w.y, w.z, w.w};
+    uint16_t p[3][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) split3_bf16(wa[j], p[0][j], p[1][j], p[2][j]);
+#pragma unroll
+    for (int s = 0; s < 3; ++s)
+      reinterpret_cast<uint2*>(w3 + s * plane)[i] =
+          make_uint2(p[s][0] | (uint32_t)p[s][1] << 16, p[s][2] | (uint32_t)p[s][3] << 16);
+  }
+}
+
+// part[hs][t][e] as route_logits_kernel, from the split planes.  Warp w owns tokens
+// 16 (w & 3) .. + 15 and experts 32 (w >> 2) .. + 31 of the 64 x 64 CTA tile.
+__global__ void __launch_bounds__(256) route_logits_tiled_kernel(const uint16_t* __restrict__ x,
+                                                                 const uint16_t* __restrict__ w3, int T, int H, int E,
+                                                                 int hsplit, float* __restrict__ part,
+                                                                 int* __restrict__ counts,
+                                                                 uint16_t* __restrict__ x16) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ __align__(128) uint8_t rt_smem[];
+  const int t0 = blockIdx.x * kRtTok, e0 = blockIdx.y * kRtExp, hs = blockIdx.z;
+  const int hlen = H / hsplit, hbeg = hs * hlen, nsteps = hlen / kRtH2;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const size_t plane = (size_t)E * H;
+  if (counts && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+    for (int e = tid; e < E; e += blockDim.x) counts[e] = 0;
+  // one 16-byte chunk of the x tile and three of the weight planes per thread and stage
+  const int lrow = tid >> 2, lseg = tid & 3;
+  const int lt = t0 + lrow, le = e0 + lrow;
+  const uint16_t* xsrc = x + (size_t)(lt < T ? lt : 0) * H + hbeg + lseg * 8;
+  const uint16_t* wsrc = w3 + (size_t)(le < E ? le : 0) * H + hbeg + lseg * 8;
+  auto load = [&](int step) {
+    uint16_t* xs = reinterpret_cast<uint16_t*>(rt_smem + (step % kRtStages) * kRtStageBytes);
+    const int h = step * kRtH2;
+    cp_async16(xs + lrow * kRtPitch2 + lseg * 8, xsrc + h, lt < T);
+#pragma unroll
+    for (int s = 0; s < 3; ++s)
+      cp_async16(xs + (kRtTok + s * kRtExp + lrow) * kRtPitch2 + lseg * 8, wsrc + s * plane + h, le < E);
+  };
+#pragma unroll
+  for (int s = 0; s < kRtStages - 1; ++s) {
+    if (s < nsteps) load(s);
+    cp_async_commit();
+  }
+  const int tg = warp & 3, eh = warp >> 2;
+  float acc[4][4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[j][i] = 0.f;
+  for (int step = 0; step < nsteps; ++step) {
+    cp_async_wait<kRtStages - 2>();
+    __syncthreads();  // this stage landed for every thread; the stage refilled below is free
+    if (step + kRtStages - 1 < nsteps) load(step + kRtStages - 1);
+    cp_async_commit();
+    const uint16_t* xs = reinterpret_cast<const uint16_t*>(rt_smem + (step % kRtStages) * kRtStageBytes);
+    if (x16 && blockIdx.y == 0 && lt < T) {  // the f16 copy of this thread's chunk
+      const uint4 v = *reinterpret_cast<const uint4*>(xs + lrow * kRtPitch2 + lseg * 8);
+      const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const __half2 hh = __floats2half2_rn(__uint_as_float(w4[j] << 16), __uint_as_float(w4[j] & 0xffff0000u));
+        o[j] = *reinterpret_cast<const uint32_t*>(&hh);
+      }
+      *reinterpret_cast<uint4*>(x16 + (size_t)lt * H + hbeg + step * kRtH2 + lseg * 8) =
+          make_uint4(o[0], o[1], o[2], o[3]);
+    }
+#pragma unroll
+    for (int ks = 0; ks < kRtH2 / 16; ++ks) {
+      uint32_t a[4];
+      ldmatrix_x4(a[0], a[1], a[2], a[3],
+                  xs + (tg * 16 + ((lane >> 3) & 1) * 8 + (lane & 7)) * kRtPitch2 + ks * 16 + (lane >> 4) * 8);
+#pragma unroll
+      for (int s = 0; s < 3; ++s) {
+        const uint16_t* ws = xs + (kRtTok + s * kRtExp) * kRtPitch2;
+#pragma unroll
+        for (int j = 0; j < 4; j += 2) {  // column tiles j, j + 1
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4(b0, b1, b2, b3,
+                      ws + (eh * 32 + (j + (lane >> 4)) * 8 + (lane & 7)) * kRtPitch2 + ks * 16 +
+                          ((lane >> 3) & 1) * 8);
+          mma_16816<true>(acc[j], a, b0, b1);
+          mma_16816<true>(acc[j + 1], a, b2, b3);
+        }
+      }
+    }
+  }
+  cp_async_wait<0>();
   const int g = lane >> 2, c2 = 2 * (lane & 3);
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -487,7 +638,23 @@ int launch_route(const uint16_t* x, const float* router, int T, int H, int E, co
                  cudaStream_t st) {
   const int hs = route_hsplit(T, E, H);
   dim3 g1((T + kRtTok - 1) / kRtTok, (E + kRtExp - 1) / kRtExp, hs);
-  int rc = launch_k(route_logits_kernel, g1, dim3(256), 0, st, x, router, T, H, E, hs, part, counts, x16);
+  int rc;
+  if (T >= kRtTiledMinT) {  // the split planes follow the partial sums in `part`
+    uint16_t* w3 = reinterpret_cast<uint16_t*>(part + ((size_t)hs * T * E + 3) / 4 * 4);
+    const size_t n4 = (size_t)E * H / 4;
+    size_t blocks = (n4 + 255) / 256;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    rc = launch_k(route_split_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st, router, n4,
+                  (size_t)E * H, w3);
+    if (rc) return rc;
+    static std::atomic<uint64_t> smem_set{0};
+    rc = ensure_smem_limit(route_logits_tiled_kernel, kRtSmem, smem_set);
+    if (rc) return rc;
+    rc = launch_k(route_logits_tiled_kernel, g1, dim3(256), kRtSmem, st, x, (const uint16_t*)w3, T, H, E, hs, part,
+                  counts, x16);
+  } else {
+    rc = launch_k(route_logits_kernel, g1, dim3(256), 0, st, x, router, T, H, E, hs, part, counts, x16);
+  }
   if (rc) return rc;
   if (T <= kTopkWideMaxT)
     return launch_k(route_topk_wide_kernel, dim3(T), dim3(256), 0, st, (const float*)part, hs, T, E, rp, ids, weights,

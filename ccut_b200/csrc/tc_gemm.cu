@@ -76,7 +76,8 @@ struct TcCfg {
   static constexpr int kDeqWarps = 8;
   static constexpr int kEpiWarps = 8;
   static constexpr int kNBar = 2 * kSW + 2 * kSA + 2 + 2 + 1;
-  static constexpr int kHeader = kNBar * 8 + 16 + 4 * (kMaxExperts + 1);
+  // barriers, tensor-memory address, item prefix over experts, the experts' row offsets
+  static constexpr int kHeader = kNBar * 8 + 16 + 2 * 4 * (kMaxExperts + 1);
   static constexpr int kXchgOff = (kHeader + 1023) / 1024 * 1024;
   static constexpr int kRowWOff = kXchgOff + kXchg;   // FFN2: routing weights of the item's 256 tokens
   static constexpr int kABOff = kXchgOff + (kXchg + 256 * 4 + 1023) / 1024 * 1024;  // 1024-aligned tiles
@@ -230,6 +231,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
   uint64_t* drain = pempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNBar);
   int* tprefix = reinterpret_cast<int*>(smem + C::kNBar * 8 + 16);
+  int* soff = tprefix + kMaxExperts + 1;  // a.offsets, read once: every role decodes items from it
   float* xchg = reinterpret_cast<float*>(smem + C::kXchgOff);
   uint8_t* ab = smem + C::kABOff;
   uint8_t* wtiles = smem + C::kWOff;
@@ -265,7 +267,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
     int carry = 0;
     for (int b = 0; b < a.num_e; b += 32) {
       const int e = b + lane;
-      const int me = e < a.num_e ? a.offsets[e + 1] - a.offsets[e] : 0;
+      const int o0 = e < a.num_e ? a.offsets[e] : 0, o1 = e < a.num_e ? a.offsets[e + 1] : 0;
+      if (e < a.num_e) soff[e] = o0;
+      if (e == a.num_e - 1) soff[e + 1] = o1;
+      const int me = o1 - o0;
       const int c = ((me + 255) / 256) * npairs;
       int inc = c;
 #pragma unroll
@@ -293,7 +298,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
       bool ok = true;
       for (int item = cluster; item < total && ok; item += nclusters) {
         int e, p, m0, rows, n;
-        tc_decode_item(item, tprefix, a.num_e, a.offsets, npairs, e, p, m0, rows, n);
+        tc_decode_item(item, tprefix, a.num_e, soff, npairs, e, p, m0, rows, n);
         const int blk = 2 * p + (int)rank;
         const bool valid = blk < ntiles;
         const uint8_t* wb = a.w + (size_t)e * a.expert_stride + (size_t)(valid ? blk : 0) * ktiles * BK::kBytes;
@@ -324,8 +329,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
       bool ok = true;
       for (int item = cluster; item < total && ok; item += nclusters) {
         int e, p, m0, rows, n;
-        tc_decode_item(item, tprefix, a.num_e, a.offsets, npairs, e, p, m0, rows, n);
-        const int brow = a.offsets[e] + m0 + (int)rank * (n / 2);
+        tc_decode_item(item, tprefix, a.num_e, soff, npairs, e, p, m0, rows, n);
+        const int brow = soff[e] + m0 + (int)rank * (n / 2);
         for (int st = 0; st < nstages; ++st, ++use) {
           const int sa = use % SA;
           if (!tc::mbar_wait_cl(&abempty[sa], ((use / SA) & 1) ^ 1, a.status)) {
@@ -345,7 +350,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
       bool ok = true;
       for (int item = cluster; item < total && ok; item += nclusters) {
         int e, p, m0, rows, n;
-        tc_decode_item(item, tprefix, a.num_e, a.offsets, npairs, e, p, m0, rows, n);
+        tc_decode_item(item, tprefix, a.num_e, soff, npairs, e, p, m0, rows, n);
         const uint32_t idesc = tc::idesc_bf16_m256((uint32_t)n);
         for (int kb = 0; kb < nkb && ok; ++kb, ++j) {
           const int slot = j & 1;
@@ -383,7 +388,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
     bool ok = true;
     for (int item = cluster; item < total && ok; item += nclusters) {
       int e, p, m0, rows, n;
-      tc_decode_item(item, tprefix, a.num_e, a.offsets, npairs, e, p, m0, rows, n);
+      tc_decode_item(item, tprefix, a.num_e, soff, npairs, e, p, m0, rows, n);
       const bool valid = 2 * p + (int)rank < ntiles;
       for (int st = 0; st < nstages; ++st, ++use) {
         const int s = use % SW, sa = use % SA;
@@ -419,12 +424,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
     bool ok = true;
     for (int item = cluster; item < total && ok; item += nclusters) {
       int e, p, m0, rows, n;
-      tc_decode_item(item, tprefix, a.num_e, a.offsets, npairs, e, p, m0, rows, n);
+      tc_decode_item(item, tprefix, a.num_e, soff, npairs, e, p, m0, rows, n);
       const int blk = 2 * p + (int)rank;
       const bool valid = blk < ntiles;
       const int ncols = max(0, min(128, n - ewg * 128));
       const uint8_t* wb = a.w + (size_t)e * a.expert_stride + (size_t)(valid ? blk : 0) * ktiles * BK::kBytes;
-      const int row0 = a.offsets[e] + m0;
+      const int row0 = soff[e] + m0;
       // FFN2: this thread's token's routing weight, loaded now so that its latency passes
       // under the item's k loop (staged through shared memory for the output phase)
       float my_wr = 1.f;
@@ -477,14 +482,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
 #pragma unroll
               for (int i = 0; i < 16; ++i) xb[i * C::kTokPitch + r] = tot[c + i];
               named_bar(1 + ewg, 128);
+              // the warp's 4 tokens: all shared-memory reads first, then the 4 row stores
+              float4 v4[4];
+              float wr4[4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                v4[j] = *reinterpret_cast<const float4*>(xb + (q * 4 + j) * C::kTokPitch + 4 * lane);
+                wr4[j] = wsm[c + q * 4 + j];
+              }
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
                 const int tl = q * 4 + j;  // token of the chunk (uniform over the warp)
                 if (ewg * 128 + c + tl < rows) {
-                  const float wr = wsm[c + tl];
-                  const float4 v = *reinterpret_cast<const float4*>(xb + tl * C::kTokPitch + 4 * lane);
-                  const __nv_bfloat162 h0 = __floats2bfloat162_rn(v.x * wr, v.y * wr);
-                  const __nv_bfloat162 h1 = __floats2bfloat162_rn(v.z * wr, v.w * wr);
+                  const __nv_bfloat162 h0 = __floats2bfloat162_rn(v4[j].x * wr4[j], v4[j].y * wr4[j]);
+                  const __nv_bfloat162 h1 = __floats2bfloat162_rn(v4[j].z * wr4[j], v4[j].w * wr4[j]);
                   uint16_t* orow = static_cast<uint16_t*>(a.out) + (size_t)(row0 + ewg * 128 + c + tl) * a.out_ld +
                                    blk * kTileN + 4 * lane;
                   *reinterpret_cast<uint2*>(orow) =

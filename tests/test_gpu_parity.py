@@ -150,6 +150,21 @@ def test_route_logits_and_ids(fmt, mode):
         assert ids_match_except_near_ties(r.ids.cpu().numpy(), ids_x, oracle_scores(lw, xb), cfg.top_k).size == 0
 
 
+def test_route_logits_prefill_sizes():
+    """From 256 tokens on the router is split once into bf16 planes and the logits GEMM is
+    pipelined: partial expert tiles (E = 72) and odd token counts against the fp32 oracle."""
+    cfg = small_cfg("awq_int4_g128", "topk_softmax", hidden=384, inter=128, experts=72, top_k=4)
+    lw = inputs.make_layer(cfg, seed=14)
+    L = gpu_layer(lw)
+    for T in (255, 256, 513, 1100):
+        xb = lw.make_x(T)
+        r = L.route(x_device(xb), want_logits=True)
+        lg_ref = formats.bf16_bits_to_f32(xb) @ lw.router.T
+        np.testing.assert_allclose(r.logits.cpu().numpy(), lg_ref, rtol=1e-4, atol=1e-5)
+        w_ref, ids_ref = routing.route(r.logits.cpu().numpy(), cfg.top_k, "topk_softmax")
+        assert np.array_equal(r.ids.cpu().numpy().astype(np.int64), ids_ref)
+
+
 # ---------------------------------------------------------------- permutation
 def test_permute_stable_counting_sort():
     cfg = small_cfg("fp8_b128", hidden=128, inter=128, experts=16, top_k=4, shared=1)
