@@ -76,8 +76,9 @@ struct TcCfg {
   static constexpr int kDeqWarps = 8;
   static constexpr int kEpiWarps = 8;
   static constexpr int kNBar = 2 * kSW + 2 * kSA + 2 + 2 + 1;
-  // barriers, tensor-memory address, item prefix over experts, the experts' row offsets
-  static constexpr int kHeader = kNBar * 8 + 16 + 2 * 4 * (kMaxExperts + 1);
+  // barriers, tensor-memory address, item prefix over experts, the experts' row offsets and
+  // tile descriptors
+  static constexpr int kHeader = kNBar * 8 + 16 + 3 * 4 * (kMaxExperts + 1);
   static constexpr int kXchgOff = (kHeader + 1023) / 1024 * 1024;
   static constexpr int kRowWOff = kXchgOff + kXchg;   // FFN2: routing weights of the item's 256 tokens
   static constexpr int kABOff = kXchgOff + (kXchg + 256 * 4 + 1023) / 1024 * 1024;  // 1024-aligned tiles
@@ -93,9 +94,11 @@ constexpr uint32_t kRegProducers = 32, kRegDequant = 48, kRegEpilogue = 176;
 static_assert(128 * kRegProducers + 256 * kRegDequant + 256 * kRegEpilogue <= 640 * 96, "register pool");
 
 // Item -> (expert e, weight block pair p, first tile row m0, rows, tile width N).  An expert's
-// M_e rows are cut into ceil(M_e / 256) tiles of equal width (a multiple of 32).
+// M_e rows are cut into ceil(M_e / 256) tiles of equal width (a multiple of 32); tdesc[e]
+// holds that width << 16 | the tile count (set up once per CTA, so a decode is a binary
+// search plus a few shared-memory reads, without integer divisions for 1 or 2 tiles).
 __device__ __forceinline__ void tc_decode_item(int item, const int* tprefix, int num_e, const int* offsets,
-                                               int npairs, int& e, int& p, int& m0, int& rows, int& n) {
+                                               const int* tdesc, int& e, int& p, int& m0, int& rows, int& n) {
   int lo = 0, hi = num_e - 1;  // last e with tprefix[e] <= item
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
@@ -103,16 +106,22 @@ __device__ __forceinline__ void tc_decode_item(int item, const int* tprefix, int
     else hi = mid - 1;
   }
   e = lo;
-  const int me = offsets[e + 1] - offsets[e];
-  const int mtiles = (me + 255) / 256;
-  const int tw = ((me + mtiles - 1) / mtiles + 31) / 32 * 32;
+  const int d = tdesc[e], mtiles = d & 0xffff, tw = d >> 16;
   const int local = item - tprefix[e];
-  p = local / mtiles;
-  const int mt = local % mtiles;
+  int mt;
+  if (mtiles == 1) {
+    p = local;
+    mt = 0;
+  } else if (mtiles == 2) {
+    p = local >> 1;
+    mt = local & 1;
+  } else {
+    p = local / mtiles;
+    mt = local - p * mtiles;
+  }
   m0 = mt * tw;
-  rows = min(tw, me - m0);
+  rows = min(tw, offsets[e + 1] - offsets[e] - m0);
   n = (rows + 31) / 32 * 32;
-  (void)npairs;
 }
 
 __device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
@@ -232,6 +241,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNBar);
   int* tprefix = reinterpret_cast<int*>(smem + C::kNBar * 8 + 16);
   int* soff = tprefix + kMaxExperts + 1;  // a.offsets, read once: every role decodes items from it
+  int* tdesc = soff + kMaxExperts + 1;    // per expert: tile width << 16 | tile count
   float* xchg = reinterpret_cast<float*>(smem + C::kXchgOff);
   uint8_t* ab = smem + C::kABOff;
   uint8_t* wtiles = smem + C::kWOff;
@@ -271,7 +281,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
       if (e < a.num_e) soff[e] = o0;
       if (e == a.num_e - 1) soff[e + 1] = o1;
       const int me = o1 - o0;
-      const int c = ((me + 255) / 256) * npairs;
+      const int mt = (me + 255) / 256;
+      if (e < a.num_e) tdesc[e] = (mt > 0 ? ((me + mt - 1) / mt + 31) / 32 * 32 : 0) << 16 | mt;
+      const int c = mt * npairs;
       int inc = c;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -298,7 +310,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
       bool ok = true;
       for (int item = cluster; item < total && ok; item += nclusters) {
         int e, p, m0, rows, n;
-        tc_decode_item(item, tprefix, a.num_e, soff, npairs, e, p, m0, rows, n);
+        tc_decode_item(item, tprefix, a.num_e, soff, tdesc, e, p, m0, rows, n);
         const int blk = 2 * p + (int)rank;
         const bool valid = blk < ntiles;
         const uint8_t* wb = a.w + (size_t)e * a.expert_stride + (size_t)(valid ? blk : 0) * ktiles * BK::kBytes;
@@ -329,7 +341,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
       bool ok = true;
       for (int item = cluster; item < total && ok; item += nclusters) {
         int e, p, m0, rows, n;
-        tc_decode_item(item, tprefix, a.num_e, soff, npairs, e, p, m0, rows, n);
+        tc_decode_item(item, tprefix, a.num_e, soff, tdesc, e, p, m0, rows, n);
         const int brow = soff[e] + m0 + (int)rank * (n / 2);
         for (int st = 0; st < nstages; ++st, ++use) {
           const int sa = use % SA;
@@ -350,7 +362,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
       bool ok = true;
       for (int item = cluster; item < total && ok; item += nclusters) {
         int e, p, m0, rows, n;
-        tc_decode_item(item, tprefix, a.num_e, soff, npairs, e, p, m0, rows, n);
+        tc_decode_item(item, tprefix, a.num_e, soff, tdesc, e, p, m0, rows, n);
         const uint32_t idesc = tc::idesc_bf16_m256((uint32_t)n);
         for (int kb = 0; kb < nkb && ok; ++kb, ++j) {
           const int slot = j & 1;
@@ -388,7 +400,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
     bool ok = true;
     for (int item = cluster; item < total && ok; item += nclusters) {
       int e, p, m0, rows, n;
-      tc_decode_item(item, tprefix, a.num_e, soff, npairs, e, p, m0, rows, n);
+      tc_decode_item(item, tprefix, a.num_e, soff, tdesc, e, p, m0, rows, n);
       const bool valid = 2 * p + (int)rank < ntiles;
       for (int st = 0; st < nstages; ++st, ++use) {
         const int s = use % SW, sa = use % SA;
@@ -424,7 +436,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
     bool ok = true;
     for (int item = cluster; item < total && ok; item += nclusters) {
       int e, p, m0, rows, n;
-      tc_decode_item(item, tprefix, a.num_e, soff, npairs, e, p, m0, rows, n);
+      tc_decode_item(item, tprefix, a.num_e, soff, tdesc, e, p, m0, rows, n);
       const int blk = 2 * p + (int)rank;
       const bool valid = blk < ntiles;
       const int ncols = max(0, min(128, n - ewg * 128));
