@@ -323,16 +323,17 @@ constexpr int kMaxTopK = 16;
 // -inf beyond E), by one warp: the routing mode's selection score, top-k by repeated warp
 // arg-max (ties to the lower index), the routing weights, and the writes of ids / weights /
 // counts for token t.
-__device__ __forceinline__ void select_topk(const float (&v)[kMaxPerLane], int lane, int t, int E,
+template <int NPL>  // experts per lane: E <= 32 * NPL
+__device__ __forceinline__ void select_topk(const float (&v)[NPL], int lane, int t, int E,
                                             const ccut_route_params& rp, int32_t* __restrict__ ids,
                                             float* __restrict__ weights, int* __restrict__ counts) {
   const int k = rp.top_k;
   // selection score
-  float sel[kMaxPerLane], sg[kMaxPerLane];
+  float sel[NPL], sg[NPL];
   if (rp.mode == CCUT_ROUTE_SIGMOID_GROUP) {
     const int gsize = E / rp.n_group;
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) {
+    for (int i = 0; i < NPL; ++i) {
       const int e = lane + 32 * i;
       sg[i] = e < E ? 1.f / (1.f + expf(-v[i])) : 0.f;
       sel[i] = e < E ? sg[i] + (rp.bias ? rp.bias[e] : 0.f) : -INFINITY;
@@ -343,7 +344,7 @@ __device__ __forceinline__ void select_topk(const float (&v)[kMaxPerLane], int l
     for (int g = 0; g < rp.n_group; ++g) {
       VI b1{-INFINITY, 0x7fffffff}, b2{-INFINITY, 0x7fffffff};
 #pragma unroll
-      for (int i = 0; i < kMaxPerLane; ++i) {
+      for (int i = 0; i < NPL; ++i) {
         const int e = lane + 32 * i;
         if (e < E && e / gsize == g) {
           if (better(sel[i], e, b1.v, b1.i)) {
@@ -378,13 +379,13 @@ __device__ __forceinline__ void select_topk(const float (&v)[kMaxPerLane], int l
       keep |= 1u << b.i;
     }
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) {
+    for (int i = 0; i < NPL; ++i) {
       const int e = lane + 32 * i;
       if (e < E && !((keep >> (e / gsize)) & 1)) sel[i] = -INFINITY;
     }
   } else {
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) {
+    for (int i = 0; i < NPL; ++i) {
       sel[i] = v[i];
       sg[i] = 0.f;
     }
@@ -396,14 +397,14 @@ __device__ __forceinline__ void select_topk(const float (&v)[kMaxPerLane], int l
   for (int j = 0; j < k; ++j) {
     VI b{-INFINITY, 0x7fffffff};
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) {
+    for (int i = 0; i < NPL; ++i) {
       const int e = lane + 32 * i;
       if (e < E && !((used >> i) & 1) && better(sel[i], e, b.v, b.i)) b = VI{sel[i], e};
     }
     b = warp_best(b);
     float lg = 0.f, sgv = 0.f;
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) {
+    for (int i = 0; i < NPL; ++i) {
       if (lane + 32 * i == b.i) {
         used |= 1u << i;
         lg = v[i];
@@ -425,7 +426,7 @@ __device__ __forceinline__ void select_topk(const float (&v)[kMaxPerLane], int l
     const float m = __shfl_sync(0xffffffffu, my_logit, 0);  // pick 0 is the max logit
     float s = 0.f;
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i)
+    for (int i = 0; i < NPL; ++i)
       if (lane + 32 * i < E) s += expf(v[i] - m);
     s = warp_sum(s);
     w = expf(my_logit - m) / fmaxf(s, 1e-30f);
@@ -449,6 +450,7 @@ __device__ __forceinline__ void select_topk(const float (&v)[kMaxPerLane], int l
   }}
 
 // One warp per token.  Logits come either from `part` (hsplit partial sums) or `logits_in`.
+template <int NPL>
 __global__ void __launch_bounds__(256) route_topk_kernel(const float* __restrict__ part, int hsplit,
                                                          const float* __restrict__ logits_in, int T, int E,
                                                          ccut_route_params rp, int32_t* __restrict__ ids,
@@ -459,9 +461,9 @@ __global__ void __launch_bounds__(256) route_topk_kernel(const float* __restrict
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + warp;
   if (t >= T) return;
-  float v[kMaxPerLane];
+  float v[NPL];
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) {
+  for (int i = 0; i < NPL; ++i) {
     const int e = lane + 32 * i;
     float val = -INFINITY;
     if (e < E) {
@@ -494,6 +496,7 @@ __global__ void __launch_bounds__(256) route_topk_kernel(const float* __restrict
 // the logits (and hence the routing) are bit-identical to it.
 constexpr int kTopkWideMaxT = 256;
 
+template <int NPL>
 __global__ void __launch_bounds__(256) route_topk_wide_kernel(const float* __restrict__ part, int hsplit, int T,
                                                               int E, ccut_route_params rp, int32_t* __restrict__ ids,
                                                               float* __restrict__ weights,
@@ -524,9 +527,9 @@ __global__ void __launch_bounds__(256) route_topk_wide_kernel(const float* __res
   }
   __syncthreads();
   if (tid >= 32) return;
-  float v[kMaxPerLane];
+  float v[NPL];
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) {
+  for (int i = 0; i < NPL; ++i) {
     const int e = tid + 32 * i;
     v[i] = e < E ? lg[e] : -INFINITY;
   }
@@ -656,17 +659,18 @@ int launch_route(const uint16_t* x, const float* router, int T, int H, int E, co
     rc = launch_k(route_logits_kernel, g1, dim3(256), 0, st, x, router, T, H, E, hs, part, counts, x16);
   }
   if (rc) return rc;
+  const bool narrow = E <= 128;  // four experts per lane instead of eight
   if (T <= kTopkWideMaxT)
-    return launch_k(route_topk_wide_kernel, dim3(T), dim3(256), 0, st, (const float*)part, hs, T, E, rp, ids, weights,
-                    logits, counts);
-  return launch_k(route_topk_kernel, dim3((T + 7) / 8), dim3(256), 0, st, (const float*)part, hs,
-                  (const float*)nullptr, T, E, rp, ids, weights, logits, counts);
+    return launch_k(narrow ? route_topk_wide_kernel<4> : route_topk_wide_kernel<kMaxPerLane>, dim3(T), dim3(256), 0,
+                    st, (const float*)part, hs, T, E, rp, ids, weights, logits, counts);
+  return launch_k(narrow ? route_topk_kernel<4> : route_topk_kernel<kMaxPerLane>, dim3((T + 7) / 8), dim3(256), 0, st,
+                  (const float*)part, hs, (const float*)nullptr, T, E, rp, ids, weights, logits, counts);
 }
 
 int launch_topk(const float* logits, int T, int E, const ccut_route_params& rp, int32_t* ids, float* weights,
                 cudaStream_t st) {
-  return launch_k(route_topk_kernel, dim3((T + 7) / 8), dim3(256), 0, st, (const float*)nullptr, 0, logits, T, E, rp,
-                  ids, weights, (float*)nullptr, (int*)nullptr);
+  return launch_k(E <= 128 ? route_topk_kernel<4> : route_topk_kernel<kMaxPerLane>, dim3((T + 7) / 8), dim3(256), 0,
+                  st, (const float*)nullptr, 0, logits, T, E, rp, ids, weights, (float*)nullptr, (int*)nullptr);
 }
 
 int launch_permute(const int32_t* ids, const float* weights, int T, int k, int E, int slices, float shared_gate,
