@@ -112,6 +112,17 @@ CCUT_DEVICE void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* 
       : "memory");
 }
 
+// ---- cp.async (16 bytes per thread; src-size 0 writes zeros) ---------------------------
+CCUT_DEVICE void cp_async16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+CCUT_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+CCUT_DEVICE void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // ---- ldmatrix / mma ------------------------------------------------------------------
 CCUT_DEVICE void ldmatrix_x4(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, const void* p) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"

@@ -170,16 +170,6 @@ constexpr int kRtStages = 4;
 constexpr int kRtStageBytes = (kRtTok + 3 * kRtExp) * kRtPitch2 * 2;  // x tile + three weight planes
 constexpr int kRtSmem = kRtStages * kRtStageBytes;
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
 // w3[s][e][h] (s = 0, 1, 2): the exact three-way bf16 split of router[e][h].
 __global__ void route_split_kernel(const float* __restrict__ router, size_t n4, size_t plane,
                                    uint16_t* __restrict__ w3) {
