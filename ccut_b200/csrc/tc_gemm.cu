@@ -467,13 +467,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
 #pragma unroll
         for (int c = 0; c < 128; c += 32) {
           if (c < ncols) {  // uniform over the warpgroup
-#pragma unroll
-            for (int c2 = 0; c2 < 32; c2 += 16) {  // 16 columns per load: registers for the totals
-              uint32_t v[16];
-              tc::ld_32x32b_x16(tl + (uint32_t)(slot * 256 + c + c2), v);
-              tc::wait_ld();
-              promote16(tot + c + c2, v, s);
-            }
+            uint32_t v[32];  // 32 columns per load (ncols is a multiple of 32)
+            tc::ld_32x32b_x32(tl + (uint32_t)(slot * 256 + c), v);
+            tc::wait_ld();
+            promote16(tot + c, *reinterpret_cast<const uint32_t(*)[16]>(v), s);
+            promote16(tot + c + 16, *reinterpret_cast<const uint32_t(*)[16]>(v + 16), s);
           }
         }
         tc::fence_before_sync();
