@@ -234,3 +234,18 @@ def test_wait_expiry_checks(lib):
     assert lib.ccut_debug_wait_expiry(NULL, 1000, NULL) == _lib.ERR_INVALID
     assert lib.ccut_debug_wait_expiry(FAKE, -1, NULL) == _lib.ERR_INVALID
     assert lib.ccut_debug_wait_expiry(FAKE, 1 << 40, NULL) == _lib.ERR_INVALID  # above the kernels' own budget
+
+
+def test_router_scratch_sizes(lib):
+    """From 256 tokens on, the router scratch also holds the exact three-way bf16 split of the
+    router (3 x E x H x 2 bytes); the expert-parallel workspace, sized once for T_cap tokens per
+    rank, never shrinks as T_cap grows, so every smaller batch fits in it."""
+    E, H = 128, 2048
+    small = lib.ccut_route_workspace_bytes(255, E, H)
+    big = lib.ccut_route_workspace_bytes(256, E, H)
+    assert big - small >= 3 * E * H * 2
+    layer = _lib.MoeLayerDesc(_lib.FMT_AWQ_INT4_G128, _lib.KERNEL_AUTO, H, 768, 16, 0, 1.0, FAKE, FAKE, FAKE, FAKE,
+                              FAKE)
+    sizes = [lib.ccut_moe_ep_forward_workspace_bytes(C.byref(layer), E, 8, t, 8) for t in range(1, 1200, 7)]
+    assert all(s > 0 for s in sizes)
+    assert all(b >= a for a, b in zip(sizes, sizes[1:]))
