@@ -165,6 +165,7 @@ int run_gate_up(const ccut_moe_layer* L, long per_expert, const uint16_t* x, con
     // fused gate/up rows: 2I packed rows, intermediate rows of I channels out
     TcArgs a{static_cast<const uint8_t*>(L->w13), ccut_w13_bytes(fmt, L->hidden, L->inter), L->hidden,
              2 * L->inter, offsets, ne, hbuf, L->inter, nullptr, status};
+    a.sched = sched;
     return launch_tc_gemm(fmt, kFfn1, map, a, num_sms(), st);
   }
   if (!x16) return CCUT_ERR_INVALID;
@@ -197,6 +198,7 @@ int run_down(const ccut_moe_layer* L, long per_expert, const uint16_t* hbuf, int
     if (rc) return rc;
     TcArgs a{static_cast<const uint8_t*>(L->w2), ccut_w2_bytes(fmt, L->hidden, L->inter), L->inter, L->hidden,
              offsets, ne, y_rows, L->hidden, row_weight, status, y_bf16};
+    a.sched = sched;
     return launch_tc_gemm(fmt, kFfn2, map, a, num_sms(), st);
   }
   GemmArgs a{static_cast<const uint8_t*>(L->w2_frags),

@@ -40,6 +40,10 @@ struct TcArgs {
   const float* row_weight;
   int* status;
   int out_bf16 = 0;  // FFN2: weighted rows as bf16 (one rounding) instead of fp32
+  // Dynamic item schedule: sched[0] hands out work items, sched[1] counts the clusters done;
+  // both zero on entry, left zero on exit (the same counters as GemmArgs::sched).  Null:
+  // static item striding.
+  int* sched = nullptr;
 };
 
 // tc_gemm.cu: the activation operand `map` covers bf16 rows [R, K] in expert order (boxes

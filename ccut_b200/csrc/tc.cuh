@@ -250,6 +250,17 @@ CCUT_DEVICE void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int 
       : "memory");
 }
 
+// 32-bit store to a shared::cluster address (this CTA's or the peer's shared memory).
+CCUT_DEVICE void st_cluster_u32(uint32_t cl_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cl_addr), "r"(v) : "memory");
+}
+// Arrival that publishes this thread's earlier stores (also to the peer's shared memory) to a
+// waiter on either CTA of the cluster (cluster-scope release; a waiter acquires with
+// mbar_wait_cl).
+CCUT_DEVICE void mbar_arrive_release_cl(uint32_t cl_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cl_addr) : "memory");
+}
+
 // Shared-memory writes of this thread become visible to the tensor cores' async proxy.
 CCUT_DEVICE void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 

@@ -49,6 +49,12 @@
 
 namespace ccut {
 
+// Work items reach every role of both CTAs through a ring of kItemRing slots that rank 0's
+// scheduler thread fills; each slot is freed by all its consumers: per CTA the two producer
+// threads and every dequant and epilogue warp, plus the MMA issuer of rank 0.
+constexpr int kItemRing = 4;
+constexpr int kItemConsumers = 2 * (2 + 8 + 8) + 1;
+
 template <int FMT>
 struct TcCfg {
   using B = Blk<FMT>;
@@ -75,10 +81,11 @@ struct TcCfg {
   static constexpr int kThreads = 640;
   static constexpr int kDeqWarps = 8;
   static constexpr int kEpiWarps = 8;
-  static constexpr int kNBar = 2 * kSW + 2 * kSA + 2 + 2 + 1;
+  static_assert(kItemConsumers == 2 * (2 + kDeqWarps + kEpiWarps) + 1, "item ring consumers");
+  static constexpr int kNBar = 2 * kSW + 2 * kSA + 2 + 2 + 1 + 2 * kItemRing + 1;
   // barriers, tensor-memory address, item prefix over experts, the experts' row offsets and
   // tile descriptors
-  static constexpr int kHeader = kNBar * 8 + 16 + 3 * 4 * (kMaxExperts + 1);
+  static constexpr int kHeader = kNBar * 8 + 16 + 3 * 4 * (kMaxExperts + 1) + 4 * kItemRing;
   static constexpr int kXchgOff = (kHeader + 1023) / 1024 * 1024;
   static constexpr int kRowWOff = kXchgOff + kXchg;   // FFN2: routing weights of the item's 256 tokens
   static constexpr int kABOff = kXchgOff + (kXchg + 256 * 4 + 1023) / 1024 * 1024;  // 1024-aligned tiles
@@ -201,6 +208,23 @@ __device__ __forceinline__ float block_scale(const uint8_t* blk, int r) {
   }
 }
 
+// The u-th work item of this CTA's walk from the item ring (one thread), its slot freed on
+// rank 0: an item id, -1 at the end of the walk, -2 when the wait ran out.
+__device__ __forceinline__ int tc_ring_item(int u, uint64_t* ifull, const int* iring, uint64_t* iempty, int* status) {
+  const int slot = u % kItemRing;
+  if (!tc::mbar_wait_cl(&ifull[slot], (u / kItemRing) & 1, status)) return -2;
+  const int item = *reinterpret_cast<const volatile int*>(&iring[slot]);
+  tc::mbar_arrive_cl(tc::mapa(&iempty[slot], 0));
+  return item;
+}
+// The same for a whole warp: lane 0 takes the slot, every lane gets the item.
+__device__ __forceinline__ int tc_ring_item_warp(int u, uint64_t* ifull, const int* iring, uint64_t* iempty,
+                                                 int* status, int lane) {
+  int item = 0;
+  if (lane == 0) item = tc_ring_item(u, ifull, iring, iempty, status);
+  return __shfl_sync(0xffffffffu, item, 0);
+}
+
 __device__ __forceinline__ void named_bar(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
@@ -238,10 +262,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
   uint64_t* pfull = abempty + SA;   // [2] partial sums of a 128-k block ready (both CTAs)
   uint64_t* pempty = pfull + 2;     // [2] rank 0: partial buffer drained by both CTAs
   uint64_t* drain = pempty + 2;
+  uint64_t* ifull = drain + 1;              // [kItemRing] item slot written (both CTAs)
+  uint64_t* iempty = ifull + kItemRing;     // [kItemRing] rank 0: item slot read by every consumer
+  uint64_t* idemand = iempty + kItemRing;   // rank 0: its weight producer took the next item
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNBar);
   int* tprefix = reinterpret_cast<int*>(smem + C::kNBar * 8 + 16);
   int* soff = tprefix + kMaxExperts + 1;  // a.offsets, read once: every role decodes items from it
   int* tdesc = soff + kMaxExperts + 1;    // per expert: tile width << 16 | tile count
+  int* iring = tdesc + kMaxExperts + 1;   // [kItemRing] work item ids (-1: end of the walk)
   float* xchg = reinterpret_cast<float*>(smem + C::kXchgOff);
   uint8_t* ab = smem + C::kABOff;
   uint8_t* wtiles = smem + C::kWOff;
@@ -270,6 +298,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
       mbar_init(&pempty[i], 2 * C::kEpiWarps);
     }
     mbar_init(drain, 1);
+    for (int i = 0; i < kItemRing; ++i) {
+      mbar_init(&ifull[i], 1);
+      mbar_init(&iempty[i], kItemConsumers);
+    }
+    mbar_init(idemand, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tc::prefetch_tmap(&bmap);
   }
@@ -308,7 +341,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
       // ------------------------------------------------------------ weight producer
       int use = 0;
       bool ok = true;
-      for (int item = cluster; item < total && ok; item += nclusters) {
+      for (int iu = 0; ok; ++iu) {
+        const int item = tc_ring_item(iu, ifull, iring, iempty, a.status);
+        if (item < 0) {
+          ok = item == -1;
+          break;
+        }
+        if (rank == 0) mbar_arrive(idemand);  // the scheduler may claim the item after this one
         int e, p, m0, rows, n;
         tc_decode_item(item, tprefix, a.num_e, soff, tdesc, e, p, m0, rows, n);
         const int blk = 2 * p + (int)rank;
@@ -339,7 +378,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
       // ------------------------------------------------------------ activation producer
       int use = 0;
       bool ok = true;
-      for (int item = cluster; item < total && ok; item += nclusters) {
+      for (int iu = 0; ok; ++iu) {
+        const int item = tc_ring_item(iu, ifull, iring, iempty, a.status);
+        if (item < 0) {
+          ok = item == -1;
+          break;
+        }
         int e, p, m0, rows, n;
         tc_decode_item(item, tprefix, a.num_e, soff, tdesc, e, p, m0, rows, n);
         const int brow = soff[e] + m0 + (int)rank * (n / 2);
@@ -356,11 +400,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
       }
       if (!ok)  // let issued loads land: the last stage's MMAs (or the timeout) end them
         for (int u = use > SA ? use - SA : 0; u < use; ++u) tc::mbar_wait_cl(&abempty[u % SA], (u / SA) & 1, nullptr);
+    } else if (warp == 3 && lane == 0 && rank == 0) {
+      // ------------------------------------------------------------ item scheduler (rank 0)
+      // Cluster c walks item c first, then (a.sched) the items a launch-wide counter hands
+      // out, so that clusters whose items ran faster take more and the SMs end together, or
+      // (no counter) c + nclusters, c + 2 nclusters, ...  An item is claimed only once rank
+      // 0's weight producer has taken the one before it, so a cluster holds at most one
+      // claimed item it has not started.  -1 ends the walk.
+      const uint32_t peer_ring = tc::mapa(iring, 1);
+      for (int u = 0;; ++u) {
+        const int slot = u % kItemRing;
+        if (!tc::mbar_wait_cl(&iempty[slot], ((u / kItemRing) & 1) ^ 1, a.status)) break;
+        if (u > 0 && !mbar_wait(idemand, (u - 1) & 1, a.status)) break;
+        int item = u == 0 ? cluster : a.sched ? nclusters + atomicAdd(&a.sched[0], 1) : cluster + u * nclusters;
+        if (item >= total) item = -1;
+        iring[slot] = item;
+        tc::st_cluster_u32(peer_ring + 4 * slot, (uint32_t)item);
+        tc::mbar_arrive_release_cl(tc::mapa(&ifull[slot], 0));
+        tc::mbar_arrive_release_cl(tc::mapa(&ifull[slot], 1));
+        if (item < 0) break;
+      }
+      // the last scheduler to finish leaves the counters zero for the next launch
+      if (a.sched && atomicAdd(&a.sched[1], 1) == nclusters - 1) {
+        a.sched[0] = 0;
+        a.sched[1] = 0;
+      }
     } else if (warp == 2 && lane == 0 && rank == 0) {
       // ------------------------------------------------------------ MMA issuer (rank 0)
       int use = 0, j = 0;
       bool ok = true;
-      for (int item = cluster; item < total && ok; item += nclusters) {
+      for (int iu = 0; ok; ++iu) {
+        const int item = tc_ring_item(iu, ifull, iring, iempty, a.status);
+        if (item < 0) {
+          ok = item == -1;
+          break;
+        }
         int e, p, m0, rows, n;
         tc_decode_item(item, tprefix, a.num_e, soff, tdesc, e, p, m0, rows, n);
         const uint32_t idesc = tc::idesc_bf16_m256((uint32_t)n);
@@ -398,14 +472,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
     const int r = dq & 127, hk = dq >> 7;  // weight row and 32-k half of the stage of this thread
     int use = 0;
     bool ok = true;
-    for (int item = cluster; item < total && ok; item += nclusters) {
+    for (int iu = 0; ok; ++iu) {
+      const int item = tc_ring_item_warp(iu, ifull, iring, iempty, a.status, lane);
+      if (item < 0) {
+        ok = item == -1;
+        break;
+      }
       int e, p, m0, rows, n;
       tc_decode_item(item, tprefix, a.num_e, soff, tdesc, e, p, m0, rows, n);
       const bool valid = 2 * p + (int)rank < ntiles;
       for (int st = 0; st < nstages; ++st, ++use) {
         const int s = use % SW, sa = use % SA;
-        if (!mbar_wait(&wfull[s], (use / SW) & 1, a.status) ||
-            !tc::mbar_wait_cl(&abempty[sa], ((use / SA) & 1) ^ 1, a.status)) {
+        const bool got = mbar_wait(&wfull[s], (use / SW) & 1, a.status) &&
+                         tc::mbar_wait_cl(&abempty[sa], ((use / SA) & 1) ^ 1, a.status);
+        if (!__all_sync(0xffffffffu, got)) {  // the warp leaves together (it shares collectives)
           ok = false;
           break;
         }
@@ -434,7 +514,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
     const uint32_t pe0 = tc::mapa(&pempty[0], 0), pe1 = tc::mapa(&pempty[1], 0);
     int j = 0;
     bool ok = true;
-    for (int item = cluster; item < total && ok; item += nclusters) {
+    for (int iu = 0; ok; ++iu) {
+      const int item = tc_ring_item_warp(iu, ifull, iring, iempty, a.status, lane);
+      if (item < 0) {
+        ok = item == -1;
+        break;
+      }
       int e, p, m0, rows, n;
       tc_decode_item(item, tprefix, a.num_e, soff, tdesc, e, p, m0, rows, n);
       const int blk = 2 * p + (int)rank;
@@ -459,8 +544,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(640, 1)
         const float s = s_cur;
         s_cur = s_nxt;
         s_nxt = (valid && kb + 2 < nkb) ? block_scale<FMT, MODE>(wb + (size_t)(kb + 2) * BK::kBytes, r) : 0.f;
-        if (!tc::mbar_wait_cl(&pfull[slot], (j >> 1) & 1, a.status)) {
-          ok = false;
+        if (!__all_sync(0xffffffffu, tc::mbar_wait_cl(&pfull[slot], (j >> 1) & 1, a.status))) {
+          ok = false;  // the warp leaves together (tensor-memory loads are warp-wide)
           break;
         }
         tc::fence_after_sync();
