@@ -21,8 +21,9 @@
 // reassociated in fp32.  Two partial buffers of 256 columns (all 512 tensor-memory columns)
 // let the MMAs of block kb + 1 run while block kb is promoted.
 //
-// Work item = (expert, token tile of up to 256 rows, pair p of 128-row weight blocks); each
-// cluster of two CTAs walks the items with a stride of the cluster count.  A 64-k stage is
+// Work item = (expert, token tile of up to 256 rows, pair p of 128-row weight blocks); cluster
+// c takes item c, then the items a launch-wide counter hands out (warp 3 of rank 0 claims
+// them and passes them to every role of both CTAs through a small ring).  A 64-k stage is
 // one A tile (128 rows x 64 k bf16, 16 KB) and one B tile (128 tokens x 64 k, 16 KB) per CTA.
 // Warp roles (20 warps per CTA):
 //   warp 0        weight producer: per stage one bulk copy of the packed 64-k half block (and
