@@ -233,7 +233,7 @@ def workload_config(wl: str, n: int, parallelism: str) -> dict:
 
 # DRAM bytes (read + write) of one gate/up launch from an ncu capture of the current kernel on
 # the same workload; workloads without such a capture report null.
-NCU_TRAFFIC: dict = {"cfg3_prefill": 388_043_264, "cfg0_decode": 202_890_240}
+NCU_TRAFFIC: dict = {"cfg3_prefill": 385_041_920, "cfg0_decode": 202_890_240}
 
 # Dense FP8 (e4m3 x e4m3) peak of this GPU, measured in the run: torch._scaled_mm 8192^3,
 # bf16 out, best of 10 (cuBLAS).  MEASURED_PEAKS.json has no FP8 figure.
